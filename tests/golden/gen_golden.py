@@ -1,0 +1,256 @@
+"""Generate the golden vectors in tests/golden/ from the reference itself.
+
+Runs the reference's own CPU path (oracle/_ref/libvoxref.so, compiled from the
+unmodified reference sources by oracle/Makefile) on seeded synthetic inputs
+and stores its outputs.  Inputs are not stored: they are regenerated from the
+recorded seeds with the oracle's counter-based generator, and a checksum of
+each input is stored so that a change of generator is caught.
+
+Outputs up to 32768 values are stored whole; larger ones as a fixed sample of
+32768 positions plus their L2 norm.
+
+    python tests/golden/gen_golden.py        # needs oracle/_ref (reference tree present)
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "..", "..", "oracle"))
+import bind as B  # noqa: E402
+
+SAMPLE = 32768
+
+
+def sample_idx(n, seed=12345):
+    if n <= SAMPLE:
+        return np.arange(n, dtype=np.int64)
+    rng = np.random.default_rng(seed + n)
+    return np.sort(rng.choice(n, SAMPLE, replace=False)).astype(np.int64)
+
+
+def pack(prefix, arr, out):
+    flat = np.asarray(arr, np.float32).reshape(-1)
+    idx = sample_idx(flat.size)
+    out[prefix + "_idx"] = idx
+    out[prefix + "_val"] = flat[idx]
+    out[prefix + "_norm"] = np.float64(np.linalg.norm(flat.astype(np.float64)))
+    out[prefix + "_size"] = np.int64(flat.size)
+
+
+def checksum(a):
+    return np.array(hashlib.sha1(np.ascontiguousarray(a).tobytes()).hexdigest()[:16])
+
+
+# (name, M, K, N, bias, path, seed)
+LINEAR_CASES = [
+    ("gemv_wq", 1, 3072, 4096, False, "linear", 11),
+    ("gemv_wk", 1, 3072, 1024, False, "linear", 12),
+    ("gemv_wo", 1, 4096, 3072, False, "linear", 13),
+    ("gemv_w1", 1, 3072, 9216, False, "linear", 14),
+    ("gemv_w2", 1, 9216, 3072, False, "linear", 15),
+    ("gemv_lmhead_slice", 1, 3072, 8192, False, "matmul_t", 16),
+    ("gemv_bias", 1, 1280, 2048, True, "linear", 17),
+    ("linear_m5_bias", 5, 1280, 2048, True, "linear", 18),
+    ("linear_m38_wq", 38, 3072, 4096, False, "linear", 19),
+    ("linear_m100_w2_bias", 100, 5120, 1280, True, "linear", 20),
+    ("linear_m8_wo", 8, 4096, 3072, False, "linear", 21),
+]
+
+
+def linear_inputs(M, K, N, bias, seed):
+    x = B.normal_f32((M, K), seed * 10 + 1)
+    W = B.normal_bf16((N, K), seed * 10 + 2)
+    b = B.normal_f32(N, seed * 10 + 3, 0.02) if bias else None
+    return x, W, b
+
+
+def gen_linear():
+    out = {}
+    for name, M, K, N, bias, path, seed in LINEAR_CASES:
+        x, W, b = linear_inputs(M, K, N, bias, seed)
+        y = B.ref_linear(x, W, b, path=path)
+        pack(name, y, out)
+        out[name + "_xsum"] = checksum(x)
+        out[name + "_wsum"] = checksum(W)
+    np.savez_compressed(os.path.join(HERE, "linear.npz"), **out)
+
+
+ROPE_POS = [0, 1, 2, 38, 750, 1000, 5000, 8191, 8192, 20000, 100000, 1234567]
+
+
+def gen_rope():
+    out = {"pos": np.array(ROPE_POS, np.int32)}
+    for hd in (128, 64):
+        out[f"freqs{hd}"] = B.ref_rope_freqs(out["pos"], hd)
+    x = B.normal_f32((len(ROPE_POS), 32 * 128), 31)
+    out["apply128"] = B.ref_apply_rope(x, out["freqs128"], 32, 128)
+    x = B.normal_f32((len(ROPE_POS), 32 * 64), 32)
+    out["apply64"] = B.ref_apply_rope(x, out["freqs64"], 32, 64)
+    np.savez_compressed(os.path.join(HERE, "rope.npz"), **out)
+
+
+# decode attention: (name, L, ring_write_slot or -1, seed)
+ATTN_DECODE = [("dec_L512", 512, -1, 41), ("dec_L2048", 2048, -1, 42),
+               ("dec_L8192", 8192, -1, 43), ("dec_ring5000", 8192, 5000, 44),
+               ("dec_L1", 1, -1, 45), ("dec_L777", 777, -1, 46)]
+
+
+def attn_decode_inputs(L, seed):
+    q = B.normal_f32((1, B.Q_DIM), seed * 10 + 1)
+    k = B.normal_f32((L, B.KV_DIM), seed * 10 + 2)
+    v = B.normal_f32((L, B.KV_DIM), seed * 10 + 3)
+    return q, k, v
+
+
+def ring_to_logical(buf, write_slot):
+    """A full ring whose newest row sits at write_slot, in logical order."""
+    return np.ascontiguousarray(np.roll(buf, -(write_slot + 1), axis=0))
+
+
+# prefill-style attention: (name, seq_q, cache_len, n_heads, n_kv, head_dim, window, seed)
+ATTN_PREFILL = [("enc_q100_c200", 100, 200, 32, 32, 64, 750, 51),
+                ("enc_q37_c750", 37, 750, 32, 32, 64, 750, 52),
+                ("dec_prefill_q38", 38, 0, 32, 8, 128, 8192, 53)]
+
+
+def attn_prefill_inputs(seq_q, cache, h, kvh, hd, seed):
+    q = B.normal_f32((seq_q, h * hd), seed * 10 + 1)
+    k = B.normal_f32((cache + seq_q, kvh * hd), seed * 10 + 2)
+    v = B.normal_f32((cache + seq_q, kvh * hd), seed * 10 + 3)
+    return q, k, v
+
+
+def gen_attention():
+    out = {}
+    for name, L, slot, seed in ATTN_DECODE:
+        q, k, v = attn_decode_inputs(L, seed)
+        if slot >= 0:
+            k, v = ring_to_logical(k, slot), ring_to_logical(v, slot)
+        o = B.ref_attention(q, k, v, 1, L, 32, 8, 128, 8192, L - 1)
+        pack(name, o, out)
+    for name, sq, cache, h, kvh, hd, win, seed in ATTN_PREFILL:
+        q, k, v = attn_prefill_inputs(sq, cache, h, kvh, hd, seed)
+        o = B.ref_attention(q, k, v, sq, cache + sq, h, kvh, hd, win, cache)
+        pack(name, o, out)
+    np.savez_compressed(os.path.join(HERE, "attention.npz"), **out)
+
+
+DEC_SEED = 0
+PROMPT = 38
+DEC_STEPS = 4
+COMPACT_MAX, COMPACT_OFFSET = 8200, 3000
+
+
+def dec_embeds(n, seed):
+    return B.normal_f32((n, B.DEC_DIM), seed, 1.0)
+
+
+def compact_kv_fill(seed):
+    k = B.normal_f32((B.DEC_LAYERS, COMPACT_MAX, B.KV_DIM), seed, 1.0)
+    v = B.normal_f32((B.DEC_LAYERS, COMPACT_MAX, B.KV_DIM), seed + 1, 1.0)
+    return k, v
+
+
+def top(logits, n=16):
+    idx = np.argsort(-logits, kind="stable")[:n]
+    return idx.astype(np.int32), logits[idx]
+
+
+def gen_decoder(w):
+    out = {}
+    ref = B.RefCtx(dec=w)
+    prompt = dec_embeds(PROMPT, 7001)
+    ref.decoder_prefill(prompt)
+    st = ref.state()
+    k, v = ref.dec_kv()
+    pack("prefill_k25", k[25, :PROMPT], out)
+    pack("prefill_v0", v[0, :PROMPT], out)
+    steps = dec_embeds(DEC_STEPS, 7002)
+    for s in range(DEC_STEPS):
+        tok, lg = ref.decoder_forward(steps[s])
+        pack(f"step{s}_logits", lg, out)
+        out[f"step{s}_token"] = np.int32(tok)
+        out[f"step{s}_top_idx"], out[f"step{s}_top_val"] = top(lg)
+    out["state_after"] = np.array(ref.state(), np.int32)
+    out["state_prefill"] = np.array(st, np.int32)
+    ref.free()
+
+    # compaction: a full cache (len == max) at logical offset COMPACT_OFFSET
+    ref = B.RefCtx(dec=w)
+    assert B.ref_lib().voxref_decoder_kv_preallocate(ref.ctx, COMPACT_MAX) == 0
+    k, v = ref.dec_kv()
+    kf, vf = compact_kv_fill(7100)
+    k[...] = kf
+    v[...] = vf
+    del kf, vf
+    B.ref_lib().voxref_set_dec_kv_state(ref.ctx, COMPACT_MAX, COMPACT_OFFSET)
+    steps = dec_embeds(2, 7003)
+    for s in range(2):
+        tok, lg = ref.decoder_forward(steps[s])
+        pack(f"compact{s}_logits", lg, out)
+        out[f"compact{s}_token"] = np.int32(tok)
+        out[f"compact{s}_state"] = np.array(ref.state(), np.int32)
+    ref.free()
+    np.savez_compressed(os.path.join(HERE, "decoder.npz"), **out)
+
+
+ENC_CHUNKS = [100, 37, 700, 100]
+
+
+def enc_chunks(seed=8001):
+    return [B.normal_f32((n, B.ENC_DIM), seed + i, 1.0) for i, n in enumerate(ENC_CHUNKS)]
+
+
+def gen_encoder(ew):
+    out = {}
+    ref = B.RefCtx(enc=ew)
+    outs = []
+    for i, x in enumerate(enc_chunks()):
+        y = ref.encoder_incremental(x)
+        outs.append(y)
+        pack(f"chunk{i}", y, out)
+        out[f"chunk{i}_state"] = np.array(ref.state(), np.int32)
+    enc = np.concatenate(outs[:2], axis=0)[:136]
+    a = ref.adapter(enc)
+    pack("adapter136", a, out)
+    ref.free()
+    np.savez_compressed(os.path.join(HERE, "encoder.npz"), **out)
+
+
+ALT_CASES = [(61, 3.0, 4, 0.999), (62, 0.5, 4, 0.5), (63, 8.0, 3, 0.99), (64, 1.0, 2, 0.9),
+             (65, 0.01, 4, 0.999)]
+
+
+def gen_alts():
+    out = {}
+    for i, (seed, std, n_alt, cut) in enumerate(ALT_CASES):
+        lg = B.normal_f32(B.VOCAB, seed, std)
+        best = int(np.argmax(lg))
+        ids = B.ref_fill_alts(lg, best, n_alt, cut)
+        out[f"case{i}_ids"] = np.array(ids, np.int32)
+        out[f"case{i}_best"] = np.int32(best)
+    np.savez_compressed(os.path.join(HERE, "alts.npz"), **out)
+
+
+def main():
+    assert B.ref_available(), "build oracle/_ref first (make -C oracle ref)"
+    t = time.time()
+    gen_linear(); print("linear", time.time() - t)
+    gen_rope(); print("rope", time.time() - t)
+    gen_attention(); print("attention", time.time() - t)
+    gen_alts(); print("alts", time.time() - t)
+    w = B.DecoderWeights(seed=DEC_SEED)
+    gen_decoder(w); print("decoder", time.time() - t)
+    del w
+    ew = B.EncoderWeights(seed=DEC_SEED)
+    gen_encoder(ew); print("encoder", time.time() - t)
+
+
+if __name__ == "__main__":
+    main()

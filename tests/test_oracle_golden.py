@@ -1,0 +1,124 @@
+"""The C restatement (oracle/vo_oracle.c) against golden vectors produced by
+the reference's own CPU path (tests/golden/gen_golden.py).  CPU only."""
+import numpy as np
+import pytest
+
+import bind as B
+import gen_golden as G
+from conftest import load_golden, unpack
+
+
+def sampled_rel(arr, g, prefix):
+    idx, val, _, size = unpack(g, prefix)
+    flat = np.asarray(arr, np.float32).reshape(-1)
+    assert flat.size == size
+    return B.rel_l2(flat[idx], val)
+
+
+@pytest.mark.parametrize("case", G.LINEAR_CASES, ids=[c[0] for c in G.LINEAR_CASES])
+def test_linear_matches_reference(case):
+    g = load_golden("linear")
+    name, M, K, N, bias, path, seed = case
+    x, W, b = G.linear_inputs(M, K, N, bias, seed)
+    assert str(g[name + "_xsum"]) == str(G.checksum(x)), "input generator changed"
+    assert str(g[name + "_wsum"]) == str(G.checksum(W)), "input generator changed"
+    y = B.linear(x, W, b)
+    assert sampled_rel(y, g, name) < 1e-5
+
+
+def test_rope_matches_reference():
+    g = load_golden("rope")
+    pos = g["pos"]
+    for hd in (128, 64):
+        f = B.rope_freqs(pos, hd)
+        ref = g[f"freqs{hd}"]
+        # Identical formula; the reference is built with -ffast-math, whose powf
+        # may differ by 1 ulp (2^-23 relative) from glibc's, so the angle error
+        # grows with the position: |d angle| <= pos * freq * 2^-23, freq <= 1.
+        bound = 1e-6 + 2.0 * 2.0**-23 * pos.astype(np.float64)
+        assert np.all(np.abs(f - ref).max(axis=1) <= bound)
+    x = B.normal_f32((len(pos), 32 * 128), 31)
+    # apply_rope with the reference's own table is exact arithmetic
+    assert np.array_equal(B.apply_rope(x, g["freqs128"], 32, 128), g["apply128"])
+    x = B.normal_f32((len(pos), 32 * 64), 32)
+    assert np.array_equal(B.apply_rope(x, g["freqs64"], 32, 64), g["apply64"])
+
+
+@pytest.mark.parametrize("case", G.ATTN_DECODE, ids=[c[0] for c in G.ATTN_DECODE])
+def test_decode_attention_matches_reference(case):
+    g = load_golden("attention")
+    name, L, slot, seed = case
+    q, k, v = G.attn_decode_inputs(L, seed)
+    if slot >= 0:
+        k, v = G.ring_to_logical(k, slot), G.ring_to_logical(v, slot)
+    o = B.causal_attention(q, k, v, 1, L, 32, 8, 128, 8192, L - 1)
+    assert sampled_rel(o, g, name) < 1e-5
+
+
+@pytest.mark.parametrize("case", G.ATTN_PREFILL, ids=[c[0] for c in G.ATTN_PREFILL])
+def test_prefill_attention_matches_reference(case):
+    g = load_golden("attention")
+    name, sq, cache, h, kvh, hd, win, seed = case
+    q, k, v = G.attn_prefill_inputs(sq, cache, h, kvh, hd, seed)
+    o = B.causal_attention(q, k, v, sq, cache + sq, h, kvh, hd, win, cache)
+    assert sampled_rel(o, g, name) < 1e-5
+
+
+def test_fill_alts_matches_reference():
+    g = load_golden("alts")
+    for i, (seed, std, n_alt, cut) in enumerate(G.ALT_CASES):
+        lg = B.normal_f32(B.VOCAB, seed, std)
+        best = int(np.argmax(lg))
+        assert best == int(g[f"case{i}_best"])
+        assert B.fill_alts(lg, best, n_alt, cut) == g[f"case{i}_ids"].tolist()
+
+
+@pytest.fixture(scope="module")
+def dec_weights():
+    return B.DecoderWeights(seed=G.DEC_SEED)
+
+
+def test_decoder_prefill_and_steps_match_reference(dec_weights):
+    g = load_golden("decoder")
+    o = B.OracleDecoder(dec_weights, 8192 + 38 + 1024)
+    o.prefill(G.dec_embeds(G.PROMPT, 7001))
+    assert list(o.state) == [int(g["state_prefill"][0]), int(g["state_prefill"][2])]
+    assert sampled_rel(o.k[25, :G.PROMPT], g, "prefill_k25") < 1e-5
+    assert sampled_rel(o.v[0, :G.PROMPT], g, "prefill_v0") < 1e-5
+    steps = G.dec_embeds(G.DEC_STEPS, 7002)
+    for s in range(G.DEC_STEPS):
+        tok, lg = o.step(steps[s])
+        assert sampled_rel(lg, g, f"step{s}_logits") < 1e-4
+        assert tok == int(g[f"step{s}_token"])
+
+
+def test_decoder_compaction_matches_reference(dec_weights):
+    g = load_golden("decoder")
+    o = B.OracleDecoder(dec_weights, G.COMPACT_MAX)
+    kf, vf = G.compact_kv_fill(7100)
+    o.k[...] = kf
+    o.v[...] = vf
+    del kf, vf
+    o.kv.len, o.kv.pos_offset = G.COMPACT_MAX, G.COMPACT_OFFSET
+    steps = G.dec_embeds(2, 7003)
+    for s in range(2):
+        tok, lg = o.step(steps[s])
+        st = g[f"compact{s}_state"]
+        assert (o.kv.len, o.kv.pos_offset) == (int(st[0]), int(st[2]))
+        assert sampled_rel(lg, g, f"compact{s}_logits") < 1e-4
+        assert tok == int(g[f"compact{s}_token"])
+
+
+def test_encoder_chunks_and_adapter_match_reference():
+    g = load_golden("encoder")
+    ew = B.EncoderWeights(seed=G.DEC_SEED)
+    o = B.OracleEncoder(ew, kv_max=2400)
+    outs = []
+    for i, x in enumerate(G.enc_chunks()):
+        y = o.step(x)
+        outs.append(y)
+        st = g[f"chunk{i}_state"]
+        assert (o.kv.len, o.kv.pos_offset) == (int(st[3]), int(st[5]))
+        assert sampled_rel(y, g, f"chunk{i}") < 1e-4
+    a = o.adapter(np.concatenate(outs[:2], axis=0)[:136])
+    assert sampled_rel(a, g, "adapter136") < 1e-4
