@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""Benchmark: multi-stream decode throughput of the Voxtral-Realtime-4B decoder
+on B200 through libvoxtral_cuda.so (BASELINE.json configs[4] shape: 8 concurrent
+streams per GPU, streams sharded data-parallel over GPUs, no collectives).
+
+One step = one batched decode step of every stream on the GPU (26 layers:
+fused QKV+RoPE+ring write, split-K attention, wo, SwiGLU w1|w3, w2, then the
+LM head + argmax), i.e. one token per stream.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--streams S]
+  python bench.py --impl reference ...    # the reference's CPU path on host cores
+
+Prints one JSON line (rank 0).  Weights are random-init bf16 (seeded), the KV
+rings hold the stream positions of a 60 s clip (39 + 100*i).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "voxtral.c_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+sys.path.insert(0, PKG)
+
+METRIC = "decode tok/s/GPU + encoder audio-s/s at 4B; GEMV HBM GB/s vs B200 peak"
+UNIT = "tokens/s"
+D, QD, KVD, HID, VOCAB, LAYERS = 3072, 4096, 1024, 9216, 131072, 26
+WEIGHT_BYTES_PER_STEP = LAYERS * 2 * (6144 * D + D * QD + 2 * HID * D + D * HID) + VOCAB * D * 2
+
+# DRAM bytes per launch of the dominant kernel (the w1|w3 SwiGLU GEMV) from
+# the ncu capture summarised in profiles/ (None until captured).
+NCU_TRAFFIC_W13 = None
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def positions(streams):
+    return [39 + 100 * i for i in range(streams)]
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (torch.distributed; no collectives on the data path)
+# ---------------------------------------------------------------------------
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference's own path (oracle/_ref) or the oracle port
+# ---------------------------------------------------------------------------
+
+def cpu_decode_rate(threads, steps, warmup=0):
+    """Decode tok/s of `threads` independent streams, one host thread each,
+    through the reference's vox_decoder_forward (oracle/_ref/libvoxref.so),
+    or the C restatement where the reference was not built.  Distinct
+    random-init weights for all 26 layers (6.9 GB of bf16, as on the GPU)."""
+    sys.path.insert(0, ORACLE)
+    import ctypes as C
+
+    import bind as B
+    w = B.DecoderWeights(seed=0, n_layers=LAYERS, distinct=LAYERS)
+    embeds = B.normal_f32((threads, D), 99)
+    logits = np.empty((threads, VOCAB), np.float32)
+    toks = np.zeros(threads, np.int32)
+    if B.ref_available():
+        kind = "reference"
+        ctxs = [B.RefCtx(dec=w) for _ in range(threads)]
+        lib = B.ref_lib()
+        for c in ctxs:
+            lib.voxref_decoder_kv_preallocate(c.ctx, 8192 + 1024)
+            lib.voxref_set_dec_kv_state(c.ctx, 400, 0)  # mid-clip cache length
+        arr = (C.c_void_p * threads)(*[c.ctx for c in ctxs])
+        if warmup:
+            lib.voxref_decode_threads(arr, threads, warmup, B.fptr(embeds), B.fptr(logits), B.iptr(toks))
+        secs = lib.voxref_decode_threads(arr, threads, steps, B.fptr(embeds), B.fptr(logits), B.iptr(toks))
+        for c in ctxs:
+            c.free()
+    else:
+        kind = "port"
+        from concurrent.futures import ThreadPoolExecutor
+        decs = [B.OracleDecoder(w, 8192 + 1024) for _ in range(threads)]
+        for o in decs:
+            o.kv.len = 400
+
+        def run(i, n):
+            for _ in range(n):
+                decs[i].step(embeds[i])
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(lambda i: run(i, warmup), range(threads)))
+            t0 = time.perf_counter()
+            list(ex.map(lambda i: run(i, steps), range(threads)))
+            secs = time.perf_counter() - t0
+    return threads * steps / secs, kind
+
+
+def reference_arm(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    threads = min(8, os.cpu_count() or 1)
+    rate, kind = cpu_decode_rate(threads, args.steps, args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * threads / rate,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 weights)",
+        "data": "synthetic (seeded random-init bf16 weights)",
+        "config": config(threads, [400] * threads, ws),
+        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{threads} streams x {args.steps} decode steps, one host thread each "
+                                   f"(vox_decoder_forward; its GEMV is single-threaded per stream)"},
+        "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config(streams, pos, ws):
+    return {
+        "workload": "configs[4] multi-stream decode: Voxtral-Realtime-4B decoder (26 layers, dim 3072, "
+                    "GQA 32/8 x 128, SwiGLU 9216, vocab 131072, tied LM head), one batched decode step "
+                    "of every stream per step",
+        "streams_per_gpu": streams, "kv_positions": pos, "kv_dtype": "f32 ring",
+        "global_batch": streams * ws, "seq_len": 1,
+        "l2": "no flush: the 6.86 GB of bf16 weights streamed per step exceed the 126 MB L2",
+        "parallelism": f"dp{ws} (independent streams, no collectives)",
+    }
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def build_device_decoder(V, torch, seed=0):
+    """Random-init bf16 weights generated on the device, handed to the
+    library, which lays them out (wq|wk|wv, w1/w3 interleaved)."""
+    dev = torch.device("cuda")
+    keep = []
+
+    def bf16(shape, s):
+        t = torch.empty(shape, dtype=torch.int16, device=dev)
+        V.check(V.lib().vox_cuda_fill_normal_bf16_dev(t.data_ptr(), t.numel(), s, 0.02, None), "fill")
+        keep.append(t)
+        return t.data_ptr()
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    ones = torch.ones(D, dtype=torch.float32, device=dev)
+    ada = (0.1 * torch.randn((LAYERS, D), generator=g, device=dev)).contiguous()
+    layers = []
+    for l in range(LAYERS):
+        b = 1000 * seed + 10 * l
+        layers.append((bf16((QD, D), b + 1), bf16((KVD, D), b + 2), bf16((KVD, D), b + 3),
+                       bf16((D, QD), b + 4), bf16((HID, D), b + 5), bf16((D, HID), b + 6),
+                       bf16((HID, D), b + 7), ones.data_ptr(), ones.data_ptr()))
+    emb = bf16((VOCAB, D), 1000 * seed + 999)
+    torch.cuda.synchronize()
+    V.lib().vox_cuda_init()
+    dec = V.Decoder(emb, ones.data_ptr(), layers, ada_scale=ada.data_ptr(), on_device=True)
+    del keep
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return dec
+
+
+def our_arm(args):
+    ws, rank, local = dist_env()
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    import voxcuda as V
+    V.init(local)
+    S = args.streams
+    dec = build_device_decoder(V, torch)
+    pos = positions(S)
+    states = [dec.state(kv_cap=8192 + 1024) for _ in range(S)]
+    for st, p in zip(states, pos):
+        st.set_position(p)
+
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1234 + rank)
+    embeds = torch.randn((S, D), generator=gen, device="cuda", dtype=torch.float32)
+    tokens = torch.zeros(S, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def reset_positions():
+        for st, p in zip(states, pos):
+            st.set_position(p)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # --- device-resident timing (value) ---
+    for _ in range(args.warmup):
+        V.step_batch_dev(states, embeds.data_ptr(), tokens.data_ptr(), sp)
+    reset_positions()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            V.step_batch_dev(states, embeds.data_ptr(), tokens.data_ptr(), sp)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms_step = ms / args.steps
+    value = ws * S * args.steps / (ms / 1000.0)
+
+    # --- end-to-end through the host API (host embeds in, tokens out) ---
+    reset_positions()
+    h_embeds = np.ascontiguousarray(embeds.cpu().numpy())
+    for _ in range(args.warmup):
+        V.step_batch(states, h_embeds)
+    reset_positions()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        V.step_batch(states, h_embeds)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e = ws * S * args.steps / e2e_s
+
+    # --- per-phase device time (kernel by kernel, events around each launch) ---
+    reset_positions()
+    prof = V.profile_batch(states, embeds.data_ptr(), iters=3)
+    hbm, peak_kind = peaks()
+    w13_bytes = 2 * HID * D * 2 + S * D * 4 + S * HID * 4        # per launch
+    w13_ms = prof["w13"] / LAYERS
+    achieved = w13_bytes / (w13_ms / 1000.0) / 1e9
+    kv_bytes = sum(LAYERS * min(p + 1, 8192) * KVD * 4 * 2 for p in pos)
+    step_bytes = WEIGHT_BYTES_PER_STEP + kv_bytes
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            threads = min(8, os.cpu_count() or 1)
+            rate, kind = cpu_decode_rate(threads, 1)
+            cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": kind,
+                   "sample": f"{threads} streams x 1 decode step (vox_decoder_forward, KV length 400), "
+                             f"one host thread per stream"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 weights)",
+            "data": "synthetic (seeded random-init bf16 weights, random embeddings)",
+            "config": config(S, pos, ws),
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": S * (D * 4 + 128 * 4 + 32),
+                    "d2h_bytes_per_step": S * 4},
+            "gpu_launches": args.steps * (5 * LAYERS + 1),
+            "roofline": {"kernel": "gemv_kernel<M=8, EPI_SWIGLU> (w1|w3 + SwiGLU)", "bound": "hbm",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": peak_kind,
+                         "traffic": NCU_TRAFFIC_W13, "bytes_per_launch": w13_bytes,
+                         "launch_ms": w13_ms},
+            "step_roofline": {"bytes_per_step": step_bytes,
+                              "achieved_gbs": step_bytes / (ms_step / 1000.0) / 1e9,
+                              "frac": step_bytes / (ms_step / 1000.0) / 1e9 / hbm},
+            "phase_ms": prof,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    for st in states:
+        st.free()
+    dec.free()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--streams", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        our_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,233 @@
+/*
+ * voxtral_cuda.h - B200 (sm_100a) backend for voxtral.c's inference hot path.
+ *
+ * A plain C ABI (no CUDA, PyTorch or C++ types in any signature) that the
+ * reference's C host calls under `#ifdef USE_CUDA`, at the same call sites
+ * where the `make mps` build calls voxtral_metal.h.  Every entry point below
+ * names the reference interface it replaces (file:line in voxtral.c's tree).
+ *
+ * Conventions
+ *   - Status: functions returning int return >= 0 on success (a token id
+ *     where stated) and a negative VOX_CUDA_ERR_* code on failure.  There is
+ *     no CPU fallback inside this library: a failure is reported, never
+ *     silently recomputed on the host.
+ *   - Pointers: "host" arguments are ordinary host memory owned by the caller
+ *     (e.g. the mmap'd safetensors); "_dev" entry points take device pointers
+ *     and an optional cudaStream_t passed as void* (NULL = the library's
+ *     stream for the calling thread's device).
+ *   - Weights are bf16 row-major [out_dim, in_dim] exactly as stored in
+ *     consolidated.safetensors; norms, biases and activations are fp32.
+ *   - Threading: calls on one decoder/encoder state must come from one host
+ *     thread at a time; different states may run concurrently.
+ */
+#ifndef VOXTRAL_CUDA_H
+#define VOXTRAL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VOX_CUDA_OK              0
+#define VOX_CUDA_ERR_UNAVAILABLE (-1)  /* no usable sm_100 device / not initialised */
+#define VOX_CUDA_ERR_ARG         (-2)  /* bad shape, NULL pointer, unsupported size */
+#define VOX_CUDA_ERR_OOM         (-3)  /* device allocation failed */
+#define VOX_CUDA_ERR_CUDA        (-4)  /* a CUDA runtime call or kernel failed */
+#define VOX_CUDA_ERR_CAPACITY    (-5)  /* KV ring / scratch capacity exceeded */
+
+/* ------------------------------------------------------------------------
+ * Lifecycle  (voxtral_metal.h:19-26, called at main.c:162-164, 283-285)
+ * ------------------------------------------------------------------------ */
+
+/* Initialise the backend on the calling thread's device (VOX_CUDA_DEVICE env
+ * var, else device 0).  Returns 1 on success, 0 if unavailable - the same
+ * convention as vox_metal_init (voxtral_metal.h:20). */
+int vox_cuda_init(void);
+
+/* 1 if vox_cuda_init succeeded on this thread's device (voxtral_metal.h:23). */
+int vox_cuda_available(void);
+
+/* Release every device resource the library holds (voxtral_metal.h:26). */
+void vox_cuda_shutdown(void);
+
+/* Bind the calling host thread to a device (multi-stream / multi-GPU hosts:
+ * one host thread per device).  Returns 0 or a VOX_CUDA_ERR_* code. */
+int vox_cuda_set_device(int device);
+
+/* Human-readable description of the last error on the calling thread. */
+const char *vox_cuda_last_error(void);
+
+/* Device bytes held by the library on the current device
+ * (vox_metal_memory_used, voxtral_metal.h:258). */
+size_t vox_cuda_memory_used(void);
+
+/* ------------------------------------------------------------------------
+ * (1) bf16-weight matmul entry points
+ * ------------------------------------------------------------------------ */
+
+/* C[M,N] = A[M,K] . B[N,K]^T (+ bias[N]) with host A, C, bias and host bf16
+ * B.  B is uploaded on first use and cached on the device keyed by its host
+ * pointer (the mmap'd tensor), like the Metal pointer-keyed weight cache.
+ * Replaces vox_metal_sgemm_bf16 (voxtral_metal.h:38-41) at the dispatch
+ * points of vox_linear_nobias_bf16 / vox_linear_bf16 / vox_matmul_t_bf16
+ * (voxtral_kernels.c:197-264).  M <= 8 runs the streaming GEMV, larger M the
+ * tcgen05 tensor-core GEMM. */
+int vox_cuda_sgemm_bf16(int M, int N, int K, const float *A, const uint16_t *B_bf16,
+                        const float *bias, float *C);
+
+/* Pre-upload a weight into the pointer-keyed cache (vox_metal_warmup_bf16,
+ * voxtral_metal.h:225). */
+int vox_cuda_warmup_bf16(const uint16_t *B_bf16, size_t num_elements);
+
+/* Device-pointer form of vox_cuda_sgemm_bf16: all pointers on the device. */
+int vox_cuda_linear_bf16_dev(int M, int N, int K, const float *A, const uint16_t *B_bf16,
+                             const float *bias, float *C, void *stream);
+
+/* ------------------------------------------------------------------------
+ * (2) (4) (5) decoder: resident weights, KV ring, single-token step
+ * ------------------------------------------------------------------------ */
+
+#define VOX_CUDA_DEC_MAX_LAYERS 26
+
+typedef struct {
+    const uint16_t *wq, *wk, *wv, *wo;   /* [4096,3072] [1024,3072] x2 [3072,4096] */
+    const uint16_t *w1, *w2, *w3;        /* [9216,3072] [3072,9216] [9216,3072] */
+    const float *attention_norm;         /* [3072] */
+    const float *ffn_norm;               /* [3072] */
+} vox_cuda_dec_layer_weights;
+
+/* The decoder half of vox_ctx_t (voxtral.h:101-137) plus ctx->ada_scale. */
+typedef struct {
+    int n_layers;                        /* VOX_DEC_LAYERS (26) */
+    int vocab;                           /* VOX_VOCAB_SIZE (131072) */
+    int weights_on_device;               /* 0: host pointers (uploaded), 1: device */
+    const uint16_t *tok_embeddings;      /* [vocab, 3072]; also the LM head */
+    const float *norm;                   /* [3072] final norm */
+    const float *ada_scale;              /* [n_layers, 3072] or NULL */
+    vox_cuda_dec_layer_weights layers[VOX_CUDA_DEC_MAX_LAYERS];
+} vox_cuda_dec_weights;
+
+typedef struct vox_cuda_decoder vox_cuda_decoder;   /* resident weights (per device) */
+typedef struct vox_cuda_dec_state vox_cuda_dec_state; /* one stream: KV ring + scratch */
+
+/* Upload (or adopt, when weights_on_device) the decoder weights into the
+ * fused device layout: wq|wk|wv concatenated, w1/w3 row-interleaved.  The
+ * counterpart of the Metal warm-up (voxtral.c:161-242).  NULL on failure. */
+vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights *w);
+void vox_cuda_decoder_free(vox_cuda_decoder *d);
+
+/* Per-stream state: device KV ring of kv_cap positions per layer (>= 8192 to
+ * hold the full sliding window; the reference preallocates 8192+1024,
+ * voxtral.c:233).  Replaces kv_cache_init / vox_decoder_kv_cache_preallocate
+ * (voxtral_decoder.c:114-139). */
+vox_cuda_dec_state *vox_cuda_dec_state_create(vox_cuda_decoder *d, int kv_cap);
+void vox_cuda_dec_state_free(vox_cuda_dec_state *s);
+
+/* Forget the cached positions (voxtral.c:857-858 sets kv_cache_len = 0 and
+ * kv_pos_offset = 0 before a new prefill). */
+int vox_cuda_dec_state_reset(vox_cuda_dec_state *s);
+
+/* Number of logical positions consumed so far (kv_pos_offset + kv_cache_len
+ * in the reference's bookkeeping). */
+int vox_cuda_dec_state_position(const vox_cuda_dec_state *s);
+
+/* Set the logical position of the next row without computing anything: the
+ * ring then holds whatever was loaded with vox_cuda_dec_state_load_kv.  Used
+ * to resume from a cache the caller filled (and by tests). */
+int vox_cuda_dec_state_set_position(vox_cuda_dec_state *s, int logical_pos);
+
+/* Copy rows of K and V ([n_rows, 1024] fp32 host arrays) for one layer into
+ * the ring at logical positions first_pos..first_pos+n_rows-1 (slot =
+ * position mod kv_cap).  Lets a caller migrate an existing CPU cache. */
+int vox_cuda_dec_state_load_kv(vox_cuda_dec_state *s, int layer, int first_pos, int n_rows,
+                               const float *k_rows, const float *v_rows);
+
+/* Read back rows of the ring (same layout as load_kv). */
+int vox_cuda_dec_state_read_kv(vox_cuda_dec_state *s, int layer, int first_pos, int n_rows,
+                               float *k_rows, float *v_rows);
+
+/* One decode step for one token: all layers, the final norm, the LM head and
+ * the argmax (first maximum, voxtral_decoder.c:507-515), with RoPE, the KV
+ * ring write and the windowed attention in-kernel.  embed: host [3072].
+ * rope_freqs: host [64][2] (cos, sin) as vox_compute_rope_freqs produces for
+ * the step's logical position, or NULL to derive them on the device.  logits:
+ * host [vocab] or NULL.  Returns the token id.  Replaces the CPU layer loop of
+ * vox_decoder_forward (voxtral_decoder.c:401-516) the way
+ * vox_metal_decoder_full_step does (voxtral_metal.h:219). */
+int vox_cuda_decoder_full_step(vox_cuda_dec_state *s, const float *embed,
+                               const float *rope_freqs, float *logits);
+
+/* Alternatives for the last step's logits, computed on the device with the
+ * semantics of stream_fill_alts (voxtral.c:778-833): ids >= 1000 other than
+ * the best, by probability, accepted while 1 - p/p_best <= cutoff.  Writes
+ * alt_ids[0] = best and returns the number of ids written (1..n_alt). */
+int vox_cuda_decoder_fill_alts(vox_cuda_dec_state *s, int n_alt, float cutoff, int *alt_ids);
+
+/* Prefill seq_len rows (host x [seq_len, 3072]) at the current position
+ * (voxtral_decoder.c:233-373; vox_metal_decoder_prefill_step,
+ * voxtral_metal.h:254).  rope_freqs: host [seq_len][64][2] or NULL. */
+int vox_cuda_decoder_prefill_step(vox_cuda_dec_state *s, const float *x, int seq_len,
+                                  const float *rope_freqs);
+
+/* Batched decode step over n independent streams that share one decoder:
+ * the weights are read once for all n tokens (n <= 8).  embeds: host
+ * [n, 3072]; tokens: host [n].  An additive entry with no single-stream
+ * counterpart in the reference (each stream is its own vox_ctx_t there). */
+int vox_cuda_decoder_step_batch(vox_cuda_dec_state *const *states, int n, const float *embeds,
+                                int *tokens);
+
+/* Device-resident form of the batched step for callers that keep the
+ * embeddings on the device: embeds_dev [n, 3072], tokens_dev [n] (int32),
+ * enqueued on `stream`; nothing is copied to or from the host. */
+int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states, int n,
+                                    const float *embeds_dev, int *tokens_dev, void *stream);
+
+/* Per-phase device time of the batched step, for profiling (the CUDA-event
+ * phase timers the reference keeps with gettimeofday, voxtral.c:679-680,
+ * 895-919).  Runs `iters` steps kernel by kernel (no graph, no overlap) with
+ * an event pair around every launch and writes the mean milliseconds per
+ * step of each phase to ms[VOX_CUDA_PROF_PHASES].  The states' positions do
+ * not advance. */
+#define VOX_CUDA_PROF_QKV      0   /* norm + wq|wk|wv GEMV + RoPE + ring write */
+#define VOX_CUDA_PROF_ATTN     1   /* split-K decode attention */
+#define VOX_CUDA_PROF_WO       2   /* wo GEMV + residual */
+#define VOX_CUDA_PROF_W13      3   /* norm + w1|w3 GEMV + SwiGLU */
+#define VOX_CUDA_PROF_W2       4   /* w2 GEMV + residual */
+#define VOX_CUDA_PROF_LM_HEAD  5   /* final norm + LM head + argmax */
+#define VOX_CUDA_PROF_PHASES   6
+int vox_cuda_decoder_profile_batch(vox_cuda_dec_state *const *states, int n,
+                                   const float *embeds_dev, int iters, float *ms);
+
+/* ------------------------------------------------------------------------
+ * Kernel-level entry points (device pointers) - the decode attention and the
+ * LM-head argmax on their own, for callers that compose their own step.
+ * ------------------------------------------------------------------------ */
+
+/* Decode attention for one token over a KV ring: q [32*128] (RoPE already
+ * applied), k_ring/v_ring [kv_cap, 1024], keys at logical positions
+ * max(0, pos-8191)..pos stored at slot = position mod kv_cap; out [32*128].
+ * vox_causal_attention with seq_q = 1 (voxtral_kernels.c:412-482, called at
+ * voxtral_decoder.c:481-483).  Scratch for the split-K partials comes from
+ * the library's per-device pool. */
+int vox_cuda_attention_decode_dev(const float *q, const float *k_ring, const float *v_ring,
+                                  int kv_cap, int pos, float *out, void *stream);
+
+/* Interleaved-pair RoPE of x [n_heads*head_dim] at logical position pos,
+ * cos/sin from rope_freqs ([head_dim/2][2], device) or, when NULL, derived on
+ * the device (vox_apply_rope, voxtral_kernels.c:502-526). */
+int vox_cuda_rope_dev(float *x, int n_heads, int head_dim, int pos, const float *rope_freqs,
+                      void *stream);
+
+/* ------------------------------------------------------------------------
+ * Synthetic weights (benchmarks and tests): fill a device bf16 buffer with
+ * seeded N(0, std) values, rounded to nearest even.
+ * ------------------------------------------------------------------------ */
+int vox_cuda_fill_normal_bf16_dev(uint16_t *dst, size_t n, uint64_t seed, float std,
+                                  void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VOXTRAL_CUDA_H */

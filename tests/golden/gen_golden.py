@@ -179,6 +179,12 @@ def gen_decoder(w):
         out[f"step{s}_top_idx"], out[f"step{s}_top_val"] = top(lg)
     out["state_after"] = np.array(ref.state(), np.int32)
     out["state_prefill"] = np.array(st, np.int32)
+    # the reference's own RoPE tables for these positions (its -ffast-math
+    # powf can differ from other builds by an ulp; a caller passes them on)
+    out["prefill_rope"] = B.ref_rope_freqs(np.arange(PROMPT), 128)
+    out["step_rope"] = B.ref_rope_freqs(np.arange(PROMPT, PROMPT + DEC_STEPS), 128)
+    out["compact_rope"] = B.ref_rope_freqs(
+        np.arange(COMPACT_OFFSET + 8200, COMPACT_OFFSET + 8202), 128)
     ref.free()
 
     # compaction: a full cache (len == max) at logical offset COMPACT_OFFSET

@@ -1,0 +1,88 @@
+// vc_common.cuh - shared device helpers for the sm_100a voxtral backend.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vc {
+
+// Model constants (voxtral.h:18-50).
+constexpr int kDecDim = 3072;
+constexpr int kDecLayersMax = 26;
+constexpr int kDecHeads = 32;
+constexpr int kDecKvHeads = 8;
+constexpr int kHeadDim = 128;
+constexpr int kQDim = kDecHeads * kHeadDim;      // 4096
+constexpr int kKvDim = kDecKvHeads * kHeadDim;   // 1024
+constexpr int kQkvRows = kQDim + 2 * kKvDim;     // 6144
+constexpr int kDecHidden = 9216;
+constexpr int kDecWindow = 8192;
+constexpr int kVocab = 131072;
+constexpr int kEncDim = 1280;
+constexpr int kEncLayers = 32;
+constexpr int kEncHeads = 32;
+constexpr int kEncHeadDim = 64;
+constexpr int kEncQkv = kEncHeads * kEncHeadDim; // 2048
+constexpr int kEncHidden = 5120;
+constexpr int kEncWindow = 750;
+constexpr float kNormEps = 1e-5f;
+constexpr float kRopeTheta = 1.0e6f;
+constexpr int kMaxBatch = 8;                     // streams per batched decode step
+
+// bf16 -> f32 is a 16-bit left shift (voxtral_kernels.c:124-128).
+__device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
+
+// Streaming 16-byte load of read-only weights: no L1 allocation, L2
+// evict-first so the weight stream does not push the KV cache and the
+// activations out of L2.
+__device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t policy) {
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p), "l"(policy));
+    return r;
+}
+
+__device__ __forceinline__ uint64_t make_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ uint64_t make_evict_last_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// 8 bf16 weights (one uint4) dotted with 8 fp32 activations, fp32 FMA in
+// index order.
+__device__ __forceinline__ float dot8(uint4 w, float4 a, float4 b, float acc) {
+    acc = fmaf(bf16lo(w.x), a.x, acc);
+    acc = fmaf(bf16hi(w.x), a.y, acc);
+    acc = fmaf(bf16lo(w.y), a.z, acc);
+    acc = fmaf(bf16hi(w.y), a.w, acc);
+    acc = fmaf(bf16lo(w.z), b.x, acc);
+    acc = fmaf(bf16hi(w.z), b.y, acc);
+    acc = fmaf(bf16lo(w.w), b.z, acc);
+    acc = fmaf(bf16hi(w.w), b.w, acc);
+    return acc;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Programmatic dependent launch: wait for the preceding kernel in the stream
+// (no-op when launched without the attribute) / allow the next one to start.
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace vc

@@ -1,0 +1,82 @@
+// vc_internal.h - internal (C++) interfaces between the runtime and kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace vc {
+
+// One stream's view of its KV ring for one decode step.  Device memory; the
+// runtime fills it before every step.
+struct StreamSlot {
+    float *k_ring;    // K ring, layer 0 base: [n_layers][cap][1024] fp32
+    float *v_ring;    // V ring, same layout
+    int cap;          // positions per layer
+    int pos;          // logical position of this step's row
+    int slot;         // pos % cap
+    int n_keys;       // keys attended: min(pos + 1, window)
+};
+
+enum GemvEpi : int {
+    EPI_STORE = 0,    // y = acc (+ bias)
+    EPI_ADD = 1,      // y += acc (+ bias)        (residual add)
+    EPI_QKV = 2,      // q (RoPE) / k (RoPE, ring write) / v (ring write)
+    EPI_SWIGLU = 3,   // rows (2i, 2i+1) = (gate_i, up_i) -> h_i = silu(g) * u
+    EPI_LOGITS = 4,   // y = acc, plus argmax across the whole launch
+};
+
+struct ArgmaxPartial {
+    float v;
+    int i;
+};
+
+struct GemvParams {
+    const uint16_t *W;      // [N, K] bf16 row-major
+    int N, K;
+    const float *x;         // [M, ldx] fp32 (device)
+    int ldx;
+    const float *norm_w;    // RMSNorm prologue weight [K] or NULL
+    const float *ada;       // (1 + ada) after the norm [K] or NULL
+    float *y;               // output [M, ldy]
+    int ldy;
+    const float *bias;      // [N] or NULL
+    // EPI_QKV
+    const StreamSlot *slots;  // [M]
+    const float *rope;        // [M][128]: (cos, sin) pairs for the step's position
+    int layer;
+    // EPI_LOGITS
+    ArgmaxPartial *partials;  // [gridDim.x * M]
+    unsigned *counter;        // 1 counter, zero between launches
+    int *tokens;              // [M]
+};
+
+// Launch the fused streaming GEMV (M = 1..8 activation rows).
+cudaError_t launch_gemv(int M, int epi, const GemvParams &p, cudaStream_t st, bool pdl);
+int gemv_grid(int M, int epi, int N);
+
+struct AttnParams {
+    const float *q;           // [M][4096], RoPE applied
+    const StreamSlot *slots;  // [M]
+    int layer;
+    float *out;               // [M][4096]
+    float *part_o;            // [M][32][S][128]
+    float *part_ml;           // [M][32][S][2]
+    unsigned *counters;       // [M][8], zero between launches
+    int S;                    // key splits per KV head
+};
+constexpr int kAttnSplits = 32;
+
+cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl);
+
+// Alternatives from device logits (stream_fill_alts semantics).
+cudaError_t launch_fill_alts(const float *logits, int vocab, const int *best, int n_alt,
+                             float cutoff, int *out_ids, cudaStream_t st);
+
+cudaError_t launch_rope(float *x, int n_heads, int head_dim, const float *cs, cudaStream_t st);
+cudaError_t launch_fill_normal_bf16(uint16_t *dst, size_t n, uint64_t seed, float std,
+                                    cudaStream_t st);
+cudaError_t launch_interleave_rows(uint16_t *dst, const uint16_t *a, const uint16_t *b,
+                                   int rows, int cols, cudaStream_t st);
+
+}  // namespace vc

@@ -1,0 +1,1249 @@
+// vc_runtime.cu - the C ABI of voxtral_cuda.h: device contexts, the
+// pointer-keyed weight cache, the resident decoder (fused weight layout), the
+// per-stream KV ring, and the decode / prefill / batched steps (enqueued as
+// one CUDA graph of programmatic-dependent launches per step shape).
+#include "voxtral_cuda.h"
+
+#include "vc_common.cuh"
+#include "vc_internal.h"
+
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+using namespace vc;
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+
+static thread_local char t_err[512] = "";
+
+static void set_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof(t_err), fmt, ap);
+    va_end(ap);
+}
+
+#define VC_TRY(call)                                                                  \
+    do {                                                                              \
+        cudaError_t e_ = (call);                                                      \
+        if (e_ != cudaSuccess) {                                                      \
+            set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
+                      __LINE__);                                                      \
+            return VOX_CUDA_ERR_CUDA;                                                 \
+        }                                                                             \
+    } while (0)
+
+#define VC_TRY_NULL(call)                                                             \
+    do {                                                                              \
+        cudaError_t e_ = (call);                                                      \
+        if (e_ != cudaSuccess) {                                                      \
+            set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
+                      __LINE__);                                                      \
+            return nullptr;                                                           \
+        }                                                                             \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// per-device context
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr int kMaxDevices = 16;
+
+struct DevCtx {
+    int device = -1;
+    bool ready = false;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;                  // guards the cache and the scratch below
+    size_t bytes = 0;               // device bytes held by the library
+    std::unordered_map<const void *, void *> wcache;   // host weight ptr -> device copy
+    std::unordered_map<const void *, size_t> wcache_n; // host weight ptr -> elements
+    // scratch for the host-pointer matmul entry and the kernel-level entries
+    float *sx = nullptr, *sy = nullptr, *sb = nullptr;
+    size_t sx_n = 0, sy_n = 0, sb_n = 0;
+    StreamSlot *attn_slot = nullptr;
+    float *attn_part_o = nullptr, *attn_part_ml = nullptr, *rope_tab = nullptr;
+    unsigned *attn_counters = nullptr;
+};
+
+DevCtx g_dev[kMaxDevices];
+std::mutex g_init_mu;
+thread_local int t_device = -1;
+
+int current_device() {
+    if (t_device >= 0) return t_device;
+    const char *e = getenv("VOX_CUDA_DEVICE");
+    return e ? atoi(e) : 0;
+}
+
+DevCtx *ctx_for(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) return nullptr;
+    DevCtx *c = &g_dev[dev];
+    return c->ready ? c : nullptr;
+}
+
+DevCtx *cur_ctx() {
+    DevCtx *c = ctx_for(current_device());
+    if (!c) set_error("vox_cuda_init has not succeeded on device %d", current_device());
+    return c;
+}
+
+cudaError_t dev_alloc(DevCtx *c, void **p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e == cudaSuccess) {
+        std::lock_guard<std::mutex> lk(c->mu);
+        c->bytes += bytes;
+    }
+    return e;
+}
+
+void dev_free(DevCtx *c, void *p, size_t bytes) {
+    if (!p) return;
+    cudaFree(p);
+    std::lock_guard<std::mutex> lk(c->mu);
+    c->bytes -= bytes;
+}
+
+// Host RoPE table for one logical position, the same formula as
+// vox_compute_rope_freqs (voxtral_kernels.c:488-500).
+void host_rope_table(int pos, int head_dim, float *cs) {
+    const float p = (float)pos;
+    for (int d = 0; d < head_dim / 2; d++) {
+        const float f = 1.0f / powf(kRopeTheta, (float)(2 * d) / (float)head_dim);
+        const float a = p * f;
+        cs[2 * d] = cosf(a);
+        cs[2 * d + 1] = sinf(a);
+    }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// lifecycle
+// ---------------------------------------------------------------------------
+
+extern "C" int vox_cuda_set_device(int device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n || device >= kMaxDevices) {
+        set_error("vox_cuda_set_device: no device %d", device);
+        return VOX_CUDA_ERR_ARG;
+    }
+    t_device = device;
+    VC_TRY(cudaSetDevice(device));
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_init(void) {
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error("vox_cuda_init: bad device %d", dev);
+        return 0;
+    }
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    DevCtx *c = &g_dev[dev];
+    if (c->ready) {
+        cudaSetDevice(dev);
+        return 1;
+    }
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || dev >= n) {
+        set_error("vox_cuda_init: no CUDA device %d", dev);
+        return 0;
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10) {
+        set_error("vox_cuda_init: device %d is not an sm_100 (Blackwell) GPU", dev);
+        return 0;
+    }
+    if (cudaSetDevice(dev) != cudaSuccess) {
+        set_error("vox_cuda_init: cudaSetDevice(%d) failed", dev);
+        return 0;
+    }
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        set_error("vox_cuda_init: stream creation failed");
+        return 0;
+    }
+    c->device = dev;
+    c->ready = true;
+    t_device = dev;
+    return 1;
+}
+
+extern "C" int vox_cuda_available(void) {
+    return ctx_for(current_device()) != nullptr ? 1 : 0;
+}
+
+extern "C" const char *vox_cuda_last_error(void) { return t_err; }
+
+extern "C" size_t vox_cuda_memory_used(void) {
+    DevCtx *c = ctx_for(current_device());
+    if (!c) return 0;
+    std::lock_guard<std::mutex> lk(c->mu);
+    return c->bytes;
+}
+
+static void release_scratch(DevCtx *c) {
+    cudaFree(c->sx);
+    cudaFree(c->sy);
+    cudaFree(c->sb);
+    cudaFree(c->attn_slot);
+    cudaFree(c->attn_part_o);
+    cudaFree(c->attn_part_ml);
+    cudaFree(c->attn_counters);
+    cudaFree(c->rope_tab);
+    c->sx = c->sy = c->sb = nullptr;
+    c->sx_n = c->sy_n = c->sb_n = 0;
+    c->attn_slot = nullptr;
+    c->attn_part_o = c->attn_part_ml = c->rope_tab = nullptr;
+    c->attn_counters = nullptr;
+}
+
+extern "C" void vox_cuda_shutdown(void) {
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    for (int d = 0; d < kMaxDevices; d++) {
+        DevCtx *c = &g_dev[d];
+        if (!c->ready) continue;
+        cudaSetDevice(d);
+        cudaStreamSynchronize(c->stream);
+        for (auto &kv : c->wcache) cudaFree(kv.second);
+        c->wcache.clear();
+        c->wcache_n.clear();
+        release_scratch(c);
+        cudaStreamDestroy(c->stream);
+        c->stream = nullptr;
+        c->bytes = 0;
+        c->ready = false;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// (1) matmul entry points
+// ---------------------------------------------------------------------------
+
+static int check_linear_args(int M, int N, int K, const void *A, const void *B, const void *C) {
+    if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) {
+        set_error("linear: bad arguments (M=%d N=%d K=%d)", M, N, K);
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (K % 8 != 0) {
+        set_error("linear: K=%d must be a multiple of 8 (16-byte weight rows)", K);
+        return VOX_CUDA_ERR_ARG;
+    }
+    return VOX_CUDA_OK;
+}
+
+// y[M,N] = x[M,K] W^T (+b), all device pointers; rows of x in chunks of 8.
+static int enqueue_linear(int M, int N, int K, const float *x, const uint16_t *W, const float *b,
+                          float *y, cudaStream_t st) {
+    for (int m0 = 0; m0 < M; m0 += kMaxBatch) {
+        const int mm = (M - m0 < kMaxBatch) ? (M - m0) : kMaxBatch;
+        GemvParams p = {};
+        p.W = W;
+        p.N = N;
+        p.K = K;
+        p.x = x + (size_t)m0 * K;
+        p.ldx = K;
+        p.y = y + (size_t)m0 * N;
+        p.ldy = N;
+        p.bias = b;
+        VC_TRY(launch_gemv(mm, EPI_STORE, p, st, false));
+    }
+    return VOX_CUDA_OK;
+}
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+extern "C" int vox_cuda_linear_bf16_dev(int M, int N, int K, const float *A, const uint16_t *B_bf16,
+                                        const float *bias, float *C, void *stream) {
+    int rc = check_linear_args(M, N, K, A, B_bf16, C);
+    if (rc) return rc;
+    if (!aligned16(A) || !aligned16(B_bf16)) {
+        set_error("linear_dev: A and B must be 16-byte aligned device pointers");
+        return VOX_CUDA_ERR_ARG;
+    }
+    DevCtx *c = cur_ctx();
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    return enqueue_linear(M, N, K, A, B_bf16, bias, C, st);
+}
+
+static const uint16_t *cached_weight(DevCtx *c, const uint16_t *host, size_t n, int *rc) {
+    {
+        std::lock_guard<std::mutex> lk(c->mu);
+        auto it = c->wcache.find(host);
+        if (it != c->wcache.end() && c->wcache_n[host] >= n) return (const uint16_t *)it->second;
+    }
+    void *d = nullptr;
+    cudaError_t e = dev_alloc(c, &d, n * sizeof(uint16_t));
+    if (e != cudaSuccess) {
+        set_error("weight cache: cudaMalloc(%zu) failed: %s", n * 2, cudaGetErrorString(e));
+        *rc = VOX_CUDA_ERR_OOM;
+        return nullptr;
+    }
+    e = cudaMemcpy(d, host, n * sizeof(uint16_t), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        set_error("weight cache: upload failed: %s", cudaGetErrorString(e));
+        dev_free(c, d, n * 2);
+        *rc = VOX_CUDA_ERR_CUDA;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(c->mu);
+    auto it = c->wcache.find(host);
+    if (it != c->wcache.end()) {  // replaced by a larger upload of the same pointer
+        c->bytes -= c->wcache_n[host] * 2;
+        cudaFree(it->second);
+    }
+    c->wcache[host] = d;
+    c->wcache_n[host] = n;
+    return (const uint16_t *)d;
+}
+
+extern "C" int vox_cuda_warmup_bf16(const uint16_t *B_bf16, size_t num_elements) {
+    DevCtx *c = cur_ctx();
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    if (!B_bf16 || num_elements == 0) {
+        set_error("warmup: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    int rc = VOX_CUDA_OK;
+    return cached_weight(c, B_bf16, num_elements, &rc) ? VOX_CUDA_OK : rc;
+}
+
+extern "C" int vox_cuda_sgemm_bf16(int M, int N, int K, const float *A, const uint16_t *B_bf16,
+                                   const float *bias, float *C) {
+    int rc = check_linear_args(M, N, K, A, B_bf16, C);
+    if (rc) return rc;
+    DevCtx *c = cur_ctx();
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    const uint16_t *W = cached_weight(c, B_bf16, (size_t)N * K, &rc);
+    if (!W) return rc;
+    std::lock_guard<std::mutex> lk(c->mu);  // one user of the host-path scratch at a time
+    // (dev_alloc takes the same mutex: allocate through grow_locked below)
+    auto grow_locked = [&](float **p, size_t *cap, size_t n) -> int {
+        if (*cap >= n) return VOX_CUDA_OK;
+        if (*p) {
+            cudaFree(*p);
+            c->bytes -= *cap * sizeof(float);
+        }
+        *p = nullptr;
+        *cap = 0;
+        if (cudaMalloc((void **)p, n * sizeof(float)) != cudaSuccess) {
+            set_error("scratch: cudaMalloc(%zu) failed", n * 4);
+            return VOX_CUDA_ERR_OOM;
+        }
+        c->bytes += n * sizeof(float);
+        *cap = n;
+        return VOX_CUDA_OK;
+    };
+    if ((rc = grow_locked(&c->sx, &c->sx_n, (size_t)M * K))) return rc;
+    if ((rc = grow_locked(&c->sy, &c->sy_n, (size_t)M * N))) return rc;
+    if (bias && (rc = grow_locked(&c->sb, &c->sb_n, (size_t)N))) return rc;
+    VC_TRY(cudaMemcpyAsync(c->sx, A, (size_t)M * K * 4, cudaMemcpyHostToDevice, c->stream));
+    if (bias) VC_TRY(cudaMemcpyAsync(c->sb, bias, (size_t)N * 4, cudaMemcpyHostToDevice, c->stream));
+    rc = enqueue_linear(M, N, K, c->sx, W, bias ? c->sb : nullptr, c->sy, c->stream);
+    if (rc) return rc;
+    VC_TRY(cudaMemcpyAsync(C, c->sy, (size_t)M * N * 4, cudaMemcpyDeviceToHost, c->stream));
+    VC_TRY(cudaStreamSynchronize(c->stream));
+    return VOX_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// kernel-level entries
+// ---------------------------------------------------------------------------
+
+static int ensure_attn_scratch(DevCtx *c) {
+    if (c->attn_slot) return VOX_CUDA_OK;
+    const size_t np = (size_t)kDecHeads * kAttnSplits;
+    if (cudaMalloc(&c->attn_slot, sizeof(StreamSlot)) != cudaSuccess ||
+        cudaMalloc(&c->attn_part_o, np * kHeadDim * 4) != cudaSuccess ||
+        cudaMalloc(&c->attn_part_ml, np * 2 * 4) != cudaSuccess ||
+        cudaMalloc(&c->attn_counters, kDecKvHeads * 4) != cudaSuccess ||
+        cudaMalloc(&c->rope_tab, 512 * 4) != cudaSuccess) {
+        set_error("attention scratch allocation failed");
+        return VOX_CUDA_ERR_OOM;
+    }
+    c->bytes += sizeof(StreamSlot) + np * kHeadDim * 4 + np * 8 + kDecKvHeads * 4 + 2048;
+    VC_TRY(cudaMemset(c->attn_counters, 0, kDecKvHeads * 4));
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_attention_decode_dev(const float *q, const float *k_ring,
+                                             const float *v_ring, int kv_cap, int pos, float *out,
+                                             void *stream) {
+    if (!q || !k_ring || !v_ring || !out || kv_cap <= 0 || pos < 0) {
+        set_error("attention_decode: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (!aligned16(q) || !aligned16(k_ring) || !aligned16(v_ring) || !aligned16(out)) {
+        set_error("attention_decode: q, k_ring, v_ring and out must be 16-byte aligned");
+        return VOX_CUDA_ERR_ARG;
+    }
+    const int n_keys = (pos + 1 < kDecWindow) ? pos + 1 : kDecWindow;
+    if (n_keys > kv_cap) {
+        set_error("attention_decode: ring of %d positions cannot hold %d keys", kv_cap, n_keys);
+        return VOX_CUDA_ERR_CAPACITY;
+    }
+    DevCtx *c = cur_ctx();
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    std::lock_guard<std::mutex> lk(c->mu);
+    int rc = ensure_attn_scratch(c);
+    if (rc) return rc;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    StreamSlot h = {const_cast<float *>(k_ring), const_cast<float *>(v_ring), kv_cap, pos,
+                    pos % kv_cap, n_keys};
+    // the slot descriptor is copied through a stream-ordered memcpy so that
+    // back-to-back calls on one stream do not race on it
+    VC_TRY(cudaMemcpyAsync(c->attn_slot, &h, sizeof(h), cudaMemcpyHostToDevice, st));
+    AttnParams p = {};
+    p.q = q;
+    p.slots = c->attn_slot;
+    p.layer = 0;
+    p.out = out;
+    p.part_o = c->attn_part_o;
+    p.part_ml = c->attn_part_ml;
+    p.counters = c->attn_counters;
+    p.S = kAttnSplits;
+    VC_TRY(launch_attn_decode(1, p, st, false));
+    VC_TRY(cudaStreamSynchronize(st));  // h lives on this stack frame
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_rope_dev(float *x, int n_heads, int head_dim, int pos,
+                                 const float *rope_freqs, void *stream) {
+    if (!x || n_heads <= 0 || head_dim <= 0 || head_dim > 512 || (head_dim & 1) || pos < 0) {
+        set_error("rope: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    DevCtx *c = cur_ctx();
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    if (rope_freqs) {
+        VC_TRY(launch_rope(x, n_heads, head_dim, rope_freqs, st));
+        return VOX_CUDA_OK;
+    }
+    std::lock_guard<std::mutex> lk(c->mu);
+    int rc = ensure_attn_scratch(c);
+    if (rc) return rc;
+    float tab[512];
+    host_rope_table(pos, head_dim, tab);
+    VC_TRY(cudaMemcpyAsync(c->rope_tab, tab, head_dim * 4, cudaMemcpyHostToDevice, st));
+    VC_TRY(launch_rope(x, n_heads, head_dim, c->rope_tab, st));
+    VC_TRY(cudaStreamSynchronize(st));
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_fill_normal_bf16_dev(uint16_t *dst, size_t n, uint64_t seed, float std,
+                                             void *stream) {
+    if (!dst) {
+        set_error("fill_normal: NULL destination");
+        return VOX_CUDA_ERR_ARG;
+    }
+    DevCtx *c = cur_ctx();
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    VC_TRY(launch_fill_normal_bf16(dst, n, seed, std, st));
+    return VOX_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// decoder
+// ---------------------------------------------------------------------------
+
+namespace {
+
+struct DecLayer {
+    const uint16_t *qkv, *wo, *w13, *w2;   // fused device layout
+    const float *attn_norm, *ffn_norm, *ada;
+};
+
+// Device workspace for one step shape (n rows).  The host staging block is
+// pinned; its layout mirrors the device block it is copied to.
+struct StepWork {
+    int n = 0;
+    int vocab = 0;
+    // device
+    char *dblock = nullptr;            // [slots | rope | embeds] uploaded per step
+    size_t dblock_bytes = 0;
+    StreamSlot *slots = nullptr;
+    float *rope = nullptr;             // [n][128]
+    float *x = nullptr;                // [n][3072] residual stream
+    float *q = nullptr, *att = nullptr;  // [n][4096]
+    float *h = nullptr;                // [n][9216]
+    float *logits = nullptr;           // [n][vocab]
+    float *part_o = nullptr, *part_ml = nullptr;
+    unsigned *counters = nullptr;      // attention [n][8] + argmax [1]
+    ArgmaxPartial *amax = nullptr;
+    int *tokens = nullptr;             // [n]
+    int *alt_ids = nullptr;            // [4]
+    size_t bytes = 0;
+    // host (pinned)
+    char *hblock = nullptr;
+    int *h_tokens = nullptr;
+    // graphs: [0] layers only (prefill), [1] layers + LM head
+    cudaGraphExec_t graph[2] = {nullptr, nullptr};
+};
+
+}  // namespace
+
+struct vox_cuda_decoder {
+    int device = 0;
+    int n_layers = 0;
+    int vocab = 0;
+    DecLayer L[kDecLayersMax];
+    const uint16_t *tok_emb = nullptr;
+    const float *norm = nullptr;
+    std::vector<std::pair<void *, size_t>> owned;
+    StepWork *batch_work[kMaxBatch + 1] = {};
+    std::mutex mu;   // serialises batched steps (they share batch_work)
+    bool pdl = true;
+};
+
+struct vox_cuda_dec_state {
+    vox_cuda_decoder *dec = nullptr;
+    int cap = 0;
+    int pos = 0;                       // logical position of the next row
+    float *k_ring = nullptr, *v_ring = nullptr;
+    size_t ring_bytes = 0;
+    StepWork *work = nullptr;          // single-stream workspace (n = 1)
+    StepWork *prefill_work = nullptr;  // n = 8 workspace for prefill chunks
+    int last_token = -1;
+    bool have_logits = false;
+};
+
+namespace {
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+void free_work(DevCtx *c, StepWork *w) {
+    if (!w) return;
+    for (auto &g : w->graph)
+        if (g) cudaGraphExecDestroy(g);
+    if (w->dblock) cudaFree(w->dblock);
+    if (w->hblock) cudaFreeHost(w->hblock);
+    if (c) {
+        std::lock_guard<std::mutex> lk(c->mu);
+        c->bytes -= w->bytes;
+    }
+    delete w;
+}
+
+StepWork *make_work(DevCtx *c, int n, int vocab) {
+    StepWork *w = new StepWork();
+    w->n = n;
+    w->vocab = vocab;
+    const size_t S = kAttnSplits;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const size_t o_slots = take(sizeof(StreamSlot) * n);
+    const size_t o_rope = take(sizeof(float) * n * kHeadDim);
+    const size_t o_x = take(sizeof(float) * n * kDecDim);
+    w->dblock_bytes = o_x + sizeof(float) * n * kDecDim;   // the uploaded prefix
+    const size_t o_q = take(sizeof(float) * n * kQDim);
+    const size_t o_att = take(sizeof(float) * n * kQDim);
+    const size_t o_h = take(sizeof(float) * n * kDecHidden);
+    const size_t o_logits = take(sizeof(float) * n * (size_t)vocab);
+    const size_t o_po = take(sizeof(float) * n * kDecHeads * S * kHeadDim);
+    const size_t o_pml = take(sizeof(float) * n * kDecHeads * S * 2);
+    const size_t o_cnt = take(sizeof(unsigned) * (n * kDecKvHeads + 1));
+    const size_t grid = (size_t)gemv_grid(n, EPI_LOGITS, vocab);
+    const size_t o_amax = take(sizeof(ArgmaxPartial) * grid * n);
+    const size_t o_tok = take(sizeof(int) * n);
+    const size_t o_alt = take(sizeof(int) * 4);
+    if (dev_alloc(c, (void **)&w->dblock, off) != cudaSuccess) {
+        set_error("decoder workspace: cudaMalloc(%zu) failed", off);
+        delete w;
+        return nullptr;
+    }
+    w->bytes = off;
+    char *b = w->dblock;
+    w->slots = (StreamSlot *)(b + o_slots);
+    w->rope = (float *)(b + o_rope);
+    w->x = (float *)(b + o_x);
+    w->q = (float *)(b + o_q);
+    w->att = (float *)(b + o_att);
+    w->h = (float *)(b + o_h);
+    w->logits = (float *)(b + o_logits);
+    w->part_o = (float *)(b + o_po);
+    w->part_ml = (float *)(b + o_pml);
+    w->counters = (unsigned *)(b + o_cnt);
+    w->amax = (ArgmaxPartial *)(b + o_amax);
+    w->tokens = (int *)(b + o_tok);
+    w->alt_ids = (int *)(b + o_alt);
+    if (cudaMemset(w->counters, 0, sizeof(unsigned) * (n * kDecKvHeads + 1)) != cudaSuccess ||
+        cudaHostAlloc((void **)&w->hblock, w->dblock_bytes + 64, cudaHostAllocDefault) != cudaSuccess) {
+        set_error("decoder workspace: staging allocation failed");
+        free_work(c, w);
+        return nullptr;
+    }
+    w->h_tokens = (int *)(w->hblock + align_up(w->dblock_bytes, 16));
+    return w;
+}
+
+// host-side views of the staging block
+StreamSlot *h_slots(StepWork *w) { return (StreamSlot *)w->hblock; }
+float *h_rope(StepWork *w) { return (float *)(w->hblock + ((char *)w->rope - w->dblock)); }
+float *h_x(StepWork *w) { return (float *)(w->hblock + ((char *)w->x - w->dblock)); }
+
+// The kernel sequence of one step over w->n rows (decoder layers, then the
+// LM head + argmax when with_head).
+// evs (profiling only): 2 events per launch, recorded around it.
+int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_t st,
+                   cudaEvent_t *evs = nullptr) {
+    const int n = w->n;
+    const bool pdl = d->pdl && evs == nullptr;
+    int ei = 0;
+#define VC_EV_BEGIN() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
+#define VC_EV_END() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
+    for (int l = 0; l < d->n_layers; l++) {
+        const DecLayer &L = d->L[l];
+        GemvParams p = {};
+        // q|k|v = rms_norm(x) Wqkv^T, RoPE, ring write
+        p.W = L.qkv;
+        p.N = kQkvRows;
+        p.K = kDecDim;
+        p.x = w->x;
+        p.ldx = kDecDim;
+        p.norm_w = L.attn_norm;
+        p.y = w->q;
+        p.ldy = kQDim;
+        p.slots = w->slots;
+        p.rope = w->rope;
+        p.layer = l;
+        VC_EV_BEGIN();
+        VC_TRY(launch_gemv(n, EPI_QKV, p, st, pdl));
+        VC_EV_END();
+        // attention over the ring
+        AttnParams a = {};
+        a.q = w->q;
+        a.slots = w->slots;
+        a.layer = l;
+        a.out = w->att;
+        a.part_o = w->part_o;
+        a.part_ml = w->part_ml;
+        a.counters = w->counters;
+        a.S = kAttnSplits;
+        VC_EV_BEGIN();
+        VC_TRY(launch_attn_decode(n, a, st, pdl));
+        VC_EV_END();
+        // x += att Wo^T
+        p = GemvParams{};
+        p.W = L.wo;
+        p.N = kDecDim;
+        p.K = kQDim;
+        p.x = w->att;
+        p.ldx = kQDim;
+        p.y = w->x;
+        p.ldy = kDecDim;
+        VC_EV_BEGIN();
+        VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
+        VC_EV_END();
+        // h = silu(xn W1^T) * (xn W3^T), xn = rms_norm(x) * (1 + ada)
+        p = GemvParams{};
+        p.W = L.w13;
+        p.N = 2 * kDecHidden;
+        p.K = kDecDim;
+        p.x = w->x;
+        p.ldx = kDecDim;
+        p.norm_w = L.ffn_norm;
+        p.ada = L.ada;
+        p.y = w->h;
+        p.ldy = kDecHidden;
+        VC_EV_BEGIN();
+        VC_TRY(launch_gemv(n, EPI_SWIGLU, p, st, pdl));
+        VC_EV_END();
+        // x += h W2^T
+        p = GemvParams{};
+        p.W = L.w2;
+        p.N = kDecDim;
+        p.K = kDecHidden;
+        p.x = w->h;
+        p.ldx = kDecHidden;
+        p.y = w->x;
+        p.ldy = kDecDim;
+        VC_EV_BEGIN();
+        VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
+        VC_EV_END();
+    }
+    if (with_head) {
+        GemvParams p = {};
+        p.W = d->tok_emb;
+        p.N = d->vocab;
+        p.K = kDecDim;
+        p.x = w->x;
+        p.ldx = kDecDim;
+        p.norm_w = d->norm;
+        p.y = w->logits;
+        p.ldy = d->vocab;
+        p.partials = w->amax;
+        p.counter = w->counters + n * kDecKvHeads;
+        p.tokens = w->tokens;
+        VC_EV_BEGIN();
+        VC_TRY(launch_gemv(n, EPI_LOGITS, p, st, pdl));
+        VC_EV_END();
+    }
+#undef VC_EV_BEGIN
+#undef VC_EV_END
+    return VOX_CUDA_OK;
+}
+
+// Upload the staged step inputs, run the (captured) kernel sequence, fetch
+// the tokens.
+int run_step(vox_cuda_decoder *d, DevCtx *c, StepWork *w, bool with_head, cudaStream_t st,
+             bool sync) {
+    VC_TRY(cudaMemcpyAsync(w->dblock, w->hblock, w->dblock_bytes, cudaMemcpyHostToDevice, st));
+    cudaGraphExec_t &g = w->graph[with_head ? 1 : 0];
+    if (!g) {
+        cudaGraph_t graph = nullptr;
+        VC_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue_layers(d, w, with_head, st);
+        cudaError_t e = cudaStreamEndCapture(st, &graph);
+        if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        VC_TRY(e);
+        e = cudaGraphInstantiate(&g, graph, 0);
+        cudaGraphDestroy(graph);
+        VC_TRY(e);
+    }
+    VC_TRY(cudaGraphLaunch(g, st));
+    if (with_head)
+        VC_TRY(cudaMemcpyAsync(w->h_tokens, w->tokens, sizeof(int) * w->n, cudaMemcpyDeviceToHost, st));
+    if (sync) VC_TRY(cudaStreamSynchronize(st));
+    (void)c;
+    return VOX_CUDA_OK;
+}
+
+void fill_slot(vox_cuda_dec_state *s, int pos, StreamSlot *slot) {
+    slot->k_ring = s->k_ring;
+    slot->v_ring = s->v_ring;
+    slot->cap = s->cap;
+    slot->pos = pos;
+    slot->slot = pos % s->cap;
+    slot->n_keys = (pos + 1 < kDecWindow) ? pos + 1 : kDecWindow;
+}
+
+// Rows first..last are written in one launch: the ring must hold, at once,
+// the window of the first row and every later row of the launch.
+int check_capacity(const vox_cuda_dec_state *s, int first, int last) {
+    const int oldest = (first - kDecWindow + 1 > 0) ? first - kDecWindow + 1 : 0;
+    const int span = last - oldest + 1;
+    if (span > s->cap) {
+        set_error("KV ring of %d positions cannot hold %d positions (%d..%d)", s->cap, span,
+                  oldest, last);
+        return VOX_CUDA_ERR_CAPACITY;
+    }
+    return VOX_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights *w) {
+    DevCtx *c = cur_ctx();
+    if (!c) return nullptr;
+    if (!w || w->n_layers <= 0 || w->n_layers > kDecLayersMax || w->vocab <= 0 ||
+        !w->tok_embeddings || !w->norm) {
+        set_error("decoder_create: bad weight descriptor");
+        return nullptr;
+    }
+    for (int l = 0; l < w->n_layers; l++) {
+        const vox_cuda_dec_layer_weights &L = w->layers[l];
+        if (!L.wq || !L.wk || !L.wv || !L.wo || !L.w1 || !L.w2 || !L.w3 || !L.attention_norm ||
+            !L.ffn_norm) {
+            set_error("decoder_create: layer %d has a NULL weight", l);
+            return nullptr;
+        }
+    }
+    vox_cuda_decoder *d = new vox_cuda_decoder();
+    d->device = c->device;
+    d->n_layers = w->n_layers;
+    d->vocab = w->vocab;
+    const char *pdl_env = getenv("VOX_CUDA_PDL");
+    d->pdl = !(pdl_env && pdl_env[0] == '0');
+    const cudaMemcpyKind kind = w->weights_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    auto alloc = [&](size_t bytes) -> void * {
+        void *p = nullptr;
+        if (dev_alloc(c, &p, bytes) != cudaSuccess) return nullptr;
+        d->owned.push_back({p, bytes});
+        return p;
+    };
+    // Weights shared between layers (aliased host pointers) are laid out once.
+    std::unordered_map<const void *, const void *> seen;
+    bool ok = true;
+    const size_t D = kDecDim;
+    for (int l = 0; l < w->n_layers && ok; l++) {
+        const vox_cuda_dec_layer_weights &L = w->layers[l];
+        DecLayer &o = d->L[l];
+        auto it = seen.find(L.wq);
+        if (it != seen.end() && seen.count(L.w1) && seen.count(L.wo) && seen.count(L.w2)) {
+            // same host tensors as an earlier layer: reuse its fused copies
+            for (int j = 0; j < l; j++)
+                if (w->layers[j].wq == L.wq && w->layers[j].wk == L.wk && w->layers[j].wv == L.wv &&
+                    w->layers[j].wo == L.wo && w->layers[j].w1 == L.w1 && w->layers[j].w2 == L.w2 &&
+                    w->layers[j].w3 == L.w3) {
+                    o.qkv = d->L[j].qkv;
+                    o.wo = d->L[j].wo;
+                    o.w13 = d->L[j].w13;
+                    o.w2 = d->L[j].w2;
+                    break;
+                }
+        }
+        if (!o.qkv) {
+            uint16_t *qkv = (uint16_t *)alloc((size_t)kQkvRows * D * 2);
+            uint16_t *wo = (uint16_t *)alloc((size_t)D * kQDim * 2);
+            uint16_t *w13 = (uint16_t *)alloc((size_t)2 * kDecHidden * D * 2);
+            uint16_t *w2 = (uint16_t *)alloc((size_t)D * kDecHidden * 2);
+            if (!qkv || !wo || !w13 || !w2) {
+                ok = false;
+                break;
+            }
+            // wq | wk | wv concatenated by rows
+            ok &= cudaMemcpy(qkv, L.wq, (size_t)kQDim * D * 2, kind) == cudaSuccess;
+            ok &= cudaMemcpy(qkv + (size_t)kQDim * D, L.wk, (size_t)kKvDim * D * 2, kind) == cudaSuccess;
+            ok &= cudaMemcpy(qkv + (size_t)(kQDim + kKvDim) * D, L.wv, (size_t)kKvDim * D * 2, kind) ==
+                  cudaSuccess;
+            ok &= cudaMemcpy(wo, L.wo, (size_t)D * kQDim * 2, kind) == cudaSuccess;
+            // w1 / w3 row-interleaved: row 2i = w1[i], row 2i+1 = w3[i]
+            ok &= cudaMemcpy2D(w13, 2 * D * 2, L.w1, D * 2, D * 2, kDecHidden, kind) == cudaSuccess;
+            ok &= cudaMemcpy2D(w13 + D, 2 * D * 2, L.w3, D * 2, D * 2, kDecHidden, kind) == cudaSuccess;
+            ok &= cudaMemcpy(w2, L.w2, (size_t)D * kDecHidden * 2, kind) == cudaSuccess;
+            o.qkv = qkv;
+            o.wo = wo;
+            o.w13 = w13;
+            o.w2 = w2;
+            seen[L.wq] = qkv;
+            seen[L.w1] = w13;
+            seen[L.wo] = wo;
+            seen[L.w2] = w2;
+        }
+        float *norms = (float *)alloc(3 * D * 4);
+        if (!norms) {
+            ok = false;
+            break;
+        }
+        ok &= cudaMemcpy(norms, L.attention_norm, D * 4, kind) == cudaSuccess;
+        ok &= cudaMemcpy(norms + D, L.ffn_norm, D * 4, kind) == cudaSuccess;
+        o.attn_norm = norms;
+        o.ffn_norm = norms + D;
+        if (w->ada_scale) {
+            ok &= cudaMemcpy(norms + 2 * D, w->ada_scale + (size_t)l * D, D * 4, kind) == cudaSuccess;
+            o.ada = norms + 2 * D;
+        } else {
+            o.ada = nullptr;
+        }
+    }
+    if (ok) {
+        uint16_t *emb = (uint16_t *)alloc((size_t)w->vocab * D * 2);
+        float *nrm = (float *)alloc(D * 4);
+        ok = emb && nrm;
+        if (ok) {
+            ok &= cudaMemcpy(emb, w->tok_embeddings, (size_t)w->vocab * D * 2, kind) == cudaSuccess;
+            ok &= cudaMemcpy(nrm, w->norm, D * 4, kind) == cudaSuccess;
+            d->tok_emb = emb;
+            d->norm = nrm;
+        }
+    }
+    if (!ok) {
+        if (!t_err[0]) set_error("decoder_create: weight upload failed");
+        vox_cuda_decoder_free(d);
+        return nullptr;
+    }
+    return d;
+}
+
+extern "C" void vox_cuda_decoder_free(vox_cuda_decoder *d) {
+    if (!d) return;
+    DevCtx *c = ctx_for(d->device);
+    cudaSetDevice(d->device);
+    if (c) cudaStreamSynchronize(c->stream);
+    for (int i = 0; i <= kMaxBatch; i++) free_work(c, d->batch_work[i]);
+    for (auto &pr : d->owned)
+        if (c) dev_free(c, pr.first, pr.second);
+        else cudaFree(pr.first);
+    delete d;
+}
+
+extern "C" vox_cuda_dec_state *vox_cuda_dec_state_create(vox_cuda_decoder *d, int kv_cap) {
+    if (!d || kv_cap <= 0) {
+        set_error("dec_state_create: bad arguments");
+        return nullptr;
+    }
+    DevCtx *c = ctx_for(d->device);
+    if (!c) {
+        set_error("dec_state_create: device not initialised");
+        return nullptr;
+    }
+    vox_cuda_dec_state *s = new vox_cuda_dec_state();
+    s->dec = d;
+    s->cap = kv_cap;
+    s->ring_bytes = (size_t)d->n_layers * kv_cap * kKvDim * sizeof(float);
+    if (dev_alloc(c, (void **)&s->k_ring, s->ring_bytes) != cudaSuccess ||
+        dev_alloc(c, (void **)&s->v_ring, s->ring_bytes) != cudaSuccess) {
+        set_error("dec_state_create: KV ring allocation (%zu bytes x 2) failed", s->ring_bytes);
+        vox_cuda_dec_state_free(s);
+        return nullptr;
+    }
+    if (cudaMemset(s->k_ring, 0, s->ring_bytes) != cudaSuccess ||
+        cudaMemset(s->v_ring, 0, s->ring_bytes) != cudaSuccess) {
+        set_error("dec_state_create: ring clear failed");
+        vox_cuda_dec_state_free(s);
+        return nullptr;
+    }
+    s->work = make_work(c, 1, d->vocab);
+    if (!s->work) {
+        vox_cuda_dec_state_free(s);
+        return nullptr;
+    }
+    return s;
+}
+
+extern "C" void vox_cuda_dec_state_free(vox_cuda_dec_state *s) {
+    if (!s) return;
+    DevCtx *c = ctx_for(s->dec->device);
+    cudaSetDevice(s->dec->device);
+    if (c) cudaStreamSynchronize(c->stream);
+    free_work(c, s->work);
+    free_work(c, s->prefill_work);
+    if (c) {
+        dev_free(c, s->k_ring, s->k_ring ? s->ring_bytes : 0);
+        dev_free(c, s->v_ring, s->v_ring ? s->ring_bytes : 0);
+    }
+    delete s;
+}
+
+extern "C" int vox_cuda_dec_state_reset(vox_cuda_dec_state *s) {
+    if (!s) return VOX_CUDA_ERR_ARG;
+    s->pos = 0;
+    s->have_logits = false;
+    s->last_token = -1;
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_dec_state_position(const vox_cuda_dec_state *s) { return s ? s->pos : -1; }
+
+extern "C" int vox_cuda_dec_state_set_position(vox_cuda_dec_state *s, int logical_pos) {
+    if (!s || logical_pos < 0) {
+        set_error("dec_state_set_position: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    s->pos = logical_pos;
+    s->have_logits = false;
+    return VOX_CUDA_OK;
+}
+
+static int kv_rows_check(vox_cuda_dec_state *s, int layer, int first_pos, int n_rows) {
+    if (!s || layer < 0 || layer >= s->dec->n_layers || first_pos < 0 || n_rows <= 0 ||
+        n_rows > s->cap) {
+        set_error("dec_state kv copy: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    return VOX_CUDA_OK;
+}
+
+static int ring_copy(vox_cuda_dec_state *s, int layer, int first_pos, int n_rows, float *host_k,
+                     float *host_v, bool to_device) {
+    int rc = kv_rows_check(s, layer, first_pos, n_rows);
+    if (rc) return rc;
+    cudaSetDevice(s->dec->device);
+    const size_t row = (size_t)kKvDim * sizeof(float);
+    int done = 0;
+    while (done < n_rows) {
+        const int slot = (first_pos + done) % s->cap;
+        int run = s->cap - slot;
+        if (run > n_rows - done) run = n_rows - done;
+        float *dk = s->k_ring + ((size_t)layer * s->cap + slot) * kKvDim;
+        float *dv = s->v_ring + ((size_t)layer * s->cap + slot) * kKvDim;
+        if (to_device) {
+            VC_TRY(cudaMemcpy(dk, host_k + (size_t)done * kKvDim, run * row, cudaMemcpyHostToDevice));
+            VC_TRY(cudaMemcpy(dv, host_v + (size_t)done * kKvDim, run * row, cudaMemcpyHostToDevice));
+        } else {
+            VC_TRY(cudaMemcpy(host_k + (size_t)done * kKvDim, dk, run * row, cudaMemcpyDeviceToHost));
+            VC_TRY(cudaMemcpy(host_v + (size_t)done * kKvDim, dv, run * row, cudaMemcpyDeviceToHost));
+        }
+        done += run;
+    }
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_dec_state_load_kv(vox_cuda_dec_state *s, int layer, int first_pos,
+                                          int n_rows, const float *k_rows, const float *v_rows) {
+    if (!k_rows || !v_rows) return VOX_CUDA_ERR_ARG;
+    return ring_copy(s, layer, first_pos, n_rows, const_cast<float *>(k_rows),
+                     const_cast<float *>(v_rows), true);
+}
+
+extern "C" int vox_cuda_dec_state_read_kv(vox_cuda_dec_state *s, int layer, int first_pos,
+                                          int n_rows, float *k_rows, float *v_rows) {
+    if (!k_rows || !v_rows) return VOX_CUDA_ERR_ARG;
+    return ring_copy(s, layer, first_pos, n_rows, k_rows, v_rows, false);
+}
+
+extern "C" int vox_cuda_decoder_full_step(vox_cuda_dec_state *s, const float *embed,
+                                          const float *rope_freqs, float *logits) {
+    if (!s || !embed) {
+        set_error("decoder_full_step: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    vox_cuda_decoder *d = s->dec;
+    DevCtx *c = ctx_for(d->device);
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(d->device);
+    int rc = check_capacity(s, s->pos, s->pos);
+    if (rc) return rc;
+    StepWork *w = s->work;
+    fill_slot(s, s->pos, h_slots(w));
+    if (rope_freqs) memcpy(h_rope(w), rope_freqs, kHeadDim * sizeof(float));
+    else host_rope_table(s->pos, kHeadDim, h_rope(w));
+    memcpy(h_x(w), embed, kDecDim * sizeof(float));
+    rc = run_step(d, c, w, true, c->stream, logits == nullptr);
+    if (rc) return rc;
+    if (logits) {
+        VC_TRY(cudaMemcpyAsync(logits, w->logits, (size_t)d->vocab * 4, cudaMemcpyDeviceToHost, c->stream));
+        VC_TRY(cudaStreamSynchronize(c->stream));
+    }
+    s->pos += 1;
+    s->last_token = w->h_tokens[0];
+    s->have_logits = true;
+    return s->last_token;
+}
+
+extern "C" int vox_cuda_decoder_fill_alts(vox_cuda_dec_state *s, int n_alt, float cutoff,
+                                          int *alt_ids) {
+    if (!s || !alt_ids || n_alt < 1 || n_alt > 4) {
+        set_error("decoder_fill_alts: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (!s->have_logits) {
+        set_error("decoder_fill_alts: no decode step since the last reset");
+        return VOX_CUDA_ERR_ARG;
+    }
+    DevCtx *c = ctx_for(s->dec->device);
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(s->dec->device);
+    StepWork *w = s->work;
+    VC_TRY(launch_fill_alts(w->logits, s->dec->vocab, w->tokens, n_alt, cutoff, w->alt_ids, c->stream));
+    int ids[4];
+    VC_TRY(cudaMemcpyAsync(ids, w->alt_ids, sizeof(ids), cudaMemcpyDeviceToHost, c->stream));
+    VC_TRY(cudaStreamSynchronize(c->stream));
+    int n = 0;
+    for (int i = 0; i < n_alt; i++) {
+        if (ids[i] < 0) break;
+        alt_ids[n++] = ids[i];
+    }
+    return n;
+}
+
+extern "C" int vox_cuda_decoder_prefill_step(vox_cuda_dec_state *s, const float *x, int seq_len,
+                                             const float *rope_freqs) {
+    if (!s || !x || seq_len <= 0) {
+        set_error("decoder_prefill_step: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    vox_cuda_decoder *d = s->dec;
+    DevCtx *c = ctx_for(d->device);
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(d->device);
+    // a row must not overwrite a ring slot still inside the window of an
+    // earlier row of the same chunk: positions pos..pos+seq_len-1 all fit
+    int rc = VOX_CUDA_OK;
+    for (int r0 = 0; r0 < seq_len; r0 += kMaxBatch) {
+        const int last = s->pos + ((seq_len - r0 < kMaxBatch) ? seq_len : r0 + kMaxBatch) - 1;
+        if ((rc = check_capacity(s, s->pos + r0, last))) return rc;
+    }
+    // Rows are processed kMaxBatch at a time as parallel "streams" sharing one
+    // ring: each row's attention covers positions <= its own, so the causal
+    // mask of the prefill (voxtral_decoder.c:321-323) is preserved.
+    for (int r0 = 0; r0 < seq_len; r0 += kMaxBatch) {
+        const int n = (seq_len - r0 < kMaxBatch) ? seq_len - r0 : kMaxBatch;
+        StepWork *&w = (n == kMaxBatch) ? s->prefill_work : d->batch_work[n];
+        std::unique_lock<std::mutex> lk(d->mu, std::defer_lock);
+        if (n != kMaxBatch) lk.lock();
+        if (!w) w = make_work(c, n, d->vocab);
+        if (!w) return VOX_CUDA_ERR_OOM;
+        for (int i = 0; i < n; i++) {
+            const int pos = s->pos + r0 + i;
+            fill_slot(s, pos, h_slots(w) + i);
+            if (rope_freqs) memcpy(h_rope(w) + i * kHeadDim, rope_freqs + (size_t)(r0 + i) * kHeadDim, kHeadDim * 4);
+            else host_rope_table(pos, kHeadDim, h_rope(w) + i * kHeadDim);
+        }
+        memcpy(h_x(w), x + (size_t)r0 * kDecDim, (size_t)n * kDecDim * sizeof(float));
+        rc = run_step(d, c, w, false, c->stream, true);
+        if (rc) return rc;
+    }
+    s->pos += seq_len;
+    s->have_logits = false;
+    return VOX_CUDA_OK;
+}
+
+static int batch_prepare(vox_cuda_dec_state *const *states, int n, vox_cuda_decoder **pd,
+                         DevCtx **pc) {
+    if (!states || n <= 0 || n > kMaxBatch) {
+        set_error("decoder_step_batch: n must be 1..%d", kMaxBatch);
+        return VOX_CUDA_ERR_ARG;
+    }
+    vox_cuda_decoder *d = states[0] ? states[0]->dec : nullptr;
+    for (int i = 0; i < n; i++) {
+        if (!states[i] || states[i]->dec != d) {
+            set_error("decoder_step_batch: states must share one decoder");
+            return VOX_CUDA_ERR_ARG;
+        }
+        for (int j = 0; j < i; j++)
+            if (states[j] == states[i]) {
+                set_error("decoder_step_batch: a state appears twice");
+                return VOX_CUDA_ERR_ARG;
+            }
+        int rc = check_capacity(states[i], states[i]->pos, states[i]->pos);
+        if (rc) return rc;
+    }
+    DevCtx *c = ctx_for(d->device);
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(d->device);
+    if (!d->batch_work[n]) d->batch_work[n] = make_work(c, n, d->vocab);
+    if (!d->batch_work[n]) return VOX_CUDA_ERR_OOM;
+    StepWork *w = d->batch_work[n];
+    for (int i = 0; i < n; i++) {
+        fill_slot(states[i], states[i]->pos, h_slots(w) + i);
+        host_rope_table(states[i]->pos, kHeadDim, h_rope(w) + i * kHeadDim);
+    }
+    *pd = d;
+    *pc = c;
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_decoder_step_batch(vox_cuda_dec_state *const *states, int n,
+                                           const float *embeds, int *tokens) {
+    if (!embeds || !tokens) {
+        set_error("decoder_step_batch: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    vox_cuda_decoder *d = nullptr;
+    DevCtx *c = nullptr;
+    if (!states || n <= 0 || n > kMaxBatch || !states[0]) return batch_prepare(states, n, &d, &c);
+    std::lock_guard<std::mutex> lk(states[0]->dec->mu);
+    int rc = batch_prepare(states, n, &d, &c);
+    if (rc) return rc;
+    StepWork *w = d->batch_work[n];
+    memcpy(h_x(w), embeds, (size_t)n * kDecDim * sizeof(float));
+    rc = run_step(d, c, w, true, c->stream, true);
+    if (rc) return rc;
+    for (int i = 0; i < n; i++) {
+        tokens[i] = w->h_tokens[i];
+        states[i]->pos += 1;
+        states[i]->have_logits = false;
+    }
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states, int n,
+                                               const float *embeds_dev, int *tokens_dev,
+                                               void *stream) {
+    if (!embeds_dev || !tokens_dev) {
+        set_error("decoder_step_batch_dev: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (((uintptr_t)embeds_dev & 3u) || ((uintptr_t)tokens_dev & 3u)) {
+        set_error("decoder_step_batch_dev: misaligned device pointers");
+        return VOX_CUDA_ERR_ARG;
+    }
+    vox_cuda_decoder *d = nullptr;
+    DevCtx *c = nullptr;
+    if (!states || n <= 0 || n > kMaxBatch || !states[0]) return batch_prepare(states, n, &d, &c);
+    std::lock_guard<std::mutex> lk(states[0]->dec->mu);
+    int rc = batch_prepare(states, n, &d, &c);
+    if (rc) return rc;
+    StepWork *w = d->batch_work[n];
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    // slots + rope tables from the host block; the embeddings from the device
+    const size_t head = (char *)w->x - w->dblock;
+    VC_TRY(cudaMemcpyAsync(w->dblock, w->hblock, head, cudaMemcpyHostToDevice, st));
+    VC_TRY(cudaMemcpyAsync(w->x, embeds_dev, (size_t)n * kDecDim * 4, cudaMemcpyDeviceToDevice, st));
+    cudaGraphExec_t &g = w->graph[1];
+    if (!g) {
+        cudaGraph_t graph = nullptr;
+        VC_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        rc = enqueue_layers(d, w, true, st);
+        cudaError_t e = cudaStreamEndCapture(st, &graph);
+        if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        VC_TRY(e);
+        e = cudaGraphInstantiate(&g, graph, 0);
+        cudaGraphDestroy(graph);
+        VC_TRY(e);
+    }
+    VC_TRY(cudaGraphLaunch(g, st));
+    VC_TRY(cudaMemcpyAsync(tokens_dev, w->tokens, sizeof(int) * n, cudaMemcpyDeviceToDevice, st));
+    // the host staging block is reused by the next call: wait for the upload
+    VC_TRY(cudaStreamSynchronize(st));
+    for (int i = 0; i < n; i++) {
+        states[i]->pos += 1;
+        states[i]->have_logits = false;
+    }
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_decoder_profile_batch(vox_cuda_dec_state *const *states, int n,
+                                              const float *embeds_dev, int iters, float *ms) {
+    if (!embeds_dev || !ms || iters <= 0) {
+        set_error("decoder_profile_batch: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    vox_cuda_decoder *d = nullptr;
+    DevCtx *c = nullptr;
+    if (!states || n <= 0 || n > kMaxBatch || !states[0]) return batch_prepare(states, n, &d, &c);
+    std::lock_guard<std::mutex> lk(states[0]->dec->mu);
+    int rc = batch_prepare(states, n, &d, &c);
+    if (rc) return rc;
+    StepWork *w = d->batch_work[n];
+    cudaStream_t st = c->stream;
+    const int n_launch = 5 * d->n_layers + 1;
+    std::vector<cudaEvent_t> evs(2 * n_launch);
+    for (auto &e : evs)
+        if (cudaEventCreate(&e) != cudaSuccess) {
+            set_error("profile: event creation failed");
+            return VOX_CUDA_ERR_CUDA;
+        }
+    double acc[VOX_CUDA_PROF_PHASES] = {0};
+    const size_t head = (char *)w->x - w->dblock;
+    for (int it = 0; it < iters && rc == VOX_CUDA_OK; it++) {
+        if (cudaMemcpyAsync(w->dblock, w->hblock, head, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(w->x, embeds_dev, (size_t)n * kDecDim * 4, cudaMemcpyDeviceToDevice, st) !=
+                cudaSuccess) {
+            set_error("profile: staging copy failed");
+            rc = VOX_CUDA_ERR_CUDA;
+            break;
+        }
+        rc = enqueue_layers(d, w, true, st, evs.data());
+        if (rc) break;
+        if (cudaStreamSynchronize(st) != cudaSuccess) {
+            set_error("profile: step failed");
+            rc = VOX_CUDA_ERR_CUDA;
+            break;
+        }
+        for (int i = 0; i < n_launch; i++) {
+            float t = 0.f;
+            cudaEventElapsedTime(&t, evs[2 * i], evs[2 * i + 1]);
+            const int phase = (i == n_launch - 1) ? VOX_CUDA_PROF_LM_HEAD : (i % 5);
+            acc[phase] += t;
+        }
+    }
+    for (auto &e : evs) cudaEventDestroy(e);
+    if (rc) return rc;
+    for (int i = 0; i < VOX_CUDA_PROF_PHASES; i++) ms[i] = (float)(acc[i] / iters);
+    return VOX_CUDA_OK;
+}

@@ -1,0 +1,265 @@
+"""ctypes binding of libvoxtral_cuda.so (include/voxtral_cuda.h).
+
+This is how Python callers (tests, bench.py) reach the C ABI; the C host of
+voxtral.c links the same library directly.  Device buffers handed to the
+`_dev` entry points are plain integers (device addresses); nothing here
+depends on PyTorch.  The library must be built (``make -C voxtral.c_b200``):
+loading fails loudly otherwise - there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libvoxtral_cuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "voxtral_cuda.h")
+
+DEC_DIM, Q_DIM, KV_DIM, DEC_HIDDEN = 3072, 4096, 1024, 9216
+MAX_LAYERS = 26
+PROF_PHASES = ("qkv", "attn", "wo", "w13", "w2", "lm_head")
+
+OK, ERR_UNAVAILABLE, ERR_ARG, ERR_OOM, ERR_CUDA, ERR_CAPACITY = 0, -1, -2, -3, -4, -5
+
+_fp = C.POINTER(C.c_float)
+_u16p = C.POINTER(C.c_uint16)
+_ip = C.POINTER(C.c_int)
+
+
+class VoxCudaError(RuntimeError):
+    pass
+
+
+def header_symbols():
+    """Every function name declared in include/voxtral_cuda.h."""
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(vox_cuda_\w+)\s*\(", src)))
+
+
+class _LayerW(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "w1", "w2", "w3",
+                                          "attention_norm", "ffn_norm")]
+
+
+class _DecW(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("vocab", C.c_int), ("weights_on_device", C.c_int),
+                ("tok_embeddings", C.c_void_p), ("norm", C.c_void_p), ("ada_scale", C.c_void_p),
+                ("layers", _LayerW * MAX_LAYERS)]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise VoxCudaError(f"{LIB_PATH} is not built (run __graft_entry__.build())")
+    L = C.CDLL(LIB_PATH)
+    sig = {
+        "vox_cuda_init": ([], C.c_int),
+        "vox_cuda_available": ([], C.c_int),
+        "vox_cuda_shutdown": ([], None),
+        "vox_cuda_set_device": ([C.c_int], C.c_int),
+        "vox_cuda_last_error": ([], C.c_char_p),
+        "vox_cuda_memory_used": ([], C.c_size_t),
+        "vox_cuda_sgemm_bf16": ([C.c_int, C.c_int, C.c_int, _fp, _u16p, _fp, _fp], C.c_int),
+        "vox_cuda_warmup_bf16": ([_u16p, C.c_size_t], C.c_int),
+        "vox_cuda_linear_bf16_dev": ([C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
+        "vox_cuda_decoder_create": ([C.c_void_p], C.c_void_p),
+        "vox_cuda_decoder_free": ([C.c_void_p], None),
+        "vox_cuda_dec_state_create": ([C.c_void_p, C.c_int], C.c_void_p),
+        "vox_cuda_dec_state_free": ([C.c_void_p], None),
+        "vox_cuda_dec_state_reset": ([C.c_void_p], C.c_int),
+        "vox_cuda_dec_state_position": ([C.c_void_p], C.c_int),
+        "vox_cuda_dec_state_set_position": ([C.c_void_p, C.c_int], C.c_int),
+        "vox_cuda_dec_state_load_kv": ([C.c_void_p, C.c_int, C.c_int, C.c_int, _fp, _fp], C.c_int),
+        "vox_cuda_dec_state_read_kv": ([C.c_void_p, C.c_int, C.c_int, C.c_int, _fp, _fp], C.c_int),
+        "vox_cuda_decoder_full_step": ([C.c_void_p, _fp, _fp, _fp], C.c_int),
+        "vox_cuda_decoder_fill_alts": ([C.c_void_p, C.c_int, C.c_float, _ip], C.c_int),
+        "vox_cuda_decoder_prefill_step": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
+        "vox_cuda_decoder_step_batch": ([C.c_void_p, C.c_int, _fp, _ip], C.c_int),
+        "vox_cuda_decoder_step_batch_dev": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                             C.c_void_p], C.c_int),
+        "vox_cuda_decoder_profile_batch": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, _fp],
+                                           C.c_int),
+        "vox_cuda_attention_decode_dev": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                           C.c_void_p, C.c_void_p], C.c_int),
+        "vox_cuda_rope_dev": ([C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p],
+                              C.c_int),
+        "vox_cuda_fill_normal_bf16_dev": ([C.c_void_p, C.c_size_t, C.c_uint64, C.c_float,
+                                           C.c_void_p], C.c_int),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = L
+    return L
+
+
+def last_error():
+    return lib().vox_cuda_last_error().decode(errors="replace")
+
+
+def check(rc, what=""):
+    if rc < 0:
+        raise VoxCudaError(f"{what}: rc={rc}: {last_error()}")
+    return rc
+
+
+def init(device=None):
+    L = lib()
+    if device is not None:
+        check(L.vox_cuda_set_device(device), "set_device")
+    if L.vox_cuda_init() != 1:
+        raise VoxCudaError("vox_cuda_init failed: " + last_error())
+
+
+def _f(a):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_fp)
+
+
+def _u16(a):
+    assert a.dtype == np.uint16 and a.flags.c_contiguous
+    return a.ctypes.data_as(_u16p)
+
+
+def sgemm_bf16(x, W, bias=None):
+    """C = x W^T (+ bias) through vox_cuda_sgemm_bf16 (host arrays)."""
+    x = np.ascontiguousarray(x, np.float32)
+    M = x.shape[0] if x.ndim == 2 else 1
+    N, K = W.shape
+    y = np.empty((M, N), np.float32)
+    check(lib().vox_cuda_sgemm_bf16(M, N, K, _f(x), _u16(W), _f(bias), _f(y)), "sgemm_bf16")
+    return y
+
+
+class Decoder:
+    """Resident decoder weights.  `layers` is a list of n_layers tuples
+    (wq, wk, wv, wo, w1, w2, w3, attention_norm, ffn_norm); arrays are host
+    numpy arrays, or device addresses (ints) with on_device=True."""
+
+    def __init__(self, tok_emb, norm, layers, ada_scale=None, vocab=131072, on_device=False):
+        def addr(a):
+            if a is None:
+                return None
+            return int(a) if on_device else a.ctypes.data
+        d = _DecW()
+        d.n_layers = len(layers)
+        d.vocab = vocab
+        d.weights_on_device = 1 if on_device else 0
+        d.tok_embeddings = addr(tok_emb)
+        d.norm = addr(norm)
+        d.ada_scale = addr(ada_scale)
+        for i, lw in enumerate(layers):
+            for name, a in zip(("wq", "wk", "wv", "wo", "w1", "w2", "w3", "attention_norm",
+                                "ffn_norm"), lw):
+                setattr(d.layers[i], name, addr(a))
+        self.vocab = vocab
+        self.n_layers = len(layers)
+        self.h = lib().vox_cuda_decoder_create(C.byref(d))
+        if not self.h:
+            raise VoxCudaError("decoder_create: " + last_error())
+
+    def state(self, kv_cap=8192 + 1024):
+        return DecState(self, kv_cap)
+
+    def free(self):
+        if self.h:
+            lib().vox_cuda_decoder_free(self.h)
+            self.h = None
+
+
+class DecState:
+    def __init__(self, dec: Decoder, kv_cap):
+        self.dec = dec
+        self.kv_cap = kv_cap
+        self.h = lib().vox_cuda_dec_state_create(dec.h, kv_cap)
+        if not self.h:
+            raise VoxCudaError("dec_state_create: " + last_error())
+
+    @property
+    def position(self):
+        return lib().vox_cuda_dec_state_position(self.h)
+
+    def set_position(self, pos):
+        check(lib().vox_cuda_dec_state_set_position(self.h, pos), "set_position")
+
+    def reset(self):
+        check(lib().vox_cuda_dec_state_reset(self.h), "reset")
+
+    def step(self, embed, rope=None, want_logits=True):
+        embed = np.ascontiguousarray(embed, np.float32).reshape(-1)
+        logits = np.empty(self.dec.vocab, np.float32) if want_logits else None
+        rope = None if rope is None else np.ascontiguousarray(rope, np.float32).reshape(-1)
+        tok = check(lib().vox_cuda_decoder_full_step(self.h, _f(embed), _f(rope), _f(logits)),
+                    "full_step")
+        return tok, logits
+
+    def prefill(self, x, rope=None):
+        x = np.ascontiguousarray(x, np.float32)
+        rope = None if rope is None else np.ascontiguousarray(rope, np.float32)
+        check(lib().vox_cuda_decoder_prefill_step(self.h, _f(x), x.shape[0], _f(rope)), "prefill")
+
+    def fill_alts(self, n_alt, cutoff):
+        ids = np.full(4, -1, np.int32)
+        n = check(lib().vox_cuda_decoder_fill_alts(self.h, n_alt, cutoff, ids.ctypes.data_as(_ip)),
+                  "fill_alts")
+        return ids[:n].tolist()
+
+    def load_kv(self, layer, first_pos, k_rows, v_rows):
+        k_rows = np.ascontiguousarray(k_rows, np.float32)
+        v_rows = np.ascontiguousarray(v_rows, np.float32)
+        check(lib().vox_cuda_dec_state_load_kv(self.h, layer, first_pos, k_rows.shape[0],
+                                               _f(k_rows), _f(v_rows)), "load_kv")
+
+    def read_kv(self, layer, first_pos, n_rows):
+        k = np.empty((n_rows, KV_DIM), np.float32)
+        v = np.empty((n_rows, KV_DIM), np.float32)
+        check(lib().vox_cuda_dec_state_read_kv(self.h, layer, first_pos, n_rows, _f(k), _f(v)),
+              "read_kv")
+        return k, v
+
+    def free(self):
+        if self.h:
+            lib().vox_cuda_dec_state_free(self.h)
+            self.h = None
+
+
+def step_batch(states, embeds):
+    embeds = np.ascontiguousarray(embeds, np.float32)
+    n = len(states)
+    arr = (C.c_void_p * n)(*[s.h for s in states])
+    toks = np.empty(n, np.int32)
+    check(lib().vox_cuda_decoder_step_batch(arr, n, _f(embeds), toks.ctypes.data_as(_ip)),
+          "step_batch")
+    return toks.tolist()
+
+
+def states_array(states):
+    return (C.c_void_p * len(states))(*[s.h for s in states])
+
+
+def step_batch_dev(states, embeds_dev, tokens_dev, stream=None):
+    """Batched step with device embeddings / tokens (device addresses)."""
+    arr = states_array(states)
+    check(lib().vox_cuda_decoder_step_batch_dev(arr, len(states), embeds_dev, tokens_dev, stream),
+          "step_batch_dev")
+
+
+def profile_batch(states, embeds_dev, iters=3):
+    """Mean ms per step of each phase (PROF_PHASES) of the batched step."""
+    ms = np.zeros(len(PROF_PHASES), np.float32)
+    check(lib().vox_cuda_decoder_profile_batch(states_array(states), len(states), embeds_dev, iters,
+                                               _f(ms)), "profile_batch")
+    return dict(zip(PROF_PHASES, ms.tolist()))
