@@ -77,11 +77,18 @@ size_t vox_cuda_memory_used(void);
 int vox_cuda_sgemm_bf16(int M, int N, int K, const float *A, const uint16_t *B_bf16,
                         const float *bias, float *C);
 
-/* Pre-upload a weight into the pointer-keyed cache (vox_metal_warmup_bf16,
- * voxtral_metal.h:225). */
-int vox_cuda_warmup_bf16(const uint16_t *B_bf16, size_t num_elements);
+/* Pre-upload a [N, K] weight into the pointer-keyed cache
+ * (vox_metal_warmup_bf16, voxtral_metal.h:225; the shape is needed here
+ * because the device copy is re-laid out into 16x16 MMA-fragment tiles). */
+int vox_cuda_warmup_bf16(const uint16_t *B_bf16, int N, int K);
 
-/* Device-pointer form of vox_cuda_sgemm_bf16: all pointers on the device. */
+/* Drop every cached weight copy on the current device.  The cache assumes a
+ * cached weight's memory is not rewritten (true for the mmap'd safetensors);
+ * a caller that frees or rewrites weight buffers calls this first. */
+void vox_cuda_weight_cache_clear(void);
+
+/* Device-pointer form of vox_cuda_sgemm_bf16: all pointers on the device,
+ * B in its row-major layout (tiled copy cached by pointer, as above). */
 int vox_cuda_linear_bf16_dev(int M, int N, int K, const float *A, const uint16_t *B_bf16,
                              const float *bias, float *C, void *stream);
 

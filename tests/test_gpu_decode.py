@@ -46,9 +46,12 @@ def test_sgemm_bf16_matches_reference(case):
     g = load_golden("linear")
     name, M, K, N, bias, path, seed = case
     x, W, b = G.linear_inputs(M, K, N, bias, seed)
+    V.lib().vox_cuda_weight_cache_clear()   # W is a fresh array at a possibly reused address
     y = V.sgemm_bf16(x, W, b)
     assert sampled_rel(y, g, name) < GEMV_TOL * 1e-2
     assert B.rel_l2(y, B.linear(x, W, b)) < 1e-5
+    y2 = V.sgemm_bf16(x, W, b)                # served from the weight cache
+    assert np.array_equal(y, y2)
 
 
 def test_linear_dev_entry_and_ragged_shapes():
@@ -61,6 +64,7 @@ def test_linear_dev_entry_and_ragged_shapes():
         dx, dW, db = (torch.from_numpy(x).cuda(), torch.from_numpy(W.view(np.int16)).cuda(),
                       torch.from_numpy(b).cuda())
         dy = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        V.lib().vox_cuda_weight_cache_clear()
         V.check(V.lib().vox_cuda_linear_bf16_dev(M, N, K, dx.data_ptr(), dW.data_ptr(), db.data_ptr(),
                                                  dy.data_ptr(), None), "linear_dev")
         torch.cuda.synchronize()

@@ -32,12 +32,16 @@ struct ArgmaxPartial {
 };
 
 struct GemvParams {
-    const uint16_t *W;      // [N, K] bf16 row-major
-    int N, K;
+    const uint16_t *W;      // fragment-tiled weights (launch_tile_weights), [Np, Kp]
+    int N, K;               // logical shape
+    int Kp;                 // K rounded up to 16 (the tiled row length)
     const float *x;         // [M, ldx] fp32 (device)
     int ldx;
     const float *norm_w;    // RMSNorm prologue weight [K] or NULL
     const float *ada;       // (1 + ada) after the norm [K] or NULL
+    const float *ss_in;     // per-row-block sums of x^2 from the producer, [M][ss_parts], or NULL
+    int ss_parts;
+    float *ss_out;          // EPI_ADD: per-row-block sums of the new y^2, [M][row blocks], or NULL
     float *y;               // output [M, ldy]
     int ldy;
     const float *bias;      // [N] or NULL
@@ -53,7 +57,13 @@ struct GemvParams {
 
 // Launch the fused streaming GEMV (M = 1..8 activation rows).
 cudaError_t launch_gemv(int M, int epi, const GemvParams &p, cudaStream_t st, bool pdl);
-int gemv_grid(int M, int epi, int N);
+int gemv_grid(int M, int epi, int N);      // row blocks (64 rows) of a launch
+int gemv_row_blocks(int N);
+constexpr int kGemvRowAlign = 64;           // tiled weights are padded to this many rows
+// Row-major [N, K] bf16 -> the GEMV's fragment-tiled layout [Np, Kp]
+// (Np = N rounded up to kGemvRowAlign, Kp = K rounded up to 16).
+cudaError_t launch_tile_weights(uint16_t *dst, const uint16_t *src, int N, int K, int Np, int Kp,
+                                cudaStream_t st);
 
 struct AttnParams {
     const float *q;           // [M][4096], RoPE applied
@@ -76,7 +86,5 @@ cudaError_t launch_fill_alts(const float *logits, int vocab, const int *best, in
 cudaError_t launch_rope(float *x, int n_heads, int head_dim, const float *cs, cudaStream_t st);
 cudaError_t launch_fill_normal_bf16(uint16_t *dst, size_t n, uint64_t seed, float std,
                                     cudaStream_t st);
-cudaError_t launch_interleave_rows(uint16_t *dst, const uint16_t *a, const uint16_t *b,
-                                   int rows, int cols, cudaStream_t st);
 
 }  // namespace vc

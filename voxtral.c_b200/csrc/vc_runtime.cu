@@ -13,6 +13,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -66,8 +67,14 @@ struct DevCtx {
     cudaStream_t stream = nullptr;
     std::mutex mu;                  // guards the cache and the scratch below
     size_t bytes = 0;               // device bytes held by the library
-    std::unordered_map<const void *, void *> wcache;   // host weight ptr -> device copy
-    std::unordered_map<const void *, size_t> wcache_n; // host weight ptr -> elements
+    struct CachedW {
+        uint16_t *dev;      // fragment-tiled copy
+        int N, K;
+        size_t bytes;
+    };
+    std::unordered_map<const void *, CachedW> wcache;  // caller's weight ptr -> tiled copy
+    uint16_t *stage = nullptr;                          // row-major upload staging
+    size_t stage_bytes = 0;
     // scratch for the host-pointer matmul entry and the kernel-level entries
     float *sx = nullptr, *sy = nullptr, *sb = nullptr;
     size_t sx_n = 0, sy_n = 0, sb_n = 0;
@@ -215,9 +222,11 @@ extern "C" void vox_cuda_shutdown(void) {
         if (!c->ready) continue;
         cudaSetDevice(d);
         cudaStreamSynchronize(c->stream);
-        for (auto &kv : c->wcache) cudaFree(kv.second);
+        for (auto &kv : c->wcache) cudaFree(kv.second.dev);
         c->wcache.clear();
-        c->wcache_n.clear();
+        cudaFree(c->stage);
+        c->stage = nullptr;
+        c->stage_bytes = 0;
         release_scratch(c);
         cudaStreamDestroy(c->stream);
         c->stream = nullptr;
@@ -235,14 +244,13 @@ static int check_linear_args(int M, int N, int K, const void *A, const void *B, 
         set_error("linear: bad arguments (M=%d N=%d K=%d)", M, N, K);
         return VOX_CUDA_ERR_ARG;
     }
-    if (K % 8 != 0) {
-        set_error("linear: K=%d must be a multiple of 8 (16-byte weight rows)", K);
-        return VOX_CUDA_ERR_ARG;
-    }
     return VOX_CUDA_OK;
 }
 
-// y[M,N] = x[M,K] W^T (+b), all device pointers; rows of x in chunks of 8.
+static int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+// y[M,N] = x[M,K] W^T (+b), all device pointers, W fragment-tiled; rows of x
+// in chunks of 8.
 static int enqueue_linear(int M, int N, int K, const float *x, const uint16_t *W, const float *b,
                           float *y, cudaStream_t st) {
     for (int m0 = 0; m0 < M; m0 += kMaxBatch) {
@@ -251,6 +259,7 @@ static int enqueue_linear(int M, int N, int K, const float *x, const uint16_t *W
         p.W = W;
         p.N = N;
         p.K = K;
+        p.Kp = round_up(K, 16);
         p.x = x + (size_t)m0 * K;
         p.ldx = K;
         p.y = y + (size_t)m0 * N;
@@ -263,60 +272,103 @@ static int enqueue_linear(int M, int N, int K, const float *x, const uint16_t *W
 
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
+static const uint16_t *cached_weight(DevCtx *c, const uint16_t *src, int N, int K, bool on_host,
+                                     int *rc);
+
 extern "C" int vox_cuda_linear_bf16_dev(int M, int N, int K, const float *A, const uint16_t *B_bf16,
                                         const float *bias, float *C, void *stream) {
     int rc = check_linear_args(M, N, K, A, B_bf16, C);
     if (rc) return rc;
-    if (!aligned16(A) || !aligned16(B_bf16)) {
-        set_error("linear_dev: A and B must be 16-byte aligned device pointers");
-        return VOX_CUDA_ERR_ARG;
-    }
+
     DevCtx *c = cur_ctx();
     if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
-    return enqueue_linear(M, N, K, A, B_bf16, bias, C, st);
+    const uint16_t *W = cached_weight(c, B_bf16, N, K, false, &rc);
+    if (!W) return rc;
+    return enqueue_linear(M, N, K, A, W, bias, C, st);
 }
 
-static const uint16_t *cached_weight(DevCtx *c, const uint16_t *host, size_t n, int *rc) {
-    {
-        std::lock_guard<std::mutex> lk(c->mu);
-        auto it = c->wcache.find(host);
-        if (it != c->wcache.end() && c->wcache_n[host] >= n) return (const uint16_t *)it->second;
+// The fragment-tiled device copy of a caller's [N, K] bf16 weight, made on
+// first use and kept, keyed by the caller's pointer (host: the mmap'd tensor;
+// device: the caller's buffer).  Like the Metal backend's pointer-keyed cache,
+// it assumes the weight memory is not rewritten while cached;
+// vox_cuda_weight_cache_clear() drops every copy.
+static const uint16_t *cached_weight(DevCtx *c, const uint16_t *src, int N, int K, bool on_host,
+                                     int *rc) {
+    std::lock_guard<std::mutex> lk(c->mu);
+    auto it = c->wcache.find(src);
+    if (it != c->wcache.end()) {
+        if (it->second.N == N && it->second.K == K) return it->second.dev;
+        cudaFree(it->second.dev);
+        c->bytes -= it->second.bytes;
+        c->wcache.erase(it);
     }
-    void *d = nullptr;
-    cudaError_t e = dev_alloc(c, &d, n * sizeof(uint16_t));
-    if (e != cudaSuccess) {
-        set_error("weight cache: cudaMalloc(%zu) failed: %s", n * 2, cudaGetErrorString(e));
+    const int Np = round_up(N, kGemvRowAlign), Kp = round_up(K, 16);
+    const size_t bytes = (size_t)Np * Kp * 2;
+    uint16_t *d = nullptr;
+    if (cudaMalloc(&d, bytes) != cudaSuccess) {
+        set_error("weight cache: cudaMalloc(%zu) failed", bytes);
         *rc = VOX_CUDA_ERR_OOM;
         return nullptr;
     }
-    e = cudaMemcpy(d, host, n * sizeof(uint16_t), cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
-        set_error("weight cache: upload failed: %s", cudaGetErrorString(e));
-        dev_free(c, d, n * 2);
+    const uint16_t *rowmajor = src;
+    const size_t raw = (size_t)N * K * 2;
+    if (on_host) {
+        if (c->stage_bytes < raw) {
+            cudaFree(c->stage);
+            c->bytes -= c->stage_bytes;
+            c->stage = nullptr;
+            c->stage_bytes = 0;
+            if (cudaMalloc(&c->stage, raw) != cudaSuccess) {
+                cudaFree(d);
+                set_error("weight cache: staging cudaMalloc(%zu) failed", raw);
+                *rc = VOX_CUDA_ERR_OOM;
+                return nullptr;
+            }
+            c->stage_bytes = raw;
+            c->bytes += raw;
+        }
+        if (cudaMemcpyAsync(c->stage, src, raw, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
+            cudaFree(d);
+            set_error("weight cache: upload failed");
+            *rc = VOX_CUDA_ERR_CUDA;
+            return nullptr;
+        }
+        rowmajor = c->stage;
+    }
+    if (launch_tile_weights(d, rowmajor, N, K, Np, Kp, c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess) {
+        cudaFree(d);
+        set_error("weight cache: tiling failed");
         *rc = VOX_CUDA_ERR_CUDA;
         return nullptr;
     }
-    std::lock_guard<std::mutex> lk(c->mu);
-    auto it = c->wcache.find(host);
-    if (it != c->wcache.end()) {  // replaced by a larger upload of the same pointer
-        c->bytes -= c->wcache_n[host] * 2;
-        cudaFree(it->second);
-    }
-    c->wcache[host] = d;
-    c->wcache_n[host] = n;
-    return (const uint16_t *)d;
+    c->wcache[src] = DevCtx::CachedW{d, N, K, bytes};
+    c->bytes += bytes;
+    return d;
 }
 
-extern "C" int vox_cuda_warmup_bf16(const uint16_t *B_bf16, size_t num_elements) {
+extern "C" void vox_cuda_weight_cache_clear(void) {
+    DevCtx *c = ctx_for(current_device());
+    if (!c) return;
+    cudaStreamSynchronize(c->stream);
+    std::lock_guard<std::mutex> lk(c->mu);
+    for (auto &kv : c->wcache) {
+        cudaFree(kv.second.dev);
+        c->bytes -= kv.second.bytes;
+    }
+    c->wcache.clear();
+}
+
+extern "C" int vox_cuda_warmup_bf16(const uint16_t *B_bf16, int N, int K) {
     DevCtx *c = cur_ctx();
     if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
-    if (!B_bf16 || num_elements == 0) {
+    if (!B_bf16 || N <= 0 || K <= 0) {
         set_error("warmup: bad arguments");
         return VOX_CUDA_ERR_ARG;
     }
     int rc = VOX_CUDA_OK;
-    return cached_weight(c, B_bf16, num_elements, &rc) ? VOX_CUDA_OK : rc;
+    return cached_weight(c, B_bf16, N, K, true, &rc) ? VOX_CUDA_OK : rc;
 }
 
 extern "C" int vox_cuda_sgemm_bf16(int M, int N, int K, const float *A, const uint16_t *B_bf16,
@@ -325,7 +377,7 @@ extern "C" int vox_cuda_sgemm_bf16(int M, int N, int K, const float *A, const ui
     if (rc) return rc;
     DevCtx *c = cur_ctx();
     if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
-    const uint16_t *W = cached_weight(c, B_bf16, (size_t)N * K, &rc);
+    const uint16_t *W = cached_weight(c, B_bf16, N, K, true, &rc);
     if (!W) return rc;
     std::lock_guard<std::mutex> lk(c->mu);  // one user of the host-path scratch at a time
     // (dev_alloc takes the same mutex: allocate through grow_locked below)
@@ -462,8 +514,10 @@ extern "C" int vox_cuda_fill_normal_bf16_dev(uint16_t *dst, size_t n, uint64_t s
 namespace {
 
 struct DecLayer {
-    const uint16_t *qkv, *wo, *w13, *w2;   // fused device layout
-    const float *attn_norm, *ffn_norm, *ada;
+    // fused, fragment-tiled device copies: wq|wk|wv [6144, 3072],
+    // wo [3072, 4096], w1/w3 row-interleaved [18432, 3072], w2 [3072, 9216]
+    const uint16_t *qkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr;
+    const float *attn_norm = nullptr, *ffn_norm = nullptr, *ada = nullptr;
 };
 
 // Device workspace for one step shape (n rows).  The host staging block is
@@ -485,6 +539,8 @@ struct StepWork {
     ArgmaxPartial *amax = nullptr;
     int *tokens = nullptr;             // [n]
     int *alt_ids = nullptr;            // [4]
+    float *ss_attn = nullptr;          // [n][48] sums of x^2 per row block, after w2 (next QKV norm)
+    float *ss_ffn = nullptr;           // [n][48] after wo (the FFN norm)
     size_t bytes = 0;
     // host (pinned)
     char *hblock = nullptr;
@@ -563,6 +619,9 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     const size_t o_amax = take(sizeof(ArgmaxPartial) * grid * n);
     const size_t o_tok = take(sizeof(int) * n);
     const size_t o_alt = take(sizeof(int) * 4);
+    const size_t n_ss = (size_t)n * gemv_row_blocks(kDecDim);
+    const size_t o_ssa = take(sizeof(float) * n_ss);
+    const size_t o_ssf = take(sizeof(float) * n_ss);
     if (dev_alloc(c, (void **)&w->dblock, off) != cudaSuccess) {
         set_error("decoder workspace: cudaMalloc(%zu) failed", off);
         delete w;
@@ -583,6 +642,8 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     w->amax = (ArgmaxPartial *)(b + o_amax);
     w->tokens = (int *)(b + o_tok);
     w->alt_ids = (int *)(b + o_alt);
+    w->ss_attn = (float *)(b + o_ssa);
+    w->ss_ffn = (float *)(b + o_ssf);
     if (cudaMemset(w->counters, 0, sizeof(unsigned) * (n * kDecKvHeads + 1)) != cudaSuccess ||
         cudaHostAlloc((void **)&w->hblock, w->dblock_bytes + 64, cudaHostAllocDefault) != cudaSuccess) {
         set_error("decoder workspace: staging allocation failed");
@@ -614,10 +675,14 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         // q|k|v = rms_norm(x) Wqkv^T, RoPE, ring write
         p.W = L.qkv;
         p.N = kQkvRows;
-        p.K = kDecDim;
+        p.K = p.Kp = kDecDim;
         p.x = w->x;
         p.ldx = kDecDim;
         p.norm_w = L.attn_norm;
+        if (l > 0) {  // layer 0 reads the embeddings: its norm sums x itself
+            p.ss_in = w->ss_attn;
+            p.ss_parts = gemv_row_blocks(kDecDim);
+        }
         p.y = w->q;
         p.ldy = kQDim;
         p.slots = w->slots;
@@ -643,11 +708,12 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p = GemvParams{};
         p.W = L.wo;
         p.N = kDecDim;
-        p.K = kQDim;
+        p.K = p.Kp = kQDim;
         p.x = w->att;
         p.ldx = kQDim;
         p.y = w->x;
         p.ldy = kDecDim;
+        p.ss_out = w->ss_ffn;
         VC_EV_BEGIN();
         VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
         VC_EV_END();
@@ -655,11 +721,13 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p = GemvParams{};
         p.W = L.w13;
         p.N = 2 * kDecHidden;
-        p.K = kDecDim;
+        p.K = p.Kp = kDecDim;
         p.x = w->x;
         p.ldx = kDecDim;
         p.norm_w = L.ffn_norm;
         p.ada = L.ada;
+        p.ss_in = w->ss_ffn;
+        p.ss_parts = gemv_row_blocks(kDecDim);
         p.y = w->h;
         p.ldy = kDecHidden;
         VC_EV_BEGIN();
@@ -669,11 +737,12 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p = GemvParams{};
         p.W = L.w2;
         p.N = kDecDim;
-        p.K = kDecHidden;
+        p.K = p.Kp = kDecHidden;
         p.x = w->h;
         p.ldx = kDecHidden;
         p.y = w->x;
         p.ldy = kDecDim;
+        p.ss_out = w->ss_attn;
         VC_EV_BEGIN();
         VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
         VC_EV_END();
@@ -682,10 +751,12 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         GemvParams p = {};
         p.W = d->tok_emb;
         p.N = d->vocab;
-        p.K = kDecDim;
+        p.K = p.Kp = kDecDim;
         p.x = w->x;
         p.ldx = kDecDim;
         p.norm_w = d->norm;
+        p.ss_in = w->ss_attn;
+        p.ss_parts = gemv_row_blocks(kDecDim);
         p.y = w->logits;
         p.ldy = d->vocab;
         p.partials = w->amax;
@@ -775,60 +846,78 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
     const char *pdl_env = getenv("VOX_CUDA_PDL");
     d->pdl = !(pdl_env && pdl_env[0] == '0');
     const cudaMemcpyKind kind = w->weights_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    cudaStream_t st = c->stream;
     auto alloc = [&](size_t bytes) -> void * {
         void *p = nullptr;
         if (dev_alloc(c, &p, bytes) != cudaSuccess) return nullptr;
         d->owned.push_back({p, bytes});
         return p;
     };
-    // Weights shared between layers (aliased host pointers) are laid out once.
-    std::unordered_map<const void *, const void *> seen;
-    bool ok = true;
     const size_t D = kDecDim;
+    // row-major staging for one fused matrix (the largest is the LM head)
+    const size_t stage_elems = std::max((size_t)w->vocab, (size_t)2 * kDecHidden) * D;
+    uint16_t *stage = nullptr;
+    if (cudaMalloc(&stage, stage_elems * 2) != cudaSuccess) {
+        set_error("decoder_create: staging allocation (%zu bytes) failed", stage_elems * 2);
+        delete d;
+        return nullptr;
+    }
+    bool ok = true;
+    // Fused matrix from row-major pieces: [rows_i x K] blocks stacked (or
+    // row-interleaved when interleave), then tiled for the GEMV.
+    auto fuse = [&](const uint16_t *const *parts, const int *rows, int n_parts, int K,
+                    bool interleave) -> uint16_t * {
+        int N = 0;
+        for (int i = 0; i < n_parts; i++) N += rows[i];
+        uint16_t *dst = (uint16_t *)alloc((size_t)round_up(N, kGemvRowAlign) * round_up(K, 16) * 2);
+        if (!dst) return nullptr;
+        if (interleave) {  // row 2i = parts[0][i], row 2i+1 = parts[1][i]
+            for (int i = 0; i < n_parts && ok; i++)
+                ok &= cudaMemcpy2DAsync(stage + (size_t)i * K, (size_t)n_parts * K * 2, parts[i],
+                                        (size_t)K * 2, (size_t)K * 2, rows[i], kind, st) == cudaSuccess;
+        } else {
+            size_t off = 0;
+            for (int i = 0; i < n_parts && ok; i++) {
+                ok &= cudaMemcpyAsync(stage + off, parts[i], (size_t)rows[i] * K * 2, kind, st) ==
+                      cudaSuccess;
+                off += (size_t)rows[i] * K;
+            }
+        }
+        ok &= launch_tile_weights(dst, stage, N, K, round_up(N, kGemvRowAlign), round_up(K, 16), st) ==
+              cudaSuccess;
+        ok &= cudaStreamSynchronize(st) == cudaSuccess;   // the stage is reused next
+        return ok ? dst : nullptr;
+    };
     for (int l = 0; l < w->n_layers && ok; l++) {
         const vox_cuda_dec_layer_weights &L = w->layers[l];
         DecLayer &o = d->L[l];
-        auto it = seen.find(L.wq);
-        if (it != seen.end() && seen.count(L.w1) && seen.count(L.wo) && seen.count(L.w2)) {
-            // same host tensors as an earlier layer: reuse its fused copies
-            for (int j = 0; j < l; j++)
-                if (w->layers[j].wq == L.wq && w->layers[j].wk == L.wk && w->layers[j].wv == L.wv &&
-                    w->layers[j].wo == L.wo && w->layers[j].w1 == L.w1 && w->layers[j].w2 == L.w2 &&
-                    w->layers[j].w3 == L.w3) {
-                    o.qkv = d->L[j].qkv;
-                    o.wo = d->L[j].wo;
-                    o.w13 = d->L[j].w13;
-                    o.w2 = d->L[j].w2;
-                    break;
-                }
-        }
-        if (!o.qkv) {
-            uint16_t *qkv = (uint16_t *)alloc((size_t)kQkvRows * D * 2);
-            uint16_t *wo = (uint16_t *)alloc((size_t)D * kQDim * 2);
-            uint16_t *w13 = (uint16_t *)alloc((size_t)2 * kDecHidden * D * 2);
-            uint16_t *w2 = (uint16_t *)alloc((size_t)D * kDecHidden * 2);
-            if (!qkv || !wo || !w13 || !w2) {
-                ok = false;
+        // layers that alias an earlier layer's tensors share its device copies
+        for (int j = 0; j < l; j++) {
+            const vox_cuda_dec_layer_weights &J = w->layers[j];
+            if (J.wq == L.wq && J.wk == L.wk && J.wv == L.wv && J.wo == L.wo && J.w1 == L.w1 &&
+                J.w2 == L.w2 && J.w3 == L.w3) {
+                o.qkv = d->L[j].qkv;
+                o.wo = d->L[j].wo;
+                o.w13 = d->L[j].w13;
+                o.w2 = d->L[j].w2;
                 break;
             }
-            // wq | wk | wv concatenated by rows
-            ok &= cudaMemcpy(qkv, L.wq, (size_t)kQDim * D * 2, kind) == cudaSuccess;
-            ok &= cudaMemcpy(qkv + (size_t)kQDim * D, L.wk, (size_t)kKvDim * D * 2, kind) == cudaSuccess;
-            ok &= cudaMemcpy(qkv + (size_t)(kQDim + kKvDim) * D, L.wv, (size_t)kKvDim * D * 2, kind) ==
-                  cudaSuccess;
-            ok &= cudaMemcpy(wo, L.wo, (size_t)D * kQDim * 2, kind) == cudaSuccess;
-            // w1 / w3 row-interleaved: row 2i = w1[i], row 2i+1 = w3[i]
-            ok &= cudaMemcpy2D(w13, 2 * D * 2, L.w1, D * 2, D * 2, kDecHidden, kind) == cudaSuccess;
-            ok &= cudaMemcpy2D(w13 + D, 2 * D * 2, L.w3, D * 2, D * 2, kDecHidden, kind) == cudaSuccess;
-            ok &= cudaMemcpy(w2, L.w2, (size_t)D * kDecHidden * 2, kind) == cudaSuccess;
-            o.qkv = qkv;
-            o.wo = wo;
-            o.w13 = w13;
-            o.w2 = w2;
-            seen[L.wq] = qkv;
-            seen[L.w1] = w13;
-            seen[L.wo] = wo;
-            seen[L.w2] = w2;
+        }
+        if (!o.qkv) {
+            const uint16_t *qkv_parts[3] = {L.wq, L.wk, L.wv};
+            const int qkv_rows[3] = {kQDim, kKvDim, kKvDim};
+            const uint16_t *wo_parts[1] = {L.wo};
+            const int wo_rows[1] = {kDecDim};
+            const uint16_t *w13_parts[2] = {L.w1, L.w3};
+            const int w13_rows[2] = {kDecHidden, kDecHidden};
+            const uint16_t *w2_parts[1] = {L.w2};
+            const int w2_rows[1] = {kDecDim};
+            o.qkv = fuse(qkv_parts, qkv_rows, 3, kDecDim, false);
+            o.wo = ok ? fuse(wo_parts, wo_rows, 1, kQDim, false) : nullptr;
+            o.w13 = ok ? fuse(w13_parts, w13_rows, 2, kDecDim, true) : nullptr;
+            o.w2 = ok ? fuse(w2_parts, w2_rows, 1, kDecHidden, false) : nullptr;
+            ok &= o.qkv && o.wo && o.w13 && o.w2;
+            if (!ok) break;
         }
         float *norms = (float *)alloc(3 * D * 4);
         if (!norms) {
@@ -847,16 +936,17 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
         }
     }
     if (ok) {
-        uint16_t *emb = (uint16_t *)alloc((size_t)w->vocab * D * 2);
+        const uint16_t *emb_parts[1] = {w->tok_embeddings};
+        const int emb_rows[1] = {w->vocab};
+        d->tok_emb = fuse(emb_parts, emb_rows, 1, kDecDim, false);
         float *nrm = (float *)alloc(D * 4);
-        ok = emb && nrm;
+        ok = d->tok_emb && nrm;
         if (ok) {
-            ok &= cudaMemcpy(emb, w->tok_embeddings, (size_t)w->vocab * D * 2, kind) == cudaSuccess;
             ok &= cudaMemcpy(nrm, w->norm, D * 4, kind) == cudaSuccess;
-            d->tok_emb = emb;
             d->norm = nrm;
         }
     }
+    cudaFree(stage);
     if (!ok) {
         if (!t_err[0]) set_error("decoder_create: weight upload failed");
         vox_cuda_decoder_free(d);

@@ -69,7 +69,8 @@ def lib():
         "vox_cuda_last_error": ([], C.c_char_p),
         "vox_cuda_memory_used": ([], C.c_size_t),
         "vox_cuda_sgemm_bf16": ([C.c_int, C.c_int, C.c_int, _fp, _u16p, _fp, _fp], C.c_int),
-        "vox_cuda_warmup_bf16": ([_u16p, C.c_size_t], C.c_int),
+        "vox_cuda_warmup_bf16": ([_u16p, C.c_int, C.c_int], C.c_int),
+        "vox_cuda_weight_cache_clear": ([], None),
         "vox_cuda_linear_bf16_dev": ([C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
         "vox_cuda_decoder_create": ([C.c_void_p], C.c_void_p),
