@@ -52,7 +52,8 @@ def test_argument_errors_are_reported_before_device_use():
     x = np.zeros((1, 12), np.float32)
     W = np.zeros((8, 12), np.uint16)
     y = np.zeros((1, 8), np.float32)
-    # K not a multiple of 8 -> VOX_CUDA_ERR_ARG regardless of the device
-    assert lib.vox_cuda_sgemm_bf16(1, 8, 12, V._f(x), V._u16(W), None, V._f(y)) == V.ERR_ARG
+    # bad shapes / NULL operands -> VOX_CUDA_ERR_ARG regardless of the device
+    assert lib.vox_cuda_sgemm_bf16(1, 8, 12, None, V._u16(W), None, V._f(y)) == V.ERR_ARG
     assert lib.vox_cuda_sgemm_bf16(0, 8, 8, V._f(x), V._u16(W), None, V._f(y)) == V.ERR_ARG
+    assert lib.vox_cuda_sgemm_bf16(1, 8, -8, V._f(x), V._u16(W), None, V._f(y)) == V.ERR_ARG
     assert lib.vox_cuda_decoder_step_batch(None, 9, None, None) == V.ERR_ARG
