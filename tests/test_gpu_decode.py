@@ -107,13 +107,14 @@ def test_rope_dev_matches_reference():
         cs = torch.from_numpy(g["freqs128"][i].copy()).cuda()
         V.check(V.lib().vox_cuda_rope_dev(dx.data_ptr(), 32, 128, int(p), cs.data_ptr(), None), "rope")
         torch.cuda.synchronize()
-        assert np.array_equal(dx.cpu().numpy(), g["apply128"][i])
-        # the device-side table (host formula, glibc powf) stays within the
-        # reference's own ulp spread
+        # same table: equal up to the FMA contraction the reference's -O3 build
+        # applies to a*c - b*s (the kernel rounds each product)
+        np.testing.assert_allclose(dx.cpu().numpy(), g["apply128"][i], rtol=2e-6, atol=2e-6)
+        # table derived by the library (glibc powf/cosf/sinf, as the oracle)
         dx2 = torch.from_numpy(x[i].copy()).cuda()
         V.check(V.lib().vox_cuda_rope_dev(dx2.data_ptr(), 32, 128, int(p), None, None), "rope")
         want = B.apply_rope(x[i:i + 1], B.rope_freqs([p], 128), 32, 128)[0]
-        assert np.array_equal(dx2.cpu().numpy(), want)
+        np.testing.assert_allclose(dx2.cpu().numpy(), want, rtol=2e-6, atol=2e-6)
 
 
 # ---------------------------------------------------------------------------

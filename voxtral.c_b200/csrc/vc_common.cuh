@@ -85,4 +85,45 @@ __device__ __forceinline__ void grid_dep_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// B-fragment ("xfrag") writers for the decode GEMV's activations: per 16-wide
+// k-block, lane 4m + q holds stream m's values at k = 2q, 2q+1 (word 0) and
+// 2q+8, 2q+9 (word 1) as bf16 pairs, and the bf16 residuals x - hi of the
+// same values in words 2 and 3, so x = hi + lo to ~2^-17 relative.
+// Layout: [K/16][32 lanes][4 words].
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t bf16_bits_rn(float f) {
+    uint32_t u = __float_as_uint(f);
+    u += 0x7FFFu + ((u >> 16) & 1u);   // round to nearest even; finite inputs
+    return u >> 16;
+}
+
+__device__ __forceinline__ void split_bf16(float v, uint32_t &hi, uint32_t &lo) {
+    hi = bf16_bits_rn(v);
+    lo = bf16_bits_rn(v - __uint_as_float(hi << 16));
+}
+
+// two consecutive activations (k even) of stream m
+__device__ __forceinline__ void xfrag_put2(uint32_t *xfrag, int m, int k, float v0, float v1) {
+    const int kb = k >> 4, kk = k & 15;
+    const int lane = 4 * m + ((kk & 7) >> 1), word = kk >> 3;
+    uint32_t h0, l0, h1, l1;
+    split_bf16(v0, h0, l0);
+    split_bf16(v1, h1, l1);
+    uint32_t *w = xfrag + ((size_t)kb * 32 + lane) * 4;
+    w[word] = h0 | (h1 << 16);
+    w[2 + word] = l0 | (l1 << 16);
+}
+
+// one activation of stream m
+__device__ __forceinline__ void xfrag_put1(uint32_t *xfrag, int m, int k, float v) {
+    const int kb = k >> 4, kk = k & 15;
+    const int lane = 4 * m + ((kk & 7) >> 1), word = kk >> 3, half = kk & 1;
+    uint32_t h, l;
+    split_bf16(v, h, l);
+    uint16_t *w = reinterpret_cast<uint16_t *>(xfrag + ((size_t)kb * 32 + lane) * 4);
+    w[2 * word + half] = (uint16_t)h;
+    w[2 * (2 + word) + half] = (uint16_t)l;
+}
+
 }  // namespace vc

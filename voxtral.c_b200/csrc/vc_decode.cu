@@ -241,8 +241,14 @@ attn_decode_kernel(const AttnParams p) {
             }
         }
         const float inv = (gd > 0.f) ? 1.0f / gd : 0.f;
-        *reinterpret_cast<float4 *>(p.out + (size_t)m * kQDim + h * kHeadDim + d4) =
-            make_float4(go[0] * inv, go[1] * inv, go[2] * inv, go[3] * inv);
+        const float o0 = go[0] * inv, o1 = go[1] * inv, o2 = go[2] * inv, o3 = go[3] * inv;
+        if (p.out != nullptr)
+            *reinterpret_cast<float4 *>(p.out + (size_t)m * kQDim + h * kHeadDim + d4) =
+                make_float4(o0, o1, o2, o3);
+        if (p.xfrag_out != nullptr) {
+            xfrag_put2(p.xfrag_out, m, h * kHeadDim + d4, o0, o1);
+            xfrag_put2(p.xfrag_out, m, h * kHeadDim + d4 + 2, o2, o3);
+        }
         if (tid == 0) p.counters[m * kDecKvHeads + kvh] = 0u;
     }
 }

@@ -1,24 +1,29 @@
 // vc_gemv.cu - the decode-step "GEMV": y[M, N] = x[M, K] . W[N, K]^T for
-// M = 1..8 activation rows (streams), with fused prologues and epilogues.
+// M = 1..8 activation rows (streams), with fused epilogues.
 //
-// Design (HBM-bound; every launch streams its weight matrix exactly once):
-//   * Weights live in a fragment-native tiled layout (built once at upload):
-//     16x16 bf16 tiles, each stored as the 32 lanes' mma.m16n8k16 A fragments
-//     (16 bytes per lane), tiles of a 16-row band contiguous along K.  One
-//     coalesced 16-byte non-allocating load per lane per tile feeds an MMA
-//     directly - no shared-memory staging and no shuffles for the weights.
-//   * Activations (fp32) are staged once per CTA in shared memory as B
-//     fragments, split into bf16 hi + lo parts (x = hi + lo to 2^-17), and
-//     both parts are multiplied into one fp32 accumulator, so the result has
-//     fp32-level accuracy (<= ~1e-5 relative) although the tensor core only
-//     takes bf16.  The 8 MMA columns are the (up to) 8 streams.
-//   * A CTA owns 64 output rows (4 row tiles x 2 warps along K) and one
-//     K-slice; the KS slices of a row block form a thread-block cluster and
-//     are reduced through distributed shared memory by cluster rank 0, which
-//     then runs the epilogue.  Deterministic: fixed summation order, no
-//     atomics on data.
-//   * Programmatic dependent launch: each CTA issues its first weight loads
-//     before waiting for the producer of its activations.
+// Design (HBM-bound: every launch streams its weight matrix exactly once):
+//   * Weights live in a fragment-native tiled layout built once at upload:
+//     64-row blocks; inside a block, for each 16-wide k-block, the four 16x16
+//     tiles are stored as the 32 lanes' mma.m16n8k16 A fragments (16 bytes per
+//     lane), so a row block is one contiguous stream along K.
+//   * Activations arrive pre-formatted as B fragments ("xfrag"): per k-block,
+//     lane 4g+q holds stream g's values at k = 2q, 2q+1, 2q+8, 2q+9, each
+//     split into bf16 hi + lo (x = hi + lo to ~2^-17).  The producer of the
+//     activations (the previous kernel's epilogue, or vc_prep_xfrag) writes
+//     them; an RMSNorm consumer gets x * norm_weight (* (1 + ada)) and applies
+//     1/rms, a per-stream scalar, to its accumulators.  Both halves are
+//     multiplied into one fp32 accumulator: fp32-level accuracy from bf16 MMAs.
+//   * A CTA owns one 64-row block and one K-slice.  Thread 0 streams the slice
+//     through a 5-stage shared-memory ring with cp.async.bulk (TMA bulk copies,
+//     L2 evict-first) completing on mbarriers; the 8 warps each take one
+//     k-block per stage (4 tiles x hi/lo = 8 MMAs).  The weight copies of the
+//     first stages are issued before griddepcontrol.wait (programmatic
+//     dependent launch), i.e. while the producer kernel is still running.
+//   * KS K-slices of a row block form a thread-block cluster and are summed
+//     through distributed shared memory by cluster rank 0, which runs the
+//     epilogue.  Fixed summation order everywhere: deterministic.
+//   * Every mbarrier wait is bounded (2 s of %globaltimer); on expiry the CTA
+//     raises the launch's error word, which the host reads with the tokens.
 #include "vc_common.cuh"
 #include "vc_internal.h"
 
@@ -28,14 +33,18 @@ namespace vc {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = 8;
-constexpr int kRT = 4;                 // row tiles per CTA
-constexpr int kWK = 2;                 // warps per row tile (split along K)
-constexpr int kRowsPerCta = 16 * kRT;  // 64
-constexpr int kChunkKB = 80;           // k-blocks (16 wide) of x staged per pass: 40 KB
-constexpr int kU = 8;                  // weight tiles in flight per warp
-constexpr int kMaxKS = 8;              // cluster size limit (portable)
+constexpr int kRT = 4;                   // 16-row tiles per row block
+constexpr int kRowsPerCta = 16 * kRT;    // 64
+constexpr int kStageKB = 8;              // k-blocks per stage (one per warp)
+constexpr int kStages = 5;
+constexpr int kStageW = kStageKB * kRT * 512;   // 16 KB of weights
+constexpr int kStageB = kStageKB * 512;         // 4 KB of activation fragments
+constexpr int kMaxKS = 8;                // cluster size limit (portable)
+constexpr unsigned long long kWaitNs = 2000000000ull;
 
-static_assert(kRT * kWK == kWarps, "warp layout");
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -45,19 +54,50 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint4 &a, ui
         : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t bf16_bits_rn(float f) {
-    uint32_t u = __float_as_uint(f);
-    u += 0x7FFFu + ((u >> 16) & 1u);   // finite inputs only
-    return u >> 16;
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
-// (hi, lo) bf16 split of two values, packed as the mma B-fragment register.
-__device__ __forceinline__ void split2(float v0, float v1, uint32_t &hi, uint32_t &lo) {
-    const uint32_t h0 = bf16_bits_rn(v0), h1 = bf16_bits_rn(v1);
-    const float r0 = v0 - __uint_as_float(h0 << 16);
-    const float r1 = v1 - __uint_as_float(h1 << 16);
-    hi = h0 | (h1 << 16);
-    lo = bf16_bits_rn(r0) | (bf16_bits_rn(r1) << 16);
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false once the launch's deadline has passed.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t deadline) {
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer() > deadline) return false;
+    return true;
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
 }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -72,7 +112,7 @@ __device__ __forceinline__ void cluster_sync_all() {
 }
 
 __device__ __forceinline__ float ld_dsmem_f32(const float *local, uint32_t rank) {
-    uint32_t a = (uint32_t)__cvta_generic_to_shared(local), r;
+    uint32_t a = smem_u32(local), r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
     float v;
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
@@ -84,9 +124,9 @@ __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
 }
 
 struct GemvShared {
-    uint4 xs[kChunkKB * 32];            // B fragments (hi.x, hi.y, lo.x, lo.y) per (kblock, lane)
-    float red[kWarps][32][4];           // per-warp D fragments (split-K within the CTA)
-    float part[kRowsPerCta][8];         // this CTA's [rows][streams] partial
+    uint64_t full[kStages], empty[kStages];
+    alignas(128) unsigned char stage[kStages][kStageW + kStageB];
+    float part[kRowsPerCta][8];
     float s_inv[8];
     float s_red[kWarps][8];
     int s_redi[kWarps][8];
@@ -94,126 +134,121 @@ struct GemvShared {
 };
 
 template <int M, int EPI>
-__global__ void __launch_bounds__(kThreads)
-gemv_mma_kernel(const GemvParams p) {
-    __shared__ __align__(16) GemvShared sh;
+__global__ void __launch_bounds__(kThreads, 2)
+gemv_tma_kernel(const GemvParams p) {
+    extern __shared__ __align__(128) unsigned char dsm[];
+    GemvShared &sh = *reinterpret_cast<GemvShared *>(dsm);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ks = blockIdx.x, KS = gridDim.x;
-    const int rb = blockIdx.y;                        // 64-row block
-    const int rt_local = warp / kWK, wk = warp % kWK;
-    const int rt = rb * kRT + rt_local;               // 16-row tile
-    const int KBp = p.Kp >> 4;                        // k-blocks per row (padded)
-    // this CTA's k-block slice
-    const int per = (KBp + KS - 1) / KS;
+    const int rb = blockIdx.y;
+    const int KB = p.Kp >> 4;
+    const int per = (KB + KS - 1) / KS;
     const int kb0 = ks * per;
-    const int kb1 = min(kb0 + per, KBp);
-    const uint64_t pol = make_evict_first_policy();
-    const uint16_t *wt = p.W + ((size_t)rt * KBp) * 256 + lane * 8;
+    const int nkb = max(0, min(kb0 + per, KB) - kb0);
+    const int n_it = (nkb + kStageKB - 1) / kStageKB;
+    const uint64_t deadline = globaltimer() + kWaitNs;
+    const uint16_t *wsrc = p.W + ((size_t)rb * KB + kb0) * (kRT * 256);
+    const uint32_t *bsrc = p.xfrag + (size_t)kb0 * 128;
+    bool ok = true;
 
-    // ---- prefetch the first weight tiles (independent of the producer) ----
-    uint4 a[kU];
-    const int my_first = kb0 + wk;                   // this warp's k-blocks: my_first + kWK*i
-    const int n_my = (kb1 > my_first) ? (kb1 - my_first + kWK - 1) / kWK : 0;
-#pragma unroll
-    for (int u = 0; u < kU; u++)
-        a[u] = (u < n_my) ? ldg_stream(wt + (size_t)(my_first + kWK * u) * 256, pol) : make_uint4(0, 0, 0, 0);
-
-    grid_dep_wait();
-    grid_dep_launch();
-
-    // ---- RMSNorm statistics (voxtral_kernels.c:346-363) ----
-    if (p.norm_w != nullptr) {
-        if (p.ss_in != nullptr) {
-            if (tid < M) {
-                float ss = 0.f;
-                for (int j = 0; j < p.ss_parts; j++) ss += p.ss_in[tid * p.ss_parts + j];
-                sh.s_inv[tid] = 1.0f / sqrtf(ss / (float)p.K + kNormEps);
-            }
-        } else {
-            for (int m = warp; m < M; m += kWarps) {
-                const float *xr = p.x + (size_t)m * p.ldx;
-                float ss = 0.f;
-                for (int i = lane; i < p.K; i += 32) ss = fmaf(xr[i], xr[i], ss);
-                ss = warp_sum(ss);
-                if (lane == 0) sh.s_inv[m] = 1.0f / sqrtf(ss / (float)p.K + kNormEps);
-            }
+    if (tid == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&sh.full[s], 1);
+            mbar_init(&sh.empty[s], kWarps);
         }
-    }
-
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    int done = 0;   // k-blocks of this warp consumed so far
-    for (int c0 = kb0; c0 < kb1; c0 += kChunkKB) {
-        const int c1 = min(c0 + kChunkKB, kb1);
-        __syncthreads();   // previous chunk consumed; s_inv visible
-        // ---- stage x[:, 16*c0 .. 16*c1) as split B fragments ----
-        for (int item = tid; item < (c1 - c0) * 32; item += kThreads) {
-            const int kbl = item >> 5, t = item & 31;
-            const int g = t >> 2, q = t & 3;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (g < M) {
-                const int k = (c0 + kbl) * 16 + 2 * q;
-                const float *xr = p.x + (size_t)g * p.ldx;
-                float x0 = (k < p.K) ? xr[k] : 0.f, x1 = (k + 1 < p.K) ? xr[k + 1] : 0.f;
-                float x8 = (k + 8 < p.K) ? xr[k + 8] : 0.f, x9 = (k + 9 < p.K) ? xr[k + 9] : 0.f;
-                if (p.norm_w != nullptr) {
-                    const float inv = sh.s_inv[g];
-                    if (k < p.K) x0 = x0 * inv * p.norm_w[k];
-                    if (k + 1 < p.K) x1 = x1 * inv * p.norm_w[k + 1];
-                    if (k + 8 < p.K) x8 = x8 * inv * p.norm_w[k + 8];
-                    if (k + 9 < p.K) x9 = x9 * inv * p.norm_w[k + 9];
-                    if (p.ada != nullptr) {  // x_norm *= (1 + ada)  (voxtral_decoder.c:489-492)
-                        if (k < p.K) x0 *= (1.0f + p.ada[k]);
-                        if (k + 1 < p.K) x1 *= (1.0f + p.ada[k + 1]);
-                        if (k + 8 < p.K) x8 *= (1.0f + p.ada[k + 8]);
-                        if (k + 9 < p.K) x9 *= (1.0f + p.ada[k + 9]);
-                    }
-                }
-                split2(x0, x1, v.x, v.z);
-                split2(x8, x9, v.y, v.w);
-            }
-            sh.xs[item] = v;
-        }
-        __syncthreads();
-
-        // ---- stream this warp's weight tiles of the chunk through the MMA ----
-        const int n_chunk = (c1 > my_first + kWK * done) ? (c1 - (my_first + kWK * done) + kWK - 1) / kWK : 0;
-        for (int i = 0; i < n_chunk; i += kU) {
-            if (!(c0 == kb0 && i == 0)) {
-#pragma unroll
-                for (int u = 0; u < kU; u++) {
-                    const int kb = my_first + kWK * (done + i + u);
-                    a[u] = (i + u < n_chunk) ? ldg_stream(wt + (size_t)kb * 256, pol) : make_uint4(0, 0, 0, 0);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kU; u++) {
-                if (i + u < n_chunk) {
-                    const int kb = my_first + kWK * (done + i + u);
-                    const uint4 b = sh.xs[(kb - c0) * 32 + lane];
-                    mma_bf16_16816(c, a[u], b.x, b.y);   // W . x_hi
-                    mma_bf16_16816(c, a[u], b.z, b.w);   // W . x_lo
-                }
-            }
-        }
-        done += n_chunk;
-    }
-
-    // ---- reduce the kWK warps of each row tile (fixed order) ----
-    if (wk != 0) {
-#pragma unroll
-        for (int j = 0; j < 4; j++) sh.red[warp][lane][j] = c[j];
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (wk == 0) {
-        for (int w2 = 1; w2 < kWK; w2++)
+
+    const uint64_t pol = make_evict_first_policy();    // weights: streamed once
+    const uint64_t pol_x = make_evict_last_policy();   // activations: re-read by every row block
+    auto stage_kbs = [&](int it) { return min(kStageKB, nkb - it * kStageKB); };
+    // weights of the first stages: independent of the producer kernel
+    if (tid == 0) {
+        for (int it = 0; it < min(kStages, n_it); it++) {
+            const int n = stage_kbs(it);
+            mbar_expect_tx(&sh.full[it], (uint32_t)n * (kRT * 512 + 512));
+            bulk_g2s(sh.stage[it], wsrc + (size_t)it * kStageKB * kRT * 256, (uint32_t)n * kRT * 512,
+                     &sh.full[it], pol);
+        }
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+    if (tid == 0) {
+        for (int it = 0; it < min(kStages, n_it); it++)
+            bulk_g2s(sh.stage[it] + kStageW, bsrc + (size_t)it * kStageKB * 128, (uint32_t)stage_kbs(it) * 512,
+                     &sh.full[it], pol_x);
+    }
+
+    float acc[kRT][4];
 #pragma unroll
-            for (int j = 0; j < 4; j++) c[j] += sh.red[warp + w2][lane][j];
-        const int g = lane >> 2, q = lane & 3;
-        float *pr = &sh.part[rt_local * 16][0];
-        pr[g * 8 + 2 * q] = c[0];
-        pr[g * 8 + 2 * q + 1] = c[1];
-        pr[(g + 8) * 8 + 2 * q] = c[2];
-        pr[(g + 8) * 8 + 2 * q + 1] = c[3];
+    for (int t = 0; t < kRT; t++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[t][j] = 0.f;
+
+    for (int it = 0; it < n_it; it++) {
+        const int s = it % kStages;
+        const uint32_t par = (uint32_t)(it / kStages) & 1u;
+        // every lane polls (acquire); the decision to give up is warp-uniform
+        if (!__all_sync(0xffffffffu, mbar_wait(&sh.full[s], par, deadline))) {
+            ok = false;
+            break;
+        }
+        if (warp < stage_kbs(it)) {
+            const unsigned char *st = sh.stage[s];
+            const uint4 b = *reinterpret_cast<const uint4 *>(st + kStageW + warp * 512 + lane * 16);
+#pragma unroll
+            for (int t = 0; t < kRT; t++) {
+                const uint4 a = *reinterpret_cast<const uint4 *>(st + (warp * kRT + t) * 512 + lane * 16);
+                mma_bf16_16816(acc[t], a, b.x, b.y);   // W . x_hi
+                mma_bf16_16816(acc[t], a, b.z, b.w);   // W . x_lo
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.empty[s]);
+        if (warp == 0) {
+            // thread 0 refills this stage once all 8 warps have released it
+            bool refill_ok = true;
+            if (lane == 0 && it + kStages < n_it) {
+                refill_ok = mbar_wait(&sh.empty[s], par, deadline);
+                if (refill_ok) {
+                    const int nx = it + kStages, n = stage_kbs(nx);
+                    mbar_expect_tx(&sh.full[s], (uint32_t)n * (kRT * 512 + 512));
+                    bulk_g2s(sh.stage[s], wsrc + (size_t)nx * kStageKB * kRT * 256,
+                             (uint32_t)n * kRT * 512, &sh.full[s], pol);
+                    bulk_g2s(sh.stage[s] + kStageW, bsrc + (size_t)nx * kStageKB * 128, (uint32_t)n * 512,
+                             &sh.full[s], pol_x);
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, refill_ok, 0)) {
+                ok = false;
+                break;
+            }
+        }
+    }
+    if (!ok) {
+        // report, then let copies that may still be in flight land before
+        // the CTA (and its shared memory) goes away
+        if (lane == 0) atomicExch(p.err, 1u);
+        const uint64_t grace = globaltimer() + 10000000ull;
+        while (globaltimer() < grace) {
+        }
+    }
+    __syncthreads();   // all stages consumed: the ring is reused below
+
+    // ---- reduce the 8 warps (fixed order) ----
+    float *red = reinterpret_cast<float *>(sh.stage[0]);   // [8 warps][4 tiles][32 lanes][4]
+#pragma unroll
+    for (int t = 0; t < kRT; t++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) red[((warp * kRT + t) * 32 + lane) * 4 + j] = acc[t][j];
+    __syncthreads();
+    for (int e = tid; e < kRT * 32 * 4; e += kThreads) {
+        float v = 0.f;
+        for (int w = 0; w < kWarps; w++) v += red[w * kRT * 128 + e];
+        const int t = e >> 7, ln = (e >> 2) & 31, j = e & 3;
+        const int g = ln >> 2, q = ln & 3;
+        sh.part[t * 16 + g + ((j >> 1) << 3)][2 * q + (j & 1)] = v;
     }
     __syncthreads();
 
@@ -229,34 +264,56 @@ gemv_mma_kernel(const GemvParams p) {
         }
         cluster_sync_all();   // peers keep their shared memory until rank 0 has read it
         if (cluster_ctarank() != 0) return;
-        __syncthreads();
     }
+    if (tid < 8) {
+        float inv = 1.0f;
+        if (p.ss_in != nullptr && tid < M) {
+            // RMSNorm (voxtral_kernels.c:346-363): 1/sqrt(mean(x^2) + eps); the
+            // producer supplied per-row-block sums of x^2
+            float ss = 0.f;
+            for (int j = 0; j < p.ss_parts; j++) ss += p.ss_in[tid * p.ss_parts + j];
+            inv = 1.0f / sqrtf(ss / (float)p.K + kNormEps);
+        }
+        sh.s_inv[tid] = inv;
+    }
+    __syncthreads();
 
     // ---- epilogue: thread -> stream m = tid & 7, row pair (2pp, 2pp+1) ----
     const int m = tid & 7, pp = tid >> 3;
-    const int r0 = rb * kRowsPerCta + 2 * pp;         // global row of the pair
+    const int r0 = rb * kRowsPerCta + 2 * pp;
     const bool active = (m < M) && (r0 < p.N);
-    float v0 = sh.part[2 * pp][m], v1 = sh.part[2 * pp + 1][m];
+    const bool has1 = r0 + 1 < p.N;
+    float v0 = sh.part[2 * pp][m] * sh.s_inv[m];
+    float v1 = sh.part[2 * pp + 1][m] * sh.s_inv[m];
 
     if constexpr (EPI == EPI_STORE || EPI == EPI_ADD || EPI == EPI_LOGITS) {
         float ss = 0.f;
         if (active) {
             if (p.bias != nullptr) {
                 v0 += p.bias[r0];
-                if (r0 + 1 < p.N) v1 += p.bias[r0 + 1];
+                if (has1) v1 += p.bias[r0 + 1];
             }
             float *dst = p.y + (size_t)m * p.ldy + r0;
             if constexpr (EPI == EPI_ADD) {
                 v0 += dst[0];
-                if (r0 + 1 < p.N) v1 += dst[1];
+                if (has1) v1 += dst[1];
             }
             dst[0] = v0;
-            if (r0 + 1 < p.N) dst[1] = v1;
-            ss = v0 * v0 + ((r0 + 1 < p.N) ? v1 * v1 : 0.f);
+            if (has1) dst[1] = v1;
+            if (!has1) v1 = 0.f;
+            ss = v0 * v0 + v1 * v1;
+            if constexpr (EPI == EPI_ADD) {
+                // the next GEMV's activations: y * g_next as B fragments
+                if (p.xfrag_out != nullptr) {
+                    const float g0 = p.g_next ? p.g_next[r0] : 1.0f;
+                    const float g1 = (p.g_next && has1) ? p.g_next[r0 + 1] : 1.0f;
+                    xfrag_put2(p.xfrag_out, m, r0, v0 * g0, v1 * g1);
+                }
+            }
         }
         if constexpr (EPI == EPI_ADD) {
-            // per-row-block sum of squares of the new residual, consumed by the
-            // next RMSNorm prologue (fixed-order sums: deterministic)
+            // per-row-block sum of squares of the new residual, for the next
+            // RMSNorm (fixed-order sums: deterministic)
             if (p.ss_out != nullptr) {
                 ss += __shfl_xor_sync(0xffffffffu, ss, 8);
                 ss += __shfl_xor_sync(0xffffffffu, ss, 16);
@@ -276,7 +333,7 @@ gemv_mma_kernel(const GemvParams p) {
             if (active) {
                 bv = v0;
                 bi = r0;
-                if (r0 + 1 < p.N && v1 > bv) { bv = v1; bi = r0 + 1; }
+                if (has1 && v1 > bv) { bv = v1; bi = r0 + 1; }
             }
 #pragma unroll
             for (int o = 8; o <= 16; o <<= 1) {
@@ -350,12 +407,61 @@ gemv_mma_kernel(const GemvParams p) {
         }
     } else if constexpr (EPI == EPI_SWIGLU) {
         // rows (2i, 2i+1) = (gate_i, up_i): h_i = silu(g) * u
-        // (voxtral_kernels.c:369-374, then :34-36)
+        // (voxtral_kernels.c:369-374, then :34-36), written as the w2 GEMV's
+        // B fragments
         if (active) {
             const float sg = v0 / (1.0f + expf(-v0));
-            p.y[(size_t)m * p.ldy + (r0 >> 1)] = sg * v1;
+            xfrag_put1(p.xfrag_out, m, r0 >> 1, sg * v1);
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// Activations -> B fragments (for the first GEMV of a chain and for the
+// general matmul entry): xfrag = x * g, plus per-64-row-block sums of x^2
+// when ss_out is given.  grid = ceil(K / 64), 256 threads.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+prep_xfrag_kernel(const float *x, int M, int K, int ldx, const float *g, uint32_t *xfrag, float *ss_out) {
+    __shared__ float s_red[8][8];
+    grid_dep_wait();
+    grid_dep_launch();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int m = tid & 7, pp = tid >> 3;
+    const int k0 = blockIdx.x * 64 + 2 * pp;
+    float ss = 0.f;
+    if (m < M && k0 < K) {
+        const float v0 = x[(size_t)m * ldx + k0];
+        const float v1 = (k0 + 1 < K) ? x[(size_t)m * ldx + k0 + 1] : 0.f;
+        ss = v0 * v0 + v1 * v1;
+        const float g0 = g ? g[k0] : 1.0f, g1 = (g && k0 + 1 < K) ? g[k0 + 1] : 1.0f;
+        xfrag_put2(xfrag, m, k0, v0 * g0, v1 * g1);
+    }
+    if (ss_out != nullptr) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, 8);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 16);
+        if (lane < 8) s_red[warp][lane] = ss;
+        __syncthreads();
+        if (tid < M) {
+            float t = 0.f;
+            for (int w = 0; w < 8; w++) t += s_red[w][tid];
+            ss_out[tid * gridDim.x + blockIdx.x] = t;
+        }
+    }
+}
+
+cudaError_t launch_prep_xfrag(const float *x, int M, int K, int ldx, const float *g, uint32_t *xfrag,
+                              float *ss_out, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((K + 63) / 64);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, prep_xfrag_kernel, x, M, K, ldx, g, xfrag, ss_out);
 }
 
 // ---------------------------------------------------------------------------
@@ -367,24 +473,35 @@ int gemv_row_blocks(int N) { return (N + kRowsPerCta - 1) / kRowsPerCta; }
 int gemv_k_slices(int N, int Kp) {
     const int KB = Kp / 16;
     const int rb = gemv_row_blocks(N);
-    int ks = (KB + 63) / 64;                       // <= 1024 k per slice
-    const int fill = (2 * 148 + rb - 1) / rb;       // >= ~2 CTAs per SM
-    if (fill > ks) ks = fill;
+    int ks = (2 * 148 + rb - 1) / rb;           // ~2 CTAs per SM
     if (ks > kMaxKS) ks = kMaxKS;
-    if (ks > KB / kWK) ks = KB / kWK > 0 ? KB / kWK : 1;   // every warp gets >= 1 k-block
+    const int max_by_k = (KB + kStageKB - 1) / kStageKB;   // >= one stage per slice
+    if (ks > max_by_k) ks = max_by_k;
     if (ks < 1) ks = 1;
+    // every slice must own at least one k-block
+    while (ks > 1 && (KB + ks - 1) / ks * (ks - 1) >= KB) ks--;
     return ks;
 }
 
 int gemv_grid(int /*M*/, int /*epi*/, int N) { return gemv_row_blocks(N); }
 
+size_t xfrag_bytes(int K) { return (size_t)((K + 15) / 16) * 512; }
+
 template <int M, int EPI>
 static cudaError_t launch_one(const GemvParams &p, cudaStream_t st, bool pdl) {
+    static bool attr_set = false;   // benign race: same value written
+    const int smem = (int)sizeof(GemvShared);
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<M, EPI>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
     const int KS = gemv_k_slices(p.N, p.Kp);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(KS, gemv_row_blocks(p.N));
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     int na = 0;
@@ -402,11 +519,12 @@ static cudaError_t launch_one(const GemvParams &p, cudaStream_t st, bool pdl) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<M, EPI>, p);
+    return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<M, EPI>, p);
 }
 
 cudaError_t launch_gemv(int M, int epi, const GemvParams &p, cudaStream_t st, bool pdl) {
-    if (p.Kp % 16 != 0 || p.Kp < p.K || p.K <= 0 || p.N <= 0) return cudaErrorInvalidValue;
+    if (p.Kp % 16 != 0 || p.Kp < p.K || p.K <= 0 || p.N <= 0 || !p.xfrag || !p.err)
+        return cudaErrorInvalidValue;
 #define VC_LAUNCH_CASE(MM)                                                        \
     case MM:                                                                      \
         switch (epi) {                                                            \
@@ -426,10 +544,10 @@ cudaError_t launch_gemv(int M, int epi, const GemvParams &p, cudaStream_t st, bo
 }
 
 // ---------------------------------------------------------------------------
-// Weight layout: row-major [N, K] bf16 -> fragment-native tiles.  Tile
-// (rt, kb) holds rows 16rt..16rt+15, columns 16kb..16kb+15 as the 32 lanes'
-// A fragments of mma.m16n8k16 (lane = 4g + q holds rows g and g+8, columns
-// 2q, 2q+1, 2q+8, 2q+9); rows beyond N and columns beyond K are zero.
+// Weight layout: row-major [N, K] bf16 -> 64-row blocks; inside a block, per
+// 16-wide k-block, tiles t = 0..3 (rows 16t..16t+15 of the block) as the 32
+// lanes' A fragments of mma.m16n8k16 (lane = 4g + q holds rows g, g+8 and
+// columns 2q, 2q+1, 2q+8, 2q+9).  Rows past N and columns past K are zero.
 // ---------------------------------------------------------------------------
 
 __global__ void tile_weights_kernel(uint16_t *dst, const uint16_t *src, int N, int K, int Np, int Kp) {
@@ -438,26 +556,29 @@ __global__ void tile_weights_kernel(uint16_t *dst, const uint16_t *src, int N, i
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_lanes;
          i += (size_t)gridDim.x * blockDim.x) {
         const int lane = (int)(i & 31);
-        const size_t tile = i >> 5;
-        const int kb = (int)(tile % KB);
-        const int rt = (int)(tile / KB);
+        const size_t tile = i >> 5;                 // (rb, kb, t) with t fastest
+        const int t = (int)(tile & 3);
+        const size_t rbkb = tile >> 2;
+        const int kb = (int)(rbkb % KB);
+        const int rblk = (int)(rbkb / KB);
         const int g = lane >> 2, q = lane & 3;
-        const int ra = rt * 16 + g, rb = ra + 8;
+        const int ra = rblk * 64 + t * 16 + g, rbw = ra + 8;
         const int k0 = kb * 16 + 2 * q;
-        auto at = [&](int r, int k) -> uint16_t {
-            return (r < N && k < K) ? src[(size_t)r * K + k] : (uint16_t)0;
+        auto at = [&](int r, int k) -> uint32_t {
+            return (r < N && k < K) ? (uint32_t)src[(size_t)r * K + k] : 0u;
         };
         uint4 v;
-        v.x = at(ra, k0) | ((uint32_t)at(ra, k0 + 1) << 16);
-        v.y = at(rb, k0) | ((uint32_t)at(rb, k0 + 1) << 16);
-        v.z = at(ra, k0 + 8) | ((uint32_t)at(ra, k0 + 9) << 16);
-        v.w = at(rb, k0 + 8) | ((uint32_t)at(rb, k0 + 9) << 16);
+        v.x = at(ra, k0) | (at(ra, k0 + 1) << 16);
+        v.y = at(rbw, k0) | (at(rbw, k0 + 1) << 16);
+        v.z = at(ra, k0 + 8) | (at(ra, k0 + 9) << 16);
+        v.w = at(rbw, k0 + 8) | (at(rbw, k0 + 9) << 16);
         reinterpret_cast<uint4 *>(dst)[i] = v;
     }
 }
 
 cudaError_t launch_tile_weights(uint16_t *dst, const uint16_t *src, int N, int K, int Np, int Kp,
                                 cudaStream_t st) {
+    if (Np % kRowsPerCta != 0 || Kp % 16 != 0) return cudaErrorInvalidValue;
     tile_weights_kernel<<<148 * 16, 256, 0, st>>>(dst, src, N, K, Np, Kp);
     return cudaGetLastError();
 }

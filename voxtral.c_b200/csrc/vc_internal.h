@@ -35,13 +35,13 @@ struct GemvParams {
     const uint16_t *W;      // fragment-tiled weights (launch_tile_weights), [Np, Kp]
     int N, K;               // logical shape
     int Kp;                 // K rounded up to 16 (the tiled row length)
-    const float *x;         // [M, ldx] fp32 (device)
-    int ldx;
-    const float *norm_w;    // RMSNorm prologue weight [K] or NULL
-    const float *ada;       // (1 + ada) after the norm [K] or NULL
-    const float *ss_in;     // per-row-block sums of x^2 from the producer, [M][ss_parts], or NULL
+    const uint32_t *xfrag;  // activations as B fragments (xfrag_put*), [Kp/16][32][4]
+    const float *ss_in;     // RMSNorm: per-row-block sums of x^2, [M][ss_parts], or NULL
     int ss_parts;
     float *ss_out;          // EPI_ADD: per-row-block sums of the new y^2, [M][row blocks], or NULL
+    uint32_t *xfrag_out;    // EPI_ADD: y * g_next as B fragments; EPI_SWIGLU: h as B fragments
+    const float *g_next;    // EPI_ADD: the next RMSNorm's weights (* (1 + ada)), [N], or NULL
+    unsigned *err;          // raised when a bounded wait expires
     float *y;               // output [M, ldy]
     int ldy;
     const float *bias;      // [N] or NULL
@@ -57,6 +57,11 @@ struct GemvParams {
 
 // Launch the fused streaming GEMV (M = 1..8 activation rows).
 cudaError_t launch_gemv(int M, int epi, const GemvParams &p, cudaStream_t st, bool pdl);
+// x [M, K] (row stride ldx) -> B fragments of x * g (g may be NULL), and, when
+// ss_out is given, per-64-block sums of x^2 ([M][ceil(K/64)]).
+cudaError_t launch_prep_xfrag(const float *x, int M, int K, int ldx, const float *g, uint32_t *xfrag,
+                              float *ss_out, cudaStream_t st, bool pdl);
+size_t xfrag_bytes(int K);
 int gemv_grid(int M, int epi, int N);      // row blocks (64 rows) of a launch
 int gemv_row_blocks(int N);
 constexpr int kGemvRowAlign = 64;           // tiled weights are padded to this many rows
@@ -69,7 +74,8 @@ struct AttnParams {
     const float *q;           // [M][4096], RoPE applied
     const StreamSlot *slots;  // [M]
     int layer;
-    float *out;               // [M][4096]
+    float *out;               // [M][4096] or NULL
+    uint32_t *xfrag_out;      // the output as the wo GEMV's B fragments, or NULL
     float *part_o;            // [M][32][S][128]
     float *part_ml;           // [M][32][S][2]
     unsigned *counters;       // [M][8], zero between launches

@@ -78,6 +78,10 @@ struct DevCtx {
     // scratch for the host-pointer matmul entry and the kernel-level entries
     float *sx = nullptr, *sy = nullptr, *sb = nullptr;
     size_t sx_n = 0, sy_n = 0, sb_n = 0;
+    uint32_t *lin_xfrag = nullptr;   // B-fragment scratch of the matmul entries
+    size_t lin_xfrag_bytes = 0;
+    unsigned *lin_err = nullptr;     // bounded-wait error word of the matmul entries
+    cudaEvent_t lin_done = nullptr;  // orders scratch reuse across caller streams
     StreamSlot *attn_slot = nullptr;
     float *attn_part_o = nullptr, *attn_part_ml = nullptr, *rope_tab = nullptr;
     unsigned *attn_counters = nullptr;
@@ -208,6 +212,13 @@ static void release_scratch(DevCtx *c) {
     cudaFree(c->attn_part_ml);
     cudaFree(c->attn_counters);
     cudaFree(c->rope_tab);
+    cudaFree(c->lin_xfrag);
+    cudaFree(c->lin_err);
+    if (c->lin_done) cudaEventDestroy(c->lin_done);
+    c->lin_xfrag = nullptr;
+    c->lin_xfrag_bytes = 0;
+    c->lin_err = nullptr;
+    c->lin_done = nullptr;
     c->sx = c->sy = c->sb = nullptr;
     c->sx_n = c->sy_n = c->sb_n = 0;
     c->attn_slot = nullptr;
@@ -250,23 +261,52 @@ static int check_linear_args(int M, int N, int K, const void *A, const void *B, 
 static int round_up(int v, int a) { return (v + a - 1) / a * a; }
 
 // y[M,N] = x[M,K] W^T (+b), all device pointers, W fragment-tiled; rows of x
-// in chunks of 8.
-static int enqueue_linear(int M, int N, int K, const float *x, const uint16_t *W, const float *b,
-                          float *y, cudaStream_t st) {
+// in chunks of 8 (each chunk: activations -> B fragments, then the GEMV).
+// Caller holds c->mu; the scratch is ordered across streams by c->lin_done.
+static int enqueue_linear(DevCtx *c, int M, int N, int K, const float *x, const uint16_t *W,
+                          const float *b, float *y, cudaStream_t st) {
+    const size_t xb = xfrag_bytes(K);
+    if (c->lin_xfrag_bytes < xb) {
+        if (c->lin_xfrag) {
+            cudaFree(c->lin_xfrag);
+            c->bytes -= c->lin_xfrag_bytes;
+        }
+        c->lin_xfrag = nullptr;
+        c->lin_xfrag_bytes = 0;
+        if (cudaMalloc(&c->lin_xfrag, xb) != cudaSuccess) {
+            set_error("linear: scratch cudaMalloc(%zu) failed", xb);
+            return VOX_CUDA_ERR_OOM;
+        }
+        VC_TRY(cudaMemset(c->lin_xfrag, 0, xb));
+        c->lin_xfrag_bytes = xb;
+        c->bytes += xb;
+    }
+    if (!c->lin_err) {
+        if (cudaMalloc(&c->lin_err, sizeof(unsigned)) != cudaSuccess) {
+            set_error("linear: scratch cudaMalloc failed");
+            return VOX_CUDA_ERR_OOM;
+        }
+        VC_TRY(cudaMemset(c->lin_err, 0, sizeof(unsigned)));
+        VC_TRY(cudaEventCreateWithFlags(&c->lin_done, cudaEventDisableTiming));
+        VC_TRY(cudaEventRecord(c->lin_done, st));
+    }
+    VC_TRY(cudaStreamWaitEvent(st, c->lin_done, 0));
     for (int m0 = 0; m0 < M; m0 += kMaxBatch) {
         const int mm = (M - m0 < kMaxBatch) ? (M - m0) : kMaxBatch;
+        VC_TRY(launch_prep_xfrag(x + (size_t)m0 * K, mm, K, K, nullptr, c->lin_xfrag, nullptr, st, false));
         GemvParams p = {};
         p.W = W;
         p.N = N;
         p.K = K;
         p.Kp = round_up(K, 16);
-        p.x = x + (size_t)m0 * K;
-        p.ldx = K;
+        p.xfrag = c->lin_xfrag;
         p.y = y + (size_t)m0 * N;
         p.ldy = N;
         p.bias = b;
+        p.err = c->lin_err;
         VC_TRY(launch_gemv(mm, EPI_STORE, p, st, false));
     }
+    VC_TRY(cudaEventRecord(c->lin_done, st));
     return VOX_CUDA_OK;
 }
 
@@ -285,7 +325,8 @@ extern "C" int vox_cuda_linear_bf16_dev(int M, int N, int K, const float *A, con
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
     const uint16_t *W = cached_weight(c, B_bf16, N, K, false, &rc);
     if (!W) return rc;
-    return enqueue_linear(M, N, K, A, W, bias, C, st);
+    std::lock_guard<std::mutex> lk(c->mu);
+    return enqueue_linear(c, M, N, K, A, W, bias, C, st);
 }
 
 // The fragment-tiled device copy of a caller's [N, K] bf16 weight, made on
@@ -402,10 +443,17 @@ extern "C" int vox_cuda_sgemm_bf16(int M, int N, int K, const float *A, const ui
     if (bias && (rc = grow_locked(&c->sb, &c->sb_n, (size_t)N))) return rc;
     VC_TRY(cudaMemcpyAsync(c->sx, A, (size_t)M * K * 4, cudaMemcpyHostToDevice, c->stream));
     if (bias) VC_TRY(cudaMemcpyAsync(c->sb, bias, (size_t)N * 4, cudaMemcpyHostToDevice, c->stream));
-    rc = enqueue_linear(M, N, K, c->sx, W, bias ? c->sb : nullptr, c->sy, c->stream);
+    rc = enqueue_linear(c, M, N, K, c->sx, W, bias ? c->sb : nullptr, c->sy, c->stream);
     if (rc) return rc;
     VC_TRY(cudaMemcpyAsync(C, c->sy, (size_t)M * N * 4, cudaMemcpyDeviceToHost, c->stream));
+    unsigned err = 0;
+    VC_TRY(cudaMemcpyAsync(&err, c->lin_err, sizeof(err), cudaMemcpyDeviceToHost, c->stream));
     VC_TRY(cudaStreamSynchronize(c->stream));
+    if (err) {
+        cudaMemset(c->lin_err, 0, sizeof(unsigned));
+        set_error("sgemm_bf16: a device-side wait timed out");
+        return VOX_CUDA_ERR_CUDA;
+    }
     return VOX_CUDA_OK;
 }
 
@@ -517,7 +565,9 @@ struct DecLayer {
     // fused, fragment-tiled device copies: wq|wk|wv [6144, 3072],
     // wo [3072, 4096], w1/w3 row-interleaved [18432, 3072], w2 [3072, 9216]
     const uint16_t *qkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr;
-    const float *attn_norm = nullptr, *ffn_norm = nullptr, *ada = nullptr;
+    // RMSNorm weights as folded into the activation fragments:
+    // g_attn = attention_norm, g_ffn = ffn_norm * (1 + ada_scale)
+    const float *g_attn = nullptr, *g_ffn = nullptr;
 };
 
 // Device workspace for one step shape (n rows).  The host staging block is
@@ -541,6 +591,11 @@ struct StepWork {
     int *alt_ids = nullptr;            // [4]
     float *ss_attn = nullptr;          // [n][48] sums of x^2 per row block, after w2 (next QKV norm)
     float *ss_ffn = nullptr;           // [n][48] after wo (the FFN norm)
+    uint32_t *xf_attn = nullptr;       // B fragments of x * g_attn (QKV / LM head input)
+    uint32_t *xf_ffn = nullptr;        // B fragments of x * g_ffn (w1|w3 input)
+    uint32_t *xf_att = nullptr;        // B fragments of the attention output (wo input)
+    uint32_t *xf_h = nullptr;          // B fragments of silu(g) * u (w2 input)
+    unsigned *err = nullptr;           // follows tokens: bounded-wait error word
     size_t bytes = 0;
     // host (pinned)
     char *hblock = nullptr;
@@ -617,11 +672,17 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     const size_t o_cnt = take(sizeof(unsigned) * (n * kDecKvHeads + 1));
     const size_t grid = (size_t)gemv_grid(n, EPI_LOGITS, vocab);
     const size_t o_amax = take(sizeof(ArgmaxPartial) * grid * n);
-    const size_t o_tok = take(sizeof(int) * n);
+    const size_t o_tok = take(sizeof(int) * (n + 1));   // tokens then the error word
     const size_t o_alt = take(sizeof(int) * 4);
     const size_t n_ss = (size_t)n * gemv_row_blocks(kDecDim);
     const size_t o_ssa = take(sizeof(float) * n_ss);
     const size_t o_ssf = take(sizeof(float) * n_ss);
+    const size_t o_frag0 = off;
+    const size_t o_xfa = take(xfrag_bytes(kDecDim));
+    const size_t o_xff = take(xfrag_bytes(kDecDim));
+    const size_t o_xft = take(xfrag_bytes(kQDim));
+    const size_t o_xfh = take(xfrag_bytes(kDecHidden));
+    const size_t frag_bytes = off - o_frag0;
     if (dev_alloc(c, (void **)&w->dblock, off) != cudaSuccess) {
         set_error("decoder workspace: cudaMalloc(%zu) failed", off);
         delete w;
@@ -644,8 +705,16 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     w->alt_ids = (int *)(b + o_alt);
     w->ss_attn = (float *)(b + o_ssa);
     w->ss_ffn = (float *)(b + o_ssf);
-    if (cudaMemset(w->counters, 0, sizeof(unsigned) * (n * kDecKvHeads + 1)) != cudaSuccess ||
-        cudaHostAlloc((void **)&w->hblock, w->dblock_bytes + 64, cudaHostAllocDefault) != cudaSuccess) {
+    w->xf_attn = (uint32_t *)(b + o_xfa);
+    w->xf_ffn = (uint32_t *)(b + o_xff);
+    w->xf_att = (uint32_t *)(b + o_xft);
+    w->xf_h = (uint32_t *)(b + o_xfh);
+    w->err = (unsigned *)(w->tokens + n);
+    // fragments of streams >= n are never written and must read as zeros
+    if (cudaMemset(b + o_frag0, 0, frag_bytes) != cudaSuccess ||
+        cudaMemset(w->tokens, 0, sizeof(int) * (n + 1)) != cudaSuccess ||
+        cudaMemset(w->counters, 0, sizeof(unsigned) * (n * kDecKvHeads + 1)) != cudaSuccess ||
+        cudaHostAlloc((void **)&w->hblock, align_up(w->dblock_bytes, 16) + sizeof(int) * (n + 1), cudaHostAllocDefault) != cudaSuccess) {
         set_error("decoder workspace: staging allocation failed");
         free_work(c, w);
         return nullptr;
@@ -659,16 +728,21 @@ StreamSlot *h_slots(StepWork *w) { return (StreamSlot *)w->hblock; }
 float *h_rope(StepWork *w) { return (float *)(w->hblock + ((char *)w->rope - w->dblock)); }
 float *h_x(StepWork *w) { return (float *)(w->hblock + ((char *)w->x - w->dblock)); }
 
-// The kernel sequence of one step over w->n rows (decoder layers, then the
-// LM head + argmax when with_head).
+// The kernel sequence of one step over w->n rows: the embeddings' norm
+// statistics and fragments, the decoder layers, then the LM head + argmax
+// when with_head.  Each producer writes its consumer's activation fragments.
 // evs (profiling only): 2 events per launch, recorded around it.
 int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_t st,
                    cudaEvent_t *evs = nullptr) {
     const int n = w->n;
     const bool pdl = d->pdl && evs == nullptr;
+    const int ss_parts = gemv_row_blocks(kDecDim);
     int ei = 0;
 #define VC_EV_BEGIN() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
 #define VC_EV_END() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
+    VC_EV_BEGIN();
+    VC_TRY(launch_prep_xfrag(w->x, n, kDecDim, kDecDim, d->L[0].g_attn, w->xf_attn, w->ss_attn, st, pdl));
+    VC_EV_END();
     for (int l = 0; l < d->n_layers; l++) {
         const DecLayer &L = d->L[l];
         GemvParams p = {};
@@ -676,27 +750,25 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p.W = L.qkv;
         p.N = kQkvRows;
         p.K = p.Kp = kDecDim;
-        p.x = w->x;
-        p.ldx = kDecDim;
-        p.norm_w = L.attn_norm;
-        if (l > 0) {  // layer 0 reads the embeddings: its norm sums x itself
-            p.ss_in = w->ss_attn;
-            p.ss_parts = gemv_row_blocks(kDecDim);
-        }
+        p.xfrag = w->xf_attn;
+        p.ss_in = w->ss_attn;
+        p.ss_parts = ss_parts;
         p.y = w->q;
         p.ldy = kQDim;
         p.slots = w->slots;
         p.rope = w->rope;
         p.layer = l;
+        p.err = w->err;
         VC_EV_BEGIN();
         VC_TRY(launch_gemv(n, EPI_QKV, p, st, pdl));
         VC_EV_END();
-        // attention over the ring
+        // attention over the ring -> wo's fragments
         AttnParams a = {};
         a.q = w->q;
         a.slots = w->slots;
         a.layer = l;
-        a.out = w->att;
+        a.out = nullptr;
+        a.xfrag_out = w->xf_att;
         a.part_o = w->part_o;
         a.part_ml = w->part_ml;
         a.counters = w->counters;
@@ -704,16 +776,18 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         VC_EV_BEGIN();
         VC_TRY(launch_attn_decode(n, a, st, pdl));
         VC_EV_END();
-        // x += att Wo^T
+        // x += att Wo^T; fragments of x * g_ffn and sums of x^2 for the FFN norm
         p = GemvParams{};
         p.W = L.wo;
         p.N = kDecDim;
         p.K = p.Kp = kQDim;
-        p.x = w->att;
-        p.ldx = kQDim;
+        p.xfrag = w->xf_att;
         p.y = w->x;
         p.ldy = kDecDim;
         p.ss_out = w->ss_ffn;
+        p.xfrag_out = w->xf_ffn;
+        p.g_next = L.g_ffn;
+        p.err = w->err;
         VC_EV_BEGIN();
         VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
         VC_EV_END();
@@ -722,27 +796,26 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p.W = L.w13;
         p.N = 2 * kDecHidden;
         p.K = p.Kp = kDecDim;
-        p.x = w->x;
-        p.ldx = kDecDim;
-        p.norm_w = L.ffn_norm;
-        p.ada = L.ada;
+        p.xfrag = w->xf_ffn;
         p.ss_in = w->ss_ffn;
-        p.ss_parts = gemv_row_blocks(kDecDim);
-        p.y = w->h;
-        p.ldy = kDecHidden;
+        p.ss_parts = ss_parts;
+        p.xfrag_out = w->xf_h;
+        p.err = w->err;
         VC_EV_BEGIN();
         VC_TRY(launch_gemv(n, EPI_SWIGLU, p, st, pdl));
         VC_EV_END();
-        // x += h W2^T
+        // x += h W2^T; fragments for the next norm (next layer's, or the final)
         p = GemvParams{};
         p.W = L.w2;
         p.N = kDecDim;
         p.K = p.Kp = kDecHidden;
-        p.x = w->h;
-        p.ldx = kDecHidden;
+        p.xfrag = w->xf_h;
         p.y = w->x;
         p.ldy = kDecDim;
         p.ss_out = w->ss_attn;
+        p.xfrag_out = w->xf_attn;
+        p.g_next = (l + 1 < d->n_layers) ? d->L[l + 1].g_attn : d->norm;
+        p.err = w->err;
         VC_EV_BEGIN();
         VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
         VC_EV_END();
@@ -752,16 +825,15 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p.W = d->tok_emb;
         p.N = d->vocab;
         p.K = p.Kp = kDecDim;
-        p.x = w->x;
-        p.ldx = kDecDim;
-        p.norm_w = d->norm;
+        p.xfrag = w->xf_attn;
         p.ss_in = w->ss_attn;
-        p.ss_parts = gemv_row_blocks(kDecDim);
+        p.ss_parts = ss_parts;
         p.y = w->logits;
         p.ldy = d->vocab;
         p.partials = w->amax;
         p.counter = w->counters + n * kDecKvHeads;
         p.tokens = w->tokens;
+        p.err = w->err;
         VC_EV_BEGIN();
         VC_TRY(launch_gemv(n, EPI_LOGITS, p, st, pdl));
         VC_EV_END();
@@ -769,6 +841,16 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
 #undef VC_EV_BEGIN
 #undef VC_EV_END
     return VOX_CUDA_OK;
+}
+
+// The error word copied back after the tokens: a device-side bounded wait
+// expired during the step.
+int check_step_error(StepWork *w, cudaStream_t st) {
+    if (w->h_tokens[w->n] == 0) return VOX_CUDA_OK;
+    w->h_tokens[w->n] = 0;
+    cudaMemsetAsync(w->err, 0, sizeof(unsigned), st);
+    set_error("decoder step: a device-side wait timed out (results discarded)");
+    return VOX_CUDA_ERR_CUDA;
 }
 
 // Upload the staged step inputs, run the (captured) kernel sequence, fetch
@@ -792,9 +874,13 @@ int run_step(vox_cuda_decoder *d, DevCtx *c, StepWork *w, bool with_head, cudaSt
         VC_TRY(e);
     }
     VC_TRY(cudaGraphLaunch(g, st));
-    if (with_head)
-        VC_TRY(cudaMemcpyAsync(w->h_tokens, w->tokens, sizeof(int) * w->n, cudaMemcpyDeviceToHost, st));
-    if (sync) VC_TRY(cudaStreamSynchronize(st));
+    // tokens and the error word in one copy
+    VC_TRY(cudaMemcpyAsync(w->h_tokens, w->tokens, sizeof(int) * (w->n + 1), cudaMemcpyDeviceToHost, st));
+    if (sync) {
+        VC_TRY(cudaStreamSynchronize(st));
+        int rc = check_step_error(w, st);
+        if (rc) return rc;
+    }
     (void)c;
     return VOX_CUDA_OK;
 }
@@ -919,21 +1005,24 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
             ok &= o.qkv && o.wo && o.w13 && o.w2;
             if (!ok) break;
         }
-        float *norms = (float *)alloc(3 * D * 4);
-        if (!norms) {
+        // g_attn = attention_norm; g_ffn = ffn_norm * (1 + ada_scale[l])
+        // (voxtral_decoder.c:466, 488-492), folded into the activation fragments
+        std::vector<float> ha(D), hf(D), hada(D, 0.0f);
+        const cudaMemcpyKind to_host = w->weights_on_device ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost;
+        ok &= cudaMemcpy(ha.data(), L.attention_norm, D * 4, to_host) == cudaSuccess;
+        ok &= cudaMemcpy(hf.data(), L.ffn_norm, D * 4, to_host) == cudaSuccess;
+        if (w->ada_scale)
+            ok &= cudaMemcpy(hada.data(), w->ada_scale + (size_t)l * D, D * 4, to_host) == cudaSuccess;
+        for (size_t i = 0; i < D; i++) hf[i] = hf[i] * (1.0f + hada[i]);
+        float *g = (float *)alloc(2 * D * 4);
+        if (!g || !ok) {
             ok = false;
             break;
         }
-        ok &= cudaMemcpy(norms, L.attention_norm, D * 4, kind) == cudaSuccess;
-        ok &= cudaMemcpy(norms + D, L.ffn_norm, D * 4, kind) == cudaSuccess;
-        o.attn_norm = norms;
-        o.ffn_norm = norms + D;
-        if (w->ada_scale) {
-            ok &= cudaMemcpy(norms + 2 * D, w->ada_scale + (size_t)l * D, D * 4, kind) == cudaSuccess;
-            o.ada = norms + 2 * D;
-        } else {
-            o.ada = nullptr;
-        }
+        ok &= cudaMemcpy(g, ha.data(), D * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+        ok &= cudaMemcpy(g + D, hf.data(), D * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+        o.g_attn = g;
+        o.g_ffn = g + D;
     }
     if (ok) {
         const uint16_t *emb_parts[1] = {w->tok_embeddings};
@@ -1104,6 +1193,7 @@ extern "C" int vox_cuda_decoder_full_step(vox_cuda_dec_state *s, const float *em
     if (logits) {
         VC_TRY(cudaMemcpyAsync(logits, w->logits, (size_t)d->vocab * 4, cudaMemcpyDeviceToHost, c->stream));
         VC_TRY(cudaStreamSynchronize(c->stream));
+        if ((rc = check_step_error(w, c->stream))) return rc;
     }
     s->pos += 1;
     s->last_token = w->h_tokens[0];
@@ -1278,8 +1368,10 @@ extern "C" int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states
     }
     VC_TRY(cudaGraphLaunch(g, st));
     VC_TRY(cudaMemcpyAsync(tokens_dev, w->tokens, sizeof(int) * n, cudaMemcpyDeviceToDevice, st));
-    // the host staging block is reused by the next call: wait for the upload
+    VC_TRY(cudaMemcpyAsync(w->h_tokens, w->tokens, sizeof(int) * (n + 1), cudaMemcpyDeviceToHost, st));
+    // the host staging block is reused by the next call: wait for the step
     VC_TRY(cudaStreamSynchronize(st));
+    if ((rc = check_step_error(w, st))) return rc;
     for (int i = 0; i < n; i++) {
         states[i]->pos += 1;
         states[i]->have_logits = false;
@@ -1301,7 +1393,7 @@ extern "C" int vox_cuda_decoder_profile_batch(vox_cuda_dec_state *const *states,
     if (rc) return rc;
     StepWork *w = d->batch_work[n];
     cudaStream_t st = c->stream;
-    const int n_launch = 5 * d->n_layers + 1;
+    const int n_launch = 5 * d->n_layers + 2;   // prep, 5 per layer, LM head
     std::vector<cudaEvent_t> evs(2 * n_launch);
     for (auto &e : evs)
         if (cudaEventCreate(&e) != cudaSuccess) {
@@ -1328,7 +1420,9 @@ extern "C" int vox_cuda_decoder_profile_batch(vox_cuda_dec_state *const *states,
         for (int i = 0; i < n_launch; i++) {
             float t = 0.f;
             cudaEventElapsedTime(&t, evs[2 * i], evs[2 * i + 1]);
-            const int phase = (i == n_launch - 1) ? VOX_CUDA_PROF_LM_HEAD : (i % 5);
+            const int phase = (i == n_launch - 1) ? VOX_CUDA_PROF_LM_HEAD
+                              : (i == 0)           ? VOX_CUDA_PROF_QKV
+                                                   : ((i - 1) % 5);
             acc[phase] += t;
         }
     }
