@@ -34,7 +34,11 @@ sys.path.insert(0, PKG)
 METRIC = "decode tok/s/GPU + encoder audio-s/s at 4B; GEMV HBM GB/s vs B200 peak"
 UNIT = "tokens/s"
 D, QD, KVD, HID, VOCAB, LAYERS = 3072, 4096, 1024, 9216, 131072, 26
-WEIGHT_BYTES_PER_STEP = LAYERS * 2 * (6144 * D + D * QD + 2 * HID * D + D * HID) + VOCAB * D * 2
+
+
+def weight_bytes_per_step(layers=LAYERS, vocab=VOCAB):
+    """bf16 weight bytes one decode step streams (SURVEY: 6,857,687,040 B)."""
+    return layers * 2 * (6144 * D + D * QD + 2 * HID * D + D * HID) + vocab * D * 2
 
 # DRAM bytes per launch of the dominant kernel (the w1|w3 SwiGLU GEMV) from
 # the ncu capture summarised in profiles/ (None until captured).
@@ -204,7 +208,7 @@ def config(streams, pos, ws):
 # our arm
 # ---------------------------------------------------------------------------
 
-def build_device_decoder(V, torch, seed=0):
+def build_device_decoder(V, torch, seed=0, layers=LAYERS, vocab=VOCAB):
     """Random-init bf16 weights generated on the device, handed to the
     library, which lays them out (wq|wk|wv, w1/w3 interleaved)."""
     dev = torch.device("cuda")
@@ -219,17 +223,17 @@ def build_device_decoder(V, torch, seed=0):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     ones = torch.ones(D, dtype=torch.float32, device=dev)
-    ada = (0.1 * torch.randn((LAYERS, D), generator=g, device=dev)).contiguous()
-    layers = []
-    for l in range(LAYERS):
+    ada = (0.1 * torch.randn((layers, D), generator=g, device=dev)).contiguous()
+    n_layers, layers = layers, []
+    for l in range(n_layers):
         b = 1000 * seed + 10 * l
         layers.append((bf16((QD, D), b + 1), bf16((KVD, D), b + 2), bf16((KVD, D), b + 3),
                        bf16((D, QD), b + 4), bf16((HID, D), b + 5), bf16((D, HID), b + 6),
                        bf16((HID, D), b + 7), ones.data_ptr(), ones.data_ptr()))
-    emb = bf16((VOCAB, D), 1000 * seed + 999)
+    emb = bf16((vocab, D), 1000 * seed + 999)
     torch.cuda.synchronize()
     V.lib().vox_cuda_init()
-    dec = V.Decoder(emb, ones.data_ptr(), layers, ada_scale=ada.data_ptr(), on_device=True)
+    dec = V.Decoder(emb, ones.data_ptr(), layers, ada_scale=ada.data_ptr(), vocab=vocab, on_device=True)
     del keep
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -250,7 +254,7 @@ def our_arm(args):
     import voxcuda as V
     V.init(local)
     S = args.streams
-    dec = build_device_decoder(V, torch)
+    dec = build_device_decoder(V, torch, layers=args.layers, vocab=args.vocab)
     pos = positions(S)
     states = [dec.state(kv_cap=8192 + 1024) for _ in range(S)]
     for st, p in zip(states, pos):
@@ -316,10 +320,10 @@ def our_arm(args):
     prof = V.profile_batch(states, embeds.data_ptr(), iters=3)
     hbm, peak_kind = peaks()
     w13_bytes = 2 * HID * D * 2 + S * D * 4 + S * HID * 4        # per launch
-    w13_ms = prof["w13"] / LAYERS
+    w13_ms = prof["w13"] / args.layers
     achieved = w13_bytes / (w13_ms / 1000.0) / 1e9
-    kv_bytes = sum(LAYERS * min(p + 1, 8192) * KVD * 4 * 2 for p in pos)
-    step_bytes = WEIGHT_BYTES_PER_STEP + kv_bytes
+    kv_bytes = sum(args.layers * min(p + 1, 8192) * KVD * 4 * 2 for p in pos)
+    step_bytes = weight_bytes_per_step(args.layers, args.vocab) + kv_bytes
 
     line = None
     if rank == 0:
@@ -335,10 +339,12 @@ def our_arm(args):
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 weights)",
             "data": "synthetic (seeded random-init bf16 weights, random embeddings)",
-            "config": config(S, pos, ws),
+            "config": dict(config(S, pos, ws), **({} if (args.layers, args.vocab) == (LAYERS, VOCAB) else
+                                                   {"reduced_for_profiling": {"layers": args.layers,
+                                                                              "vocab": args.vocab}})),
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": S * (D * 4 + 128 * 4 + 32),
                     "d2h_bytes_per_step": S * 4},
-            "gpu_launches": args.steps * (5 * LAYERS + 1),
+            "gpu_launches": args.steps * (5 * args.layers + 2),
             "roofline": {"kernel": "gemv_kernel<M=8, EPI_SWIGLU> (w1|w3 + SwiGLU)", "bound": "hbm",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "peak_kind": peak_kind,
@@ -368,6 +374,9 @@ def main():
     ap.add_argument("--streams", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # reduced model, for small ncu captures only (the headline uses the full model)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--vocab", type=int, default=VOCAB)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

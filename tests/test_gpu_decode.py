@@ -154,8 +154,9 @@ def test_decoder_prefill_and_steps_match_reference(gpu_dec):
     assert st.position == G.PROMPT
     k25, _ = st.read_kv(25, 0, G.PROMPT)
     _, v0 = st.read_kv(0, 0, G.PROMPT)
-    assert sampled_rel(k25, g, "prefill_k25") < 1e-5
-    assert sampled_rel(v0, g, "prefill_v0") < 1e-5
+    # split-bf16 tensor-core GEMV: ~1e-5 per matmul (contract 1e-3)
+    assert sampled_rel(k25, g, "prefill_k25") < 1e-4
+    assert sampled_rel(v0, g, "prefill_v0") < 1e-4
     steps = G.dec_embeds(G.DEC_STEPS, 7002)
     for s in range(G.DEC_STEPS):
         tok, lg = st.step(steps[s], rope=g["step_rope"][s])
