@@ -13,28 +13,18 @@ __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
 }
 
 // ---------------------------------------------------------------------------
-// Split-K GQA decode attention over the KV ring.
+// Split-K GQA decode attention over the KV ring (vox_causal_attention with
+// seq_q = 1, voxtral_kernels.c:412-482, as called at voxtral_decoder.c:481-483).
 //
 // grid (S, 8 KV heads, M streams), 128 threads.  A CTA takes one KV head and
-// one contiguous range of keys; its 4 query heads share every K/V load.
-// Within a warp, 8 lanes cover one key (16 of the 128 dims each), so a warp
-// walks 4 keys at a time with a 3-step shuffle reduction per score.  Each
-// lane group keeps the reference's online-softmax state (running max, sum,
-// weighted V; voxtral_kernels.c:440-479); groups, warps and finally the S
-// splits are merged with the usual rescaling.  The last CTA of each
-// (stream, KV head) merges the splits (atomic ticket, no spinning).
+// up to 64 consecutive keys of the window; its 4 query heads share every K/V
+// load.  Instead of the reference's per-key online softmax (a serial chain),
+// the CTA runs three parallel passes: all scores (thread = key half-row, 16
+// float4 loads in flight each), the softmax of its keys (one warp per head),
+// then P.V with coalesced float4 loads of V (warp = key group, lane = 4
+// dims).  Splits are merged with the usual max rescaling by the last CTA of
+// each (stream, KV head) to finish (atomic ticket; no spinning).
 // ---------------------------------------------------------------------------
-
-struct SoftState {
-    float mx, den;
-};
-
-__device__ __forceinline__ void merge_scale(float ma, float da, float mb, float db, float &mn,
-                                            float &ca, float &cb) {
-    mn = fmaxf(ma, mb);
-    ca = (da > 0.f) ? expf(ma - mn) : 0.f;
-    cb = (db > 0.f) ? expf(mb - mn) : 0.f;
-}
 
 constexpr int kKeysPerSplit = 64;
 
@@ -42,9 +32,10 @@ __global__ void __launch_bounds__(128)
 attn_decode_kernel(const AttnParams p) {
     const int s = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int grp = lane >> 3, sl = lane & 7;
-    __shared__ float sm_o[4][4][kHeadDim];
-    __shared__ float sm_ml[4][4][2];
+    __shared__ __align__(16) float sq[4][kHeadDim];       // the 4 query heads of this KV head
+    __shared__ float ssc[4][kKeysPerSplit];               // scores, then exp(score - max)
+    __shared__ __align__(16) float so[4][4][kHeadDim];    // P.V per key group [group][head][dim]
+    __shared__ float sml[4][2];                            // per head: (max, sum of exp)
     __shared__ int s_last;
 
     grid_dep_wait();
@@ -52,163 +43,129 @@ attn_decode_kernel(const AttnParams p) {
 
     const StreamSlot slt = p.slots[m];
     const int n_keys = slt.n_keys;
-    // splits actually used for this stream: ~kKeysPerSplit keys per CTA
     const int S = max(1, min(p.S, (n_keys + kKeysPerSplit - 1) / kKeysPerSplit));
-    if (s >= S) return;   // CTA-uniform; no barrier has been reached yet
-    const int chunk = (n_keys + S - 1) / S;
+    if (s >= S) return;   // CTA-uniform, before any barrier
+    const int chunk = (n_keys + S - 1) / S;               // <= kKeysPerSplit
     const int kb = s * chunk;
-    const int ke = min(kb + chunk, n_keys);
-    const int first = slt.pos - n_keys + 1;   // logical position of key 0
+    const int nk = max(0, min(kb + chunk, n_keys) - kb);
+    const int first = slt.pos - n_keys + 1;              // logical position of key 0
     const int cap = slt.cap;
     const float scale = 1.0f / sqrtf((float)kHeadDim);
-
-    float q[4][16];
-    const float *qb = p.q + (size_t)m * kQDim + (kvh * 4) * kHeadDim + sl * 16;
-#pragma unroll
-    for (int hh = 0; hh < 4; hh++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float4 v = *reinterpret_cast<const float4 *>(qb + hh * kHeadDim + 4 * i);
-            q[hh][4 * i] = v.x;
-            q[hh][4 * i + 1] = v.y;
-            q[hh][4 * i + 2] = v.z;
-            q[hh][4 * i + 3] = v.w;
-        }
-
-    float mx[4], den[4], o[4][16];
-#pragma unroll
-    for (int hh = 0; hh < 4; hh++) {
-        mx[hh] = -INFINITY;
-        den[hh] = 0.f;
-#pragma unroll
-        for (int d = 0; d < 16; d++) o[hh][d] = 0.f;
-    }
-
-    const size_t layer_off = (size_t)p.layer * cap * kKvDim + kvh * kHeadDim + sl * 16;
+    const size_t layer_off = (size_t)p.layer * cap * kKvDim + kvh * kHeadDim;
     const float *kbase = slt.k_ring + layer_off;
     const float *vbase = slt.v_ring + layer_off;
 
-    // K/V of key i (zeros past the range), loaded one iteration ahead
-    auto load_key = [&](int i, float4 (&kv)[4], float4 (&vv)[4]) {
-        if (i < ke) {
-            const int slot = (first + i) % cap;
-            const float4 *kr = reinterpret_cast<const float4 *>(kbase + (size_t)slot * kKvDim);
-            const float4 *vr = reinterpret_cast<const float4 *>(vbase + (size_t)slot * kKvDim);
-#pragma unroll
-            for (int j = 0; j < 4; j++) kv[j] = __ldcg(kr + j);
-#pragma unroll
-            for (int j = 0; j < 4; j++) vv[j] = __ldcg(vr + j);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 4; j++) kv[j] = vv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    };
+    {   // queries
+        const float4 v = *reinterpret_cast<const float4 *>(p.q + (size_t)m * kQDim +
+                                                           (kvh * 4 + warp) * kHeadDim + 4 * lane);
+        *reinterpret_cast<float4 *>(&sq[warp][4 * lane]) = v;
+    }
+    __syncthreads();
 
-    // The loop bound is warp-uniform (the shuffles below use the full mask);
-    // a lane group past the end of the range computes on zeros and skips
-    // the update.
-    float4 kv[4], vv[4];
-    load_key(kb + warp * 4 + grp, kv, vv);
-    for (int base = kb + warp * 4; base < ke; base += 16) {
-        const int i = base + grp;
-        const bool valid = i < ke;
-        float4 kn[4], vn[4];
-        load_key(i + 16, kn, vn);
-        float sc[4];
+    // ---- scores: thread -> key j = tid / 2, dims 64 * (tid & 1) .. +63 ----
+    {
+        const int j = tid >> 1, hf = tid & 1;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        if (j < nk) {
+            const int slot = (first + kb + j) % cap;
+            const float4 *kr = reinterpret_cast<const float4 *>(kbase + (size_t)slot * kKvDim + 64 * hf);
+            float4 kv[16];
 #pragma unroll
-        for (int hh = 0; hh < 4; hh++) {
-            float a = 0.f;
+            for (int i = 0; i < 16; i++) kv[i] = __ldcg(kr + i);
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                a = fmaf(q[hh][4 * j], kv[j].x, a);
-                a = fmaf(q[hh][4 * j + 1], kv[j].y, a);
-                a = fmaf(q[hh][4 * j + 2], kv[j].z, a);
-                a = fmaf(q[hh][4 * j + 3], kv[j].w, a);
-            }
-            a += __shfl_xor_sync(0xffffffffu, a, 1);
-            a += __shfl_xor_sync(0xffffffffu, a, 2);
-            a += __shfl_xor_sync(0xffffffffu, a, 4);
-            sc[hh] = a * scale;
-        }
-        if (valid) {
-            const float vf[16] = {vv[0].x, vv[0].y, vv[0].z, vv[0].w, vv[1].x, vv[1].y, vv[1].z, vv[1].w,
-                                  vv[2].x, vv[2].y, vv[2].z, vv[2].w, vv[3].x, vv[3].y, vv[3].z, vv[3].w};
+            for (int h = 0; h < 4; h++) {
+                const float4 *qh = reinterpret_cast<const float4 *>(&sq[h][64 * hf]);
+                float a = 0.f;
 #pragma unroll
-            for (int hh = 0; hh < 4; hh++) {
-                if (sc[hh] > mx[hh]) {
-                    const float c = expf(mx[hh] - sc[hh]);
-                    den[hh] = den[hh] * c + 1.0f;
-#pragma unroll
-                    for (int d = 0; d < 16; d++) o[hh][d] = o[hh][d] * c + vf[d];
-                    mx[hh] = sc[hh];
-                } else {
-                    const float wgt = expf(sc[hh] - mx[hh]);
-                    den[hh] += wgt;
-#pragma unroll
-                    for (int d = 0; d < 16; d++) o[hh][d] = fmaf(wgt, vf[d], o[hh][d]);
+                for (int i = 0; i < 16; i++) {
+                    const float4 q4 = qh[i];
+                    a = fmaf(q4.x, kv[i].x, a);
+                    a = fmaf(q4.y, kv[i].y, a);
+                    a = fmaf(q4.z, kv[i].z, a);
+                    a = fmaf(q4.w, kv[i].w, a);
                 }
+                d[h] = a;
             }
         }
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            kv[j] = kn[j];
-            vv[j] = vn[j];
-        }
-    }
-
-    // merge the 4 lane groups of the warp
-#pragma unroll
-    for (int off = 8; off <= 16; off <<= 1) {
-#pragma unroll
-        for (int hh = 0; hh < 4; hh++) {
-            const float mo = __shfl_xor_sync(0xffffffffu, mx[hh], off);
-            const float dn = __shfl_xor_sync(0xffffffffu, den[hh], off);
-            float mn, ca, cb;
-            merge_scale(mx[hh], den[hh], mo, dn, mn, ca, cb);
-            den[hh] = den[hh] * ca + dn * cb;
-#pragma unroll
-            for (int d = 0; d < 16; d++) {
-                const float oo = __shfl_xor_sync(0xffffffffu, o[hh][d], off);
-                o[hh][d] = o[hh][d] * ca + oo * cb;
-            }
-            mx[hh] = mn;
-        }
-    }
-    if (grp == 0) {
-#pragma unroll
-        for (int hh = 0; hh < 4; hh++) {
-#pragma unroll
-            for (int d = 0; d < 16; d++) sm_o[warp][hh][sl * 16 + d] = o[hh][d];
-            if (sl == 0) {
-                sm_ml[warp][hh][0] = mx[hh];
-                sm_ml[warp][hh][1] = den[hh];
-            }
+        for (int h = 0; h < 4; h++) {
+            const float t = d[h] + __shfl_xor_sync(0xffffffffu, d[h], 1);
+            if (hf == 0 && j < nk) ssc[h][j] = t * scale;
         }
     }
     __syncthreads();
 
-    // merge the 4 warps; thread -> (head hh, dims 4*(tid&31)..+3)
+    // ---- softmax of this split's keys: warp = head ----
     {
-        const int hh = tid >> 5, d4 = (tid & 31) * 4;
-        float gm = -INFINITY;
-        for (int w = 0; w < 4; w++)
-            if (sm_ml[w][hh][1] > 0.f) gm = fmaxf(gm, sm_ml[w][hh][0]);
-        float gd = 0.f, go[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int w = 0; w < 4; w++) {
-            const float dw = sm_ml[w][hh][1];
-            if (dw > 0.f) {
-                const float c = expf(sm_ml[w][hh][0] - gm);
-                gd += dw * c;
+        const int h = warp;
+        const float a = (lane < nk) ? ssc[h][lane] : -INFINITY;
+        const float b = (lane + 32 < nk) ? ssc[h][lane + 32] : -INFINITY;
+        float mx = fmaxf(a, b);
 #pragma unroll
-                for (int j = 0; j < 4; j++) go[j] += sm_o[w][hh][d4 + j] * c;
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float pa = (lane < nk) ? expf(a - mx) : 0.f;
+        const float pb = (lane + 32 < nk) ? expf(b - mx) : 0.f;
+        if (lane < nk) ssc[h][lane] = pa;
+        if (lane + 32 < nk) ssc[h][lane + 32] = pb;
+        const float sum = warp_sum(pa + pb);
+        if (lane == 0) {
+            sml[h][0] = mx;
+            sml[h][1] = sum;
+        }
+    }
+    __syncthreads();
+
+    // ---- P.V: warp = key group (keys warp, warp+4, ...), lane = dims 4*lane..+3 ----
+    {
+        float acc[4][4];
+#pragma unroll
+        for (int h = 0; h < 4; h++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) acc[h][c] = 0.f;
+        float4 vv[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const int j = warp + 4 * i;
+            if (j < nk) {
+                const int slot = (first + kb + j) % cap;
+                vv[i] = __ldcg(reinterpret_cast<const float4 *>(vbase + (size_t)slot * kKvDim) + lane);
+            } else {
+                vv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const int j = warp + 4 * i;
+            if (j < nk) {
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                    const float pw = ssc[h][j];
+                    acc[h][0] = fmaf(pw, vv[i].x, acc[h][0]);
+                    acc[h][1] = fmaf(pw, vv[i].y, acc[h][1]);
+                    acc[h][2] = fmaf(pw, vv[i].z, acc[h][2]);
+                    acc[h][3] = fmaf(pw, vv[i].w, acc[h][3]);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 4; h++)
+            *reinterpret_cast<float4 *>(&so[warp][h][4 * lane]) =
+                make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    }
+    __syncthreads();
+
+    // ---- this split's partial: thread -> head hh = warp, dims 4*lane..+3 ----
+    {
+        const int hh = warp, d4 = 4 * lane;
+        float go[4];
+#pragma unroll
+        for (int c = 0; c < 4; c++) go[c] = so[0][hh][d4 + c] + so[1][hh][d4 + c] + so[2][hh][d4 + c] + so[3][hh][d4 + c];
         const int h = kvh * 4 + hh;
         const size_t pidx = ((size_t)m * kDecHeads + h) * p.S + s;
         *reinterpret_cast<float4 *>(p.part_o + pidx * kHeadDim + d4) = make_float4(go[0], go[1], go[2], go[3]);
-        if ((tid & 31) == 0) {
-            p.part_ml[pidx * 2] = gm;
-            p.part_ml[pidx * 2 + 1] = gd;
+        if (lane == 0) {
+            p.part_ml[pidx * 2] = sml[hh][0];
+            p.part_ml[pidx * 2 + 1] = sml[hh][1];
         }
     }
     __threadfence();
@@ -218,8 +175,9 @@ attn_decode_kernel(const AttnParams p) {
     if (!s_last) return;
     __threadfence();
 
+    // ---- merge the S splits (last CTA of this stream / KV head) ----
     {
-        const int hh = tid >> 5, d4 = (tid & 31) * 4;
+        const int hh = warp, d4 = 4 * lane;
         const int h = kvh * 4 + hh;
         const size_t pbase = ((size_t)m * kDecHeads + h) * p.S;
         float gm = -INFINITY;

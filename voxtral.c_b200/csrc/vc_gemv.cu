@@ -40,6 +40,7 @@ constexpr int kStages = 5;
 constexpr int kStageW = kStageKB * kRT * 512;   // 16 KB of weights
 constexpr int kStageB = kStageKB * 512;         // 4 KB of activation fragments
 constexpr int kMaxKS = 8;                // cluster size limit (portable)
+static_assert(kMaxKS * kRowsPerCta * 8 * 4 <= kStageW + kStageB, "cluster reduction area fits a stage");
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -111,12 +112,11 @@ __device__ __forceinline__ void cluster_sync_all() {
                  "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ float ld_dsmem_f32(const float *local, uint32_t rank) {
+// store v at the same shared-memory offset as `local`, in cluster CTA `rank`
+__device__ __forceinline__ void st_dsmem_f32(float *local, uint32_t rank, float v) {
     uint32_t a = smem_u32(local), r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
-    return v;
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(r), "f"(v) : "memory");
 }
 
 __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
@@ -235,6 +235,8 @@ gemv_tma_kernel(const GemvParams p) {
         }
     }
     __syncthreads();   // all stages consumed: the ring is reused below
+    // tell the cluster this CTA's ring is free (its peers will write into it)
+    if (KS > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
     // ---- reduce the 8 warps (fixed order) ----
     float *red = reinterpret_cast<float *>(sh.stage[0]);   // [8 warps][4 tiles][32 lanes][4]
@@ -252,18 +254,23 @@ gemv_tma_kernel(const GemvParams p) {
     }
     __syncthreads();
 
-    // ---- reduce the KS slices of the cluster into rank 0 ----
+    // ---- reduce the KS slices of the cluster into rank 0: each peer stores
+    // its partial into rank 0's (drained) ring; rank 0 sums in rank order ----
     if (KS > 1) {
-        cluster_sync_all();
-        if (cluster_ctarank() == 0) {
-            for (int e = tid; e < kRowsPerCta * 8; e += kThreads) {
-                float v = (&sh.part[0][0])[e];
-                for (int r = 1; r < KS; r++) v += ld_dsmem_f32(&sh.part[0][0] + e, (uint32_t)r);
-                (&sh.part[0][0])[e] = v;
-            }
+        asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // all rings drained
+        const uint32_t rank = cluster_ctarank();
+        float *area = reinterpret_cast<float *>(sh.stage[1]);         // [KS][64*8]
+        if (rank != 0)
+            for (int e = tid; e < kRowsPerCta * 8; e += kThreads)
+                st_dsmem_f32(area + rank * (kRowsPerCta * 8) + e, 0u, (&sh.part[0][0])[e]);
+        cluster_sync_all();   // the peers' stores are visible in rank 0
+        if (rank != 0) return;
+        for (int e = tid; e < kRowsPerCta * 8; e += kThreads) {
+            float v = (&sh.part[0][0])[e];
+            for (int r = 1; r < KS; r++) v += area[r * (kRowsPerCta * 8) + e];
+            (&sh.part[0][0])[e] = v;
         }
-        cluster_sync_all();   // peers keep their shared memory until rank 0 has read it
-        if (cluster_ctarank() != 0) return;
+        __syncthreads();
     }
     if (tid < 8) {
         float inv = 1.0f;

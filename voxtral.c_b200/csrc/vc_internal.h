@@ -81,7 +81,7 @@ struct AttnParams {
     unsigned *counters;       // [M][8], zero between launches
     int S;                    // key splits per KV head
 };
-constexpr int kAttnSplits = 32;
+constexpr int kAttnSplits = 128;   // >= 8192 / 64 keys per split
 
 cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl);
 
