@@ -30,12 +30,13 @@ constexpr int kKeysPerSplit = 64;
 
 __global__ void __launch_bounds__(128)
 attn_decode_kernel(const AttnParams p) {
-    const int s = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
+    const int kvh = blockIdx.y, m = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ __align__(16) float sq[4][kHeadDim];       // the 4 query heads of this KV head
     __shared__ float ssc[4][kKeysPerSplit];               // scores, then exp(score - max)
     __shared__ __align__(16) float so[4][4][kHeadDim];    // P.V per key group [group][head][dim]
     __shared__ float sml[4][2];                            // per head: (max, sum of exp)
+    __shared__ float smw[4][kAttnSplits];                  // merge weights per split
     __shared__ int s_last;
 
     grid_dep_wait();
@@ -44,10 +45,8 @@ attn_decode_kernel(const AttnParams p) {
     const StreamSlot slt = p.slots[m];
     const int n_keys = slt.n_keys;
     const int S = max(1, min(p.S, (n_keys + kKeysPerSplit - 1) / kKeysPerSplit));
-    if (s >= S) return;   // CTA-uniform, before any barrier
+    if ((int)blockIdx.x >= S) return;   // CTA-uniform, before any barrier
     const int chunk = (n_keys + S - 1) / S;               // <= kKeysPerSplit
-    const int kb = s * chunk;
-    const int nk = max(0, min(kb + chunk, n_keys) - kb);
     const int first = slt.pos - n_keys + 1;              // logical position of key 0
     const int cap = slt.cap;
     const float scale = 1.0f / sqrtf((float)kHeadDim);
@@ -60,69 +59,21 @@ attn_decode_kernel(const AttnParams p) {
                                                            (kvh * 4 + warp) * kHeadDim + 4 * lane);
         *reinterpret_cast<float4 *>(&sq[warp][4 * lane]) = v;
     }
-    __syncthreads();
 
-    // ---- scores: thread -> key j = tid / 2, dims 64 * (tid & 1) .. +63 ----
-    {
-        const int j = tid >> 1, hf = tid & 1;
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        if (j < nk) {
-            const int slot = (first + kb + j) % cap;
+    int n_done = 0;
+    for (int s = blockIdx.x; s < S; s += gridDim.x) {
+        const int kb = s * chunk;
+        const int nk = max(0, min(kb + chunk, n_keys) - kb);
+        // K (thread = key half-row) and V (warp = key group, lane = 4 dims) of
+        // this split, all loads issued before any use
+        const int jk = tid >> 1, hf = tid & 1;
+        float4 kv[16], vv[16];
+        if (jk < nk) {
+            const int slot = (first + kb + jk) % cap;
             const float4 *kr = reinterpret_cast<const float4 *>(kbase + (size_t)slot * kKvDim + 64 * hf);
-            float4 kv[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) kv[i] = __ldcg(kr + i);
-#pragma unroll
-            for (int h = 0; h < 4; h++) {
-                const float4 *qh = reinterpret_cast<const float4 *>(&sq[h][64 * hf]);
-                float a = 0.f;
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const float4 q4 = qh[i];
-                    a = fmaf(q4.x, kv[i].x, a);
-                    a = fmaf(q4.y, kv[i].y, a);
-                    a = fmaf(q4.z, kv[i].z, a);
-                    a = fmaf(q4.w, kv[i].w, a);
-                }
-                d[h] = a;
-            }
         }
-#pragma unroll
-        for (int h = 0; h < 4; h++) {
-            const float t = d[h] + __shfl_xor_sync(0xffffffffu, d[h], 1);
-            if (hf == 0 && j < nk) ssc[h][j] = t * scale;
-        }
-    }
-    __syncthreads();
-
-    // ---- softmax of this split's keys: warp = head ----
-    {
-        const int h = warp;
-        const float a = (lane < nk) ? ssc[h][lane] : -INFINITY;
-        const float b = (lane + 32 < nk) ? ssc[h][lane + 32] : -INFINITY;
-        float mx = fmaxf(a, b);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        const float pa = (lane < nk) ? expf(a - mx) : 0.f;
-        const float pb = (lane + 32 < nk) ? expf(b - mx) : 0.f;
-        if (lane < nk) ssc[h][lane] = pa;
-        if (lane + 32 < nk) ssc[h][lane + 32] = pb;
-        const float sum = warp_sum(pa + pb);
-        if (lane == 0) {
-            sml[h][0] = mx;
-            sml[h][1] = sum;
-        }
-    }
-    __syncthreads();
-
-    // ---- P.V: warp = key group (keys warp, warp+4, ...), lane = dims 4*lane..+3 ----
-    {
-        float acc[4][4];
-#pragma unroll
-        for (int h = 0; h < 4; h++)
-#pragma unroll
-            for (int c = 0; c < 4; c++) acc[h][c] = 0.f;
-        float4 vv[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) {
             const int j = warp + 4 * i;
@@ -133,70 +84,158 @@ attn_decode_kernel(const AttnParams p) {
                 vv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const int j = warp + 4 * i;
-            if (j < nk) {
+        __syncthreads();   // sq ready (first split); previous split's ssc / so consumed
+
+        // ---- scores ----
+        {
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+            if (jk < nk) {
 #pragma unroll
                 for (int h = 0; h < 4; h++) {
-                    const float pw = ssc[h][j];
-                    acc[h][0] = fmaf(pw, vv[i].x, acc[h][0]);
-                    acc[h][1] = fmaf(pw, vv[i].y, acc[h][1]);
-                    acc[h][2] = fmaf(pw, vv[i].z, acc[h][2]);
-                    acc[h][3] = fmaf(pw, vv[i].w, acc[h][3]);
+                    const float4 *qh = reinterpret_cast<const float4 *>(&sq[h][64 * hf]);
+                    float a = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const float4 q4 = qh[i];
+                        a = fmaf(q4.x, kv[i].x, a);
+                        a = fmaf(q4.y, kv[i].y, a);
+                        a = fmaf(q4.z, kv[i].z, a);
+                        a = fmaf(q4.w, kv[i].w, a);
+                    }
+                    d[h] = a;
                 }
             }
-        }
 #pragma unroll
-        for (int h = 0; h < 4; h++)
-            *reinterpret_cast<float4 *>(&so[warp][h][4 * lane]) =
-                make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-    }
-    __syncthreads();
+            for (int h = 0; h < 4; h++) {
+                const float t = d[h] + __shfl_xor_sync(0xffffffffu, d[h], 1);
+                if (hf == 0 && jk < nk) ssc[h][jk] = t * scale;
+            }
+        }
+        __syncthreads();
 
-    // ---- this split's partial: thread -> head hh = warp, dims 4*lane..+3 ----
-    {
-        const int hh = warp, d4 = 4 * lane;
-        float go[4];
+        // ---- softmax of this split's keys: warp = head ----
+        {
+            const int h = warp;
+            const float a = (lane < nk) ? ssc[h][lane] : -INFINITY;
+            const float b = (lane + 32 < nk) ? ssc[h][lane + 32] : -INFINITY;
+            float mx = fmaxf(a, b);
 #pragma unroll
-        for (int c = 0; c < 4; c++) go[c] = so[0][hh][d4 + c] + so[1][hh][d4 + c] + so[2][hh][d4 + c] + so[3][hh][d4 + c];
-        const int h = kvh * 4 + hh;
-        const size_t pidx = ((size_t)m * kDecHeads + h) * p.S + s;
-        *reinterpret_cast<float4 *>(p.part_o + pidx * kHeadDim + d4) = make_float4(go[0], go[1], go[2], go[3]);
-        if (lane == 0) {
-            p.part_ml[pidx * 2] = sml[hh][0];
-            p.part_ml[pidx * 2 + 1] = sml[hh][1];
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float pa = (lane < nk) ? expf(a - mx) : 0.f;
+            const float pb = (lane + 32 < nk) ? expf(b - mx) : 0.f;
+            if (lane < nk) ssc[h][lane] = pa;
+            if (lane + 32 < nk) ssc[h][lane + 32] = pb;
+            const float sum = warp_sum(pa + pb);
+            if (lane == 0) {
+                sml[h][0] = mx;
+                sml[h][1] = sum;
+            }
         }
+        __syncthreads();
+
+        // ---- P.V ----
+        {
+            float acc[4][4];
+#pragma unroll
+            for (int h = 0; h < 4; h++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) acc[h][c] = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const int j = warp + 4 * i;
+                if (j < nk) {
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const float pw = ssc[h][j];
+                        acc[h][0] = fmaf(pw, vv[i].x, acc[h][0]);
+                        acc[h][1] = fmaf(pw, vv[i].y, acc[h][1]);
+                        acc[h][2] = fmaf(pw, vv[i].z, acc[h][2]);
+                        acc[h][3] = fmaf(pw, vv[i].w, acc[h][3]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < 4; h++)
+                *reinterpret_cast<float4 *>(&so[warp][h][4 * lane]) =
+                    make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        }
+        __syncthreads();
+
+        // ---- this split's partial: warp = head, lane = 4 dims ----
+        {
+            const int hh = warp, d4 = 4 * lane;
+            float go[4];
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                go[c] = so[0][hh][d4 + c] + so[1][hh][d4 + c] + so[2][hh][d4 + c] + so[3][hh][d4 + c];
+            const size_t pidx = ((size_t)m * kDecHeads + kvh * 4 + hh) * p.S + s;
+            *reinterpret_cast<float4 *>(p.part_o + pidx * kHeadDim + d4) = make_float4(go[0], go[1], go[2], go[3]);
+            if (lane == 0) {
+                p.part_ml[pidx * 2] = sml[hh][0];
+                p.part_ml[pidx * 2 + 1] = sml[hh][1];
+            }
+        }
+        n_done++;
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&p.counters[m * kDecKvHeads + kvh], 1u) == (unsigned)(S - 1));
+    if (tid == 0)
+        s_last = (atomicAdd(&p.counters[m * kDecKvHeads + kvh], (unsigned)n_done) + n_done == (unsigned)S);
     __syncthreads();
     if (!s_last) return;
     __threadfence();
 
-    // ---- merge the S splits (last CTA of this stream / KV head) ----
+    // ---- merge the S splits (last CTA of this stream / KV head): warp = head ----
     {
         const int hh = warp, d4 = 4 * lane;
         const int h = kvh * 4 + hh;
         const size_t pbase = ((size_t)m * kDecHeads + h) * p.S;
+        float mloc[kAttnSplits / 32], dloc[kAttnSplits / 32];
         float gm = -INFINITY;
-        for (int t = 0; t < S; t++) {
-            const float dn = __ldcg(p.part_ml + (pbase + t) * 2 + 1);
-            if (dn > 0.f) gm = fmaxf(gm, __ldcg(p.part_ml + (pbase + t) * 2));
+#pragma unroll
+        for (int i = 0; i < kAttnSplits / 32; i++) {
+            const int t = lane + 32 * i;
+            mloc[i] = (t < S) ? __ldcg(p.part_ml + (pbase + t) * 2) : -INFINITY;
+            dloc[i] = (t < S) ? __ldcg(p.part_ml + (pbase + t) * 2 + 1) : 0.f;
         }
-        float gd = 0.f, go[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int t = 0; t < S; t++) {
-            const float dn = __ldcg(p.part_ml + (pbase + t) * 2 + 1);
-            if (dn > 0.f) {
-                const float c = expf(__ldcg(p.part_ml + (pbase + t) * 2) - gm);
-                gd += dn * c;
-                const float4 ov = __ldcg(reinterpret_cast<const float4 *>(p.part_o + (pbase + t) * kHeadDim + d4));
-                go[0] += ov.x * c;
-                go[1] += ov.y * c;
-                go[2] += ov.z * c;
-                go[3] += ov.w * c;
+#pragma unroll
+        for (int i = 0; i < kAttnSplits / 32; i++)
+            if (dloc[i] > 0.f) gm = fmaxf(gm, mloc[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+        float gd = 0.f;
+#pragma unroll
+        for (int i = 0; i < kAttnSplits / 32; i++) {
+            const int t = lane + 32 * i;
+            const float c = (dloc[i] > 0.f) ? expf(mloc[i] - gm) : 0.f;
+            gd += dloc[i] * c;
+            if (t < kAttnSplits) smw[hh][t] = c;
+        }
+        gd = warp_sum(gd);
+        __syncwarp();
+        float go[4] = {0.f, 0.f, 0.f, 0.f};
+        int t = 0;
+        for (; t + 4 <= S; t += 4) {   // 4 independent loads in flight
+            float4 ov[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                ov[u] = __ldcg(reinterpret_cast<const float4 *>(p.part_o + (pbase + t + u) * kHeadDim + d4));
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float c = smw[hh][t + u];
+                go[0] += ov[u].x * c;
+                go[1] += ov[u].y * c;
+                go[2] += ov[u].z * c;
+                go[3] += ov[u].w * c;
             }
+        }
+        for (; t < S; t++) {
+            const float4 ov = __ldcg(reinterpret_cast<const float4 *>(p.part_o + (pbase + t) * kHeadDim + d4));
+            const float c = smw[hh][t];
+            go[0] += ov.x * c;
+            go[1] += ov.y * c;
+            go[2] += ov.z * c;
+            go[3] += ov.w * c;
         }
         const float inv = (gd > 0.f) ? 1.0f / gd : 0.f;
         const float o0 = go[0] * inv, o1 = go[1] * inv, o2 = go[2] * inv, o3 = go[3] * inv;
@@ -211,9 +250,15 @@ attn_decode_kernel(const AttnParams p) {
     }
 }
 
+// CTAs per (stream, KV head): each loops over splits blockIdx.x + G*i.
+int attn_ctas_per_head(int M) {
+    const int g = kAttnSplits / (M > 0 ? M : 1);
+    return g < 16 ? 16 : g;
+}
+
 cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.S, kDecKvHeads, M);
+    cfg.gridDim = dim3(attn_ctas_per_head(M), kDecKvHeads, M);
     cfg.blockDim = dim3(128);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];

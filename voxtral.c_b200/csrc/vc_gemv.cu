@@ -477,11 +477,21 @@ cudaError_t launch_prep_xfrag(const float *x, int M, int K, int ldx, const float
 
 int gemv_row_blocks(int N) { return (N + kRowsPerCta - 1) / kRowsPerCta; }
 
+// K-slices per row block: as many as keep the whole launch in one wave of
+// resident CTAs (2 per SM), so no SM waits on a ragged second wave; at most 6
+// so that the slice clusters pack into the GPCs.
 int gemv_k_slices(int N, int Kp) {
+    static int slots = 0;
+    if (slots == 0) {
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess)
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        slots = 2 * sms;
+    }
     const int KB = Kp / 16;
     const int rb = gemv_row_blocks(N);
-    int ks = (2 * 148 + rb - 1) / rb;           // ~2 CTAs per SM
-    if (ks > kMaxKS) ks = kMaxKS;
+    int ks = slots / rb;
+    if (ks > 6) ks = 6;
     const int max_by_k = (KB + kStageKB - 1) / kStageKB;   // >= one stage per slice
     if (ks > max_by_k) ks = max_by_k;
     if (ks < 1) ks = 1;
