@@ -5,6 +5,7 @@
 #include "vc_internal.h"
 
 #include <math.h>
+#include <stdlib.h>
 
 namespace vc {
 
@@ -252,6 +253,12 @@ attn_decode_kernel(const AttnParams p) {
 
 // CTAs per (stream, KV head): each loops over splits blockIdx.x + G*i.
 int attn_ctas_per_head(int M) {
+    static int fixed = -1;
+    if (fixed < 0) {   // tuning knob: VOX_CUDA_ATTN_CTAS fixes the CTAs per (stream, KV head)
+        const char *e = getenv("VOX_CUDA_ATTN_CTAS");
+        fixed = (e && atoi(e) >= 1 && atoi(e) <= kAttnSplits) ? atoi(e) : 0;
+    }
+    if (fixed > 0) return fixed;
     const int g = kAttnSplits / (M > 0 ? M : 1);
     return g < 16 ? 16 : g;
 }

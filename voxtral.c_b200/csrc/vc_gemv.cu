@@ -28,6 +28,7 @@
 #include "vc_internal.h"
 
 #include <math.h>
+#include <stdlib.h>
 
 namespace vc {
 
@@ -477,21 +478,25 @@ cudaError_t launch_prep_xfrag(const float *x, int M, int K, int ldx, const float
 
 int gemv_row_blocks(int N) { return (N + kRowsPerCta - 1) / kRowsPerCta; }
 
-// K-slices per row block: as many as keep the whole launch in one wave of
-// resident CTAs (2 per SM), so no SM waits on a ragged second wave; at most 6
-// so that the slice clusters pack into the GPCs.
+// K-slices per row block.  Measured on B200 (launch lists of the decode
+// step): ~1.3 CTAs per SM (192 CTAs) is the sweet spot - enough weight bytes
+// in flight, a single wave, small slice clusters; more slices add cluster
+// and epilogue cost, fewer leave SMs idle.
 int gemv_k_slices(int N, int Kp) {
-    static int slots = 0;
-    if (slots == 0) {
+    static int target = 0, max_ks = -1;
+    if (target == 0) {
         int dev = 0, sms = 148;
         if (cudaGetDevice(&dev) == cudaSuccess)
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        slots = 2 * sms;
+        target = (sms * 4) / 3;
+        // tuning knob: VOX_CUDA_GEMV_MAXKS caps the K-split (default 6)
+        const char *e = getenv("VOX_CUDA_GEMV_MAXKS");
+        max_ks = (e && atoi(e) >= 1 && atoi(e) <= kMaxKS) ? atoi(e) : 6;
     }
     const int KB = Kp / 16;
     const int rb = gemv_row_blocks(N);
-    int ks = slots / rb;
-    if (ks > 6) ks = 6;
+    int ks = (target + rb / 2) / rb;
+    if (ks > max_ks) ks = max_ks;
     const int max_by_k = (KB + kStageKB - 1) / kStageKB;   // >= one stage per slice
     if (ks > max_by_k) ks = max_by_k;
     if (ks < 1) ks = 1;
