@@ -221,6 +221,26 @@ int vox_cuda_decoder_profile_batch(vox_cuda_dec_state *const *states, int n,
 int vox_cuda_attention_decode_dev(const float *q, const float *k_ring, const float *v_ring,
                                   int kv_cap, int pos, float *out, void *stream);
 
+/* The same decode attention for callers that cannot allocate device memory
+ * (hosts that forbid cudaMalloc after start-up, e.g. a real-time audio
+ * pipeline that must not stall in the allocator, or code handed a fixed
+ * device arena).  No counterpart in the reference: the reference has no GPU
+ * path with allocation constraints.  Arguments and result are those of
+ * vox_cuda_attention_decode_dev, except that `stream` may be NULL (the legacy
+ * default stream) and vox_cuda_init is not required; the CUDA device that is
+ * current on the calling thread is used.  The split scratch is a fixed
+ * ~2.1 MB array in device memory that every GPU loading the library holds
+ * until the process exits; it bounds the attended keys to 8192 (128 splits
+ * of 64 keys), the decoder's full window, and larger requests are rejected
+ * with VOX_CUDA_ERR_CAPACITY.  The first call on a device looks up the
+ * array's device address and should come before any stream capture.  All
+ * calls on a device share the array, which keeps the last call's contents:
+ * calls that overlap on the GPU (other threads or streams) race, so callers
+ * serialise them.  Returns 0 or a VOX_CUDA_ERR_* code; the call returns after
+ * the result is in `out`. */
+int vox_cuda_attention_decode_noalloc(const float *q, const float *k_ring, const float *v_ring,
+                                      int kv_cap, int pos, float *out, void *stream);
+
 /* Interleaved-pair RoPE of x [n_heads*head_dim] at logical position pos,
  * cos/sin from rope_freqs ([head_dim/2][2], device) or, when NULL, derived on
  * the device (vox_apply_rope, voxtral_kernels.c:502-526). */

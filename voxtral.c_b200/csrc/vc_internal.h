@@ -89,6 +89,9 @@ cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool
 cudaError_t launch_fill_alts(const float *logits, int vocab, const int *best, int n_alt,
                              float cutoff, int *out_ids, cudaStream_t st);
 
+// Set the message vox_cuda_last_error() returns on the calling thread.
+void set_last_error(const char *fmt, ...);
+
 cudaError_t launch_rope(float *x, int n_heads, int head_dim, const float *cs, cudaStream_t st);
 cudaError_t launch_fill_normal_bf16(uint16_t *dst, size_t n, uint64_t seed, float std,
                                     cudaStream_t st);

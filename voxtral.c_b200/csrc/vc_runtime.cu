@@ -33,6 +33,15 @@ static void set_error(const char *fmt, ...) {
     va_end(ap);
 }
 
+namespace vc {
+void set_last_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof(t_err), fmt, ap);
+    va_end(ap);
+}
+}  // namespace vc
+
 #define VC_TRY(call)                                                                  \
     do {                                                                              \
         cudaError_t e_ = (call);                                                      \

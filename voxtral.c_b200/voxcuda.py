@@ -92,6 +92,8 @@ def lib():
                                            C.c_int),
         "vox_cuda_attention_decode_dev": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                            C.c_void_p, C.c_void_p], C.c_int),
+        "vox_cuda_attention_decode_noalloc": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                               C.c_int, C.c_void_p, C.c_void_p], C.c_int),
         "vox_cuda_rope_dev": ([C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p],
                               C.c_int),
         "vox_cuda_fill_normal_bf16_dev": ([C.c_void_p, C.c_size_t, C.c_uint64, C.c_float,
