@@ -72,8 +72,9 @@ size_t vox_cuda_memory_used(void);
  * pointer (the mmap'd tensor), like the Metal pointer-keyed weight cache.
  * Replaces vox_metal_sgemm_bf16 (voxtral_metal.h:38-41) at the dispatch
  * points of vox_linear_nobias_bf16 / vox_linear_bf16 / vox_matmul_t_bf16
- * (voxtral_kernels.c:197-264).  M <= 8 runs the streaming GEMV, larger M the
- * tcgen05 tensor-core GEMM. */
+ * (voxtral_kernels.c:197-264).  M <= 8 runs the streaming GEMV (fp32-level
+ * accuracy); larger M the tcgen05 tensor-core GEMM, whose activations are
+ * rounded to bf16 (<= 5e-3 relative L2 per matmul). */
 int vox_cuda_sgemm_bf16(int M, int N, int K, const float *A, const uint16_t *B_bf16,
                         const float *bias, float *C);
 
@@ -91,6 +92,13 @@ void vox_cuda_weight_cache_clear(void);
  * B in its row-major layout (tiled copy cached by pointer, as above). */
 int vox_cuda_linear_bf16_dev(int M, int N, int K, const float *A, const uint16_t *B_bf16,
                              const float *bias, float *C, void *stream);
+
+/* Tensor-core GEMM on device pointers: C[M,N] (fp32) = A[M,K] . W[N,K]^T
+ * (+ bias) with bf16 A and W, fp32 accumulation (tcgen05 / TMEM, TMA-fed).
+ * K must be a multiple of 8 and A, W 16-byte aligned.  The building block of
+ * the encoder chunk and adapter (voxtral_encoder.c:542-616, 663-667). */
+int vox_cuda_gemm_bf16_dev(int M, int N, int K, const uint16_t *A_bf16, const uint16_t *W_bf16,
+                           const float *bias, float *C, void *stream);
 
 /* ------------------------------------------------------------------------
  * (2) (4) (5) decoder: resident weights, KV ring, single-token step

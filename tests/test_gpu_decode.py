@@ -48,8 +48,11 @@ def test_sgemm_bf16_matches_reference(case):
     x, W, b = G.linear_inputs(M, K, N, bias, seed)
     V.lib().vox_cuda_weight_cache_clear()   # W is a fresh array at a possibly reused address
     y = V.sgemm_bf16(x, W, b)
-    assert sampled_rel(y, g, name) < GEMV_TOL * 1e-2
-    assert B.rel_l2(y, B.linear(x, W, b)) < 1e-5
+    if M <= 8:   # streaming GEMV: fp32-level accuracy (contract 1e-3)
+        assert sampled_rel(y, g, name) < GEMV_TOL * 1e-2
+        assert B.rel_l2(y, B.linear(x, W, b)) < 1e-5
+    else:        # tensor-core GEMM on bf16 activations (contract 5e-3)
+        assert sampled_rel(y, g, name) < 5e-3
     y2 = V.sgemm_bf16(x, W, b)                # served from the weight cache
     assert np.array_equal(y, y2)
 

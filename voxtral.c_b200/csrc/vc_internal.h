@@ -89,6 +89,41 @@ cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool
 cudaError_t launch_fill_alts(const float *logits, int vocab, const int *best, int n_alt,
                              float cutoff, int *out_ids, cudaStream_t st);
 
+// ---- tcgen05 tensor-core GEMM (vc_gemm_tc.cu) ----
+enum TcEpi : int {
+    TC_STORE = 0,     // out = acc (+ bias) (GELU if act == 1); fp32, or bf16 when out_bf16
+    TC_RESID = 1,     // out += acc (+ bias)   (fp32 residual stream)
+    TC_SWIGLU = 2,    // cols (2i, 2i+1) = (gate_i, up_i) -> out_bf16[i] = silu(g) * u
+    TC_QKV_ENC = 3,   // encoder q|k|v: bias, RoPE, q (fp16) out, k / v (fp16) to the ring
+};
+
+struct TcGemmParams {
+    int M, N, K;
+    float *out;              // fp32 [M, ldo]
+    int ldo;
+    const float *bias;       // [N] (TC_QKV_ENC: the q bias) or NULL
+    const float *bias2;      // TC_QKV_ENC: the v bias, or NULL
+    int act;                 // TC_STORE: 0 none, 1 tanh-GELU
+    uint16_t *out_bf16;      // bf16 output [M, ldo_bf16] or NULL
+    int ldo_bf16;
+    // TC_QKV_ENC
+    const float *rope;       // [M][64]: (cos, sin) pairs of each row's position
+    uint16_t *q_out;         // fp16 [M][2048]
+    uint16_t *k_ring;        // fp16 [cap][2048] (this layer)
+    uint16_t *v_ring;
+    int cap, pos0;           // row r sits at logical position pos0 + r, slot (pos0 + r) % cap
+    unsigned *err;           // raised when a bounded wait expires
+};
+
+// C = A . W^T with bf16 A [M, K] and W [N, K] (row-major, 16-byte aligned,
+// K % 8 == 0).  bn = 0 picks the tile width.
+cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p, const void *A, const void *W, cudaStream_t st,
+                           bool pdl, int bn = 0);
+int tc_gemm_bn(int M, int N);
+// fp32 rows -> bf16 rows, optionally RMS-normalised with weights w.
+cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const float *w, uint16_t *out,
+                                cudaStream_t st, bool pdl);
+
 // Set the message vox_cuda_last_error() returns on the calling thread.
 void set_last_error(const char *fmt, ...);
 

@@ -82,6 +82,9 @@ struct DevCtx {
         size_t bytes;
     };
     std::unordered_map<const void *, CachedW> wcache;  // caller's weight ptr -> tiled copy
+    std::unordered_map<const void *, CachedW> wcache_rm;  // ... -> row-major copy (tensor-core GEMM)
+    uint16_t *sa16 = nullptr;                           // bf16 activations of the M > 8 path
+    size_t sa16_n = 0;
     uint16_t *stage = nullptr;                          // row-major upload staging
     size_t stage_bytes = 0;
     // scratch for the host-pointer matmul entry and the kernel-level entries
@@ -244,6 +247,11 @@ extern "C" void vox_cuda_shutdown(void) {
         cudaStreamSynchronize(c->stream);
         for (auto &kv : c->wcache) cudaFree(kv.second.dev);
         c->wcache.clear();
+        for (auto &kv : c->wcache_rm) cudaFree(kv.second.dev);
+        c->wcache_rm.clear();
+        cudaFree(c->sa16);
+        c->sa16 = nullptr;
+        c->sa16_n = 0;
         cudaFree(c->stage);
         c->stage = nullptr;
         c->stage_bytes = 0;
@@ -408,6 +416,39 @@ extern "C" void vox_cuda_weight_cache_clear(void) {
         c->bytes -= kv.second.bytes;
     }
     c->wcache.clear();
+    for (auto &kv : c->wcache_rm) {
+        cudaFree(kv.second.dev);
+        c->bytes -= kv.second.bytes;
+    }
+    c->wcache_rm.clear();
+}
+
+// Row-major device copy of a host [N, K] weight for the tensor-core GEMM
+// (same keying and staleness rules as cached_weight).  Caller holds c->mu.
+static const uint16_t *cached_weight_rm(DevCtx *c, const uint16_t *host, int N, int K, int *rc) {
+    auto it = c->wcache_rm.find(host);
+    if (it != c->wcache_rm.end()) {
+        if (it->second.N == N && it->second.K == K) return it->second.dev;
+        cudaFree(it->second.dev);
+        c->bytes -= it->second.bytes;
+        c->wcache_rm.erase(it);
+    }
+    const size_t bytes = (size_t)N * K * 2;
+    uint16_t *d = nullptr;
+    if (cudaMalloc(&d, bytes) != cudaSuccess) {
+        set_error("weight cache: cudaMalloc(%zu) failed", bytes);
+        *rc = VOX_CUDA_ERR_OOM;
+        return nullptr;
+    }
+    if (cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(d);
+        set_error("weight cache: upload failed");
+        *rc = VOX_CUDA_ERR_CUDA;
+        return nullptr;
+    }
+    c->wcache_rm[host] = DevCtx::CachedW{d, N, K, bytes};
+    c->bytes += bytes;
+    return d;
 }
 
 extern "C" int vox_cuda_warmup_bf16(const uint16_t *B_bf16, int N, int K) {
@@ -427,9 +468,17 @@ extern "C" int vox_cuda_sgemm_bf16(int M, int N, int K, const float *A, const ui
     if (rc) return rc;
     DevCtx *c = cur_ctx();
     if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
-    const uint16_t *W = cached_weight(c, B_bf16, N, K, true, &rc);
-    if (!W) return rc;
+    const bool tensor_core = M > kMaxBatch && K % 8 == 0;
+    const uint16_t *W = nullptr;
+    if (!tensor_core) {
+        W = cached_weight(c, B_bf16, N, K, true, &rc);
+        if (!W) return rc;
+    }
     std::lock_guard<std::mutex> lk(c->mu);  // one user of the host-path scratch at a time
+    if (tensor_core) {
+        W = cached_weight_rm(c, B_bf16, N, K, &rc);
+        if (!W) return rc;
+    }
     // (dev_alloc takes the same mutex: allocate through grow_locked below)
     auto grow_locked = [&](float **p, size_t *cap, size_t n) -> int {
         if (*cap >= n) return VOX_CUDA_OK;
@@ -452,8 +501,41 @@ extern "C" int vox_cuda_sgemm_bf16(int M, int N, int K, const float *A, const ui
     if (bias && (rc = grow_locked(&c->sb, &c->sb_n, (size_t)N))) return rc;
     VC_TRY(cudaMemcpyAsync(c->sx, A, (size_t)M * K * 4, cudaMemcpyHostToDevice, c->stream));
     if (bias) VC_TRY(cudaMemcpyAsync(c->sb, bias, (size_t)N * 4, cudaMemcpyHostToDevice, c->stream));
-    rc = enqueue_linear(c, M, N, K, c->sx, W, bias ? c->sb : nullptr, c->sy, c->stream);
-    if (rc) return rc;
+    if (tensor_core) {
+        // activations rounded to bf16 for the tensor cores (contract: <= 5e-3
+        // relative L2 per tensor-core GEMM); fp32 accumulation and output
+        if (c->sa16_n < (size_t)M * K) {
+            cudaFree(c->sa16);
+            c->bytes -= c->sa16_n * 2;
+            c->sa16 = nullptr;
+            c->sa16_n = 0;
+            if (cudaMalloc(&c->sa16, (size_t)M * K * 2) != cudaSuccess) {
+                set_error("scratch: cudaMalloc(%zu) failed", (size_t)M * K * 2);
+                return VOX_CUDA_ERR_OOM;
+            }
+            c->sa16_n = (size_t)M * K;
+            c->bytes += c->sa16_n * 2;
+        }
+        if (!c->lin_err) {
+            if (cudaMalloc(&c->lin_err, sizeof(unsigned)) != cudaSuccess) return VOX_CUDA_ERR_OOM;
+            VC_TRY(cudaMemset(c->lin_err, 0, sizeof(unsigned)));
+            VC_TRY(cudaEventCreateWithFlags(&c->lin_done, cudaEventDisableTiming));
+            VC_TRY(cudaEventRecord(c->lin_done, c->stream));
+        }
+        VC_TRY(launch_rows_to_bf16(c->sx, M, K, K, nullptr, c->sa16, c->stream, false));
+        TcGemmParams tp = {};
+        tp.M = M;
+        tp.N = N;
+        tp.K = K;
+        tp.out = c->sy;
+        tp.ldo = N;
+        tp.bias = bias ? c->sb : nullptr;
+        tp.err = c->lin_err;
+        VC_TRY(launch_tc_gemm(TC_STORE, tp, c->sa16, W, c->stream, false));
+    } else {
+        rc = enqueue_linear(c, M, N, K, c->sx, W, bias ? c->sb : nullptr, c->sy, c->stream);
+        if (rc) return rc;
+    }
     VC_TRY(cudaMemcpyAsync(C, c->sy, (size_t)M * N * 4, cudaMemcpyDeviceToHost, c->stream));
     unsigned err = 0;
     VC_TRY(cudaMemcpyAsync(&err, c->lin_err, sizeof(err), cudaMemcpyDeviceToHost, c->stream));
@@ -1438,5 +1520,37 @@ extern "C" int vox_cuda_decoder_profile_batch(vox_cuda_dec_state *const *states,
     for (auto &e : evs) cudaEventDestroy(e);
     if (rc) return rc;
     for (int i = 0; i < VOX_CUDA_PROF_PHASES; i++) ms[i] = (float)(acc[i] / iters);
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_gemm_bf16_dev(int M, int N, int K, const uint16_t *A_bf16, const uint16_t *W_bf16,
+                                      const float *bias, float *C, void *stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || K % 8 != 0 || !A_bf16 || !W_bf16 || !C) {
+        set_error("gemm_bf16_dev: bad arguments (M=%d N=%d K=%d; K must be a multiple of 8)", M, N, K);
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (!aligned16(A_bf16) || !aligned16(W_bf16)) {
+        set_error("gemm_bf16_dev: A and W must be 16-byte aligned");
+        return VOX_CUDA_ERR_ARG;
+    }
+    DevCtx *c = cur_ctx();
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    std::lock_guard<std::mutex> lk(c->mu);
+    if (!c->lin_err) {
+        if (cudaMalloc(&c->lin_err, sizeof(unsigned)) != cudaSuccess) return VOX_CUDA_ERR_OOM;
+        VC_TRY(cudaMemset(c->lin_err, 0, sizeof(unsigned)));
+        VC_TRY(cudaEventCreateWithFlags(&c->lin_done, cudaEventDisableTiming));
+        VC_TRY(cudaEventRecord(c->lin_done, st));
+    }
+    TcGemmParams tp = {};
+    tp.M = M;
+    tp.N = N;
+    tp.K = K;
+    tp.out = C;
+    tp.ldo = N;
+    tp.bias = bias;
+    tp.err = c->lin_err;
+    VC_TRY(launch_tc_gemm(TC_STORE, tp, A_bf16, W_bf16, st, false));
     return VOX_CUDA_OK;
 }

@@ -73,6 +73,8 @@ def lib():
         "vox_cuda_weight_cache_clear": ([], None),
         "vox_cuda_linear_bf16_dev": ([C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
+        "vox_cuda_gemm_bf16_dev": ([C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_void_p, C.c_void_p], C.c_int),
         "vox_cuda_decoder_create": ([C.c_void_p], C.c_void_p),
         "vox_cuda_decoder_free": ([C.c_void_p], None),
         "vox_cuda_dec_state_create": ([C.c_void_p, C.c_int], C.c_void_p),
