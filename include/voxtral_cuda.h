@@ -216,6 +216,69 @@ int vox_cuda_decoder_profile_batch(vox_cuda_dec_state *const *states, int n,
                                    const float *embeds_dev, int iters, float *ms);
 
 /* ------------------------------------------------------------------------
+ * (3) (5) encoder chunk + adapter: tcgen05 GEMMs, windowed attention, ring
+ * ------------------------------------------------------------------------ */
+
+#define VOX_CUDA_ENC_MAX_LAYERS 32
+
+typedef struct {
+    const uint16_t *wq, *wk, *wv;        /* bf16 [2048,1280] each */
+    const uint16_t *wo;                  /* bf16 [1280,2048] */
+    const uint16_t *w1, *w2, *w3;        /* bf16 [5120,1280] [1280,5120] [5120,1280] */
+    const float *wq_bias, *wv_bias;      /* [2048] (wk has no bias) */
+    const float *wo_bias, *w2_bias;      /* [1280] */
+    const float *attention_norm;         /* [1280] */
+    const float *ffn_norm;               /* [1280] */
+} vox_cuda_enc_layer_weights;
+
+/* The encoder and adapter halves of vox_ctx_t (voxtral.h:56-95, 143-148). */
+typedef struct {
+    int n_layers;                        /* VOX_ENC_LAYERS (32) */
+    int weights_on_device;               /* 0: host pointers (uploaded), 1: device */
+    const float *norm;                   /* [1280] final encoder norm */
+    const uint16_t *adapter0;            /* bf16 [3072, 5120] */
+    const uint16_t *adapter1;            /* bf16 [3072, 3072] */
+    vox_cuda_enc_layer_weights layers[VOX_CUDA_ENC_MAX_LAYERS];
+} vox_cuda_enc_weights;
+
+typedef struct vox_cuda_encoder vox_cuda_encoder;     /* resident encoder + adapter weights */
+typedef struct vox_cuda_enc_state vox_cuda_enc_state; /* one stream: encoder KV ring + workspace */
+
+/* Upload the encoder and adapter weights (wq|wk|wv concatenated, w1/w3
+ * row-interleaved, bf16 row-major for the TMA-fed tensor-core GEMM).  The
+ * counterpart of the Metal encoder warm-up (voxtral.c:169-192). */
+vox_cuda_encoder *vox_cuda_encoder_create(const vox_cuda_enc_weights *w);
+void vox_cuda_encoder_free(vox_cuda_encoder *e);
+
+/* Per-stream encoder state for chunks of up to max_chunk rows: an fp16 KV
+ * ring of 750 + max_chunk positions per layer (the 750-row window plus a
+ * chunk; the Metal build preallocates 750+256, voxtral.c:236) and the chunk
+ * workspace.  Replaces vox_encoder_kv_cache_preallocate and the enc_inc_*
+ * buffers (voxtral_encoder.c:328-446). */
+vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, int max_chunk);
+void vox_cuda_enc_state_free(vox_cuda_enc_state *s);
+int vox_cuda_enc_state_reset(vox_cuda_enc_state *s);      /* voxtral.c:959-961 */
+int vox_cuda_enc_state_position(const vox_cuda_enc_state *s);
+
+/* Incremental encoder over new_len post-conv-stem rows, in place on host x
+ * [new_len, 1280]: 32 layers of RMSNorm, QKV (+bias, RoPE, ring write),
+ * causal window-750 attention, wo (+bias) + residual, RMSNorm, w1|w3 SwiGLU,
+ * w2 (+bias) + residual, then the final norm (vox_encoder_forward_incremental,
+ * voxtral_encoder.c:452-636; vox_metal_encoder_full_step, voxtral_metal.h:245).
+ * rope_freqs: host [new_len][32][2] or NULL.  GEMM activations are rounded to
+ * bf16 and attention runs in fp16 with fp32 accumulation. */
+int vox_cuda_encoder_full_step(vox_cuda_enc_state *s, float *x, int new_len, const float *rope_freqs);
+
+/* Device-resident form: x_dev [new_len, 1280] on the device, in place. */
+int vox_cuda_encoder_step_dev(vox_cuda_enc_state *s, float *x_dev, int new_len, void *stream);
+
+/* Adapter over n encoder rows (n a multiple of 4, at most 4 * max_chunk / 4 of
+ * the state's workspace): 4x frame stacking, Linear(5120->3072), GELU,
+ * Linear(3072->3072); host enc [n, 1280] -> out [n/4, 3072]
+ * (vox_adapter_forward, voxtral_encoder.c:642-674). */
+int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc, int n, float *out);
+
+/* ------------------------------------------------------------------------
  * Kernel-level entry points (device pointers) - the decode attention and the
  * LM-head argmax on their own, for callers that compose their own step.
  * ------------------------------------------------------------------------ */

@@ -1,0 +1,99 @@
+"""Encoder chunk (tcgen05 GEMMs + windowed fp16 flash attention + fp16 ring)
+and adapter against the reference's golden vectors and the oracle.
+
+The GEMMs round activations to bf16 (<= 5e-3 per matmul, tested in
+test_gpu_gemm_tc.py) and attention runs on fp16 inputs; over 32 residual
+layers the encoder output stays within ENC_TOL of the fp32 reference."""
+import numpy as np
+import pytest
+
+import bind as B
+import gen_golden as G
+import voxcuda as V
+from conftest import load_golden, unpack
+
+pytestmark = pytest.mark.gpu
+
+ENC_TOL = 1e-2       # 32-layer encoder output rel-L2 vs the fp32 reference (measured ~3e-3)
+ADAPTER_TOL = 1e-2   # adapter (2 tensor-core GEMMs) on identical inputs
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda():
+    V.init()
+    yield
+
+
+def make_gpu_encoder(ew):
+    layers = [tuple(ew.layer_w[i]) + tuple(ew.layer_b[i]) + tuple(ew.layer_n[i])
+              for i in range(ew.n_layers)]
+    return V.Encoder(layers, ew.norm, ew.adapter0, ew.adapter1)
+
+
+@pytest.fixture(scope="module")
+def enc_w():
+    return B.EncoderWeights(seed=G.DEC_SEED)
+
+
+@pytest.fixture(scope="module")
+def gpu_enc(enc_w):
+    e = make_gpu_encoder(enc_w)
+    yield e
+    e.free()
+
+
+def sampled_rel(arr, g, prefix):
+    idx, val, _, size = unpack(g, prefix)
+    flat = np.asarray(arr, np.float32).reshape(-1)
+    assert flat.size == size
+    return B.rel_l2(flat[idx], val)
+
+
+def test_encoder_chunks_match_reference(gpu_enc):
+    """Chunks of 100, 37, 700, 100 rows: the last two cross the 750-row window
+    (the reference compacts its cache before the fourth)."""
+    g = load_golden("encoder")
+    st = gpu_enc.state(max_chunk=1024)
+    rels = []
+    for i, x in enumerate(G.enc_chunks()):
+        y = st.step(x)
+        assert np.isfinite(y).all()
+        rels.append(sampled_rel(y, g, f"chunk{i}"))
+    print("encoder chunk rel-L2 vs reference:", rels)
+    assert max(rels) < ENC_TOL, rels
+    assert st.position == sum(G.ENC_CHUNKS)
+    st.free()
+
+
+def test_encoder_matches_oracle_small_model():
+    ew = B.EncoderWeights(seed=5, n_layers=3, distinct=3, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    st = e.state(max_chunk=256)
+    o = B.OracleEncoder(ew, kv_max=2400)
+    for i, n in enumerate([64, 200, 3, 250, 130]):   # crosses the window, ragged sizes
+        x = B.normal_f32((n, B.ENC_DIM), 900 + i)
+        yo = o.step(x)
+        yg = st.step(x)
+        assert B.rel_l2(yg, yo) < 5e-3, (i, B.rel_l2(yg, yo))
+    st.free()
+    e.free()
+
+
+def test_adapter_matches_oracle(gpu_enc, enc_w):
+    o = B.OracleEncoder(enc_w, kv_max=2400)
+    chunks = G.enc_chunks()
+    enc = np.concatenate([o.step(chunks[0]), o.step(chunks[1])], axis=0)[:136]
+    want = o.adapter(enc)
+    st = gpu_enc.state(max_chunk=256)
+    got = st.adapter(enc)
+    assert B.rel_l2(got, want) < ADAPTER_TOL
+    g = load_golden("encoder")
+    assert sampled_rel(got, g, "adapter136") < ADAPTER_TOL
+    st.free()
+
+
+def test_encoder_rejects_oversized_chunk(gpu_enc):
+    st = gpu_enc.state(max_chunk=64)
+    with pytest.raises(V.VoxCudaError):
+        st.step(np.zeros((65, B.ENC_DIM), np.float32))
+    st.free()

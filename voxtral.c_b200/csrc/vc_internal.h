@@ -124,6 +124,19 @@ int tc_gemm_bn(int M, int N);
 cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const float *w, uint16_t *out,
                                 cudaStream_t st, bool pdl);
 
+// ---- encoder (vc_encoder.cu) ----
+struct EncAttnParams {
+    const uint16_t *q;        // fp16 [M][2048], RoPE applied
+    const uint16_t *k_ring;   // fp16 [cap][2048], this layer
+    const uint16_t *v_ring;
+    int cap;                  // ring positions (>= M + 749)
+    int pos0;                 // logical position of query row 0
+    int M;
+    uint16_t *out;            // bf16 [M][2048]
+};
+cudaError_t launch_enc_attn(const EncAttnParams &p, cudaStream_t st, bool pdl);
+cudaError_t launch_rows_rmsnorm(float *x, int M, int K, const float *w, cudaStream_t st, bool pdl);
+
 // Set the message vox_cuda_last_error() returns on the calling thread.
 void set_last_error(const char *fmt, ...);
 

@@ -1554,3 +1554,410 @@ extern "C" int vox_cuda_gemm_bf16_dev(int M, int N, int K, const uint16_t *A_bf1
     VC_TRY(launch_tc_gemm(TC_STORE, tp, A_bf16, W_bf16, st, false));
     return VOX_CUDA_OK;
 }
+
+// ---------------------------------------------------------------------------
+// encoder chunk + adapter
+// ---------------------------------------------------------------------------
+
+namespace {
+
+struct EncLayer {
+    const uint16_t *qkv = nullptr;   // [6144, 1280] wq|wk|wv
+    const uint16_t *wo = nullptr;    // [1280, 2048]
+    const uint16_t *w13 = nullptr;   // [10240, 1280] w1/w3 row-interleaved
+    const uint16_t *w2 = nullptr;    // [1280, 5120]
+    const float *bq = nullptr, *bv = nullptr, *bo = nullptr, *b2 = nullptr;
+    const float *attn_norm = nullptr, *ffn_norm = nullptr;
+};
+
+// Host RoPE table (head_dim 64) for logical positions pos0..pos0+n-1.
+void host_rope_rows(int pos0, int n, int head_dim, float *cs) {
+    for (int i = 0; i < n; i++) host_rope_table(pos0 + i, head_dim, cs + (size_t)i * head_dim);
+}
+
+}  // namespace
+
+struct vox_cuda_encoder {
+    int device = 0;
+    int n_layers = 0;
+    EncLayer L[kEncLayers];
+    const float *norm = nullptr;
+    const uint16_t *adapter0 = nullptr, *adapter1 = nullptr;
+    std::vector<std::pair<void *, size_t>> owned;
+    bool pdl = true;
+};
+
+struct vox_cuda_enc_state {
+    vox_cuda_encoder *enc = nullptr;
+    int max_chunk = 0, cap = 0, pos = 0;
+    uint16_t *k_ring = nullptr, *v_ring = nullptr;   // fp16 [layers][cap][2048]
+    size_t ring_bytes = 0;
+    char *ws = nullptr;                              // workspace block
+    size_t ws_bytes = 0;
+    float *x = nullptr;          // [Mx][1280] residual stream (fp32)
+    uint16_t *xn16 = nullptr;    // [Mx][1280] bf16 normalised activations
+    uint16_t *att16 = nullptr;   // [Mx][2048] bf16 attention output
+    uint16_t *h16 = nullptr;     // [Mx][5120] bf16 SwiGLU output
+    uint16_t *q16 = nullptr;     // [Mx][2048] fp16 queries
+    float *rope = nullptr;       // [Mx][64]
+    float *aout = nullptr;       // adapter: [Mx/4][3072] fp32 out (Mx/4 x 5120 fp32 in shares x)
+    uint16_t *a16 = nullptr;     // adapter: [Mx/4][5120] bf16 in
+    uint16_t *mid16 = nullptr;   // adapter: [Mx/4][3072] bf16 mid
+    unsigned *err = nullptr;
+    float *h_rope = nullptr;     // pinned [Mx][64]
+};
+
+extern "C" vox_cuda_encoder *vox_cuda_encoder_create(const vox_cuda_enc_weights *w) {
+    DevCtx *c = cur_ctx();
+    if (!c) return nullptr;
+    if (!w || w->n_layers <= 0 || w->n_layers > kEncLayers || !w->norm || !w->adapter0 || !w->adapter1) {
+        set_error("encoder_create: bad weight descriptor");
+        return nullptr;
+    }
+    for (int l = 0; l < w->n_layers; l++) {
+        const vox_cuda_enc_layer_weights &L = w->layers[l];
+        if (!L.wq || !L.wk || !L.wv || !L.wo || !L.w1 || !L.w2 || !L.w3 || !L.wq_bias || !L.wv_bias ||
+            !L.wo_bias || !L.w2_bias || !L.attention_norm || !L.ffn_norm) {
+            set_error("encoder_create: layer %d has a NULL tensor", l);
+            return nullptr;
+        }
+    }
+    vox_cuda_encoder *e = new vox_cuda_encoder();
+    e->device = c->device;
+    e->n_layers = w->n_layers;
+    const char *pdl_env = getenv("VOX_CUDA_PDL");
+    e->pdl = !(pdl_env && pdl_env[0] == '0');
+    const cudaMemcpyKind kind = w->weights_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    bool ok = true;
+    auto alloc = [&](size_t bytes) -> void * {
+        void *p = nullptr;
+        if (dev_alloc(c, &p, bytes) != cudaSuccess) return nullptr;
+        e->owned.push_back({p, bytes});
+        return p;
+    };
+    auto copy_f32 = [&](const float *src, size_t n) -> const float * {
+        float *d = (float *)alloc(n * 4);
+        if (!d || cudaMemcpy(d, src, n * 4, kind) != cudaSuccess) {
+            ok = false;
+            return nullptr;
+        }
+        return d;
+    };
+    const size_t D = kEncDim, Q = kEncQkv, H = kEncHidden;
+    for (int l = 0; l < w->n_layers && ok; l++) {
+        const vox_cuda_enc_layer_weights &L = w->layers[l];
+        EncLayer &o = e->L[l];
+        for (int j = 0; j < l; j++) {   // aliased layers share device copies
+            const vox_cuda_enc_layer_weights &J = w->layers[j];
+            if (J.wq == L.wq && J.wk == L.wk && J.wv == L.wv && J.wo == L.wo && J.w1 == L.w1 && J.w2 == L.w2 &&
+                J.w3 == L.w3) {
+                o.qkv = e->L[j].qkv;
+                o.wo = e->L[j].wo;
+                o.w13 = e->L[j].w13;
+                o.w2 = e->L[j].w2;
+                break;
+            }
+        }
+        if (!o.qkv) {
+            uint16_t *qkv = (uint16_t *)alloc(3 * Q * D * 2);
+            uint16_t *wo = (uint16_t *)alloc(D * Q * 2);
+            uint16_t *w13 = (uint16_t *)alloc(2 * H * D * 2);
+            uint16_t *w2 = (uint16_t *)alloc(D * H * 2);
+            ok = qkv && wo && w13 && w2;
+            if (!ok) break;
+            ok &= cudaMemcpy(qkv, L.wq, Q * D * 2, kind) == cudaSuccess;
+            ok &= cudaMemcpy(qkv + Q * D, L.wk, Q * D * 2, kind) == cudaSuccess;
+            ok &= cudaMemcpy(qkv + 2 * Q * D, L.wv, Q * D * 2, kind) == cudaSuccess;
+            ok &= cudaMemcpy(wo, L.wo, D * Q * 2, kind) == cudaSuccess;
+            ok &= cudaMemcpy2D(w13, 2 * D * 2, L.w1, D * 2, D * 2, H, kind) == cudaSuccess;
+            ok &= cudaMemcpy2D(w13 + D, 2 * D * 2, L.w3, D * 2, D * 2, H, kind) == cudaSuccess;
+            ok &= cudaMemcpy(w2, L.w2, D * H * 2, kind) == cudaSuccess;
+            o.qkv = qkv;
+            o.wo = wo;
+            o.w13 = w13;
+            o.w2 = w2;
+        }
+        o.bq = copy_f32(L.wq_bias, Q);
+        o.bv = copy_f32(L.wv_bias, Q);
+        o.bo = copy_f32(L.wo_bias, D);
+        o.b2 = copy_f32(L.w2_bias, D);
+        o.attn_norm = copy_f32(L.attention_norm, D);
+        o.ffn_norm = copy_f32(L.ffn_norm, D);
+    }
+    if (ok) {
+        e->norm = copy_f32(w->norm, D);
+        uint16_t *a0 = (uint16_t *)alloc((size_t)kDecDim * 4 * D * 2);
+        uint16_t *a1 = (uint16_t *)alloc((size_t)kDecDim * kDecDim * 2);
+        ok = ok && a0 && a1;
+        if (ok) {
+            ok &= cudaMemcpy(a0, w->adapter0, (size_t)kDecDim * 4 * D * 2, kind) == cudaSuccess;
+            ok &= cudaMemcpy(a1, w->adapter1, (size_t)kDecDim * kDecDim * 2, kind) == cudaSuccess;
+            e->adapter0 = a0;
+            e->adapter1 = a1;
+        }
+    }
+    if (!ok) {
+        if (!t_err[0]) set_error("encoder_create: weight upload failed");
+        vox_cuda_encoder_free(e);
+        return nullptr;
+    }
+    return e;
+}
+
+extern "C" void vox_cuda_encoder_free(vox_cuda_encoder *e) {
+    if (!e) return;
+    DevCtx *c = ctx_for(e->device);
+    cudaSetDevice(e->device);
+    if (c) cudaStreamSynchronize(c->stream);
+    for (auto &pr : e->owned)
+        if (c) dev_free(c, pr.first, pr.second);
+        else cudaFree(pr.first);
+    delete e;
+}
+
+extern "C" vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, int max_chunk) {
+    if (!e || max_chunk <= 0 || max_chunk > 8192) {
+        set_error("enc_state_create: max_chunk must be 1..8192");
+        return nullptr;
+    }
+    DevCtx *c = ctx_for(e->device);
+    if (!c) {
+        set_error("enc_state_create: device not initialised");
+        return nullptr;
+    }
+    cudaSetDevice(e->device);
+    vox_cuda_enc_state *s = new vox_cuda_enc_state();
+    s->enc = e;
+    s->max_chunk = (max_chunk + 3) / 4 * 4;
+    s->cap = kEncWindow + s->max_chunk;
+    s->ring_bytes = (size_t)e->n_layers * s->cap * kEncQkv * 2;
+    const size_t Mx = s->max_chunk;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const size_t o_x = take(Mx * kEncDim * 4);
+    const size_t o_xn = take(Mx * kEncDim * 2);
+    const size_t o_att = take(Mx * kEncQkv * 2);
+    const size_t o_h = take(Mx * kEncHidden * 2);
+    const size_t o_q = take(Mx * kEncQkv * 2);
+    const size_t o_rope = take(Mx * kEncHeadDim * 4);
+    const size_t o_aout = take(Mx / 4 * kDecDim * 4);
+    const size_t o_a16 = take(Mx / 4 * 4 * kEncDim * 2);
+    const size_t o_mid = take(Mx / 4 * kDecDim * 2);
+    const size_t o_err = take(sizeof(unsigned));
+    s->ws_bytes = off;
+    if (dev_alloc(c, (void **)&s->k_ring, s->ring_bytes) != cudaSuccess ||
+        dev_alloc(c, (void **)&s->v_ring, s->ring_bytes) != cudaSuccess ||
+        dev_alloc(c, (void **)&s->ws, s->ws_bytes) != cudaSuccess ||
+        cudaHostAlloc((void **)&s->h_rope, Mx * kEncHeadDim * 4, cudaHostAllocDefault) != cudaSuccess) {
+        set_error("enc_state_create: allocation failed");
+        vox_cuda_enc_state_free(s);
+        return nullptr;
+    }
+    s->x = (float *)(s->ws + o_x);
+    s->xn16 = (uint16_t *)(s->ws + o_xn);
+    s->att16 = (uint16_t *)(s->ws + o_att);
+    s->h16 = (uint16_t *)(s->ws + o_h);
+    s->q16 = (uint16_t *)(s->ws + o_q);
+    s->rope = (float *)(s->ws + o_rope);
+    s->aout = (float *)(s->ws + o_aout);
+    s->a16 = (uint16_t *)(s->ws + o_a16);
+    s->mid16 = (uint16_t *)(s->ws + o_mid);
+    s->err = (unsigned *)(s->ws + o_err);
+    if (cudaMemset(s->k_ring, 0, s->ring_bytes) != cudaSuccess ||
+        cudaMemset(s->v_ring, 0, s->ring_bytes) != cudaSuccess ||
+        cudaMemset(s->ws, 0, s->ws_bytes) != cudaSuccess) {
+        set_error("enc_state_create: clear failed");
+        vox_cuda_enc_state_free(s);
+        return nullptr;
+    }
+    return s;
+}
+
+extern "C" void vox_cuda_enc_state_free(vox_cuda_enc_state *s) {
+    if (!s) return;
+    DevCtx *c = ctx_for(s->enc->device);
+    cudaSetDevice(s->enc->device);
+    if (c) cudaStreamSynchronize(c->stream);
+    if (c) {
+        dev_free(c, s->k_ring, s->k_ring ? s->ring_bytes : 0);
+        dev_free(c, s->v_ring, s->v_ring ? s->ring_bytes : 0);
+        dev_free(c, s->ws, s->ws ? s->ws_bytes : 0);
+    }
+    if (s->h_rope) cudaFreeHost(s->h_rope);
+    delete s;
+}
+
+extern "C" int vox_cuda_enc_state_reset(vox_cuda_enc_state *s) {
+    if (!s) return VOX_CUDA_ERR_ARG;
+    s->pos = 0;
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_enc_state_position(const vox_cuda_enc_state *s) { return s ? s->pos : -1; }
+
+namespace {
+
+// The 32 layers + final norm over s->x (M rows at logical positions s->pos..).
+int enqueue_encoder(vox_cuda_enc_state *s, int M, cudaStream_t st) {
+    vox_cuda_encoder *e = s->enc;
+    const bool pdl = e->pdl;
+    const int pos0 = s->pos;
+    const size_t ring_layer = (size_t)s->cap * kEncQkv;
+    for (int l = 0; l < e->n_layers; l++) {
+        const EncLayer &L = e->L[l];
+        VC_TRY(launch_rows_to_bf16(s->x, M, kEncDim, kEncDim, L.attn_norm, s->xn16, st, pdl));
+        TcGemmParams p = {};
+        p.M = M;
+        p.N = 3 * kEncQkv;
+        p.K = kEncDim;
+        p.bias = L.bq;
+        p.bias2 = L.bv;
+        p.rope = s->rope;
+        p.q_out = s->q16;
+        p.k_ring = s->k_ring + l * ring_layer;
+        p.v_ring = s->v_ring + l * ring_layer;
+        p.cap = s->cap;
+        p.pos0 = pos0;
+        p.err = s->err;
+        VC_TRY(launch_tc_gemm(TC_QKV_ENC, p, s->xn16, L.qkv, st, pdl));
+        EncAttnParams a = {};
+        a.q = s->q16;
+        a.k_ring = s->k_ring + l * ring_layer;
+        a.v_ring = s->v_ring + l * ring_layer;
+        a.cap = s->cap;
+        a.pos0 = pos0;
+        a.M = M;
+        a.out = s->att16;
+        VC_TRY(launch_enc_attn(a, st, pdl));
+        p = TcGemmParams{};
+        p.M = M;
+        p.N = kEncDim;
+        p.K = kEncQkv;
+        p.out = s->x;
+        p.ldo = kEncDim;
+        p.bias = L.bo;
+        p.err = s->err;
+        VC_TRY(launch_tc_gemm(TC_RESID, p, s->att16, L.wo, st, pdl));
+        VC_TRY(launch_rows_to_bf16(s->x, M, kEncDim, kEncDim, L.ffn_norm, s->xn16, st, pdl));
+        p = TcGemmParams{};
+        p.M = M;
+        p.N = 2 * kEncHidden;
+        p.K = kEncDim;
+        p.out_bf16 = s->h16;
+        p.ldo_bf16 = kEncHidden;
+        p.err = s->err;
+        VC_TRY(launch_tc_gemm(TC_SWIGLU, p, s->xn16, L.w13, st, pdl));
+        p = TcGemmParams{};
+        p.M = M;
+        p.N = kEncDim;
+        p.K = kEncHidden;
+        p.out = s->x;
+        p.ldo = kEncDim;
+        p.bias = L.b2;
+        p.err = s->err;
+        VC_TRY(launch_tc_gemm(TC_RESID, p, s->h16, L.w2, st, pdl));
+    }
+    VC_TRY(launch_rows_rmsnorm(s->x, M, kEncDim, e->norm, st, pdl));
+    return VOX_CUDA_OK;
+}
+
+int enc_check(vox_cuda_enc_state *s, int new_len) {
+    if (!s || new_len <= 0) {
+        set_error("encoder step: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (new_len > s->max_chunk) {
+        set_error("encoder step: %d rows exceed the state's max_chunk %d", new_len, s->max_chunk);
+        return VOX_CUDA_ERR_CAPACITY;
+    }
+    if (!ctx_for(s->enc->device)) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(s->enc->device);
+    return VOX_CUDA_OK;
+}
+
+int enc_err_check(vox_cuda_enc_state *s, cudaStream_t st) {
+    unsigned err = 0;
+    VC_TRY(cudaMemcpyAsync(&err, s->err, sizeof(err), cudaMemcpyDeviceToHost, st));
+    VC_TRY(cudaStreamSynchronize(st));
+    if (err) {
+        cudaMemset(s->err, 0, sizeof(unsigned));
+        set_error("encoder: a device-side wait timed out (results discarded)");
+        return VOX_CUDA_ERR_CUDA;
+    }
+    return VOX_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" int vox_cuda_encoder_full_step(vox_cuda_enc_state *s, float *x, int new_len,
+                                          const float *rope_freqs) {
+    int rc = enc_check(s, new_len);
+    if (rc) return rc;
+    if (!x) return VOX_CUDA_ERR_ARG;
+    DevCtx *c = ctx_for(s->enc->device);
+    cudaStream_t st = c->stream;
+    if (rope_freqs) memcpy(s->h_rope, rope_freqs, (size_t)new_len * kEncHeadDim * 4);
+    else host_rope_rows(s->pos, new_len, kEncHeadDim, s->h_rope);
+    VC_TRY(cudaMemcpyAsync(s->rope, s->h_rope, (size_t)new_len * kEncHeadDim * 4, cudaMemcpyHostToDevice, st));
+    VC_TRY(cudaMemcpyAsync(s->x, x, (size_t)new_len * kEncDim * 4, cudaMemcpyHostToDevice, st));
+    if ((rc = enqueue_encoder(s, new_len, st))) return rc;
+    VC_TRY(cudaMemcpyAsync(x, s->x, (size_t)new_len * kEncDim * 4, cudaMemcpyDeviceToHost, st));
+    if ((rc = enc_err_check(s, st))) return rc;
+    s->pos += new_len;
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_encoder_step_dev(vox_cuda_enc_state *s, float *x_dev, int new_len, void *stream) {
+    int rc = enc_check(s, new_len);
+    if (rc) return rc;
+    if (!x_dev) return VOX_CUDA_ERR_ARG;
+    DevCtx *c = ctx_for(s->enc->device);
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    host_rope_rows(s->pos, new_len, kEncHeadDim, s->h_rope);
+    VC_TRY(cudaMemcpyAsync(s->rope, s->h_rope, (size_t)new_len * kEncHeadDim * 4, cudaMemcpyHostToDevice, st));
+    VC_TRY(cudaMemcpyAsync(s->x, x_dev, (size_t)new_len * kEncDim * 4, cudaMemcpyDeviceToDevice, st));
+    if ((rc = enqueue_encoder(s, new_len, st))) return rc;
+    VC_TRY(cudaMemcpyAsync(x_dev, s->x, (size_t)new_len * kEncDim * 4, cudaMemcpyDeviceToDevice, st));
+    if ((rc = enc_err_check(s, st))) return rc;   // also keeps h_rope stable until the copy ran
+    s->pos += new_len;
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc, int n, float *out) {
+    int rc = enc_check(s, n);
+    if (rc) return rc;
+    if (!enc || !out || n % 4 != 0) {
+        set_error("adapter_forward: n must be a positive multiple of 4");
+        return VOX_CUDA_ERR_ARG;
+    }
+    DevCtx *c = ctx_for(s->enc->device);
+    cudaStream_t st = c->stream;
+    vox_cuda_encoder *e = s->enc;
+    const int rows = n / 4, K0 = 4 * kEncDim;
+    // 4 consecutive [1280] rows are one [5120] row: the same memory
+    VC_TRY(cudaMemcpyAsync(s->x, enc, (size_t)n * kEncDim * 4, cudaMemcpyHostToDevice, st));
+    VC_TRY(launch_rows_to_bf16(s->x, rows, K0, K0, nullptr, s->a16, st, false));
+    TcGemmParams p = {};
+    p.M = rows;
+    p.N = kDecDim;
+    p.K = K0;
+    p.act = 1;                  // GELU (voxtral_encoder.c:664)
+    p.out_bf16 = s->mid16;
+    p.ldo_bf16 = kDecDim;
+    p.err = s->err;
+    VC_TRY(launch_tc_gemm(TC_STORE, p, s->a16, e->adapter0, st, false));
+    p = TcGemmParams{};
+    p.M = rows;
+    p.N = kDecDim;
+    p.K = kDecDim;
+    p.out = s->aout;
+    p.ldo = kDecDim;
+    p.err = s->err;
+    VC_TRY(launch_tc_gemm(TC_STORE, p, s->mid16, e->adapter1, st, false));
+    VC_TRY(cudaMemcpyAsync(out, s->aout, (size_t)rows * kDecDim * 4, cudaMemcpyDeviceToHost, st));
+    return enc_err_check(s, st);
+}

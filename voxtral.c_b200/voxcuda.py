@@ -51,6 +51,17 @@ class _DecW(C.Structure):
                 ("layers", _LayerW * MAX_LAYERS)]
 
 
+class _EncLayerW(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "w1", "w2", "w3", "wq_bias",
+                                          "wv_bias", "wo_bias", "w2_bias", "attention_norm",
+                                          "ffn_norm")]
+
+
+class _EncW(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("weights_on_device", C.c_int), ("norm", C.c_void_p),
+                ("adapter0", C.c_void_p), ("adapter1", C.c_void_p), ("layers", _EncLayerW * 32)]
+
+
 _lib = None
 
 
@@ -92,6 +103,15 @@ def lib():
                                              C.c_void_p], C.c_int),
         "vox_cuda_decoder_profile_batch": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, _fp],
                                            C.c_int),
+        "vox_cuda_encoder_create": ([C.c_void_p], C.c_void_p),
+        "vox_cuda_encoder_free": ([C.c_void_p], None),
+        "vox_cuda_enc_state_create": ([C.c_void_p, C.c_int], C.c_void_p),
+        "vox_cuda_enc_state_free": ([C.c_void_p], None),
+        "vox_cuda_enc_state_reset": ([C.c_void_p], C.c_int),
+        "vox_cuda_enc_state_position": ([C.c_void_p], C.c_int),
+        "vox_cuda_encoder_full_step": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
+        "vox_cuda_encoder_step_dev": ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p], C.c_int),
+        "vox_cuda_adapter_forward": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
         "vox_cuda_attention_decode_dev": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                            C.c_void_p, C.c_void_p], C.c_int),
         "vox_cuda_attention_decode_noalloc": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
@@ -268,3 +288,68 @@ def profile_batch(states, embeds_dev, iters=3):
     check(lib().vox_cuda_decoder_profile_batch(states_array(states), len(states), embeds_dev, iters,
                                                _f(ms)), "profile_batch")
     return dict(zip(PROF_PHASES, ms.tolist()))
+
+
+class Encoder:
+    """Resident encoder + adapter weights.  `layers`: n tuples of
+    (wq, wk, wv, wo, w1, w2, w3, wq_bias, wv_bias, wo_bias, w2_bias,
+    attention_norm, ffn_norm); host numpy arrays, or device addresses with
+    on_device=True."""
+
+    def __init__(self, layers, norm, adapter0, adapter1, on_device=False):
+        def addr(a):
+            return int(a) if on_device else a.ctypes.data
+        d = _EncW()
+        d.n_layers = len(layers)
+        d.weights_on_device = 1 if on_device else 0
+        d.norm = addr(norm)
+        d.adapter0 = addr(adapter0)
+        d.adapter1 = addr(adapter1)
+        names = ("wq", "wk", "wv", "wo", "w1", "w2", "w3", "wq_bias", "wv_bias", "wo_bias", "w2_bias",
+                 "attention_norm", "ffn_norm")
+        for i, lw in enumerate(layers):
+            for name, a in zip(names, lw):
+                setattr(d.layers[i], name, addr(a))
+        self.h = lib().vox_cuda_encoder_create(C.byref(d))
+        if not self.h:
+            raise VoxCudaError("encoder_create: " + last_error())
+
+    def state(self, max_chunk=1500):
+        return EncState(self, max_chunk)
+
+    def free(self):
+        if self.h:
+            lib().vox_cuda_encoder_free(self.h)
+            self.h = None
+
+
+class EncState:
+    def __init__(self, enc, max_chunk):
+        self.enc = enc
+        self.h = lib().vox_cuda_enc_state_create(enc.h, max_chunk)
+        if not self.h:
+            raise VoxCudaError("enc_state_create: " + last_error())
+
+    @property
+    def position(self):
+        return lib().vox_cuda_enc_state_position(self.h)
+
+    def step(self, x, rope=None):
+        x = np.array(x, dtype=np.float32, copy=True, order="C")
+        rope = None if rope is None else np.ascontiguousarray(rope, np.float32)
+        check(lib().vox_cuda_encoder_full_step(self.h, _f(x), x.shape[0], _f(rope)), "encoder_full_step")
+        return x
+
+    def adapter(self, enc):
+        enc = np.ascontiguousarray(enc, np.float32)
+        out = np.empty((enc.shape[0] // 4, DEC_DIM), np.float32)
+        check(lib().vox_cuda_adapter_forward(self.h, _f(enc), enc.shape[0], _f(out)), "adapter_forward")
+        return out
+
+    def reset(self):
+        check(lib().vox_cuda_enc_state_reset(self.h), "enc_state_reset")
+
+    def free(self):
+        if self.h:
+            lib().vox_cuda_enc_state_free(self.h)
+            self.h = None
