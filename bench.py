@@ -240,6 +240,100 @@ def build_device_decoder(V, torch, seed=0, layers=LAYERS, vocab=VOCAB):
     return dec
 
 
+ENC_D, ENC_Q, ENC_H, ENC_LAYERS = 1280, 2048, 5120, 32
+ENC_FLOPS_PER_ROW = 2 * ENC_LAYERS * (3 * ENC_Q * ENC_D + ENC_D * ENC_Q + 2 * ENC_H * ENC_D + ENC_D * ENC_H)
+
+
+def build_device_encoder(V, torch, seed=1):
+    """32 distinct random-init encoder layers + adapter, generated on the device."""
+    dev = torch.device("cuda")
+    keep = []
+
+    def bf16(shape, s):
+        t = torch.empty(shape, dtype=torch.int16, device=dev)
+        V.check(V.lib().vox_cuda_fill_normal_bf16_dev(t.data_ptr(), t.numel(), s, 0.02, None), "fill")
+        keep.append(t)
+        return t.data_ptr()
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def f32(n, std):
+        t = (std * torch.randn(n, generator=g, device=dev)).contiguous()
+        keep.append(t)
+        return t.data_ptr()
+    ones = torch.ones(ENC_H, dtype=torch.float32, device=dev)
+    layers = []
+    for l in range(ENC_LAYERS):
+        b = 100000 * seed + 20 * l
+        layers.append((bf16((ENC_Q, ENC_D), b + 1), bf16((ENC_Q, ENC_D), b + 2), bf16((ENC_Q, ENC_D), b + 3),
+                       bf16((ENC_D, ENC_Q), b + 4), bf16((ENC_H, ENC_D), b + 5), bf16((ENC_D, ENC_H), b + 6),
+                       bf16((ENC_H, ENC_D), b + 7), f32(ENC_Q, 0.02), f32(ENC_Q, 0.02), f32(ENC_D, 0.02),
+                       f32(ENC_D, 0.02), ones.data_ptr(), ones.data_ptr()))
+    a0 = bf16((D, 4 * ENC_D), 100000 * seed + 9001)
+    a1 = bf16((D, D), 100000 * seed + 9002)
+    torch.cuda.synchronize()
+    enc = V.Encoder(layers, ones.data_ptr(), a0, a1, on_device=True)
+    del keep
+    torch.cuda.synchronize()
+    return enc
+
+
+def encoder_bench(V, torch, steps):
+    """Encoder chunk throughput: 32 layers at M = 100,
+    500, 1500 rows (2, 10, 30 s of audio at 50 Hz) with a full 750-row window
+    of earlier context, plus the per-phase profile at M = 1500."""
+    enc = build_device_encoder(V, torch)
+    st = enc.state(max_chunk=1500)
+    stream = torch.cuda.current_stream()
+    out = {"audio_s_per_s": {}, "ms_per_chunk": {}}
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(77)
+    x0 = torch.randn((1500, ENC_D), generator=gen, device="cuda", dtype=torch.float32)
+    for M in (100, 500, 1500):
+        n = max(3, steps // (M // 100 + 1))
+        x = torch.empty((M, ENC_D), dtype=torch.float32, device="cuda")
+        for _ in range(2):
+            st.set_position(750)
+            x.copy_(x0[:M])
+            st.step_dev(x.data_ptr(), M, stream.cuda_stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            st.set_position(750)
+            st.step_dev(x.data_ptr(), M, stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        out["ms_per_chunk"][f"M{M}"] = ms
+        out["audio_s_per_s"][f"M{M}"] = (M / 50.0) / (ms / 1000.0)
+    st.set_position(750)
+    x = x0[:1500].contiguous()
+    prof = st.profile(x.data_ptr(), 1500, iters=3)
+    out["phase_ms_M1500"] = prof
+    w13_flops = 2 * 1500 * 2 * ENC_H * ENC_D * ENC_LAYERS
+    _, _ = peaks()
+    tflops = w13_flops / (prof["w13"] / 1000.0) / 1e12
+    gemm_flops = 1500 * ENC_FLOPS_PER_ROW
+    gemm_ms = prof["qkv"] + prof["wo"] + prof["w13"] + prof["w2"]
+    bf16_peak = bf16_peaks()
+    out["roofline"] = {"kernel": "tc_gemm_kernel<256, TC_SWIGLU> (w1|w3, M=1500)", "bound": "tensor",
+                       "achieved": tflops, "peak": bf16_peak, "unit": "TFLOP/s", "frac": tflops / bf16_peak,
+                       "all_gemms_tflops": gemm_flops / (gemm_ms / 1000.0) / 1e12}
+    st.free()
+    enc.free()
+    return out
+
+
+def bf16_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
+
+
 def our_arm(args):
     ws, rank, local = dist_env()
     import torch
@@ -325,6 +419,11 @@ def our_arm(args):
     kv_bytes = sum(args.layers * min(p + 1, 8192) * KVD * 4 * 2 for p in pos)
     step_bytes = weight_bytes_per_step(args.layers, args.vocab) + kv_bytes
 
+    for st in states:
+        st.free()
+    dec.free()
+    enc_res = None if args.no_encoder else encoder_bench(V, torch, args.steps)
+
     line = None
     if rank == 0:
         cpu = None
@@ -356,11 +455,9 @@ def our_arm(args):
             "phase_ms": prof,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "encoder": enc_res,
         }
         print(json.dumps(line), flush=True)
-    for st in states:
-        st.free()
-    dec.free()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -374,6 +471,7 @@ def main():
     ap.add_argument("--streams", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-encoder", action="store_true")
     # reduced model, for small ncu captures only (the headline uses the full model)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--vocab", type=int, default=VOCAB)

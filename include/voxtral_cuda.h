@@ -272,6 +272,21 @@ int vox_cuda_encoder_full_step(vox_cuda_enc_state *s, float *x, int new_len, con
 /* Device-resident form: x_dev [new_len, 1280] on the device, in place. */
 int vox_cuda_encoder_step_dev(vox_cuda_enc_state *s, float *x_dev, int new_len, void *stream);
 
+/* Set the logical position of the next chunk's first row (resume, tests). */
+int vox_cuda_enc_state_set_position(vox_cuda_enc_state *s, int logical_pos);
+
+/* Per-phase device time of an encoder chunk (kernel by kernel, an event pair
+ * around every launch; the stream position does not advance): mean ms per
+ * chunk written to ms[VOX_CUDA_EPROF_PHASES]. */
+#define VOX_CUDA_EPROF_NORM   0   /* RMSNorm -> bf16 activations (both norms, final norm) */
+#define VOX_CUDA_EPROF_QKV    1   /* wq|wk|wv GEMM + bias + RoPE + ring write */
+#define VOX_CUDA_EPROF_ATTN   2   /* window-750 flash attention */
+#define VOX_CUDA_EPROF_WO     3   /* wo GEMM + bias + residual */
+#define VOX_CUDA_EPROF_W13    4   /* w1|w3 GEMM + SwiGLU */
+#define VOX_CUDA_EPROF_W2     5   /* w2 GEMM + bias + residual */
+#define VOX_CUDA_EPROF_PHASES 6
+int vox_cuda_encoder_profile(vox_cuda_enc_state *s, const float *x_dev, int new_len, int iters, float *ms);
+
 /* Adapter over n encoder rows (n a multiple of 4, at most 4 * max_chunk / 4 of
  * the state's workspace): 4x frame stacking, Linear(5120->3072), GELU,
  * Linear(3072->3072); host enc [n, 1280] -> out [n/4, 3072]

@@ -69,8 +69,9 @@ enc_attn_kernel(const EncAttnParams p) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r0 = blockIdx.x * kEaRows, head = blockIdx.y;
     const int M = p.M;
-    const int p_first = p.pos0 + r0;
-    const int p_last = p.pos0 + min(r0 + kEaRows, M) - 1;
+    const int pos0 = p.pos0_dev ? *p.pos0_dev : p.pos0;
+    const int p_first = pos0 + r0;
+    const int p_last = pos0 + min(r0 + kEaRows, M) - 1;
     const int k_lo = max(0, p_first - (kEncWindow - 1));
     const int n_blocks = (p_last - k_lo) / kEaKeys + 1;
 
@@ -114,7 +115,7 @@ enc_attn_kernel(const EncAttnParams p) {
 
     const int g = lane >> 2, q4 = lane & 3;
     const int row_a = r0 + warp * 16 + g, row_b = row_a + 8;   // this thread's two query rows
-    const int pos_a = p.pos0 + row_a, pos_b = p.pos0 + row_b;
+    const int pos_a = pos0 + row_a, pos_b = pos0 + row_b;
     const float scale = 1.0f / sqrtf((float)kEncHeadDim);
     float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
     float o[8][4];

@@ -168,9 +168,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 } else if constexpr (EPI == TC_QKV_ENC) {
                     // [0,2048): q (+bias, RoPE), [2048,4096): k (RoPE), [4096,6144): v (+bias)
                     // (voxtral_encoder.c:542-559); k and v go to the ring slot of the row
-                    const int pos = p.pos0 + row;
+                    const int pos = (p.pos0_dev ? *p.pos0_dev : p.pos0) + row;
                     const size_t slot = (size_t)(pos % p.cap);
-                    const float *cs = p.rope + (size_t)row * kEncHeadDim;
+                    const float *cs = p.rope ? p.rope + (size_t)row * kEncHeadDim : nullptr;
 #pragma unroll
                     for (int j = 0; j < 16; j += 2) {
                         const int col = col0 + j;
@@ -181,7 +181,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                 b += p.bias[col + 1];
                             }
                             const int d = (col & (kEncHeadDim - 1)) >> 1;
-                            const float c0 = cs[2 * d], s0 = cs[2 * d + 1];
+                            float c0, s0;
+                            if (cs) {
+                                c0 = cs[2 * d];
+                                s0 = cs[2 * d + 1];
+                            } else {   // angle = pos * inv_freq exactly as the host formula
+                                sincosf((float)pos * p.inv_freq[d], &s0, &c0);
+                            }
                             const float oa = __fsub_rn(__fmul_rn(a, c0), __fmul_rn(b, s0));
                             const float ob = __fadd_rn(__fmul_rn(a, s0), __fmul_rn(b, c0));
                             if (col < kEncQkv) {

@@ -107,7 +107,9 @@ struct TcGemmParams {
     uint16_t *out_bf16;      // bf16 output [M, ldo_bf16] or NULL
     int ldo_bf16;
     // TC_QKV_ENC
-    const float *rope;       // [M][64]: (cos, sin) pairs of each row's position
+    const float *rope;       // [M][64]: (cos, sin) pairs of each row's position, or NULL:
+    const float *inv_freq;   //   then cos/sin(pos * inv_freq[d]) on the device ([32])
+    const int *pos0_dev;     // if non-NULL, the logical position of row 0 (overrides pos0)
     uint16_t *q_out;         // fp16 [M][2048]
     uint16_t *k_ring;        // fp16 [cap][2048] (this layer)
     uint16_t *v_ring;
@@ -131,6 +133,7 @@ struct EncAttnParams {
     const uint16_t *v_ring;
     int cap;                  // ring positions (>= M + 749)
     int pos0;                 // logical position of query row 0
+    const int *pos0_dev;      // if non-NULL, overrides pos0
     int M;
     uint16_t *out;            // bf16 [M][2048]
 };

@@ -14,6 +14,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -1570,11 +1571,6 @@ struct EncLayer {
     const float *attn_norm = nullptr, *ffn_norm = nullptr;
 };
 
-// Host RoPE table (head_dim 64) for logical positions pos0..pos0+n-1.
-void host_rope_rows(int pos0, int n, int head_dim, float *cs) {
-    for (int i = 0; i < n; i++) host_rope_table(pos0 + i, head_dim, cs + (size_t)i * head_dim);
-}
-
 }  // namespace
 
 struct vox_cuda_encoder {
@@ -1583,6 +1579,7 @@ struct vox_cuda_encoder {
     EncLayer L[kEncLayers];
     const float *norm = nullptr;
     const uint16_t *adapter0 = nullptr, *adapter1 = nullptr;
+    const float *inv_freq = nullptr;   // [32] RoPE inverse frequencies (head_dim 64)
     std::vector<std::pair<void *, size_t>> owned;
     bool pdl = true;
 };
@@ -1604,7 +1601,10 @@ struct vox_cuda_enc_state {
     uint16_t *a16 = nullptr;     // adapter: [Mx/4][5120] bf16 in
     uint16_t *mid16 = nullptr;   // adapter: [Mx/4][3072] bf16 mid
     unsigned *err = nullptr;
+    int *pos_dev = nullptr;      // logical position of the chunk's first row
     float *h_rope = nullptr;     // pinned [Mx][64]
+    int *h_pos = nullptr;        // pinned
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;   // (rows, rope table?) -> step graph
 };
 
 extern "C" vox_cuda_encoder *vox_cuda_encoder_create(const vox_cuda_enc_weights *w) {
@@ -1685,6 +1685,16 @@ extern "C" vox_cuda_encoder *vox_cuda_encoder_create(const vox_cuda_enc_weights 
         o.ffn_norm = copy_f32(L.ffn_norm, D);
     }
     if (ok) {
+        // RoPE inverse frequencies with the host formula of vox_compute_rope_freqs
+        // (voxtral_kernels.c:494); the device forms pos * inv_freq and its cos/sin
+        float invf[kEncHeadDim / 2];
+        for (int d = 0; d < kEncHeadDim / 2; d++)
+            invf[d] = 1.0f / powf(kRopeTheta, (float)(2 * d) / (float)kEncHeadDim);
+        float *dinv = (float *)alloc(sizeof(invf));
+        ok = dinv && cudaMemcpy(dinv, invf, sizeof(invf), cudaMemcpyHostToDevice) == cudaSuccess;
+        e->inv_freq = dinv;
+    }
+    if (ok) {
         e->norm = copy_f32(w->norm, D);
         uint16_t *a0 = (uint16_t *)alloc((size_t)kDecDim * 4 * D * 2);
         uint16_t *a1 = (uint16_t *)alloc((size_t)kDecDim * kDecDim * 2);
@@ -1748,11 +1758,13 @@ extern "C" vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, in
     const size_t o_a16 = take(Mx / 4 * 4 * kEncDim * 2);
     const size_t o_mid = take(Mx / 4 * kDecDim * 2);
     const size_t o_err = take(sizeof(unsigned));
+    const size_t o_pos = take(sizeof(int));
     s->ws_bytes = off;
     if (dev_alloc(c, (void **)&s->k_ring, s->ring_bytes) != cudaSuccess ||
         dev_alloc(c, (void **)&s->v_ring, s->ring_bytes) != cudaSuccess ||
         dev_alloc(c, (void **)&s->ws, s->ws_bytes) != cudaSuccess ||
-        cudaHostAlloc((void **)&s->h_rope, Mx * kEncHeadDim * 4, cudaHostAllocDefault) != cudaSuccess) {
+        cudaHostAlloc((void **)&s->h_rope, Mx * kEncHeadDim * 4, cudaHostAllocDefault) != cudaSuccess ||
+        cudaHostAlloc((void **)&s->h_pos, sizeof(int), cudaHostAllocDefault) != cudaSuccess) {
         set_error("enc_state_create: allocation failed");
         vox_cuda_enc_state_free(s);
         return nullptr;
@@ -1767,6 +1779,7 @@ extern "C" vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, in
     s->a16 = (uint16_t *)(s->ws + o_a16);
     s->mid16 = (uint16_t *)(s->ws + o_mid);
     s->err = (unsigned *)(s->ws + o_err);
+    s->pos_dev = (int *)(s->ws + o_pos);
     if (cudaMemset(s->k_ring, 0, s->ring_bytes) != cudaSuccess ||
         cudaMemset(s->v_ring, 0, s->ring_bytes) != cudaSuccess ||
         cudaMemset(s->ws, 0, s->ws_bytes) != cudaSuccess) {
@@ -1788,6 +1801,8 @@ extern "C" void vox_cuda_enc_state_free(vox_cuda_enc_state *s) {
         dev_free(c, s->ws, s->ws ? s->ws_bytes : 0);
     }
     if (s->h_rope) cudaFreeHost(s->h_rope);
+    if (s->h_pos) cudaFreeHost(s->h_pos);
+    for (auto &kv : s->graphs) cudaGraphExecDestroy(kv.second);
     delete s;
 }
 
@@ -1801,38 +1816,50 @@ extern "C" int vox_cuda_enc_state_position(const vox_cuda_enc_state *s) { return
 
 namespace {
 
-// The 32 layers + final norm over s->x (M rows at logical positions s->pos..).
-int enqueue_encoder(vox_cuda_enc_state *s, int M, cudaStream_t st) {
+// The 32 layers + final norm over s->x: M rows at the logical positions
+// *s->pos_dev.. (read on the device, so the sequence can be replayed as a
+// graph); RoPE from the uploaded table (table) or computed on the device.
+// evs (profiling only): 2 events per launch, recorded around it.
+int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, cudaEvent_t *evs = nullptr) {
     vox_cuda_encoder *e = s->enc;
-    const bool pdl = e->pdl;
-    const int pos0 = s->pos;
+    const bool pdl = e->pdl && evs == nullptr;
+    int ei = 0;
+#define VC_EV_BEGIN() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
+#define VC_EV_END() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
     const size_t ring_layer = (size_t)s->cap * kEncQkv;
     for (int l = 0; l < e->n_layers; l++) {
         const EncLayer &L = e->L[l];
+        VC_EV_BEGIN();
         VC_TRY(launch_rows_to_bf16(s->x, M, kEncDim, kEncDim, L.attn_norm, s->xn16, st, pdl));
+        VC_EV_END();
         TcGemmParams p = {};
         p.M = M;
         p.N = 3 * kEncQkv;
         p.K = kEncDim;
         p.bias = L.bq;
         p.bias2 = L.bv;
-        p.rope = s->rope;
+        p.rope = table ? s->rope : nullptr;
+        p.inv_freq = e->inv_freq;
+        p.pos0_dev = s->pos_dev;
         p.q_out = s->q16;
         p.k_ring = s->k_ring + l * ring_layer;
         p.v_ring = s->v_ring + l * ring_layer;
         p.cap = s->cap;
-        p.pos0 = pos0;
         p.err = s->err;
+        VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_QKV_ENC, p, s->xn16, L.qkv, st, pdl));
+        VC_EV_END();
         EncAttnParams a = {};
         a.q = s->q16;
         a.k_ring = s->k_ring + l * ring_layer;
         a.v_ring = s->v_ring + l * ring_layer;
         a.cap = s->cap;
-        a.pos0 = pos0;
+        a.pos0_dev = s->pos_dev;
         a.M = M;
         a.out = s->att16;
+        VC_EV_BEGIN();
         VC_TRY(launch_enc_attn(a, st, pdl));
+        VC_EV_END();
         p = TcGemmParams{};
         p.M = M;
         p.N = kEncDim;
@@ -1841,8 +1868,12 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, cudaStream_t st) {
         p.ldo = kEncDim;
         p.bias = L.bo;
         p.err = s->err;
+        VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_RESID, p, s->att16, L.wo, st, pdl));
+        VC_EV_END();
+        VC_EV_BEGIN();
         VC_TRY(launch_rows_to_bf16(s->x, M, kEncDim, kEncDim, L.ffn_norm, s->xn16, st, pdl));
+        VC_EV_END();
         p = TcGemmParams{};
         p.M = M;
         p.N = 2 * kEncHidden;
@@ -1850,7 +1881,9 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, cudaStream_t st) {
         p.out_bf16 = s->h16;
         p.ldo_bf16 = kEncHidden;
         p.err = s->err;
+        VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_SWIGLU, p, s->xn16, L.w13, st, pdl));
+        VC_EV_END();
         p = TcGemmParams{};
         p.M = M;
         p.N = kEncDim;
@@ -1859,9 +1892,39 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, cudaStream_t st) {
         p.ldo = kEncDim;
         p.bias = L.b2;
         p.err = s->err;
+        VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_RESID, p, s->h16, L.w2, st, pdl));
+        VC_EV_END();
     }
+    VC_EV_BEGIN();
     VC_TRY(launch_rows_rmsnorm(s->x, M, kEncDim, e->norm, st, pdl));
+    VC_EV_END();
+#undef VC_EV_BEGIN
+#undef VC_EV_END
+    return VOX_CUDA_OK;
+}
+
+// Upload the chunk position, then replay (capturing on first use) the
+// encoder graph for this chunk shape.
+int run_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st) {
+    *s->h_pos = s->pos;
+    VC_TRY(cudaMemcpyAsync(s->pos_dev, s->h_pos, sizeof(int), cudaMemcpyHostToDevice, st));
+    cudaGraphExec_t &g = s->graphs[std::make_pair(M, table ? 1 : 0)];
+    if (!g) {
+        cudaGraph_t graph = nullptr;
+        VC_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue_encoder(s, M, table, st);
+        cudaError_t e = cudaStreamEndCapture(st, &graph);
+        if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        VC_TRY(e);
+        e = cudaGraphInstantiate(&g, graph, 0);
+        cudaGraphDestroy(graph);
+        VC_TRY(e);
+    }
+    VC_TRY(cudaGraphLaunch(g, st));
     return VOX_CUDA_OK;
 }
 
@@ -1900,11 +1963,12 @@ extern "C" int vox_cuda_encoder_full_step(vox_cuda_enc_state *s, float *x, int n
     if (!x) return VOX_CUDA_ERR_ARG;
     DevCtx *c = ctx_for(s->enc->device);
     cudaStream_t st = c->stream;
-    if (rope_freqs) memcpy(s->h_rope, rope_freqs, (size_t)new_len * kEncHeadDim * 4);
-    else host_rope_rows(s->pos, new_len, kEncHeadDim, s->h_rope);
-    VC_TRY(cudaMemcpyAsync(s->rope, s->h_rope, (size_t)new_len * kEncHeadDim * 4, cudaMemcpyHostToDevice, st));
+    if (rope_freqs) {
+        memcpy(s->h_rope, rope_freqs, (size_t)new_len * kEncHeadDim * 4);
+        VC_TRY(cudaMemcpyAsync(s->rope, s->h_rope, (size_t)new_len * kEncHeadDim * 4, cudaMemcpyHostToDevice, st));
+    }
     VC_TRY(cudaMemcpyAsync(s->x, x, (size_t)new_len * kEncDim * 4, cudaMemcpyHostToDevice, st));
-    if ((rc = enqueue_encoder(s, new_len, st))) return rc;
+    if ((rc = run_encoder(s, new_len, rope_freqs != nullptr, st))) return rc;
     VC_TRY(cudaMemcpyAsync(x, s->x, (size_t)new_len * kEncDim * 4, cudaMemcpyDeviceToHost, st));
     if ((rc = enc_err_check(s, st))) return rc;
     s->pos += new_len;
@@ -1917,12 +1981,10 @@ extern "C" int vox_cuda_encoder_step_dev(vox_cuda_enc_state *s, float *x_dev, in
     if (!x_dev) return VOX_CUDA_ERR_ARG;
     DevCtx *c = ctx_for(s->enc->device);
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
-    host_rope_rows(s->pos, new_len, kEncHeadDim, s->h_rope);
-    VC_TRY(cudaMemcpyAsync(s->rope, s->h_rope, (size_t)new_len * kEncHeadDim * 4, cudaMemcpyHostToDevice, st));
     VC_TRY(cudaMemcpyAsync(s->x, x_dev, (size_t)new_len * kEncDim * 4, cudaMemcpyDeviceToDevice, st));
-    if ((rc = enqueue_encoder(s, new_len, st))) return rc;
+    if ((rc = run_encoder(s, new_len, false, st))) return rc;
     VC_TRY(cudaMemcpyAsync(x_dev, s->x, (size_t)new_len * kEncDim * 4, cudaMemcpyDeviceToDevice, st));
-    if ((rc = enc_err_check(s, st))) return rc;   // also keeps h_rope stable until the copy ran
+    if ((rc = enc_err_check(s, st))) return rc;   // also keeps h_pos stable until the copy ran
     s->pos += new_len;
     return VOX_CUDA_OK;
 }
@@ -1960,4 +2022,54 @@ extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc,
     VC_TRY(launch_tc_gemm(TC_STORE, p, s->mid16, e->adapter1, st, false));
     VC_TRY(cudaMemcpyAsync(out, s->aout, (size_t)rows * kDecDim * 4, cudaMemcpyDeviceToHost, st));
     return enc_err_check(s, st);
+}
+
+extern "C" int vox_cuda_enc_state_set_position(vox_cuda_enc_state *s, int logical_pos) {
+    if (!s || logical_pos < 0) {
+        set_error("enc_state_set_position: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    s->pos = logical_pos;
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_encoder_profile(vox_cuda_enc_state *s, const float *x_dev, int new_len, int iters,
+                                        float *ms) {
+    int rc = enc_check(s, new_len);
+    if (rc) return rc;
+    if (!x_dev || !ms || iters <= 0) return VOX_CUDA_ERR_ARG;
+    DevCtx *c = ctx_for(s->enc->device);
+    cudaStream_t st = c->stream;
+    const int n_launch = 7 * s->enc->n_layers + 1;
+    std::vector<cudaEvent_t> evs(2 * n_launch);
+    for (auto &e : evs)
+        if (cudaEventCreate(&e) != cudaSuccess) return VOX_CUDA_ERR_CUDA;
+    double acc[VOX_CUDA_EPROF_PHASES] = {0};
+    static const int phase_of[7] = {VOX_CUDA_EPROF_NORM, VOX_CUDA_EPROF_QKV, VOX_CUDA_EPROF_ATTN,
+                                    VOX_CUDA_EPROF_WO, VOX_CUDA_EPROF_NORM, VOX_CUDA_EPROF_W13,
+                                    VOX_CUDA_EPROF_W2};
+    for (int it = 0; it < iters && rc == VOX_CUDA_OK; it++) {
+        *s->h_pos = s->pos;
+        if (cudaMemcpyAsync(s->pos_dev, s->h_pos, sizeof(int), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(s->x, x_dev, (size_t)new_len * kEncDim * 4, cudaMemcpyDeviceToDevice, st) !=
+                cudaSuccess) {
+            rc = VOX_CUDA_ERR_CUDA;
+            break;
+        }
+        rc = enqueue_encoder(s, new_len, false, st, evs.data());
+        if (rc) break;
+        if (cudaStreamSynchronize(st) != cudaSuccess) {
+            rc = VOX_CUDA_ERR_CUDA;
+            break;
+        }
+        for (int i = 0; i < n_launch; i++) {
+            float t = 0.f;
+            cudaEventElapsedTime(&t, evs[2 * i], evs[2 * i + 1]);
+            acc[(i == n_launch - 1) ? VOX_CUDA_EPROF_NORM : phase_of[i % 7]] += t;
+        }
+    }
+    for (auto &e : evs) cudaEventDestroy(e);
+    if (rc) return rc;
+    for (int i = 0; i < VOX_CUDA_EPROF_PHASES; i++) ms[i] = (float)(acc[i] / iters);
+    return VOX_CUDA_OK;
 }

@@ -21,6 +21,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "voxtral_cuda.h")
 DEC_DIM, Q_DIM, KV_DIM, DEC_HIDDEN = 3072, 4096, 1024, 9216
 MAX_LAYERS = 26
 PROF_PHASES = ("qkv", "attn", "wo", "w13", "w2", "lm_head")
+ENC_PROF_PHASES = ("norm", "qkv", "attn", "wo", "w13", "w2")
 
 OK, ERR_UNAVAILABLE, ERR_ARG, ERR_OOM, ERR_CUDA, ERR_CAPACITY = 0, -1, -2, -3, -4, -5
 
@@ -111,6 +112,8 @@ def lib():
         "vox_cuda_enc_state_position": ([C.c_void_p], C.c_int),
         "vox_cuda_encoder_full_step": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
         "vox_cuda_encoder_step_dev": ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p], C.c_int),
+        "vox_cuda_enc_state_set_position": ([C.c_void_p, C.c_int], C.c_int),
+        "vox_cuda_encoder_profile": ([C.c_void_p, C.c_void_p, C.c_int, C.c_int, _fp], C.c_int),
         "vox_cuda_adapter_forward": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
         "vox_cuda_attention_decode_dev": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                            C.c_void_p, C.c_void_p], C.c_int),
@@ -348,6 +351,17 @@ class EncState:
 
     def reset(self):
         check(lib().vox_cuda_enc_state_reset(self.h), "enc_state_reset")
+
+    def set_position(self, pos):
+        check(lib().vox_cuda_enc_state_set_position(self.h, pos), "enc_state_set_position")
+
+    def step_dev(self, x_dev, n, stream=None):
+        check(lib().vox_cuda_encoder_step_dev(self.h, x_dev, n, stream), "encoder_step_dev")
+
+    def profile(self, x_dev, n, iters=3):
+        ms = np.zeros(len(ENC_PROF_PHASES), np.float32)
+        check(lib().vox_cuda_encoder_profile(self.h, x_dev, n, iters, _f(ms)), "encoder_profile")
+        return dict(zip(ENC_PROF_PHASES, ms.tolist()))
 
     def free(self):
         if self.h:
