@@ -279,7 +279,7 @@ def build_device_encoder(V, torch, seed=1):
     return enc
 
 
-def encoder_bench(V, torch, steps):
+def encoder_bench(V, torch, steps, only_rows=0):
     """Encoder chunk throughput: 32 layers at M = 100,
     500, 1500 rows (2, 10, 30 s of audio at 50 Hz) with a full 750-row window
     of earlier context, plus the per-phase profile at M = 1500."""
@@ -290,7 +290,7 @@ def encoder_bench(V, torch, steps):
     gen = torch.Generator(device="cuda")
     gen.manual_seed(77)
     x0 = torch.randn((1500, ENC_D), generator=gen, device="cuda", dtype=torch.float32)
-    for M in (100, 500, 1500):
+    for M in ((only_rows,) if only_rows else (100, 500, 1500)):
         n = max(3, steps // (M // 100 + 1))
         x = torch.empty((M, ENC_D), dtype=torch.float32, device="cuda")
         for _ in range(2):
@@ -308,6 +308,10 @@ def encoder_bench(V, torch, steps):
         ms = e0.elapsed_time(e1) / n
         out["ms_per_chunk"][f"M{M}"] = ms
         out["audio_s_per_s"][f"M{M}"] = (M / 50.0) / (ms / 1000.0)
+    if only_rows and only_rows != 1500:
+        st.free()
+        enc.free()
+        return out
     st.set_position(750)
     x = x0[:1500].contiguous()
     prof = st.profile(x.data_ptr(), 1500, iters=3)
@@ -347,6 +351,14 @@ def our_arm(args):
                                 device_id=torch.device("cuda", local))
     import voxcuda as V
     V.init(local)
+    if args.no_decode:   # encoder only (profiling captures)
+        res = encoder_bench(V, torch, args.steps, args.enc_rows)
+        if rank == 0:
+            print(json.dumps({"encoder": res}), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     S = args.streams
     dec = build_device_decoder(V, torch, layers=args.layers, vocab=args.vocab)
     pos = positions(S)
@@ -422,7 +434,7 @@ def our_arm(args):
     for st in states:
         st.free()
     dec.free()
-    enc_res = None if args.no_encoder else encoder_bench(V, torch, args.steps)
+    enc_res = None if args.no_encoder else encoder_bench(V, torch, args.steps, args.enc_rows)
 
     line = None
     if rank == 0:
@@ -472,6 +484,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder", action="store_true")
+    # encoder-only / single chunk size, for small ncu captures
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--enc-rows", type=int, default=0)
     # reduced model, for small ncu captures only (the headline uses the full model)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--vocab", type=int, default=VOCAB)
