@@ -65,6 +65,49 @@ def test_encoder_chunks_match_reference(gpu_enc):
     st.free()
 
 
+@pytest.mark.parametrize("pair", ["0", "1"])
+def test_encoder_epilogue_paths_agree(pair, monkeypatch):
+    """The TMA-store epilogue (staged tiles, TMA reduce-add for the residual)
+    and the direct-store epilogue compute the same values in the same order:
+    outputs agree bit for bit, also across the ring's wrap and ragged tails."""
+    monkeypatch.setenv("VOX_CUDA_TC_PAIR", pair)
+    ew = B.EncoderWeights(seed=7, n_layers=3, distinct=3, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    outs = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("VOX_CUDA_TC_TMA_OUT", mode)
+        st = e.state(max_chunk=256)
+        ys = []
+        for i, n in enumerate([64, 200, 3, 250, 130, 250, 256, 77]):   # wraps the 1006-slot ring
+            ys.append(st.step(B.normal_f32((n, B.ENC_DIM), 950 + i)))
+        outs[mode] = ys
+        st.free()
+    e.free()
+    for a, b in zip(outs["1"], outs["0"]):
+        assert np.isfinite(a).all()
+        assert np.array_equal(a, b)
+
+
+def test_encoder_host_rope_table_matches_device_table():
+    """vox_cuda_encoder_full_step with the host's RoPE table (the reference
+    API passes rope_freqs) and with the table computed on the device.  The two
+    tables differ in the last ulp of some angles, which moves a few fp16 / bf16
+    roundings downstream (~5e-4 rel-L2); a wrongly laid out table is O(1) off."""
+    ew = B.EncoderWeights(seed=8, n_layers=2, distinct=2, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    sa, sb = e.state(max_chunk=256), e.state(max_chunk=256)
+    pos = 0
+    for i, n in enumerate([100, 256, 37, 250, 200]):
+        x = B.normal_f32((n, B.ENC_DIM), 970 + i)
+        ya = sa.step(x, rope=B.rope_freqs(np.arange(pos, pos + n), B.ENC_HEAD_DIM))
+        yb = sb.step(x)
+        pos += n
+        assert B.rel_l2(ya, yb) < 2e-3, (i, B.rel_l2(ya, yb))
+    sa.free()
+    sb.free()
+    e.free()
+
+
 def test_encoder_matches_oracle_small_model():
     ew = B.EncoderWeights(seed=5, n_layers=3, distinct=3, norm_noise=0.1)
     e = make_gpu_encoder(ew)

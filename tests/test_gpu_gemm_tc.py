@@ -56,6 +56,28 @@ def test_tc_gemm_exact_inputs(M, N, K):
     assert B.rel_l2(C, ref) < 1e-5
 
 
+# (VOX_CUDA_TC_PAIR, VOX_CUDA_TC_BN, VOX_CUDA_TC_TMA_OUT): single-CTA tiles of each
+# width and CTA-pair tiles, with the TMA-store and the direct-store epilogue
+KERNEL_MODES = [("0", "64", "1"), ("0", "128", "1"), ("0", "256", "1"), ("1", "128", "1"), ("1", "256", "1"),
+                ("0", "256", "0"), ("1", "256", "0")]
+
+
+@pytest.mark.parametrize("mode", KERNEL_MODES, ids=[f"pair{p}-bn{b}-tma{t}" for p, b, t in KERNEL_MODES])
+@pytest.mark.parametrize("M,N,K", [(1500, 10240, 1280), (300, 1280, 5120), (129, 64, 64), (257, 200, 72)],
+                         ids=["w13", "w2", "tiny", "ragged"])
+def test_tc_gemm_kernel_variants(M, N, K, mode, monkeypatch):
+    monkeypatch.setenv("VOX_CUDA_TC_PAIR", mode[0])
+    monkeypatch.setenv("VOX_CUDA_TC_BN", mode[1])
+    monkeypatch.setenv("VOX_CUDA_TC_TMA_OUT", mode[2])
+    A = B.normal_bf16((M, K), 1100 + M, std=1.0)
+    W = B.normal_bf16((N, K), 2100 + N + K)
+    bias = B.normal_f32(N, 3100 + N, 0.02)
+    C = run_gemm(A, W, bias)
+    ref = B.bf16_to_f32(A).astype(np.float64) @ B.bf16_to_f32(W).astype(np.float64).T + bias
+    assert np.isfinite(C).all()
+    assert B.rel_l2(C, ref) < 1e-5
+
+
 @pytest.mark.parametrize("case", [c for c in G.LINEAR_CASES if c[1] > 8], ids=[c[0] for c in G.LINEAR_CASES if c[1] > 8])
 def test_sgemm_tensor_core_path_matches_reference(case):
     g = load_golden("linear")

@@ -266,6 +266,44 @@ rows_rmsnorm_kernel(float *x, int M, int K, const float *w) {
     for (int i = lane; i < K; i += 32) xr[i] = xr[i] * inv * w[i];
 }
 
+// Per-chunk RoPE planes, once for all layers: tab[d][row] = cos and
+// tab[32 + d][row] = sin of (pos0 + row) * inv_freq[d], the same angles and
+// sincosf the q|k epilogue would otherwise evaluate per pair and per layer
+// (vox_compute_rope_freqs, voxtral_kernels.c:488-503, on the device); or the
+// host's table src[row][32] (cos, sin) transposed.
+__global__ void __launch_bounds__(256)
+enc_rope_table_kernel(float *tab, int ld, int M, const float *src, const int *pos0_dev, const float *inv_freq) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;   // row * 32 + d
+    if (i >= M * (kEncHeadDim / 2)) return;
+    const int row = i / (kEncHeadDim / 2), d = i % (kEncHeadDim / 2);
+    float sn, cs;
+    if (src) {
+        cs = src[2 * i];
+        sn = src[2 * i + 1];
+    } else {
+        sincosf((float)(*pos0_dev + row) * inv_freq[d], &sn, &cs);
+    }
+    tab[(size_t)d * ld + row] = cs;
+    tab[(size_t)(kEncHeadDim / 2 + d) * ld + row] = sn;
+}
+
+cudaError_t launch_enc_rope_table(float *tab, int ld, int M, const float *src, const int *pos0_dev,
+                                  const float *inv_freq, cudaStream_t st, bool pdl) {
+    const int n = M * (kEncHeadDim / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((n + 255) / 256);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, enc_rope_table_kernel, tab, ld, M, src, pos0_dev, inv_freq);
+}
+
 cudaError_t launch_rows_rmsnorm(float *x, int M, int K, const float *w, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((M + 7) / 8);

@@ -2,16 +2,22 @@
 // and M > 8 matmuls: C[M, N] = A[M, K] . W[N, K]^T with bf16 A and W (both
 // K-major, row-major as stored), fp32 accumulation in TMEM, fused epilogues.
 //
-// One CTA computes one 128 x BN output tile:
+// Persistent: one CTA per SM walks the 128 x BN output tiles t = blockIdx.x,
+// blockIdx.x + gridDim.x, ... (row tiles fastest, so the CTAs of one wave
+// share W tiles in L2).
 //   warp 0 (one thread)  TMA producer: 128x64 A and BNx64 W tiles, 128-byte
-//                        swizzle, into a STAGES-deep shared-memory ring
-//   warp 1 (one thread)  tcgen05.mma issuer (M=128, N=BN, K=16, cta_group::1);
-//                        tcgen05.commit releases ring stages and finally
-//                        signals the epilogue; warp 1 also owns the TMEM
-//                        allocation (BN fp32 columns x 128 lanes)
-//   warps 2-5            epilogue: tcgen05.ld of their 32-lane quarter of the
-//                        accumulator, bias / residual / activation / RoPE,
-//                        stores to global memory
+//                        swizzle, into a STAGES-deep shared-memory ring that
+//                        runs on across tiles
+//   warp 1 (one thread)  tcgen05.mma issuer (M=128, N=BN, K=16, cta_group::1)
+//                        into one of two TMEM accumulators (2 x BN fp32
+//                        columns); tcgen05.commit releases ring stages and
+//                        hands a finished accumulator to the epilogue
+//   warps 2-9            epilogue, two warps per 32-lane TMEM quarter (warp
+//                        id mod 4 selects the quarter), each taking half of
+//                        the columns: tcgen05.ld (32 columns per load), bias /
+//                        residual / activation / RoPE, 16-byte stores; then
+//                        the accumulator goes back to the issuer, so the
+//                        epilogue of tile i overlaps the MMAs of tile i + 1
 // Every mbarrier wait is bounded (2 s of %globaltimer); on expiry the CTA sets
 // the launch's error word and exits after a grace period for in-flight copies.
 #include "vc_common.cuh"
@@ -21,7 +27,10 @@
 #include <cuda_fp16.h>
 #include <math.h>
 #include <stdlib.h>
+#include <string.h>
 
+#include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 
@@ -29,9 +38,12 @@ namespace vc {
 
 using namespace tc;
 
-constexpr int kTcThreads = 192;
+constexpr int kEpiWarps = 8;                 // two per TMEM lane quarter, each half the columns
+constexpr int kTcThreads = 64 + 32 * kEpiWarps;
 constexpr int kBM = 128;
 constexpr int kBK = 64;                     // one 128-byte swizzle row of bf16
+constexpr int kEpiCols = 32;                // accumulator columns per tcgen05.ld
+constexpr int kStageBytes = 32 * 128;       // a warp's staging tile: 32 rows x 128 bytes
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 
 template <int BN>
@@ -39,7 +51,9 @@ struct TcCfg {
     static constexpr int kStages = (BN >= 256) ? 4 : 6;
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
-    static constexpr int kSmem = kStages * (kABytes + kBBytes) + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int kTmemCols = 2 * BN;    // two accumulators
+    static constexpr int kSmem =
+        kStages * (kABytes + kBBytes) + kEpiWarps * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ float gelu_tanh(float v) {
@@ -49,23 +63,305 @@ __device__ __forceinline__ float gelu_tanh(float v) {
     return 0.5f * v * (1.0f + tanhf(inner));
 }
 
+// SiLU with the fast exp / divide intrinsics: a few ulp of fp32, far below the
+// bf16 rounding of the product that follows.  g -> -inf gives -0.
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    return bf16_bits_rn(a) | (bf16_bits_rn(b) << 16);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__device__ __forceinline__ void st16(void *dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    *reinterpret_cast<uint4 *>(dst) = make_uint4(a, b, c, d);
+}
+
+// Per-thread facts of one tile row, fixed across its column chunks.
+struct EpiRow {
+    int row;        // output row (this thread's TMEM lane)
+    int pos;        // TC_QKV_ENC: logical position of the row
+    size_t slot;    // TC_QKV_ENC: ring slot of the row
+};
+
+// Encoder q|k RoPE of one row's 16 pairs (v[2i], v[2i+1]) at pair indices
+// d0..d0+15 of a head (vox_apply_rope, voxtral_kernels.c:505-526; cos/sin as
+// in :488-503).  The table holds a cos plane and a sin plane, [32][rope_ld]
+// each, indexed by row, so a warp's 32 rows read 32 consecutive floats; all
+// 32 loads are issued before the first use.
+__device__ __forceinline__ void enc_rope_chunk(const TcGemmParams &p, const EpiRow &er, int d0, float (&v)[kEpiCols]) {
+    float cs[kEpiCols / 2], sn[kEpiCols / 2];
+    if (p.rope) {
+        const float *cp = p.rope + (size_t)d0 * p.rope_ld + er.row;
+        const float *sp = p.rope + (size_t)(kEncHeadDim / 2 + d0) * p.rope_ld + er.row;
+#pragma unroll
+        for (int i = 0; i < kEpiCols / 2; i++) {
+            cs[i] = __ldg(cp + (size_t)i * p.rope_ld);
+            sn[i] = __ldg(sp + (size_t)i * p.rope_ld);
+        }
+    } else {   // angle = pos * inv_freq exactly as the host formula
+#pragma unroll
+        for (int i = 0; i < kEpiCols / 2; i++) sincosf((float)er.pos * p.inv_freq[d0 + i], &sn[i], &cs[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kEpiCols / 2; i++) {
+        const float a = v[2 * i], b = v[2 * i + 1];
+        v[2 * i] = __fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i]));
+        v[2 * i + 1] = __fadd_rn(__fmul_rn(a, sn[i]), __fmul_rn(b, cs[i]));
+    }
+}
+
+// v[j] += bias[col0 + j] for the columns inside N
+__device__ __forceinline__ void add_bias(float (&v)[kEpiCols], const float *bias, int col0, int N) {
+    if (!bias) return;
+    if (col0 + kEpiCols <= N) {
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 4) {
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + col0 + j));
+            v[j] += b.x, v[j + 1] += b.y, v[j + 2] += b.z, v[j + 3] += b.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j++)
+            if (col0 + j < N) v[j] += __ldg(bias + col0 + j);
+    }
+}
+
+// The q|k|v region of encoder column col0 (32-column chunks never straddle two):
+// [0,2048) q (+bias, RoPE), [2048,4096) k (RoPE), [4096,6144) v (+bias)
+// (voxtral_encoder.c:542-559).  Applies bias and RoPE to v in place.
+__device__ __forceinline__ int qkv_apply(const TcGemmParams &p, const EpiRow &er, float (&v)[kEpiCols], int col0) {
+    if (col0 < 2 * kEncQkv) {
+        if (col0 < kEncQkv) add_bias(v, p.bias, col0, kEncQkv);
+        enc_rope_chunk(p, er, (col0 & (kEncHeadDim - 1)) >> 1, v);
+        return col0 < kEncQkv ? 0 : 1;
+    }
+    add_bias(v, p.bias2, col0 - 2 * kEncQkv, kEncQkv);
+    return 2;
+}
+
+// Direct stores of one row's chunk [col0, col0 + 32), all inside N, 16-byte
+// aligned destinations (p.vec).  TC_QKV_ENC: bias / RoPE already applied.
+template <int EPI>
+__device__ __forceinline__ void epi_vec(const TcGemmParams &p, const EpiRow &er, float (&v)[kEpiCols], int col0,
+                                        int region) {
+    const int row = er.row;
+    if constexpr (EPI == TC_STORE || EPI == TC_RESID) {
+        add_bias(v, p.bias, col0, p.N);
+        float *o = p.out + (size_t)row * p.ldo + col0;
+        if constexpr (EPI == TC_RESID) {
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j += 4) {
+                const float4 r = *reinterpret_cast<const float4 *>(o + j);
+                v[j] += r.x, v[j + 1] += r.y, v[j + 2] += r.z, v[j + 3] += r.w;
+            }
+        }
+        if (p.act == 1) {
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j++) v[j] = gelu_tanh(v[j]);
+        }
+        if (p.out_bf16) {
+            uint16_t *ob = p.out_bf16 + (size_t)row * p.ldo_bf16 + col0;
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j += 8)
+                st16(ob + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                     pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j += 4)
+                *reinterpret_cast<float4 *>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+    } else if constexpr (EPI == TC_SWIGLU) {
+        // columns (2i, 2i+1) = (gate_i, up_i) -> h_i = silu(g) * u
+        // (voxtral_kernels.c:369-374, then :34-36), bf16 for the next GEMM
+        uint32_t h[kEpiCols / 4];
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 4)
+            h[j >> 2] = pack_bf16x2(silu_fast(v[j]) * v[j + 1], silu_fast(v[j + 2]) * v[j + 3]);
+        uint16_t *o = p.out_bf16 + (size_t)row * p.ldo_bf16 + (col0 >> 1);
+#pragma unroll
+        for (int j = 0; j < kEpiCols / 4; j += 4) st16(o + 2 * j, h[j], h[j + 1], h[j + 2], h[j + 3]);
+    } else if constexpr (EPI == TC_QKV_ENC) {
+        uint16_t *dst = region == 0   ? p.q_out + (size_t)row * kEncQkv + col0
+                        : region == 1 ? p.k_ring + er.slot * kEncQkv + (col0 - kEncQkv)
+                                      : p.v_ring + er.slot * kEncQkv + (col0 - 2 * kEncQkv);
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 8)
+            st16(dst + j, pack_half2(v[j], v[j + 1]), pack_half2(v[j + 2], v[j + 3]), pack_half2(v[j + 4], v[j + 5]),
+                 pack_half2(v[j + 6], v[j + 7]));
+    }
+}
+
+// Element-wise direct stores for a chunk that reaches past N or whose
+// destinations are not 16-byte aligned.  TC_QKV_ENC: bias / RoPE applied.
+template <int EPI>
+__device__ __forceinline__ void epi_scalar(const TcGemmParams &p, const EpiRow &er, float (&v)[kEpiCols], int col0,
+                                           int region) {
+    const int row = er.row;
+    if constexpr (EPI == TC_STORE || EPI == TC_RESID) {
+        add_bias(v, p.bias, col0, p.N);
+        float *o = p.out + (size_t)row * p.ldo + col0;
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j++) {
+            if (col0 + j >= p.N) break;
+            float x = v[j];
+            if constexpr (EPI == TC_RESID) x += o[j];
+            if (p.act == 1) x = gelu_tanh(x);
+            if (p.out_bf16) p.out_bf16[(size_t)row * p.ldo_bf16 + col0 + j] = (uint16_t)bf16_bits_rn(x);
+            else o[j] = x;
+        }
+    } else if constexpr (EPI == TC_SWIGLU) {
+        uint16_t *o = p.out_bf16 + (size_t)row * p.ldo_bf16 + (col0 >> 1);
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 2) {
+            if (col0 + j + 1 >= p.N) break;
+            o[j >> 1] = (uint16_t)bf16_bits_rn(silu_fast(v[j]) * v[j + 1]);
+        }
+    } else if constexpr (EPI == TC_QKV_ENC) {
+        uint16_t *dst = region == 0   ? p.q_out + (size_t)row * kEncQkv + col0
+                        : region == 1 ? p.k_ring + er.slot * kEncQkv + (col0 - kEncQkv)
+                                      : p.v_ring + er.slot * kEncQkv + (col0 - 2 * kEncQkv);
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 2)
+            *reinterpret_cast<uint32_t *>(dst + j) = pack_half2(v[j], v[j + 1]);
+    }
+}
+
+// Tensor maps of the TMA-store epilogue (p.tma_out): o = the output (q for
+// TC_QKV_ENC), k / v = this layer's rings.
+struct EpiMaps {
+    const CUtensorMap *o, *k, *v;
+};
+
+// TMA-store epilogue of one warp's 32 rows x 32 accumulator columns: stage
+// the converted chunk in shared memory (`stg`, 4 KB, swizzled to the map's
+// span) and let lane 0 store it, or add it (TC_RESID).  Rows / columns past
+// the map's extent are not written.  The ring rows of TC_QKV_ENC are written
+// this way only when the warp's 32 rows are all valid and do not wrap.
+template <int EPI>
+__device__ __forceinline__ void epi_tma(const TcGemmParams &p, const EpiMaps &mp, const EpiRow &er,
+                                        float (&v)[kEpiCols], int row0, int col0, int lane, unsigned char *stg) {
+    int region = 0;
+    if constexpr (EPI == TC_QKV_ENC) {
+        region = qkv_apply(p, er, v, col0);
+        if (region != 0) {
+            const int slot0 = __shfl_sync(0xffffffffu, (int)er.slot, 0);
+            if (row0 + 32 > p.M || slot0 + 32 > p.cap) {   // tail rows or wrap: direct stores
+                if (er.row < p.M) epi_vec<EPI>(p, er, v, col0, region);
+                return;
+            }
+        }
+    } else {
+        add_bias(v, p.bias, col0, p.N);
+        if constexpr (EPI == TC_STORE) {
+            if (p.act == 1) {
+#pragma unroll
+                for (int j = 0; j < kEpiCols; j++) v[j] = gelu_tanh(v[j]);
+            }
+        }
+    }
+    if (lane == 0) bulk_wait_read_all();   // the previous store has read the staging tile
+    __syncwarp();
+    if constexpr (EPI == TC_SWIGLU) {
+        uint32_t h[kEpiCols / 4];
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 4)
+            h[j >> 2] = pack_bf16x2(silu_fast(v[j]) * v[j + 1], silu_fast(v[j + 2]) * v[j + 3]);
+        swz_put<32>(stg, lane, 0, make_uint4(h[0], h[1], h[2], h[3]));
+        swz_put<32>(stg, lane, 1, make_uint4(h[4], h[5], h[6], h[7]));
+    } else if (EPI == TC_QKV_ENC || p.out_bf16) {   // 16-bit outputs, 64-byte rows
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const float *w = v + 8 * c;
+            const uint4 u = EPI == TC_QKV_ENC
+                                ? make_uint4(pack_half2(w[0], w[1]), pack_half2(w[2], w[3]), pack_half2(w[4], w[5]),
+                                             pack_half2(w[6], w[7]))
+                                : make_uint4(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]),
+                                             pack_bf16x2(w[4], w[5]), pack_bf16x2(w[6], w[7]));
+            swz_put<64>(stg, lane, c, u);
+        }
+    } else {   // fp32 outputs, 128-byte rows
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+            swz_put<128>(stg, lane, c,
+                         make_uint4(__float_as_uint(v[4 * c]), __float_as_uint(v[4 * c + 1]),
+                                    __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3])));
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        if constexpr (EPI == TC_SWIGLU) {
+            tma_store_2d(mp.o, stg, col0 >> 1, row0);
+        } else if constexpr (EPI == TC_RESID) {
+            tma_reduce_add_2d(mp.o, stg, col0, row0);
+        } else if constexpr (EPI == TC_QKV_ENC) {
+            if (region == 0) tma_store_2d(mp.o, stg, col0, row0);
+            else tma_store_2d(region == 1 ? mp.k : mp.v, stg, col0 - region * kEncQkv, (int)er.slot);
+        } else {
+            tma_store_2d(mp.o, stg, col0, row0);
+        }
+        bulk_commit();
+    }
+}
+
+// The epilogue of one accumulator for one epilogue warp: this thread's row
+// (its TMEM lane) and the warp's half of the BN columns from n0, 32 columns
+// per tcgen05.ld.  row0 = the warp's first row.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const TcGemmParams &p, const EpiMaps &mp, uint32_t tbase, int row0,
+                                              int n0, int half, int lane, unsigned char *stg) {
+    static_assert(BN % (2 * kEpiCols) == 0, "each epilogue warp takes whole 32-column chunks");
+    EpiRow er;
+    er.row = row0 + lane;
+    er.pos = 0;
+    er.slot = 0;
+    if constexpr (EPI == TC_QKV_ENC) {
+        er.pos = (p.pos0_dev ? *p.pos0_dev : p.pos0) + er.row;
+        er.slot = (size_t)(er.pos % p.cap);
+    }
+    const bool rv = er.row < p.M;
+#pragma unroll 1
+    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
+        float v[kEpiCols];
+        tmem_ld32(tbase + (uint32_t)c, v);   // warp-collective: before any branch
+        const int col0 = n0 + c;
+        if (col0 >= p.N) continue;           // warp-uniform
+        if (p.tma_out) {
+            epi_tma<EPI>(p, mp, er, v, row0, col0, lane, stg);
+            continue;
+        }
+        if (!rv) continue;
+        int region = 0;
+        if constexpr (EPI == TC_QKV_ENC) region = qkv_apply(p, er, v, col0);
+        if (p.vec && col0 + kEpiCols <= p.N) epi_vec<EPI>(p, er, v, col0, region);
+        else epi_scalar<EPI>(p, er, v, col0, region);
+    }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const TcGemmParams p) {
+               const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, const TcGemmParams p) {
     using Cfg = TcCfg<BN>;
     constexpr int S = Cfg::kStages;
     extern __shared__ unsigned char smem_raw[];
     unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     unsigned char *sA = smem;
     unsigned char *sB = smem + S * Cfg::kABytes;
-    uint64_t *full = reinterpret_cast<uint64_t *>(sB + S * Cfg::kBBytes);
+    unsigned char *sStage = sB + S * Cfg::kBBytes;   // [kEpiWarps][kStageBytes] epilogue staging
+    uint64_t *full = reinterpret_cast<uint64_t *>(sStage + kEpiWarps * kStageBytes);
     uint64_t *empty = full + S;
-    uint64_t *tfull = empty + S;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfull + 1);
+    uint64_t *tfull = empty + S;     // [2] accumulator b holds a finished tile
+    uint64_t *tempty = tfull + 2;    // [2] accumulator b was drained by the epilogue
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
+    const int MT = (p.M + kBM - 1) / kBM;
+    const int tiles = MT * ((p.N + BN - 1) / BN);
     const int KB = (p.K + kBK - 1) / kBK;
     const uint64_t deadline = globaltimer() + kTcWaitNs;
     bool ok = true;
@@ -75,13 +371,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(tfull, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], kEpiWarps);    // one arrival per epilogue warp
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
+        if (p.tma_out) prefetch_tensormap(&tmO);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, BN);
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -94,125 +394,81 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (warp == 0) {
         if (lane == 0) {
-            uint64_t pol_a, pol_b;
-            asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_a));
-            asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_b));
-            for (int kb = 0; kb < KB; kb++) {
-                const int s = kb % S;
-                if (kb >= S && !mbar_wait(&empty[s], (uint32_t)((kb / S) + 1) & 1u, deadline)) {
-                    ok = false;
-                    break;
+            // A and W are both re-read by other tiles (A by every column tile,
+            // W by every row tile); keep both in L2.
+            uint64_t pol;
+            asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+            uint32_t it = 0;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int m0 = (t % MT) * kBM, n0 = (t / MT) * BN;
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % S;
+                    if (it >= (uint32_t)S && !mbar_wait(&empty[s], ((it / S) + 1) & 1u, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], Cfg::kABytes + Cfg::kBBytes);
+                    tma_load_2d(sA + s * Cfg::kABytes, &tmA, kb * kBK, m0, &full[s], pol);
+                    tma_load_2d(sB + s * Cfg::kBBytes, &tmB, kb * kBK, n0, &full[s], pol);
                 }
-                mbar_expect_tx(&full[s], Cfg::kABytes + Cfg::kBBytes);
-                tma_load_2d(sA + s * Cfg::kABytes, &tmA, kb * kBK, m0, &full[s], pol_a);
-                tma_load_2d(sB + s * Cfg::kBBytes, &tmB, kb * kBK, n0, &full[s], pol_b);
             }
+            // tail: every stage's last release has arrived before the CTA can exit
+            for (uint32_t j = it > (uint32_t)S ? it - S : 0; j < it && ok; j++)
+                ok = mbar_wait(&empty[j % S], (j / S) & 1u, deadline);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16(kBM, BN);
-            for (int kb = 0; kb < KB; kb++) {
-                const int s = kb % S;
-                if (!mbar_wait(&full[s], (uint32_t)(kb / S) & 1u, deadline)) {
+            uint32_t it = 0, lt = 0;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, lt++) {
+                const uint32_t b = lt & 1u;
+                if (lt >= 2 && !mbar_wait(&tempty[b], ((lt >> 1) + 1) & 1u, deadline)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint64_t a0 = smem_desc_sw128(sA + s * Cfg::kABytes);
-                const uint64_t b0 = smem_desc_sw128(sB + s * Cfg::kBBytes);
+                const uint32_t d = tmem + b * BN;
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % S;
+                    if (!mbar_wait(&full[s], (it / S) & 1u, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t a0 = smem_desc_sw128(sA + s * Cfg::kABytes);
+                    const uint64_t b0 = smem_desc_sw128(sB + s * Cfg::kBBytes);
 #pragma unroll
-                for (int k = 0; k < kBK / 16; k++)   // +32 bytes (2 x 16) per K=16 step
-                    tc_mma_bf16(tmem, a0 + 2 * k, b0 + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
-                tc_commit(&empty[s]);
+                    for (int k = 0; k < kBK / 16; k++)   // +32 bytes (2 x 16) per K=16 step
+                        tc_mma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                    tc_commit(&empty[s]);
+                }
+                if (ok) tc_commit(&tfull[b]);
             }
-            if (ok) tc_commit(tfull);
         }
     } else {
         // ---- epilogue: warp quarter q owns TMEM lanes 32q..32q+31 = tile rows ----
-        const bool got = mbar_wait(tfull, 0u, deadline);
-        if (!__all_sync(0xffffffffu, got)) {
-            ok = false;
-        } else {
-            tc_fence_after();
-            const int q = warp & 3;
-            const int row = m0 + 32 * q + lane;
-            const bool rv = row < p.M;
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 16) {
-                float v[16];
-                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
-                const int col0 = n0 + c;
-                if (!rv || col0 >= p.N) continue;
-                if constexpr (EPI == TC_STORE || EPI == TC_RESID) {
-                    float *o = p.out + (size_t)row * p.ldo + col0;
-#pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        if (col0 + j >= p.N) break;
-                        float x = v[j];
-                        if (p.bias) x += p.bias[col0 + j];
-                        if constexpr (EPI == TC_RESID) x += o[j];
-                        if (p.act == 1) x = gelu_tanh(x);
-                        if (p.out_bf16) p.out_bf16[(size_t)row * p.ldo_bf16 + col0 + j] = (uint16_t)bf16_bits_rn(x);
-                        else o[j] = x;
-                    }
-                } else if constexpr (EPI == TC_SWIGLU) {
-                    // columns (2i, 2i+1) = (gate_i, up_i) -> h_i = silu(g) * u
-                    // (voxtral_kernels.c:369-374, then :34-36), bf16 for the next GEMM
-                    uint16_t *o = p.out_bf16 + (size_t)row * p.ldo_bf16 + (col0 >> 1);
-#pragma unroll
-                    for (int j = 0; j < 16; j += 2) {
-                        const float g = v[j], u = v[j + 1];
-                        const float sg = g / (1.0f + expf(-g));
-                        o[j >> 1] = (uint16_t)bf16_bits_rn(sg * u);
-                    }
-                } else if constexpr (EPI == TC_QKV_ENC) {
-                    // [0,2048): q (+bias, RoPE), [2048,4096): k (RoPE), [4096,6144): v (+bias)
-                    // (voxtral_encoder.c:542-559); k and v go to the ring slot of the row
-                    const int pos = (p.pos0_dev ? *p.pos0_dev : p.pos0) + row;
-                    const size_t slot = (size_t)(pos % p.cap);
-                    const float *cs = p.rope ? p.rope + (size_t)row * kEncHeadDim : nullptr;
-#pragma unroll
-                    for (int j = 0; j < 16; j += 2) {
-                        const int col = col0 + j;
-                        float a = v[j], b = v[j + 1];
-                        if (col < 2 * kEncQkv) {
-                            if (col < kEncQkv && p.bias) {
-                                a += p.bias[col];
-                                b += p.bias[col + 1];
-                            }
-                            const int d = (col & (kEncHeadDim - 1)) >> 1;
-                            float c0, s0;
-                            if (cs) {
-                                c0 = cs[2 * d];
-                                s0 = cs[2 * d + 1];
-                            } else {   // angle = pos * inv_freq exactly as the host formula
-                                sincosf((float)pos * p.inv_freq[d], &s0, &c0);
-                            }
-                            const float oa = __fsub_rn(__fmul_rn(a, c0), __fmul_rn(b, s0));
-                            const float ob = __fadd_rn(__fmul_rn(a, s0), __fmul_rn(b, c0));
-                            if (col < kEncQkv) {
-                                __half2 *qo = reinterpret_cast<__half2 *>(p.q_out + (size_t)row * kEncQkv + col);
-                                static_assert(sizeof(__half2) == 4, "half2");
-                                *qo = __floats2half2_rn(oa, ob);
-                            } else {
-                                __half2 *ko = reinterpret_cast<__half2 *>(p.k_ring + slot * kEncQkv + (col - kEncQkv));
-                                *ko = __floats2half2_rn(oa, ob);
-                            }
-                        } else {
-                            const int cv = col - 2 * kEncQkv;
-                            if (p.bias2) {
-                                a += p.bias2[cv];
-                                b += p.bias2[cv + 1];
-                            }
-                            __half2 *vo = reinterpret_cast<__half2 *>(p.v_ring + slot * kEncQkv + cv);
-                            *vo = __floats2half2_rn(a, b);
-                        }
-                    }
-                }
+        const int q = warp & 3, half = (warp - 2) >> 2;   // TMEM lane quarter, column half
+        const EpiMaps mp = {&tmO, &tmK, &tmV};
+        unsigned char *stg = sStage + (warp - 2) * kStageBytes;
+        uint32_t lt = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, lt++) {
+            const uint32_t b = lt & 1u;
+            const bool got = mbar_wait(&tfull[b], (lt >> 1) & 1u, deadline);
+            if (!__all_sync(0xffffffffu, got)) {
+                ok = false;
+                break;
             }
+            tc_fence_after();
+            const int m0 = (t % MT) * kBM, n0 = (t / MT) * BN;
+            epilogue_tile<BN, EPI>(p, mp, tmem + ((uint32_t)(32 * q) << 16) + b * BN, m0 + 32 * q, n0, half, lane,
+                                   stg);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
         }
     }
 
+    if (warp >= 2 && lane == 0 && p.tma_out) bulk_wait_all();   // epilogue stores complete
     if (!__all_sync(0xffffffffu, ok)) ok = false;
     if (!ok) {
         if (lane == 0) atomicExch(p.err, 1u);
@@ -224,7 +480,176 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+}
+
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs computes a 256 x BN tile with
+// cta_group::2 MMAs (M = 256).  CTA r loads A rows [m0 + 128 r, +128) and W
+// rows [n0 + r BN/2, +BN/2) into its own shared memory; both halves land on
+// rank 0's `full` barrier; rank 0 issues the MMAs, which read A and W from
+// both CTAs and write each CTA's 128 rows x BN columns to that CTA's TMEM.
+// Per SM, a k-block moves (128 + BN/2) x 64 operand elements instead of
+// (128 + BN) x 64, a third less L2 -> shared memory traffic at BN = 256.
+// Both CTAs run the epilogue over their own rows; accumulator releases go to
+// rank 0's `tempty`.  No load is multicast.
+// ---------------------------------------------------------------------------
+template <int BN>
+struct Tc2Cfg {
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = (BN / 2) * kBK * 2;
+    static constexpr int kStages = (196608 / (kABytes + kBBytes)) < 8 ? (196608 / (kABytes + kBBytes)) : 8;
+    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kSmem =
+        kStages * (kABytes + kBBytes) + kEpiWarps * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, const TcGemmParams p) {
+    using Cfg = Tc2Cfg<BN>;
+    constexpr int S = Cfg::kStages;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char *sA = smem;
+    unsigned char *sB = smem + S * Cfg::kABytes;
+    unsigned char *sStage = sB + S * Cfg::kBBytes;   // [kEpiWarps][kStageBytes] epilogue staging
+    uint64_t *full = reinterpret_cast<uint64_t *>(sStage + kEpiWarps * kStageBytes);   // used on rank 0
+    uint64_t *empty = full + S;
+    uint64_t *tfull = empty + S;      // [2]
+    uint64_t *tempty = tfull + 2;     // [2], used on rank 0
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int cl = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+    const int MT = (p.M + 2 * kBM - 1) / (2 * kBM);
+    const int tiles = MT * ((p.N + BN - 1) / BN);
+    const int KB = (p.K + kBK - 1) / kBK;
+    const uint64_t deadline = globaltimer() + kTcWaitNs;
+    bool ok = true;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * kEpiWarps);    // epilogue warps of both CTAs
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+        if (p.tma_out) prefetch_tensormap(&tmO);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    grid_dep_wait();
+    grid_dep_launch();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint64_t pol;
+            asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+            uint32_t it = 0;
+            for (int t = cl; t < tiles && ok; t += ncl) {
+                const int m0 = (t % MT) * 2 * kBM + (int)rank * kBM;
+                const int nb = (t / MT) * BN + (int)rank * (BN / 2);
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % S;
+                    if (it >= (uint32_t)S && !mbar_wait(&empty[s], ((it / S) + 1) & 1u, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    if (rank == 0) mbar_expect_tx(&full[s], 2 * (Cfg::kABytes + Cfg::kBBytes));
+                    const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+                    tma_load_2d_pair(sA + s * Cfg::kABytes, &tmA, kb * kBK, m0, fb, pol);
+                    tma_load_2d_pair(sB + s * Cfg::kBBytes, &tmB, kb * kBK, nb, fb, pol);
+                }
+            }
+            // tail: every stage's last release (committed by rank 0) has arrived
+            for (uint32_t j = it > (uint32_t)S ? it - S : 0; j < it && ok; j++)
+                ok = mbar_wait(&empty[j % S], (j / S) & 1u, deadline);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_bf16(2 * kBM, BN);
+            uint32_t it = 0, lt = 0;
+            for (int t = cl; t < tiles && ok; t += ncl, lt++) {
+                const uint32_t b = lt & 1u;
+                if (lt >= 2 && !mbar_wait(&tempty[b], ((lt >> 1) + 1) & 1u, deadline)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + b * BN;
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % S;
+                    if (!mbar_wait(&full[s], (it / S) & 1u, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t a0 = smem_desc_sw128(sA + s * Cfg::kABytes);
+                    const uint64_t b0 = smem_desc_sw128(sB + s * Cfg::kBBytes);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)
+                        tc_mma_bf16_pair(d, a0 + 2 * k, b0 + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                    tc_commit_pair_both(&empty[s]);
+                }
+                if (!ok) break;
+                tc_commit_pair_both(&tfull[b]);
+            }
+        }
+    } else {
+        const int q = warp & 3, half = (warp - 2) >> 2;   // TMEM lane quarter, column half
+        const EpiMaps mp = {&tmO, &tmK, &tmV};
+        unsigned char *stg = sStage + (warp - 2) * kStageBytes;
+        const uint32_t te0 = mapa_shared(smem_u32(&tempty[0]), 0);
+        const uint32_t te1 = mapa_shared(smem_u32(&tempty[1]), 0);
+        uint32_t lt = 0;
+        for (int t = cl; t < tiles; t += ncl, lt++) {
+            const uint32_t b = lt & 1u;
+            const bool got = mbar_wait(&tfull[b], (lt >> 1) & 1u, deadline);
+            if (!__all_sync(0xffffffffu, got)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int m0 = (t % MT) * 2 * kBM + (int)rank * kBM, n0 = (t / MT) * BN;
+            epilogue_tile<BN, EPI>(p, mp, tmem + ((uint32_t)(32 * q) << 16) + b * BN, m0 + 32 * q, n0, half, lane,
+                                   stg);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(b ? te1 : te0);
+        }
+    }
+
+    if (warp >= 2 && lane == 0 && p.tma_out) bulk_wait_all();   // epilogue stores complete
+    if (!__all_sync(0xffffffffu, ok)) ok = false;
+    if (!ok) {
+        if (lane == 0) atomicExch(p.err, 1u);
+        const uint64_t grace = globaltimer() + 10000000ull;   // let in-flight copies / MMAs land
+        while (globaltimer() < grace) {
+        }
+    }
+    tc_fence_before();
+    cluster_sync_all();   // both CTAs done with TMEM and with each other's barriers
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, Cfg::kTmemCols);
     }
 }
 
@@ -251,32 +676,90 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// bf16 row-major [rows, cols] (cols contiguous), box [box_rows, 64], 128B swizzle
-bool make_map(CUtensorMap *m, const void *ptr, int rows, int cols, int box_rows) {
+// Row-major [rows, cols] tensor (row stride `ld` elements) of `esize`-byte
+// elements, box [box_rows, box_cols], given swizzle.
+bool make_map_2d(CUtensorMap *m, const void *ptr, CUtensorMapDataType dt, int esize, int rows, int cols, int ld,
+                 int box_cols, int box_rows, CUtensorMapSwizzle swz) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * (cuuint64_t)esize};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return fn(m, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// bf16 row-major [rows, cols] operand, box [box_rows, 64], 128B swizzle
+bool make_map(CUtensorMap *m, const void *ptr, int rows, int cols, int box_rows) {
+    return make_map_2d(m, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, cols, kBK, box_rows,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Output maps of the TMA-store epilogue: one warp's 32 x 32 accumulator
+// chunk per box.  Returns false when the epilogue must use direct stores.
+bool make_out_maps(int epi, const TcGemmParams &p, CUtensorMap *mo, CUtensorMap *mk, CUtensorMap *mv) {
+    switch (epi) {
+        case TC_STORE:
+            if (p.out_bf16)
+                return make_map_2d(mo, p.out_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.N, p.ldo_bf16, 32, 32,
+                                   CU_TENSOR_MAP_SWIZZLE_64B);
+            return make_map_2d(mo, p.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.M, p.N, p.ldo, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+        case TC_RESID:   // out += acc + bias as one fp32 add per element, in L2
+            if (p.out_bf16 || p.act != 0) return false;
+            return make_map_2d(mo, p.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.M, p.N, p.ldo, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+        case TC_SWIGLU:
+            return make_map_2d(mo, p.out_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.N / 2, p.ldo_bf16, 16, 32,
+                               CU_TENSOR_MAP_SWIZZLE_32B);
+        case TC_QKV_ENC:
+            if (p.N != 3 * kEncQkv || p.cap < 32) return false;
+            return make_map_2d(mo, p.q_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.M, kEncQkv, kEncQkv, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_64B) &&
+                   make_map_2d(mk, p.k_ring, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.cap, kEncQkv, kEncQkv, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_64B) &&
+                   make_map_2d(mv, p.v_ring, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.cap, kEncQkv, kEncQkv, 32, 32,
+                               CU_TENSOR_MAP_SWIZZLE_64B);
+    }
+    return false;
+}
+
+int device_sms(int dev) {
+    static std::atomic<int> cache[64];
+    if (dev >= 0 && dev < 64) {
+        const int v = cache[dev].load();
+        if (v) return v;
+    }
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    if (dev >= 0 && dev < 64) cache[dev].store(n);
+    return n;
+}
+
+bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
 template <int BN, int EPI>
-cudaError_t launch_bn(const TcGemmParams &p, const void *A, const void *W, cudaStream_t st, bool pdl) {
+cudaError_t launch_bn(const TcGemmParams &p, const void *A, const void *W, cudaStream_t st, bool pdl,
+                      const CUtensorMap &mo, const CUtensorMap &mk, const CUtensorMap &mv) {
     CUtensorMap ma, mb;
     if (!make_map(&ma, A, p.M, p.K, kBM) || !make_map(&mb, W, p.N, p.K, BN)) return cudaErrorInvalidValue;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             TcCfg<BN>::kSmem);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    // the shared-memory opt-in is per device
+    static std::atomic<uint64_t> attr_set{0};
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+        e = cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 TcCfg<BN>::kSmem);
         if (e != cudaSuccess) return e;
-        attr = true;
+        attr_set.fetch_or(bit);
     }
+    const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+    const int sms = device_sms(dev);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((p.N + BN - 1) / BN, (p.M + kBM - 1) / kBM);
+    cfg.gridDim = dim3(tiles < sms ? tiles : sms);
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = TcCfg<BN>::kSmem;
     cfg.stream = st;
@@ -285,32 +768,172 @@ cudaError_t launch_bn(const TcGemmParams &p, const void *A, const void *W, cudaS
     attr1[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr1;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, EPI>, ma, mb, p);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, EPI>, ma, mb, mo, mk, mv, p);
+}
+
+int max_pair_clusters(const void *fn, int smem, int dev) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute a[1];
+    a[0].id = cudaLaunchAttributeClusterDimension;
+    a[0].val.clusterDim.x = 2;
+    a[0].val.clusterDim.y = 1;
+    a[0].val.clusterDim.z = 1;
+    cfg.attrs = a;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = device_sms(dev) / 2;
+    }
+    return n;
+}
+
+template <int BN, int EPI>
+cudaError_t launch_pair(const TcGemmParams &p, const void *A, const void *W, cudaStream_t st, bool pdl,
+                        const CUtensorMap &mo, const CUtensorMap &mk, const CUtensorMap &mv) {
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, A, p.M, p.K, kBM) || !make_map(&mb, W, p.N, p.K, BN / 2)) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const void *fn = (const void *)tc_gemm2_kernel<BN, EPI>;
+    static std::atomic<uint64_t> attr_set{0};
+    static std::atomic<int> clusters[64];
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+        e = cudaFuncSetAttribute(tc_gemm2_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Tc2Cfg<BN>::kSmem);
+        if (e != cudaSuccess) return e;
+        clusters[dev & 63].store(max_pair_clusters(fn, Tc2Cfg<BN>::kSmem, dev));
+        attr_set.fetch_or(bit);
+    }
+    const int tiles = ((p.M + 2 * kBM - 1) / (2 * kBM)) * ((p.N + BN - 1) / BN);
+    const int ncl = std::min(tiles, std::max(1, clusters[dev & 63].load()));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * ncl);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = Tc2Cfg<BN>::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute a[2];
+    a[0].id = cudaLaunchAttributeClusterDimension;
+    a[0].val.clusterDim.x = 2;
+    a[0].val.clusterDim.y = 1;
+    a[0].val.clusterDim.z = 1;
+    a[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = a;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, tc_gemm2_kernel<BN, EPI>, ma, mb, mo, mk, mv, p);
+}
+
+// VOX_CUDA_TC_PAIR = 0 | 1 forces the single-CTA or the CTA-pair kernel (read
+// at every launch, so a test can switch it).
+int env_tc_pair() {
+    const char *s = getenv("VOX_CUDA_TC_PAIR");
+    return (s && *s) ? atoi(s) : -1;
+}
+
+int env_tc_bn() {
+    const char *s = getenv("VOX_CUDA_TC_BN");
+    const int n = s ? atoi(s) : 0;
+    return (n == 64 || n == 128 || n == 256) ? n : 0;
 }
 
 }  // namespace
 
-// Tile width: enough CTAs to cover the SMs, widest tile otherwise.
+// Tile width: the widest tile (fewest operand bytes per MMA flop) that still
+// gives at least half as many tiles as SMs.  Measured on B200 at the encoder
+// shapes (M = 1500): 256 for N = 10240 and 6144, 128 for N = 1280 (60 tiles of
+// 256 leave half the SMs idle).  VOX_CUDA_TC_BN = 64 | 128 | 256 forces a width.
 int tc_gemm_bn(int M, int N) {
+    if (const int f = env_tc_bn()) return f;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = device_sms(dev);
     const int mt = (M + kBM - 1) / kBM;
-    if (N % 256 == 0 && mt * (N / 256) >= 148) return 256;
-    if (mt * ((N + 127) / 128) >= 100) return 128;
+    for (int bn = 256; bn > 64; bn >>= 1)
+        if (2 * mt * ((N + bn - 1) / bn) >= sms) return bn;
     return 64;
 }
 
-cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p, const void *A, const void *W, cudaStream_t st,
+// Pair tile width (256 x BN per CTA pair), same cost model over SM pairs.
+int tc_gemm2_bn(int M, int N) {
+    if (const int f = env_tc_bn()) return f >= 128 ? f : 128;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int pairs = device_sms(dev) / 2;
+    const int mt = (M + 2 * kBM - 1) / (2 * kBM);
+    const int widths[2] = {256, 128};
+    const float col_cost[2] = {1.0f, 1.1f};
+    int best = 256;
+    float best_t = 1e30f;
+    for (int i = 0; i < 2; i++) {
+        const int tiles = mt * ((N + widths[i] - 1) / widths[i]);
+        const float t = (float)((tiles + pairs - 1) / pairs) * (float)widths[i] * col_cost[i];
+        if (t < best_t) best_t = t, best = widths[i];
+    }
+    return best;
+}
+
+cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, const void *W, cudaStream_t st,
                            bool pdl, int bn) {
+    TcGemmParams p = p_in;
     if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.K % 8 != 0 || !p.err || ((uintptr_t)A & 15) || ((uintptr_t)W & 15))
         return cudaErrorInvalidValue;
     if (epi == TC_SWIGLU && (p.N % 32 != 0)) return cudaErrorInvalidValue;
+    switch (epi) {
+        case TC_STORE:
+        case TC_RESID: {
+            const bool need_out = epi == TC_RESID || !p.out_bf16;
+            p.vec = (!p.bias || al16(p.bias)) && (!need_out || (al16(p.out) && p.ldo % 4 == 0)) &&
+                    (!p.out_bf16 || (al16(p.out_bf16) && p.ldo_bf16 % 8 == 0));
+            break;
+        }
+        case TC_SWIGLU: p.vec = al16(p.out_bf16) && p.ldo_bf16 % 8 == 0; break;
+        case TC_QKV_ENC:
+            p.vec = al16(p.q_out) && al16(p.k_ring) && al16(p.v_ring) && (!p.bias || al16(p.bias)) &&
+                    (!p.bias2 || al16(p.bias2));
+            break;
+        default: return cudaErrorInvalidValue;
+    }
+    // TMA-store epilogue when the destinations allow 16-byte access
+    // (VOX_CUDA_TC_TMA_OUT = 0 forces direct stores)
+    CUtensorMap mo, mk, mv;
+    memset(&mo, 0, sizeof(mo));
+    memset(&mk, 0, sizeof(mk));
+    memset(&mv, 0, sizeof(mv));
+    const char *env_tma = getenv("VOX_CUDA_TC_TMA_OUT");
+    p.tma_out = (p.vec && !(env_tma && atoi(env_tma) == 0) && make_out_maps(epi, p, &mo, &mk, &mv)) ? 1 : 0;
+    // CTA pairs only on request: at the encoder shapes they measured no faster
+    // than single-CTA tiles (the MMA pipe, not L2 -> SMEM traffic, is the limit)
+    const bool pair = env_tc_pair() == 1 && p.M > kBM;
+    if (pair) {
+        const int pbn = tc_gemm2_bn(p.M, p.N);
+#define VC_TC2_CASE(BN)                                                            \
+        if (pbn == BN) {                                                           \
+            switch (epi) {                                                         \
+                case TC_STORE: return launch_pair<BN, TC_STORE>(p, A, W, st, pdl, mo, mk, mv);     \
+                case TC_RESID: return launch_pair<BN, TC_RESID>(p, A, W, st, pdl, mo, mk, mv);     \
+                case TC_SWIGLU: return launch_pair<BN, TC_SWIGLU>(p, A, W, st, pdl, mo, mk, mv);   \
+                case TC_QKV_ENC: return launch_pair<BN, TC_QKV_ENC>(p, A, W, st, pdl, mo, mk, mv); \
+            }                                                                      \
+        }
+        VC_TC2_CASE(128)
+        VC_TC2_CASE(256)
+#undef VC_TC2_CASE
+        return cudaErrorInvalidValue;
+    }
     if (bn == 0) bn = tc_gemm_bn(p.M, p.N);
 #define VC_TC_CASE(BN)                                                             \
     if (bn == BN) {                                                                \
         switch (epi) {                                                             \
-            case TC_STORE: return launch_bn<BN, TC_STORE>(p, A, W, st, pdl);       \
-            case TC_RESID: return launch_bn<BN, TC_RESID>(p, A, W, st, pdl);       \
-            case TC_SWIGLU: return launch_bn<BN, TC_SWIGLU>(p, A, W, st, pdl);     \
-            case TC_QKV_ENC: return launch_bn<BN, TC_QKV_ENC>(p, A, W, st, pdl);   \
+            case TC_STORE: return launch_bn<BN, TC_STORE>(p, A, W, st, pdl, mo, mk, mv);       \
+            case TC_RESID: return launch_bn<BN, TC_RESID>(p, A, W, st, pdl, mo, mk, mv);       \
+            case TC_SWIGLU: return launch_bn<BN, TC_SWIGLU>(p, A, W, st, pdl, mo, mk, mv);     \
+            case TC_QKV_ENC: return launch_bn<BN, TC_QKV_ENC>(p, A, W, st, pdl, mo, mk, mv);   \
         }                                                                          \
     }
     VC_TC_CASE(64)
@@ -321,22 +944,88 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p, const void *A, const 
 }
 
 // fp32 [M, K] (row stride ld) -> bf16 [M, K], optionally RMS-normalised with
-// weights w (voxtral_kernels.c:346-363).  One warp per row.
+// weights w (voxtral_kernels.c:346-363).  One warp per row; float4 loads and
+// 8-byte stores when K, ld and the pointers allow (vec).
+constexpr int kRowRegs = 16;   // float4 per lane kept in registers: rows up to 2048 floats
+
 __global__ void __launch_bounds__(256)
-rows_to_bf16_kernel(const float *x, int M, int K, int ld, const float *w, uint16_t *out) {
+rows_to_bf16_kernel(const float *x, int M, int K, int ld, const float *w, uint16_t *out, int vec) {
     grid_dep_wait();
     grid_dep_launch();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M) return;
     const float *xr = x + (size_t)warp * ld;
+    uint16_t *o = out + (size_t)warp * K;
     float inv = 1.0f;
+    if (vec && K <= 32 * 4 * kRowRegs) {
+        // the row stays in registers between the sum of squares and the scaling
+        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+        const float4 *w4 = reinterpret_cast<const float4 *>(w);
+        const int K4 = K >> 2;
+        float4 a[kRowRegs];
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < kRowRegs; j++) {
+            const int i = lane + 32 * j;
+            a[j] = i < K4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            ss = fmaf(a[j].x, a[j].x, ss);
+            ss = fmaf(a[j].y, a[j].y, ss);
+            ss = fmaf(a[j].z, a[j].z, ss);
+            ss = fmaf(a[j].w, a[j].w, ss);
+        }
+        if (w) {
+            ss = warp_sum(ss);
+            inv = 1.0f / sqrtf(ss / (float)K + kNormEps);
+        }
+#pragma unroll
+        for (int j = 0; j < kRowRegs; j++) {
+            const int i = lane + 32 * j;
+            if (i >= K4) break;
+            float4 v = a[j];
+            if (w) {
+                const float4 g = __ldg(w4 + i);
+                v.x = v.x * inv * g.x, v.y = v.y * inv * g.y, v.z = v.z * inv * g.z, v.w = v.w * inv * g.w;
+            }
+            *reinterpret_cast<uint2 *>(o + 4 * i) =
+                make_uint2(bf16_bits_rn(v.x) | (bf16_bits_rn(v.y) << 16), bf16_bits_rn(v.z) | (bf16_bits_rn(v.w) << 16));
+        }
+        return;
+    }
+    if (vec) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+        const int K4 = K >> 2;
+        if (w) {
+            float ss = 0.f;
+#pragma unroll 4
+            for (int i = lane; i < K4; i += 32) {
+                const float4 a = x4[i];
+                ss = fmaf(a.x, a.x, ss);
+                ss = fmaf(a.y, a.y, ss);
+                ss = fmaf(a.z, a.z, ss);
+                ss = fmaf(a.w, a.w, ss);
+            }
+            ss = warp_sum(ss);
+            inv = 1.0f / sqrtf(ss / (float)K + kNormEps);
+        }
+        const float4 *w4 = reinterpret_cast<const float4 *>(w);
+#pragma unroll 4
+        for (int i = lane; i < K4; i += 32) {
+            float4 a = x4[i];
+            if (w) {
+                const float4 g = __ldg(w4 + i);
+                a.x = a.x * inv * g.x, a.y = a.y * inv * g.y, a.z = a.z * inv * g.z, a.w = a.w * inv * g.w;
+            }
+            *reinterpret_cast<uint2 *>(o + 4 * i) =
+                make_uint2(bf16_bits_rn(a.x) | (bf16_bits_rn(a.y) << 16), bf16_bits_rn(a.z) | (bf16_bits_rn(a.w) << 16));
+        }
+        return;
+    }
     if (w) {
         float ss = 0.f;
         for (int i = lane; i < K; i += 32) ss = fmaf(xr[i], xr[i], ss);
         ss = warp_sum(ss);
         inv = 1.0f / sqrtf(ss / (float)K + kNormEps);
     }
-    uint16_t *o = out + (size_t)warp * K;
     for (int i = lane; i < K; i += 32) {
         const float v = w ? xr[i] * inv * w[i] : xr[i];
         o[i] = (uint16_t)bf16_bits_rn(v);
@@ -345,6 +1034,10 @@ rows_to_bf16_kernel(const float *x, int M, int K, int ld, const float *w, uint16
 
 cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const float *w, uint16_t *out,
                                 cudaStream_t st, bool pdl) {
+    const int vec = (K % 4 == 0 && ld % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 &&
+                     ((uintptr_t)out & 7) == 0)
+                        ? 1
+                        : 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((M + 7) / 8);
     cfg.blockDim = dim3(256);
@@ -354,7 +1047,7 @@ cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const floa
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, rows_to_bf16_kernel, x, M, K, ld, w, out);
+    return cudaLaunchKernelEx(&cfg, rows_to_bf16_kernel, x, M, K, ld, w, out, vec);
 }
 
 }  // namespace vc

@@ -107,14 +107,17 @@ struct TcGemmParams {
     uint16_t *out_bf16;      // bf16 output [M, ldo_bf16] or NULL
     int ldo_bf16;
     // TC_QKV_ENC
-    const float *rope;       // [M][64]: (cos, sin) pairs of each row's position, or NULL:
-    const float *inv_freq;   //   then cos/sin(pos * inv_freq[d]) on the device ([32])
+    const float *rope;       // cos plane [32][rope_ld] then sin plane [32][rope_ld], indexed
+    int rope_ld;             //   [pair d][row]; or NULL: cos/sin(pos * inv_freq[d]) on the device
+    const float *inv_freq;   // [32]
     const int *pos0_dev;     // if non-NULL, the logical position of row 0 (overrides pos0)
     uint16_t *q_out;         // fp16 [M][2048]
     uint16_t *k_ring;        // fp16 [cap][2048] (this layer)
     uint16_t *v_ring;
     int cap, pos0;           // row r sits at logical position pos0 + r, slot (pos0 + r) % cap
     unsigned *err;           // raised when a bounded wait expires
+    int vec;                 // set by launch_tc_gemm: all destinations allow 16-byte stores
+    int tma_out;             // set by launch_tc_gemm: the epilogue stores through TMA
 };
 
 // C = A . W^T with bf16 A [M, K] and W [N, K] (row-major, 16-byte aligned,
@@ -139,6 +142,12 @@ struct EncAttnParams {
 };
 cudaError_t launch_enc_attn(const EncAttnParams &p, cudaStream_t st, bool pdl);
 cudaError_t launch_rows_rmsnorm(float *x, int M, int K, const float *w, cudaStream_t st, bool pdl);
+// RoPE planes of a chunk for the q|k epilogue: tab[d][row] = cos and
+// tab[32 + d][row] = sin (row stride ld) of the angle of logical position
+// *pos0_dev + row, taken from the host table src[row][32] (cos, sin) pairs
+// when src is non-NULL, else computed on the device from inv_freq.
+cudaError_t launch_enc_rope_table(float *tab, int ld, int M, const float *src, const int *pos0_dev,
+                                  const float *inv_freq, cudaStream_t st, bool pdl);
 
 // Set the message vox_cuda_last_error() returns on the calling thread.
 void set_last_error(const char *fmt, ...);

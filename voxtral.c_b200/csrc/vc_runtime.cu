@@ -1596,7 +1596,8 @@ struct vox_cuda_enc_state {
     uint16_t *att16 = nullptr;   // [Mx][2048] bf16 attention output
     uint16_t *h16 = nullptr;     // [Mx][5120] bf16 SwiGLU output
     uint16_t *q16 = nullptr;     // [Mx][2048] fp16 queries
-    float *rope = nullptr;       // [Mx][64]
+    float *rope = nullptr;       // RoPE planes [64][Mx]: cos of pair d at [d][row], sin at [32 + d][row]
+    float *rope_src = nullptr;   // the host's table [Mx][64] (cos, sin pairs), when given
     float *aout = nullptr;       // adapter: [Mx/4][3072] fp32 out (Mx/4 x 5120 fp32 in shares x)
     uint16_t *a16 = nullptr;     // adapter: [Mx/4][5120] bf16 in
     uint16_t *mid16 = nullptr;   // adapter: [Mx/4][3072] bf16 mid
@@ -1754,6 +1755,7 @@ extern "C" vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, in
     const size_t o_h = take(Mx * kEncHidden * 2);
     const size_t o_q = take(Mx * kEncQkv * 2);
     const size_t o_rope = take(Mx * kEncHeadDim * 4);
+    const size_t o_rope_src = take(Mx * kEncHeadDim * 4);
     const size_t o_aout = take(Mx / 4 * kDecDim * 4);
     const size_t o_a16 = take(Mx / 4 * 4 * kEncDim * 2);
     const size_t o_mid = take(Mx / 4 * kDecDim * 2);
@@ -1775,6 +1777,7 @@ extern "C" vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, in
     s->h16 = (uint16_t *)(s->ws + o_h);
     s->q16 = (uint16_t *)(s->ws + o_q);
     s->rope = (float *)(s->ws + o_rope);
+    s->rope_src = (float *)(s->ws + o_rope_src);
     s->aout = (float *)(s->ws + o_aout);
     s->a16 = (uint16_t *)(s->ws + o_a16);
     s->mid16 = (uint16_t *)(s->ws + o_mid);
@@ -1818,8 +1821,9 @@ namespace {
 
 // The 32 layers + final norm over s->x: M rows at the logical positions
 // *s->pos_dev.. (read on the device, so the sequence can be replayed as a
-// graph); RoPE from the uploaded table (table) or computed on the device.
-// evs (profiling only): 2 events per launch, recorded around it.
+// graph); RoPE from the uploaded table (table) or from a table computed on
+// the device for this chunk.  evs (profiling only): 2 events per launch,
+// recorded around it.
 int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, cudaEvent_t *evs = nullptr) {
     vox_cuda_encoder *e = s->enc;
     const bool pdl = e->pdl && evs == nullptr;
@@ -1827,6 +1831,8 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
 #define VC_EV_BEGIN() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
 #define VC_EV_END() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
     const size_t ring_layer = (size_t)s->cap * kEncQkv;
+    VC_TRY(launch_enc_rope_table(s->rope, s->max_chunk, M, table ? s->rope_src : nullptr, s->pos_dev, e->inv_freq,
+                                 st, false));
     for (int l = 0; l < e->n_layers; l++) {
         const EncLayer &L = e->L[l];
         VC_EV_BEGIN();
@@ -1838,7 +1844,8 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         p.K = kEncDim;
         p.bias = L.bq;
         p.bias2 = L.bv;
-        p.rope = table ? s->rope : nullptr;
+        p.rope = s->rope;
+        p.rope_ld = s->max_chunk;
         p.inv_freq = e->inv_freq;
         p.pos0_dev = s->pos_dev;
         p.q_out = s->q16;
@@ -1965,7 +1972,8 @@ extern "C" int vox_cuda_encoder_full_step(vox_cuda_enc_state *s, float *x, int n
     cudaStream_t st = c->stream;
     if (rope_freqs) {
         memcpy(s->h_rope, rope_freqs, (size_t)new_len * kEncHeadDim * 4);
-        VC_TRY(cudaMemcpyAsync(s->rope, s->h_rope, (size_t)new_len * kEncHeadDim * 4, cudaMemcpyHostToDevice, st));
+        VC_TRY(cudaMemcpyAsync(s->rope_src, s->h_rope, (size_t)new_len * kEncHeadDim * 4, cudaMemcpyHostToDevice,
+                               st));
     }
     VC_TRY(cudaMemcpyAsync(s->x, x, (size_t)new_len * kEncDim * 4, cudaMemcpyHostToDevice, st));
     if ((rc = run_encoder(s, new_len, rope_freqs != nullptr, st))) return rc;
