@@ -7,6 +7,8 @@
 #include <math.h>
 #include <stdlib.h>
 
+#include <atomic>
+
 namespace vc {
 
 __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
@@ -17,32 +19,66 @@ __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
 // Split-K GQA decode attention over the KV ring (vox_causal_attention with
 // seq_q = 1, voxtral_kernels.c:412-482, as called at voxtral_decoder.c:481-483).
 //
-// grid (S, 8 KV heads, M streams), 128 threads.  A CTA takes one KV head and
-// up to 64 consecutive keys of the window; its 4 query heads share every K/V
-// load.  Instead of the reference's per-key online softmax (a serial chain),
-// the CTA runs three parallel passes: all scores (thread = key half-row, 16
-// float4 loads in flight each), the softmax of its keys (one warp per head),
-// then P.V with coalesced float4 loads of V (warp = key group, lane = 4
-// dims).  Splits are merged with the usual max rescaling by the last CTA of
-// each (stream, KV head) to finish (atomic ticket; no spinning).
+// grid (G, 8 KV heads, M streams), 128 threads.  A CTA takes one KV head and
+// splits of up to 64 consecutive keys (s = blockIdx.x, + G, ...); its 4 query
+// heads share every K/V row.  The split's K and V rows (512 bytes each per
+// key) are staged in shared memory with cp.async, so registers do not bound
+// the bytes in flight.  Keys older than the step's own position are not
+// written by the preceding kernel (the q|k|v GEMV writes only this step's
+// slot), so their copies are issued before griddepcontrol.wait and overlap
+// that kernel's tail; the newest key and q are read after it.
+// (Within one launch, streams that share a ring are consecutive rows of one
+// sequence, the decoder prefill: keys from the lowest such position on are
+// all fresh.)
+// Instead of the reference's per-key online softmax (a serial chain), each
+// split runs three parallel passes: scores (warp = query head, lane = key,
+// rotated float4 reads), the softmax of the split (per warp), then P.V
+// (thread = dimension).  Splits are merged with the usual max rescaling by the
+// last CTA of each (stream, KV head) to finish (atomic ticket; no spinning).
 // ---------------------------------------------------------------------------
 
 constexpr int kKeysPerSplit = 64;
 
+struct AttnShared {
+    float k[kKeysPerSplit][kHeadDim];   // 32 KB; the merge reuses it for its weights
+    float v[kKeysPerSplit][kHeadDim];   // 32 KB
+    float q[4][kHeadDim];
+    float p[4][kKeysPerSplit];          // exp(score - split max)
+    float ml[4][2];                     // per head: (split max, sum of exp)
+    int last;
+};
+static_assert(sizeof(float) * kKeysPerSplit * kHeadDim >= sizeof(float) * 4 * kAttnSplits, "merge weights fit");
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// cp.async of the K and V rows of keys [j0, j1) of a split (key j of the
+// split at ring slot (first + kb + j) % cap), 16 bytes per copy.
+__device__ __forceinline__ void attn_stage_keys(AttnShared &sh, const float *kbase, const float *vbase, int first,
+                                                int kb, int cap, int j0, int j1, int tid) {
+    const int n = (j1 - j0) * (kHeadDim / 4);   // 16-byte pieces per matrix
+    for (int c = tid; c < n; c += 128) {
+        const int j = j0 + c / (kHeadDim / 4), piece = c % (kHeadDim / 4);
+        const size_t row = (size_t)((first + kb + j) % cap) * kKvDim + 4 * piece;
+        cp_async16(&sh.k[j][4 * piece], kbase + row);
+        cp_async16(&sh.v[j][4 * piece], vbase + row);
+    }
+}
+
 __global__ void __launch_bounds__(128)
 attn_decode_kernel(const AttnParams p) {
+    extern __shared__ __align__(16) unsigned char attn_smem[];
+    AttnShared &sh = *reinterpret_cast<AttnShared *>(attn_smem);
     const int kvh = blockIdx.y, m = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    __shared__ __align__(16) float sq[4][kHeadDim];       // the 4 query heads of this KV head
-    __shared__ float ssc[4][kKeysPerSplit];               // scores, then exp(score - max)
-    __shared__ __align__(16) float so[4][4][kHeadDim];    // P.V per key group [group][head][dim]
-    __shared__ float sml[4][2];                            // per head: (max, sum of exp)
-    __shared__ float smw[4][kAttnSplits];                  // merge weights per split
-    __shared__ int s_last;
 
-    grid_dep_wait();
-    grid_dep_launch();
-
+    // The slots were written before this step's first kernel; ring rows of
+    // positions below slt.pos were written by earlier steps.
     const StreamSlot slt = p.slots[m];
     const int n_keys = slt.n_keys;
     const int S = max(1, min(p.S, (n_keys + kKeysPerSplit - 1) / kKeysPerSplit));
@@ -55,125 +91,93 @@ attn_decode_kernel(const AttnParams p) {
     const float *kbase = slt.k_ring + layer_off;
     const float *vbase = slt.v_ring + layer_off;
 
-    {   // queries
+    // keys [0, n_old) predate this launch
+    int fresh_first = slt.pos;
+    for (int i = 0; i < (int)gridDim.z; i++)
+        if (p.slots[i].k_ring == slt.k_ring) fresh_first = min(fresh_first, p.slots[i].pos);
+    const int n_old = max(0, fresh_first - first);
+    {   // the first split's old keys, before the wait
+        const int kb = blockIdx.x * chunk;
+        const int nk = max(0, min(kb + chunk, n_keys) - kb);
+        attn_stage_keys(sh, kbase, vbase, first, kb, cap, 0, max(0, min(nk, n_old - kb)), tid);
+        cp_async_commit();
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+    {   // queries (warp = head, lane = 4 dims)
         const float4 v = *reinterpret_cast<const float4 *>(p.q + (size_t)m * kQDim +
                                                            (kvh * 4 + warp) * kHeadDim + 4 * lane);
-        *reinterpret_cast<float4 *>(&sq[warp][4 * lane]) = v;
+        *reinterpret_cast<float4 *>(&sh.q[warp][4 * lane]) = v;
     }
 
     int n_done = 0;
     for (int s = blockIdx.x; s < S; s += gridDim.x) {
         const int kb = s * chunk;
         const int nk = max(0, min(kb + chunk, n_keys) - kb);
-        // K (thread = key half-row) and V (warp = key group, lane = 4 dims) of
-        // this split, all loads issued before any use
-        const int jk = tid >> 1, hf = tid & 1;
-        float4 kv[16], vv[16];
-        if (jk < nk) {
-            const int slot = (first + kb + jk) % cap;
-            const float4 *kr = reinterpret_cast<const float4 *>(kbase + (size_t)slot * kKvDim + 64 * hf);
-#pragma unroll
-            for (int i = 0; i < 16; i++) kv[i] = __ldcg(kr + i);
+        if (s == (int)blockIdx.x) {
+            // the fresh keys of the first split (written by the preceding kernel)
+            attn_stage_keys(sh, kbase, vbase, first, kb, cap, max(0, min(nk, n_old - kb)), nk, tid);
+        } else {
+            __syncthreads();   // the previous split's K / V / p consumed
+            attn_stage_keys(sh, kbase, vbase, first, kb, cap, 0, nk, tid);
         }
+        cp_async_commit();
+        cp_async_wait_all();
+        __syncthreads();
+
+        // ---- scores and softmax: warp = query head, lane = keys lane, lane + 32 ----
+        {
+            const int h = warp;
+            const float4 *q4 = reinterpret_cast<const float4 *>(sh.q[h]);
+            float sc[2];
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const int j = warp + 4 * i;
-            if (j < nk) {
-                const int slot = (first + kb + j) % cap;
-                vv[i] = __ldcg(reinterpret_cast<const float4 *>(vbase + (size_t)slot * kKvDim) + lane);
-            } else {
-                vv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int u = 0; u < 2; u++) {
+                const int j = lane + 32 * u;
+                const float4 *k4 = reinterpret_cast<const float4 *>(sh.k[j]);
+                float a = 0.f;
+#pragma unroll 8
+                for (int i = 0; i < kHeadDim / 4; i++) {
+                    const int f = (i + lane) & (kHeadDim / 4 - 1);   // rotation: no bank conflicts
+                    const float4 kk = k4[f], qq = q4[f];
+                    a = fmaf(qq.x, kk.x, a);
+                    a = fmaf(qq.y, kk.y, a);
+                    a = fmaf(qq.z, kk.z, a);
+                    a = fmaf(qq.w, kk.w, a);
+                }
+                sc[u] = (j < nk) ? a * scale : -INFINITY;
+            }
+            float mx = fmaxf(sc[0], sc[1]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float pa = (lane < nk) ? expf(sc[0] - mx) : 0.f;
+            const float pb = (lane + 32 < nk) ? expf(sc[1] - mx) : 0.f;
+            sh.p[h][lane] = pa;
+            sh.p[h][lane + 32] = pb;
+            const float sum = warp_sum(pa + pb);
+            if (lane == 0) {
+                sh.ml[h][0] = mx;
+                sh.ml[h][1] = sum;
             }
         }
-        __syncthreads();   // sq ready (first split); previous split's ssc / so consumed
+        __syncthreads();
 
-        // ---- scores ----
+        // ---- P.V: thread = dimension, 4 heads ----
         {
-            float d[4] = {0.f, 0.f, 0.f, 0.f};
-            if (jk < nk) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int j = 0; j < nk; j++) {
+                const float vj = sh.v[j][tid];
 #pragma unroll
-                for (int h = 0; h < 4; h++) {
-                    const float4 *qh = reinterpret_cast<const float4 *>(&sq[h][64 * hf]);
-                    float a = 0.f;
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const float4 q4 = qh[i];
-                        a = fmaf(q4.x, kv[i].x, a);
-                        a = fmaf(q4.y, kv[i].y, a);
-                        a = fmaf(q4.z, kv[i].z, a);
-                        a = fmaf(q4.w, kv[i].w, a);
-                    }
-                    d[h] = a;
-                }
+                for (int h = 0; h < 4; h++) acc[h] = fmaf(sh.p[h][j], vj, acc[h]);
             }
 #pragma unroll
             for (int h = 0; h < 4; h++) {
-                const float t = d[h] + __shfl_xor_sync(0xffffffffu, d[h], 1);
-                if (hf == 0 && jk < nk) ssc[h][jk] = t * scale;
+                const size_t pidx = ((size_t)m * kDecHeads + kvh * 4 + h) * p.S + s;
+                p.part_o[pidx * kHeadDim + tid] = acc[h];
             }
-        }
-        __syncthreads();
-
-        // ---- softmax of this split's keys: warp = head ----
-        {
-            const int h = warp;
-            const float a = (lane < nk) ? ssc[h][lane] : -INFINITY;
-            const float b = (lane + 32 < nk) ? ssc[h][lane + 32] : -INFINITY;
-            float mx = fmaxf(a, b);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            const float pa = (lane < nk) ? expf(a - mx) : 0.f;
-            const float pb = (lane + 32 < nk) ? expf(b - mx) : 0.f;
-            if (lane < nk) ssc[h][lane] = pa;
-            if (lane + 32 < nk) ssc[h][lane + 32] = pb;
-            const float sum = warp_sum(pa + pb);
-            if (lane == 0) {
-                sml[h][0] = mx;
-                sml[h][1] = sum;
-            }
-        }
-        __syncthreads();
-
-        // ---- P.V ----
-        {
-            float acc[4][4];
-#pragma unroll
-            for (int h = 0; h < 4; h++)
-#pragma unroll
-                for (int c = 0; c < 4; c++) acc[h][c] = 0.f;
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const int j = warp + 4 * i;
-                if (j < nk) {
-#pragma unroll
-                    for (int h = 0; h < 4; h++) {
-                        const float pw = ssc[h][j];
-                        acc[h][0] = fmaf(pw, vv[i].x, acc[h][0]);
-                        acc[h][1] = fmaf(pw, vv[i].y, acc[h][1]);
-                        acc[h][2] = fmaf(pw, vv[i].z, acc[h][2]);
-                        acc[h][3] = fmaf(pw, vv[i].w, acc[h][3]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int h = 0; h < 4; h++)
-                *reinterpret_cast<float4 *>(&so[warp][h][4 * lane]) =
-                    make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-        }
-        __syncthreads();
-
-        // ---- this split's partial: warp = head, lane = 4 dims ----
-        {
-            const int hh = warp, d4 = 4 * lane;
-            float go[4];
-#pragma unroll
-            for (int c = 0; c < 4; c++)
-                go[c] = so[0][hh][d4 + c] + so[1][hh][d4 + c] + so[2][hh][d4 + c] + so[3][hh][d4 + c];
-            const size_t pidx = ((size_t)m * kDecHeads + kvh * 4 + hh) * p.S + s;
-            *reinterpret_cast<float4 *>(p.part_o + pidx * kHeadDim + d4) = make_float4(go[0], go[1], go[2], go[3]);
-            if (lane == 0) {
-                p.part_ml[pidx * 2] = sml[hh][0];
-                p.part_ml[pidx * 2 + 1] = sml[hh][1];
+            if (tid < 4) {
+                const size_t pidx = ((size_t)m * kDecHeads + kvh * 4 + tid) * p.S + s;
+                p.part_ml[pidx * 2] = sh.ml[tid][0];
+                p.part_ml[pidx * 2 + 1] = sh.ml[tid][1];
             }
         }
         n_done++;
@@ -181,13 +185,14 @@ attn_decode_kernel(const AttnParams p) {
     __threadfence();
     __syncthreads();
     if (tid == 0)
-        s_last = (atomicAdd(&p.counters[m * kDecKvHeads + kvh], (unsigned)n_done) + n_done == (unsigned)S);
+        sh.last = (atomicAdd(&p.counters[m * kDecKvHeads + kvh], (unsigned)n_done) + n_done == (unsigned)S);
     __syncthreads();
-    if (!s_last) return;
+    if (!sh.last) return;
     __threadfence();
 
     // ---- merge the S splits (last CTA of this stream / KV head): warp = head ----
     {
+        float(*smw)[kAttnSplits] = reinterpret_cast<float(*)[kAttnSplits]>(&sh.k[0][0]);
         const int hh = warp, d4 = 4 * lane;
         const int h = kvh * 4 + hh;
         const size_t pbase = ((size_t)m * kDecHeads + h) * p.S;
@@ -210,7 +215,7 @@ attn_decode_kernel(const AttnParams p) {
             const int t = lane + 32 * i;
             const float c = (dloc[i] > 0.f) ? expf(mloc[i] - gm) : 0.f;
             gd += dloc[i] * c;
-            if (t < kAttnSplits) smw[hh][t] = c;
+            smw[hh][t] = c;
         }
         gd = warp_sum(gd);
         __syncwarp();
@@ -264,9 +269,21 @@ int attn_ctas_per_head(int M) {
 }
 
 cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static std::atomic<uint64_t> attr_set{0};   // the shared-memory opt-in is per device
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+        e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(AttnShared));
+        if (e != cudaSuccess) return e;
+        attr_set.fetch_or(bit);
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(attn_ctas_per_head(M), kDecKvHeads, M);
     cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = sizeof(AttnShared);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
