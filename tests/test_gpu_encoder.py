@@ -88,6 +88,27 @@ def test_encoder_epilogue_paths_agree(pair, monkeypatch):
         assert np.array_equal(a, b)
 
 
+def test_encoder_attention_kernels_agree(monkeypatch):
+    """The tcgen05 attention (S and P.V in TMEM, fp16 P) and the mma.sync
+    flash attention on the same chunks, across the window and the ring's
+    wrap: the same math with different roundings of P and of exp."""
+    ew = B.EncoderWeights(seed=9, n_layers=3, distinct=3, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    outs = {}
+    for mode in ("tc", "mma"):
+        monkeypatch.setenv("VOX_CUDA_ENC_ATTN", mode)
+        st = e.state(max_chunk=256)
+        ys = []
+        for i, n in enumerate([64, 200, 3, 250, 130, 250, 256, 77, 129]):
+            ys.append(st.step(B.normal_f32((n, B.ENC_DIM), 990 + i)))
+        outs[mode] = ys
+        st.free()
+    e.free()
+    for i, (a, b) in enumerate(zip(outs["tc"], outs["mma"])):
+        assert np.isfinite(a).all()
+        assert B.rel_l2(a, b) < 2e-3, (i, B.rel_l2(a, b))
+
+
 def test_encoder_host_rope_table_matches_device_table():
     """vox_cuda_encoder_full_step with the host's RoPE table (the reference
     API passes rope_freqs) and with the table computed on the device.  The two

@@ -1,0 +1,392 @@
+// vc_enc_attn_tc.cu - encoder sliding-window attention on the tcgen05 tensor
+// cores (vox_causal_attention for seq_q = new_len, window 750, 32 heads x 64,
+// voxtral_kernels.c:412-482 as called at voxtral_encoder.c:574-576).
+//
+// One CTA = 128 query rows of one head (TMEM lane = query row), 192 threads,
+// three CTAs per SM (64 KB shared memory, 128 TMEM columns, <= 112 registers)
+// so that a 1500-row chunk's 12 x 32 tiles run in one wave:
+//   warp 0 (one thread)  TMA: the Q tile once, then 64-key blocks of K and V
+//                        from the fp16 ring into a double-buffered ring
+//   warp 1 (one thread)  MMAs: S_b = Q K_b^T (M 128, N 64, K 64) into TMEM
+//                        columns [0,64); O += P_b V_b (M 128, N 64, K 64, V
+//                        an MN-major operand) accumulating in columns [64,128)
+//   warps 2-5            softmax, thread = row: one tcgen05.ld of S_b, mask
+//                        (the row's own window [pos - 749, pos]), block max,
+//                        P_b = 2^(s - m) as fp16 into shared memory (the A
+//                        operand of the O MMA), row sum in fp32
+// The running max m of a row moves only when a block's max exceeds it by more
+// than 2^8 (P stays <= 256, exact enough in fp16 and fp32); then the thread
+// rescales its O row in TMEM (tcgen05.ld / st) and its sum before writing
+// P_b.  Once P_b is in shared memory the MMA warp issues S_{b+1} and then
+// O += P_b V_b; the softmax takes the max of S_{b+1} before it waits for that
+// O MMA (whose completion also frees P).  Key blocks start at multiples of 64
+// positions and the ring capacity is a multiple of 128, so a block never
+// wraps in the ring.  Every mbarrier wait is bounded (2 s of %globaltimer);
+// on expiry the CTA raises the error word and exits after a grace period.
+#include "vc_common.cuh"
+#include "vc_internal.h"
+#include "vc_tc.cuh"
+
+#include <cuda_fp16.h>
+#include <math.h>
+#include <stdlib.h>
+
+#include <atomic>
+#include <mutex>
+
+namespace vc {
+
+using namespace tc;
+
+constexpr int kFaRows = 128;      // query rows per CTA = TMEM lanes
+constexpr int kFaKeys = 64;       // keys per block
+constexpr int kFaThreads = 192;
+constexpr int kFaTmemCols = 128;  // S [0,64), O [64,128)
+constexpr uint64_t kFaWaitNs = 2000000000ull;
+constexpr float kFaRescale = 8.0f;   // log2 of the largest P before the max moves
+
+struct FaSmem {
+    unsigned char q[kFaRows * 128];        // Q [128 rows][64 dims] fp16, 128-byte swizzle
+    unsigned char k[2][kFaKeys * 128];     // K blocks [64 keys][64 dims]
+    unsigned char v[2][kFaKeys * 128];     // V blocks [64 keys][64 dims] (MN-major B of P.V)
+    unsigned char p[kFaRows * 128];        // P [128 rows][64 keys], K-major
+    uint64_t q_full, s_full, p_full, o_full;
+    uint64_t kv_full[2], kv_empty[2];
+    uint32_t tmem;
+};
+
+// Instruction descriptor, kind::f16 with fp16 A and B (format 0), fp32 D;
+// b_mn: B is MN-major (bit 16).
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool b_mn) {
+    return (1u << 4) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Shared-memory descriptor of an MN-major operand in the 128-byte-swizzle
+// canonical layout whose MN extent is one 64-element atom: rows of 128 bytes
+// along K, 8-row groups 1024 bytes apart (stride byte offset); the leading
+// byte offset (between MN atoms) is unused at this width.
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(const void *p) {
+    const uint64_t addr = smem_u32(p);
+    return ((addr >> 4) & 0x3FFFull) | ((uint64_t)(16384 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t half2_bits(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__global__ void __launch_bounds__(kFaThreads, 3)
+enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const EncAttnParams p) {
+    extern __shared__ __align__(1024) unsigned char fa_smem_raw[];
+    FaSmem &sh = *reinterpret_cast<FaSmem *>(fa_smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = blockIdx.x * kFaRows, head = blockIdx.y;
+    const uint64_t deadline = globaltimer() + kFaWaitNs;
+    bool ok = (smem_u32(fa_smem_raw) & 1023u) == 0;   // the swizzled tiles need 1024-byte alignment
+
+    if (threadIdx.x == 0) {
+        mbar_init(&sh.q_full, 1);
+        mbar_init(&sh.s_full, 1);
+        mbar_init(&sh.p_full, 4);   // one arrival per softmax warp
+        mbar_init(&sh.o_full, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&sh.kv_full[i], 1);
+            mbar_init(&sh.kv_empty[i], 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        prefetch_tensormap(&tmQ);
+        prefetch_tensormap(&tmK);
+        prefetch_tensormap(&tmV);
+    }
+    if (warp == 1) {
+        tmem_alloc(&sh.tmem, kFaTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sh.tmem;
+
+    grid_dep_wait();
+    grid_dep_launch();
+
+    const int M = p.M;
+    const int pos0 = p.pos0_dev ? *p.pos0_dev : p.pos0;
+    const int p_first = pos0 + r0;
+    const int p_last = pos0 + min(r0 + kFaRows, M) - 1;
+    const int kstart = max(0, p_first - (kEncWindow - 1)) / kFaKeys * kFaKeys;
+    const int nb = (p_last - kstart) / kFaKeys + 1;
+
+    if (!ok) {
+        // misaligned shared memory: nothing was issued
+    } else if (warp == 0) {
+        if (lane == 0) {
+            uint64_t pol;
+            asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+            mbar_expect_tx(&sh.q_full, kFaRows * 128);
+            tma_load_2d(sh.q, &tmQ, head * kEncHeadDim, r0, &sh.q_full, pol);
+            for (int b = 0; b < nb; b++) {
+                const int buf = b & 1;
+                if (b >= 2 && !mbar_wait(&sh.kv_empty[buf], ((b >> 1) + 1) & 1u, deadline)) {
+                    ok = false;
+                    break;
+                }
+                const int slot = (kstart + b * kFaKeys) % p.cap;
+                mbar_expect_tx(&sh.kv_full[buf], 2 * kFaKeys * 128);
+                tma_load_2d(sh.k[buf], &tmK, head * kEncHeadDim, slot, &sh.kv_full[buf], pol);
+                tma_load_2d(sh.v[buf], &tmV, head * kEncHeadDim, slot, &sh.kv_full[buf], pol);
+            }
+            // tail: the last releases of both buffers have arrived
+            for (int b = nb > 2 ? nb - 2 : 0; b < nb && ok; b++)
+                ok = mbar_wait(&sh.kv_empty[b & 1], (b >> 1) & 1u, deadline);
+        }
+    } else if (warp == 1) {
+        // MMA issue order: S_0; then per block b, once P_b is in shared memory:
+        // S_{b+1} (the softmax already read S_b), then O += P_b V_b.
+        if (lane == 0) {
+            constexpr uint32_t id_s = idesc_f16(kFaRows, kFaKeys, false);
+            constexpr uint32_t id_o = idesc_f16(kFaRows, kEncHeadDim, true);
+            auto issue_s = [&](int b) {
+                const uint64_t a0 = smem_desc_sw128(sh.q), b0 = smem_desc_sw128(sh.k[b & 1]);
+#pragma unroll
+                for (int k = 0; k < kEncHeadDim / 16; k++)   // +32 bytes per K=16 step
+                    tc_mma_f16(tmem, a0 + 2 * k, b0 + 2 * k, id_s, k != 0 ? 1u : 0u);
+                tc_commit(&sh.s_full);
+            };
+            ok = mbar_wait(&sh.q_full, 0u, deadline) && mbar_wait(&sh.kv_full[0], 0u, deadline);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0);
+            }
+            for (int b = 0; b < nb && ok; b++) {
+                if (!mbar_wait(&sh.p_full, b & 1u, deadline)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (b + 1 < nb) {
+                    if (!mbar_wait(&sh.kv_full[(b + 1) & 1], ((b + 1) >> 1) & 1u, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_s(b + 1);
+                }
+                const uint64_t a0 = smem_desc_sw128(sh.p);
+#pragma unroll
+                for (int t = 0; t < kFaKeys / 16; t++) {   // 4 steps of 16 keys
+                    const uint64_t bv = smem_desc_sw128_mn(sh.v[b & 1] + t * 16 * 128);
+                    tc_mma_f16(tmem + kFaKeys, a0 + 2 * t, bv, id_o, (b | t) != 0 ? 1u : 0u);
+                }
+                tc_commit(&sh.o_full);
+                tc_commit(&sh.kv_empty[b & 1]);
+            }
+        }
+    } else {
+        // ---- softmax: thread = query row = TMEM lane ----
+        const int q = warp & 3;
+        const int row = 32 * q + lane;
+        const int pr = pos0 + r0 + row;                     // this row's logical position
+        const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
+        const float sl2 = 0.18033688011112042f;              // (1 / sqrt(64)) * log2(e)
+        float m = -INFINITY, l = 0.f;
+        for (int b = 0; b < nb; b++) {
+            const bool got = mbar_wait(&sh.s_full, b & 1u, deadline);
+            if (!__all_sync(0xffffffffu, got)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sa[32], sb[32];   // S_b columns 0-31 and 32-63
+            tmem_ld32(tl, sa);
+            tmem_ld32(tl + 32u, sb);
+#define SV(j) ((j) < 32 ? sa[(j) & 31] : sb[(j) & 31])
+            const int kb0 = kstart + b * kFaKeys;
+            // every key of the block inside every valid row's window: no mask;
+            // else key offset c is valid for this row iff (unsigned)(c - lo) <= 749
+            const bool full = kb0 >= p_last - (kEncWindow - 1) && kb0 + kFaKeys - 1 <= p_first;
+            const int lo = pr - (kEncWindow - 1) - kb0;
+            if (!full) {
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    if ((unsigned)(j - lo) > (unsigned)(kEncWindow - 1)) sa[j] = -INFINITY;
+                    if ((unsigned)(j + 32 - lo) > (unsigned)(kEncWindow - 1)) sb[j] = -INFINITY;
+                }
+            }
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                mx4[j & 3] = fmaxf(mx4[j & 3], sa[j]);
+                mx4[j & 3] = fmaxf(mx4[j & 3], sb[j]);
+            }
+            const float mb = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+            // move the running max only when this block's max exceeds it by > 2^8
+            const bool move = mb > m + kFaRescale;
+            float factor = 1.f;
+            if (move) {
+                factor = (m == -INFINITY) ? 0.f : fast_exp2(m - mb);
+                m = mb;
+                l *= factor;
+            }
+            // O += P_{b-1} V_{b-1} complete: P is free and O can be rescaled
+            if (b > 0) {
+                const bool got_o = mbar_wait(&sh.o_full, (b - 1) & 1u, deadline);
+                if (!__all_sync(0xffffffffu, got_o)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
+            const float base = (m == -INFINITY) ? 0.f : m;
+            // P = 2^(s * sl2 - m) as fp16, row sum in fp32 (4 chains)
+            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+            unsigned char *ph = sh.p + row * 128;
+#pragma unroll
+            for (int c = 0; c < kFaKeys; c += 8) {
+                uint32_t h[4];
+#pragma unroll
+                for (int j = 0; j < 8; j += 2) {
+                    const float ea = fast_exp2(fmaf(SV(c + j), sl2, -base));
+                    const float eb = fast_exp2(fmaf(SV(c + j + 1), sl2, -base));
+                    rs4[(j >> 1) & 3] += ea + eb;
+                    h[j >> 1] = half2_bits(ea, eb);
+                }
+                *reinterpret_cast<uint4 *>(ph + 16 * ((c >> 3) ^ (row & 7))) = make_uint4(h[0], h[1], h[2], h[3]);
+            }
+#undef SV
+            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+            // rows whose max moved rescale their O row (after P, so S is dead)
+            if (b > 0 && __any_sync(0xffffffffu, move)) {
+#pragma unroll
+                for (int c = 0; c < kEncHeadDim; c += 32) {
+                    float ov[32];
+                    tmem_ld32(tl + kFaKeys + (uint32_t)c, ov);
+#pragma unroll
+                    for (int j = 0; j < 32; j++) ov[j] *= factor;
+                    tmem_st32(tl + kFaKeys + (uint32_t)c, ov);
+                }
+            }
+            fence_async_smem();   // P visible to the tensor core
+            tc_fence_before();    // S / O accesses ordered before the next MMAs
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.p_full);
+        }
+        // the last O MMA, then o / l as bf16 (the wo GEMM's A operand)
+        bool got_o = ok && nb > 0 && mbar_wait(&sh.o_full, (nb - 1) & 1u, deadline);
+        if (!__all_sync(0xffffffffu, got_o)) ok = false;
+        if (ok) {
+            tc_fence_after();
+            const float il = (l > 0.f) ? 1.0f / l : 0.f;
+            uint16_t *dst = p.out + (size_t)(r0 + row) * kEncQkv + head * kEncHeadDim;
+            const bool rv = r0 + row < M;
+#pragma unroll
+            for (int c = 0; c < kEncHeadDim; c += 32) {
+                float ov[32];
+                tmem_ld32(tl + kFaKeys + (uint32_t)c, ov);
+                if (rv) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8)
+                        *reinterpret_cast<uint4 *>(dst + c + j) = make_uint4(
+                            bf16_bits_rn(ov[j] * il) | (bf16_bits_rn(ov[j + 1] * il) << 16),
+                            bf16_bits_rn(ov[j + 2] * il) | (bf16_bits_rn(ov[j + 3] * il) << 16),
+                            bf16_bits_rn(ov[j + 4] * il) | (bf16_bits_rn(ov[j + 5] * il) << 16),
+                            bf16_bits_rn(ov[j + 6] * il) | (bf16_bits_rn(ov[j + 7] * il) << 16));
+                }
+            }
+        }
+    }
+
+    if (!__all_sync(0xffffffffu, ok)) ok = false;
+    if (!ok) {
+        if (lane == 0 && p.err) atomicExch(p.err, 1u);
+        const uint64_t grace = globaltimer() + 10000000ull;   // let in-flight copies / MMAs land
+        while (globaltimer() < grace) {
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kFaTmemCols);
+    }
+}
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn fa_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *q = nullptr;
+        cudaDriverEntryPointQueryResult r;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)q;
+    });
+    return fn;
+}
+
+// fp16 [rows][2048], box box_rows x 64 columns (one head), 128-byte swizzle
+bool fa_map(CUtensorMap *m, const void *ptr, int rows, int box_rows) {
+    EncodeTiledFn fn = fa_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)kEncQkv, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kEncQkv * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kEncHeadDim, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool enc_attn_tc_supported(const EncAttnParams &p) {
+    return p.cap % kEncRingAlign == 0 && p.cap >= p.M + kEncWindow - 1 && p.err != nullptr &&
+           ((uintptr_t)p.q & 15) == 0 && ((uintptr_t)p.k_ring & 15) == 0 && ((uintptr_t)p.v_ring & 15) == 0 &&
+           ((uintptr_t)p.out & 15) == 0;
+}
+
+cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl) {
+    if (p.M <= 0 || !enc_attn_tc_supported(p)) return cudaErrorInvalidValue;
+    CUtensorMap mq, mk, mv;
+    if (!fa_map(&mq, p.q, p.M, kFaRows) || !fa_map(&mk, p.k_ring, p.cap, kFaKeys) ||
+        !fa_map(&mv, p.v_ring, p.cap, kFaKeys))
+        return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static std::atomic<uint64_t> attr_set{0};   // the shared-memory opt-in is per device
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+        e = cudaFuncSetAttribute(enc_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(FaSmem));
+        if (e != cudaSuccess) return e;
+        attr_set.fetch_or(bit);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((p.M + kFaRows - 1) / kFaRows, kEncHeads);
+    cfg.blockDim = dim3(kFaThreads);
+    cfg.dynamicSmemBytes = sizeof(FaSmem);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel, mq, mk, mv, p);
+}
+
+}  // namespace vc

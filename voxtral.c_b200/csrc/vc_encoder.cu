@@ -15,6 +15,8 @@
 
 #include <cuda_fp16.h>
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 namespace vc {
 
@@ -239,6 +241,8 @@ enc_attn_kernel(const EncAttnParams p) {
 
 cudaError_t launch_enc_attn(const EncAttnParams &p, cudaStream_t st, bool pdl) {
     if (p.M <= 0 || p.cap < p.M + kEncWindow - 1) return cudaErrorInvalidValue;
+    const char *sel = getenv("VOX_CUDA_ENC_ATTN");   // "mma" forces the mma.sync kernel
+    if (!(sel && strcmp(sel, "mma") == 0) && enc_attn_tc_supported(p)) return launch_enc_attn_tc(p, st, pdl);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((p.M + kEaRows - 1) / kEaRows, kEncHeads);
     cfg.blockDim = dim3(128);

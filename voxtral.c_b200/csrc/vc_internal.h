@@ -139,8 +139,15 @@ struct EncAttnParams {
     const int *pos0_dev;      // if non-NULL, overrides pos0
     int M;
     uint16_t *out;            // bf16 [M][2048]
+    unsigned *err;            // raised when a bounded wait expires (tensor-core kernel)
 };
+// Windowed encoder attention: the tcgen05 kernel when enc_attn_tc_supported
+// (ring capacity a multiple of 128, err set) unless VOX_CUDA_ENC_ATTN=mma,
+// else the mma.sync kernel.
 cudaError_t launch_enc_attn(const EncAttnParams &p, cudaStream_t st, bool pdl);
+bool enc_attn_tc_supported(const EncAttnParams &p);
+cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl);
+constexpr int kEncRingAlign = 128;   // encoder ring capacities are multiples of this
 cudaError_t launch_rows_rmsnorm(float *x, int M, int K, const float *w, cudaStream_t st, bool pdl);
 // RoPE planes of a chunk for the q|k epilogue: tab[d][row] = cos and
 // tab[32 + d][row] = sin (row stride ld) of the angle of logical position

@@ -1740,7 +1740,7 @@ extern "C" vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, in
     vox_cuda_enc_state *s = new vox_cuda_enc_state();
     s->enc = e;
     s->max_chunk = (max_chunk + 3) / 4 * 4;
-    s->cap = kEncWindow + s->max_chunk;
+    s->cap = (kEncWindow + s->max_chunk + kEncRingAlign - 1) / kEncRingAlign * kEncRingAlign;
     s->ring_bytes = (size_t)e->n_layers * s->cap * kEncQkv * 2;
     const size_t Mx = s->max_chunk;
     size_t off = 0;
@@ -1864,6 +1864,7 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         a.pos0_dev = s->pos_dev;
         a.M = M;
         a.out = s->att16;
+        a.err = s->err;
         VC_EV_BEGIN();
         VC_TRY(launch_enc_attn(a, st, pdl));
         VC_EV_END();
