@@ -229,6 +229,50 @@ def gen_encoder(ew):
     np.savez_compressed(os.path.join(HERE, "encoder.npz"), **out)
 
 
+# End-to-end chain (configs[3] in small): post-conv-stem chunks -> encoder ->
+# adapter -> decoder inputs adapter_out[i] + tok_embed(id) (voxtral.c:346)
+# -> prompt [BOS] + [STREAMING_PAD] * (32 + 6 delay tokens) prefilled as
+# 38 rows + one step (voxtral.c:839-867), then teacher-forced steps on the
+# reference's own tokens (voxtral.c:898-906).
+CHAIN_CHUNKS = [120, 80]
+CHAIN_PROMPT = 1 + 32 + 6
+CHAIN_STEPS = 9
+TOKEN_BOS, TOKEN_PAD = 1, 32
+
+
+def chain_chunks(seed=8101):
+    return [B.normal_f32((n, B.ENC_DIM), seed + i, 1.0) for i, n in enumerate(CHAIN_CHUNKS)]
+
+
+def chain_embed(w, adapter_row, token):
+    return adapter_row + B.bf16_to_f32(w.tok_emb[token])
+
+
+def gen_chain(w, ew):
+    out = {}
+    ref = B.RefCtx(dec=w, enc=ew)
+    enc = np.concatenate([ref.encoder_incremental(x) for x in chain_chunks()], axis=0)
+    ad = ref.adapter(enc)
+    pack("adapter", ad, out)
+    prompt = np.stack([chain_embed(w, ad[i], TOKEN_BOS if i == 0 else TOKEN_PAD)
+                       for i in range(CHAIN_PROMPT)])
+    ref.decoder_prefill(prompt[:CHAIN_PROMPT - 1])
+    inputs = []
+    tok, lg = ref.decoder_forward(prompt[CHAIN_PROMPT - 1])
+    for g in range(CHAIN_STEPS):
+        if g > 0:
+            inputs.append(tok)
+            tok, lg = ref.decoder_forward(chain_embed(w, ad[CHAIN_PROMPT - 1 + g], tok))
+        pack(f"step{g}_logits", lg, out)
+        out[f"step{g}_token"] = np.int32(tok)
+        srt = np.sort(lg)
+        out[f"step{g}_margin"] = np.float32(srt[-1] - srt[-2])
+        out[f"step{g}_top_idx"], out[f"step{g}_top_val"] = top(lg)
+    out["teacher_tokens"] = np.array(inputs, np.int32)   # the token fed at steps 1..
+    ref.free()
+    np.savez_compressed(os.path.join(HERE, "chain.npz"), **out)
+
+
 ALT_CASES = [(61, 3.0, 4, 0.999), (62, 0.5, 4, 0.5), (63, 8.0, 3, 0.99), (64, 1.0, 2, 0.9),
              (65, 0.01, 4, 0.999)]
 
@@ -247,6 +291,10 @@ def gen_alts():
 def main():
     assert B.ref_available(), "build oracle/_ref first (make -C oracle ref)"
     t = time.time()
+    if sys.argv[1:] == ["chain"]:   # only the end-to-end chain
+        gen_chain(B.DecoderWeights(seed=DEC_SEED), B.EncoderWeights(seed=DEC_SEED))
+        print("chain", time.time() - t)
+        return
     gen_linear(); print("linear", time.time() - t)
     gen_rope(); print("rope", time.time() - t)
     gen_attention(); print("attention", time.time() - t)
@@ -256,6 +304,7 @@ def main():
     del w
     ew = B.EncoderWeights(seed=DEC_SEED)
     gen_encoder(ew); print("encoder", time.time() - t)
+    gen_chain(B.DecoderWeights(seed=DEC_SEED), ew); print("chain", time.time() - t)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,65 @@
+"""End-to-end chain against the reference's own CPU path (BASELINE configs[3]
+in small): post-conv-stem chunks -> 32-layer encoder -> adapter -> decoder
+inputs adapter_out[i] + tok_embed(id) -> prompt prefill -> teacher-forced
+decode steps.  Golden: tests/golden/chain.npz (gen_golden.py gen_chain).
+
+Contract (north_star): teacher-forced logits within 1e-2 relative L2, greedy
+token ids bit-exact wherever the reference's top-1 margin exceeds 1e-3."""
+import numpy as np
+import pytest
+
+import bind as B
+import gen_golden as G
+import voxcuda as V
+from conftest import load_golden, unpack
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-2      # contract: teacher-forced logits rel-L2
+ADAPTER_TOL = 1e-2    # encoder (32 layers of bf16 tensor-core GEMMs) + adapter
+MARGIN = 1e-3         # contract: ids must agree where the reference's top-1 margin exceeds this
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda():
+    V.init()
+    yield
+
+
+def test_chain_encoder_adapter_decoder_matches_reference():
+    g = load_golden("chain")
+    w = B.DecoderWeights(seed=G.DEC_SEED)
+    ew = B.EncoderWeights(seed=G.DEC_SEED)
+
+    enc = V.Encoder([tuple(ew.layer_w[i]) + tuple(ew.layer_b[i]) + tuple(ew.layer_n[i])
+                     for i in range(ew.n_layers)], ew.norm, ew.adapter0, ew.adapter1)
+    est = enc.state(max_chunk=256)
+    enc_out = np.concatenate([est.step(x) for x in G.chain_chunks()], axis=0)
+    ad = est.adapter(enc_out)
+    idx, val, _, _ = unpack(g, "adapter")
+    rel_ad = B.rel_l2(ad.reshape(-1)[idx], val)
+    est.free()
+    enc.free()
+
+    dec = V.Decoder(w.tok_emb, w.norm, [tuple(w.layer_w[i]) + tuple(w.layer_n[i]) for i in range(w.n_layers)],
+                    ada_scale=w.ada_scale, vocab=w.vocab)
+    ds = dec.state()
+    P = G.CHAIN_PROMPT
+    prompt = np.stack([G.chain_embed(w, ad[i], G.TOKEN_BOS if i == 0 else G.TOKEN_PAD) for i in range(P)])
+    ds.prefill(prompt[:P - 1])
+    teacher = g["teacher_tokens"]
+    rels, ours, refs = [], [], []
+    for s in range(G.CHAIN_STEPS):
+        embed = prompt[P - 1] if s == 0 else G.chain_embed(w, ad[P - 1 + s], int(teacher[s - 1]))
+        tok, lg = ds.step(embed)
+        idx, val, _, _ = unpack(g, f"step{s}_logits")
+        rels.append(B.rel_l2(lg[idx], val))
+        ours.append(tok)
+        refs.append(int(g[f"step{s}_token"]))
+        if float(g[f"step{s}_margin"]) > MARGIN:
+            assert tok == refs[-1], (s, tok, refs[-1], float(g[f"step{s}_margin"]), rels[-1])
+    ds.free()
+    dec.free()
+    print("chain: adapter rel-L2", rel_ad, "logit rel-L2 per step", rels, "ids", ours)
+    assert rel_ad < ADAPTER_TOL
+    assert max(rels) < LOGIT_TOL, rels
