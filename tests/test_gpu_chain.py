@@ -15,8 +15,8 @@ from conftest import load_golden, unpack
 
 pytestmark = pytest.mark.gpu
 
-LOGIT_TOL = 1e-2      # contract: teacher-forced logits rel-L2
-ADAPTER_TOL = 1e-2    # encoder (32 layers of bf16 tensor-core GEMMs) + adapter
+LOGIT_TOL = 1e-2      # contract: teacher-forced logits rel-L2 (measured ~9e-4)
+ADAPTER_TOL = 2e-3    # encoder (32 layers of fp16-operand tensor-core GEMMs) + adapter (measured ~5e-4)
 MARGIN = 1e-3         # contract: ids must agree where the reference's top-1 margin exceeds this
 
 

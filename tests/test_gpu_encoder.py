@@ -1,9 +1,9 @@
 """Encoder chunk (tcgen05 GEMMs + windowed fp16 flash attention + fp16 ring)
 and adapter against the reference's golden vectors and the oracle.
 
-The GEMMs round activations to bf16 (<= 5e-3 per matmul, tested in
-test_gpu_gemm_tc.py) and attention runs on fp16 inputs; over 32 residual
-layers the encoder output stays within ENC_TOL of the fp32 reference."""
+The GEMMs round activations (and the bf16 weights, exactly) to fp16 and
+attention runs on fp16 inputs; over 32 residual layers the encoder output
+stays within ENC_TOL of the fp32 reference."""
 import numpy as np
 import pytest
 
@@ -14,7 +14,7 @@ from conftest import load_golden, unpack
 
 pytestmark = pytest.mark.gpu
 
-ENC_TOL = 1e-2       # 32-layer encoder output rel-L2 vs the fp32 reference (measured ~3e-3)
+ENC_TOL = 2e-3       # 32-layer encoder output rel-L2 vs the fp32 reference (measured ~4.4e-4)
 ADAPTER_TOL = 1e-2   # adapter (2 tensor-core GEMMs) on identical inputs
 
 

@@ -13,7 +13,8 @@
 //   warps 2-5            softmax, thread = row: one tcgen05.ld of S_b, mask
 //                        (the row's own window [pos - 749, pos]), block max,
 //                        P_b = 2^(s - m) as fp16 into shared memory (the A
-//                        operand of the O MMA), row sum in fp32
+//                        operand of the O MMA), row sum in fp32; at the end
+//                        O / l as fp16 (or bf16) for the wo GEMM
 // The running max m of a row moves only when a block's max exceeds it by more
 // than 2^8 (P stays <= 256, exact enough in fp16 and fp32); then the thread
 // rescales its O row in TMEM (tcgen05.ld / st) and its sum before writing
@@ -80,6 +81,11 @@ __device__ __forceinline__ float fast_exp2(float x) {
 __device__ __forceinline__ uint32_t half2_bits(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// the output pair as fp16 (f16) or bf16
+__device__ __forceinline__ uint32_t out16x2(float a, float b, int f16) {
+    return f16 ? half2_bits(a, b) : (bf16_bits_rn(a) | (bf16_bits_rn(b) << 16));
 }
 
 __global__ void __launch_bounds__(kFaThreads, 3)
@@ -294,11 +300,11 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 if (rv) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 8)
-                        *reinterpret_cast<uint4 *>(dst + c + j) = make_uint4(
-                            bf16_bits_rn(ov[j] * il) | (bf16_bits_rn(ov[j + 1] * il) << 16),
-                            bf16_bits_rn(ov[j + 2] * il) | (bf16_bits_rn(ov[j + 3] * il) << 16),
-                            bf16_bits_rn(ov[j + 4] * il) | (bf16_bits_rn(ov[j + 5] * il) << 16),
-                            bf16_bits_rn(ov[j + 6] * il) | (bf16_bits_rn(ov[j + 7] * il) << 16));
+                        *reinterpret_cast<uint4 *>(dst + c + j) =
+                            make_uint4(out16x2(ov[j] * il, ov[j + 1] * il, p.f16),
+                                       out16x2(ov[j + 2] * il, ov[j + 3] * il, p.f16),
+                                       out16x2(ov[j + 4] * il, ov[j + 5] * il, p.f16),
+                                       out16x2(ov[j + 6] * il, ov[j + 7] * il, p.f16));
                 }
             }
         }

@@ -221,20 +221,20 @@ enc_attn_kernel(const EncAttnParams p) {
         __syncthreads();
     }
 
-    // ---- O / l -> bf16 (the wo GEMM's A operand) ----
+    // ---- O / l -> fp16 or bf16 (the wo GEMM's A operand) ----
     const float ia = (l_a > 0.f) ? 1.0f / l_a : 0.f, ib = (l_b > 0.f) ? 1.0f / l_b : 0.f;
 #pragma unroll
     for (int n = 0; n < 8; n++) {
         const int col = head * kEncHeadDim + n * 8 + 2 * q4;
         if (row_a < M) {
             uint16_t *dst = p.out + (size_t)row_a * kEncQkv + col;
-            dst[0] = (uint16_t)bf16_bits_rn(o[n][0] * ia);
-            dst[1] = (uint16_t)bf16_bits_rn(o[n][1] * ia);
+            *reinterpret_cast<uint32_t *>(dst) = p.f16 ? pack_half2(o[n][0] * ia, o[n][1] * ia)
+                                                       : (bf16_bits_rn(o[n][0] * ia) | (bf16_bits_rn(o[n][1] * ia) << 16));
         }
         if (row_b < M) {
             uint16_t *dst = p.out + (size_t)row_b * kEncQkv + col;
-            dst[0] = (uint16_t)bf16_bits_rn(o[n][2] * ib);
-            dst[1] = (uint16_t)bf16_bits_rn(o[n][3] * ib);
+            *reinterpret_cast<uint32_t *>(dst) = p.f16 ? pack_half2(o[n][2] * ib, o[n][3] * ib)
+                                                       : (bf16_bits_rn(o[n][2] * ib) | (bf16_bits_rn(o[n][3] * ib) << 16));
         }
     }
 }

@@ -76,6 +76,14 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+// two 16-bit operand values (the next GEMM's A): fp16 or bf16
+__device__ __forceinline__ uint32_t pack16x2(float a, float b, int f16) {
+    return f16 ? pack_half2(a, b) : pack_bf16x2(a, b);
+}
+__device__ __forceinline__ uint16_t bits16(float a, int f16) {
+    return f16 ? __half_as_ushort(__float2half_rn(a)) : (uint16_t)bf16_bits_rn(a);
+}
+
 __device__ __forceinline__ void st16(void *dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     *reinterpret_cast<uint4 *>(dst) = make_uint4(a, b, c, d);
 }
@@ -167,8 +175,8 @@ __device__ __forceinline__ void epi_vec(const TcGemmParams &p, const EpiRow &er,
             uint16_t *ob = p.out_bf16 + (size_t)row * p.ldo_bf16 + col0;
 #pragma unroll
             for (int j = 0; j < kEpiCols; j += 8)
-                st16(ob + j, pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
-                     pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
+                st16(ob + j, pack16x2(v[j], v[j + 1], p.f16), pack16x2(v[j + 2], v[j + 3], p.f16),
+                     pack16x2(v[j + 4], v[j + 5], p.f16), pack16x2(v[j + 6], v[j + 7], p.f16));
         } else {
 #pragma unroll
             for (int j = 0; j < kEpiCols; j += 4)
@@ -180,7 +188,7 @@ __device__ __forceinline__ void epi_vec(const TcGemmParams &p, const EpiRow &er,
         uint32_t h[kEpiCols / 4];
 #pragma unroll
         for (int j = 0; j < kEpiCols; j += 4)
-            h[j >> 2] = pack_bf16x2(silu_fast(v[j]) * v[j + 1], silu_fast(v[j + 2]) * v[j + 3]);
+            h[j >> 2] = pack16x2(silu_fast(v[j]) * v[j + 1], silu_fast(v[j + 2]) * v[j + 3], p.f16);
         uint16_t *o = p.out_bf16 + (size_t)row * p.ldo_bf16 + (col0 >> 1);
 #pragma unroll
         for (int j = 0; j < kEpiCols / 4; j += 4) st16(o + 2 * j, h[j], h[j + 1], h[j + 2], h[j + 3]);
@@ -210,7 +218,7 @@ __device__ __forceinline__ void epi_scalar(const TcGemmParams &p, const EpiRow &
             float x = v[j];
             if constexpr (EPI == TC_RESID) x += o[j];
             if (p.act == 1) x = gelu_tanh(x);
-            if (p.out_bf16) p.out_bf16[(size_t)row * p.ldo_bf16 + col0 + j] = (uint16_t)bf16_bits_rn(x);
+            if (p.out_bf16) p.out_bf16[(size_t)row * p.ldo_bf16 + col0 + j] = bits16(x, p.f16);
             else o[j] = x;
         }
     } else if constexpr (EPI == TC_SWIGLU) {
@@ -218,7 +226,7 @@ __device__ __forceinline__ void epi_scalar(const TcGemmParams &p, const EpiRow &
 #pragma unroll
         for (int j = 0; j < kEpiCols; j += 2) {
             if (col0 + j + 1 >= p.N) break;
-            o[j >> 1] = (uint16_t)bf16_bits_rn(silu_fast(v[j]) * v[j + 1]);
+            o[j >> 1] = bits16(silu_fast(v[j]) * v[j + 1], p.f16);
         }
     } else if constexpr (EPI == TC_QKV_ENC) {
         uint16_t *dst = region == 0   ? p.q_out + (size_t)row * kEncQkv + col0
@@ -269,7 +277,7 @@ __device__ __forceinline__ void epi_tma(const TcGemmParams &p, const EpiMaps &mp
         uint32_t h[kEpiCols / 4];
 #pragma unroll
         for (int j = 0; j < kEpiCols; j += 4)
-            h[j >> 2] = pack_bf16x2(silu_fast(v[j]) * v[j + 1], silu_fast(v[j + 2]) * v[j + 3]);
+            h[j >> 2] = pack16x2(silu_fast(v[j]) * v[j + 1], silu_fast(v[j + 2]) * v[j + 3], p.f16);
         swz_put<32>(stg, lane, 0, make_uint4(h[0], h[1], h[2], h[3]));
         swz_put<32>(stg, lane, 1, make_uint4(h[4], h[5], h[6], h[7]));
     } else if (EPI == TC_QKV_ENC || p.out_bf16) {   // 16-bit outputs, 64-byte rows
@@ -279,8 +287,8 @@ __device__ __forceinline__ void epi_tma(const TcGemmParams &p, const EpiMaps &mp
             const uint4 u = EPI == TC_QKV_ENC
                                 ? make_uint4(pack_half2(w[0], w[1]), pack_half2(w[2], w[3]), pack_half2(w[4], w[5]),
                                              pack_half2(w[6], w[7]))
-                                : make_uint4(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]),
-                                             pack_bf16x2(w[4], w[5]), pack_bf16x2(w[6], w[7]));
+                                : make_uint4(pack16x2(w[0], w[1], p.f16), pack16x2(w[2], w[3], p.f16),
+                                             pack16x2(w[4], w[5], p.f16), pack16x2(w[6], w[7], p.f16));
             swz_put<64>(stg, lane, c, u);
         }
     } else {   // fp32 outputs, 128-byte rows
@@ -418,7 +426,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+            // kind::f16 operand formats: bf16 (1) or fp16 (0) for A (bits 7-9) and B (10-12)
+            const uint32_t idesc = p.f16 ? (idesc_bf16(kBM, BN) & ~((1u << 7) | (1u << 10))) : idesc_bf16(kBM, BN);
             uint32_t it = 0, lt = 0;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, lt++) {
                 const uint32_t b = lt & 1u;
@@ -585,7 +594,8 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = idesc_bf16(2 * kBM, BN);
+            const uint32_t idesc =
+                p.f16 ? (idesc_bf16(2 * kBM, BN) & ~((1u << 7) | (1u << 10))) : idesc_bf16(2 * kBM, BN);
             uint32_t it = 0, lt = 0;
             for (int t = cl; t < tiles && ok; t += ncl, lt++) {
                 const uint32_t b = lt & 1u;
@@ -949,7 +959,7 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
 constexpr int kRowRegs = 16;   // float4 per lane kept in registers: rows up to 2048 floats
 
 __global__ void __launch_bounds__(256)
-rows_to_bf16_kernel(const float *x, int M, int K, int ld, const float *w, uint16_t *out, int vec) {
+rows_to_bf16_kernel(const float *x, int M, int K, int ld, const float *w, uint16_t *out, int vec, int f16) {
     grid_dep_wait();
     grid_dep_launch();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -986,8 +996,7 @@ rows_to_bf16_kernel(const float *x, int M, int K, int ld, const float *w, uint16
                 const float4 g = __ldg(w4 + i);
                 v.x = v.x * inv * g.x, v.y = v.y * inv * g.y, v.z = v.z * inv * g.z, v.w = v.w * inv * g.w;
             }
-            *reinterpret_cast<uint2 *>(o + 4 * i) =
-                make_uint2(bf16_bits_rn(v.x) | (bf16_bits_rn(v.y) << 16), bf16_bits_rn(v.z) | (bf16_bits_rn(v.w) << 16));
+            *reinterpret_cast<uint2 *>(o + 4 * i) = make_uint2(pack16x2(v.x, v.y, f16), pack16x2(v.z, v.w, f16));
         }
         return;
     }
@@ -1015,8 +1024,7 @@ rows_to_bf16_kernel(const float *x, int M, int K, int ld, const float *w, uint16
                 const float4 g = __ldg(w4 + i);
                 a.x = a.x * inv * g.x, a.y = a.y * inv * g.y, a.z = a.z * inv * g.z, a.w = a.w * inv * g.w;
             }
-            *reinterpret_cast<uint2 *>(o + 4 * i) =
-                make_uint2(bf16_bits_rn(a.x) | (bf16_bits_rn(a.y) << 16), bf16_bits_rn(a.z) | (bf16_bits_rn(a.w) << 16));
+            *reinterpret_cast<uint2 *>(o + 4 * i) = make_uint2(pack16x2(a.x, a.y, f16), pack16x2(a.z, a.w, f16));
         }
         return;
     }
@@ -1028,12 +1036,24 @@ rows_to_bf16_kernel(const float *x, int M, int K, int ld, const float *w, uint16
     }
     for (int i = lane; i < K; i += 32) {
         const float v = w ? xr[i] * inv * w[i] : xr[i];
-        o[i] = (uint16_t)bf16_bits_rn(v);
+        o[i] = bits16(v, f16);
     }
 }
 
+__global__ void __launch_bounds__(256) bf16_to_f16_kernel(uint16_t *p, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        p[i] = __half_as_ushort(__float2half_rn(__uint_as_float((uint32_t)p[i] << 16)));
+}
+
+cudaError_t launch_bf16_to_f16(uint16_t *p, size_t n, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    const size_t blocks = (n + 255) / 256;
+    bf16_to_f16_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(p, n);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const float *w, uint16_t *out,
-                                cudaStream_t st, bool pdl) {
+                                cudaStream_t st, bool pdl, bool f16) {
     const int vec = (K % 4 == 0 && ld % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 &&
                      ((uintptr_t)out & 7) == 0)
                         ? 1
@@ -1047,7 +1067,7 @@ cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const floa
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, rows_to_bf16_kernel, x, M, K, ld, w, out, vec);
+    return cudaLaunchKernelEx(&cfg, rows_to_bf16_kernel, x, M, K, ld, w, out, vec, f16 ? 1 : 0);
 }
 
 }  // namespace vc

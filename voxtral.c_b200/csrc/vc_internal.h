@@ -116,6 +116,8 @@ struct TcGemmParams {
     uint16_t *v_ring;
     int cap, pos0;           // row r sits at logical position pos0 + r, slot (pos0 + r) % cap
     unsigned *err;           // raised when a bounded wait expires
+    int f16;                 // A and W are fp16 (kind::f16 with fp16 operands) and so are the
+                             //   16-bit outputs (out_bf16, SwiGLU h); else bf16
     int vec;                 // set by launch_tc_gemm: all destinations allow 16-byte stores
     int tma_out;             // set by launch_tc_gemm: the epilogue stores through TMA
 };
@@ -125,9 +127,12 @@ struct TcGemmParams {
 cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p, const void *A, const void *W, cudaStream_t st,
                            bool pdl, int bn = 0);
 int tc_gemm_bn(int M, int N);
-// fp32 rows -> bf16 rows, optionally RMS-normalised with weights w.
+// fp32 rows -> bf16 (or fp16, f16) rows, optionally RMS-normalised with weights w.
 cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const float *w, uint16_t *out,
-                                cudaStream_t st, bool pdl);
+                                cudaStream_t st, bool pdl, bool f16 = false);
+// In place: bf16 -> fp16 (round to nearest even; the values of bf16 weights
+// are inside fp16's range).
+cudaError_t launch_bf16_to_f16(uint16_t *p, size_t n, cudaStream_t st);
 
 // ---- encoder (vc_encoder.cu) ----
 struct EncAttnParams {
@@ -138,7 +143,8 @@ struct EncAttnParams {
     int pos0;                 // logical position of query row 0
     const int *pos0_dev;      // if non-NULL, overrides pos0
     int M;
-    uint16_t *out;            // bf16 [M][2048]
+    uint16_t *out;            // [M][2048], bf16 or (f16) fp16: the wo GEMM's A operand
+    int f16;
     unsigned *err;            // raised when a bounded wait expires (tensor-core kernel)
 };
 // Windowed encoder attention: the tcgen05 kernel when enc_attn_tc_supported

@@ -1673,6 +1673,13 @@ extern "C" vox_cuda_encoder *vox_cuda_encoder_create(const vox_cuda_enc_weights 
             ok &= cudaMemcpy2D(w13, 2 * D * 2, L.w1, D * 2, D * 2, H, kind) == cudaSuccess;
             ok &= cudaMemcpy2D(w13 + D, 2 * D * 2, L.w3, D * 2, D * 2, H, kind) == cudaSuccess;
             ok &= cudaMemcpy(w2, L.w2, D * H * 2, kind) == cudaSuccess;
+            // the tensor-core GEMMs take fp16 operands: activations keep 11
+            // mantissa bits instead of bf16's 8 (weights convert exactly
+            // except below fp16's normal range, ~6e-5)
+            ok &= launch_bf16_to_f16(qkv, 3 * Q * D, 0) == cudaSuccess;
+            ok &= launch_bf16_to_f16(wo, D * Q, 0) == cudaSuccess;
+            ok &= launch_bf16_to_f16(w13, 2 * H * D, 0) == cudaSuccess;
+            ok &= launch_bf16_to_f16(w2, D * H, 0) == cudaSuccess;
             o.qkv = qkv;
             o.wo = wo;
             o.w13 = w13;
@@ -1703,6 +1710,9 @@ extern "C" vox_cuda_encoder *vox_cuda_encoder_create(const vox_cuda_enc_weights 
         if (ok) {
             ok &= cudaMemcpy(a0, w->adapter0, (size_t)kDecDim * 4 * D * 2, kind) == cudaSuccess;
             ok &= cudaMemcpy(a1, w->adapter1, (size_t)kDecDim * kDecDim * 2, kind) == cudaSuccess;
+            ok &= launch_bf16_to_f16(a0, (size_t)kDecDim * 4 * D, 0) == cudaSuccess;
+            ok &= launch_bf16_to_f16(a1, (size_t)kDecDim * kDecDim, 0) == cudaSuccess;
+            ok &= cudaDeviceSynchronize() == cudaSuccess;
             e->adapter0 = a0;
             e->adapter1 = a1;
         }
@@ -1836,7 +1846,7 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
     for (int l = 0; l < e->n_layers; l++) {
         const EncLayer &L = e->L[l];
         VC_EV_BEGIN();
-        VC_TRY(launch_rows_to_bf16(s->x, M, kEncDim, kEncDim, L.attn_norm, s->xn16, st, pdl));
+        VC_TRY(launch_rows_to_bf16(s->x, M, kEncDim, kEncDim, L.attn_norm, s->xn16, st, pdl, true));
         VC_EV_END();
         TcGemmParams p = {};
         p.M = M;
@@ -1853,6 +1863,7 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         p.v_ring = s->v_ring + l * ring_layer;
         p.cap = s->cap;
         p.err = s->err;
+        p.f16 = 1;
         VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_QKV_ENC, p, s->xn16, L.qkv, st, pdl));
         VC_EV_END();
@@ -1864,6 +1875,7 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         a.pos0_dev = s->pos_dev;
         a.M = M;
         a.out = s->att16;
+        a.f16 = 1;
         a.err = s->err;
         VC_EV_BEGIN();
         VC_TRY(launch_enc_attn(a, st, pdl));
@@ -1876,11 +1888,12 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         p.ldo = kEncDim;
         p.bias = L.bo;
         p.err = s->err;
+        p.f16 = 1;
         VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_RESID, p, s->att16, L.wo, st, pdl));
         VC_EV_END();
         VC_EV_BEGIN();
-        VC_TRY(launch_rows_to_bf16(s->x, M, kEncDim, kEncDim, L.ffn_norm, s->xn16, st, pdl));
+        VC_TRY(launch_rows_to_bf16(s->x, M, kEncDim, kEncDim, L.ffn_norm, s->xn16, st, pdl, true));
         VC_EV_END();
         p = TcGemmParams{};
         p.M = M;
@@ -1889,6 +1902,7 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         p.out_bf16 = s->h16;
         p.ldo_bf16 = kEncHidden;
         p.err = s->err;
+        p.f16 = 1;
         VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_SWIGLU, p, s->xn16, L.w13, st, pdl));
         VC_EV_END();
@@ -1900,6 +1914,7 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         p.ldo = kEncDim;
         p.bias = L.b2;
         p.err = s->err;
+        p.f16 = 1;
         VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_RESID, p, s->h16, L.w2, st, pdl));
         VC_EV_END();
@@ -2011,15 +2026,16 @@ extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc,
     const int rows = n / 4, K0 = 4 * kEncDim;
     // 4 consecutive [1280] rows are one [5120] row: the same memory
     VC_TRY(cudaMemcpyAsync(s->x, enc, (size_t)n * kEncDim * 4, cudaMemcpyHostToDevice, st));
-    VC_TRY(launch_rows_to_bf16(s->x, rows, K0, K0, nullptr, s->a16, st, false));
+    VC_TRY(launch_rows_to_bf16(s->x, rows, K0, K0, nullptr, s->a16, st, false, true));
     TcGemmParams p = {};
     p.M = rows;
     p.N = kDecDim;
     p.K = K0;
     p.act = 1;                  // GELU (voxtral_encoder.c:664)
-    p.out_bf16 = s->mid16;
+    p.out_bf16 = s->mid16;      // fp16, the next GEMM's A
     p.ldo_bf16 = kDecDim;
     p.err = s->err;
+    p.f16 = 1;
     VC_TRY(launch_tc_gemm(TC_STORE, p, s->a16, e->adapter0, st, false));
     p = TcGemmParams{};
     p.M = rows;
@@ -2028,6 +2044,7 @@ extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc,
     p.out = s->aout;
     p.ldo = kDecDim;
     p.err = s->err;
+    p.f16 = 1;
     VC_TRY(launch_tc_gemm(TC_STORE, p, s->mid16, e->adapter1, st, false));
     VC_TRY(cudaMemcpyAsync(out, s->aout, (size_t)rows * kDecDim * 4, cudaMemcpyDeviceToHost, st));
     return enc_err_check(s, st);
