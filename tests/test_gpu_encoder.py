@@ -109,6 +109,24 @@ def test_encoder_attention_kernels_agree(monkeypatch):
         assert B.rel_l2(a, b) < 2e-3, (i, B.rel_l2(a, b))
 
 
+def test_encoder_split_k_matches_unsplit(monkeypatch):
+    """Small chunks run their GEMMs split along K (fp32 partials summed in a
+    fixed slice order by the last slice to finish); against the same chunks
+    with split-K off only the fp32 summation grouping differs."""
+    ew = B.EncoderWeights(seed=10, n_layers=3, distinct=3, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    outs = {}
+    for mode in ("", "1"):
+        monkeypatch.setenv("VOX_CUDA_TC_KSPLIT", mode)
+        st = e.state(max_chunk=256)
+        outs[mode] = [st.step(B.normal_f32((n, B.ENC_DIM), 1010 + i)) for i, n in enumerate([100, 3, 256, 64])]
+        st.free()
+    e.free()
+    for i, (a, b) in enumerate(zip(outs[""], outs["1"])):
+        assert np.isfinite(a).all()
+        assert B.rel_l2(a, b) < 2e-3, (i, B.rel_l2(a, b))
+
+
 def test_encoder_host_rope_table_matches_device_table():
     """vox_cuda_encoder_full_step with the host's RoPE table (the reference
     API passes rope_freqs) and with the table computed on the device.  The two

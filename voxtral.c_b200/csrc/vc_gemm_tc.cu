@@ -44,6 +44,8 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;                     // one 128-byte swizzle row of bf16
 constexpr int kEpiCols = 32;                // accumulator columns per tcgen05.ld
 constexpr int kStageBytes = 32 * 128;       // a warp's staging tile: 32 rows x 128 bytes
+constexpr int kTcMaxSplit = 4;              // split-K slices at most
+constexpr int kTcSplitMinKB = 64;           // split-K only for K >= 64 k-blocks (4096)
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 
 template <int BN>
@@ -349,6 +351,94 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams &p, const EpiMa
     }
 }
 
+// Split-K: one warp's 32 rows x BN/2 columns of slice ks -> the fp32
+// workspace ws[ks][M][N] (rows / columns past M / N are not written).
+template <int BN>
+__device__ __forceinline__ void split_partial(const TcGemmParams &p, uint32_t tbase, int row0, int n0, int half,
+                                              int lane, int ks) {
+    const int row = row0 + lane;
+    float *dst = p.ws + ((size_t)ks * p.M + row) * p.N;
+#pragma unroll 1
+    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
+        float v[kEpiCols];
+        tmem_ld32(tbase + (uint32_t)c, v);
+        const int col0 = n0 + c;
+        if (row >= p.M || col0 >= p.N) continue;
+        if (col0 + kEpiCols <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j += 4)
+                __stcg(reinterpret_cast<float4 *>(dst + col0 + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j++)
+                if (col0 + j < p.N) __stcg(dst + col0 + j, v[j]);
+        }
+    }
+}
+
+// Split-K: sum the KS slices of the sub-tile in slice order (the same sum
+// whichever slice finished last) and run the epilogue on it.
+template <int BN, int EPI>
+__device__ __forceinline__ void split_finish(const TcGemmParams &p, const EpiMaps &mp, int row0, int n0, int half,
+                                             int lane, unsigned char *stg, int KS) {
+    EpiRow er;
+    er.row = row0 + lane;
+    er.pos = 0;
+    er.slot = 0;
+    if constexpr (EPI == TC_QKV_ENC) {
+        er.pos = (p.pos0_dev ? *p.pos0_dev : p.pos0) + er.row;
+        er.slot = (size_t)(er.pos % p.cap);
+    }
+    const bool rv = er.row < p.M;
+    const size_t slice = (size_t)p.M * p.N;
+#pragma unroll 1
+    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
+        const int col0 = n0 + c;
+        if (col0 >= p.N) continue;   // warp-uniform
+        float v[kEpiCols];
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j++) v[j] = 0.f;
+        if (rv) {
+            const float *src = p.ws + (size_t)er.row * p.N + col0;
+            if (col0 + kEpiCols <= p.N && (p.N & 3) == 0) {
+                // two slices in flight: the loads of slice s+1 are issued
+                // before the adds of slice s (the adds stay in slice order)
+                float4 cur[kEpiCols / 4], nxt[kEpiCols / 4];
+#pragma unroll
+                for (int j = 0; j < kEpiCols / 4; j++) cur[j] = __ldcg(reinterpret_cast<const float4 *>(src) + j);
+                for (int s = 0; s < KS; s++) {
+                    if (s + 1 < KS) {
+                        const float4 *nsrc = reinterpret_cast<const float4 *>(src + (size_t)(s + 1) * slice);
+#pragma unroll
+                        for (int j = 0; j < kEpiCols / 4; j++) nxt[j] = __ldcg(nsrc + j);
+                    }
+#pragma unroll
+                    for (int j = 0; j < kEpiCols / 4; j++)
+                        v[4 * j] += cur[j].x, v[4 * j + 1] += cur[j].y, v[4 * j + 2] += cur[j].z,
+                            v[4 * j + 3] += cur[j].w;
+#pragma unroll
+                    for (int j = 0; j < kEpiCols / 4; j++) cur[j] = nxt[j];
+                }
+            } else {
+                for (int s = 0; s < KS; s++, src += slice) {
+#pragma unroll
+                    for (int j = 0; j < kEpiCols; j++)
+                        if (col0 + j < p.N) v[j] += __ldcg(src + j);
+                }
+            }
+        }
+        if (p.tma_out) {
+            epi_tma<EPI>(p, mp, er, v, row0, col0, lane, stg);
+            continue;
+        }
+        if (!rv) continue;
+        int region = 0;
+        if constexpr (EPI == TC_QKV_ENC) region = qkv_apply(p, er, v, col0);
+        if (p.vec && col0 + kEpiCols <= p.N) epi_vec<EPI>(p, er, v, col0, region);
+        else epi_scalar<EPI>(p, er, v, col0, region);
+    }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -371,6 +461,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int MT = (p.M + kBM - 1) / kBM;
     const int tiles = MT * ((p.N + BN - 1) / BN);
     const int KB = (p.K + kBK - 1) / kBK;
+    const int KS = p.ksplit > 1 ? p.ksplit : 1;   // K slices per tile (split-K)
+    const int units = tiles * KS;
     const uint64_t deadline = globaltimer() + kTcWaitNs;
     bool ok = true;
 
@@ -407,9 +499,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             uint64_t pol;
             asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
             uint32_t it = 0;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                const int t = u / KS, ks = u % KS;
                 const int m0 = (t % MT) * kBM, n0 = (t / MT) * BN;
-                for (int kb = 0; kb < KB; kb++, it++) {
+                for (int kb = ks * KB / KS; kb < (ks + 1) * KB / KS; kb++, it++) {
                     const int s = it % S;
                     if (it >= (uint32_t)S && !mbar_wait(&empty[s], ((it / S) + 1) & 1u, deadline)) {
                         ok = false;
@@ -429,7 +522,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // kind::f16 operand formats: bf16 (1) or fp16 (0) for A (bits 7-9) and B (10-12)
             const uint32_t idesc = p.f16 ? (idesc_bf16(kBM, BN) & ~((1u << 7) | (1u << 10))) : idesc_bf16(kBM, BN);
             uint32_t it = 0, lt = 0;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, lt++) {
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, lt++) {
+                const int ks = u % KS, kb_first = ks * KB / KS;
                 const uint32_t b = lt & 1u;
                 if (lt >= 2 && !mbar_wait(&tempty[b], ((lt >> 1) + 1) & 1u, deadline)) {
                     ok = false;
@@ -437,7 +531,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + b * BN;
-                for (int kb = 0; kb < KB; kb++, it++) {
+                for (int kb = kb_first; kb < (ks + 1) * KB / KS; kb++, it++) {
                     const int s = it % S;
                     if (!mbar_wait(&full[s], (it / S) & 1u, deadline)) {
                         ok = false;
@@ -448,7 +542,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint64_t b0 = smem_desc_sw128(sB + s * Cfg::kBBytes);
 #pragma unroll
                     for (int k = 0; k < kBK / 16; k++)   // +32 bytes (2 x 16) per K=16 step
-                        tc_mma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                        tc_mma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc, (kb != kb_first || k != 0) ? 1u : 0u);
                     tc_commit(&empty[s]);
                 }
                 if (ok) tc_commit(&tfull[b]);
@@ -460,7 +554,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const EpiMaps mp = {&tmO, &tmK, &tmV};
         unsigned char *stg = sStage + (warp - 2) * kStageBytes;
         uint32_t lt = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, lt++) {
+        for (int u = blockIdx.x; u < units; u += gridDim.x, lt++) {
+            const int t = u / KS, ks = u % KS;
             const uint32_t b = lt & 1u;
             const bool got = mbar_wait(&tfull[b], (lt >> 1) & 1u, deadline);
             if (!__all_sync(0xffffffffu, got)) {
@@ -469,11 +564,31 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             tc_fence_after();
             const int m0 = (t % MT) * kBM, n0 = (t / MT) * BN;
-            epilogue_tile<BN, EPI>(p, mp, tmem + ((uint32_t)(32 * q) << 16) + b * BN, m0 + 32 * q, n0, half, lane,
-                                   stg);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[b]);
+            const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + b * BN;
+            if (KS == 1) {
+                epilogue_tile<BN, EPI>(p, mp, tb, m0 + 32 * q, n0, half, lane, stg);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);
+            } else {
+                // this split's partial of the warp's 32 x BN/2 sub-tile -> workspace
+                split_partial<BN>(p, tb, m0 + 32 * q, n0, half, lane, ks);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);   // the accumulator is free already
+                // the last of the KS partials of this sub-tile sums them (fixed
+                // order) and runs the epilogue
+                __threadfence();
+                __syncwarp();
+                unsigned prev = 0;
+                if (lane == 0) prev = atomicAdd(&p.ws_cnt[t * kEpiWarps + (warp - 2)], 1u);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == (unsigned)(KS - 1)) {
+                    __threadfence();
+                    split_finish<BN, EPI>(p, mp, m0 + 32 * q, n0, half, lane, stg, KS);
+                    if (lane == 0) p.ws_cnt[t * kEpiWarps + (warp - 2)] = 0u;
+                }
+            }
         }
     }
 
@@ -766,10 +881,11 @@ cudaError_t launch_bn(const TcGemmParams &p, const void *A, const void *W, cudaS
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
-    const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+    // work units: tiles x K slices (split-K)
+    const int units = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * (p.ksplit > 1 ? p.ksplit : 1);
     const int sms = device_sms(dev);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tiles < sms ? tiles : sms);
+    cfg.gridDim = dim3(units < sms ? units : sms);
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = TcCfg<BN>::kSmem;
     cfg.stream = st;
@@ -937,6 +1053,31 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
         return cudaErrorInvalidValue;
     }
     if (bn == 0) bn = tc_gemm_bn(p.M, p.N);
+    p.ksplit = 1;
+    if (p.ws && p.ws_cnt && !pair) {
+        // Split-K when the tiles leave most SMs idle (small M): up to
+        // kTcMaxSplit K slices of >= 4 k-blocks each, at most one unit per SM.
+        // VOX_CUDA_TC_KSPLIT = n caps the slices (1: off).
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int sms = device_sms(dev);
+        const int mt = (p.M + kBM - 1) / kBM, KB = (p.K + kBK - 1) / kBK;
+        // measured at M = 100: a win for K = 5120 (w2), a loss for K = 2048 (wo)
+        if (2 * mt * ((p.N + bn - 1) / bn) < sms && KB >= kTcSplitMinKB) {
+            // the last slice to finish sums the others: few slices and
+            // narrow tiles keep that sum short (one 32-column chunk per warp)
+            const int bw = env_tc_bn() ? env_tc_bn() : (p.N >= 4096 ? 128 : 64);
+            const int tiles = mt * ((p.N + bw - 1) / bw);
+            int ks = std::min(kTcMaxSplit, std::min(sms / tiles, KB / 4));
+            ks = (int)std::min<size_t>((size_t)ks, p.ws_floats / ((size_t)p.M * p.N));
+            const char *ev = getenv("VOX_CUDA_TC_KSPLIT");
+            if (ev && atoi(ev) >= 1) ks = std::min(ks, atoi(ev));
+            if (ks >= 2 && tiles * kEpiWarps <= kTcSplitCounters) {
+                bn = bw;
+                p.ksplit = ks;
+            }
+        }
+    }
 #define VC_TC_CASE(BN)                                                             \
     if (bn == BN) {                                                                \
         switch (epi) {                                                             \

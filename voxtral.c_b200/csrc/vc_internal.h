@@ -116,11 +116,20 @@ struct TcGemmParams {
     uint16_t *v_ring;
     int cap, pos0;           // row r sits at logical position pos0 + r, slot (pos0 + r) % cap
     unsigned *err;           // raised when a bounded wait expires
+    // split-K (few tiles, long K): the caller's fp32 workspace and zeroed
+    // counters; launch_tc_gemm picks the split count ksplit (1: none)
+    float *ws;               // >= ksplit * M * N floats
+    size_t ws_floats;
+    unsigned *ws_cnt;        // kTcSplitCounters counters, zero between launches
+    int ksplit;
     int f16;                 // A and W are fp16 (kind::f16 with fp16 operands) and so are the
                              //   16-bit outputs (out_bf16, SwiGLU h); else bf16
     int vec;                 // set by launch_tc_gemm: all destinations allow 16-byte stores
     int tma_out;             // set by launch_tc_gemm: the epilogue stores through TMA
 };
+
+constexpr int kTcSplitCounters = 4096;   // split-K tickets a caller provides (8 per tile)
+constexpr size_t kEncSplitFloats = (size_t)4 << 20;   // the encoder state's split-K workspace (16 MB)
 
 // C = A . W^T with bf16 A [M, K] and W [N, K] (row-major, 16-byte aligned,
 // K % 8 == 0).  bn = 0 picks the tile width.

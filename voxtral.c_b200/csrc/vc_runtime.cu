@@ -1603,6 +1603,8 @@ struct vox_cuda_enc_state {
     uint16_t *mid16 = nullptr;   // adapter: [Mx/4][3072] bf16 mid
     unsigned *err = nullptr;
     int *pos_dev = nullptr;      // logical position of the chunk's first row
+    float *split = nullptr;      // split-K partials of small-M GEMMs [kEncSplitFloats]
+    unsigned *split_cnt = nullptr;
     float *h_rope = nullptr;     // pinned [Mx][64]
     int *h_pos = nullptr;        // pinned
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;   // (rows, rope table?) -> step graph
@@ -1771,6 +1773,8 @@ extern "C" vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, in
     const size_t o_mid = take(Mx / 4 * kDecDim * 2);
     const size_t o_err = take(sizeof(unsigned));
     const size_t o_pos = take(sizeof(int));
+    const size_t o_split = take(kEncSplitFloats * 4);            // split-K partials
+    const size_t o_split_cnt = take(kTcSplitCounters * 4);       // split-K tickets
     s->ws_bytes = off;
     if (dev_alloc(c, (void **)&s->k_ring, s->ring_bytes) != cudaSuccess ||
         dev_alloc(c, (void **)&s->v_ring, s->ring_bytes) != cudaSuccess ||
@@ -1793,6 +1797,8 @@ extern "C" vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, in
     s->mid16 = (uint16_t *)(s->ws + o_mid);
     s->err = (unsigned *)(s->ws + o_err);
     s->pos_dev = (int *)(s->ws + o_pos);
+    s->split = (float *)(s->ws + o_split);
+    s->split_cnt = (unsigned *)(s->ws + o_split_cnt);
     if (cudaMemset(s->k_ring, 0, s->ring_bytes) != cudaSuccess ||
         cudaMemset(s->v_ring, 0, s->ring_bytes) != cudaSuccess ||
         cudaMemset(s->ws, 0, s->ws_bytes) != cudaSuccess) {
@@ -1864,6 +1870,9 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         p.cap = s->cap;
         p.err = s->err;
         p.f16 = 1;
+        p.ws = s->split;
+        p.ws_floats = kEncSplitFloats;
+        p.ws_cnt = s->split_cnt;
         VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_QKV_ENC, p, s->xn16, L.qkv, st, pdl));
         VC_EV_END();
@@ -1889,6 +1898,9 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         p.bias = L.bo;
         p.err = s->err;
         p.f16 = 1;
+        p.ws = s->split;
+        p.ws_floats = kEncSplitFloats;
+        p.ws_cnt = s->split_cnt;
         VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_RESID, p, s->att16, L.wo, st, pdl));
         VC_EV_END();
@@ -1903,6 +1915,9 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         p.ldo_bf16 = kEncHidden;
         p.err = s->err;
         p.f16 = 1;
+        p.ws = s->split;
+        p.ws_floats = kEncSplitFloats;
+        p.ws_cnt = s->split_cnt;
         VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_SWIGLU, p, s->xn16, L.w13, st, pdl));
         VC_EV_END();
@@ -1915,6 +1930,9 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         p.bias = L.b2;
         p.err = s->err;
         p.f16 = 1;
+        p.ws = s->split;
+        p.ws_floats = kEncSplitFloats;
+        p.ws_cnt = s->split_cnt;
         VC_EV_BEGIN();
         VC_TRY(launch_tc_gemm(TC_RESID, p, s->h16, L.w2, st, pdl));
         VC_EV_END();
@@ -2036,6 +2054,9 @@ extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc,
     p.ldo_bf16 = kDecDim;
     p.err = s->err;
     p.f16 = 1;
+    p.ws = s->split;
+    p.ws_floats = kEncSplitFloats;
+    p.ws_cnt = s->split_cnt;
     VC_TRY(launch_tc_gemm(TC_STORE, p, s->a16, e->adapter0, st, false));
     p = TcGemmParams{};
     p.M = rows;
@@ -2045,6 +2066,9 @@ extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc,
     p.ldo = kDecDim;
     p.err = s->err;
     p.f16 = 1;
+    p.ws = s->split;
+    p.ws_floats = kEncSplitFloats;
+    p.ws_cnt = s->split_cnt;
     VC_TRY(launch_tc_gemm(TC_STORE, p, s->mid16, e->adapter1, st, false));
     VC_TRY(cudaMemcpyAsync(out, s->aout, (size_t)rows * kDecDim * 4, cudaMemcpyDeviceToHost, st));
     return enc_err_check(s, st);
