@@ -293,6 +293,27 @@ int vox_cuda_encoder_profile(vox_cuda_enc_state *s, const float *x_dev, int new_
  * (vox_adapter_forward, voxtral_encoder.c:642-674). */
 int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc, int n, float *out);
 
+/* Conv stem: the encoder's two causal convolutions over the mel stream,
+ * conv0 (128 -> 1280, kernel 3, stride 1) and conv1 (1280 -> 1280, kernel 3,
+ * stride 2), each followed by GELU, with the streaming state of
+ * stream_conv_stem (voxtral.c:487-665; vox_causal_conv1d,
+ * voxtral_kernels.c:293-340).  Weights as vox_encoder_t holds them
+ * (voxtral.h:84-88): conv0 [1280, 128, 3], conv1 [1280, 1280, 3] fp32, biases
+ * [1280]; they are copied (as fp16) at creation.  max_mel bounds the mel
+ * frames of one step. */
+typedef struct vox_cuda_conv_stem vox_cuda_conv_stem;
+vox_cuda_conv_stem *vox_cuda_conv_stem_create(const float *conv0_weight, const float *conv0_bias,
+                                              const float *conv1_weight, const float *conv1_bias, int max_mel);
+void vox_cuda_conv_stem_free(vox_cuda_conv_stem *s);
+/* Start a new stream (the reference's conv_stem_initialized = 0). */
+int vox_cuda_conv_stem_reset(vox_cuda_conv_stem *s);
+/* n_new >= 1 mel frames, host [n_new, 128] row-major as the mel context
+ * yields them -> host out [rows, 1280] post-conv positions, the encoder's
+ * input; returns rows = floor((T + n_new) / 2) - floor(T / 2) for T frames
+ * consumed before (0 is possible), or a negative error.  out must hold
+ * n_new / 2 + 1 rows. */
+int vox_cuda_conv_stem_step(vox_cuda_conv_stem *s, const float *mel_new, int n_new, float *out);
+
 /* ------------------------------------------------------------------------
  * Kernel-level entry points (device pointers) - the decode attention and the
  * LM-head argmax on their own, for callers that compose their own step.

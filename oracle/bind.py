@@ -128,6 +128,12 @@ def ref_lib():
         lib.voxref_fill_alts.restype = C.c_int
         lib.voxref_decode_threads.argtypes = [C.c_void_p, C.c_int, C.c_int, _fp, _fp, _ip]
         lib.voxref_decode_threads.restype = C.c_double
+        lib.voxref_set_conv.argtypes = [C.c_void_p, _fp, _fp, _fp, _fp]
+        lib.voxref_stem_new.argtypes = [C.c_void_p]
+        lib.voxref_stem_new.restype = C.c_void_p
+        lib.voxref_stem_step.argtypes = [C.c_void_p, _fp, C.c_int, _fp]
+        lib.voxref_stem_step.restype = C.c_int
+        lib.voxref_stem_free.argtypes = [C.c_void_p]
         _ref = lib
     return _ref
 
@@ -211,6 +217,44 @@ def fill_alts(logits, best, n_alt, cutoff):
 # ---------------------------------------------------------------------------
 # synthetic decoder / encoder weights (reference layout, bf16 row-major)
 # ---------------------------------------------------------------------------
+
+MEL_BINS = 128
+
+
+class ConvStemWeights:
+    """The encoder's conv stem (voxtral.h:84-88): conv0 [1280, 128, 3] and
+    conv1 [1280, 1280, 3] fp32 with fp32 biases, seeded."""
+
+    def __init__(self, seed=0, std=0.02):
+        s = seed * 1000 + 60000
+        self.w0 = normal_f32((ENC_DIM, MEL_BINS, 3), s + 1, std)
+        self.b0 = normal_f32(ENC_DIM, s + 2, std)
+        self.w1 = normal_f32((ENC_DIM, ENC_DIM, 3), s + 3, std)
+        self.b1 = normal_f32(ENC_DIM, s + 4, std)
+
+
+class RefStem:
+    """The reference's stateful conv stem (stream_conv_stem) over a bare stream."""
+
+    def __init__(self, w: ConvStemWeights):
+        lib = ref_lib()
+        self.lib, self.w = lib, w
+        self.ctx = lib.voxref_ctx_new()
+        lib.voxref_set_conv(self.ctx, fptr(w.w0), fptr(w.b0), fptr(w.w1), fptr(w.b1))
+        self.st = lib.voxref_stem_new(self.ctx)
+
+    def step(self, mel):
+        mel = np.ascontiguousarray(mel, np.float32)
+        out = np.empty((mel.shape[0] // 2 + 2, ENC_DIM), np.float32)
+        n = self.lib.voxref_stem_step(self.st, fptr(mel), mel.shape[0], fptr(out))
+        return out[:n].copy()
+
+    def free(self):
+        if self.st:
+            self.lib.voxref_stem_free(self.st)
+            self.lib.voxref_ctx_free(self.ctx, 0)
+            self.st = None
+
 
 class DecoderWeights:
     """Decoder weights: `distinct` independent layer sets cycled over

@@ -270,3 +270,41 @@ double voxref_decode_threads(vox_ctx_t **ctxs, int n, int steps,
     free(th);
     return (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
 }
+
+/* ---- conv stem (stream_conv_stem, voxtral.c:487-665) on a bare stream ---- */
+
+/* conv0: [1280, 128, 3] + [1280]; conv1: [1280, 1280, 3] + [1280] (fp32, as
+ * vox_encoder_t holds them, voxtral.h:84-88). */
+void voxref_set_conv(vox_ctx_t *ctx, const float *w0, const float *b0, const float *w1, const float *b1) {
+    ctx->encoder.conv0_weight = (float *)w0;
+    ctx->encoder.conv0_bias = (float *)b0;
+    ctx->encoder.conv1_weight = (float *)w1;
+    ctx->encoder.conv1_bias = (float *)b1;
+}
+
+/* A stream with only the conv-stem state in use. */
+void *voxref_stem_new(vox_ctx_t *ctx) {
+    vox_stream_t *s = (vox_stream_t *)calloc(1, sizeof(vox_stream_t));
+    if (s) s->ctx = ctx;
+    return s;
+}
+
+/* n new mel frames [n][128] -> post-conv rows [len][1280] into out; returns len. */
+int voxref_stem_step(void *st, const float *mel_new, int n, float *out) {
+    int len = 0;
+    float *r = stream_conv_stem((vox_stream_t *)st, mel_new, n, &len);
+    if (r) {
+        memcpy(out, r, (size_t)len * VOX_ENC_DIM * sizeof(float));
+        free(r);
+    }
+    return len;
+}
+
+void voxref_stem_free(void *st) {
+    vox_stream_t *s = (vox_stream_t *)st;
+    if (!s) return;
+    free(s->mel_tail);
+    free(s->conv0_tail);
+    free(s->conv0_residual);
+    free(s);
+}

@@ -273,6 +273,28 @@ def gen_chain(w, ew):
     np.savez_compressed(os.path.join(HERE, "chain.npz"), **out)
 
 
+# Conv stem (stream_conv_stem, voxtral.c:487-665): mel chunks of odd and even
+# lengths, one frame, and a first chunk shorter than the kernel.
+STEM_CHUNKS = [2, 150, 37, 1, 200, 64, 5]
+
+
+def stem_chunks(seed=8201):
+    return [B.normal_f32((n, B.MEL_BINS), seed + i, 1.0) for i, n in enumerate(STEM_CHUNKS)]
+
+
+def gen_stem():
+    out = {}
+    w = B.ConvStemWeights(seed=DEC_SEED)
+    ref = B.RefStem(w)
+    for i, mel in enumerate(stem_chunks()):
+        y = ref.step(mel)
+        out[f"chunk{i}_rows"] = np.int32(y.shape[0])
+        if y.size:
+            pack(f"chunk{i}", y, out)
+    ref.free()
+    np.savez_compressed(os.path.join(HERE, "stem.npz"), **out)
+
+
 ALT_CASES = [(61, 3.0, 4, 0.999), (62, 0.5, 4, 0.5), (63, 8.0, 3, 0.99), (64, 1.0, 2, 0.9),
              (65, 0.01, 4, 0.999)]
 
@@ -291,6 +313,10 @@ def gen_alts():
 def main():
     assert B.ref_available(), "build oracle/_ref first (make -C oracle ref)"
     t = time.time()
+    if sys.argv[1:] == ["stem"]:   # only the conv stem
+        gen_stem()
+        print("stem", time.time() - t)
+        return
     if sys.argv[1:] == ["chain"]:   # only the end-to-end chain
         gen_chain(B.DecoderWeights(seed=DEC_SEED), B.EncoderWeights(seed=DEC_SEED))
         print("chain", time.time() - t)
@@ -299,6 +325,7 @@ def main():
     gen_rope(); print("rope", time.time() - t)
     gen_attention(); print("attention", time.time() - t)
     gen_alts(); print("alts", time.time() - t)
+    gen_stem(); print("stem", time.time() - t)
     w = B.DecoderWeights(seed=DEC_SEED)
     gen_decoder(w); print("decoder", time.time() - t)
     del w

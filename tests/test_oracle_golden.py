@@ -122,3 +122,47 @@ def test_encoder_chunks_and_adapter_match_reference():
         assert sampled_rel(y, g, f"chunk{i}") < 1e-4
     a = o.adapter(np.concatenate(outs[:2], axis=0)[:136])
     assert sampled_rel(a, g, "adapter136") < 1e-4
+
+
+def _gelu(v):
+    # tanh GELU (vox_gelu, voxtral_kernels.c:376-384)
+    return 0.5 * v * (1.0 + np.tanh(0.7978845608028654 * (v + 0.044715 * v ** 3)))
+
+
+def _stem_restated(w, chunks):
+    """The conv stem chunk by chunk (stream_conv_stem, voxtral.c:487-665),
+    restated as causal convs over the mel stream with two pieces of state:
+    the last two mel frames (after a one-frame chunk the older of the two is
+    zero: the reference rebuilds its tail as [0, frame], voxtral.c:519-524,
+    551-556) and the conv0 outputs by global frame index.  Chunk i yields
+    conv1 rows floor(T_i / 2) .. floor(T_{i+1} / 2) - 1."""
+    w0, w1 = w.w0.astype(np.float64), w.w1.astype(np.float64)
+    hist = np.zeros((2, w0.shape[1]))
+    c0 = {}
+    t, outs = 0, []
+    for mel in chunks:
+        n = mel.shape[0]
+        ext = np.concatenate([hist, mel.astype(np.float64)], axis=0)   # frames t-2 .. t+n-1
+        for r in range(n):
+            win = ext[r:r + 3]
+            c0[t + r] = _gelu(w.b0 + np.einsum("oik,ki->o", w0, win))
+        u0, u1 = t // 2, (t + n) // 2
+        rows = []
+        for u in range(u0, u1):
+            win = np.stack([c0[i] if i >= 0 else np.zeros(w1.shape[1]) for i in (2 * u - 1, 2 * u, 2 * u + 1)])
+            rows.append(_gelu(w.b1 + np.einsum("oik,ki->o", w1, win)))
+        outs.append(np.array(rows).reshape(-1, w1.shape[0]))
+        hist = ext[-2:].copy() if n >= 2 else np.stack([np.zeros(w0.shape[1]), ext[-1]])
+        t += n
+    return outs
+
+
+def test_conv_stem_matches_reference_golden():
+    g = load_golden("stem")
+    w = B.ConvStemWeights(seed=G.DEC_SEED)
+    outs = _stem_restated(w, G.stem_chunks())
+    for i, y in enumerate(outs):
+        assert int(g[f"chunk{i}_rows"]) == y.shape[0]
+        if y.size:
+            idx, val, _, _ = unpack(g, f"chunk{i}")
+            assert B.rel_l2(y.reshape(-1)[idx], val) < 1e-5, i

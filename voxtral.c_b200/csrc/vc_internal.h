@@ -171,6 +171,14 @@ cudaError_t launch_rows_rmsnorm(float *x, int M, int K, const float *w, cudaStre
 cudaError_t launch_enc_rope_table(float *tab, int ld, int M, const float *src, const int *pos0_dev,
                                   const float *inv_freq, cudaStream_t st, bool pdl);
 
+// ---- conv stem (vc_stem.cu) ----
+cudaError_t launch_stem_im2col0(const float *mel_new, const float *mel_hist, int n, uint16_t *a0, cudaStream_t st);
+cudaError_t launch_stem_im2col1(const uint16_t *c0_new, const uint16_t *c0_hist, long long f0, long long u0,
+                                int n_out, uint16_t *a1, cudaStream_t st);
+cudaError_t launch_stem_state(const float *mel_new, int n, float *mel_hist, const uint16_t *c0_new,
+                              uint16_t *c0_hist, cudaStream_t st);
+cudaError_t launch_f32_to_f16(const float *src, uint16_t *dst, size_t n, cudaStream_t st);
+
 // Set the message vox_cuda_last_error() returns on the calling thread.
 void set_last_error(const char *fmt, ...);
 

@@ -2123,3 +2123,165 @@ extern "C" int vox_cuda_encoder_profile(vox_cuda_enc_state *s, const float *x_de
     for (int i = 0; i < VOX_CUDA_EPROF_PHASES; i++) ms[i] = (float)(acc[i] / iters);
     return VOX_CUDA_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Conv stem (stream_conv_stem, voxtral.c:487-665): im2col + tcgen05 GEMM
+// with bias + GELU, twice, with the streaming state on the device.
+// ---------------------------------------------------------------------------
+
+struct vox_cuda_conv_stem {
+    int device = 0;
+    int max_mel = 0;
+    long long frames = 0;           // mel frames consumed so far
+    uint16_t *w0 = nullptr;         // fp16 [1280][384]
+    uint16_t *w1 = nullptr;         // fp16 [1280][3840]
+    float *b0 = nullptr, *b1 = nullptr;
+    char *ws = nullptr;             // workspace block
+    size_t ws_bytes = 0;
+    float *mel = nullptr;           // [max_mel][128] this chunk's frames
+    float *mel_hist = nullptr;      // [2][128]
+    uint16_t *c0_hist = nullptr;    // [2][1280] conv0 outputs of the last two frames
+    uint16_t *a0 = nullptr;         // [max_mel][384] conv0 im2col
+    uint16_t *c0 = nullptr;         // [max_mel][1280] conv0 outputs (fp16)
+    uint16_t *a1 = nullptr;         // [max_out][3840] conv1 im2col
+    float *out = nullptr;           // [max_out][1280]
+    unsigned *err = nullptr;
+};
+
+extern "C" vox_cuda_conv_stem *vox_cuda_conv_stem_create(const float *conv0_weight, const float *conv0_bias,
+                                                         const float *conv1_weight, const float *conv1_bias,
+                                                         int max_mel) {
+    DevCtx *c = cur_ctx();
+    if (!c) return nullptr;
+    if (!conv0_weight || !conv0_bias || !conv1_weight || !conv1_bias || max_mel <= 0 || max_mel > 1 << 20) {
+        set_error("conv_stem_create: bad arguments");
+        return nullptr;
+    }
+    vox_cuda_conv_stem *s = new vox_cuda_conv_stem();
+    s->device = c->device;
+    s->max_mel = max_mel;
+    const size_t Mx = (size_t)max_mel, Ox = Mx / 2 + 2;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const size_t n_w0 = (size_t)kEncDim * 3 * 128, n_w1 = (size_t)kEncDim * 3 * kEncDim;
+    const size_t o_w0 = take(n_w0 * 2), o_w1 = take(n_w1 * 2), o_b0 = take(kEncDim * 4), o_b1 = take(kEncDim * 4);
+    const size_t o_stage = take(n_w1 * 4);   // fp32 staging of a weight before conversion
+    const size_t o_mel = take(Mx * 128 * 4), o_mh = take(2 * 128 * 4), o_ch = take(2 * kEncDim * 2);
+    const size_t o_a0 = take(Mx * 3 * 128 * 2), o_c0 = take(Mx * kEncDim * 2);
+    const size_t o_a1 = take(Ox * 3 * kEncDim * 2), o_out = take(Ox * kEncDim * 4), o_err = take(4);
+    s->ws_bytes = off;
+    if (dev_alloc(c, (void **)&s->ws, s->ws_bytes) != cudaSuccess) {
+        set_error("conv_stem_create: allocation of %zu bytes failed", s->ws_bytes);
+        delete s;
+        return nullptr;
+    }
+    s->w0 = (uint16_t *)(s->ws + o_w0);
+    s->w1 = (uint16_t *)(s->ws + o_w1);
+    s->b0 = (float *)(s->ws + o_b0);
+    s->b1 = (float *)(s->ws + o_b1);
+    s->mel = (float *)(s->ws + o_mel);
+    s->mel_hist = (float *)(s->ws + o_mh);
+    s->c0_hist = (uint16_t *)(s->ws + o_ch);
+    s->a0 = (uint16_t *)(s->ws + o_a0);
+    s->c0 = (uint16_t *)(s->ws + o_c0);
+    s->a1 = (uint16_t *)(s->ws + o_a1);
+    s->out = (float *)(s->ws + o_out);
+    s->err = (unsigned *)(s->ws + o_err);
+    float *stage = (float *)(s->ws + o_stage);
+    bool ok = cudaMemset(s->ws, 0, s->ws_bytes) == cudaSuccess &&
+              cudaMemcpy(stage, conv0_weight, n_w0 * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              launch_f32_to_f16(stage, s->w0, n_w0, 0) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+              cudaMemcpy(stage, conv1_weight, n_w1 * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              launch_f32_to_f16(stage, s->w1, n_w1, 0) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+              cudaMemcpy(s->b0, conv0_bias, kEncDim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(s->b1, conv1_bias, kEncDim * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+    if (!ok) {
+        set_error("conv_stem_create: weight upload failed");
+        vox_cuda_conv_stem_free(s);
+        return nullptr;
+    }
+    return s;
+}
+
+extern "C" void vox_cuda_conv_stem_free(vox_cuda_conv_stem *s) {
+    if (!s) return;
+    DevCtx *c = ctx_for(s->device);
+    cudaSetDevice(s->device);
+    if (c) {
+        cudaStreamSynchronize(c->stream);
+        dev_free(c, s->ws, s->ws ? s->ws_bytes : 0);
+    }
+    delete s;
+}
+
+extern "C" int vox_cuda_conv_stem_reset(vox_cuda_conv_stem *s) {
+    if (!s) return VOX_CUDA_ERR_ARG;
+    DevCtx *c = ctx_for(s->device);
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(s->device);
+    VC_TRY(cudaMemsetAsync(s->mel_hist, 0, 2 * 128 * 4, c->stream));
+    VC_TRY(cudaMemsetAsync(s->c0_hist, 0, 2 * kEncDim * 2, c->stream));
+    VC_TRY(cudaStreamSynchronize(c->stream));
+    s->frames = 0;
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_conv_stem_step(vox_cuda_conv_stem *s, const float *mel_new, int n_new, float *out) {
+    if (!s || !mel_new || !out || n_new <= 0) {
+        set_error("conv_stem_step: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (n_new > s->max_mel) {
+        set_error("conv_stem_step: %d mel frames exceed the state's %d", n_new, s->max_mel);
+        return VOX_CUDA_ERR_CAPACITY;
+    }
+    DevCtx *c = ctx_for(s->device);
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(s->device);
+    std::lock_guard<std::mutex> lk(c->mu);
+    cudaStream_t st = c->stream;
+    const long long f0 = s->frames, u0 = f0 / 2;
+    const int n_out = (int)((f0 + n_new) / 2 - u0);
+    VC_TRY(cudaMemcpyAsync(s->mel, mel_new, (size_t)n_new * 128 * 4, cudaMemcpyHostToDevice, st));
+    VC_TRY(launch_stem_im2col0(s->mel, s->mel_hist, n_new, s->a0, st));
+    TcGemmParams p = {};
+    p.M = n_new;
+    p.N = kEncDim;
+    p.K = 3 * 128;
+    p.bias = s->b0;
+    p.act = 1;                 // GELU (voxtral.c:515)
+    p.out_bf16 = s->c0;        // fp16: the conv1 im2col's source
+    p.ldo_bf16 = kEncDim;
+    p.err = s->err;
+    p.f16 = 1;
+    VC_TRY(launch_tc_gemm(TC_STORE, p, s->a0, s->w0, st, false));
+    if (n_out > 0) {
+        VC_TRY(launch_stem_im2col1(s->c0, s->c0_hist, f0, u0, n_out, s->a1, st));
+        p = TcGemmParams{};
+        p.M = n_out;
+        p.N = kEncDim;
+        p.K = 3 * kEncDim;
+        p.bias = s->b1;
+        p.act = 1;             // GELU (voxtral.c:648)
+        p.out = s->out;
+        p.ldo = kEncDim;
+        p.err = s->err;
+        p.f16 = 1;
+        VC_TRY(launch_tc_gemm(TC_STORE, p, s->a1, s->w1, st, false));
+        VC_TRY(cudaMemcpyAsync(out, s->out, (size_t)n_out * kEncDim * 4, cudaMemcpyDeviceToHost, st));
+    }
+    VC_TRY(launch_stem_state(s->mel, n_new, s->mel_hist, s->c0, s->c0_hist, st));
+    unsigned h_err = 0;
+    VC_TRY(cudaMemcpyAsync(&h_err, s->err, 4, cudaMemcpyDeviceToHost, st));
+    VC_TRY(cudaStreamSynchronize(st));
+    if (h_err) {
+        set_error("conv_stem_step: a tensor-core GEMM wait timed out");
+        return VOX_CUDA_ERR_CUDA;
+    }
+    s->frames += n_new;
+    return n_out;
+}

@@ -115,6 +115,10 @@ def lib():
         "vox_cuda_enc_state_set_position": ([C.c_void_p, C.c_int], C.c_int),
         "vox_cuda_encoder_profile": ([C.c_void_p, C.c_void_p, C.c_int, C.c_int, _fp], C.c_int),
         "vox_cuda_adapter_forward": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
+        "vox_cuda_conv_stem_create": ([_fp, _fp, _fp, _fp, C.c_int], C.c_void_p),
+        "vox_cuda_conv_stem_free": ([C.c_void_p], None),
+        "vox_cuda_conv_stem_reset": ([C.c_void_p], C.c_int),
+        "vox_cuda_conv_stem_step": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
         "vox_cuda_attention_decode_dev": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                            C.c_void_p, C.c_void_p], C.c_int),
         "vox_cuda_attention_decode_noalloc": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
@@ -366,4 +370,29 @@ class EncState:
     def free(self):
         if self.h:
             lib().vox_cuda_enc_state_free(self.h)
+            self.h = None
+
+
+class ConvStem:
+    """The encoder's conv stem with its streaming state
+    (vox_cuda_conv_stem_*): mel chunks [n, 128] -> post-conv rows [*, 1280]."""
+
+    def __init__(self, w0, b0, w1, b1, max_mel=3000):
+        self._keep = [np.ascontiguousarray(a, np.float32) for a in (w0, b0, w1, b1)]
+        self.h = lib().vox_cuda_conv_stem_create(*[_f(a) for a in self._keep], max_mel)
+        if not self.h:
+            raise VoxCudaError("conv_stem_create: " + last_error())
+
+    def step(self, mel):
+        mel = np.ascontiguousarray(mel, np.float32)
+        out = np.empty((mel.shape[0] // 2 + 1, 1280), np.float32)
+        n = check(lib().vox_cuda_conv_stem_step(self.h, _f(mel), mel.shape[0], _f(out)), "conv_stem_step")
+        return out[:n]
+
+    def reset(self):
+        check(lib().vox_cuda_conv_stem_reset(self.h), "conv_stem_reset")
+
+    def free(self):
+        if self.h:
+            lib().vox_cuda_conv_stem_free(self.h)
             self.h = None
