@@ -303,7 +303,9 @@ def encoder_bench(V, torch, steps, only_rows=0):
     of earlier context, plus the per-phase profile at M = 1500."""
     enc = build_device_encoder(V, torch)
     st = enc.state(max_chunk=1500)
-    stream = torch.cuda.current_stream()
+    # a dedicated stream: step_dev is asynchronous, and the legacy default
+    # stream's handle (0) would mean "the library's own stream"
+    stream = torch.cuda.Stream()
     out = {"audio_s_per_s": {}, "ms_per_chunk": {}}
     gen = torch.Generator(device="cuda")
     gen.manual_seed(77)
@@ -326,6 +328,8 @@ def encoder_bench(V, torch, steps, only_rows=0):
         ms = e0.elapsed_time(e1) / n
         out["ms_per_chunk"][f"M{M}"] = ms
         out["audio_s_per_s"][f"M{M}"] = (M / 50.0) / (ms / 1000.0)
+    if not only_rows:
+        out["multi_stream_M100"] = multi_stream_encoder(enc, torch, x0, steps)
     if only_rows and only_rows != 1500:
         st.free()
         enc.free()
@@ -347,6 +351,48 @@ def encoder_bench(V, torch, steps, only_rows=0):
     st.free()
     enc.free()
     return out
+
+
+def multi_stream_encoder(enc, torch, x0, steps, streams=8, rows=100):
+    """configs[4]'s encoder load: `streams` streams each feeding a 2 s chunk
+    (100 rows) with a full window behind it, every stream on its own CUDA
+    stream (vox_cuda_encoder_step_dev per state; weights shared), against the
+    same chunks run one after another on one stream."""
+    states = [enc.state(max_chunk=rows) for _ in range(streams)]
+    cstreams = [torch.cuda.Stream() for _ in range(streams)]
+    xs = [torch.empty((rows, ENC_D), dtype=torch.float32, device="cuda") for _ in range(streams)]
+    main = torch.cuda.Stream()
+
+    def round_(concurrent):
+        for i, (st, x) in enumerate(zip(states, xs)):
+            st.set_position(750)
+            x.copy_(x0[i * 10:i * 10 + rows])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(main)
+        for st, x, cs in zip(states, xs, cstreams):
+            s = cs if concurrent else main
+            if concurrent:
+                s.wait_event(e0)
+            st.step_dev(x.data_ptr(), rows, s.cuda_stream)
+        if concurrent:
+            for cs in cstreams:
+                main.wait_stream(cs)
+        e1.record(main)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    res = {}
+    for concurrent in (False, True):
+        for _ in range(2):
+            round_(concurrent)
+        ms = sorted(round_(concurrent) for _ in range(max(3, steps // 2)))[0]
+        key = "concurrent" if concurrent else "serial"
+        res[key] = {"ms_per_round": ms, "audio_s_per_s": streams * rows / 50.0 / (ms / 1000.0)}
+    res["streams"], res["rows_per_chunk"] = streams, rows
+    for st in states:
+        st.free()
+    return res
 
 
 def bf16_peaks():
@@ -395,7 +441,7 @@ def our_arm(args):
     gen.manual_seed(1234 + rank)
     embeds = torch.randn((S, D), generator=gen, device="cuda", dtype=torch.float32)
     tokens = torch.zeros(S, dtype=torch.int32, device="cuda")
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()   # the library's step_dev calls do not synchronise the host
     sp = stream.cuda_stream
 
     def reset_positions():

@@ -195,7 +195,12 @@ int vox_cuda_decoder_step_batch(vox_cuda_dec_state *const *states, int n, const 
 
 /* Device-resident form of the batched step for callers that keep the
  * embeddings on the device: embeds_dev [n, 3072], tokens_dev [n] (int32),
- * enqueued on `stream`; nothing is copied to or from the host. */
+ * enqueued on `stream` (NULL: the library's stream) without waiting for it,
+ * so the host prepares step k + 1 while step k runs; tokens_dev is valid once
+ * `stream` reaches this call's work.  Only the slot and RoPE tables (a few
+ * hundred bytes) cross from the host.  A device-side wait that timed out is
+ * reported by a later call.  Every synchronous entry point of the decoder and
+ * its states is ordered after the pending asynchronous steps. */
 int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states, int n,
                                     const float *embeds_dev, int *tokens_dev, void *stream);
 
@@ -266,10 +271,15 @@ int vox_cuda_enc_state_position(const vox_cuda_enc_state *s);
  * w2 (+bias) + residual, then the final norm (vox_encoder_forward_incremental,
  * voxtral_encoder.c:452-636; vox_metal_encoder_full_step, voxtral_metal.h:245).
  * rope_freqs: host [new_len][32][2] or NULL.  GEMM activations are rounded to
- * bf16 and attention runs in fp16 with fp32 accumulation. */
+ * fp16 and attention runs in fp16 with fp32 accumulation. */
 int vox_cuda_encoder_full_step(vox_cuda_enc_state *s, float *x, int new_len, const float *rope_freqs);
 
-/* Device-resident form: x_dev [new_len, 1280] on the device, in place. */
+/* Device-resident form: x_dev [new_len, 1280] on the device, in place,
+ * enqueued on `stream` (NULL: the library's stream) without waiting for it,
+ * so several states (streams of audio) can run concurrently on their own
+ * CUDA streams.  A device-side wait that timed out is reported by the next
+ * call on the same state.  No counterpart in the reference (its encoder is
+ * synchronous on the host). */
 int vox_cuda_encoder_step_dev(vox_cuda_enc_state *s, float *x_dev, int new_len, void *stream);
 
 /* Set the logical position of the next chunk's first row (resume, tests). */

@@ -259,3 +259,43 @@ def test_batched_step_matches_single_streams_and_oracle(small_w):
     for st in batch_states + single_states:
         st.free()
     d.free()
+
+
+def test_async_batched_steps_match_sync_batched_steps(small_w):
+    """vox_cuda_decoder_step_batch_dev enqueues without waiting for the step:
+    steps issued back to back on a side stream give the tokens of the
+    synchronous host-pointer steps, each step's tokens land in its own device
+    buffer, and a synchronous ring read right after the last call sees every
+    asynchronous step's K/V rows."""
+    import torch
+    d = make_gpu_decoder(small_w)
+    n, steps = 3, 6
+    prompts = [B.normal_f32((4 + i, B.DEC_DIM), 700 + i) for i in range(n)]
+    sync_states, async_states = [], []
+    for i in range(n):
+        for lst in (sync_states, async_states):
+            st = d.state(kv_cap=64)
+            st.prefill(prompts[i])
+            lst.append(st)
+    embeds = [B.normal_f32((n, B.DEC_DIM), 800 + s) for s in range(steps)]
+    want = [V.step_batch(sync_states, e) for e in embeds]
+    stream = torch.cuda.Stream()
+    dev_embeds = [torch.from_numpy(e).cuda() for e in embeds]
+    dev_tokens = [torch.zeros(n, dtype=torch.int32, device="cuda") for _ in range(steps)]
+    torch.cuda.synchronize()
+    for e, t in zip(dev_embeds, dev_tokens):
+        V.step_batch_dev(async_states, e.data_ptr(), t.data_ptr(), stream.cuda_stream)
+    # no host wait here: the ring read orders itself after the pending steps
+    for i in range(n):
+        last = 4 + i + steps - 1
+        ka, va = async_states[i].read_kv(small_w.n_layers - 1, last - steps + 1, steps)
+        ks, vs = sync_states[i].read_kv(small_w.n_layers - 1, last - steps + 1, steps)
+        assert np.array_equal(ka, ks) and np.array_equal(va, vs), i
+    stream.synchronize()
+    for s in range(steps):
+        assert np.array_equal(dev_tokens[s].cpu().numpy(), want[s]), s
+    for i in range(n):
+        assert async_states[i].position == sync_states[i].position
+    for st in sync_states + async_states:
+        st.free()
+    d.free()

@@ -127,6 +127,31 @@ def test_encoder_split_k_matches_unsplit(monkeypatch):
         assert B.rel_l2(a, b) < 2e-3, (i, B.rel_l2(a, b))
 
 
+def test_encoder_async_steps_match_sync_steps():
+    """vox_cuda_encoder_step_dev enqueues without waiting: chunks issued back
+    to back (positions travel by value) equal the synchronous host-pointer
+    steps."""
+    import torch
+    ew = B.EncoderWeights(seed=11, n_layers=2, distinct=2, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    chunks = [B.normal_f32((n, B.ENC_DIM), 1030 + i) for i, n in enumerate([100, 37, 256, 90])]
+    sa = e.state(max_chunk=256)
+    ref = [sa.step(x) for x in chunks]
+    sb = e.state(max_chunk=256)
+    stream = torch.cuda.Stream()
+    devs = [torch.from_numpy(x).cuda() for x in chunks]
+    torch.cuda.synchronize()
+    for d in devs:
+        sb.step_dev(d.data_ptr(), d.shape[0], stream.cuda_stream)
+    stream.synchronize()
+    for d, r in zip(devs, ref):
+        assert np.array_equal(d.cpu().numpy(), r)
+    assert sb.position == sa.position == sum(x.shape[0] for x in chunks)
+    sa.free()
+    sb.free()
+    e.free()
+
+
 def test_encoder_host_rope_table_matches_device_table():
     """vox_cuda_encoder_full_step with the host's RoPE table (the reference
     API passes rope_freqs) and with the table computed on the device.  The two

@@ -308,6 +308,13 @@ cudaError_t launch_enc_rope_table(float *tab, int ld, int M, const float *src, c
     return cudaLaunchKernelEx(&cfg, enc_rope_table_kernel, tab, ld, M, src, pos0_dev, inv_freq);
 }
 
+__global__ void set_int_kernel(int *dst, int v) { *dst = v; }
+
+cudaError_t launch_set_int(int *dst, int v, cudaStream_t st) {
+    set_int_kernel<<<1, 1, 0, st>>>(dst, v);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_rows_rmsnorm(float *x, int M, int K, const float *w, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((M + 7) / 8);

@@ -164,6 +164,8 @@ bool enc_attn_tc_supported(const EncAttnParams &p);
 cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl);
 constexpr int kEncRingAlign = 128;   // encoder ring capacities are multiples of this
 cudaError_t launch_rows_rmsnorm(float *x, int M, int K, const float *w, cudaStream_t st, bool pdl);
+// *dst = v in stream order (the value travels as a kernel argument)
+cudaError_t launch_set_int(int *dst, int v, cudaStream_t st);
 // RoPE planes of a chunk for the q|k epilogue: tab[d][row] = cos and
 // tab[32 + d][row] = sin (row stride ld) of the angle of logical position
 // *pos0_dev + row, taken from the host table src[row][32] (cos, sin) pairs

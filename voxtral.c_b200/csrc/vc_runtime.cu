@@ -692,6 +692,12 @@ struct StepWork {
     // host (pinned)
     char *hblock = nullptr;
     int *h_tokens = nullptr;
+    // asynchronous steps (step_batch_dev): the host block's upload and the
+    // error word's copy back, each behind an event
+    cudaEvent_t staged = nullptr;
+    cudaEvent_t err_ev = nullptr;
+    bool staged_pending = false;
+    bool err_pending = false;
     // graphs: [0] layers only (prefill), [1] layers + LM head
     cudaGraphExec_t graph[2] = {nullptr, nullptr};
 };
@@ -709,6 +715,8 @@ struct vox_cuda_decoder {
     StepWork *batch_work[kMaxBatch + 1] = {};
     std::mutex mu;   // serialises batched steps (they share batch_work)
     bool pdl = true;
+    cudaEvent_t tail = nullptr;   // the end of the last asynchronous step
+    bool tail_set = false;
 };
 
 struct vox_cuda_dec_state {
@@ -731,6 +739,8 @@ void free_work(DevCtx *c, StepWork *w) {
     if (!w) return;
     for (auto &g : w->graph)
         if (g) cudaGraphExecDestroy(g);
+    if (w->staged) cudaEventDestroy(w->staged);
+    if (w->err_ev) cudaEventDestroy(w->err_ev);
     if (w->dblock) cudaFree(w->dblock);
     if (w->hblock) cudaFreeHost(w->hblock);
     if (c) {
@@ -806,12 +816,15 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     if (cudaMemset(b + o_frag0, 0, frag_bytes) != cudaSuccess ||
         cudaMemset(w->tokens, 0, sizeof(int) * (n + 1)) != cudaSuccess ||
         cudaMemset(w->counters, 0, sizeof(unsigned) * (n * kDecKvHeads + 1)) != cudaSuccess ||
-        cudaHostAlloc((void **)&w->hblock, align_up(w->dblock_bytes, 16) + sizeof(int) * (n + 1), cudaHostAllocDefault) != cudaSuccess) {
+        cudaHostAlloc((void **)&w->hblock, align_up(w->dblock_bytes, 16) + sizeof(int) * (n + 1), cudaHostAllocDefault) != cudaSuccess ||
+        cudaEventCreateWithFlags(&w->staged, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&w->err_ev, cudaEventDisableTiming) != cudaSuccess) {
         set_error("decoder workspace: staging allocation failed");
         free_work(c, w);
         return nullptr;
     }
     w->h_tokens = (int *)(w->hblock + align_up(w->dblock_bytes, 16));
+    w->h_tokens[n] = 0;
     return w;
 }
 
@@ -1140,8 +1153,9 @@ extern "C" void vox_cuda_decoder_free(vox_cuda_decoder *d) {
     if (!d) return;
     DevCtx *c = ctx_for(d->device);
     cudaSetDevice(d->device);
-    if (c) cudaStreamSynchronize(c->stream);
+    if (c) cudaStreamSynchronize(c->stream);   // also waits for asynchronous steps (see step_batch_dev)
     for (int i = 0; i <= kMaxBatch; i++) free_work(c, d->batch_work[i]);
+    if (d->tail) cudaEventDestroy(d->tail);
     for (auto &pr : d->owned)
         if (c) dev_free(c, pr.first, pr.second);
         else cudaFree(pr.first);
@@ -1230,6 +1244,8 @@ static int ring_copy(vox_cuda_dec_state *s, int layer, int first_pos, int n_rows
     int rc = kv_rows_check(s, layer, first_pos, n_rows);
     if (rc) return rc;
     cudaSetDevice(s->dec->device);
+    // the library stream is ordered after pending asynchronous steps, which write the ring
+    if (DevCtx *c = ctx_for(s->dec->device)) VC_TRY(cudaStreamSynchronize(c->stream));
     const size_t row = (size_t)kKvDim * sizeof(float);
     int done = 0;
     while (done < n_rows) {
@@ -1387,6 +1403,11 @@ static int batch_prepare(vox_cuda_dec_state *const *states, int n, vox_cuda_deco
     if (!d->batch_work[n]) d->batch_work[n] = make_work(c, n, d->vocab);
     if (!d->batch_work[n]) return VOX_CUDA_ERR_OOM;
     StepWork *w = d->batch_work[n];
+    // an asynchronous step's upload of the host block may still be queued
+    if (w->staged_pending) {
+        VC_TRY(cudaEventSynchronize(w->staged));
+        w->staged_pending = false;
+    }
     for (int i = 0; i < n; i++) {
         fill_slot(states[i], states[i]->pos, h_slots(w) + i);
         host_rope_table(states[i]->pos, kHeadDim, h_rope(w) + i * kHeadDim);
@@ -1411,6 +1432,7 @@ extern "C" int vox_cuda_decoder_step_batch(vox_cuda_dec_state *const *states, in
     StepWork *w = d->batch_work[n];
     memcpy(h_x(w), embeds, (size_t)n * kDecDim * sizeof(float));
     rc = run_step(d, c, w, true, c->stream, true);
+    w->err_pending = false;   // this step's error check covered the earlier ones
     if (rc) return rc;
     for (int i = 0; i < n; i++) {
         tokens[i] = w->h_tokens[i];
@@ -1439,9 +1461,23 @@ extern "C" int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states
     if (rc) return rc;
     StepWork *w = d->batch_work[n];
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    // a timeout raised by an earlier asynchronous step (its error word was
+    // copied back behind err_ev) is reported now
+    if (w->err_pending && cudaEventQuery(w->err_ev) == cudaSuccess) {
+        w->err_pending = false;
+        if ((rc = check_step_error(w, st))) return rc;
+    }
+    if (!d->tail && cudaEventCreateWithFlags(&d->tail, cudaEventDisableTiming) != cudaSuccess) {
+        set_error("decoder_step_batch_dev: event creation failed");
+        return VOX_CUDA_ERR_CUDA;
+    }
+    // the previous asynchronous step may have run on another stream
+    if (d->tail_set && st != c->stream) VC_TRY(cudaStreamWaitEvent(st, d->tail, 0));
     // slots + rope tables from the host block; the embeddings from the device
     const size_t head = (char *)w->x - w->dblock;
     VC_TRY(cudaMemcpyAsync(w->dblock, w->hblock, head, cudaMemcpyHostToDevice, st));
+    VC_TRY(cudaEventRecord(w->staged, st));
+    w->staged_pending = true;
     VC_TRY(cudaMemcpyAsync(w->x, embeds_dev, (size_t)n * kDecDim * 4, cudaMemcpyDeviceToDevice, st));
     cudaGraphExec_t &g = w->graph[1];
     if (!g) {
@@ -1460,10 +1496,16 @@ extern "C" int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states
     }
     VC_TRY(cudaGraphLaunch(g, st));
     VC_TRY(cudaMemcpyAsync(tokens_dev, w->tokens, sizeof(int) * n, cudaMemcpyDeviceToDevice, st));
-    VC_TRY(cudaMemcpyAsync(w->h_tokens, w->tokens, sizeof(int) * (n + 1), cudaMemcpyDeviceToHost, st));
-    // the host staging block is reused by the next call: wait for the step
-    VC_TRY(cudaStreamSynchronize(st));
-    if ((rc = check_step_error(w, st))) return rc;
+    if (!w->err_pending) {   // one error-word copy in flight at a time
+        VC_TRY(cudaMemcpyAsync(w->h_tokens + n, w->err, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+        VC_TRY(cudaEventRecord(w->err_ev, st));
+        w->err_pending = true;
+    }
+    // order the library stream (every synchronous entry point, the frees)
+    // after this step, without a host wait
+    VC_TRY(cudaEventRecord(d->tail, st));
+    if (st != c->stream) VC_TRY(cudaStreamWaitEvent(c->stream, d->tail, 0));
+    d->tail_set = true;
     for (int i = 0; i < n; i++) {
         states[i]->pos += 1;
         states[i]->have_logits = false;
@@ -1607,6 +1649,11 @@ struct vox_cuda_enc_state {
     unsigned *split_cnt = nullptr;
     float *h_rope = nullptr;     // pinned [Mx][64]
     int *h_pos = nullptr;        // pinned
+    unsigned *h_err = nullptr;   // pinned: the error flag as of the last asynchronous step
+    cudaEvent_t err_ev = nullptr;
+    bool err_pending = false;
+    cudaEvent_t tail = nullptr;  // the end of the last asynchronous step
+    bool tail_set = false;
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;   // (rows, rope table?) -> step graph
 };
 
@@ -1780,11 +1827,15 @@ extern "C" vox_cuda_enc_state *vox_cuda_enc_state_create(vox_cuda_encoder *e, in
         dev_alloc(c, (void **)&s->v_ring, s->ring_bytes) != cudaSuccess ||
         dev_alloc(c, (void **)&s->ws, s->ws_bytes) != cudaSuccess ||
         cudaHostAlloc((void **)&s->h_rope, Mx * kEncHeadDim * 4, cudaHostAllocDefault) != cudaSuccess ||
-        cudaHostAlloc((void **)&s->h_pos, sizeof(int), cudaHostAllocDefault) != cudaSuccess) {
+        cudaHostAlloc((void **)&s->h_pos, sizeof(int), cudaHostAllocDefault) != cudaSuccess ||
+        cudaHostAlloc((void **)&s->h_err, sizeof(unsigned), cudaHostAllocDefault) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s->err_ev, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s->tail, cudaEventDisableTiming) != cudaSuccess) {
         set_error("enc_state_create: allocation failed");
         vox_cuda_enc_state_free(s);
         return nullptr;
     }
+    *s->h_err = 0;
     s->x = (float *)(s->ws + o_x);
     s->xn16 = (uint16_t *)(s->ws + o_xn);
     s->att16 = (uint16_t *)(s->ws + o_att);
@@ -1813,7 +1864,7 @@ extern "C" void vox_cuda_enc_state_free(vox_cuda_enc_state *s) {
     if (!s) return;
     DevCtx *c = ctx_for(s->enc->device);
     cudaSetDevice(s->enc->device);
-    if (c) cudaStreamSynchronize(c->stream);
+    if (c) cudaStreamSynchronize(c->stream);   // also waits for asynchronous steps (see step_dev)
     if (c) {
         dev_free(c, s->k_ring, s->k_ring ? s->ring_bytes : 0);
         dev_free(c, s->v_ring, s->v_ring ? s->ring_bytes : 0);
@@ -1821,6 +1872,9 @@ extern "C" void vox_cuda_enc_state_free(vox_cuda_enc_state *s) {
     }
     if (s->h_rope) cudaFreeHost(s->h_rope);
     if (s->h_pos) cudaFreeHost(s->h_pos);
+    if (s->h_err) cudaFreeHost(s->h_err);
+    if (s->err_ev) cudaEventDestroy(s->err_ev);
+    if (s->tail) cudaEventDestroy(s->tail);
     for (auto &kv : s->graphs) cudaGraphExecDestroy(kv.second);
     delete s;
 }
@@ -1948,8 +2002,8 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
 // Upload the chunk position, then replay (capturing on first use) the
 // encoder graph for this chunk shape.
 int run_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st) {
-    *s->h_pos = s->pos;
-    VC_TRY(cudaMemcpyAsync(s->pos_dev, s->h_pos, sizeof(int), cudaMemcpyHostToDevice, st));
+    // the position by value: back-to-back asynchronous calls cannot race on it
+    VC_TRY(launch_set_int(s->pos_dev, s->pos, st));
     cudaGraphExec_t &g = s->graphs[std::make_pair(M, table ? 1 : 0)];
     if (!g) {
         cudaGraph_t graph = nullptr;
@@ -1987,6 +2041,7 @@ int enc_err_check(vox_cuda_enc_state *s, cudaStream_t st) {
     unsigned err = 0;
     VC_TRY(cudaMemcpyAsync(&err, s->err, sizeof(err), cudaMemcpyDeviceToHost, st));
     VC_TRY(cudaStreamSynchronize(st));
+    s->err_pending = false;   // this check covered the asynchronous steps before it
     if (err) {
         cudaMemset(s->err, 0, sizeof(unsigned));
         set_error("encoder: a device-side wait timed out (results discarded)");
@@ -2023,10 +2078,32 @@ extern "C" int vox_cuda_encoder_step_dev(vox_cuda_enc_state *s, float *x_dev, in
     if (!x_dev) return VOX_CUDA_ERR_ARG;
     DevCtx *c = ctx_for(s->enc->device);
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    // a timeout raised by an earlier chunk on this state (its flag was copied
+    // back behind err_ev) is reported now
+    if (s->err_pending && cudaEventQuery(s->err_ev) == cudaSuccess) {
+        s->err_pending = false;
+        if (*s->h_err) {
+            *s->h_err = 0;
+            VC_TRY(cudaMemsetAsync(s->err, 0, sizeof(unsigned), st));
+            set_error("encoder: a device-side wait of an earlier chunk timed out (its results are invalid)");
+            return VOX_CUDA_ERR_CUDA;
+        }
+    }
+    // the previous asynchronous chunk may have run on another stream
+    if (s->tail_set && st != c->stream) VC_TRY(cudaStreamWaitEvent(st, s->tail, 0));
     VC_TRY(cudaMemcpyAsync(s->x, x_dev, (size_t)new_len * kEncDim * 4, cudaMemcpyDeviceToDevice, st));
     if ((rc = run_encoder(s, new_len, false, st))) return rc;
     VC_TRY(cudaMemcpyAsync(x_dev, s->x, (size_t)new_len * kEncDim * 4, cudaMemcpyDeviceToDevice, st));
-    if ((rc = enc_err_check(s, st))) return rc;   // also keeps h_pos stable until the copy ran
+    if (!s->err_pending) {   // one flag copy in flight at a time
+        VC_TRY(cudaMemcpyAsync(s->h_err, s->err, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+        VC_TRY(cudaEventRecord(s->err_ev, st));
+        s->err_pending = true;
+    }
+    // order the library stream (every synchronous entry point, the frees)
+    // after this chunk, without a host wait
+    VC_TRY(cudaEventRecord(s->tail, st));
+    if (st != c->stream) VC_TRY(cudaStreamWaitEvent(c->stream, s->tail, 0));
+    s->tail_set = true;
     s->pos += new_len;
     return VOX_CUDA_OK;
 }
