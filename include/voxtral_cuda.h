@@ -220,6 +220,17 @@ int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states, int n,
 int vox_cuda_decoder_profile_batch(vox_cuda_dec_state *const *states, int n,
                                    const float *embeds_dev, int iters, float *ms);
 
+/* Steady-state device time of one phase's kernel: after one whole step, the
+ * phase's launches of all layers (the LM head: its one launch) are captured
+ * back to back in a CUDA graph with programmatic dependent launch, as in the
+ * step, and replayed `iters` times between two events; *ms_per_launch =
+ * elapsed / (iters x launches).  Each layer streams its own weights, so
+ * successive launches do not hit in L2.  Profiling only: the states'
+ * activations are left as garbage (positions do not advance). */
+int vox_cuda_decoder_profile_sequence(vox_cuda_dec_state *const *states, int n,
+                                      const float *embeds_dev, int phase, int iters,
+                                      float *ms_per_launch);
+
 /* ------------------------------------------------------------------------
  * (3) (5) encoder chunk + adapter: tcgen05 GEMMs, windowed attention, ring
  * ------------------------------------------------------------------------ */
@@ -323,6 +334,52 @@ int vox_cuda_conv_stem_reset(vox_cuda_conv_stem *s);
  * consumed before (0 is possible), or a negative error.  out must hold
  * n_new / 2 + 1 rows. */
 int vox_cuda_conv_stem_step(vox_cuda_conv_stem *s, const float *mel_new, int n_new, float *out);
+
+/* ------------------------------------------------------------------------
+ * (6) log-mel front end: 16 kHz mono fp32 samples -> [frames, 128] log-mel
+ * rows (hop 160, window 400, direct 201-bin DFT, Slaney filters, log10).
+ * ------------------------------------------------------------------------ */
+
+/* Incremental context: vox_mel_ctx_init (voxtral_audio.h:46; called at
+ * voxtral.c:936 with 32 tokens of silence, 40960 samples).  The stream starts
+ * with 200 + left_pad_samples zeros.  max_feed_samples sizes the device
+ * sample ring; longer feeds are processed in pieces. */
+typedef struct vox_cuda_mel vox_cuda_mel;
+vox_cuda_mel *vox_cuda_mel_create(int left_pad_samples, int max_feed_samples);
+void vox_cuda_mel_free(vox_cuda_mel *m);                 /* vox_mel_free (voxtral_audio.h:63) */
+
+/* Frames computed so far (the count vox_mel_data reports, voxtral_audio.h:60). */
+int vox_cuda_mel_frames(const vox_cuda_mel *m);
+
+/* Frames that feeding n_samples more will produce (for sizing mel_out). */
+int vox_cuda_mel_frames_for(const vox_cuda_mel *m, int n_samples);
+
+/* vox_mel_feed (voxtral_audio.h:50; called at voxtral.c:972, 998): append host
+ * samples and compute every frame whose window now fits.  The new rows go to
+ * host mel_out [max_frames, 128]; returns their count, VOX_CUDA_ERR_CAPACITY
+ * (nothing consumed) if more than max_frames, VOX_CUDA_ERR_ARG after finish
+ * (the reference would keep appending past its reflection padding). */
+int vox_cuda_mel_feed(vox_cuda_mel *m, const float *samples, int n_samples, float *mel_out,
+                      int max_frames);
+
+/* Device-resident form: samples_dev and mel_dev on the device, enqueued on
+ * `stream` without waiting. */
+int vox_cuda_mel_feed_dev(vox_cuda_mel *m, const float *samples_dev, int n_samples, float *mel_dev,
+                          int max_frames, void *stream);
+
+/* vox_mel_finish (voxtral_audio.h:56; called at voxtral.c:1003): append
+ * right_pad_samples zeros, then the 200-sample reflection of the signal that
+ * preceded them, compute the remaining frames and drop the last one.  The
+ * rows kept go to mel_out; returns their count (0 when already finished). */
+int vox_cuda_mel_finish(vox_cuda_mel *m, int right_pad_samples, float *mel_out, int max_frames);
+int vox_cuda_mel_finish_dev(vox_cuda_mel *m, int right_pad_samples, float *mel_dev, int max_frames,
+                            void *stream);
+
+/* One-shot log-mel of a whole clip: vox_mel_spectrogram (voxtral_audio.h:33):
+ * reflection padding of 200 on both sides, the last frame dropped.  Returns
+ * the frame count (n_samples / 160) or VOX_CUDA_ERR_ARG when it is 0 (the
+ * reference's "audio too short"). */
+int vox_cuda_mel_spectrogram(const float *samples, int n_samples, float *mel_out, int max_frames);
 
 /* ------------------------------------------------------------------------
  * Kernel-level entry points (device pointers) - the decode attention and the

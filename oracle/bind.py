@@ -128,6 +128,19 @@ def ref_lib():
         lib.voxref_fill_alts.restype = C.c_int
         lib.voxref_decode_threads.argtypes = [C.c_void_p, C.c_int, C.c_int, _fp, _fp, _ip]
         lib.voxref_decode_threads.restype = C.c_double
+        # incremental log-mel (voxtral_audio.h:40-63) and the one-shot form (:33)
+        lib.vox_mel_ctx_init.argtypes = [C.c_int]
+        lib.vox_mel_ctx_init.restype = C.c_void_p
+        lib.vox_mel_feed.argtypes = [C.c_void_p, _fp, C.c_int]
+        lib.vox_mel_feed.restype = C.c_int
+        lib.vox_mel_finish.argtypes = [C.c_void_p, C.c_int]
+        lib.vox_mel_finish.restype = C.c_int
+        lib.vox_mel_data.argtypes = [C.c_void_p, _ip]
+        lib.vox_mel_data.restype = _fp
+        lib.vox_mel_free.argtypes = [C.c_void_p]
+        lib.vox_mel_spectrogram.argtypes = [_fp, C.c_int, _ip]
+        lib.vox_mel_spectrogram.restype = _fp
+        lib.free.argtypes = [C.c_void_p]
         lib.voxref_set_conv.argtypes = [C.c_void_p, _fp, _fp, _fp, _fp]
         lib.voxref_stem_new.argtypes = [C.c_void_p]
         lib.voxref_stem_new.restype = C.c_void_p
@@ -254,6 +267,86 @@ class RefStem:
             self.lib.voxref_stem_free(self.st)
             self.lib.voxref_ctx_free(self.ctx, 0)
             self.st = None
+
+
+SAMPLE_RATE = 16000
+HOP = 160
+RAW_AUDIO_PER_TOKEN = 1280     # samples per decoder token (voxtral.h, 80 ms)
+
+
+def synthetic_audio(n, seed, level_db=-20.0):
+    """Seeded test audio in [-1, 1]: pink-ish noise (a one-pole low-pass of
+    white noise) plus tone bursts of 200-3000 Hz, scaled to `level_db` dBFS
+    RMS.  Stands in for the reference's sample WAVs (not part of the tree)."""
+    rng = np.random.default_rng(seed)
+    white = rng.standard_normal(n).astype(np.float64)
+    pink = np.empty(n)
+    acc = 0.0
+    for i in range(n):          # small n only (tests)
+        acc = 0.97 * acc + white[i]
+        pink[i] = acc
+    t = np.arange(n) / SAMPLE_RATE
+    tones = np.zeros(n)
+    for _ in range(max(1, n // 8000)):
+        f = rng.uniform(200.0, 3000.0)
+        a0 = int(rng.integers(0, max(1, n - 1)))
+        ln = int(rng.integers(800, 6400))
+        sl = slice(a0, min(n, a0 + ln))
+        tones[sl] += np.sin(2 * np.pi * f * t[sl]) * 3.0
+    x = pink / (np.std(pink) + 1e-12) + tones
+    x *= 10 ** (level_db / 20.0) / (np.sqrt(np.mean(x * x)) + 1e-12)
+    return np.clip(x, -1.0, 1.0).astype(np.float32)
+
+
+class RefMel:
+    """The reference's incremental log-mel context (vox_mel_ctx_t,
+    voxtral_audio.c:392-612)."""
+
+    def __init__(self, left_pad_samples):
+        self.lib = ref_lib()
+        self.ctx = self.lib.vox_mel_ctx_init(left_pad_samples)
+        assert self.ctx
+        self.seen = 0
+
+    def _new_frames(self):
+        n = np.zeros(1, np.int32)
+        p = self.lib.vox_mel_data(self.ctx, iptr(n))
+        total = int(n[0])
+        if total <= self.seen:
+            self.seen = total
+            return np.zeros((0, MEL_BINS), np.float32)
+        arr = np.ctypeslib.as_array(p, shape=(total * MEL_BINS,)).reshape(total, MEL_BINS)
+        out = arr[self.seen:total].copy()
+        self.seen = total
+        return out
+
+    def feed(self, samples):
+        samples = np.ascontiguousarray(samples, np.float32)
+        self.lib.vox_mel_feed(self.ctx, fptr(samples), samples.size)
+        return self._new_frames()
+
+    def finish(self, right_pad_samples=0):
+        self.lib.vox_mel_finish(self.ctx, right_pad_samples)
+        return self._new_frames()
+
+    def free(self):
+        if self.ctx:
+            self.lib.vox_mel_free(self.ctx)
+            self.ctx = None
+
+
+def ref_mel_spectrogram(samples):
+    """The reference's one-shot vox_mel_spectrogram (voxtral_audio.c:290-395):
+    [frames, 128], or None where it rejects the input as too short."""
+    lib = ref_lib()
+    samples = np.ascontiguousarray(samples, np.float32)
+    n = np.zeros(1, np.int32)
+    p = lib.vox_mel_spectrogram(fptr(samples), samples.size, iptr(n))
+    if not p:
+        return None
+    out = np.ctypeslib.as_array(p, shape=(int(n[0]) * MEL_BINS,)).reshape(-1, MEL_BINS).copy()
+    lib.free(C.cast(p, C.c_void_p))
+    return out
 
 
 class DecoderWeights:

@@ -295,6 +295,57 @@ def gen_stem():
     np.savez_compressed(os.path.join(HERE, "stem.npz"), **out)
 
 
+# Log-mel front end (voxtral_audio.c).  Streaming: the stream path's left
+# pad of 32 tokens of silence (voxtral.c:936) with feeds of 1, 159, 160, 161,
+# 400 ... samples, the stream finish's zero feeds in 4096-sample pieces then
+# vox_mel_finish(0) (voxtral.c:985-1003); and a context without left pad
+# finished with right_pad > 0.  One-shot: the whole clip and clips of 150
+# (rejected), 399, 500 and 561 samples.
+MEL_AUDIO = 24000
+MEL_FEEDS_A = [1, 159, 160, 161, 400, 3200, 7, 12000]
+MEL_PAD_A = 40960
+MEL_RIGHT_A = 1280 * 9 + 1000      # zeros fed before finish(0)
+MEL_FEEDS_B = [399, 1, 5000]
+MEL_RIGHT_B = 1000                 # finish(1000)
+MEL_ONESHOT = [MEL_AUDIO, 150, 399, 500, 561]
+
+
+def mel_audio(seed=8301):
+    return B.synthetic_audio(MEL_AUDIO, seed)
+
+
+def mel_feeds(feeds):
+    return feeds + [MEL_AUDIO - sum(feeds)]
+
+
+def gen_mel():
+    out = {}
+    x = mel_audio()
+    out["audio_sum"] = checksum(x)
+    for tag, pad, feeds, zeros, right in (("a", MEL_PAD_A, mel_feeds(MEL_FEEDS_A), MEL_RIGHT_A, 0),
+                                          ("b", 0, mel_feeds(MEL_FEEDS_B), 0, MEL_RIGHT_B)):
+        ref = B.RefMel(pad)
+        off, rows = 0, []
+        for f in feeds:
+            rows.append(ref.feed(x[off:off + f]))
+            off += f
+        z = zeros
+        while z > 0:
+            c = min(z, 4096)
+            rows.append(ref.feed(np.zeros(c, np.float32)))
+            z -= c
+        rows.append(ref.finish(right))
+        out[f"{tag}_counts"] = np.array([r.shape[0] for r in rows], np.int32)
+        pack(f"{tag}_mel", np.concatenate(rows, axis=0), out)
+        ref.free()
+    for n in MEL_ONESHOT:
+        m = B.ref_mel_spectrogram(x[:n])
+        out[f"oneshot{n}_frames"] = np.int32(0 if m is None else m.shape[0])
+        if m is not None:
+            pack(f"oneshot{n}", m, out)
+    np.savez_compressed(os.path.join(HERE, "mel.npz"), **out)
+
+
 ALT_CASES = [(61, 3.0, 4, 0.999), (62, 0.5, 4, 0.5), (63, 8.0, 3, 0.99), (64, 1.0, 2, 0.9),
              (65, 0.01, 4, 0.999)]
 
@@ -313,6 +364,10 @@ def gen_alts():
 def main():
     assert B.ref_available(), "build oracle/_ref first (make -C oracle ref)"
     t = time.time()
+    if sys.argv[1:] == ["mel"]:   # only the log-mel front end
+        gen_mel()
+        print("mel", time.time() - t)
+        return
     if sys.argv[1:] == ["stem"]:   # only the conv stem
         gen_stem()
         print("stem", time.time() - t)
@@ -326,6 +381,7 @@ def main():
     gen_attention(); print("attention", time.time() - t)
     gen_alts(); print("alts", time.time() - t)
     gen_stem(); print("stem", time.time() - t)
+    gen_mel(); print("mel", time.time() - t)
     w = B.DecoderWeights(seed=DEC_SEED)
     gen_decoder(w); print("decoder", time.time() - t)
     del w

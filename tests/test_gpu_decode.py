@@ -299,3 +299,21 @@ def test_async_batched_steps_match_sync_batched_steps(small_w):
     for st in sync_states + async_states:
         st.free()
     d.free()
+
+
+def test_profile_sequence_times_every_phase(small_w):
+    """vox_cuda_decoder_profile_sequence: each phase's launches replayed back
+    to back give a positive per-launch time; positions do not advance."""
+    import torch
+    d = make_gpu_decoder(small_w)
+    states = [d.state(kv_cap=64) for _ in range(2)]
+    for i, st in enumerate(states):
+        st.set_position(5 + i)
+    embeds = torch.from_numpy(B.normal_f32((2, B.DEC_DIM), 900)).cuda()
+    for ph in V.PROF_PHASES:
+        ms = V.profile_sequence(states, embeds.data_ptr(), ph, iters=2)
+        assert 0.0 < ms < 50.0, (ph, ms)
+    assert [st.position for st in states] == [5, 6]
+    for st in states:
+        st.free()
+    d.free()

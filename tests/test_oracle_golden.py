@@ -166,3 +166,57 @@ def test_conv_stem_matches_reference_golden():
         if y.size:
             idx, val, _, _ = unpack(g, f"chunk{i}")
             assert B.rel_l2(y.reshape(-1)[idx], val) < 1e-5, i
+
+
+# log-mel: fp32 sums of 400 (DFT) and 201 (filters) terms in another order than
+# the reference's vectorised -ffast-math loops; the weakest bands (highest mel
+# bins of pink noise) carry the largest relative error after log10.
+MEL_MAX_ABS = 1e-3
+MEL_REL = 1e-4
+
+
+def mel_stream_rows(tag):
+    """The restated streaming context over the golden's feed schedule."""
+    import mel as M
+    x = G.mel_audio()
+    feeds, pad, zeros, right = ((G.mel_feeds(G.MEL_FEEDS_A), G.MEL_PAD_A, G.MEL_RIGHT_A, 0) if tag == "a"
+                                else (G.mel_feeds(G.MEL_FEEDS_B), 0, 0, G.MEL_RIGHT_B))
+    m = M.StreamingMel(pad)
+    rows, off = [], 0
+    for f in feeds:
+        rows.append(m.feed(x[off:off + f]))
+        off += f
+    while zeros > 0:
+        c = min(zeros, 4096)
+        rows.append(m.feed(np.zeros(c, np.float32)))
+        zeros -= c
+    rows.append(m.finish(right))
+    return rows
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_streaming_mel_matches_reference_golden(tag):
+    g = load_golden("mel")
+    assert str(g["audio_sum"]) == str(G.checksum(G.mel_audio())), "audio generator changed"
+    rows = mel_stream_rows(tag)
+    assert [r.shape[0] for r in rows] == g[f"{tag}_counts"].tolist()
+    mel = np.concatenate(rows, axis=0)
+    idx, val, _, size = unpack(g, f"{tag}_mel")
+    assert mel.size == size
+    assert np.abs(mel.reshape(-1)[idx] - val).max() < MEL_MAX_ABS
+    assert B.rel_l2(mel.reshape(-1)[idx], val) < MEL_REL
+
+
+@pytest.mark.parametrize("n", G.MEL_ONESHOT)
+def test_oneshot_mel_matches_reference_golden(n):
+    import mel as M
+    g = load_golden("mel")
+    m = M.mel_spectrogram(G.mel_audio()[:n])
+    frames = int(g[f"oneshot{n}_frames"])
+    if frames == 0:
+        assert m is None
+        return
+    idx, val, _, size = unpack(g, f"oneshot{n}")
+    assert m.size == size
+    assert np.abs(m.reshape(-1)[idx] - val).max() < MEL_MAX_ABS
+    assert B.rel_l2(m.reshape(-1)[idx], val) < MEL_REL

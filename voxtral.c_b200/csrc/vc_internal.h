@@ -181,6 +181,28 @@ cudaError_t launch_stem_state(const float *mel_new, int n, float *mel_hist, cons
                               uint16_t *c0_hist, cudaStream_t st);
 cudaError_t launch_f32_to_f16(const float *src, uint16_t *dst, size_t n, cudaStream_t st);
 
+// log-mel front end (vc_mel.cu; voxtral_audio.c:31-37 constants)
+constexpr int kMelRate = 16000;
+constexpr int kMelBins = 128;
+constexpr int kMelHop = 160;
+constexpr int kMelWin = 400;                  // window = DFT length
+constexpr int kMelFreq = kMelWin / 2 + 1;     // 201 bins
+constexpr int kMelCenterPad = kMelWin / 2;    // center=True padding
+constexpr float kMelLogMax = 1.5f;
+constexpr int kMelFrames = 4;                 // frames per CTA
+
+struct MelTables {          // device copies of mel_host_tables' output
+    const float *win;       // [400] periodic Hann
+    const float *cos_t;     // [400][201] cos(2 pi k n / 400), bin fastest
+    const float *sin_t;     // [400][201]
+    const float *filt_t;    // [201][128] mel filters, mel fastest
+};
+void mel_host_tables(float *win, float *cos_t, float *sin_t, float *filt_t);
+cudaError_t launch_mel_frames(const float *ring, long long mask, long long pad, long long t0, int n_frames,
+                              const MelTables &t, float *out, cudaStream_t st);
+cudaError_t launch_mel_reflect(const float *ring, long long mask, long long pad, long long src0, int n,
+                               float *dst, cudaStream_t st);
+
 // Set the message vox_cuda_last_error() returns on the calling thread.
 void set_last_error(const char *fmt, ...);
 

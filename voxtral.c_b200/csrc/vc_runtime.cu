@@ -837,18 +837,23 @@ float *h_x(StepWork *w) { return (float *)(w->hblock + ((char *)w->x - w->dblock
 // statistics and fragments, the decoder layers, then the LM head + argmax
 // when with_head.  Each producer writes its consumer's activation fragments.
 // evs (profiling only): 2 events per launch, recorded around it.
+// only (profiling only): >= 0 enqueues that phase's launches alone
+// (VOX_CUDA_PROF_*), one per layer, back to back.
 int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_t st,
-                   cudaEvent_t *evs = nullptr) {
+                   cudaEvent_t *evs = nullptr, int only = -1) {
     const int n = w->n;
     const bool pdl = d->pdl && evs == nullptr;
     const int ss_parts = gemv_row_blocks(kDecDim);
     int ei = 0;
 #define VC_EV_BEGIN() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
 #define VC_EV_END() do { if (evs) VC_TRY(cudaEventRecord(evs[ei++], st)); } while (0)
-    VC_EV_BEGIN();
-    VC_TRY(launch_prep_xfrag(w->x, n, kDecDim, kDecDim, d->L[0].g_attn, w->xf_attn, w->ss_attn, st, pdl));
-    VC_EV_END();
-    for (int l = 0; l < d->n_layers; l++) {
+#define VC_PHASE(ph) if (only < 0 || only == (ph))
+    if (only < 0) {
+        VC_EV_BEGIN();
+        VC_TRY(launch_prep_xfrag(w->x, n, kDecDim, kDecDim, d->L[0].g_attn, w->xf_attn, w->ss_attn, st, pdl));
+        VC_EV_END();
+    }
+    for (int l = 0; l < d->n_layers && only != VOX_CUDA_PROF_LM_HEAD; l++) {
         const DecLayer &L = d->L[l];
         GemvParams p = {};
         // q|k|v = rms_norm(x) Wqkv^T, RoPE, ring write
@@ -864,9 +869,11 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p.rope = w->rope;
         p.layer = l;
         p.err = w->err;
-        VC_EV_BEGIN();
-        VC_TRY(launch_gemv(n, EPI_QKV, p, st, pdl));
-        VC_EV_END();
+        VC_PHASE(VOX_CUDA_PROF_QKV) {
+            VC_EV_BEGIN();
+            VC_TRY(launch_gemv(n, EPI_QKV, p, st, pdl));
+            VC_EV_END();
+        }
         // attention over the ring -> wo's fragments
         AttnParams a = {};
         a.q = w->q;
@@ -878,9 +885,11 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         a.part_ml = w->part_ml;
         a.counters = w->counters;
         a.S = kAttnSplits;
-        VC_EV_BEGIN();
-        VC_TRY(launch_attn_decode(n, a, st, pdl));
-        VC_EV_END();
+        VC_PHASE(VOX_CUDA_PROF_ATTN) {
+            VC_EV_BEGIN();
+            VC_TRY(launch_attn_decode(n, a, st, pdl));
+            VC_EV_END();
+        }
         // x += att Wo^T; fragments of x * g_ffn and sums of x^2 for the FFN norm
         p = GemvParams{};
         p.W = L.wo;
@@ -893,9 +902,11 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p.xfrag_out = w->xf_ffn;
         p.g_next = L.g_ffn;
         p.err = w->err;
-        VC_EV_BEGIN();
-        VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
-        VC_EV_END();
+        VC_PHASE(VOX_CUDA_PROF_WO) {
+            VC_EV_BEGIN();
+            VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
+            VC_EV_END();
+        }
         // h = silu(xn W1^T) * (xn W3^T), xn = rms_norm(x) * (1 + ada)
         p = GemvParams{};
         p.W = L.w13;
@@ -906,9 +917,11 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p.ss_parts = ss_parts;
         p.xfrag_out = w->xf_h;
         p.err = w->err;
-        VC_EV_BEGIN();
-        VC_TRY(launch_gemv(n, EPI_SWIGLU, p, st, pdl));
-        VC_EV_END();
+        VC_PHASE(VOX_CUDA_PROF_W13) {
+            VC_EV_BEGIN();
+            VC_TRY(launch_gemv(n, EPI_SWIGLU, p, st, pdl));
+            VC_EV_END();
+        }
         // x += h W2^T; fragments for the next norm (next layer's, or the final)
         p = GemvParams{};
         p.W = L.w2;
@@ -921,11 +934,13 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p.xfrag_out = w->xf_attn;
         p.g_next = (l + 1 < d->n_layers) ? d->L[l + 1].g_attn : d->norm;
         p.err = w->err;
-        VC_EV_BEGIN();
-        VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
-        VC_EV_END();
+        VC_PHASE(VOX_CUDA_PROF_W2) {
+            VC_EV_BEGIN();
+            VC_TRY(launch_gemv(n, EPI_ADD, p, st, pdl));
+            VC_EV_END();
+        }
     }
-    if (with_head) {
+    if (with_head && (only < 0 || only == VOX_CUDA_PROF_LM_HEAD)) {
         GemvParams p = {};
         p.W = d->tok_emb;
         p.N = d->vocab;
@@ -945,6 +960,7 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
     }
 #undef VC_EV_BEGIN
 #undef VC_EV_END
+#undef VC_PHASE
     return VOX_CUDA_OK;
 }
 
@@ -1563,6 +1579,63 @@ extern "C" int vox_cuda_decoder_profile_batch(vox_cuda_dec_state *const *states,
     for (auto &e : evs) cudaEventDestroy(e);
     if (rc) return rc;
     for (int i = 0; i < VOX_CUDA_PROF_PHASES; i++) ms[i] = (float)(acc[i] / iters);
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_decoder_profile_sequence(vox_cuda_dec_state *const *states, int n,
+                                                 const float *embeds_dev, int phase, int iters,
+                                                 float *ms_per_launch) {
+    if (!embeds_dev || !ms_per_launch || iters <= 0 || phase < 0 || phase >= VOX_CUDA_PROF_PHASES) {
+        set_error("decoder_profile_sequence: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    vox_cuda_decoder *d = nullptr;
+    DevCtx *c = nullptr;
+    if (!states || n <= 0 || n > kMaxBatch || !states[0]) return batch_prepare(states, n, &d, &c);
+    std::lock_guard<std::mutex> lk(states[0]->dec->mu);
+    int rc = batch_prepare(states, n, &d, &c);
+    if (rc) return rc;
+    StepWork *w = d->batch_work[n];
+    cudaStream_t st = c->stream;
+    const size_t head = (char *)w->x - w->dblock;
+    // one whole step first: every phase's inputs then hold real activations
+    VC_TRY(cudaMemcpyAsync(w->dblock, w->hblock, head, cudaMemcpyHostToDevice, st));
+    VC_TRY(cudaMemcpyAsync(w->x, embeds_dev, (size_t)n * kDecDim * 4, cudaMemcpyDeviceToDevice, st));
+    if ((rc = enqueue_layers(d, w, true, st))) return rc;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    VC_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    rc = enqueue_layers(d, w, true, st, nullptr, phase);
+    cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (rc) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    VC_TRY(e);
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    VC_TRY(e);
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    float t = 0.f;
+    bool ok = cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
+    for (int i = 0; ok && i < 2; i++) ok = cudaGraphLaunch(exec, st) == cudaSuccess;   // warm-up
+    ok = ok && cudaEventRecord(e0, st) == cudaSuccess;
+    for (int i = 0; ok && i < iters; i++) ok = cudaGraphLaunch(exec, st) == cudaSuccess;
+    ok = ok && cudaEventRecord(e1, st) == cudaSuccess && cudaEventSynchronize(e1) == cudaSuccess &&
+         cudaEventElapsedTime(&t, e0, e1) == cudaSuccess;
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    cudaGraphExecDestroy(exec);
+    if (!ok) {
+        set_error("decoder_profile_sequence: timing failed");
+        return VOX_CUDA_ERR_CUDA;
+    }
+    VC_TRY(cudaMemcpyAsync(w->h_tokens + n, w->err, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+    VC_TRY(cudaStreamSynchronize(st));
+    w->err_pending = false;
+    if ((rc = check_step_error(w, st))) return rc;
+    const int launches = phase == VOX_CUDA_PROF_LM_HEAD ? 1 : d->n_layers;
+    *ms_per_launch = t / ((float)iters * launches);
     return VOX_CUDA_OK;
 }
 
@@ -2361,4 +2434,287 @@ extern "C" int vox_cuda_conv_stem_step(vox_cuda_conv_stem *s, const float *mel_n
     }
     s->frames += n_new;
     return n_out;
+}
+
+// ---------------------------------------------------------------------------
+// log-mel front end: the incremental context (vox_mel_ctx_t,
+// voxtral_audio.c:392-612) and the one-shot spectrogram (:290-395)
+// ---------------------------------------------------------------------------
+
+struct vox_cuda_mel {
+    int device = 0;
+    long long pad = 0;         // logical samples before the first real one (zeros, never stored)
+    long long n_samples = 0;   // logical samples so far, pad included
+    long long n_frames = 0;    // frames computed (and reported) so far
+    bool finished = false;
+    int ring_len = 0;          // power of two
+    float *block = nullptr;    // tables | ring | reflection | staging
+    size_t bytes = 0;
+    float *ring = nullptr, *refl = nullptr, *stage = nullptr;
+    int stage_frames = 0;
+    MelTables t = {};
+};
+
+namespace {
+
+long long mel_frames_upto(long long n_samples) {
+    return n_samples >= kMelWin ? (n_samples - kMelWin) / kMelHop + 1 : 0;
+}
+
+// upload the 4 host tables into dst (win | cos | sin | filt) and point t at them
+int mel_upload_tables(float *dst, MelTables *t, cudaStream_t st) {
+    const size_t n_tab = kMelWin + 2 * (size_t)kMelWin * kMelFreq + (size_t)kMelFreq * kMelBins;
+    std::vector<float> h(n_tab);
+    float *win = h.data(), *cs = win + kMelWin, *sn = cs + (size_t)kMelWin * kMelFreq;
+    float *ft = sn + (size_t)kMelWin * kMelFreq;
+    mel_host_tables(win, cs, sn, ft);
+    VC_TRY(cudaMemcpyAsync(dst, h.data(), n_tab * 4, cudaMemcpyHostToDevice, st));
+    VC_TRY(cudaStreamSynchronize(st));   // h is on this stack frame
+    t->win = dst;
+    t->cos_t = dst + kMelWin;
+    t->sin_t = t->cos_t + (size_t)kMelWin * kMelFreq;
+    t->filt_t = t->sin_t + (size_t)kMelWin * kMelFreq;
+    return VOX_CUDA_OK;
+}
+
+constexpr size_t kMelTableFloats = kMelWin + 2 * (size_t)kMelWin * kMelFreq + (size_t)kMelFreq * kMelBins;
+
+// Append n samples (src, or zeros when src is NULL) at the stream's end.
+int mel_append(vox_cuda_mel *m, const float *src, int n, cudaMemcpyKind kind, cudaStream_t st) {
+    long long at = m->n_samples - m->pad;   // ring index of the first new sample
+    int done = 0;
+    while (done < n) {
+        const int slot = (int)(at & (m->ring_len - 1));
+        int run = m->ring_len - slot;
+        if (run > n - done) run = n - done;
+        if (src) VC_TRY(cudaMemcpyAsync(m->ring + slot, src + done, (size_t)run * 4, kind, st));
+        else VC_TRY(cudaMemsetAsync(m->ring + slot, 0, (size_t)run * 4, st));
+        done += run;
+        at += run;
+    }
+    m->n_samples += n;
+    return VOX_CUDA_OK;
+}
+
+// Compute every frame that now fits into out; returns the count (or < 0).
+int mel_compute(vox_cuda_mel *m, float *out, cudaStream_t st) {
+    const long long t1 = mel_frames_upto(m->n_samples);
+    const int nf = (int)(t1 - m->n_frames);
+    if (nf <= 0) return 0;
+    VC_TRY(launch_mel_frames(m->ring, m->ring_len - 1, m->pad, m->n_frames, nf, m->t, out, st));
+    m->n_frames = t1;
+    return nf;
+}
+
+// The largest piece appended at once: the frame in progress keeps < 400
+// samples live in the ring.
+int mel_piece(const vox_cuda_mel *m) { return m->ring_len - kMelWin; }
+
+// Feed n samples in ring-sized pieces; frames go to out (device) when
+// out_dev, else through the staging block to the host buffer.
+int mel_feed_impl(vox_cuda_mel *m, const float *samples, int n, float *out, int max_frames, bool dev,
+                  cudaStream_t st) {
+    if (!m || (!samples && n > 0) || !out || n < 0 || max_frames < 0) {
+        set_error("mel_feed: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (m->finished) {
+        set_error("mel_feed: the context is finished");
+        return VOX_CUDA_ERR_ARG;
+    }
+    const long long want = mel_frames_upto(m->n_samples + n) - m->n_frames;
+    if (want > max_frames) {
+        set_error("mel_feed: %lld frames exceed the output's %d", want, max_frames);
+        return VOX_CUDA_ERR_CAPACITY;
+    }
+    cudaSetDevice(m->device);
+    const cudaMemcpyKind kind = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    int written = 0, done = 0, rc;
+    while (done < n) {
+        const int k = std::min(n - done, mel_piece(m));
+        if ((rc = mel_append(m, samples + done, k, kind, st))) return rc;
+        done += k;
+        float *dst = dev ? out + (size_t)written * kMelBins : m->stage;
+        const int nf = mel_compute(m, dst, st);
+        if (nf < 0) return nf;
+        if (!dev && nf > 0)
+            VC_TRY(cudaMemcpyAsync(out + (size_t)written * kMelBins, m->stage, (size_t)nf * kMelBins * 4,
+                                   cudaMemcpyDeviceToHost, st));
+        written += nf;
+        if (!dev) VC_TRY(cudaStreamSynchronize(st));   // the staging block is reused by the next piece
+    }
+    return written;
+}
+
+int mel_finish_impl(vox_cuda_mel *m, int right_pad, float *out, int max_frames, bool dev, cudaStream_t st) {
+    if (!m || !out || right_pad < 0 || max_frames < 0) {
+        set_error("mel_finish: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (m->finished) return 0;
+    const long long final_samples = m->n_samples + right_pad + kMelCenterPad;
+    const long long computed = mel_frames_upto(final_samples) - m->n_frames;
+    const long long report = computed > 0 ? computed - 1 : 0;   // the last frame is dropped
+    if (report > max_frames) {
+        set_error("mel_finish: %lld frames exceed the output's %d", report, max_frames);
+        return VOX_CUDA_ERR_CAPACITY;
+    }
+    cudaSetDevice(m->device);
+    // the reflection of the signal before the right pad, taken first: the pad
+    // may overwrite its source in the ring (voxtral_audio.c:583-590)
+    VC_TRY(launch_mel_reflect(m->ring, m->ring_len - 1, m->pad, m->n_samples - 2, kMelCenterPad, m->refl, st));
+    int written = 0, rc;
+    auto emit = [&](int nf) -> int {   // copy the stage's first rows that are reported
+        const int keep = (int)std::min<long long>(nf, report - written);
+        if (keep > 0)
+            VC_TRY(cudaMemcpyAsync(out + (size_t)written * kMelBins, m->stage, (size_t)keep * kMelBins * 4,
+                                   dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+        written += keep > 0 ? keep : 0;
+        VC_TRY(cudaStreamSynchronize(st));   // the staging block is reused by the next piece
+        return VOX_CUDA_OK;
+    };
+    int left = right_pad;
+    while (left > 0) {
+        const int k = std::min(left, mel_piece(m));
+        if ((rc = mel_append(m, nullptr, k, cudaMemcpyDeviceToDevice, st))) return rc;
+        left -= k;
+        const int nf = mel_compute(m, m->stage, st);
+        if (nf < 0) return nf;
+        if ((rc = emit(nf))) return rc;
+    }
+    if ((rc = mel_append(m, m->refl, kMelCenterPad, cudaMemcpyDeviceToDevice, st))) return rc;
+    const int nf = mel_compute(m, m->stage, st);
+    if (nf < 0) return nf;
+    if ((rc = emit(nf))) return rc;
+    if (m->n_frames > 0) m->n_frames -= 1;
+    m->finished = true;
+    return written;
+}
+
+}  // namespace
+
+extern "C" vox_cuda_mel *vox_cuda_mel_create(int left_pad_samples, int max_feed_samples) {
+    DevCtx *c = cur_ctx();
+    if (!c) return nullptr;
+    if (left_pad_samples < 0 || max_feed_samples <= 0) {
+        set_error("mel_create: bad arguments");
+        return nullptr;
+    }
+    vox_cuda_mel *m = new vox_cuda_mel();
+    m->device = c->device;
+    m->pad = kMelCenterPad + (long long)left_pad_samples;
+    m->n_samples = m->pad;
+    m->ring_len = 1024;
+    while (m->ring_len < max_feed_samples + kMelWin) m->ring_len *= 2;
+    // the first piece also yields the frames over the leading zeros
+    m->stage_frames = (int)((m->pad + m->ring_len) / kMelHop + 4);
+    const size_t n = kMelTableFloats + m->ring_len + kMelCenterPad + (size_t)m->stage_frames * kMelBins;
+    m->bytes = n * 4;
+    if (dev_alloc(c, (void **)&m->block, m->bytes) != cudaSuccess) {
+        set_error("mel_create: cudaMalloc(%zu) failed", m->bytes);
+        delete m;
+        return nullptr;
+    }
+    m->ring = m->block + kMelTableFloats;
+    m->refl = m->ring + m->ring_len;
+    m->stage = m->refl + kMelCenterPad;
+    if (mel_upload_tables(m->block, &m->t, c->stream) != VOX_CUDA_OK) {
+        vox_cuda_mel_free(m);
+        return nullptr;
+    }
+    return m;
+}
+
+extern "C" void vox_cuda_mel_free(vox_cuda_mel *m) {
+    if (!m) return;
+    DevCtx *c = ctx_for(m->device);
+    cudaSetDevice(m->device);
+    if (c) {
+        cudaStreamSynchronize(c->stream);
+        dev_free(c, m->block, m->block ? m->bytes : 0);
+    }
+    delete m;
+}
+
+extern "C" int vox_cuda_mel_frames(const vox_cuda_mel *m) { return m ? (int)m->n_frames : VOX_CUDA_ERR_ARG; }
+
+extern "C" int vox_cuda_mel_frames_for(const vox_cuda_mel *m, int n_samples) {
+    if (!m || n_samples < 0) return VOX_CUDA_ERR_ARG;
+    return (int)(mel_frames_upto(m->n_samples + n_samples) - m->n_frames);
+}
+
+extern "C" int vox_cuda_mel_feed(vox_cuda_mel *m, const float *samples, int n_samples, float *mel_out,
+                                 int max_frames) {
+    DevCtx *c = m ? ctx_for(m->device) : nullptr;
+    if (m && !c) return VOX_CUDA_ERR_UNAVAILABLE;
+    return mel_feed_impl(m, samples, n_samples, mel_out, max_frames, false, c ? c->stream : nullptr);
+}
+
+extern "C" int vox_cuda_mel_feed_dev(vox_cuda_mel *m, const float *samples_dev, int n_samples, float *mel_dev,
+                                     int max_frames, void *stream) {
+    DevCtx *c = m ? ctx_for(m->device) : nullptr;
+    if (m && !c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaStream_t st = stream ? (cudaStream_t)stream : (c ? c->stream : nullptr);
+    return mel_feed_impl(m, samples_dev, n_samples, mel_dev, max_frames, true, st);
+}
+
+extern "C" int vox_cuda_mel_finish(vox_cuda_mel *m, int right_pad_samples, float *mel_out, int max_frames) {
+    DevCtx *c = m ? ctx_for(m->device) : nullptr;
+    if (m && !c) return VOX_CUDA_ERR_UNAVAILABLE;
+    return mel_finish_impl(m, right_pad_samples, mel_out, max_frames, false, c ? c->stream : nullptr);
+}
+
+extern "C" int vox_cuda_mel_finish_dev(vox_cuda_mel *m, int right_pad_samples, float *mel_dev, int max_frames,
+                                       void *stream) {
+    DevCtx *c = m ? ctx_for(m->device) : nullptr;
+    if (m && !c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaStream_t st = stream ? (cudaStream_t)stream : (c ? c->stream : nullptr);
+    return mel_finish_impl(m, right_pad_samples, mel_dev, max_frames, true, st);
+}
+
+extern "C" int vox_cuda_mel_spectrogram(const float *samples, int n_samples, float *mel_out, int max_frames) {
+    if (!samples || !mel_out || n_samples <= 0 || max_frames < 0) {
+        set_error("mel_spectrogram: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    // center padding by reflection on both sides, the last frame dropped
+    const long long padded_len = (long long)n_samples + 2 * kMelCenterPad;
+    const long long frames = mel_frames_upto(padded_len) - 1;
+    if (frames <= 0) {
+        set_error("mel_spectrogram: audio too short (%d samples)", n_samples);
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (frames > max_frames) {
+        set_error("mel_spectrogram: %lld frames exceed the output's %d", frames, max_frames);
+        return VOX_CUDA_ERR_CAPACITY;
+    }
+    DevCtx *c = cur_ctx();
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    std::vector<float> padded((size_t)padded_len);
+    for (int i = 0; i < kMelCenterPad; i++) {
+        const int l = kMelCenterPad - i, r = n_samples - 2 - i;
+        padded[i] = l < n_samples ? samples[l] : 0.0f;
+        padded[(size_t)kMelCenterPad + n_samples + i] = r >= 0 ? samples[r] : 0.0f;
+    }
+    memcpy(padded.data() + kMelCenterPad, samples, (size_t)n_samples * 4);
+    const size_t n = kMelTableFloats + (size_t)padded_len + (size_t)frames * kMelBins;
+    float *block = nullptr;
+    if (dev_alloc(c, (void **)&block, n * 4) != cudaSuccess) {
+        set_error("mel_spectrogram: cudaMalloc(%zu) failed", n * 4);
+        return VOX_CUDA_ERR_OOM;
+    }
+    MelTables t;
+    int rc = mel_upload_tables(block, &t, c->stream);
+    float *sig = block + kMelTableFloats, *out = sig + padded_len;
+    cudaStream_t st = c->stream;
+    if (rc == VOX_CUDA_OK &&
+        (cudaMemcpyAsync(sig, padded.data(), (size_t)padded_len * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+         launch_mel_frames(sig, -1, 0, 0, (int)frames, t, out, st) != cudaSuccess ||
+         cudaMemcpyAsync(mel_out, out, (size_t)frames * kMelBins * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+         cudaStreamSynchronize(st) != cudaSuccess)) {
+        set_error("mel_spectrogram: %s", cudaGetErrorString(cudaGetLastError()));
+        rc = VOX_CUDA_ERR_CUDA;
+    }
+    dev_free(c, block, n * 4);
+    return rc == VOX_CUDA_OK ? (int)frames : rc;
 }

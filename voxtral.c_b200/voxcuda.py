@@ -104,6 +104,8 @@ def lib():
                                              C.c_void_p], C.c_int),
         "vox_cuda_decoder_profile_batch": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, _fp],
                                            C.c_int),
+        "vox_cuda_decoder_profile_sequence": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int,
+                                               _fp], C.c_int),
         "vox_cuda_encoder_create": ([C.c_void_p], C.c_void_p),
         "vox_cuda_encoder_free": ([C.c_void_p], None),
         "vox_cuda_enc_state_create": ([C.c_void_p, C.c_int], C.c_void_p),
@@ -119,6 +121,16 @@ def lib():
         "vox_cuda_conv_stem_free": ([C.c_void_p], None),
         "vox_cuda_conv_stem_reset": ([C.c_void_p], C.c_int),
         "vox_cuda_conv_stem_step": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
+        "vox_cuda_mel_create": ([C.c_int, C.c_int], C.c_void_p),
+        "vox_cuda_mel_free": ([C.c_void_p], None),
+        "vox_cuda_mel_frames": ([C.c_void_p], C.c_int),
+        "vox_cuda_mel_frames_for": ([C.c_void_p, C.c_int], C.c_int),
+        "vox_cuda_mel_feed": ([C.c_void_p, _fp, C.c_int, _fp, C.c_int], C.c_int),
+        "vox_cuda_mel_feed_dev": ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p],
+                                  C.c_int),
+        "vox_cuda_mel_finish": ([C.c_void_p, C.c_int, _fp, C.c_int], C.c_int),
+        "vox_cuda_mel_finish_dev": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p], C.c_int),
+        "vox_cuda_mel_spectrogram": ([_fp, C.c_int, _fp, C.c_int], C.c_int),
         "vox_cuda_attention_decode_dev": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                            C.c_void_p, C.c_void_p], C.c_int),
         "vox_cuda_attention_decode_noalloc": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
@@ -297,6 +309,16 @@ def profile_batch(states, embeds_dev, iters=3):
     return dict(zip(PROF_PHASES, ms.tolist()))
 
 
+def profile_sequence(states, embeds_dev, phase, iters=5):
+    """Steady-state ms per launch of one phase's kernel (PROF_PHASES name),
+    its per-layer launches replayed back to back in a graph."""
+    ms = np.zeros(1, np.float32)
+    check(lib().vox_cuda_decoder_profile_sequence(states_array(states), len(states), embeds_dev,
+                                                  PROF_PHASES.index(phase), iters, _f(ms)),
+          "profile_sequence")
+    return float(ms[0])
+
+
 class Encoder:
     """Resident encoder + adapter weights.  `layers`: n tuples of
     (wq, wk, wv, wo, w1, w2, w3, wq_bias, wv_bias, wo_bias, w2_bias,
@@ -396,3 +418,58 @@ class ConvStem:
         if self.h:
             lib().vox_cuda_conv_stem_free(self.h)
             self.h = None
+
+
+MEL_BINS = 128
+
+
+class Mel:
+    """Incremental log-mel context on the device (vox_cuda_mel_*): the
+    reference's vox_mel_ctx_init / vox_mel_feed / vox_mel_finish."""
+
+    def __init__(self, left_pad_samples=0, max_feed_samples=32000):
+        self.h = lib().vox_cuda_mel_create(left_pad_samples, max_feed_samples)
+        if not self.h:
+            raise VoxCudaError("mel_create: " + last_error())
+
+    @property
+    def frames(self):
+        return lib().vox_cuda_mel_frames(self.h)
+
+    def frames_for(self, n_samples):
+        return lib().vox_cuda_mel_frames_for(self.h, n_samples)
+
+    def feed(self, samples):
+        samples = np.ascontiguousarray(samples, np.float32)
+        cap = max(self.frames_for(samples.size), 1)
+        out = np.empty((cap, MEL_BINS), np.float32)
+        n = check(lib().vox_cuda_mel_feed(self.h, _f(samples), samples.size, _f(out), cap), "mel_feed")
+        return out[:n]
+
+    def feed_dev(self, samples_dev, n_samples, mel_dev, max_frames, stream=None):
+        return check(lib().vox_cuda_mel_feed_dev(self.h, samples_dev, n_samples, mel_dev, max_frames, stream),
+                     "mel_feed_dev")
+
+    def finish(self, right_pad_samples=0):
+        cap = max(self.frames_for(right_pad_samples + 200), 1)
+        out = np.empty((cap, MEL_BINS), np.float32)
+        n = check(lib().vox_cuda_mel_finish(self.h, right_pad_samples, _f(out), cap), "mel_finish")
+        return out[:n]
+
+    def finish_dev(self, right_pad_samples, mel_dev, max_frames, stream=None):
+        return check(lib().vox_cuda_mel_finish_dev(self.h, right_pad_samples, mel_dev, max_frames, stream),
+                     "mel_finish_dev")
+
+    def free(self):
+        if self.h:
+            lib().vox_cuda_mel_free(self.h)
+            self.h = None
+
+
+def mel_spectrogram(samples):
+    """One-shot log-mel (vox_cuda_mel_spectrogram): [n // 160, 128]."""
+    samples = np.ascontiguousarray(samples, np.float32)
+    cap = max(samples.size // 160, 1)
+    out = np.empty((cap, MEL_BINS), np.float32)
+    n = check(lib().vox_cuda_mel_spectrogram(_f(samples), samples.size, _f(out), cap), "mel_spectrogram")
+    return out[:n]
