@@ -330,6 +330,7 @@ def encoder_bench(V, torch, steps, only_rows=0):
         out["audio_s_per_s"][f"M{M}"] = (M / 50.0) / (ms / 1000.0)
     if not only_rows:
         out["multi_stream_M100"] = multi_stream_encoder(enc, torch, x0, steps)
+        out["front_end_2s_chunks"] = front_bench(V, torch, steps)
     if only_rows and only_rows != 1500:
         st.free()
         enc.free()
@@ -392,6 +393,57 @@ def multi_stream_encoder(enc, torch, x0, steps, streams=8, rows=100):
     res["streams"], res["rows_per_chunk"] = streams, rows
     for st in states:
         st.free()
+    return res
+
+
+def front_bench(V, torch, steps, streams=8):
+    """The audio front end per 2 s chunk of every stream (configs[4]'s feed
+    interval): 32000 samples -> 200 log-mel frames (vox_cuda_mel_feed_dev) ->
+    100 conv-stem rows (vox_cuda_conv_stem_step_dev), each stream on its own
+    CUDA stream, no host waits.  Random-init conv weights."""
+    rng = np.random.default_rng(5)
+    w0 = (rng.standard_normal((ENC_D, 128, 3)) * 0.02).astype(np.float32)
+    w1 = (rng.standard_normal((ENC_D, ENC_D, 3)) * 0.02).astype(np.float32)
+    b0 = (rng.standard_normal(ENC_D) * 0.02).astype(np.float32)
+    b1 = (rng.standard_normal(ENC_D) * 0.02).astype(np.float32)
+    chunk = 32000
+    mels = [V.Mel(32 * 1280, chunk) for _ in range(streams)]
+    stems = [V.ConvStem(w0, b0, w1, b1, max_mel=512) for _ in range(streams)]
+    cstreams = [torch.cuda.Stream() for _ in range(streams)]
+    main = torch.cuda.Stream()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(91)
+    audio = (torch.rand((streams, chunk), generator=gen, device="cuda") - 0.5) * 0.2
+    mel_out = [torch.empty((512, 128), dtype=torch.float32, device="cuda") for _ in range(streams)]
+    conv_out = [torch.empty((256, ENC_D), dtype=torch.float32, device="cuda") for _ in range(streams)]
+
+    def round_(mel_only):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(main)
+        for i in range(streams):
+            cs = cstreams[i]
+            cs.wait_event(e0)
+            n = mels[i].feed_dev(audio[i].data_ptr(), chunk, mel_out[i].data_ptr(), 512, cs.cuda_stream)
+            if not mel_only:
+                stems[i].step_dev(mel_out[i].data_ptr(), n, conv_out[i].data_ptr(), cs.cuda_stream)
+        for cs in cstreams:
+            main.wait_stream(cs)
+        e1.record(main)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    res = {}
+    for mel_only in (True, False):
+        for _ in range(3):
+            round_(mel_only)
+        ms = statistics.median(round_(mel_only) for _ in range(max(3, steps // 2)))
+        key = "mel" if mel_only else "mel_and_stem"
+        res[key] = {"ms_per_round": ms, "audio_s_per_s": streams * 2.0 / (ms / 1000.0)}
+    res["streams"], res["samples_per_chunk"], res["mel_frames_per_chunk"] = streams, chunk, 200
+    for m in mels:
+        m.free()
+    for s_ in stems:
+        s_.free()
     return res
 
 

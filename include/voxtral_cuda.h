@@ -334,6 +334,13 @@ int vox_cuda_conv_stem_reset(vox_cuda_conv_stem *s);
  * consumed before (0 is possible), or a negative error.  out must hold
  * n_new / 2 + 1 rows. */
 int vox_cuda_conv_stem_step(vox_cuda_conv_stem *s, const float *mel_new, int n_new, float *out);
+/* Device-resident form: mel_dev [n_new, 128] and out_dev [rows, 1280] on the
+ * device, enqueued on `stream` without waiting (the mel context's _dev rows
+ * feed it directly, and its rows the encoder's step_dev).  Returns rows; a
+ * GEMM wait that timed out is reported by a later call.  Synchronous entry
+ * points on the state are ordered after the pending steps. */
+int vox_cuda_conv_stem_step_dev(vox_cuda_conv_stem *s, const float *mel_dev, int n_new, float *out_dev,
+                                void *stream);
 
 /* ------------------------------------------------------------------------
  * (6) log-mel front end: 16 kHz mono fp32 samples -> [frames, 128] log-mel

@@ -346,6 +346,79 @@ def gen_mel():
     np.savez_compressed(os.path.join(HERE, "mel.npz"), **out)
 
 
+# Audio front end end to end: samples -> incremental log-mel -> conv stem ->
+# encoder -> adapter, chunked as the stream path chunks it
+# (stream_run_encoder, voxtral.c:668-690): the first conv-stem call once 312
+# mel frames are pending, later ones at 200; vox_stream_finish feeds the
+# right pad as zeros (align to 1280 + (delay 6 + 1 + 10) tokens), finishes
+# the mel and runs the rest (voxtral.c:979-1007).
+FRONT_SAMPLES = 48000
+FRONT_FEED = 8000
+FRONT_LEFT_PAD = 32 * 1280
+FRONT_DELAY = 6
+
+
+def front_right_pad(n_samples):
+    align = (1280 - n_samples % 1280) % 1280
+    return align + (FRONT_DELAY + 1 + 10) * 1280
+
+
+def front_stem_chunks(feed_frames, finish_frames):
+    """Mel frames per conv-stem call for the given frames per feed."""
+    chunks, pending, first = [], 0, True
+    for n in feed_frames:
+        pending += n
+        if pending >= (312 if first else 200):
+            chunks.append(pending)
+            pending, first = 0, False
+    pending += finish_frames
+    if pending > 0:
+        chunks.append(pending)
+    return chunks
+
+
+def front_audio(seed=8401):
+    return B.synthetic_audio(FRONT_SAMPLES, seed)
+
+
+def gen_front(ew):
+    out = {}
+    x = front_audio()
+    out["audio_sum"] = checksum(x)
+    mel = B.RefMel(FRONT_LEFT_PAD)
+    rows = [mel.feed(x[o:o + FRONT_FEED]) for o in range(0, FRONT_SAMPLES, FRONT_FEED)]
+    z = front_right_pad(FRONT_SAMPLES)
+    tail = []
+    while z > 0:
+        c = min(z, 4096)
+        tail.append(mel.feed(np.zeros(c, np.float32)))
+        z -= c
+    tail.append(mel.finish(0))
+    mel.free()
+    feed_frames = [r.shape[0] for r in rows]
+    fin = sum(t.shape[0] for t in tail)
+    chunks = front_stem_chunks(feed_frames, fin)
+    out["stem_chunks"] = np.array(chunks, np.int32)
+    all_mel = np.concatenate(rows + tail, axis=0)
+    assert all_mel.shape[0] == sum(chunks)
+    stem = B.RefStem(B.ConvStemWeights(seed=DEC_SEED))
+    ref = B.RefCtx(enc=ew)
+    enc, off = [], 0
+    for i, n in enumerate(chunks):
+        conv = stem.step(all_mel[off:off + n])
+        off += n
+        out[f"stem{i}_rows"] = np.int32(conv.shape[0])
+        if conv.shape[0]:
+            enc.append(ref.encoder_incremental(conv))
+    enc = np.concatenate(enc, axis=0)
+    pack("encoder", enc, out)
+    usable = enc.shape[0] // 4 * 4
+    pack("adapter", ref.adapter(enc[:usable]), out)
+    stem.free()
+    ref.free()
+    np.savez_compressed(os.path.join(HERE, "front.npz"), **out)
+
+
 ALT_CASES = [(61, 3.0, 4, 0.999), (62, 0.5, 4, 0.5), (63, 8.0, 3, 0.99), (64, 1.0, 2, 0.9),
              (65, 0.01, 4, 0.999)]
 
@@ -364,6 +437,10 @@ def gen_alts():
 def main():
     assert B.ref_available(), "build oracle/_ref first (make -C oracle ref)"
     t = time.time()
+    if sys.argv[1:] == ["front"]:   # only the audio front end chain
+        gen_front(B.EncoderWeights(seed=DEC_SEED))
+        print("front", time.time() - t)
+        return
     if sys.argv[1:] == ["mel"]:   # only the log-mel front end
         gen_mel()
         print("mel", time.time() - t)
@@ -388,6 +465,7 @@ def main():
     ew = B.EncoderWeights(seed=DEC_SEED)
     gen_encoder(ew); print("encoder", time.time() - t)
     gen_chain(B.DecoderWeights(seed=DEC_SEED), ew); print("chain", time.time() - t)
+    gen_front(ew); print("front", time.time() - t)
 
 
 if __name__ == "__main__":

@@ -2296,6 +2296,10 @@ struct vox_cuda_conv_stem {
     uint16_t *a1 = nullptr;         // [max_out][3840] conv1 im2col
     float *out = nullptr;           // [max_out][1280]
     unsigned *err = nullptr;
+    // asynchronous steps (step_dev): deferred error flag, ordering event
+    unsigned *h_err = nullptr;      // pinned
+    cudaEvent_t err_ev = nullptr, tail = nullptr;
+    bool err_pending = false, tail_set = false;
 };
 
 extern "C" vox_cuda_conv_stem *vox_cuda_conv_stem_create(const float *conv0_weight, const float *conv0_bias,
@@ -2348,7 +2352,11 @@ extern "C" vox_cuda_conv_stem *vox_cuda_conv_stem_create(const float *conv0_weig
               cudaMemcpy(stage, conv1_weight, n_w1 * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
               launch_f32_to_f16(stage, s->w1, n_w1, 0) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
               cudaMemcpy(s->b0, conv0_bias, kEncDim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-              cudaMemcpy(s->b1, conv1_bias, kEncDim * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+              cudaMemcpy(s->b1, conv1_bias, kEncDim * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaHostAlloc((void **)&s->h_err, sizeof(unsigned), cudaHostAllocDefault) == cudaSuccess &&
+              cudaEventCreateWithFlags(&s->err_ev, cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreateWithFlags(&s->tail, cudaEventDisableTiming) == cudaSuccess;
+    if (s->h_err) *s->h_err = 0;
     if (!ok) {
         set_error("conv_stem_create: weight upload failed");
         vox_cuda_conv_stem_free(s);
@@ -2362,9 +2370,12 @@ extern "C" void vox_cuda_conv_stem_free(vox_cuda_conv_stem *s) {
     DevCtx *c = ctx_for(s->device);
     cudaSetDevice(s->device);
     if (c) {
-        cudaStreamSynchronize(c->stream);
+        cudaStreamSynchronize(c->stream);   // also waits for asynchronous steps (see step_dev)
         dev_free(c, s->ws, s->ws ? s->ws_bytes : 0);
     }
+    if (s->h_err) cudaFreeHost(s->h_err);
+    if (s->err_ev) cudaEventDestroy(s->err_ev);
+    if (s->tail) cudaEventDestroy(s->tail);
     delete s;
 }
 
@@ -2380,24 +2391,14 @@ extern "C" int vox_cuda_conv_stem_reset(vox_cuda_conv_stem *s) {
     return VOX_CUDA_OK;
 }
 
-extern "C" int vox_cuda_conv_stem_step(vox_cuda_conv_stem *s, const float *mel_new, int n_new, float *out) {
-    if (!s || !mel_new || !out || n_new <= 0) {
-        set_error("conv_stem_step: bad arguments");
-        return VOX_CUDA_ERR_ARG;
-    }
-    if (n_new > s->max_mel) {
-        set_error("conv_stem_step: %d mel frames exceed the state's %d", n_new, s->max_mel);
-        return VOX_CUDA_ERR_CAPACITY;
-    }
-    DevCtx *c = ctx_for(s->device);
-    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
-    cudaSetDevice(s->device);
-    std::lock_guard<std::mutex> lk(c->mu);
-    cudaStream_t st = c->stream;
+namespace {
+
+// One stem step's kernels: mel [n_new][128] (device) -> out [n_out][1280]
+// (device), the streaming state updated on the device.  Returns n_out.
+int stem_enqueue(vox_cuda_conv_stem *s, const float *mel, int n_new, float *out, cudaStream_t st) {
     const long long f0 = s->frames, u0 = f0 / 2;
     const int n_out = (int)((f0 + n_new) / 2 - u0);
-    VC_TRY(cudaMemcpyAsync(s->mel, mel_new, (size_t)n_new * 128 * 4, cudaMemcpyHostToDevice, st));
-    VC_TRY(launch_stem_im2col0(s->mel, s->mel_hist, n_new, s->a0, st));
+    VC_TRY(launch_stem_im2col0(mel, s->mel_hist, n_new, s->a0, st));
     TcGemmParams p = {};
     p.M = n_new;
     p.N = kEncDim;
@@ -2417,22 +2418,83 @@ extern "C" int vox_cuda_conv_stem_step(vox_cuda_conv_stem *s, const float *mel_n
         p.K = 3 * kEncDim;
         p.bias = s->b1;
         p.act = 1;             // GELU (voxtral.c:648)
-        p.out = s->out;
+        p.out = out;
         p.ldo = kEncDim;
         p.err = s->err;
         p.f16 = 1;
         VC_TRY(launch_tc_gemm(TC_STORE, p, s->a1, s->w1, st, false));
-        VC_TRY(cudaMemcpyAsync(out, s->out, (size_t)n_out * kEncDim * 4, cudaMemcpyDeviceToHost, st));
     }
-    VC_TRY(launch_stem_state(s->mel, n_new, s->mel_hist, s->c0, s->c0_hist, st));
+    VC_TRY(launch_stem_state(mel, n_new, s->mel_hist, s->c0, s->c0_hist, st));
+    s->frames += n_new;
+    return n_out;
+}
+
+int stem_check(vox_cuda_conv_stem *s, const void *mel, int n_new, const void *out, const char *what) {
+    if (!s || !mel || !out || n_new <= 0) {
+        set_error("%s: bad arguments", what);
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (n_new > s->max_mel) {
+        set_error("%s: %d mel frames exceed the state's %d", what, n_new, s->max_mel);
+        return VOX_CUDA_ERR_CAPACITY;
+    }
+    if (!ctx_for(s->device)) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(s->device);
+    return VOX_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" int vox_cuda_conv_stem_step(vox_cuda_conv_stem *s, const float *mel_new, int n_new, float *out) {
+    int rc = stem_check(s, mel_new, n_new, out, "conv_stem_step");
+    if (rc) return rc;
+    DevCtx *c = ctx_for(s->device);
+    std::lock_guard<std::mutex> lk(c->mu);
+    cudaStream_t st = c->stream;
+    VC_TRY(cudaMemcpyAsync(s->mel, mel_new, (size_t)n_new * 128 * 4, cudaMemcpyHostToDevice, st));
+    const int n_out = stem_enqueue(s, s->mel, n_new, s->out, st);
+    if (n_out < 0) return n_out;
+    if (n_out > 0)
+        VC_TRY(cudaMemcpyAsync(out, s->out, (size_t)n_out * kEncDim * 4, cudaMemcpyDeviceToHost, st));
     unsigned h_err = 0;
     VC_TRY(cudaMemcpyAsync(&h_err, s->err, 4, cudaMemcpyDeviceToHost, st));
     VC_TRY(cudaStreamSynchronize(st));
+    s->err_pending = false;   // this check covered the asynchronous steps before it
     if (h_err) {
+        cudaMemset(s->err, 0, sizeof(unsigned));
         set_error("conv_stem_step: a tensor-core GEMM wait timed out");
         return VOX_CUDA_ERR_CUDA;
     }
-    s->frames += n_new;
+    return n_out;
+}
+
+extern "C" int vox_cuda_conv_stem_step_dev(vox_cuda_conv_stem *s, const float *mel_dev, int n_new, float *out_dev,
+                                           void *stream) {
+    int rc = stem_check(s, mel_dev, n_new, out_dev, "conv_stem_step_dev");
+    if (rc) return rc;
+    DevCtx *c = ctx_for(s->device);
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    // a timeout raised by an earlier asynchronous step is reported now
+    if (s->err_pending && cudaEventQuery(s->err_ev) == cudaSuccess) {
+        s->err_pending = false;
+        if (*s->h_err) {
+            *s->h_err = 0;
+            VC_TRY(cudaMemsetAsync(s->err, 0, sizeof(unsigned), st));
+            set_error("conv_stem: a tensor-core GEMM wait of an earlier step timed out (its rows are invalid)");
+            return VOX_CUDA_ERR_CUDA;
+        }
+    }
+    if (s->tail_set && st != c->stream) VC_TRY(cudaStreamWaitEvent(st, s->tail, 0));
+    const int n_out = stem_enqueue(s, mel_dev, n_new, out_dev, st);
+    if (n_out < 0) return n_out;
+    if (!s->err_pending) {
+        VC_TRY(cudaMemcpyAsync(s->h_err, s->err, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+        VC_TRY(cudaEventRecord(s->err_ev, st));
+        s->err_pending = true;
+    }
+    VC_TRY(cudaEventRecord(s->tail, st));
+    if (st != c->stream) VC_TRY(cudaStreamWaitEvent(c->stream, s->tail, 0));
+    s->tail_set = true;
     return n_out;
 }
 

@@ -121,6 +121,7 @@ def lib():
         "vox_cuda_conv_stem_free": ([C.c_void_p], None),
         "vox_cuda_conv_stem_reset": ([C.c_void_p], C.c_int),
         "vox_cuda_conv_stem_step": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
+        "vox_cuda_conv_stem_step_dev": ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
         "vox_cuda_mel_create": ([C.c_int, C.c_int], C.c_void_p),
         "vox_cuda_mel_free": ([C.c_void_p], None),
         "vox_cuda_mel_frames": ([C.c_void_p], C.c_int),
@@ -410,6 +411,11 @@ class ConvStem:
         out = np.empty((mel.shape[0] // 2 + 1, 1280), np.float32)
         n = check(lib().vox_cuda_conv_stem_step(self.h, _f(mel), mel.shape[0], _f(out)), "conv_stem_step")
         return out[:n]
+
+    def step_dev(self, mel_dev, n_new, out_dev, stream=None):
+        """Device addresses; returns the rows written to out_dev."""
+        return check(lib().vox_cuda_conv_stem_step_dev(self.h, mel_dev, n_new, out_dev, stream),
+                     "conv_stem_step_dev")
 
     def reset(self):
         check(lib().vox_cuda_conv_stem_reset(self.h), "conv_stem_reset")
