@@ -396,6 +396,37 @@ def multi_stream_encoder(enc, torch, x0, steps, streams=8, rows=100):
     return res
 
 
+def prefill_bench(V, dec, layers, prompt=38, reps=5):
+    """Stream start: the 38-row prompt prefill (voxtral.c:843-891) of one
+    stream, and of three streams in shared launches (vox_cuda_decoder_
+    prefill_batch), on the tensor cores.  Host rows in, KV rings written;
+    wall clock around the synchronous call.  Roofline: every launch sequence
+    streams the layers' weights once (HBM-bound at these row counts)."""
+    rng = np.random.default_rng(3)
+    out = {}
+    hbm, _ = peaks()
+    w_bytes = layers * ((QD + 2 * KVD) * D + D * QD + 2 * HID * D + D * HID) * 2
+    for n_streams in (1, 3):
+        sts = [dec.state(kv_cap=1024) for _ in range(n_streams)]
+        rows = [(rng.standard_normal((prompt, D)) * 0.5).astype(np.float32) for _ in range(n_streams)]
+        times = []
+        for r in range(reps + 2):
+            for st in sts:
+                st.set_position(0)
+            t0 = time.perf_counter()
+            V.prefill_batch(sts, rows)
+            if r >= 2:
+                times.append(time.perf_counter() - t0)
+        ms = statistics.median(times) * 1000.0
+        out[f"streams{n_streams}"] = {"rows": n_streams * prompt, "ms": ms,
+                                      "weight_gbs": w_bytes / (ms / 1000.0) / 1e9,
+                                      "frac_of_hbm": w_bytes / (ms / 1000.0) / 1e9 / hbm}
+        for st in sts:
+            st.free()
+    out["weight_bytes_per_launch_sequence"] = w_bytes
+    return out
+
+
 def front_bench(V, torch, steps, streams=8):
     """The audio front end per 2 s chunk of every stream (configs[4]'s feed
     interval): 32000 samples -> 200 log-mel frames (vox_cuda_mel_feed_dev) ->
@@ -555,6 +586,7 @@ def our_arm(args):
     kv_bytes = sum(args.layers * min(p + 1, 8192) * KVD * 4 * 2 for p in pos)
     step_bytes = weight_bytes_per_step(args.layers, args.vocab) + kv_bytes
 
+    pf_res = prefill_bench(V, dec, args.layers)
     for st in states:
         st.free()
     dec.free()
@@ -592,6 +624,7 @@ def our_arm(args):
             "step_roofline": {"bytes_per_step": step_bytes,
                               "achieved_gbs": step_bytes / (ms_step / 1000.0) / 1e9,
                               "frac": step_bytes / (ms_step / 1000.0) / 1e9 / hbm},
+            "prefill": pf_res,
             "phase_ms": prof,
             "launch_ms_in_sequence": seq_ms,
             "clocks": clk.summary(),

@@ -186,6 +186,19 @@ int vox_cuda_decoder_fill_alts(vox_cuda_dec_state *s, int n_alt, float cutoff, i
 int vox_cuda_decoder_prefill_step(vox_cuda_dec_state *s, const float *x, int seq_len,
                                   const float *rope_freqs);
 
+/* Prefill of several streams in shared launches: state i takes the next
+ * seq_lens[i] rows of x (host [sum seq_lens, 3072]; rope_freqs host
+ * [sum seq_lens][64][2] or NULL) from its current position.  Up to 128 rows
+ * (e.g. three streams' 38-row prompts) share each tensor-core GEMM, whose
+ * weight reads dominate at these sizes.  The prefill runs on the tcgen05
+ * tensor cores with bf16 weights and activations split into bf16 hi + lo
+ * (fp32-level products); VOX_CUDA_DEC_TC_PREFILL=0 at decoder creation keeps
+ * no row-major weight copies (-6 GB at 4B) and prefills through the decode
+ * kernels instead.  Additive: the reference prefills one context at a time
+ * (voxtral.c:843-891). */
+int vox_cuda_decoder_prefill_batch(vox_cuda_dec_state *const *states, int n, const float *x,
+                                   const int *seq_lens, const float *rope_freqs);
+
 /* Batched decode step over n independent streams that share one decoder:
  * the weights are read once for all n tokens (n <= 8).  embeds: host
  * [n, 3072]; tokens: host [n].  An additive entry with no single-stream

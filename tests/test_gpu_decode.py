@@ -317,3 +317,70 @@ def test_profile_sequence_times_every_phase(small_w):
     for st in states:
         st.free()
     d.free()
+
+
+# ---------------------------------------------------------------------------
+# tensor-core prefill (default) against the decode-kernel prefill
+# ---------------------------------------------------------------------------
+
+PREFILL_TOL = 1e-4   # the prefill K / V bound against the reference's golden
+
+def test_tc_prefill_matches_decode_kernel_prefill(small_w, monkeypatch):
+    """The tcgen05 prefill (bf16 weights, activations as bf16 hi + lo)
+    against the prefill through the decode-step kernels (fragment GEMV, same
+    split): K / V rows of every layer and the next step's logits.  150 rows
+    span two 128-row launch sequences.  Both sit ~1e-5 from the fp32
+    reference (its golden bound is 1e-4); their distance grows with depth
+    (~2e-5 after 3 layers), so the bound here is the golden one."""
+    a = make_gpu_decoder(small_w)
+    monkeypatch.setenv("VOX_CUDA_DEC_TC_PREFILL", "0")
+    b = make_gpu_decoder(small_w)
+    monkeypatch.delenv("VOX_CUDA_DEC_TC_PREFILL")
+    for n in (38, 150):
+        sa, sb = a.state(kv_cap=256), b.state(kv_cap=256)
+        prompt = B.normal_f32((n, B.DEC_DIM), 950 + n)
+        sa.prefill(prompt)
+        sb.prefill(prompt)
+        for layer in range(small_w.n_layers):
+            ka, va = sa.read_kv(layer, 0, n)
+            kb, vb = sb.read_kv(layer, 0, n)
+            assert B.rel_l2(ka, kb) < PREFILL_TOL and B.rel_l2(va, vb) < PREFILL_TOL, (n, layer, B.rel_l2(ka, kb))
+        e = B.normal_f32(B.DEC_DIM, 960 + n)
+        ta, la = sa.step(e)
+        tb, lb = sb.step(e)
+        assert B.rel_l2(la, lb) < PREFILL_TOL
+        assert ta == tb or np.sort(lb)[-1] - np.sort(lb)[-2] <= MARGIN
+        sa.free()
+        sb.free()
+    a.free()
+    b.free()
+
+
+def test_prefill_batch_matches_one_state_at_a_time(small_w):
+    """Several streams' prompts in shared tensor-core launches (one with no
+    rows, one continuing from position 7) equal per-state prefills."""
+    d = make_gpu_decoder(small_w)
+    lens = [5, 38, 0, 90]
+    rows = [B.normal_f32((n, B.DEC_DIM), 970 + i) if n else np.zeros((0, B.DEC_DIM), np.float32)
+            for i, n in enumerate(lens)]
+    one = [d.state(kv_cap=256) for _ in lens]
+    many = [d.state(kv_cap=256) for _ in lens]
+    pre = B.normal_f32((7, B.DEC_DIM), 990)
+    one[3].prefill(pre)
+    many[3].prefill(pre)
+    for st, r in zip(one, rows):
+        if r.shape[0]:
+            st.prefill(r)
+    V.prefill_batch(many, rows)
+    for i, n in enumerate(lens):
+        assert many[i].position == one[i].position
+        if n == 0:
+            continue
+        first = 7 if i == 3 else 0
+        for layer in (0, small_w.n_layers - 1):
+            k1, v1 = one[i].read_kv(layer, first, n)
+            k2, v2 = many[i].read_kv(layer, first, n)
+            assert B.rel_l2(k1, k2) < PREFILL_TOL and B.rel_l2(v1, v2) < PREFILL_TOL, (i, layer)
+    for st in one + many:
+        st.free()
+    d.free()

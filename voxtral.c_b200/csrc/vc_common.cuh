@@ -98,6 +98,12 @@ __device__ __forceinline__ uint32_t bf16_bits_rn(float f) {
     return u >> 16;
 }
 
+// Split-activation layout of the tensor-core prefill: row r of a matrix x
+// is stored as bf16 hi = bf16(x_r) at hilo_row(r) and lo = bf16(x_r - hi) at
+// hilo_row(r) + 64, i.e. every 64 rows form one 128-row MMA tile [hi; lo].
+__host__ __device__ __forceinline__ int hilo_row(int r) { return ((r >> 6) << 7) + (r & 63); }
+__host__ __device__ __forceinline__ int hilo_rows(int M) { return ((M + 63) >> 6) << 7; }
+
 __device__ __forceinline__ void split_bf16(float v, uint32_t &hi, uint32_t &lo) {
     hi = bf16_bits_rn(v);
     lo = bf16_bits_rn(v - __uint_as_float(hi << 16));

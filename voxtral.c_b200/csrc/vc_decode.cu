@@ -7,6 +7,7 @@
 #include <math.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <atomic>
 
 namespace vc {
@@ -252,6 +253,17 @@ attn_decode_kernel(const AttnParams p) {
             xfrag_put2(p.xfrag_out, m, h * kHeadDim + d4, o0, o1);
             xfrag_put2(p.xfrag_out, m, h * kHeadDim + d4 + 2, o2, o3);
         }
+        if (p.out_hilo != nullptr) {
+            uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
+            split_bf16(o0, h0, l0);
+            split_bf16(o1, h1, l1);
+            split_bf16(o2, h2, l2);
+            split_bf16(o3, h3, l3);
+            const size_t e = (size_t)hilo_row(m) * kQDim + h * kHeadDim + d4;
+            *reinterpret_cast<uint2 *>(p.out_hilo + e) = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
+            *reinterpret_cast<uint2 *>(p.out_hilo + e + (size_t)64 * kQDim) =
+                make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
+        }
         if (tid == 0) p.counters[m * kDecKvHeads + kvh] = 0u;
     }
 }
@@ -281,7 +293,10 @@ cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool
         attr_set.fetch_or(bit);
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(attn_ctas_per_head(M), kDecKvHeads, M);
+    // CTAs per (row, KV head): no more than the splits this launch can have
+    // (a prefill of fresh rows attends to few keys: S = 1)
+    const int g = std::min(attn_ctas_per_head(M), std::max(1, p.S));
+    cfg.gridDim = dim3(g, kDecKvHeads, M);
     cfg.blockDim = dim3(128);
     cfg.dynamicSmemBytes = sizeof(AttnShared);
     cfg.stream = st;

@@ -86,6 +86,12 @@ __device__ __forceinline__ uint16_t bits16(float a, int f16) {
     return f16 ? __half_as_ushort(__float2half_rn(a)) : (uint16_t)bf16_bits_rn(a);
 }
 
+// v = hi + lo in bf16: hi = bf16(v), lo = bf16(v - hi) (~2^-17 relative)
+__device__ __forceinline__ float bf16_hi_f(float v) { return __uint_as_float(bf16_bits_rn(v) << 16); }
+__device__ __forceinline__ uint32_t pack_bf16_lo2(float a, float b) {
+    return pack_bf16x2(a - bf16_hi_f(a), b - bf16_hi_f(b));
+}
+
 __device__ __forceinline__ void st16(void *dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     *reinterpret_cast<uint4 *>(dst) = make_uint4(a, b, c, d);
 }
@@ -95,7 +101,65 @@ struct EpiRow {
     int row;        // output row (this thread's TMEM lane)
     int pos;        // TC_QKV_ENC: logical position of the row
     size_t slot;    // TC_QKV_ENC: ring slot of the row
+    float *kd, *vd; // TC_QKV_DEC: the row's K / V ring rows (this layer)
 };
+
+// The per-row facts of TC_QKV_ENC / TC_QKV_DEC for output row `row`.
+template <int EPI>
+__device__ __forceinline__ EpiRow epi_row(const TcGemmParams &p, int row) {
+    EpiRow er;
+    er.row = row;
+    er.pos = 0;
+    er.slot = 0;
+    er.kd = er.vd = nullptr;
+    if constexpr (EPI == TC_QKV_ENC) {
+        er.pos = (p.pos0_dev ? *p.pos0_dev : p.pos0) + row;
+        er.slot = (size_t)(er.pos % p.cap);
+    }
+    if constexpr (EPI == TC_QKV_DEC) {
+        if (row < p.M) {
+            const StreamSlot sl = p.slots[row];
+            const size_t off = ((size_t)p.layer * sl.cap + sl.slot) * kKvDim;
+            er.kd = sl.k_ring + off;
+            er.vd = sl.v_ring + off;
+        }
+    }
+    return er;
+}
+
+// Decoder q|k RoPE of one row's 16 pairs at pair indices d0..d0+15 of a
+// 128-wide head (vox_apply_rope, voxtral_kernels.c:505-526, as the prefill
+// applies it, voxtral_decoder.c:303-306), cos / sin from the row's table.
+__device__ __forceinline__ void dec_rope_chunk(const TcGemmParams &p, const EpiRow &er, int d0, float (&v)[kEpiCols]) {
+    const float4 *t = reinterpret_cast<const float4 *>(p.rope_rows + (size_t)er.row * kHeadDim + 2 * d0);
+    float4 cs[kEpiCols / 4];
+#pragma unroll
+    for (int i = 0; i < kEpiCols / 4; i++) cs[i] = __ldg(t + i);   // (cos, sin) of 2 pairs each
+#pragma unroll
+    for (int i = 0; i < kEpiCols / 4; i++) {
+        const float c0 = cs[i].x, s0 = cs[i].y, c1 = cs[i].z, s1 = cs[i].w;
+        float a = v[4 * i], b = v[4 * i + 1];
+        v[4 * i] = __fsub_rn(__fmul_rn(a, c0), __fmul_rn(b, s0));
+        v[4 * i + 1] = __fadd_rn(__fmul_rn(a, s0), __fmul_rn(b, c0));
+        a = v[4 * i + 2], b = v[4 * i + 3];
+        v[4 * i + 2] = __fsub_rn(__fmul_rn(a, c1), __fmul_rn(b, s1));
+        v[4 * i + 3] = __fadd_rn(__fmul_rn(a, s1), __fmul_rn(b, c1));
+    }
+}
+
+// The q|k|v region of decoder column col0 (32-column chunks never straddle
+// two): [0,4096) q (RoPE), [4096,5120) k (RoPE), [5120,6144) v.
+__device__ __forceinline__ int dec_qkv_apply(const TcGemmParams &p, const EpiRow &er, float (&v)[kEpiCols], int col0) {
+    if (col0 >= kQDim + kKvDim) return 2;
+    dec_rope_chunk(p, er, (col0 & (kHeadDim - 1)) >> 1, v);
+    return col0 < kQDim ? 0 : 1;
+}
+
+__device__ __forceinline__ float *dec_qkv_dst(const TcGemmParams &p, const EpiRow &er, int col0, int region) {
+    return region == 0 ? p.q32 + (size_t)er.row * kQDim + col0
+           : region == 1 ? er.kd + (col0 - kQDim)
+                         : er.vd + (col0 - kQDim - kKvDim);
+}
 
 // Encoder q|k RoPE of one row's 16 pairs (v[2i], v[2i+1]) at pair indices
 // d0..d0+15 of a head (vox_apply_rope, voxtral_kernels.c:505-526; cos/sin as
@@ -191,9 +255,25 @@ __device__ __forceinline__ void epi_vec(const TcGemmParams &p, const EpiRow &er,
 #pragma unroll
         for (int j = 0; j < kEpiCols; j += 4)
             h[j >> 2] = pack16x2(silu_fast(v[j]) * v[j + 1], silu_fast(v[j + 2]) * v[j + 3], p.f16);
-        uint16_t *o = p.out_bf16 + (size_t)row * p.ldo_bf16 + (col0 >> 1);
+        const int orow = p.out_hilo ? hilo_row(row) : row;
+        uint16_t *o = p.out_bf16 + (size_t)orow * p.ldo_bf16 + (col0 >> 1);
 #pragma unroll
         for (int j = 0; j < kEpiCols / 4; j += 4) st16(o + 2 * j, h[j], h[j + 1], h[j + 2], h[j + 3]);
+        if (p.out_hilo) {   // the lo rows for a split-activation consumer (bf16 only)
+            float hv[kEpiCols / 2];
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j += 2) hv[j >> 1] = silu_fast(v[j]) * v[j + 1];
+            uint16_t *ol = p.out_bf16 + (size_t)(orow + 64) * p.ldo_bf16 + (col0 >> 1);
+#pragma unroll
+            for (int j = 0; j < kEpiCols / 2; j += 8)
+                st16(ol + j, pack_bf16_lo2(hv[j], hv[j + 1]), pack_bf16_lo2(hv[j + 2], hv[j + 3]),
+                     pack_bf16_lo2(hv[j + 4], hv[j + 5]), pack_bf16_lo2(hv[j + 6], hv[j + 7]));
+        }
+    } else if constexpr (EPI == TC_QKV_DEC) {
+        float *dst = dec_qkv_dst(p, er, col0, region);
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 4)
+            *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     } else if constexpr (EPI == TC_QKV_ENC) {
         uint16_t *dst = region == 0   ? p.q_out + (size_t)row * kEncQkv + col0
                         : region == 1 ? p.k_ring + er.slot * kEncQkv + (col0 - kEncQkv)
@@ -224,12 +304,21 @@ __device__ __forceinline__ void epi_scalar(const TcGemmParams &p, const EpiRow &
             else o[j] = x;
         }
     } else if constexpr (EPI == TC_SWIGLU) {
-        uint16_t *o = p.out_bf16 + (size_t)row * p.ldo_bf16 + (col0 >> 1);
+        const int orow = p.out_hilo ? hilo_row(row) : row;
+        uint16_t *o = p.out_bf16 + (size_t)orow * p.ldo_bf16 + (col0 >> 1);
 #pragma unroll
         for (int j = 0; j < kEpiCols; j += 2) {
             if (col0 + j + 1 >= p.N) break;
-            o[j >> 1] = bits16(silu_fast(v[j]) * v[j + 1], p.f16);
+            const float h = silu_fast(v[j]) * v[j + 1];
+            o[j >> 1] = bits16(h, p.f16);
+            if (p.out_hilo)
+                p.out_bf16[(size_t)(orow + 64) * p.ldo_bf16 + ((col0 + j) >> 1)] =
+                    (uint16_t)bf16_bits_rn(h - bf16_hi_f(h));
         }
+    } else if constexpr (EPI == TC_QKV_DEC) {
+        float *dst = dec_qkv_dst(p, er, col0, region);
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j++) dst[j] = v[j];
     } else if constexpr (EPI == TC_QKV_ENC) {
         uint16_t *dst = region == 0   ? p.q_out + (size_t)row * kEncQkv + col0
                         : region == 1 ? p.k_ring + er.slot * kEncQkv + (col0 - kEncQkv)
@@ -254,6 +343,9 @@ struct EpiMaps {
 template <int EPI>
 __device__ __forceinline__ void epi_tma(const TcGemmParams &p, const EpiMaps &mp, const EpiRow &er,
                                         float (&v)[kEpiCols], int row0, int col0, int lane, unsigned char *stg) {
+    if constexpr (EPI == TC_QKV_DEC) {
+        return;   // launch_tc_gemm never enables TMA stores for it
+    }
     int region = 0;
     if constexpr (EPI == TC_QKV_ENC) {
         region = qkv_apply(p, er, v, col0);
@@ -324,14 +416,7 @@ template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const TcGemmParams &p, const EpiMaps &mp, uint32_t tbase, int row0,
                                               int n0, int half, int lane, unsigned char *stg) {
     static_assert(BN % (2 * kEpiCols) == 0, "each epilogue warp takes whole 32-column chunks");
-    EpiRow er;
-    er.row = row0 + lane;
-    er.pos = 0;
-    er.slot = 0;
-    if constexpr (EPI == TC_QKV_ENC) {
-        er.pos = (p.pos0_dev ? *p.pos0_dev : p.pos0) + er.row;
-        er.slot = (size_t)(er.pos % p.cap);
-    }
+    const EpiRow er = epi_row<EPI>(p, row0 + lane);
     const bool rv = er.row < p.M;
 #pragma unroll 1
     for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
@@ -346,24 +431,26 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams &p, const EpiMa
         if (!rv) continue;
         int region = 0;
         if constexpr (EPI == TC_QKV_ENC) region = qkv_apply(p, er, v, col0);
+        if constexpr (EPI == TC_QKV_DEC) region = dec_qkv_apply(p, er, v, col0);
         if (p.vec && col0 + kEpiCols <= p.N) epi_vec<EPI>(p, er, v, col0, region);
         else epi_scalar<EPI>(p, er, v, col0, region);
     }
 }
 
 // Split-K: one warp's 32 rows x BN/2 columns of slice ks -> the fp32
-// workspace ws[ks][M][N] (rows / columns past M / N are not written).
+// workspace ws[ks][rows][N] (rows / columns past rows / N are not written;
+// rows = M, or the A rows of the split-activation layout).
 template <int BN>
 __device__ __forceinline__ void split_partial(const TcGemmParams &p, uint32_t tbase, int row0, int n0, int half,
-                                              int lane, int ks) {
+                                              int lane, int ks, int rows) {
     const int row = row0 + lane;
-    float *dst = p.ws + ((size_t)ks * p.M + row) * p.N;
+    float *dst = p.ws + ((size_t)ks * rows + row) * p.N;
 #pragma unroll 1
     for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
         float v[kEpiCols];
         tmem_ld32(tbase + (uint32_t)c, v);
         const int col0 = n0 + c;
-        if (row >= p.M || col0 >= p.N) continue;
+        if (row >= rows || col0 >= p.N) continue;
         if (col0 + kEpiCols <= p.N && (p.N & 3) == 0) {
 #pragma unroll
             for (int j = 0; j < kEpiCols; j += 4)
@@ -381,14 +468,7 @@ __device__ __forceinline__ void split_partial(const TcGemmParams &p, uint32_t tb
 template <int BN, int EPI>
 __device__ __forceinline__ void split_finish(const TcGemmParams &p, const EpiMaps &mp, int row0, int n0, int half,
                                              int lane, unsigned char *stg, int KS) {
-    EpiRow er;
-    er.row = row0 + lane;
-    er.pos = 0;
-    er.slot = 0;
-    if constexpr (EPI == TC_QKV_ENC) {
-        er.pos = (p.pos0_dev ? *p.pos0_dev : p.pos0) + er.row;
-        er.slot = (size_t)(er.pos % p.cap);
-    }
+    const EpiRow er = epi_row<EPI>(p, row0 + lane);
     const bool rv = er.row < p.M;
     const size_t slice = (size_t)p.M * p.N;
 #pragma unroll 1
@@ -434,12 +514,125 @@ __device__ __forceinline__ void split_finish(const TcGemmParams &p, const EpiMap
         if (!rv) continue;
         int region = 0;
         if constexpr (EPI == TC_QKV_ENC) region = qkv_apply(p, er, v, col0);
+        if constexpr (EPI == TC_QKV_DEC) region = dec_qkv_apply(p, er, v, col0);
         if (p.vec && col0 + kEpiCols <= p.N) epi_vec<EPI>(p, er, v, col0, region);
         else epi_scalar<EPI>(p, er, v, col0, region);
     }
 }
 
+// ---- split activations (p.hilo): accumulator rows r (hi) and r + 64 (lo)
+// of a tile belong to output row tm * 64 + r.  TMEM lane quarters 0, 1 hold
+// the hi rows, 2, 3 the lo rows; the epilogue warp of lo quarter q + 2 hands
+// its chunk to the warp of quarter q (same column half) through shared
+// memory, paced by two shared-memory counters per pair (chunks staged,
+// chunks consumed) whose waits are bounded like every other wait.
+
+// lane 0 spins until *f == want (or the deadline passes); warp-uniform result
+__device__ __forceinline__ bool flag_wait(volatile int *f, int want, uint64_t deadline, int lane) {
+    int bad = 0;
+    if (lane == 0) {
+        while (*f != want)
+            if (globaltimer() > deadline) {
+                bad = 1;
+                break;
+            }
+        __threadfence_block();
+    }
+    return __shfl_sync(0xffffffffu, bad, 0) == 0;
+}
+
+// The direct-store epilogue of one finished output chunk (token rows).
+template <int EPI>
+__device__ __forceinline__ void epi_direct(const TcGemmParams &p, const EpiRow &er, float (&v)[kEpiCols], int col0) {
+    int region = 0;
+    if constexpr (EPI == TC_QKV_ENC) region = qkv_apply(p, er, v, col0);
+    if constexpr (EPI == TC_QKV_DEC) region = dec_qkv_apply(p, er, v, col0);
+    if (p.vec && col0 + kEpiCols <= p.N) epi_vec<EPI>(p, er, v, col0, region);
+    else epi_scalar<EPI>(p, er, v, col0, region);
+}
+
+// One accumulator of a split-activation tile: warp quarter q, column half.
+// xch: the pair's exchange tile (the lo warp's staging area, 32 x 32 fp32,
+// column-major so both sides access it without bank conflicts); flg: the
+// pair's counters {staged, consumed}; seq: chunks exchanged so far by this
+// pair.  Returns false when a wait expired.
 template <int BN, int EPI>
+__device__ __forceinline__ bool epilogue_pair(const TcGemmParams &p, uint32_t tbase, int tm, int n0, int q, int half,
+                                              int lane, float *xch, volatile int *flg, int &seq, uint64_t deadline) {
+    const bool hi = q < 2;
+    const EpiRow er = epi_row<EPI>(p, tm * 64 + 32 * (q & 1) + lane);
+    const bool rv = er.row < p.M;
+#pragma unroll 1
+    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
+        float v[kEpiCols];
+        tmem_ld32(tbase + (uint32_t)c, v);   // warp-collective: before any branch
+        const int col0 = n0 + c;
+        if (col0 >= p.N) continue;           // the same for both warps of the pair
+        if (!hi) {
+            if (!flag_wait(&flg[1], seq, deadline, lane)) return false;   // previous chunk consumed
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j++) xch[j * 32 + lane] = v[j];
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();
+                flg[0] = seq + 1;
+            }
+            seq++;
+            continue;
+        }
+        if (!flag_wait(&flg[0], seq + 1, deadline, lane)) return false;   // this chunk staged
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j++) v[j] += xch[j * 32 + lane];
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            flg[1] = seq + 1;
+        }
+        seq++;
+        if (rv) epi_direct<EPI>(p, er, v, col0);
+    }
+    return true;
+}
+
+// Split-K finish of one pair's 32 output rows x BN/2 columns: the slices of
+// the hi and the lo accumulator rows summed in slice order.
+template <int BN, int EPI>
+__device__ __forceinline__ void split_finish_pair(const TcGemmParams &p, int tm, int qq, int n0, int half, int lane,
+                                                  int KS) {
+    const EpiRow er = epi_row<EPI>(p, tm * 64 + 32 * qq + lane);
+    if (er.row >= p.M) return;
+    const int rows = hilo_rows(p.M);
+    const size_t slice = (size_t)rows * p.N;
+    const float *src = p.ws + (size_t)(tm * kBM + 32 * qq + lane) * p.N;
+#pragma unroll 1
+    for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
+        const int col0 = n0 + c;
+        if (col0 >= p.N) continue;
+        float v[kEpiCols];
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j++) v[j] = 0.f;
+        for (int s = 0; s < KS; s++) {
+            const float *a = src + (size_t)s * slice + col0;
+            const float *b = a + (size_t)64 * p.N;
+            if (col0 + kEpiCols <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+                for (int j = 0; j < kEpiCols; j += 4) {
+                    const float4 x = __ldcg(reinterpret_cast<const float4 *>(a + j));
+                    const float4 y = __ldcg(reinterpret_cast<const float4 *>(b + j));
+                    v[j] += x.x + y.x, v[j + 1] += x.y + y.y, v[j + 2] += x.z + y.z, v[j + 3] += x.w + y.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kEpiCols; j++)
+                    if (col0 + j < p.N) v[j] += __ldcg(a + j) + __ldcg(b + j);
+            }
+        }
+        epi_direct<EPI>(p, er, v, col0);
+    }
+}
+
+template <int BN, int EPI, bool HILO = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmK,
@@ -456,9 +649,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t *tfull = empty + S;     // [2] accumulator b holds a finished tile
     uint64_t *tempty = tfull + 2;    // [2] accumulator b was drained by the epilogue
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    volatile int *pair_flags = reinterpret_cast<volatile int *>(tmem_slot + 1);   // HILO: [4 pairs][2]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int MT = (p.M + kBM - 1) / kBM;
+    // row tiles: 128 output rows, or (HILO) 64 output rows = 128 A rows [hi; lo]
+    const int MT = HILO ? (p.M + 63) / 64 : (p.M + kBM - 1) / kBM;
     const int tiles = MT * ((p.N + BN - 1) / BN);
     const int KB = (p.K + kBK - 1) / kBK;
     const int KS = p.ksplit > 1 ? p.ksplit : 1;   // K slices per tile (split-K)
@@ -475,6 +670,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], kEpiWarps);    // one arrival per epilogue warp
         }
+        for (int i = 0; i < 8; i++) pair_flags[i] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
@@ -553,6 +749,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int q = warp & 3, half = (warp - 2) >> 2;   // TMEM lane quarter, column half
         const EpiMaps mp = {&tmO, &tmK, &tmV};
         unsigned char *stg = sStage + (warp - 2) * kStageBytes;
+        int pair_seq = 0;   // HILO: chunks this warp's pair has exchanged
         uint32_t lt = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, lt++) {
             const int t = u / KS, ks = u % KS;
@@ -565,6 +762,38 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc_fence_after();
             const int m0 = (t % MT) * kBM, n0 = (t / MT) * BN;
             const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + b * BN;
+            if constexpr (HILO) {
+                if (KS == 1) {
+                    // the lo warp of the pair (warp - 2 for a hi warp) stages its chunks
+                    float *xch = reinterpret_cast<float *>(sStage + ((q < 2 ? warp - 2 : warp) - 2) * kStageBytes);
+                    if (!epilogue_pair<BN, EPI>(p, tb, t % MT, n0, q, half, lane, xch,
+                                                pair_flags + 2 * (half * 2 + (q & 1)), pair_seq, deadline)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[b]);
+                } else {
+                    split_partial<BN>(p, tb, m0 + 32 * q, n0, half, lane, ks, MT * kBM);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[b]);
+                    // the pair's 2 x KS partials: the last to arrive finishes the rows
+                    __threadfence();
+                    __syncwarp();
+                    const int pair = half * 2 + (q & 1);
+                    unsigned prev = 0;
+                    if (lane == 0) prev = atomicAdd(&p.ws_cnt[t * 4 + pair], 1u);
+                    prev = __shfl_sync(0xffffffffu, prev, 0);
+                    if (prev == (unsigned)(2 * KS - 1)) {
+                        __threadfence();
+                        split_finish_pair<BN, EPI>(p, t % MT, q & 1, n0, half, lane, KS);
+                        if (lane == 0) p.ws_cnt[t * 4 + pair] = 0u;
+                    }
+                }
+                continue;
+            }
             if (KS == 1) {
                 epilogue_tile<BN, EPI>(p, mp, tb, m0 + 32 * q, n0, half, lane, stg);
                 tc_fence_before();
@@ -572,7 +801,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if (lane == 0) mbar_arrive(&tempty[b]);
             } else {
                 // this split's partial of the warp's 32 x BN/2 sub-tile -> workspace
-                split_partial<BN>(p, tb, m0 + 32 * q, n0, half, lane, ks);
+                split_partial<BN>(p, tb, m0 + 32 * q, n0, half, lane, ks, p.M);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[b]);   // the accumulator is free already
@@ -864,11 +1093,13 @@ int device_sms(int dev) {
 
 bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool HILO = false>
 cudaError_t launch_bn(const TcGemmParams &p, const void *A, const void *W, cudaStream_t st, bool pdl,
                       const CUtensorMap &mo, const CUtensorMap &mk, const CUtensorMap &mv) {
     CUtensorMap ma, mb;
-    if (!make_map(&ma, A, p.M, p.K, kBM) || !make_map(&mb, W, p.N, p.K, BN)) return cudaErrorInvalidValue;
+    // HILO: A holds hilo_rows(M) rows (per 64 output rows, their hi then lo rows)
+    const int a_rows = HILO ? hilo_rows(p.M) : p.M;
+    if (!make_map(&ma, A, a_rows, p.K, kBM) || !make_map(&mb, W, p.N, p.K, BN)) return cudaErrorInvalidValue;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -876,13 +1107,14 @@ cudaError_t launch_bn(const TcGemmParams &p, const void *A, const void *W, cudaS
     static std::atomic<uint64_t> attr_set{0};
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_set.load() & bit)) {
-        e = cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(tc_gemm_kernel<BN, EPI, HILO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  TcCfg<BN>::kSmem);
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
     // work units: tiles x K slices (split-K)
-    const int units = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * (p.ksplit > 1 ? p.ksplit : 1);
+    const int mt = HILO ? (p.M + 63) / 64 : (p.M + kBM - 1) / kBM;
+    const int units = mt * ((p.N + BN - 1) / BN) * (p.ksplit > 1 ? p.ksplit : 1);
     const int sms = device_sms(dev);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(units < sms ? units : sms);
@@ -894,7 +1126,7 @@ cudaError_t launch_bn(const TcGemmParams &p, const void *A, const void *W, cudaS
     attr1[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr1;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, EPI>, ma, mb, mo, mk, mv, p);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, EPI, HILO>, ma, mb, mo, mk, mv, p);
 }
 
 int max_pair_clusters(const void *fn, int smem, int dev) {
@@ -1019,6 +1251,10 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
             break;
         }
         case TC_SWIGLU: p.vec = al16(p.out_bf16) && p.ldo_bf16 % 8 == 0; break;
+        case TC_QKV_DEC:
+            if (!p.hilo || p.N != kQkvRows || !p.q32 || !p.slots || !p.rope_rows) return cudaErrorInvalidValue;
+            p.vec = al16(p.q32) && al16(p.rope_rows);
+            break;
         case TC_QKV_ENC:
             p.vec = al16(p.q_out) && al16(p.k_ring) && al16(p.v_ring) && (!p.bias || al16(p.bias)) &&
                     (!p.bias2 || al16(p.bias2));
@@ -1032,10 +1268,14 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     memset(&mk, 0, sizeof(mk));
     memset(&mv, 0, sizeof(mv));
     const char *env_tma = getenv("VOX_CUDA_TC_TMA_OUT");
-    p.tma_out = (p.vec && !(env_tma && atoi(env_tma) == 0) && make_out_maps(epi, p, &mo, &mk, &mv)) ? 1 : 0;
+    // (the split-activation epilogue stores directly)
+    p.tma_out = (p.vec && !(env_tma && atoi(env_tma) == 0) && !p.hilo && make_out_maps(epi, p, &mo, &mk, &mv))
+                    ? 1
+                    : 0;
+    if (p.hilo && p.f16) return cudaErrorInvalidValue;   // the split is into bf16 halves
     // CTA pairs only on request: at the encoder shapes they measured no faster
     // than single-CTA tiles (the MMA pipe, not L2 -> SMEM traffic, is the limit)
-    const bool pair = env_tc_pair() == 1 && p.M > kBM;
+    const bool pair = env_tc_pair() == 1 && p.M > kBM && !p.hilo;
     if (pair) {
         const int pbn = tc_gemm2_bn(p.M, p.N);
 #define VC_TC2_CASE(BN)                                                            \
@@ -1061,7 +1301,8 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
         int dev = 0;
         cudaGetDevice(&dev);
         const int sms = device_sms(dev);
-        const int mt = (p.M + kBM - 1) / kBM, KB = (p.K + kBK - 1) / kBK;
+        const int mt = p.hilo ? (p.M + 63) / 64 : (p.M + kBM - 1) / kBM, KB = (p.K + kBK - 1) / kBK;
+        const size_t ws_rows = p.hilo ? (size_t)hilo_rows(p.M) : (size_t)p.M;
         // measured at M = 100: a win for K = 5120 (w2), a loss for K = 2048 (wo)
         if (2 * mt * ((p.N + bn - 1) / bn) < sms && KB >= kTcSplitMinKB) {
             // the last slice to finish sums the others: few slices and
@@ -1069,14 +1310,29 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
             const int bw = env_tc_bn() ? env_tc_bn() : (p.N >= 4096 ? 128 : 64);
             const int tiles = mt * ((p.N + bw - 1) / bw);
             int ks = std::min(kTcMaxSplit, std::min(sms / tiles, KB / 4));
-            ks = (int)std::min<size_t>((size_t)ks, p.ws_floats / ((size_t)p.M * p.N));
+            ks = (int)std::min<size_t>((size_t)ks, p.ws_floats / (ws_rows * p.N));
             const char *ev = getenv("VOX_CUDA_TC_KSPLIT");
             if (ev && atoi(ev) >= 1) ks = std::min(ks, atoi(ev));
-            if (ks >= 2 && tiles * kEpiWarps <= kTcSplitCounters) {
+            if (ks >= 2 && tiles * kEpiWarps <= kTcSplitCounters) {   // (HILO uses 4 per tile)
                 bn = bw;
                 p.ksplit = ks;
             }
         }
+    }
+    if (p.hilo) {   // split activations: [hi; lo] A tiles, paired epilogue
+        if (bn > 128) bn = 128;
+#define VC_TCH_CASE(BN)                                                                       \
+        if (bn == BN) {                                                                       \
+            switch (epi) {                                                                    \
+                case TC_RESID: return launch_bn<BN, TC_RESID, true>(p, A, W, st, pdl, mo, mk, mv);     \
+                case TC_SWIGLU: return launch_bn<BN, TC_SWIGLU, true>(p, A, W, st, pdl, mo, mk, mv);   \
+                case TC_QKV_DEC: return launch_bn<BN, TC_QKV_DEC, true>(p, A, W, st, pdl, mo, mk, mv); \
+            }                                                                                 \
+        }
+        VC_TCH_CASE(64)
+        VC_TCH_CASE(128)
+#undef VC_TCH_CASE
+        return cudaErrorInvalidValue;
     }
 #define VC_TC_CASE(BN)                                                             \
     if (bn == BN) {                                                                \
@@ -1191,6 +1447,78 @@ cudaError_t launch_bf16_to_f16(uint16_t *p, size_t n, cudaStream_t st) {
     const size_t blocks = (n + 255) / 256;
     bf16_to_f16_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(p, n);
     return cudaGetLastError();
+}
+
+// fp32 rows -> bf16 hi / lo rows (the HILO GEMM's A), optionally
+// RMS-normalised (vox_rms_norm, voxtral_kernels.c:346-363): v = x * inv * w,
+// hi = bf16(v) at row hilo_row(r), lo = bf16(v - hi) 64 rows below.  One CTA of 256
+// threads per row (the rows are few: a warp per row left the prefill's
+// three norms per layer latency-bound); the row stays in registers between
+// the sum of squares and the scaling.  K % 4 == 0, K <= 8192, 16-byte rows.
+constexpr int kHiloRegs = 8;   // float4 per thread: rows up to 8192 floats
+
+__global__ void __launch_bounds__(256)
+rows_hilo_kernel(const float *x, int M, int K, int ld, const float *w, uint16_t *out) {
+    __shared__ float red[8];
+    grid_dep_wait();
+    grid_dep_launch();
+    const int row = blockIdx.x, tid = threadIdx.x;
+    if (row >= M) return;   // CTA-uniform
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)row * ld);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    uint2 *oh = reinterpret_cast<uint2 *>(out + (size_t)hilo_row(row) * K);
+    uint2 *ol = reinterpret_cast<uint2 *>(out + (size_t)(hilo_row(row) + 64) * K);
+    const int K4 = K >> 2;
+    float4 a[kHiloRegs];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kHiloRegs; j++) {
+        const int i = tid + 256 * j;
+        a[j] = i < K4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ss = fmaf(a[j].x, a[j].x, ss);
+        ss = fmaf(a[j].y, a[j].y, ss);
+        ss = fmaf(a[j].z, a[j].z, ss);
+        ss = fmaf(a[j].w, a[j].w, ss);
+    }
+    float inv = 1.0f;
+    if (w) {
+        ss = warp_sum(ss);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) t += red[i];
+        inv = 1.0f / sqrtf(t / (float)K + kNormEps);
+    }
+#pragma unroll
+    for (int j = 0; j < kHiloRegs; j++) {
+        const int i = tid + 256 * j;
+        if (i >= K4) break;
+        float4 v = a[j];
+        if (w) {
+            const float4 g = __ldg(w4 + i);
+            v.x = v.x * inv * g.x, v.y = v.y * inv * g.y, v.z = v.z * inv * g.z, v.w = v.w * inv * g.w;
+        }
+        oh[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+        ol[i] = make_uint2(pack_bf16_lo2(v.x, v.y), pack_bf16_lo2(v.z, v.w));
+    }
+}
+
+cudaError_t launch_rows_hilo(const float *x, int M, int K, int ld, const float *w, uint16_t *out,
+                             cudaStream_t st, bool pdl) {
+    if (M <= 0 || K % 4 != 0 || K > 4 * 256 * kHiloRegs || ld % 4 != 0 || ((uintptr_t)x & 15) ||
+        ((uintptr_t)w & 15) || ((uintptr_t)out & 7))
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, rows_hilo_kernel, x, M, K, ld, w, out);
 }
 
 cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const float *w, uint16_t *out,

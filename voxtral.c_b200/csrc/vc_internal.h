@@ -76,6 +76,7 @@ struct AttnParams {
     int layer;
     float *out;               // [M][4096] or NULL
     uint32_t *xfrag_out;      // the output as the wo GEMV's B fragments, or NULL
+    uint16_t *out_hilo;       // the output as bf16 hi / lo rows (hilo_row layout), or NULL
     float *part_o;            // [M][32][S][128]
     float *part_ml;           // [M][32][S][2]
     unsigned *counters;       // [M][8], zero between launches
@@ -95,6 +96,7 @@ enum TcEpi : int {
     TC_RESID = 1,     // out += acc (+ bias)   (fp32 residual stream)
     TC_SWIGLU = 2,    // cols (2i, 2i+1) = (gate_i, up_i) -> out_bf16[i] = silu(g) * u
     TC_QKV_ENC = 3,   // encoder q|k|v: bias, RoPE, q (fp16) out, k / v (fp16) to the ring
+    TC_QKV_DEC = 4,   // decoder q|k|v: RoPE, q (fp32) out, k / v (fp32) to each row's ring slot
 };
 
 struct TcGemmParams {
@@ -124,6 +126,17 @@ struct TcGemmParams {
     int ksplit;
     int f16;                 // A and W are fp16 (kind::f16 with fp16 operands) and so are the
                              //   16-bit outputs (out_bf16, SwiGLU h); else bf16
+    // split activations (decoder prefill): A is in the hi / lo layout of
+    // hilo_row() (per 64 output rows, their bf16 hi rows then their bf16
+    // lo = x - hi rows); one 128-row MMA tile covers both and the epilogue
+    // adds accumulator rows r and r + 64: fp32-level products from bf16 MMAs
+    int hilo;
+    int out_hilo;            // TC_SWIGLU: h written as bf16 hi / lo rows in that layout
+    // TC_QKV_DEC
+    float *q32;              // fp32 [M][4096]
+    const StreamSlot *slots; // [M]: each row's ring and slot
+    int layer;
+    const float *rope_rows;  // [M][128]: (cos, sin) of pair d at [2d], [2d + 1]
     int vec;                 // set by launch_tc_gemm: all destinations allow 16-byte stores
     int tma_out;             // set by launch_tc_gemm: the epilogue stores through TMA
 };
@@ -141,6 +154,10 @@ cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const floa
                                 cudaStream_t st, bool pdl, bool f16 = false);
 // In place: bf16 -> fp16 (round to nearest even; the values of bf16 weights
 // are inside fp16's range).
+// fp32 rows -> bf16 hi / lo rows in the hilo_row layout, v = x
+// (RMS-normalised with weights w when w).
+cudaError_t launch_rows_hilo(const float *x, int M, int K, int ld, const float *w, uint16_t *out,
+                             cudaStream_t st, bool pdl);
 cudaError_t launch_bf16_to_f16(uint16_t *p, size_t n, cudaStream_t st);
 
 // ---- encoder (vc_encoder.cu) ----

@@ -657,6 +657,9 @@ struct DecLayer {
     // fused, fragment-tiled device copies: wq|wk|wv [6144, 3072],
     // wo [3072, 4096], w1/w3 row-interleaved [18432, 3072], w2 [3072, 9216]
     const uint16_t *qkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr;
+    // the same fused matrices row-major (bf16, as stored), the tcgen05
+    // prefill's TMA-fed W operands; NULL when the tensor-core prefill is off
+    const uint16_t *qkv_rm = nullptr, *wo_rm = nullptr, *w13_rm = nullptr, *w2_rm = nullptr;
     // RMSNorm weights as folded into the activation fragments:
     // g_attn = attention_norm, g_ffn = ffn_norm * (1 + ada_scale)
     const float *g_attn = nullptr, *g_ffn = nullptr;
@@ -702,6 +705,35 @@ struct StepWork {
     cudaGraphExec_t graph[2] = {nullptr, nullptr};
 };
 
+// Device workspace of the tensor-core prefill (shared by the decoder's
+// states, serialised by the decoder's mutex): up to `cap` rows per launch
+// sequence.  Split activations (xn, att16, h16) are in the hilo_row layout:
+// per 64 rows their bf16 hi rows, then their bf16 lo rows (2 x cap rows).
+struct PrefillTc {
+    int cap = 0;                 // rows
+    int splits = 0;              // attention key splits the partial buffers hold
+    char *block = nullptr;
+    size_t bytes = 0;
+    float *part = nullptr;       // attention partials (grown with `splits`)
+    size_t part_bytes = 0;
+    // the head, uploaded per call: slots, RoPE tables, input rows
+    StreamSlot *slots = nullptr; // [cap]
+    float *rope = nullptr;       // [cap][128]
+    float *x = nullptr;          // [cap][3072] fp32 residual stream
+    size_t head_bytes = 0;       // bytes before x
+    float *q = nullptr;          // [cap][4096] fp32 (RoPE applied)
+    uint16_t *xn = nullptr;      // [2 cap][3072] bf16 hi / lo
+    uint16_t *att16 = nullptr;   // [2 cap][4096]
+    uint16_t *h16 = nullptr;     // [2 cap][9216]
+    unsigned *counters = nullptr;  // [cap][8]
+    float *split = nullptr;      // split-K partials [kEncSplitFloats]
+    unsigned *split_cnt = nullptr;
+    unsigned *err = nullptr;
+    char *hblock = nullptr;      // pinned mirror of the head
+    unsigned *h_err = nullptr;   // pinned
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;   // (rows, splits) -> layers
+};
+
 }  // namespace
 
 struct vox_cuda_decoder {
@@ -717,6 +749,8 @@ struct vox_cuda_decoder {
     bool pdl = true;
     cudaEvent_t tail = nullptr;   // the end of the last asynchronous step
     bool tail_set = false;
+    bool tc_prefill = false;      // row-major weights kept: prefill on the tensor cores
+    PrefillTc *pf = nullptr;
 };
 
 struct vox_cuda_dec_state {
@@ -1028,6 +1062,212 @@ int check_capacity(const vox_cuda_dec_state *s, int first, int last) {
     return VOX_CUDA_OK;
 }
 
+// ---- tensor-core prefill -------------------------------------------------
+
+constexpr int kPrefillRows = 128;   // rows per launch sequence (one M tile)
+
+void free_prefill(DevCtx *c, PrefillTc *f) {
+    if (!f) return;
+    for (auto &kv : f->graphs) cudaGraphExecDestroy(kv.second);
+    if (c) {
+        dev_free(c, f->block, f->block ? f->bytes : 0);
+        dev_free(c, f->part, f->part ? f->part_bytes : 0);
+    }
+    if (f->hblock) cudaFreeHost(f->hblock);
+    if (f->h_err) cudaFreeHost(f->h_err);
+    delete f;
+}
+
+PrefillTc *make_prefill(DevCtx *c, int cap) {
+    PrefillTc *f = new PrefillTc();
+    f->cap = cap;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const size_t C = (size_t)cap;
+    const size_t o_slots = take(sizeof(StreamSlot) * C), o_rope = take(4 * C * kHeadDim);
+    const size_t o_x = take(4 * C * kDecDim);
+    f->head_bytes = o_x;   // + the rows of x actually used
+    const size_t o_q = take(4 * C * kQDim);
+    const size_t o_xn = take(2 * 2 * C * kDecDim), o_att16 = take(2 * 2 * C * kQDim);
+    const size_t o_h16 = take(2 * 2 * C * kDecHidden), o_cnt = take(4 * C * kDecKvHeads);
+    const size_t o_split = take(4 * kEncSplitFloats), o_scnt = take(4 * kTcSplitCounters), o_err = take(4);
+    f->bytes = off;
+    if (dev_alloc(c, (void **)&f->block, f->bytes) != cudaSuccess ||
+        cudaMemset(f->block, 0, f->bytes) != cudaSuccess ||
+        cudaHostAlloc((void **)&f->hblock, o_x + 4 * C * kDecDim, cudaHostAllocDefault) != cudaSuccess ||
+        cudaHostAlloc((void **)&f->h_err, sizeof(unsigned), cudaHostAllocDefault) != cudaSuccess) {
+        set_error("prefill workspace: allocation of %zu bytes failed", f->bytes);
+        free_prefill(c, f);
+        return nullptr;
+    }
+    char *b = f->block;
+    f->slots = (StreamSlot *)(b + o_slots);
+    f->rope = (float *)(b + o_rope);
+    f->x = (float *)(b + o_x);
+    f->q = (float *)(b + o_q);
+    f->xn = (uint16_t *)(b + o_xn);
+    f->att16 = (uint16_t *)(b + o_att16);
+    f->h16 = (uint16_t *)(b + o_h16);
+    f->counters = (unsigned *)(b + o_cnt);
+    f->split = (float *)(b + o_split);
+    f->split_cnt = (unsigned *)(b + o_scnt);
+    f->err = (unsigned *)(b + o_err);
+    *f->h_err = 0;
+    return f;
+}
+
+// Grow the attention partials to `splits` key splits per (row, head).
+int prefill_reserve_splits(DevCtx *c, PrefillTc *f, int splits) {
+    if (splits <= f->splits) return VOX_CUDA_OK;
+    const size_t bytes = (size_t)f->cap * kDecHeads * splits * (kHeadDim + 2) * 4;
+    float *np = nullptr;
+    if (dev_alloc(c, (void **)&np, bytes) != cudaSuccess) {
+        set_error("prefill workspace: attention partials (%zu bytes) failed", bytes);
+        return VOX_CUDA_ERR_OOM;
+    }
+    VC_TRY(cudaStreamSynchronize(c->stream));
+    dev_free(c, f->part, f->part ? f->part_bytes : 0);
+    for (auto &kv : f->graphs) cudaGraphExecDestroy(kv.second);   // they hold the old pointers
+    f->graphs.clear();
+    f->part = np;
+    f->part_bytes = bytes;
+    f->splits = splits;
+    return VOX_CUDA_OK;
+}
+
+// The layers of one prefill launch sequence over M rows (their slots, RoPE
+// tables and inputs already in f): per layer RMSNorm -> hi / lo rows,
+// q|k|v GEMM (RoPE, ring writes), attention over each row's ring, wo GEMM +
+// residual, FFN RMSNorm * (1 + ada), w1|w3 GEMM + SwiGLU, w2 GEMM + residual
+// (vox_decoder_prefill, voxtral_decoder.c:233-373).  bf16 tensor-core
+// operands: the weights as stored, the activations as hi + lo pairs.
+int enqueue_prefill(vox_cuda_decoder *d, PrefillTc *f, int M, int S, cudaStream_t st) {
+    const bool pdl = d->pdl;
+    float *part_o = f->part;
+    float *part_ml = f->part + (size_t)f->cap * kDecHeads * S * kHeadDim;
+    auto gemm = [&](int M_, int N, int K) {
+        TcGemmParams p = {};
+        p.M = M_;
+        p.N = N;
+        p.K = K;
+        p.hilo = 1;
+        p.err = f->err;
+        p.ws = f->split;
+        p.ws_floats = kEncSplitFloats;
+        p.ws_cnt = f->split_cnt;
+        return p;
+    };
+    for (int l = 0; l < d->n_layers; l++) {
+        const DecLayer &L = d->L[l];
+        VC_TRY(launch_rows_hilo(f->x, M, kDecDim, kDecDim, L.g_attn, f->xn, st, pdl));
+        TcGemmParams p = gemm(M, kQkvRows, kDecDim);
+        p.q32 = f->q;
+        p.slots = f->slots;
+        p.layer = l;
+        p.rope_rows = f->rope;
+        VC_TRY(launch_tc_gemm(TC_QKV_DEC, p, f->xn, L.qkv_rm, st, pdl));
+        AttnParams a = {};
+        a.q = f->q;
+        a.slots = f->slots;
+        a.layer = l;
+        a.out_hilo = f->att16;   // straight into the wo GEMM's split operand
+        a.part_o = part_o;
+        a.part_ml = part_ml;
+        a.counters = f->counters;
+        a.S = S;
+        VC_TRY(launch_attn_decode(M, a, st, pdl));
+        p = gemm(M, kDecDim, kQDim);
+        p.out = f->x;
+        p.ldo = kDecDim;
+        VC_TRY(launch_tc_gemm(TC_RESID, p, f->att16, L.wo_rm, st, pdl));
+        VC_TRY(launch_rows_hilo(f->x, M, kDecDim, kDecDim, L.g_ffn, f->xn, st, pdl));
+        p = gemm(M, 2 * kDecHidden, kDecDim);
+        p.out_bf16 = f->h16;
+        p.ldo_bf16 = kDecHidden;
+        p.out_hilo = 1;
+        VC_TRY(launch_tc_gemm(TC_SWIGLU, p, f->xn, L.w13_rm, st, pdl));
+        p = gemm(M, kDecDim, kDecHidden);
+        p.out = f->x;
+        p.ldo = kDecDim;
+        VC_TRY(launch_tc_gemm(TC_RESID, p, f->h16, L.w2_rm, st, pdl));
+    }
+    return VOX_CUDA_OK;
+}
+
+// Rows of one or more states (state i contributes n_rows[i] consecutive
+// rows from its current position), in launch sequences of <= kPrefillRows
+// rows; x: host [sum n_rows][3072]; rope: host [sum n_rows][64][2] or NULL.
+// Caller holds d->mu.
+int prefill_tc_rows(vox_cuda_decoder *d, DevCtx *c, vox_cuda_dec_state *const *states, const int *n_rows,
+                    int n_states, const float *x, const float *rope) {
+    if (!d->pf && !(d->pf = make_prefill(c, kPrefillRows))) return VOX_CUDA_ERR_OOM;
+    PrefillTc *f = d->pf;
+    cudaStream_t st = c->stream;
+    StreamSlot *h_slots = (StreamSlot *)f->hblock;
+    float *h_rope = (float *)(f->hblock + ((char *)f->rope - f->block));
+    float *h_x = (float *)(f->hblock + ((char *)f->x - f->block));
+    int si = 0, done_in_state = 0;   // next row: state si, its row done_in_state
+    size_t row_in = 0;               // next row of x / rope
+    while (si < n_states) {
+        // gather up to kPrefillRows rows
+        int M = 0, max_keys = 1;
+        while (si < n_states && M < f->cap) {
+            const int take = std::min(n_rows[si] - done_in_state, f->cap - M);
+            vox_cuda_dec_state *s = states[si];
+            for (int r = 0; r < take; r++) {
+                const int pos = s->pos + done_in_state + r;
+                fill_slot(s, pos, h_slots + M + r);
+                max_keys = std::max(max_keys, h_slots[M + r].n_keys);
+                if (rope) memcpy(h_rope + (size_t)(M + r) * kHeadDim, rope + (row_in + r) * kHeadDim, kHeadDim * 4);
+                else host_rope_table(pos, kHeadDim, h_rope + (size_t)(M + r) * kHeadDim);
+            }
+            memcpy(h_x + (size_t)M * kDecDim, x + row_in * kDecDim, (size_t)take * kDecDim * 4);
+            M += take;
+            row_in += take;
+            done_in_state += take;
+            if (done_in_state == n_rows[si]) {
+                si++;
+                done_in_state = 0;
+            }
+        }
+        const int S = (max_keys + 63) / 64;
+        int rc = prefill_reserve_splits(c, f, S);
+        if (rc) return rc;
+        VC_TRY(cudaMemcpyAsync(f->block, f->hblock, f->head_bytes + (size_t)M * kDecDim * 4, cudaMemcpyHostToDevice,
+                               st));
+        cudaGraphExec_t &g = f->graphs[std::make_pair(M, S)];
+        if (!g) {
+            cudaGraph_t graph = nullptr;
+            VC_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            rc = enqueue_prefill(d, f, M, S, st);
+            cudaError_t e = cudaStreamEndCapture(st, &graph);
+            if (rc) {
+                if (graph) cudaGraphDestroy(graph);
+                f->graphs.erase(std::make_pair(M, S));
+                return rc;
+            }
+            VC_TRY(e);
+            e = cudaGraphInstantiate(&g, graph, 0);
+            cudaGraphDestroy(graph);
+            VC_TRY(e);
+        }
+        VC_TRY(cudaGraphLaunch(g, st));
+        VC_TRY(cudaMemcpyAsync(f->h_err, f->err, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+        VC_TRY(cudaStreamSynchronize(st));   // the host block is reused by the next sequence
+        if (*f->h_err) {
+            *f->h_err = 0;
+            cudaMemset(f->err, 0, sizeof(unsigned));
+            set_error("decoder prefill: a device-side wait timed out (results discarded)");
+            return VOX_CUDA_ERR_CUDA;
+        }
+    }
+    return VOX_CUDA_OK;
+}
+
 }  // namespace
 
 extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights *w) {
@@ -1072,8 +1312,12 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
     bool ok = true;
     // Fused matrix from row-major pieces: [rows_i x K] blocks stacked (or
     // row-interleaved when interleave), then tiled for the GEMV.
-    auto fuse = [&](const uint16_t *const *parts, const int *rows, int n_parts, int K,
-                    bool interleave) -> uint16_t * {
+    // VOX_CUDA_DEC_TC_PREFILL = 0 drops the row-major copies (6 GB at 4B):
+    // the prefill then runs through the decode-step kernels
+    const char *tcp_env = getenv("VOX_CUDA_DEC_TC_PREFILL");
+    d->tc_prefill = !(tcp_env && tcp_env[0] == '0');
+    auto fuse = [&](const uint16_t *const *parts, const int *rows, int n_parts, int K, bool interleave,
+                    const uint16_t **rm = nullptr) -> uint16_t * {
         int N = 0;
         for (int i = 0; i < n_parts; i++) N += rows[i];
         uint16_t *dst = (uint16_t *)alloc((size_t)round_up(N, kGemvRowAlign) * round_up(K, 16) * 2);
@@ -1092,6 +1336,11 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
         }
         ok &= launch_tile_weights(dst, stage, N, K, round_up(N, kGemvRowAlign), round_up(K, 16), st) ==
               cudaSuccess;
+        if (rm && ok) {   // the row-major fused matrix as staged
+            uint16_t *r = (uint16_t *)alloc((size_t)N * K * 2);
+            ok &= r && cudaMemcpyAsync(r, stage, (size_t)N * K * 2, cudaMemcpyDeviceToDevice, st) == cudaSuccess;
+            *rm = r;
+        }
         ok &= cudaStreamSynchronize(st) == cudaSuccess;   // the stage is reused next
         return ok ? dst : nullptr;
     };
@@ -1107,6 +1356,10 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
                 o.wo = d->L[j].wo;
                 o.w13 = d->L[j].w13;
                 o.w2 = d->L[j].w2;
+                o.qkv_rm = d->L[j].qkv_rm;
+                o.wo_rm = d->L[j].wo_rm;
+                o.w13_rm = d->L[j].w13_rm;
+                o.w2_rm = d->L[j].w2_rm;
                 break;
             }
         }
@@ -1119,10 +1372,11 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
             const int w13_rows[2] = {kDecHidden, kDecHidden};
             const uint16_t *w2_parts[1] = {L.w2};
             const int w2_rows[1] = {kDecDim};
-            o.qkv = fuse(qkv_parts, qkv_rows, 3, kDecDim, false);
-            o.wo = ok ? fuse(wo_parts, wo_rows, 1, kQDim, false) : nullptr;
-            o.w13 = ok ? fuse(w13_parts, w13_rows, 2, kDecDim, true) : nullptr;
-            o.w2 = ok ? fuse(w2_parts, w2_rows, 1, kDecHidden, false) : nullptr;
+            const bool rm = d->tc_prefill;
+            o.qkv = fuse(qkv_parts, qkv_rows, 3, kDecDim, false, rm ? &o.qkv_rm : nullptr);
+            o.wo = ok ? fuse(wo_parts, wo_rows, 1, kQDim, false, rm ? &o.wo_rm : nullptr) : nullptr;
+            o.w13 = ok ? fuse(w13_parts, w13_rows, 2, kDecDim, true, rm ? &o.w13_rm : nullptr) : nullptr;
+            o.w2 = ok ? fuse(w2_parts, w2_rows, 1, kDecHidden, false, rm ? &o.w2_rm : nullptr) : nullptr;
             ok &= o.qkv && o.wo && o.w13 && o.w2;
             if (!ok) break;
         }
@@ -1171,6 +1425,7 @@ extern "C" void vox_cuda_decoder_free(vox_cuda_decoder *d) {
     cudaSetDevice(d->device);
     if (c) cudaStreamSynchronize(c->stream);   // also waits for asynchronous steps (see step_batch_dev)
     for (int i = 0; i <= kMaxBatch; i++) free_work(c, d->batch_work[i]);
+    free_prefill(c, d->pf);
     if (d->tail) cudaEventDestroy(d->tail);
     for (auto &pr : d->owned)
         if (c) dev_free(c, pr.first, pr.second);
@@ -1361,9 +1616,22 @@ extern "C" int vox_cuda_decoder_prefill_step(vox_cuda_dec_state *s, const float 
     DevCtx *c = ctx_for(d->device);
     if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
     cudaSetDevice(d->device);
+    int rc = VOX_CUDA_OK;
+    if (d->tc_prefill) {
+        // rows in launch sequences of kPrefillRows on the tensor cores
+        for (int r0 = 0; r0 < seq_len; r0 += kPrefillRows) {
+            const int last = s->pos + std::min(seq_len, r0 + kPrefillRows) - 1;
+            if ((rc = check_capacity(s, s->pos + r0, last))) return rc;
+        }
+        std::lock_guard<std::mutex> lk(d->mu);
+        rc = prefill_tc_rows(d, c, &s, &seq_len, 1, x, rope_freqs);
+        if (rc) return rc;
+        s->pos += seq_len;
+        s->have_logits = false;
+        return VOX_CUDA_OK;
+    }
     // a row must not overwrite a ring slot still inside the window of an
     // earlier row of the same chunk: positions pos..pos+seq_len-1 all fit
-    int rc = VOX_CUDA_OK;
     for (int r0 = 0; r0 < seq_len; r0 += kMaxBatch) {
         const int last = s->pos + ((seq_len - r0 < kMaxBatch) ? seq_len : r0 + kMaxBatch) - 1;
         if ((rc = check_capacity(s, s->pos + r0, last))) return rc;
@@ -1378,6 +1646,10 @@ extern "C" int vox_cuda_decoder_prefill_step(vox_cuda_dec_state *s, const float 
         if (n != kMaxBatch) lk.lock();
         if (!w) w = make_work(c, n, d->vocab);
         if (!w) return VOX_CUDA_ERR_OOM;
+        if (w->staged_pending) {   // an asynchronous step's upload of the host block
+            VC_TRY(cudaEventSynchronize(w->staged));
+            w->staged_pending = false;
+        }
         for (int i = 0; i < n; i++) {
             const int pos = s->pos + r0 + i;
             fill_slot(s, pos, h_slots(w) + i);
@@ -1390,6 +1662,56 @@ extern "C" int vox_cuda_decoder_prefill_step(vox_cuda_dec_state *s, const float 
     }
     s->pos += seq_len;
     s->have_logits = false;
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_decoder_prefill_batch(vox_cuda_dec_state *const *states, int n, const float *x,
+                                              const int *seq_lens, const float *rope_freqs) {
+    if (!states || n <= 0 || !x || !seq_lens || !states[0]) {
+        set_error("decoder_prefill_batch: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    vox_cuda_decoder *d = states[0]->dec;
+    for (int i = 0; i < n; i++) {
+        if (!states[i] || states[i]->dec != d || seq_lens[i] < 0) {
+            set_error("decoder_prefill_batch: states must share one decoder, lengths >= 0");
+            return VOX_CUDA_ERR_ARG;
+        }
+        for (int j = 0; j < i; j++)
+            if (states[j] == states[i]) {
+                set_error("decoder_prefill_batch: a state appears twice");
+                return VOX_CUDA_ERR_ARG;
+            }
+    }
+    if (!d->tc_prefill) {   // one state after the other through the decode-step kernels
+        size_t off = 0;
+        for (int i = 0; i < n; i++) {
+            if (seq_lens[i] == 0) continue;
+            int rc = vox_cuda_decoder_prefill_step(states[i], x + off * kDecDim,
+                                                   seq_lens[i], rope_freqs ? rope_freqs + off * kHeadDim : nullptr);
+            if (rc) return rc;
+            off += seq_lens[i];
+        }
+        return VOX_CUDA_OK;
+    }
+    // a launch sequence holds at most kPrefillRows rows: each state's rows in
+    // any one of them fit its ring together with the window before them
+    for (int i = 0; i < n; i++)
+        for (int r0 = 0; r0 < seq_lens[i]; r0 += kPrefillRows) {
+            const int last = states[i]->pos + std::min(seq_lens[i], r0 + kPrefillRows) - 1;
+            int rc = check_capacity(states[i], states[i]->pos + r0, last);
+            if (rc) return rc;
+        }
+    DevCtx *c = ctx_for(d->device);
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(d->device);
+    std::lock_guard<std::mutex> lk(d->mu);
+    int rc = prefill_tc_rows(d, c, states, seq_lens, n, x, rope_freqs);
+    if (rc) return rc;
+    for (int i = 0; i < n; i++) {
+        states[i]->pos += seq_lens[i];
+        if (seq_lens[i]) states[i]->have_logits = false;
+    }
     return VOX_CUDA_OK;
 }
 

@@ -99,6 +99,7 @@ def lib():
         "vox_cuda_decoder_full_step": ([C.c_void_p, _fp, _fp, _fp], C.c_int),
         "vox_cuda_decoder_fill_alts": ([C.c_void_p, C.c_int, C.c_float, _ip], C.c_int),
         "vox_cuda_decoder_prefill_step": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
+        "vox_cuda_decoder_prefill_batch": ([C.c_void_p, C.c_int, _fp, _ip, _fp], C.c_int),
         "vox_cuda_decoder_step_batch": ([C.c_void_p, C.c_int, _fp, _ip], C.c_int),
         "vox_cuda_decoder_step_batch_dev": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                              C.c_void_p], C.c_int),
@@ -293,6 +294,16 @@ def step_batch(states, embeds):
 
 def states_array(states):
     return (C.c_void_p * len(states))(*[s.h for s in states])
+
+
+def prefill_batch(states, rows, rope=None):
+    """Prefill several states in shared launches: rows[i] is state i's
+    [n_i, 3072] block (n_i may be 0)."""
+    lens = np.array([np.asarray(r).shape[0] for r in rows], np.int32)
+    x = np.ascontiguousarray(np.concatenate([np.asarray(r, np.float32).reshape(-1, 3072) for r in rows], axis=0))
+    rp = None if rope is None else np.ascontiguousarray(rope, np.float32)
+    check(lib().vox_cuda_decoder_prefill_batch(states_array(states), len(states), _f(x), lens.ctypes.data_as(_ip),
+                                               _f(rp) if rp is not None else None), "prefill_batch")
 
 
 def step_batch_dev(states, embeds_dev, tokens_dev, stream=None):
