@@ -396,6 +396,42 @@ def multi_stream_encoder(enc, torch, x0, steps, streams=8, rows=100):
     return res
 
 
+def upload_bench(V, torch, layers=4, vocab=VOCAB):
+    """Decoder creation from host bf16 weights (the reference hands over its
+    mmap'd safetensors, voxtral.c:161-242): `layers` layers plus the full
+    805 MB embedding / LM head.  Wall clock around vox_cuda_decoder_create
+    (the library's pinned, pipelined upload; best of 3, the first also pins
+    the upload ring), beside a plain pageable host -> device copy of the same
+    bytes through torch for scale."""
+    rng = np.random.default_rng(11)
+    base = ((rng.standard_normal(1 << 24).astype(np.float32) * 0.02).view(np.uint32) >> 16).astype(np.uint16)
+
+    def mat(n, k):
+        return np.resize(base, (n, k))
+
+    tok = mat(vocab, D)
+    norm = np.ones(D, np.float32)
+    lw = [(mat(QD, D), mat(KVD, D), mat(KVD, D), mat(D, QD), mat(HID, D), mat(D, HID), mat(HID, D),
+           norm, norm) for _ in range(layers)]
+    host_bytes = tok.nbytes + sum(a.nbytes for t in lw for a in t[:7])
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        d = V.Decoder(tok, norm, lw, vocab=vocab)
+        times.append(time.perf_counter() - t0)
+        d.free()
+    flat = torch.from_numpy(tok.reshape(-1).view(np.int16))
+    dev = torch.empty_like(flat, device="cuda")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    dev.copy_(flat)
+    torch.cuda.synchronize()
+    pageable = flat.numel() * 2 / (time.perf_counter() - t0) / 1e9
+    del dev
+    return {"host_bytes": host_bytes, "layers": layers, "create_s": min(times), "create_s_first": times[0],
+            "host_gbs": host_bytes / min(times) / 1e9, "pageable_copy_gbs": pageable}
+
+
 def prefill_bench(V, dec, layers, prompt=38, reps=5):
     """Stream start: the 38-row prompt prefill (voxtral.c:843-891) of one
     stream, and of three streams in shared launches (vox_cuda_decoder_
@@ -590,6 +626,7 @@ def our_arm(args):
     for st in states:
         st.free()
     dec.free()
+    up_res = upload_bench(V, torch) if not args.no_encoder else None
     enc_res = None if args.no_encoder else encoder_bench(V, torch, args.steps, args.enc_rows)
 
     line = None
@@ -625,6 +662,7 @@ def our_arm(args):
                               "achieved_gbs": step_bytes / (ms_step / 1000.0) / 1e9,
                               "frac": step_bytes / (ms_step / 1000.0) / 1e9 / hbm},
             "prefill": pf_res,
+            "weight_upload": up_res,
             "phase_ms": prof,
             "launch_ms_in_sequence": seq_ms,
             "clocks": clk.summary(),
