@@ -541,6 +541,16 @@ def our_arm(args):
                                 device_id=torch.device("cuda", local))
     import voxcuda as V
     V.init(local)
+    if args.prefill_only:   # the prompt prefill alone (profiling captures)
+        dec = build_device_decoder(V, torch, layers=args.layers, vocab=args.vocab)
+        res = prefill_bench(V, dec, args.layers)
+        dec.free()
+        if rank == 0:
+            print(json.dumps({"prefill": res}), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.no_decode:   # encoder only (profiling captures)
         res = encoder_bench(V, torch, args.steps, args.enc_rows)
         if rank == 0:
@@ -686,6 +696,7 @@ def main():
     ap.add_argument("--no-encoder", action="store_true")
     # encoder-only / single chunk size, for small ncu captures
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--prefill-only", action="store_true")
     ap.add_argument("--enc-rows", type=int, default=0)
     # reduced model, for small ncu captures only (the headline uses the full model)
     ap.add_argument("--layers", type=int, default=LAYERS)

@@ -29,8 +29,8 @@ __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
 // slot), so their copies are issued before griddepcontrol.wait and overlap
 // that kernel's tail; the newest key and q are read after it.
 // (Within one launch, streams that share a ring are consecutive rows of one
-// sequence, the decoder prefill: keys from the lowest such position on are
-// all fresh.)
+// sequence, the decoder prefill: keys from the lowest such position on,
+// which the host passes as the slot's `fresh`, are all fresh.)
 // Instead of the reference's per-key online softmax (a serial chain), each
 // split runs three parallel passes: scores (warp = query head, lane = key,
 // rotated float4 reads), the softmax of the split (per warp), then P.V
@@ -93,10 +93,7 @@ attn_decode_kernel(const AttnParams p) {
     const float *vbase = slt.v_ring + layer_off;
 
     // keys [0, n_old) predate this launch
-    int fresh_first = slt.pos;
-    for (int i = 0; i < (int)gridDim.z; i++)
-        if (p.slots[i].k_ring == slt.k_ring) fresh_first = min(fresh_first, p.slots[i].pos);
-    const int n_old = max(0, fresh_first - first);
+    const int n_old = max(0, min(slt.fresh, slt.pos) - first);
     {   // the first split's old keys, before the wait
         const int kb = blockIdx.x * chunk;
         const int nk = max(0, min(kb + chunk, n_keys) - kb);

@@ -16,6 +16,8 @@ struct StreamSlot {
     int pos;          // logical position of this step's row
     int slot;         // pos % cap
     int n_keys;       // keys attended: min(pos + 1, window)
+    int fresh;        // the lowest position this launch writes into this ring (the
+                      //   launch's first row of this sequence): older keys predate it
 };
 
 enum GemvEpi : int {

@@ -22,15 +22,16 @@ using namespace vc;
 namespace {
 
 // Layout of the static scratch, in floats:
-//   [0, 8)                   ring descriptor (StreamSlot, 32 bytes)
-//   [8, 16)                  split tickets (8 KV heads)
-//   [16, 16 + kPartML)       per-split (max, sum) of the 32 query heads
+//   [0, 16)                  ring descriptor (StreamSlot, <= 64 bytes)
+//   [16, 24)                 split tickets (8 KV heads)
+//   [32, 32 + kPartML)       per-split (max, sum) of the 32 query heads
 //   [.., .. + kPartO)        per-split weighted V sums of the 32 query heads
+constexpr size_t kSlotFloats = 16, kTicketOff = 16, kPartOff = 32;
 constexpr size_t kPartML = (size_t)kDecHeads * kAttnSplits * 2;
 constexpr size_t kPartO = (size_t)kDecHeads * kAttnSplits * kHeadDim;
-constexpr size_t kScratchFloats = 16 + kPartML + kPartO;   // ~2.1 MB
+constexpr size_t kScratchFloats = kPartOff + kPartML + kPartO;   // ~2.1 MB
 
-static_assert(sizeof(StreamSlot) <= 8 * sizeof(float), "descriptor fits its slot");
+static_assert(sizeof(StreamSlot) <= kSlotFloats * sizeof(float), "descriptor fits its slot");
 
 // Every GPU that loads the library holds this array until the process exits.
 static __device__ __align__(256) float g_noalloc_scratch[kScratchFloats];
@@ -89,9 +90,9 @@ extern "C" int vox_cuda_attention_decode_noalloc(const float *q, const float *k_
     }
     cudaStream_t st = (cudaStream_t)stream;
     StreamSlot h = {const_cast<float *>(k_ring), const_cast<float *>(v_ring), kv_cap, pos,
-                    pos % kv_cap, n_keys};
+                    pos % kv_cap, n_keys, pos};
     StreamSlot *slot = reinterpret_cast<StreamSlot *>(base);
-    unsigned *tickets = reinterpret_cast<unsigned *>(base + 8);
+    unsigned *tickets = reinterpret_cast<unsigned *>(base + kTicketOff);
     // the descriptor and the tickets (which must start at zero) are rewritten
     // by every call: the array keeps the previous call's contents
     if (cudaMemcpyAsync(slot, &h, sizeof(h), cudaMemcpyHostToDevice, st) != cudaSuccess ||
@@ -104,8 +105,8 @@ extern "C" int vox_cuda_attention_decode_noalloc(const float *q, const float *k_
     p.slots = slot;
     p.layer = 0;
     p.out = out;
-    p.part_ml = base + 16;
-    p.part_o = base + 16 + kPartML;
+    p.part_ml = base + kPartOff;
+    p.part_o = base + kPartOff + kPartML;
     p.counters = tickets;
     p.S = kAttnSplits;
     cudaError_t e = launch_attn_decode(1, p, st, false);

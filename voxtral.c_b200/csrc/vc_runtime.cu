@@ -720,7 +720,7 @@ extern "C" int vox_cuda_attention_decode_dev(const float *q, const float *k_ring
     if (rc) return rc;
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
     StreamSlot h = {const_cast<float *>(k_ring), const_cast<float *>(v_ring), kv_cap, pos,
-                    pos % kv_cap, n_keys};
+                    pos % kv_cap, n_keys, pos};
     // the slot descriptor is copied through a stream-ordered memcpy so that
     // back-to-back calls on one stream do not race on it
     VC_TRY(cudaMemcpyAsync(c->attn_slot, &h, sizeof(h), cudaMemcpyHostToDevice, st));
@@ -1175,6 +1175,7 @@ void fill_slot(vox_cuda_dec_state *s, int pos, StreamSlot *slot) {
     slot->pos = pos;
     slot->slot = pos % s->cap;
     slot->n_keys = (pos + 1 < kDecWindow) ? pos + 1 : kDecWindow;
+    slot->fresh = pos;   // a launch with more rows of this sequence lowers it
 }
 
 // Rows first..last are written in one launch: the ring must hold, at once,
@@ -1349,6 +1350,7 @@ int prefill_tc_rows(vox_cuda_decoder *d, DevCtx *c, vox_cuda_dec_state *const *s
             for (int r = 0; r < take; r++) {
                 const int pos = s->pos + done_in_state + r;
                 fill_slot(s, pos, h_slots + M + r);
+                h_slots[M + r].fresh = s->pos + done_in_state;   // this launch's first row of the state
                 max_keys = std::max(max_keys, h_slots[M + r].n_keys);
                 if (rope) memcpy(h_rope + (size_t)(M + r) * kHeadDim, rope + (row_in + r) * kHeadDim, kHeadDim * 4);
                 else host_rope_table(pos, kHeadDim, h_rope + (size_t)(M + r) * kHeadDim);
@@ -1793,6 +1795,7 @@ extern "C" int vox_cuda_decoder_prefill_step(vox_cuda_dec_state *s, const float 
         for (int i = 0; i < n; i++) {
             const int pos = s->pos + r0 + i;
             fill_slot(s, pos, h_slots(w) + i);
+            h_slots(w)[i].fresh = s->pos + r0;   // the chunk's first row
             if (rope_freqs) memcpy(h_rope(w) + i * kHeadDim, rope_freqs + (size_t)(r0 + i) * kHeadDim, kHeadDim * 4);
             else host_rope_table(pos, kHeadDim, h_rope(w) + i * kHeadDim);
         }
