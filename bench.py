@@ -329,7 +329,7 @@ def encoder_bench(V, torch, steps, only_rows=0):
         out["ms_per_chunk"][f"M{M}"] = ms
         out["audio_s_per_s"][f"M{M}"] = (M / 50.0) / (ms / 1000.0)
     if not only_rows:
-        out["multi_stream_M100"] = multi_stream_encoder(enc, torch, x0, steps)
+        out["multi_stream_M100"] = multi_stream_encoder(V, enc, torch, x0, steps)
         out["front_end_2s_chunks"] = front_bench(V, torch, steps)
     if only_rows and only_rows != 1500:
         st.free()
@@ -354,42 +354,45 @@ def encoder_bench(V, torch, steps, only_rows=0):
     return out
 
 
-def multi_stream_encoder(enc, torch, x0, steps, streams=8, rows=100):
+def multi_stream_encoder(V, enc, torch, x0, steps, streams=8, rows=100):
     """configs[4]'s encoder load: `streams` streams each feeding a 2 s chunk
-    (100 rows) with a full window behind it, every stream on its own CUDA
-    stream (vox_cuda_encoder_step_dev per state; weights shared), against the
-    same chunks run one after another on one stream."""
+    (100 rows) with a full window behind it: one after another on one CUDA
+    stream (serial), every stream on its own CUDA stream (concurrent,
+    vox_cuda_encoder_step_dev per state; weights shared), and all streams'
+    rows as one launch (batched, vox_cuda_encoder_step_batch_dev)."""
     states = [enc.state(max_chunk=rows) for _ in range(streams)]
     cstreams = [torch.cuda.Stream() for _ in range(streams)]
     xs = [torch.empty((rows, ENC_D), dtype=torch.float32, device="cuda") for _ in range(streams)]
     main = torch.cuda.Stream()
 
-    def round_(concurrent):
+    def round_(mode):
         for i, (st, x) in enumerate(zip(states, xs)):
             st.set_position(750)
             x.copy_(x0[i * 10:i * 10 + rows])
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(main)
-        for st, x, cs in zip(states, xs, cstreams):
-            s = cs if concurrent else main
-            if concurrent:
-                s.wait_event(e0)
-            st.step_dev(x.data_ptr(), rows, s.cuda_stream)
-        if concurrent:
-            for cs in cstreams:
-                main.wait_stream(cs)
+        if mode == "batched":   # one launch over all streams' rows
+            V.encoder_step_batch_dev(states, [x.data_ptr() for x in xs], [rows] * streams, main.cuda_stream)
+        else:
+            for st, x, cs in zip(states, xs, cstreams):
+                s = cs if mode == "concurrent" else main
+                if mode == "concurrent":
+                    s.wait_event(e0)
+                st.step_dev(x.data_ptr(), rows, s.cuda_stream)
+            if mode == "concurrent":
+                for cs in cstreams:
+                    main.wait_stream(cs)
         e1.record(main)
         torch.cuda.synchronize()
         return e0.elapsed_time(e1)
 
     res = {}
-    for concurrent in (False, True):
+    for mode in ("serial", "concurrent", "batched"):
         for _ in range(2):
-            round_(concurrent)
-        ms = sorted(round_(concurrent) for _ in range(max(3, steps // 2)))[0]
-        key = "concurrent" if concurrent else "serial"
-        res[key] = {"ms_per_round": ms, "audio_s_per_s": streams * rows / 50.0 / (ms / 1000.0)}
+            round_(mode)
+        ms = sorted(round_(mode) for _ in range(max(3, steps // 2)))[0]
+        res[mode] = {"ms_per_round": ms, "audio_s_per_s": streams * rows / 50.0 / (ms / 1000.0)}
     res["streams"], res["rows_per_chunk"] = streams, rows
     for st in states:
         st.free()

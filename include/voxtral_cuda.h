@@ -306,6 +306,16 @@ int vox_cuda_encoder_full_step(vox_cuda_enc_state *s, float *x, int new_len, con
  * synchronous on the host). */
 int vox_cuda_encoder_step_dev(vox_cuda_enc_state *s, float *x_dev, int new_len, void *stream);
 
+/* Several streams' chunks as one launch: state i takes new_lens[i] rows at
+ * x_dev[i] (device, in place), n <= 8 states of one encoder.  The norms and
+ * the tensor-core GEMMs run once over all rows (8 x 100 rows -> M = 800,
+ * tensor-bound instead of SM-count-bound); each state's windowed attention
+ * runs over its own ring, concurrently.  Enqueued on `stream` without
+ * waiting, like vox_cuda_encoder_step_dev; each state's position advances.
+ * Additive: the reference runs one encoder context at a time. */
+int vox_cuda_encoder_step_batch_dev(vox_cuda_enc_state *const *states, int n, float *const *x_dev,
+                                    const int *new_lens, void *stream);
+
 /* Set the logical position of the next chunk's first row (resume, tests). */
 int vox_cuda_enc_state_set_position(vox_cuda_enc_state *s, int logical_pos);
 

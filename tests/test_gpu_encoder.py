@@ -204,3 +204,36 @@ def test_encoder_rejects_oversized_chunk(gpu_enc):
     with pytest.raises(V.VoxCudaError):
         st.step(np.zeros((65, B.ENC_DIM), np.float32))
     st.free()
+
+
+def test_encoder_batched_launch_matches_per_state_steps():
+    """vox_cuda_encoder_step_batch_dev: four states' chunks (100, 37, 256 and
+    90 rows, two rounds, the second state starting from position 300) as
+    one launch per round against each state stepping alone.  The GEMMs see
+    another M (tiling and split-K choices differ), so the fp16 operands may
+    round differently: the encoder tolerance applies."""
+    import torch
+    ew = B.EncoderWeights(seed=12, n_layers=3, distinct=3, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    lens = [100, 37, 256, 90]
+    alone = [e.state(max_chunk=256) for _ in lens]
+    batch = [e.state(max_chunk=256) for _ in lens]
+    alone[1].set_position(300)
+    batch[1].set_position(300)
+    stream = torch.cuda.Stream()
+    for rnd in range(2):
+        xs = [B.normal_f32((n, B.ENC_DIM), 1100 + 10 * rnd + i) for i, n in enumerate(lens)]
+        want = [st.step(x) for st, x in zip(alone, xs)]
+        devs = [torch.from_numpy(x).cuda() for x in xs]
+        torch.cuda.synchronize()
+        V.encoder_step_batch_dev(batch, [d.data_ptr() for d in devs], lens, stream.cuda_stream)
+        stream.synchronize()
+        for i, (d, w) in enumerate(zip(devs, want)):
+            got = d.cpu().numpy()
+            assert np.isfinite(got).all()
+            assert B.rel_l2(got, w) < ENC_TOL, (rnd, i, B.rel_l2(got, w))
+    for a, b in zip(alone, batch):
+        assert a.position == b.position
+        a.free()
+        b.free()
+    e.free()

@@ -308,6 +308,36 @@ cudaError_t launch_enc_rope_table(float *tab, int ld, int M, const float *src, c
     return cudaLaunchKernelEx(&cfg, enc_rope_table_kernel, tab, ld, M, src, pos0_dev, inv_freq);
 }
 
+__global__ void __launch_bounds__(256)
+enc_rope_table_segs_kernel(float *tab, int ld, int M, const EncSeg *segs, int n_segs, const float *inv_freq) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;   // row * 32 + d
+    if (i >= M * (kEncHeadDim / 2)) return;
+    const int row = i / (kEncHeadDim / 2), d = i % (kEncHeadDim / 2);
+    int s = 0;
+    while (s + 1 < n_segs && row >= segs[s + 1].row0) s++;
+    float sn, cs;
+    sincosf((float)(*segs[s].pos0_dev + (row - segs[s].row0)) * inv_freq[d], &sn, &cs);
+    tab[(size_t)d * ld + row] = cs;
+    tab[(size_t)(kEncHeadDim / 2 + d) * ld + row] = sn;
+}
+
+cudaError_t launch_enc_rope_table_segs(float *tab, int ld, int M, const EncSeg *segs, int n_segs,
+                                       const float *inv_freq, cudaStream_t st, bool pdl) {
+    const int n = M * (kEncHeadDim / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((n + 255) / 256);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, enc_rope_table_segs_kernel, tab, ld, M, segs, n_segs, inv_freq);
+}
+
 __global__ void set_int_kernel(int *dst, int v) { *dst = v; }
 
 cudaError_t launch_set_int(int *dst, int v, cudaStream_t st) {

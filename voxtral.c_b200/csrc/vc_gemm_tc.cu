@@ -101,6 +101,8 @@ struct EpiRow {
     int row;        // output row (this thread's TMEM lane)
     int pos;        // TC_QKV_ENC: logical position of the row
     size_t slot;    // TC_QKV_ENC: ring slot of the row
+    uint16_t *ek, *ev;   // TC_QKV_ENC: the row's rings (this layer)
+    int ecap;            // TC_QKV_ENC: their capacity
     float *kd, *vd; // TC_QKV_DEC: the row's K / V ring rows (this layer)
 };
 
@@ -112,9 +114,25 @@ __device__ __forceinline__ EpiRow epi_row(const TcGemmParams &p, int row) {
     er.pos = 0;
     er.slot = 0;
     er.kd = er.vd = nullptr;
+    er.ek = er.ev = nullptr;
+    er.ecap = 0;
     if constexpr (EPI == TC_QKV_ENC) {
-        er.pos = (p.pos0_dev ? *p.pos0_dev : p.pos0) + row;
-        er.slot = (size_t)(er.pos % p.cap);
+        if (p.segs) {   // several streams' rows: the row's segment (row0 ascending)
+            int s = 0;
+            while (s + 1 < p.n_segs && row >= p.segs[s + 1].row0) s++;
+            const EncSeg g = p.segs[s];
+            er.pos = *g.pos0_dev + (row - g.row0);
+            er.ecap = g.cap;
+            const size_t lo = (size_t)p.layer * g.cap * kEncQkv;
+            er.ek = g.k_ring + lo;
+            er.ev = g.v_ring + lo;
+        } else {
+            er.pos = (p.pos0_dev ? *p.pos0_dev : p.pos0) + row;
+            er.ecap = p.cap;
+            er.ek = p.k_ring;
+            er.ev = p.v_ring;
+        }
+        er.slot = (size_t)(er.pos % er.ecap);
     }
     if constexpr (EPI == TC_QKV_DEC) {
         if (row < p.M) {
@@ -276,8 +294,8 @@ __device__ __forceinline__ void epi_vec(const TcGemmParams &p, const EpiRow &er,
             *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     } else if constexpr (EPI == TC_QKV_ENC) {
         uint16_t *dst = region == 0   ? p.q_out + (size_t)row * kEncQkv + col0
-                        : region == 1 ? p.k_ring + er.slot * kEncQkv + (col0 - kEncQkv)
-                                      : p.v_ring + er.slot * kEncQkv + (col0 - 2 * kEncQkv);
+                        : region == 1 ? er.ek + er.slot * kEncQkv + (col0 - kEncQkv)
+                                      : er.ev + er.slot * kEncQkv + (col0 - 2 * kEncQkv);
 #pragma unroll
         for (int j = 0; j < kEpiCols; j += 8)
             st16(dst + j, pack_half2(v[j], v[j + 1]), pack_half2(v[j + 2], v[j + 3]), pack_half2(v[j + 4], v[j + 5]),
@@ -321,8 +339,8 @@ __device__ __forceinline__ void epi_scalar(const TcGemmParams &p, const EpiRow &
         for (int j = 0; j < kEpiCols; j++) dst[j] = v[j];
     } else if constexpr (EPI == TC_QKV_ENC) {
         uint16_t *dst = region == 0   ? p.q_out + (size_t)row * kEncQkv + col0
-                        : region == 1 ? p.k_ring + er.slot * kEncQkv + (col0 - kEncQkv)
-                                      : p.v_ring + er.slot * kEncQkv + (col0 - 2 * kEncQkv);
+                        : region == 1 ? er.ek + er.slot * kEncQkv + (col0 - kEncQkv)
+                                      : er.ev + er.slot * kEncQkv + (col0 - 2 * kEncQkv);
 #pragma unroll
         for (int j = 0; j < kEpiCols; j += 2)
             *reinterpret_cast<uint32_t *>(dst + j) = pack_half2(v[j], v[j + 1]);
@@ -1067,8 +1085,8 @@ bool make_out_maps(int epi, const TcGemmParams &p, CUtensorMap *mo, CUtensorMap 
         case TC_SWIGLU:
             return make_map_2d(mo, p.out_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.N / 2, p.ldo_bf16, 16, 32,
                                CU_TENSOR_MAP_SWIZZLE_32B);
-        case TC_QKV_ENC:
-            if (p.N != 3 * kEncQkv || p.cap < 32) return false;
+        case TC_QKV_ENC:   // (a batched launch's rows go to several rings: direct stores)
+            if (p.N != 3 * kEncQkv || p.cap < 32 || p.segs) return false;
             return make_map_2d(mo, p.q_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.M, kEncQkv, kEncQkv, 32, 32,
                                CU_TENSOR_MAP_SWIZZLE_64B) &&
                    make_map_2d(mk, p.k_ring, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.cap, kEncQkv, kEncQkv, 32, 32,

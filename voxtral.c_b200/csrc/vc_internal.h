@@ -101,6 +101,17 @@ enum TcEpi : int {
     TC_QKV_DEC = 4,   // decoder q|k|v: RoPE, q (fp32) out, k / v (fp32) to each row's ring slot
 };
 
+// One stream's rows in a batched encoder launch: rows [row0, next row0) of
+// the launch sit at logical positions *pos0_dev + (row - row0) of this
+// state's ring (layer `TcGemmParams::layer` at k_ring + layer * cap * 2048).
+struct EncSeg {
+    uint16_t *k_ring, *v_ring;   // layer 0 base, fp16 [layers][cap][2048]
+    const int *pos0_dev;
+    int cap;
+    int row0;
+};
+constexpr int kEncMaxSegs = 8;
+
 struct TcGemmParams {
     int M, N, K;
     float *out;              // fp32 [M, ldo]
@@ -139,6 +150,9 @@ struct TcGemmParams {
     const StreamSlot *slots; // [M]: each row's ring and slot
     int layer;
     const float *rope_rows;  // [M][128]: (cos, sin) of pair d at [2d], [2d + 1]
+    // TC_QKV_ENC over several streams' rows (batched encoder), or NULL
+    const EncSeg *segs;      // device [n_segs], row0 ascending
+    int n_segs;
     int vec;                 // set by launch_tc_gemm: all destinations allow 16-byte stores
     int tma_out;             // set by launch_tc_gemm: the epilogue stores through TMA
 };
@@ -183,6 +197,9 @@ bool enc_attn_tc_supported(const EncAttnParams &p);
 cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl);
 constexpr int kEncRingAlign = 128;   // encoder ring capacities are multiples of this
 cudaError_t launch_rows_rmsnorm(float *x, int M, int K, const float *w, cudaStream_t st, bool pdl);
+// RoPE planes of a batched encoder launch: each row's position from its segment
+cudaError_t launch_enc_rope_table_segs(float *tab, int ld, int M, const EncSeg *segs, int n_segs,
+                                       const float *inv_freq, cudaStream_t st, bool pdl);
 // *dst = v in stream order (the value travels as a kernel argument)
 cudaError_t launch_set_int(int *dst, int v, cudaStream_t st);
 // RoPE planes of a chunk for the q|k epilogue: tab[d][row] = cos and

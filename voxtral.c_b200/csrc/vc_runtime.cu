@@ -2153,6 +2153,41 @@ struct EncLayer {
 
 }  // namespace
 
+namespace {
+
+// Workspace of batched encoder launches (several states' chunks as one row
+// block, vox_cuda_encoder_step_batch_dev): the row-wise kernels and GEMMs run
+// once over all rows; each state's attention runs on its own side stream,
+// forked and joined inside the captured graph.
+struct EncBatch {
+    int cap = 0;                  // rows
+    char *ws = nullptr;
+    size_t ws_bytes = 0;
+    float *x = nullptr;           // [cap][1280]
+    uint16_t *xn16 = nullptr;     // [cap][1280] fp16
+    uint16_t *att16 = nullptr;    // [cap][2048]
+    uint16_t *h16 = nullptr;      // [cap][5120]
+    uint16_t *q16 = nullptr;      // [cap][2048]
+    float *rope = nullptr;        // planes [64][cap]
+    float *split = nullptr;       // split-K partials [kEncSplitFloats]
+    unsigned *split_cnt = nullptr;
+    unsigned *err = nullptr;
+    unsigned *h_err = nullptr;    // pinned
+    cudaEvent_t err_ev = nullptr;
+    bool err_pending = false;
+    cudaStream_t side[kEncMaxSegs] = {};
+    cudaEvent_t fork = nullptr, join[kEncMaxSegs] = {};
+    struct Graph {
+        cudaGraphExec_t exec = nullptr;
+        EncSeg *segs = nullptr;   // device [n]: this key's segments
+    };
+    // (states, rows) of a launch -> its graph
+    std::map<std::vector<std::pair<const void *, int>>, Graph> graphs;
+};
+void free_enc_batch(DevCtx *c, EncBatch *b);
+
+}  // namespace
+
 struct vox_cuda_encoder {
     int device = 0;
     int n_layers = 0;
@@ -2162,6 +2197,8 @@ struct vox_cuda_encoder {
     const float *inv_freq = nullptr;   // [32] RoPE inverse frequencies (head_dim 64)
     std::vector<std::pair<void *, size_t>> owned;
     bool pdl = true;
+    EncBatch *batch = nullptr;
+    std::mutex mu;   // serialises batched launches (they share `batch`)
 };
 
 struct vox_cuda_enc_state {
@@ -2318,6 +2355,7 @@ extern "C" void vox_cuda_encoder_free(vox_cuda_encoder *e) {
     DevCtx *c = ctx_for(e->device);
     cudaSetDevice(e->device);
     if (c) cudaStreamSynchronize(c->stream);
+    free_enc_batch(c, e->batch);
     for (auto &pr : e->owned)
         if (c) dev_free(c, pr.first, pr.second);
         else cudaFree(pr.first);
@@ -2644,6 +2682,240 @@ extern "C" int vox_cuda_encoder_step_dev(vox_cuda_enc_state *s, float *x_dev, in
     if (st != c->stream) VC_TRY(cudaStreamWaitEvent(c->stream, s->tail, 0));
     s->tail_set = true;
     s->pos += new_len;
+    return VOX_CUDA_OK;
+}
+
+namespace {
+
+void free_enc_batch(DevCtx *c, EncBatch *b) {
+    if (!b) return;
+    for (auto &kv : b->graphs) {
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+        if (kv.second.segs) cudaFree(kv.second.segs);
+    }
+    if (c) dev_free(c, b->ws, b->ws ? b->ws_bytes : 0);
+    if (b->h_err) cudaFreeHost(b->h_err);
+    if (b->err_ev) cudaEventDestroy(b->err_ev);
+    if (b->fork) cudaEventDestroy(b->fork);
+    for (int i = 0; i < kEncMaxSegs; i++) {
+        if (b->side[i]) cudaStreamDestroy(b->side[i]);
+        if (b->join[i]) cudaEventDestroy(b->join[i]);
+    }
+    delete b;
+}
+
+EncBatch *make_enc_batch(DevCtx *c, int rows) {
+    EncBatch *b = new EncBatch();
+    b->cap = (int)align_up((size_t)rows, 128);
+    const size_t R = (size_t)b->cap;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const size_t o_x = take(R * kEncDim * 4), o_xn = take(R * kEncDim * 2), o_att = take(R * kEncQkv * 2);
+    const size_t o_h = take(R * kEncHidden * 2), o_q = take(R * kEncQkv * 2), o_rope = take(R * kEncHeadDim * 4);
+    const size_t o_split = take(kEncSplitFloats * 4), o_cnt = take(kTcSplitCounters * 4), o_err = take(4);
+    b->ws_bytes = off;
+    bool ok = dev_alloc(c, (void **)&b->ws, b->ws_bytes) == cudaSuccess &&
+              cudaMemset(b->ws, 0, b->ws_bytes) == cudaSuccess &&
+              cudaHostAlloc((void **)&b->h_err, sizeof(unsigned), cudaHostAllocDefault) == cudaSuccess &&
+              cudaEventCreateWithFlags(&b->err_ev, cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreateWithFlags(&b->fork, cudaEventDisableTiming) == cudaSuccess;
+    for (int i = 0; i < kEncMaxSegs && ok; i++)
+        ok = cudaStreamCreateWithFlags(&b->side[i], cudaStreamNonBlocking) == cudaSuccess &&
+             cudaEventCreateWithFlags(&b->join[i], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
+        set_error("encoder batch workspace: allocation of %zu bytes failed", b->ws_bytes);
+        free_enc_batch(c, b);
+        return nullptr;
+    }
+    *b->h_err = 0;
+    char *w = b->ws;
+    b->x = (float *)(w + o_x);
+    b->xn16 = (uint16_t *)(w + o_xn);
+    b->att16 = (uint16_t *)(w + o_att);
+    b->h16 = (uint16_t *)(w + o_h);
+    b->q16 = (uint16_t *)(w + o_q);
+    b->rope = (float *)(w + o_rope);
+    b->split = (float *)(w + o_split);
+    b->split_cnt = (unsigned *)(w + o_cnt);
+    b->err = (unsigned *)(w + o_err);
+    return b;
+}
+
+// The layers of one batched launch over M rows of n states (segments `segs`,
+// rows[i] rows of state i from row0[i]): the encoder chunk of
+// vox_encoder_forward_incremental (voxtral_encoder.c:452-636) for all of them,
+// the row-wise work once, the attention per state on forked side streams.
+int enqueue_encoder_batch(vox_cuda_encoder *e, EncBatch *b, vox_cuda_enc_state *const *states, const int *rows,
+                          const int *row0, int n, int M, const EncSeg *segs, cudaStream_t st) {
+    const bool pdl = e->pdl;
+    VC_TRY(launch_enc_rope_table_segs(b->rope, b->cap, M, segs, n, e->inv_freq, st, false));
+    auto gemm = [&](int N, int K) {
+        TcGemmParams p = {};
+        p.M = M;
+        p.N = N;
+        p.K = K;
+        p.err = b->err;
+        p.f16 = 1;
+        p.ws = b->split;
+        p.ws_floats = kEncSplitFloats;
+        p.ws_cnt = b->split_cnt;
+        return p;
+    };
+    for (int l = 0; l < e->n_layers; l++) {
+        const EncLayer &L = e->L[l];
+        VC_TRY(launch_rows_to_bf16(b->x, M, kEncDim, kEncDim, L.attn_norm, b->xn16, st, pdl, true));
+        TcGemmParams p = gemm(3 * kEncQkv, kEncDim);
+        p.bias = L.bq;
+        p.bias2 = L.bv;
+        p.rope = b->rope;
+        p.rope_ld = b->cap;
+        p.inv_freq = e->inv_freq;
+        p.q_out = b->q16;
+        p.segs = segs;
+        p.n_segs = n;
+        p.layer = l;
+        p.cap = 1 << 30;   // (the rings are the segments')
+        VC_TRY(launch_tc_gemm(TC_QKV_ENC, p, b->xn16, L.qkv, st, pdl));
+        // each state's windowed attention over its own ring, concurrently
+        VC_TRY(cudaEventRecord(b->fork, st));
+        for (int i = 0; i < n; i++) {
+            vox_cuda_enc_state *s = states[i];
+            const size_t ring_layer = (size_t)s->cap * kEncQkv;
+            VC_TRY(cudaStreamWaitEvent(b->side[i], b->fork, 0));
+            EncAttnParams a = {};
+            a.q = b->q16 + (size_t)row0[i] * kEncQkv;
+            a.k_ring = s->k_ring + l * ring_layer;
+            a.v_ring = s->v_ring + l * ring_layer;
+            a.cap = s->cap;
+            a.pos0_dev = s->pos_dev;
+            a.M = rows[i];
+            a.out = b->att16 + (size_t)row0[i] * kEncQkv;
+            a.f16 = 1;
+            a.err = b->err;
+            VC_TRY(launch_enc_attn(a, b->side[i], false));
+            VC_TRY(cudaEventRecord(b->join[i], b->side[i]));
+            VC_TRY(cudaStreamWaitEvent(st, b->join[i], 0));
+        }
+        p = gemm(kEncDim, kEncQkv);
+        p.out = b->x;
+        p.ldo = kEncDim;
+        p.bias = L.bo;
+        VC_TRY(launch_tc_gemm(TC_RESID, p, b->att16, L.wo, st, false));
+        VC_TRY(launch_rows_to_bf16(b->x, M, kEncDim, kEncDim, L.ffn_norm, b->xn16, st, pdl, true));
+        p = gemm(2 * kEncHidden, kEncDim);
+        p.out_bf16 = b->h16;
+        p.ldo_bf16 = kEncHidden;
+        VC_TRY(launch_tc_gemm(TC_SWIGLU, p, b->xn16, L.w13, st, pdl));
+        p = gemm(kEncDim, kEncHidden);
+        p.out = b->x;
+        p.ldo = kEncDim;
+        p.bias = L.b2;
+        VC_TRY(launch_tc_gemm(TC_RESID, p, b->h16, L.w2, st, pdl));
+    }
+    VC_TRY(launch_rows_rmsnorm(b->x, M, kEncDim, e->norm, st, pdl));
+    return VOX_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" int vox_cuda_encoder_step_batch_dev(vox_cuda_enc_state *const *states, int n, float *const *x_dev,
+                                               const int *new_lens, void *stream) {
+    if (!states || n <= 0 || n > kEncMaxSegs || !x_dev || !new_lens || !states[0]) {
+        set_error("encoder_step_batch_dev: 1..%d states with their rows", kEncMaxSegs);
+        return VOX_CUDA_ERR_ARG;
+    }
+    vox_cuda_encoder *e = states[0]->enc;
+    int M = 0, row0[kEncMaxSegs];
+    for (int i = 0; i < n; i++) {
+        int rc = enc_check(states[i], new_lens[i]);
+        if (rc) return rc;
+        if (!x_dev[i] || states[i]->enc != e) {
+            set_error("encoder_step_batch_dev: states must share one encoder, x_dev non-NULL");
+            return VOX_CUDA_ERR_ARG;
+        }
+        for (int j = 0; j < i; j++)
+            if (states[j] == states[i]) {
+                set_error("encoder_step_batch_dev: a state appears twice");
+                return VOX_CUDA_ERR_ARG;
+            }
+        row0[i] = M;
+        M += new_lens[i];
+    }
+    DevCtx *c = ctx_for(e->device);
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    std::lock_guard<std::mutex> lk(e->mu);
+    EncBatch *b = e->batch;
+    if (b && b->cap < M) {   // grow: the graphs hold the old pointers
+        VC_TRY(cudaDeviceSynchronize());
+        free_enc_batch(c, b);
+        b = e->batch = nullptr;
+    }
+    if (!b && !(b = e->batch = make_enc_batch(c, std::max(M, 1024)))) return VOX_CUDA_ERR_OOM;
+    // a timeout raised by an earlier batched launch is reported now
+    if (b->err_pending && cudaEventQuery(b->err_ev) == cudaSuccess) {
+        b->err_pending = false;
+        if (*b->h_err) {
+            *b->h_err = 0;
+            VC_TRY(cudaMemsetAsync(b->err, 0, sizeof(unsigned), st));
+            set_error("encoder batch: a device-side wait of an earlier launch timed out (its results are invalid)");
+            return VOX_CUDA_ERR_CUDA;
+        }
+    }
+    std::vector<std::pair<const void *, int>> key;
+    for (int i = 0; i < n; i++) key.push_back({states[i], new_lens[i]});
+    EncBatch::Graph &g = b->graphs[key];
+    if (!g.exec) {
+        EncSeg h[kEncMaxSegs];
+        for (int i = 0; i < n; i++) h[i] = EncSeg{states[i]->k_ring, states[i]->v_ring, states[i]->pos_dev,
+                                                  states[i]->cap, row0[i]};
+        if (cudaMalloc((void **)&g.segs, sizeof(EncSeg) * n) != cudaSuccess ||
+            cudaMemcpy(g.segs, h, sizeof(EncSeg) * n, cudaMemcpyHostToDevice) != cudaSuccess) {
+            set_error("encoder_step_batch_dev: segment table allocation failed");
+            b->graphs.erase(key);
+            return VOX_CUDA_ERR_CUDA;
+        }
+        cudaGraph_t graph = nullptr;
+        VC_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue_encoder_batch(e, b, states, new_lens, row0, n, M, g.segs, st);
+        cudaError_t ce = cudaStreamEndCapture(st, &graph);
+        if (rc == VOX_CUDA_OK && ce == cudaSuccess) ce = cudaGraphInstantiate(&g.exec, graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+        if (rc || ce != cudaSuccess) {
+            cudaFree(g.segs);
+            b->graphs.erase(key);
+            if (!rc) set_error("encoder_step_batch_dev: graph capture failed: %s", cudaGetErrorString(ce));
+            return rc ? rc : VOX_CUDA_ERR_CUDA;
+        }
+    }
+    for (int i = 0; i < n; i++) {
+        vox_cuda_enc_state *s = states[i];
+        // the previous asynchronous step of this state may have run on another stream
+        if (s->tail_set && st != c->stream) VC_TRY(cudaStreamWaitEvent(st, s->tail, 0));
+        VC_TRY(launch_set_int(s->pos_dev, s->pos, st));
+        VC_TRY(cudaMemcpyAsync(b->x + (size_t)row0[i] * kEncDim, x_dev[i], (size_t)new_lens[i] * kEncDim * 4,
+                               cudaMemcpyDeviceToDevice, st));
+    }
+    VC_TRY(cudaGraphLaunch(g.exec, st));
+    for (int i = 0; i < n; i++)
+        VC_TRY(cudaMemcpyAsync(x_dev[i], b->x + (size_t)row0[i] * kEncDim, (size_t)new_lens[i] * kEncDim * 4,
+                               cudaMemcpyDeviceToDevice, st));
+    if (!b->err_pending) {   // one flag copy in flight at a time
+        VC_TRY(cudaMemcpyAsync(b->h_err, b->err, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+        VC_TRY(cudaEventRecord(b->err_ev, st));
+        b->err_pending = true;
+    }
+    // order the library stream after this launch for every state (as step_dev)
+    for (int i = 0; i < n; i++) {
+        vox_cuda_enc_state *s = states[i];
+        VC_TRY(cudaEventRecord(s->tail, st));
+        if (st != c->stream) VC_TRY(cudaStreamWaitEvent(c->stream, s->tail, 0));
+        s->tail_set = true;
+        s->pos += new_lens[i];
+    }
     return VOX_CUDA_OK;
 }
 

@@ -107,6 +107,7 @@ def lib():
                                            C.c_int),
         "vox_cuda_decoder_profile_sequence": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int,
                                                _fp], C.c_int),
+        "vox_cuda_encoder_step_batch_dev": ([C.c_void_p, C.c_int, C.c_void_p, _ip, C.c_void_p], C.c_int),
         "vox_cuda_encoder_create": ([C.c_void_p], C.c_void_p),
         "vox_cuda_encoder_free": ([C.c_void_p], None),
         "vox_cuda_enc_state_create": ([C.c_void_p, C.c_int], C.c_void_p),
@@ -329,6 +330,16 @@ def profile_sequence(states, embeds_dev, phase, iters=5):
                                                   PROF_PHASES.index(phase), iters, _f(ms)),
           "profile_sequence")
     return float(ms[0])
+
+
+def encoder_step_batch_dev(states, x_devs, lens, stream=None):
+    """One launch over several encoder states' chunks (device addresses x_devs,
+    rows lens), in place."""
+    n = len(states)
+    xs = (C.c_void_p * n)(*x_devs)
+    ln = np.ascontiguousarray(lens, np.int32)
+    check(lib().vox_cuda_encoder_step_batch_dev(states_array(states), n, xs, ln.ctypes.data_as(_ip), stream),
+          "encoder_step_batch_dev")
 
 
 class Encoder:
