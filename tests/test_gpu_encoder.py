@@ -234,6 +234,20 @@ def test_encoder_batched_launch_matches_per_state_steps():
             assert B.rel_l2(got, w) < ENC_TOL, (rnd, i, B.rel_l2(got, w))
     for a, b in zip(alone, batch):
         assert a.position == b.position
+    # a state freed and replaced (possibly at the same address) must not reuse
+    # the launch captured with the old one
+    batch[1].free()
+    alone[1].free()
+    batch[1], alone[1] = e.state(max_chunk=256), e.state(max_chunk=256)
+    xs = [B.normal_f32((n, B.ENC_DIM), 1200 + i) for i, n in enumerate(lens)]
+    want = [st.step(x) for st, x in zip(alone, xs)]
+    devs = [torch.from_numpy(x).cuda() for x in xs]
+    torch.cuda.synchronize()
+    V.encoder_step_batch_dev(batch, [d.data_ptr() for d in devs], lens, stream.cuda_stream)
+    stream.synchronize()
+    for i, (d, w) in enumerate(zip(devs, want)):
+        assert B.rel_l2(d.cpu().numpy(), w) < ENC_TOL, (i, B.rel_l2(d.cpu().numpy(), w))
+    for a, b in zip(alone, batch):
         a.free()
         b.free()
     e.free()

@@ -2185,6 +2185,9 @@ struct EncBatch {
     std::map<std::vector<std::pair<const void *, int>>, Graph> graphs;
 };
 void free_enc_batch(DevCtx *c, EncBatch *b);
+// Destroy the batched graphs that name `state` (all of them when NULL): a
+// graph holds its states' ring and position pointers.
+void drop_batch_graphs(EncBatch *b, const void *state);
 
 }  // namespace
 
@@ -2453,6 +2456,10 @@ extern "C" void vox_cuda_enc_state_free(vox_cuda_enc_state *s) {
     if (s->err_ev) cudaEventDestroy(s->err_ev);
     if (s->tail) cudaEventDestroy(s->tail);
     for (auto &kv : s->graphs) cudaGraphExecDestroy(kv.second);
+    {   // batched launches captured with this state must not outlive it
+        std::lock_guard<std::mutex> lk(s->enc->mu);
+        if (s->enc->batch) drop_batch_graphs(s->enc->batch, s);
+    }
     delete s;
 }
 
@@ -2687,12 +2694,23 @@ extern "C" int vox_cuda_encoder_step_dev(vox_cuda_enc_state *s, float *x_dev, in
 
 namespace {
 
+void drop_batch_graphs(EncBatch *b, const void *state) {
+    for (auto it = b->graphs.begin(); it != b->graphs.end();) {
+        bool hit = state == nullptr;
+        for (const auto &kv : it->first) hit = hit || kv.first == state;
+        if (!hit) {
+            ++it;
+            continue;
+        }
+        if (it->second.exec) cudaGraphExecDestroy(it->second.exec);
+        if (it->second.segs) cudaFree(it->second.segs);
+        it = b->graphs.erase(it);
+    }
+}
+
 void free_enc_batch(DevCtx *c, EncBatch *b) {
     if (!b) return;
-    for (auto &kv : b->graphs) {
-        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-        if (kv.second.segs) cudaFree(kv.second.segs);
-    }
+    drop_batch_graphs(b, nullptr);
     if (c) dev_free(c, b->ws, b->ws ? b->ws_bytes : 0);
     if (b->h_err) cudaFreeHost(b->h_err);
     if (b->err_ev) cudaEventDestroy(b->err_ev);
@@ -2867,6 +2885,10 @@ extern "C" int vox_cuda_encoder_step_batch_dev(vox_cuda_enc_state *const *states
     }
     std::vector<std::pair<const void *, int>> key;
     for (int i = 0; i < n; i++) key.push_back({states[i], new_lens[i]});
+    if (b->graphs.size() >= 64 && !b->graphs.count(key)) {   // bound the cache (ragged chunk sizes)
+        VC_TRY(cudaStreamSynchronize(st));
+        drop_batch_graphs(b, nullptr);
+    }
     EncBatch::Graph &g = b->graphs[key];
     if (!g.exec) {
         EncSeg h[kEncMaxSegs];
