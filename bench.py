@@ -440,6 +440,58 @@ def upload_bench(V, torch, layers=4, vocab=VOCAB):
             "host_gbs": host_bytes / min(times) / 1e9, "pageable_copy_gbs": pageable}
 
 
+def single_stream_and_attention(V, torch, dec, steps):
+    """SURVEY configs[1]-[2] beside the batched step: one stream's decode
+    step (M = 1, the reference's own case: per-token latency), and the
+    stand-alone decode attention (vox_cuda_attention_decode_dev) over
+    L = 512 / 2048 / 8192 keys of a ring (the last in a wrapped 8192 + 1024
+    ring), each against its HBM bytes (8192 per key: K + V, 8 heads x 128
+    fp32)."""
+    out = {}
+    stream = torch.cuda.Stream()
+    st = dec.state(kv_cap=8192 + 1024)
+    st.set_position(739)
+    emb = torch.randn((1, D), device="cuda", dtype=torch.float32)
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for _ in range(3):
+        V.step_batch_dev([st], emb.data_ptr(), tok.data_ptr(), stream.cuda_stream)
+    st.set_position(739)
+    torch.cuda.synchronize()
+    n = max(10, steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        V.step_batch_dev([st], emb.data_ptr(), tok.data_ptr(), stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    out["single_stream"] = {"ms_per_token": ms, "tokens_per_s": 1000.0 / ms, "kv_len": 740}
+    st.free()
+    hbm, _ = peaks()
+    cap = 8192 + 1024
+    k = torch.randn((cap, KVD), device="cuda", dtype=torch.float32)
+    v = torch.randn((cap, KVD), device="cuda", dtype=torch.float32)
+    q = torch.randn((QD,), device="cuda", dtype=torch.float32)
+    o = torch.empty((QD,), device="cuda", dtype=torch.float32)
+    att = {}
+    for L, pos in ((512, 511), (2048, 2047), (8192, 5000 + 8192 - 1)):
+        for _ in range(3):
+            V.attention_decode_dev(q.data_ptr(), k.data_ptr(), v.data_ptr(), cap, pos, o.data_ptr(),
+                                   stream.cuda_stream)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(20):
+            V.attention_decode_dev(q.data_ptr(), k.data_ptr(), v.data_ptr(), cap, pos, o.data_ptr(),
+                                   stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / 20 * 1000.0
+        gbs = L * KVD * 4 * 2 / (us / 1e6) / 1e9
+        att[f"L{L}"] = {"us": us, "gbs": gbs, "frac_of_hbm": gbs / hbm}
+    out["attention_one_stream"] = att
+    return out
+
+
 def prefill_bench(V, dec, layers, prompt=38, reps=5):
     """Stream start: the 38-row prompt prefill (voxtral.c:843-891) of one
     stream, and of three streams in shared launches (vox_cuda_decoder_
@@ -641,6 +693,7 @@ def our_arm(args):
     step_bytes = weight_bytes_per_step(args.layers, args.vocab) + kv_bytes
 
     pf_res = prefill_bench(V, dec, args.layers)
+    ss_res = single_stream_and_attention(V, torch, dec, args.steps)
     for st in states:
         st.free()
     dec.free()
@@ -680,6 +733,7 @@ def our_arm(args):
                               "achieved_gbs": step_bytes / (ms_step / 1000.0) / 1e9,
                               "frac": step_bytes / (ms_step / 1000.0) / 1e9 / hbm},
             "prefill": pf_res,
+            "single_stream_decode_and_attention": ss_res,
             "weight_upload": up_res,
             "phase_ms": prof,
             "launch_ms_in_sequence": seq_ms,

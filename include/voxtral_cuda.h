@@ -421,7 +421,9 @@ int vox_cuda_mel_spectrogram(const float *samples, int n_samples, float *mel_out
  * max(0, pos-8191)..pos stored at slot = position mod kv_cap; out [32*128].
  * vox_causal_attention with seq_q = 1 (voxtral_kernels.c:412-482, called at
  * voxtral_decoder.c:481-483).  Scratch for the split-K partials comes from
- * the library's per-device pool. */
+ * the library's per-device pool.  Enqueued on `stream` without a host wait;
+ * calls on different streams are ordered on the device (they share the
+ * scratch). */
 int vox_cuda_attention_decode_dev(const float *q, const float *k_ring, const float *v_ring,
                                   int kv_cap, int pos, float *out, void *stream);
 

@@ -89,6 +89,7 @@ def test_attention_decode_matches_reference(case):
     out = torch.empty(B.Q_DIM, dtype=torch.float32, device="cuda")
     V.check(V.lib().vox_cuda_attention_decode_dev(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), cap,
                                                   pos, out.data_ptr(), None), "attention_decode")
+    torch.cuda.synchronize()   # the call is asynchronous on the library's stream
     assert sampled_rel(out.cpu().numpy(), g, name) < 1e-5
 
 

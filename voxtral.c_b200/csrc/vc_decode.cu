@@ -277,6 +277,13 @@ int attn_ctas_per_head(int M) {
     return g < 16 ? 16 : g;
 }
 
+__global__ void set_slot_kernel(StreamSlot *dst, StreamSlot v) { *dst = v; }
+
+cudaError_t launch_set_slot(StreamSlot *dst, const StreamSlot &v, cudaStream_t st) {
+    set_slot_kernel<<<1, 1, 0, st>>>(dst, v);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

@@ -87,6 +87,8 @@ struct AttnParams {
 constexpr int kAttnSplits = 128;   // >= 8192 / 64 keys per split
 
 cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl);
+// *dst = v in stream order (the descriptor travels as a kernel argument)
+cudaError_t launch_set_slot(StreamSlot *dst, const StreamSlot &v, cudaStream_t st);
 
 // Alternatives from device logits (stream_fill_alts semantics).
 cudaError_t launch_fill_alts(const float *logits, int vocab, const int *best, int n_alt,

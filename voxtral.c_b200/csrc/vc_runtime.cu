@@ -101,6 +101,7 @@ struct DevCtx {
     StreamSlot *attn_slot = nullptr;
     float *attn_part_o = nullptr, *attn_part_ml = nullptr, *rope_tab = nullptr;
     unsigned *attn_counters = nullptr;
+    cudaEvent_t attn_done = nullptr;   // orders the attention scratch across caller streams
 };
 
 DevCtx g_dev[kMaxDevices];
@@ -354,6 +355,8 @@ static void release_scratch(DevCtx *c) {
     cudaFree(c->lin_xfrag);
     cudaFree(c->lin_err);
     if (c->lin_done) cudaEventDestroy(c->lin_done);
+    if (c->attn_done) cudaEventDestroy(c->attn_done);
+    c->attn_done = nullptr;
     c->lin_xfrag = nullptr;
     c->lin_xfrag_bytes = 0;
     c->lin_err = nullptr;
@@ -721,9 +724,12 @@ extern "C" int vox_cuda_attention_decode_dev(const float *q, const float *k_ring
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
     StreamSlot h = {const_cast<float *>(k_ring), const_cast<float *>(v_ring), kv_cap, pos,
                     pos % kv_cap, n_keys, pos};
-    // the slot descriptor is copied through a stream-ordered memcpy so that
-    // back-to-back calls on one stream do not race on it
-    VC_TRY(cudaMemcpyAsync(c->attn_slot, &h, sizeof(h), cudaMemcpyHostToDevice, st));
+    // the scratch is shared: a call on another stream waits for the last one
+    if (!c->attn_done) VC_TRY(cudaEventCreateWithFlags(&c->attn_done, cudaEventDisableTiming));
+    else VC_TRY(cudaStreamWaitEvent(st, c->attn_done, 0));
+    // the slot descriptor travels by value into a stream-ordered write, so
+    // back-to-back calls neither race on it nor wait on the host
+    VC_TRY(launch_set_slot(c->attn_slot, h, st));
     AttnParams p = {};
     p.q = q;
     p.slots = c->attn_slot;
@@ -734,7 +740,7 @@ extern "C" int vox_cuda_attention_decode_dev(const float *q, const float *k_ring
     p.counters = c->attn_counters;
     p.S = kAttnSplits;
     VC_TRY(launch_attn_decode(1, p, st, false));
-    VC_TRY(cudaStreamSynchronize(st));  // h lives on this stack frame
+    VC_TRY(cudaEventRecord(c->attn_done, st));
     return VOX_CUDA_OK;
 }
 

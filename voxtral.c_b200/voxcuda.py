@@ -297,6 +297,12 @@ def states_array(states):
     return (C.c_void_p * len(states))(*[s.h for s in states])
 
 
+def attention_decode_dev(q, k_ring, v_ring, kv_cap, pos, out, stream=None):
+    """Stand-alone decode attention on device addresses."""
+    check(lib().vox_cuda_attention_decode_dev(q, k_ring, v_ring, kv_cap, pos, out, stream),
+          "attention_decode_dev")
+
+
 def prefill_batch(states, rows, rope=None):
     """Prefill several states in shared launches: rows[i] is state i's
     [n_i, 3072] block (n_i may be 0)."""
