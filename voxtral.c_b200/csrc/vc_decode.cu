@@ -6,6 +6,7 @@
 
 #include <math.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 #include <atomic>
@@ -57,6 +58,33 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// The merged output of 4 dimensions (idx .. idx + 3 of row m's 4096) in every
+// form the launch asks for: fp32 rows, the wo GEMV's B fragments, the split
+// bf16 hi / lo rows of a tensor-core consumer.
+__device__ __forceinline__ void attn_store_out(const AttnParams &p, int m, int idx, float o0, float o1, float o2,
+                                               float o3) {
+    if (p.out != nullptr)
+        *reinterpret_cast<float4 *>(p.out + (size_t)m * kQDim + idx) = make_float4(o0, o1, o2, o3);
+    if (p.xfrag_out != nullptr) {
+        xfrag_put2(p.xfrag_out, m, idx, o0, o1);
+        xfrag_put2(p.xfrag_out, m, idx + 2, o2, o3);
+    }
+    if (p.out_hilo != nullptr) {
+        uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
+        split_bf16(o0, h0, l0);
+        split_bf16(o1, h1, l1);
+        split_bf16(o2, h2, l2);
+        split_bf16(o3, h3, l3);
+        const size_t e = (size_t)hilo_row(m) * kQDim + idx;
+        *reinterpret_cast<uint2 *>(p.out_hilo + e) = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
+        *reinterpret_cast<uint2 *>(p.out_hilo + e + (size_t)64 * kQDim) = make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
+    }
+}
 
 // cp.async of the K and V rows of keys [j0, j1) of a split (key j of the
 // split at ring slot (first + kb + j) % cap), 16 bytes per copy.
@@ -242,30 +270,240 @@ attn_decode_kernel(const AttnParams p) {
             go[3] += ov.w * c;
         }
         const float inv = (gd > 0.f) ? 1.0f / gd : 0.f;
-        const float o0 = go[0] * inv, o1 = go[1] * inv, o2 = go[2] * inv, o3 = go[3] * inv;
-        if (p.out != nullptr)
-            *reinterpret_cast<float4 *>(p.out + (size_t)m * kQDim + h * kHeadDim + d4) =
-                make_float4(o0, o1, o2, o3);
-        if (p.xfrag_out != nullptr) {
-            xfrag_put2(p.xfrag_out, m, h * kHeadDim + d4, o0, o1);
-            xfrag_put2(p.xfrag_out, m, h * kHeadDim + d4 + 2, o2, o3);
+        attn_store_out(p, m, h * kHeadDim + d4, go[0] * inv, go[1] * inv, go[2] * inv, go[3] * inv);
+        if (tid == 0) p.counters[m * kDecKvHeads + kvh] = 0u;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// v4: the same attention with 32-key tiles pipelined inside each CTA.
+//
+// A CTA takes a contiguous range of 32-key tiles of one (row, KV head) and
+// runs an online softmax over them: while tile t is computed, tile t + 1 is
+// in flight (cp.async double buffer), so one CTA keeps loading as it
+// computes and a row's keys need fewer CTAs (fewer partials to merge).  K
+// rows are staged chunk-swizzled (16-byte chunk c of key j at c ^ j), so
+// lane j reading its key's chunk c is conflict-free while the query chunk is
+// one broadcast read per warp; each K element is read once per query head.
+// P.V: thread = dimension, V rows coalesced, probabilities broadcast.
+// ---------------------------------------------------------------------------
+
+constexpr int kTileKeys = 32;
+
+struct Attn4Shared {
+    float k[2][kTileKeys][kHeadDim];   // 2 x 16 KB, chunk-swizzled
+    float v[2][kTileKeys][kHeadDim];   // 2 x 16 KB
+    float q[4][kHeadDim];
+    float p[4][kTileKeys];             // this tile's exp(s - m)
+    float alpha[4];                    // this tile's rescale of the running sums
+    int last;
+};
+static_assert(sizeof(float) * 2 * kTileKeys * kHeadDim >= sizeof(float) * 4 * kAttnSplits, "merge weights fit");
+
+// cp.async of keys [j0, j1) of the tile starting at key kb (logical index
+// from `first`) into buffer b: K swizzled, V as is.
+__device__ __forceinline__ void attn4_stage(Attn4Shared &sh, int b, const float *kbase, const float *vbase,
+                                            int first, int kb, int cap, int j0, int j1, int tid) {
+    const int n = (j1 - j0) * (kHeadDim / 4);
+    for (int c = tid; c < n; c += 128) {
+        const int j = j0 + c / (kHeadDim / 4), ch = c % (kHeadDim / 4);
+        const size_t row = (size_t)((first + kb + j) % cap) * kKvDim + 4 * ch;
+        cp_async16(&sh.k[b][j][4 * (ch ^ j)], kbase + row);
+        cp_async16(&sh.v[b][j][4 * ch], vbase + row);
+    }
+}
+
+__global__ void __launch_bounds__(128)
+attn_decode_v4_kernel(const AttnParams p) {
+    extern __shared__ __align__(16) unsigned char attn_smem[];
+    Attn4Shared &sh = *reinterpret_cast<Attn4Shared *>(attn_smem);
+    const int kvh = blockIdx.y, m = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    const StreamSlot slt = p.slots[m];
+    const int n_keys = slt.n_keys;
+    const int tiles = (n_keys + kTileKeys - 1) / kTileKeys;
+    const int P = min((int)gridDim.x, tiles);           // CTAs with keys = partials
+    if ((int)blockIdx.x >= P) return;                   // CTA-uniform, before any barrier
+    const int t0 = (int)((long long)blockIdx.x * tiles / P), t1 = (int)((long long)(blockIdx.x + 1) * tiles / P);
+    const int first = slt.pos - n_keys + 1;
+    const int cap = slt.cap;
+    const float scale = 1.0f / sqrtf((float)kHeadDim);
+    const size_t layer_off = (size_t)p.layer * cap * kKvDim + kvh * kHeadDim;
+    const float *kbase = slt.k_ring + layer_off;
+    const float *vbase = slt.v_ring + layer_off;
+    const int n_old = max(0, min(slt.fresh, slt.pos) - first);   // keys [0, n_old) predate this launch
+    auto tile_keys = [&](int t) { return min(kTileKeys, n_keys - t * kTileKeys); };
+
+    // the old keys of the first two tiles, before the wait (they overlap the
+    // producer kernel's tail)
+    for (int t = t0; t < min(t1, t0 + 2); t++) {
+        const int kb = t * kTileKeys;
+        attn4_stage(sh, t & 1, kbase, vbase, first, kb, cap, 0, max(0, min(tile_keys(t), n_old - kb)), tid);
+    }
+    cp_async_commit();
+    grid_dep_wait();
+    grid_dep_launch();
+    {   // queries (warp = head, lane = 4 dims)
+        const float4 v = *reinterpret_cast<const float4 *>(p.q + (size_t)m * kQDim +
+                                                           (kvh * 4 + warp) * kHeadDim + 4 * lane);
+        *reinterpret_cast<float4 *>(&sh.q[warp][4 * lane]) = v;
+    }
+    for (int t = t0; t < min(t1, t0 + 2); t++) {   // their fresh keys, one group per tile
+        const int kb = t * kTileKeys;
+        attn4_stage(sh, t & 1, kbase, vbase, first, kb, cap, max(0, min(tile_keys(t), n_old - kb)), tile_keys(t),
+                    tid);
+        cp_async_commit();
+    }
+
+    float m_run = -INFINITY, l_run = 0.f;    // warp h: head h's running max / sum
+    float o[4] = {0.f, 0.f, 0.f, 0.f};       // thread = dimension, 4 heads
+    for (int t = t0; t < t1; t++) {
+        const int b = t & 1, nk = tile_keys(t);
+        if (t + 1 < t1) cp_async_wait_group<1>();
+        else cp_async_wait_group<0>();
+        __syncthreads();
+        {   // scores (warp = head, lane = key): swizzled K chunks, broadcast q
+            const int h = warp;
+            const float4 *q4 = reinterpret_cast<const float4 *>(sh.q[h]);
+            const float *kr = sh.k[b][lane];
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll 8
+            for (int c = 0; c < kHeadDim / 4; c += 2) {
+                const float4 k0 = *reinterpret_cast<const float4 *>(kr + 4 * (c ^ lane));
+                const float4 k1 = *reinterpret_cast<const float4 *>(kr + 4 * ((c + 1) ^ lane));
+                const float4 x0 = q4[c], x1 = q4[c + 1];
+                a0 = fmaf(x0.x, k0.x, a0);
+                a0 = fmaf(x0.y, k0.y, a0);
+                a0 = fmaf(x0.z, k0.z, a0);
+                a0 = fmaf(x0.w, k0.w, a0);
+                a1 = fmaf(x1.x, k1.x, a1);
+                a1 = fmaf(x1.y, k1.y, a1);
+                a1 = fmaf(x1.z, k1.z, a1);
+                a1 = fmaf(x1.w, k1.w, a1);
+            }
+            const bool valid = lane < nk;
+            const float sc = valid ? (a0 + a1) * scale : -INFINITY;
+            float tm = sc;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
+            const float nm = fmaxf(m_run, tm);                       // finite: the tile has a valid key
+            const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - nm);
+            const float pj = valid ? expf(sc - nm) : 0.f;
+            l_run = l_run * alpha + warp_sum(pj);
+            m_run = nm;
+            sh.p[h][lane] = pj;
+            if (lane == 0) sh.alpha[h] = alpha;
         }
-        if (p.out_hilo != nullptr) {
-            uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
-            split_bf16(o0, h0, l0);
-            split_bf16(o1, h1, l1);
-            split_bf16(o2, h2, l2);
-            split_bf16(o3, h3, l3);
-            const size_t e = (size_t)hilo_row(m) * kQDim + h * kHeadDim + d4;
-            *reinterpret_cast<uint2 *>(p.out_hilo + e) = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
-            *reinterpret_cast<uint2 *>(p.out_hilo + e + (size_t)64 * kQDim) =
-                make_uint2(l0 | (l1 << 16), l2 | (l3 << 16));
+        __syncthreads();
+        {   // P.V: thread = dimension
+#pragma unroll
+            for (int h = 0; h < 4; h++) o[h] *= sh.alpha[h];
+            for (int j = 0; j < nk; j++) {
+                const float vj = sh.v[b][j][tid];
+#pragma unroll
+                for (int h = 0; h < 4; h++) o[h] = fmaf(sh.p[h][j], vj, o[h]);
+            }
         }
+        __syncthreads();   // buffer b consumed
+        if (t + 2 < t1) {
+            attn4_stage(sh, b, kbase, vbase, first, (t + 2) * kTileKeys, cap, 0, tile_keys(t + 2), tid);
+            cp_async_commit();
+        }
+    }
+    // this CTA's partial: unnormalised o, running (max, sum) per head
+    const int s = blockIdx.x;
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+        const size_t pidx = ((size_t)m * kDecHeads + kvh * 4 + h) * p.S + s;
+        p.part_o[pidx * kHeadDim + tid] = o[h];
+    }
+    if (lane == 0) {
+        const size_t pidx = ((size_t)m * kDecHeads + kvh * 4 + warp) * p.S + s;
+        p.part_ml[pidx * 2] = m_run;
+        p.part_ml[pidx * 2 + 1] = l_run;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sh.last = (atomicAdd(&p.counters[m * kDecKvHeads + kvh], 1u) + 1u == (unsigned)P);
+    __syncthreads();
+    if (!sh.last) return;
+    __threadfence();
+
+    // ---- merge the P partials (last CTA of this row / KV head): warp = head ----
+    {
+        float(*smw)[kAttnSplits] = reinterpret_cast<float(*)[kAttnSplits]>(&sh.k[0][0][0]);
+        const int hh = warp, d4 = 4 * lane;
+        const int h = kvh * 4 + hh;
+        const size_t pbase = ((size_t)m * kDecHeads + h) * p.S;
+        float mloc[kAttnSplits / 32], dloc[kAttnSplits / 32];
+        float gm = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kAttnSplits / 32; i++) {
+            const int t = lane + 32 * i;
+            mloc[i] = (t < P) ? __ldcg(p.part_ml + (pbase + t) * 2) : -INFINITY;
+            dloc[i] = (t < P) ? __ldcg(p.part_ml + (pbase + t) * 2 + 1) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < kAttnSplits / 32; i++)
+            if (dloc[i] > 0.f) gm = fmaxf(gm, mloc[i]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, off));
+        float gd = 0.f;
+#pragma unroll
+        for (int i = 0; i < kAttnSplits / 32; i++) {
+            const int t = lane + 32 * i;
+            const float c = (dloc[i] > 0.f) ? expf(mloc[i] - gm) : 0.f;
+            gd += dloc[i] * c;
+            smw[hh][t] = c;
+        }
+        gd = warp_sum(gd);
+        __syncwarp();
+        float go[4] = {0.f, 0.f, 0.f, 0.f};
+        int t = 0;
+        for (; t + 4 <= P; t += 4) {   // 4 independent loads in flight
+            float4 ov[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                ov[u] = __ldcg(reinterpret_cast<const float4 *>(p.part_o + (pbase + t + u) * kHeadDim + d4));
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float c = smw[hh][t + u];
+                go[0] += ov[u].x * c;
+                go[1] += ov[u].y * c;
+                go[2] += ov[u].z * c;
+                go[3] += ov[u].w * c;
+            }
+        }
+        for (; t < P; t++) {
+            const float4 ov = __ldcg(reinterpret_cast<const float4 *>(p.part_o + (pbase + t) * kHeadDim + d4));
+            const float c = smw[hh][t];
+            go[0] += ov.x * c;
+            go[1] += ov.y * c;
+            go[2] += ov.z * c;
+            go[3] += ov.w * c;
+        }
+        const float inv = (gd > 0.f) ? 1.0f / gd : 0.f;
+        attn_store_out(p, m, h * kHeadDim + d4, go[0] * inv, go[1] * inv, go[2] * inv, go[3] * inv);
         if (tid == 0) p.counters[m * kDecKvHeads + kvh] = 0u;
     }
 }
 
 // CTAs per (stream, KV head): each loops over splits blockIdx.x + G*i.
+// v4: CTAs per (row, KV head).  A long context (8192 keys = 256 tiles) at
+// M = 1 gets 48 CTAs of ~5 pipelined tiles (3 CTAs/SM x 148 SMs over the 8 KV
+// heads); several rows share the SMs, 16 CTAs each at M >= 3.
+int attn4_ctas_per_head(int M) {
+    static int fixed = -1;
+    if (fixed < 0) {   // tuning knob: VOX_CUDA_ATTN_CTAS fixes the CTAs per (stream, KV head)
+        const char *e = getenv("VOX_CUDA_ATTN_CTAS");
+        fixed = (e && atoi(e) >= 1 && atoi(e) <= kAttnSplits) ? atoi(e) : 0;
+    }
+    if (fixed > 0) return fixed;
+    const int g = 48 / (M > 0 ? M : 1);
+    return g < 16 ? 16 : g;
+}
+
 int attn_ctas_per_head(int M) {
     static int fixed = -1;
     if (fixed < 0) {   // tuning knob: VOX_CUDA_ATTN_CTAS fixes the CTAs per (stream, KV head)
@@ -284,32 +522,50 @@ cudaError_t launch_set_slot(StreamSlot *dst, const StreamSlot &v, cudaStream_t s
     return cudaGetLastError();
 }
 
+// Which kernel for a launch of M rows.  Measured on B200: v4's pipelined
+// tiles win for one or two rows (one stream at 740 keys: 1.605 vs 1.641
+// ms/token; 8192 keys: 29.6 vs 39.3 us), v3's one 64-key split per CTA for
+// many rows of short contexts (8 streams at 40..740 keys: 11.5 vs 15.4 us per
+// layer).  VOX_CUDA_ATTN = v3 | v4 forces one (A/B runs).
+static bool attn_use_v3(int M) {
+    static int forced = -1;   // 0 auto, 3, 4
+    if (forced < 0) {
+        const char *e = getenv("VOX_CUDA_ATTN");
+        forced = (e && strcmp(e, "v3") == 0) ? 3 : (e && strcmp(e, "v4") == 0) ? 4 : 0;
+    }
+    return forced == 3 || (forced == 0 && M > 2);
+}
+
 cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    const bool v3 = attn_use_v3(M);
     static std::atomic<uint64_t> attr_set{0};   // the shared-memory opt-in is per device
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_set.load() & bit)) {
         e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)sizeof(AttnShared));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attn_decode_v4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)sizeof(Attn4Shared));
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
     cudaLaunchConfig_t cfg = {};
-    // CTAs per (row, KV head): no more than the splits this launch can have
-    // (a prefill of fresh rows attends to few keys: S = 1)
-    const int g = std::min(attn_ctas_per_head(M), std::max(1, p.S));
+    // CTAs per (row, KV head): no more than the partials this launch's
+    // buffers hold (a prefill of fresh rows attends to few keys: S = 1)
+    const int g = std::min(v3 ? attn_ctas_per_head(M) : attn4_ctas_per_head(M), std::max(1, p.S));
     cfg.gridDim = dim3(g, kDecKvHeads, M);
     cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = sizeof(AttnShared);
+    cfg.dynamicSmemBytes = v3 ? sizeof(AttnShared) : sizeof(Attn4Shared);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel, p);
+    return v3 ? cudaLaunchKernelEx(&cfg, attn_decode_kernel, p) : cudaLaunchKernelEx(&cfg, attn_decode_v4_kernel, p);
 }
 
 // ---------------------------------------------------------------------------
