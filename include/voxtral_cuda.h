@@ -453,6 +453,15 @@ int vox_cuda_attention_decode_noalloc(const float *q, const float *k_ring, const
 int vox_cuda_rope_dev(float *x, int n_heads, int head_dim, int pos, const float *rope_freqs,
                       void *stream);
 
+/* Diagnostics: runs a kernel whose bounded wait (the mbarrier wait with a
+ * %globaltimer deadline that every tensor-core kernel uses) can never
+ * complete, with a deadline of wait_ms.  The kernel raises its error word at
+ * the deadline and returns; the call reports it exactly as a step reports a
+ * timed-out wait: VOX_CUDA_ERR_CUDA with a "timed out" message.  The GPU does
+ * not fault and the context stays usable.  No counterpart in the reference
+ * (it has no device-side waits). */
+int vox_cuda_selftest_wait_timeout(int wait_ms);
+
 /* ------------------------------------------------------------------------
  * Synthetic weights (benchmarks and tests): fill a device bf16 buffer with
  * seeded N(0, std) values, rounded to nearest even.

@@ -385,3 +385,20 @@ def test_prefill_batch_matches_one_state_at_a_time(small_w):
     for st in one + many:
         st.free()
     d.free()
+
+
+def test_bounded_wait_timeout_is_reported_and_context_survives(small_w):
+    """A device-side wait that can never complete (an mbarrier nothing
+    arrives at, the tensor-core kernels' bounded wait) ends at its 50 ms
+    deadline: the call reports a timeout, the GPU does not fault, and the
+    next steps run normally."""
+    rc = V.lib().vox_cuda_selftest_wait_timeout(50)
+    assert rc == V.ERR_CUDA
+    assert "timed out" in V.last_error()
+    d = make_gpu_decoder(small_w)
+    st = d.state(kv_cap=64)
+    st.prefill(B.normal_f32((3, B.DEC_DIM), 31))
+    tok, lg = st.step(B.normal_f32(B.DEC_DIM, 32))
+    assert np.isfinite(lg).all() and 0 <= tok < small_w.vocab
+    st.free()
+    d.free()

@@ -202,6 +202,8 @@ cudaError_t launch_rows_rmsnorm(float *x, int M, int K, const float *w, cudaStre
 // RoPE planes of a batched encoder launch: each row's position from its segment
 cudaError_t launch_enc_rope_table_segs(float *tab, int ld, int M, const EncSeg *segs, int n_segs,
                                        const float *inv_freq, cudaStream_t st, bool pdl);
+// A kernel whose bounded wait cannot complete: raises *err after wait_ns.
+cudaError_t launch_stuck_wait(unsigned *err, unsigned long long wait_ns, cudaStream_t st);
 // *dst = v in stream order (the value travels as a kernel argument)
 cudaError_t launch_set_int(int *dst, int v, cudaStream_t st);
 // RoPE planes of a chunk for the q|k epilogue: tab[d][row] = cos and

@@ -768,6 +768,36 @@ extern "C" int vox_cuda_rope_dev(float *x, int n_heads, int head_dim, int pos,
     return VOX_CUDA_OK;
 }
 
+extern "C" int vox_cuda_selftest_wait_timeout(int wait_ms) {
+    if (wait_ms <= 0 || wait_ms > 10000) {
+        set_error("selftest_wait_timeout: wait_ms must be 1..10000");
+        return VOX_CUDA_ERR_ARG;
+    }
+    DevCtx *c = cur_ctx();
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    unsigned *err = nullptr;
+    unsigned h = 0;
+    if (dev_alloc(c, (void **)&err, sizeof(unsigned)) != cudaSuccess) {
+        set_error("selftest_wait_timeout: allocation failed");
+        return VOX_CUDA_ERR_OOM;
+    }
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(unsigned), c->stream);
+    if (e == cudaSuccess) e = launch_stuck_wait(err, (unsigned long long)wait_ms * 1000000ull, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h, err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    dev_free(c, err, sizeof(unsigned));
+    if (e != cudaSuccess) {
+        set_error("selftest_wait_timeout: %s", cudaGetErrorString(e));
+        return VOX_CUDA_ERR_CUDA;
+    }
+    if (h) {   // the expected outcome, reported as every kernel's timeout is
+        set_error("selftest: a device-side wait timed out after %d ms (results discarded)", wait_ms);
+        return VOX_CUDA_ERR_CUDA;
+    }
+    set_error("selftest_wait_timeout: the wait did not time out");
+    return VOX_CUDA_OK;
+}
+
 extern "C" int vox_cuda_fill_normal_bf16_dev(uint16_t *dst, size_t n, uint64_t seed, float std,
                                              void *stream) {
     if (!dst) {

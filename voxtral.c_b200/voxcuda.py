@@ -124,6 +124,7 @@ def lib():
         "vox_cuda_conv_stem_reset": ([C.c_void_p], C.c_int),
         "vox_cuda_conv_stem_step": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
         "vox_cuda_conv_stem_step_dev": ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
+        "vox_cuda_selftest_wait_timeout": ([C.c_int], C.c_int),
         "vox_cuda_mel_create": ([C.c_int, C.c_int], C.c_void_p),
         "vox_cuda_mel_free": ([C.c_void_p], None),
         "vox_cuda_mel_frames": ([C.c_void_p], C.c_int),
