@@ -467,6 +467,15 @@ def single_stream_and_attention(V, torch, dec, steps):
     ms = e0.elapsed_time(e1) / n
     out["single_stream"] = {"ms_per_token": ms, "tokens_per_s": 1000.0 / ms, "kv_len": 740}
     st.free()
+    out["attention_one_stream"] = attention_bench(V, torch)
+    return out
+
+
+def attention_bench(V, torch):
+    """The stand-alone decode attention (vox_cuda_attention_decode_dev) over
+    L = 512 / 2048 / 8192 keys, the last in a wrapped 8192 + 1024 ring."""
+    stream = torch.cuda.Stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     hbm, _ = peaks()
     cap = 8192 + 1024
     k = torch.randn((cap, KVD), device="cuda", dtype=torch.float32)
@@ -488,8 +497,7 @@ def single_stream_and_attention(V, torch, dec, steps):
         us = e0.elapsed_time(e1) / 20 * 1000.0
         gbs = L * KVD * 4 * 2 / (us / 1e6) / 1e9
         att[f"L{L}"] = {"us": us, "gbs": gbs, "frac_of_hbm": gbs / hbm}
-    out["attention_one_stream"] = att
-    return out
+    return att
 
 
 def prefill_bench(V, dec, layers, prompt=38, reps=5):
@@ -601,6 +609,14 @@ def our_arm(args):
                                 device_id=torch.device("cuda", local))
     import voxcuda as V
     V.init(local)
+    if args.attention_only:   # the stand-alone decode attention (profiling captures)
+        res = attention_bench(V, torch)
+        if rank == 0:
+            print(json.dumps({"attention_one_stream": res}), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.prefill_only:   # the prompt prefill alone (profiling captures)
         dec = build_device_decoder(V, torch, layers=args.layers, vocab=args.vocab)
         res = prefill_bench(V, dec, args.layers)
@@ -759,6 +775,7 @@ def main():
     # encoder-only / single chunk size, for small ncu captures
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--prefill-only", action="store_true")
+    ap.add_argument("--attention-only", action="store_true")
     ap.add_argument("--enc-rows", type=int, default=0)
     # reduced model, for small ncu captures only (the headline uses the full model)
     ap.add_argument("--layers", type=int, default=LAYERS)
