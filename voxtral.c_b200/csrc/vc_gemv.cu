@@ -371,12 +371,25 @@ gemv_tma_kernel(const GemvParams p) {
             if (sh.s_last) {
                 __threadfence();
                 if (warp < M) {
+                    // 2048 partials at the 4B vocabulary: 8 loads in flight per
+                    // lane (one 8-byte (value, index) load each), not one
                     float b = -INFINITY;
                     int ib = 0x7fffffff;
-                    for (int j = lane; j < (int)gridDim.y; j += 32) {
-                        const float v = __ldcg(&p.partials[(size_t)j * M + warp].v);
-                        const int i = __ldcg(&p.partials[(size_t)j * M + warp].i);
-                        if (arg_better(v, i, b, ib)) { b = v; ib = i; }
+                    const int G = (int)gridDim.y;
+                    const int2 *pp = reinterpret_cast<const int2 *>(p.partials);
+                    for (int j0 = lane; j0 < G; j0 += 32 * 8) {
+                        int2 t[8];
+#pragma unroll
+                        for (int u = 0; u < 8; u++) {
+                            const int j = j0 + 32 * u;
+                            t[u] = j < G ? __ldcg(pp + (size_t)j * M + warp) : make_int2(__float_as_int(-INFINITY),
+                                                                                          0x7fffffff);
+                        }
+#pragma unroll
+                        for (int u = 0; u < 8; u++) {
+                            const float v = __int_as_float(t[u].x);
+                            if (arg_better(v, t[u].y, b, ib)) { b = v; ib = t[u].y; }
+                        }
                     }
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) {

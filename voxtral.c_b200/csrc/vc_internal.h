@@ -28,10 +28,11 @@ enum GemvEpi : int {
     EPI_LOGITS = 4,   // y = acc, plus argmax across the whole launch
 };
 
-struct ArgmaxPartial {
+struct alignas(8) ArgmaxPartial {   // read back as one 8-byte load
     float v;
     int i;
 };
+static_assert(sizeof(ArgmaxPartial) == 8, "(value, index) pairs are 8 bytes");
 
 struct GemvParams {
     const uint16_t *W;      // fragment-tiled weights (launch_tile_weights), [Np, Kp]
