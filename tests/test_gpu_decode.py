@@ -402,3 +402,33 @@ def test_bounded_wait_timeout_is_reported_and_context_survives(small_w):
     assert np.isfinite(lg).all() and 0 <= tok < small_w.vocab
     st.free()
     d.free()
+
+
+def test_tc_prefill_across_the_ring_wrap(small_w, monkeypatch):
+    """Prefill rows whose ring slots wrap (positions 8392..8491 in a ring of
+    8192 + 256, a full 8192-key window behind each row): the tensor-core
+    prefill against the decode-kernel prefill, K / V of the new rows and
+    the next step's logits."""
+    a = make_gpu_decoder(small_w)
+    monkeypatch.setenv("VOX_CUDA_DEC_TC_PREFILL", "0")
+    b = make_gpu_decoder(small_w)
+    monkeypatch.delenv("VOX_CUDA_DEC_TC_PREFILL")
+    cap, p0, n = 8192 + 256, 8192 + 200, 100
+    sa, sb = a.state(kv_cap=cap), b.state(kv_cap=cap)
+    sa.set_position(p0)
+    sb.set_position(p0)
+    prompt = B.normal_f32((n, B.DEC_DIM), 1410)
+    sa.prefill(prompt)
+    sb.prefill(prompt)
+    for layer in (0, small_w.n_layers - 1):
+        ka, va = sa.read_kv(layer, p0, n)
+        kb, vb = sb.read_kv(layer, p0, n)
+        assert B.rel_l2(ka, kb) < PREFILL_TOL and B.rel_l2(va, vb) < PREFILL_TOL, layer
+    e = B.normal_f32(B.DEC_DIM, 1411)
+    _, la = sa.step(e)
+    _, lb = sb.step(e)
+    assert B.rel_l2(la, lb) < PREFILL_TOL
+    sa.free()
+    sb.free()
+    a.free()
+    b.free()

@@ -251,3 +251,26 @@ def test_encoder_batched_launch_matches_per_state_steps():
         a.free()
         b.free()
     e.free()
+
+
+def test_encoder_ring_wraps_match_oracle():
+    """Chunks of 1..64 rows until the positions pass twice the ring's
+    capacity (max_chunk 64: 896 slots), so the fp16 ring wraps twice, q|k|v
+    rows land across the wrap and attention key blocks follow it; against
+    the oracle's compacting cache (the reference's keep-the-last-750 rule)."""
+    ew = B.EncoderWeights(seed=21, n_layers=1, distinct=1, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    st = e.state(max_chunk=64)
+    o = B.OracleEncoder(ew, kv_max=1024)
+    rng = np.random.default_rng(3)
+    pos, i = 0, 0
+    while pos < 2 * 896 + 100:
+        n = int(rng.integers(1, 65))
+        x = B.normal_f32((n, B.ENC_DIM), 1300 + i)
+        yo, yg = o.step(x), st.step(x)
+        assert B.rel_l2(yg, yo) < 5e-3, (i, pos, n, B.rel_l2(yg, yo))
+        pos += n
+        i += 1
+    assert st.position == pos
+    st.free()
+    e.free()
