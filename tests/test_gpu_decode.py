@@ -302,6 +302,32 @@ def test_async_batched_steps_match_sync_batched_steps(small_w):
     d.free()
 
 
+def test_l2_weight_prefetch_changes_no_result(small_w, monkeypatch):
+    """Each decode kernel starts pulling the next kernel's weights into L2
+    (cp.async.bulk.prefetch.L2, budgets VOX_CUDA_L2PF_MB / _ATTN_MB): single
+    and batched steps give bit-identical logits and tokens with the prefetch
+    off, at the default budgets, and with budgets above a matrix's size."""
+    n = 3
+    prompts = [B.normal_f32((5 + i, B.DEC_DIM), 820 + i) for i in range(n)]
+    embeds = [B.normal_f32((n, B.DEC_DIM), 830 + s) for s in range(3)]
+    runs = {}
+    for mb, attn in (("0", "0"), ("", ""), ("4096", "4096")):
+        monkeypatch.setenv("VOX_CUDA_L2PF_MB", mb)
+        monkeypatch.setenv("VOX_CUDA_L2PF_ATTN_MB", attn)
+        d = make_gpu_decoder(small_w)
+        states = [d.state(kv_cap=64) for _ in range(n)]
+        for st, p in zip(states, prompts):
+            st.prefill(p)
+        out = [V.step_batch(states, e) for e in embeds]
+        out += [states[0].step(e[0])[1] for e in embeds]
+        runs[mb] = out
+        for st in states:
+            st.free()
+        d.free()
+    for a, b, c in zip(runs["0"], runs[""], runs["4096"]):
+        assert np.array_equal(a, b) and np.array_equal(a, c)
+
+
 def test_profile_sequence_times_every_phase(small_w):
     """vox_cuda_decoder_profile_sequence: each phase's launches replayed back
     to back give a positive per-launch time; positions do not advance."""

@@ -85,6 +85,24 @@ __device__ __forceinline__ void grid_dep_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// This CTA's share of an L2 prefetch of [base, base + bytes): the weights of
+// a later kernel in the stream, which depend on nothing this kernel writes.
+// One thread per CTA calls it; the bulk prefetches (<= 64 KB each, shares of
+// whole 4 KB pages) complete on their own.  base and bytes: multiples of 16.
+__device__ __forceinline__ void l2_prefetch_share(const void *base, unsigned long long bytes) {
+    if (!base || bytes == 0) return;
+    const unsigned long long nb = (unsigned long long)gridDim.x * gridDim.y * gridDim.z;
+    const unsigned long long b =
+        blockIdx.x + (unsigned long long)gridDim.x * (blockIdx.y + (unsigned long long)gridDim.y * blockIdx.z);
+    const unsigned long long share = ((bytes + nb - 1) / nb + 4095ull) & ~4095ull;
+    const unsigned long long end = min((b + 1) * share, bytes);
+    const char *p = static_cast<const char *>(base);
+    for (unsigned long long off = b * share; off < end; off += 65536ull) {
+        const unsigned n = (unsigned)min(65536ull, end - off);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"(n) : "memory");
+    }
+}
+
 // ---------------------------------------------------------------------------
 // B-fragment ("xfrag") writers for the decode GEMV's activations: per 16-wide
 // k-block, lane 4m + q holds stream m's values at k = 2q, 2q+1 (word 0) and

@@ -105,6 +105,7 @@ attn_decode_kernel(const AttnParams p) {
     AttnShared &sh = *reinterpret_cast<AttnShared *>(attn_smem);
     const int kvh = blockIdx.y, m = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) l2_prefetch_share(p.pf, p.pf_bytes);   // the wo GEMV's weights (this kernel leaves HBM idle)
 
     // The slots were written before this step's first kernel; ring rows of
     // positions below slt.pos were written by earlier steps.
@@ -319,6 +320,7 @@ attn_decode_v4_kernel(const AttnParams p) {
     Attn4Shared &sh = *reinterpret_cast<Attn4Shared *>(attn_smem);
     const int kvh = blockIdx.y, m = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) l2_prefetch_share(p.pf, p.pf_bytes);   // the wo GEMV's weights (this kernel leaves HBM idle)
 
     const StreamSlot slt = p.slots[m];
     const int n_keys = slt.n_keys;

@@ -172,6 +172,10 @@ gemv_tma_kernel(const GemvParams p) {
             bulk_g2s(sh.stage[it], wsrc + (size_t)it * kStageKB * kRT * 256, (uint32_t)n * kRT * 512,
                      &sh.full[it], pol);
         }
+        // the first bytes of the next weight stream, behind this CTA's own
+        // first stages: HBM stays busy through this launch's reduction tail
+        // and the next one's ramp
+        l2_prefetch_share(p.pf, p.pf_bytes);
     }
     grid_dep_wait();
     grid_dep_launch();

@@ -56,6 +56,9 @@ struct GemvParams {
     ArgmaxPartial *partials;  // [gridDim.x * M]
     unsigned *counter;        // 1 counter, zero between launches
     int *tokens;              // [M]
+    // weights of a later kernel to start pulling into L2 (or NULL)
+    const void *pf;
+    unsigned long long pf_bytes;   // a multiple of 16
 };
 
 // Launch the fused streaming GEMV (M = 1..8 activation rows).
@@ -84,6 +87,8 @@ struct AttnParams {
     float *part_ml;           // [M][32][S][2]
     unsigned *counters;       // [M][8], zero between launches
     int S;                    // key splits per KV head
+    const void *pf;           // weights of a later kernel to start pulling into L2 (or NULL)
+    unsigned long long pf_bytes;   // a multiple of 16
 };
 constexpr int kAttnSplits = 128;   // >= 8192 / 64 keys per split
 
