@@ -3,10 +3,12 @@
 // voxtral_kernels.c:412-482 as called at voxtral_encoder.c:574-576).
 //
 // One CTA = 128 query rows of one head (TMEM lane = query row), 192 threads,
-// three CTAs per SM (64 KB shared memory, 128 TMEM columns, <= 112 registers)
+// three CTAs per SM (72 KB shared memory, 128 TMEM columns, <= 112 registers)
 // so that a 1500-row chunk's 12 x 32 tiles run in one wave:
 //   warp 0 (one thread)  TMA: the Q tile once, then 64-key blocks of K and V
-//                        from the fp16 ring into a double-buffered ring
+//                        from the fp16 ring: K into a 3-deep ring (a slot is
+//                        free once its S MMA completes), V into a 2-deep one
+//                        (free once its P.V MMA completes)
 //   warp 1 (one thread)  MMAs: S_b = Q K_b^T (M 128, N 64, K 64) into TMEM
 //                        columns [0,64); O += P_b V_b (M 128, N 64, K 64, V
 //                        an MN-major operand) accumulating in columns [64,128)
@@ -17,9 +19,11 @@
 //                        O / l as fp16 (or bf16) for the wo GEMM
 // The running max m of a row moves only when a block's max exceeds it by more
 // than 2^8 (P stays <= 256, exact enough in fp16 and fp32); then the thread
-// rescales its O row in TMEM (tcgen05.ld / st) and its sum before writing
-// P_b.  Once P_b is in shared memory the MMA warp issues S_{b+1} and then
-// O += P_b V_b; the softmax takes the max of S_{b+1} before it waits for that
+// rescales its O row in TMEM (tcgen05.ld / st) and its sum after writing
+// P_b.  As soon as the softmax warps have read S_b into registers the MMA
+// warp issues S_{b+1} (S has one TMEM buffer), so that MMA overlaps the
+// exponentials of block b; once P_b is in shared memory it issues
+// O += P_b V_b.  The softmax takes the max of S_{b+1} before it waits for that
 // O MMA (whose completion also frees P).  Key blocks start at multiples of 64
 // positions and the ring capacity is a multiple of 128, so a block never
 // wraps in the ring.  Every mbarrier wait is bounded (2 s of %globaltimer);
@@ -45,14 +49,17 @@ constexpr int kFaThreads = 192;
 constexpr int kFaTmemCols = 128;  // S [0,64), O [64,128)
 constexpr uint64_t kFaWaitNs = 2000000000ull;
 constexpr float kFaRescale = 8.0f;   // log2 of the largest P before the max moves
+constexpr int kFaKStages = 3;        // K ring depth
+constexpr int kFaVStages = 2;        // V ring depth
 
 struct FaSmem {
-    unsigned char q[kFaRows * 128];        // Q [128 rows][64 dims] fp16, 128-byte swizzle
-    unsigned char k[2][kFaKeys * 128];     // K blocks [64 keys][64 dims]
-    unsigned char v[2][kFaKeys * 128];     // V blocks [64 keys][64 dims] (MN-major B of P.V)
-    unsigned char p[kFaRows * 128];        // P [128 rows][64 keys], K-major
-    uint64_t q_full, s_full, p_full, o_full;
-    uint64_t kv_full[2], kv_empty[2];
+    unsigned char q[kFaRows * 128];                // Q [128 rows][64 dims] fp16, 128-byte swizzle
+    unsigned char k[kFaKStages][kFaKeys * 128];    // K blocks [64 keys][64 dims]
+    unsigned char v[kFaVStages][kFaKeys * 128];    // V blocks [64 keys][64 dims] (MN-major B of P.V)
+    unsigned char p[kFaRows * 128];                // P [128 rows][64 keys], K-major
+    uint64_t q_full, s_full, s_free, p_full, o_full;
+    uint64_t k_full[kFaKStages], k_empty[kFaKStages];
+    uint64_t v_full[kFaVStages], v_empty[kFaVStages];
     uint32_t tmem;
 };
 
@@ -101,11 +108,16 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (threadIdx.x == 0) {
         mbar_init(&sh.q_full, 1);
         mbar_init(&sh.s_full, 1);
-        mbar_init(&sh.p_full, 4);   // one arrival per softmax warp
+        mbar_init(&sh.s_free, 4);   // one arrival per softmax warp
+        mbar_init(&sh.p_full, 4);
         mbar_init(&sh.o_full, 1);
-        for (int i = 0; i < 2; i++) {
-            mbar_init(&sh.kv_full[i], 1);
-            mbar_init(&sh.kv_empty[i], 1);
+        for (int i = 0; i < kFaKStages; i++) {
+            mbar_init(&sh.k_full[i], 1);
+            mbar_init(&sh.k_empty[i], 1);
+        }
+        for (int i = 0; i < kFaVStages; i++) {
+            mbar_init(&sh.v_full[i], 1);
+            mbar_init(&sh.v_empty[i], 1);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         prefetch_tensormap(&tmQ);
@@ -140,60 +152,77 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             mbar_expect_tx(&sh.q_full, kFaRows * 128);
             tma_load_2d(sh.q, &tmQ, head * kEncHeadDim, r0, &sh.q_full, pol);
             for (int b = 0; b < nb; b++) {
-                const int buf = b & 1;
-                if (b >= 2 && !mbar_wait(&sh.kv_empty[buf], ((b >> 1) + 1) & 1u, deadline)) {
+                const int kbuf = b % kFaKStages, vbuf = b % kFaVStages;
+                const int slot = (kstart + b * kFaKeys) % p.cap;
+                if (b >= kFaKStages &&
+                    !mbar_wait(&sh.k_empty[kbuf], ((b / kFaKStages) + 1) & 1u, deadline)) {
                     ok = false;
                     break;
                 }
-                const int slot = (kstart + b * kFaKeys) % p.cap;
-                mbar_expect_tx(&sh.kv_full[buf], 2 * kFaKeys * 128);
-                tma_load_2d(sh.k[buf], &tmK, head * kEncHeadDim, slot, &sh.kv_full[buf], pol);
-                tma_load_2d(sh.v[buf], &tmV, head * kEncHeadDim, slot, &sh.kv_full[buf], pol);
+                mbar_expect_tx(&sh.k_full[kbuf], kFaKeys * 128);
+                tma_load_2d(sh.k[kbuf], &tmK, head * kEncHeadDim, slot, &sh.k_full[kbuf], pol);
+                if (b >= kFaVStages &&
+                    !mbar_wait(&sh.v_empty[vbuf], ((b / kFaVStages) + 1) & 1u, deadline)) {
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(&sh.v_full[vbuf], kFaKeys * 128);
+                tma_load_2d(sh.v[vbuf], &tmV, head * kEncHeadDim, slot, &sh.v_full[vbuf], pol);
             }
-            // tail: the last releases of both buffers have arrived
-            for (int b = nb > 2 ? nb - 2 : 0; b < nb && ok; b++)
-                ok = mbar_wait(&sh.kv_empty[b & 1], (b >> 1) & 1u, deadline);
+            // tail: the last releases of every buffer have arrived
+            for (int b = nb > kFaKStages ? nb - kFaKStages : 0; b < nb && ok; b++)
+                ok = mbar_wait(&sh.k_empty[b % kFaKStages], (b / kFaKStages) & 1u, deadline);
+            for (int b = nb > kFaVStages ? nb - kFaVStages : 0; b < nb && ok; b++)
+                ok = mbar_wait(&sh.v_empty[b % kFaVStages], (b / kFaVStages) & 1u, deadline);
         }
     } else if (warp == 1) {
-        // MMA issue order: S_0; then per block b, once P_b is in shared memory:
-        // S_{b+1} (the softmax already read S_b), then O += P_b V_b.
+        // MMA issue order: S_0; then per block b: S_{b+1} once the softmax
+        // has read S_b (and K_{b+1} is in), then O += P_b V_b once P_b is in
+        // shared memory (and V_b is in).
         if (lane == 0) {
             constexpr uint32_t id_s = idesc_f16(kFaRows, kFaKeys, false);
             constexpr uint32_t id_o = idesc_f16(kFaRows, kEncHeadDim, true);
-            auto issue_s = [&](int b) {
-                const uint64_t a0 = smem_desc_sw128(sh.q), b0 = smem_desc_sw128(sh.k[b & 1]);
+            auto issue_s = [&](int b) -> bool {
+                const int kbuf = b % kFaKStages;
+                if (!mbar_wait(&sh.k_full[kbuf], (b / kFaKStages) & 1u, deadline)) return false;
+                tc_fence_after();
+                const uint64_t a0 = smem_desc_sw128(sh.q), b0 = smem_desc_sw128(sh.k[kbuf]);
 #pragma unroll
                 for (int k = 0; k < kEncHeadDim / 16; k++)   // +32 bytes per K=16 step
                     tc_mma_f16(tmem, a0 + 2 * k, b0 + 2 * k, id_s, k != 0 ? 1u : 0u);
                 tc_commit(&sh.s_full);
+                tc_commit(&sh.k_empty[kbuf]);
+                return true;
             };
-            ok = mbar_wait(&sh.q_full, 0u, deadline) && mbar_wait(&sh.kv_full[0], 0u, deadline);
-            if (ok) {
-                tc_fence_after();
-                issue_s(0);
-            }
+            ok = mbar_wait(&sh.q_full, 0u, deadline) && issue_s(0);
             for (int b = 0; b < nb && ok; b++) {
-                if (!mbar_wait(&sh.p_full, b & 1u, deadline)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
                 if (b + 1 < nb) {
-                    if (!mbar_wait(&sh.kv_full[(b + 1) & 1], ((b + 1) >> 1) & 1u, deadline)) {
+                    // S is one TMEM buffer: S_{b+1} after the softmax's read of S_b
+                    if (!mbar_wait(&sh.s_free, b & 1u, deadline)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    issue_s(b + 1);
+                    if (!issue_s(b + 1)) {
+                        ok = false;
+                        break;
+                    }
                 }
+                const int vbuf = b % kFaVStages;
+                if (!mbar_wait(&sh.p_full, b & 1u, deadline) ||
+                    !mbar_wait(&sh.v_full[vbuf], (b / kFaVStages) & 1u, deadline)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
                 const uint64_t a0 = smem_desc_sw128(sh.p);
 #pragma unroll
                 for (int t = 0; t < kFaKeys / 16; t++) {   // 4 steps of 16 keys
-                    const uint64_t bv = smem_desc_sw128_mn(sh.v[b & 1] + t * 16 * 128);
+                    const uint64_t bv = smem_desc_sw128_mn(sh.v[vbuf] + t * 16 * 128);
                     tc_mma_f16(tmem + kFaKeys, a0 + 2 * t, bv, id_o, (b | t) != 0 ? 1u : 0u);
                 }
                 tc_commit(&sh.o_full);
-                tc_commit(&sh.kv_empty[b & 1]);
+                tc_commit(&sh.v_empty[vbuf]);
             }
         }
     } else {
@@ -214,6 +243,10 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             float sa[32], sb[32];   // S_b columns 0-31 and 32-63
             tmem_ld32(tl, sa);
             tmem_ld32(tl + 32u, sb);
+            // S_b is in registers: the MMA warp may overwrite S with S_{b+1}
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.s_free);
 #define SV(j) ((j) < 32 ? sa[(j) & 31] : sb[(j) & 31])
             const int kb0 = kstart + b * kFaKeys;
             // every key of the block inside every valid row's window: no mask;
