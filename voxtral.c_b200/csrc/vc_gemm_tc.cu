@@ -455,29 +455,30 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams &p, const EpiMa
     }
 }
 
-// Split-K: one warp's 32 rows x BN/2 columns of slice ks -> the fp32
-// workspace ws[ks][rows][N] (rows / columns past rows / N are not written;
-// rows = M, or the A rows of the split-activation layout).
+// Split-K workspace: one region of 32 rows x BN/2 columns per (slice ks,
+// tile t, epilogue warp), the warp's TMEM lane quarter q and column half.
+// Inside a region, column chunk cc (32 columns) holds 8 float4 groups, each
+// with the 32 lanes' float4s side by side: every warp-wide store or load
+// covers 512 consecutive bytes.  All rows and chunks below N are written
+// (rows past M hold the products of zero-filled A rows and are never used).
+__device__ __forceinline__ size_t split_region(int ks, int t, int tiles, int q, int half, int bn) {
+    return (((size_t)ks * tiles + t) * kEpiWarps + half * 4 + q) * (size_t)(16 * bn);
+}
+
+// Split-K: one warp's 32 rows x BN/2 columns of slice ks -> its region.
 template <int BN>
-__device__ __forceinline__ void split_partial(const TcGemmParams &p, uint32_t tbase, int row0, int n0, int half,
-                                              int lane, int ks, int rows) {
-    const int row = row0 + lane;
-    float *dst = p.ws + ((size_t)ks * rows + row) * p.N;
+__device__ __forceinline__ void split_partial(const TcGemmParams &p, uint32_t tbase, int q, int n0, int half,
+                                              int lane, int ks, int t, int tiles) {
+    float4 *dst = reinterpret_cast<float4 *>(p.ws + split_region(ks, t, tiles, q, half, BN)) + lane;
 #pragma unroll 1
     for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
         float v[kEpiCols];
-        tmem_ld32(tbase + (uint32_t)c, v);
-        const int col0 = n0 + c;
-        if (row >= rows || col0 >= p.N) continue;
-        if (col0 + kEpiCols <= p.N && (p.N & 3) == 0) {
+        tmem_ld32(tbase + (uint32_t)c, v);   // warp-collective: before any branch
+        if (n0 + c >= p.N) continue;          // warp-uniform
+        float4 *d = dst + (size_t)((c - half * (BN / 2)) / kEpiCols) * (kEpiCols / 4) * 32;
 #pragma unroll
-            for (int j = 0; j < kEpiCols; j += 4)
-                __stcg(reinterpret_cast<float4 *>(dst + col0 + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-        } else {
-#pragma unroll
-            for (int j = 0; j < kEpiCols; j++)
-                if (col0 + j < p.N) __stcg(dst + col0 + j, v[j]);
-        }
+        for (int j = 0; j < kEpiCols / 4; j++)
+            __stcg(d + 32 * j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
     }
 }
 
@@ -485,10 +486,11 @@ __device__ __forceinline__ void split_partial(const TcGemmParams &p, uint32_t tb
 // whichever slice finished last) and run the epilogue on it.
 template <int BN, int EPI>
 __device__ __forceinline__ void split_finish(const TcGemmParams &p, const EpiMaps &mp, int row0, int n0, int half,
-                                             int lane, unsigned char *stg, int KS) {
+                                             int lane, unsigned char *stg, int KS, int q, int t, int tiles) {
     const EpiRow er = epi_row<EPI>(p, row0 + lane);
     const bool rv = er.row < p.M;
-    const size_t slice = (size_t)p.M * p.N;
+    const size_t slice = (size_t)tiles * kEpiWarps * 16 * BN;   // floats between slices
+    const float4 *src0 = reinterpret_cast<const float4 *>(p.ws + split_region(0, t, tiles, q, half, BN)) + lane;
 #pragma unroll 1
     for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
         const int col0 = n0 + c;
@@ -497,32 +499,24 @@ __device__ __forceinline__ void split_finish(const TcGemmParams &p, const EpiMap
 #pragma unroll
         for (int j = 0; j < kEpiCols; j++) v[j] = 0.f;
         if (rv) {
-            const float *src = p.ws + (size_t)er.row * p.N + col0;
-            if (col0 + kEpiCols <= p.N && (p.N & 3) == 0) {
-                // two slices in flight: the loads of slice s+1 are issued
-                // before the adds of slice s (the adds stay in slice order)
-                float4 cur[kEpiCols / 4], nxt[kEpiCols / 4];
+            const float4 *src = src0 + (size_t)((c - half * (BN / 2)) / kEpiCols) * (kEpiCols / 4) * 32;
+            // two slices in flight: the loads of slice s+1 are issued before
+            // the adds of slice s (the adds stay in slice order)
+            float4 cur[kEpiCols / 4], nxt[kEpiCols / 4];
 #pragma unroll
-                for (int j = 0; j < kEpiCols / 4; j++) cur[j] = __ldcg(reinterpret_cast<const float4 *>(src) + j);
-                for (int s = 0; s < KS; s++) {
-                    if (s + 1 < KS) {
-                        const float4 *nsrc = reinterpret_cast<const float4 *>(src + (size_t)(s + 1) * slice);
+            for (int j = 0; j < kEpiCols / 4; j++) cur[j] = __ldcg(src + 32 * j);
+            for (int s = 0; s < KS; s++) {
+                if (s + 1 < KS) {
+                    const float4 *nsrc = src + (size_t)(s + 1) * (slice / 4);
 #pragma unroll
-                        for (int j = 0; j < kEpiCols / 4; j++) nxt[j] = __ldcg(nsrc + j);
-                    }
-#pragma unroll
-                    for (int j = 0; j < kEpiCols / 4; j++)
-                        v[4 * j] += cur[j].x, v[4 * j + 1] += cur[j].y, v[4 * j + 2] += cur[j].z,
-                            v[4 * j + 3] += cur[j].w;
-#pragma unroll
-                    for (int j = 0; j < kEpiCols / 4; j++) cur[j] = nxt[j];
+                    for (int j = 0; j < kEpiCols / 4; j++) nxt[j] = __ldcg(nsrc + 32 * j);
                 }
-            } else {
-                for (int s = 0; s < KS; s++, src += slice) {
 #pragma unroll
-                    for (int j = 0; j < kEpiCols; j++)
-                        if (col0 + j < p.N) v[j] += __ldcg(src + j);
-                }
+                for (int j = 0; j < kEpiCols / 4; j++)
+                    v[4 * j] += cur[j].x, v[4 * j + 1] += cur[j].y, v[4 * j + 2] += cur[j].z,
+                        v[4 * j + 3] += cur[j].w;
+#pragma unroll
+                for (int j = 0; j < kEpiCols / 4; j++) cur[j] = nxt[j];
             }
         }
         if (p.tma_out) {
@@ -614,36 +608,33 @@ __device__ __forceinline__ bool epilogue_pair(const TcGemmParams &p, uint32_t tb
 }
 
 // Split-K finish of one pair's 32 output rows x BN/2 columns: the slices of
-// the hi and the lo accumulator rows summed in slice order.
+// the hi (lane quarter qq) and the lo (quarter qq + 2) accumulator rows
+// summed in slice order.
 template <int BN, int EPI>
 __device__ __forceinline__ void split_finish_pair(const TcGemmParams &p, int tm, int qq, int n0, int half, int lane,
-                                                  int KS) {
+                                                  int KS, int t, int tiles) {
     const EpiRow er = epi_row<EPI>(p, tm * 64 + 32 * qq + lane);
     if (er.row >= p.M) return;
-    const int rows = hilo_rows(p.M);
-    const size_t slice = (size_t)rows * p.N;
-    const float *src = p.ws + (size_t)(tm * kBM + 32 * qq + lane) * p.N;
+    const size_t slice = (size_t)tiles * kEpiWarps * 16 * BN / 4;   // float4s between slices
+    const float4 *hi0 = reinterpret_cast<const float4 *>(p.ws + split_region(0, t, tiles, qq, half, BN)) + lane;
+    const float4 *lo0 = reinterpret_cast<const float4 *>(p.ws + split_region(0, t, tiles, qq + 2, half, BN)) + lane;
 #pragma unroll 1
     for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
         const int col0 = n0 + c;
         if (col0 >= p.N) continue;
+        const size_t cc = (size_t)((c - half * (BN / 2)) / kEpiCols) * (kEpiCols / 4) * 32;
         float v[kEpiCols];
 #pragma unroll
         for (int j = 0; j < kEpiCols; j++) v[j] = 0.f;
         for (int s = 0; s < KS; s++) {
-            const float *a = src + (size_t)s * slice + col0;
-            const float *b = a + (size_t)64 * p.N;
-            if (col0 + kEpiCols <= p.N && (p.N & 3) == 0) {
+            const float4 *a = hi0 + (size_t)s * slice + cc;
+            const float4 *b = lo0 + (size_t)s * slice + cc;
 #pragma unroll
-                for (int j = 0; j < kEpiCols; j += 4) {
-                    const float4 x = __ldcg(reinterpret_cast<const float4 *>(a + j));
-                    const float4 y = __ldcg(reinterpret_cast<const float4 *>(b + j));
-                    v[j] += x.x + y.x, v[j + 1] += x.y + y.y, v[j + 2] += x.z + y.z, v[j + 3] += x.w + y.w;
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < kEpiCols; j++)
-                    if (col0 + j < p.N) v[j] += __ldcg(a + j) + __ldcg(b + j);
+            for (int j = 0; j < kEpiCols / 4; j++) {
+                const float4 x = __ldcg(a + 32 * j);
+                const float4 y = __ldcg(b + 32 * j);
+                v[4 * j] += x.x + y.x, v[4 * j + 1] += x.y + y.y, v[4 * j + 2] += x.z + y.z,
+                    v[4 * j + 3] += x.w + y.w;
             }
         }
         epi_direct<EPI>(p, er, v, col0);
@@ -793,7 +784,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[b]);
                 } else {
-                    split_partial<BN>(p, tb, m0 + 32 * q, n0, half, lane, ks, MT * kBM);
+                    split_partial<BN>(p, tb, q, n0, half, lane, ks, t, tiles);
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[b]);
@@ -806,7 +797,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     prev = __shfl_sync(0xffffffffu, prev, 0);
                     if (prev == (unsigned)(2 * KS - 1)) {
                         __threadfence();
-                        split_finish_pair<BN, EPI>(p, t % MT, q & 1, n0, half, lane, KS);
+                        split_finish_pair<BN, EPI>(p, t % MT, q & 1, n0, half, lane, KS, t, tiles);
                         if (lane == 0) p.ws_cnt[t * 4 + pair] = 0u;
                     }
                 }
@@ -819,7 +810,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if (lane == 0) mbar_arrive(&tempty[b]);
             } else {
                 // this split's partial of the warp's 32 x BN/2 sub-tile -> workspace
-                split_partial<BN>(p, tb, m0 + 32 * q, n0, half, lane, ks, p.M);
+                split_partial<BN>(p, tb, q, n0, half, lane, ks, t, tiles);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[b]);   // the accumulator is free already
@@ -832,7 +823,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 prev = __shfl_sync(0xffffffffu, prev, 0);
                 if (prev == (unsigned)(KS - 1)) {
                     __threadfence();
-                    split_finish<BN, EPI>(p, mp, m0 + 32 * q, n0, half, lane, stg, KS);
+                    split_finish<BN, EPI>(p, mp, m0 + 32 * q, n0, half, lane, stg, KS, q, t, tiles);
                     if (lane == 0) p.ws_cnt[t * kEpiWarps + (warp - 2)] = 0u;
                 }
             }
@@ -1320,7 +1311,6 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
         cudaGetDevice(&dev);
         const int sms = device_sms(dev);
         const int mt = p.hilo ? (p.M + 63) / 64 : (p.M + kBM - 1) / kBM, KB = (p.K + kBK - 1) / kBK;
-        const size_t ws_rows = p.hilo ? (size_t)hilo_rows(p.M) : (size_t)p.M;
         // measured at M = 100: a win for K = 5120 (w2), a loss for K = 2048 (wo)
         if (2 * mt * ((p.N + bn - 1) / bn) < sms && KB >= kTcSplitMinKB) {
             // the last slice to finish sums the others: few slices and
@@ -1328,7 +1318,8 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
             const int bw = env_tc_bn() ? env_tc_bn() : (p.N >= 4096 ? 128 : 64);
             const int tiles = mt * ((p.N + bw - 1) / bw);
             int ks = std::min(kTcMaxSplit, std::min(sms / tiles, KB / 4));
-            ks = (int)std::min<size_t>((size_t)ks, p.ws_floats / (ws_rows * p.N));
+            // one 128 x bw region set per tile and slice (split_region)
+            ks = (int)std::min<size_t>((size_t)ks, p.ws_floats / ((size_t)tiles * kBM * bw));
             const char *ev = getenv("VOX_CUDA_TC_KSPLIT");
             if (ev && atoi(ev) >= 1) ks = std::min(ks, atoi(ev));
             if (ks >= 2 && tiles * kEpiWarps <= kTcSplitCounters) {   // (HILO uses 4 per tile)

@@ -141,7 +141,7 @@ struct TcGemmParams {
     unsigned *err;           // raised when a bounded wait expires
     // split-K (few tiles, long K): the caller's fp32 workspace and zeroed
     // counters; launch_tc_gemm picks the split count ksplit (1: none)
-    float *ws;               // >= ksplit * M * N floats
+    float *ws;               // ws_floats; launch_tc_gemm fits ksplit x tiles x 128 x BN floats
     size_t ws_floats;
     unsigned *ws_cnt;        // kTcSplitCounters counters, zero between launches
     int ksplit;
