@@ -7,6 +7,8 @@
 
 #include <stdarg.h>
 
+#include <array>
+
 using namespace vc;
 using namespace vc::rt;
 
@@ -75,11 +77,19 @@ void dev_free(DevCtx *c, void *p, size_t bytes) {
 }
 
 // Host RoPE table for one logical position, the same formula as
-// vox_compute_rope_freqs (voxtral_kernels.c:488-500).
+// vox_compute_rope_freqs (voxtral_kernels.c:488-500).  The frequencies of the
+// decoder's head size are computed once (the same expression, so the same
+// values): the synchronous steps build these tables on the host before every
+// launch, and the powf calls were most of that time.
 void host_rope_table(int pos, int head_dim, float *cs) {
+    static const std::array<float, kHeadDim / 2> freq = [] {
+        std::array<float, kHeadDim / 2> f{};
+        for (int d = 0; d < kHeadDim / 2; d++) f[d] = 1.0f / powf(kRopeTheta, (float)(2 * d) / (float)kHeadDim);
+        return f;
+    }();
     const float p = (float)pos;
     for (int d = 0; d < head_dim / 2; d++) {
-        const float f = 1.0f / powf(kRopeTheta, (float)(2 * d) / (float)head_dim);
+        const float f = head_dim == kHeadDim ? freq[d] : 1.0f / powf(kRopeTheta, (float)(2 * d) / (float)head_dim);
         const float a = p * f;
         cs[2 * d] = cosf(a);
         cs[2 * d + 1] = sinf(a);
