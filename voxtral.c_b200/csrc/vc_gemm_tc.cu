@@ -50,10 +50,12 @@ constexpr uint64_t kTcWaitNs = 2000000000ull;
 
 template <int BN>
 struct TcCfg {
-    static constexpr int kStages = (BN >= 256) ? 4 : 6;
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
-    static constexpr int kTmemCols = 2 * BN;    // two accumulators
+    // as many stages as fit 192 KB, at most 6 (BN 64 / 128: 6, 192 / 256: 4)
+    static constexpr int kStages = (196608 / (kABytes + kBBytes)) < 6 ? (196608 / (kABytes + kBBytes)) : 6;
+    // two accumulators of BN columns; the allocation is a power of two
+    static constexpr int kTmemCols = (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
     static constexpr int kSmem =
         kStages * (kABytes + kBBytes) + kEpiWarps * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -735,7 +737,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d = tmem + b * BN;
+                const uint32_t d = tmem + b * (Cfg::kTmemCols / 2);   // accumulator b at half the allocation
                 for (int kb = kb_first; kb < (ks + 1) * KB / KS; kb++, it++) {
                     const int s = it % S;
                     if (!mbar_wait(&full[s], (it / S) & 1u, deadline)) {
@@ -770,7 +772,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             tc_fence_after();
             const int m0 = (t % MT) * kBM, n0 = (t / MT) * BN;
-            const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + b * BN;
+            const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + b * (Cfg::kTmemCols / 2);
             if constexpr (HILO) {
                 if (KS == 1) {
                     // the lo warp of the pair (warp - 2 for a hi warp) stages its chunks
@@ -1206,29 +1208,38 @@ int env_tc_pair() {
 int env_tc_bn() {
     const char *s = getenv("VOX_CUDA_TC_BN");
     const int n = s ? atoi(s) : 0;
-    return (n == 64 || n == 128 || n == 256) ? n : 0;
+    return (n == 64 || n == 128 || n == 192 || n == 256) ? n : 0;
 }
 
 }  // namespace
 
-// Tile width: the widest tile (fewest operand bytes per MMA flop) that still
-// gives at least half as many tiles as SMs.  Measured on B200 at the encoder
-// shapes (M = 1500): 256 for N = 10240 and 6144, 128 for N = 1280 (60 tiles of
-// 256 leave half the SMs idle).  VOX_CUDA_TC_BN = 64 | 128 | 256 forces a width.
+// Tile width by a cost model of the persistent kernel: rounds of tiles over
+// the SMs (ceil(tiles / SMs)) times the time of one tile, which measured
+// ~120 + BN in the same units (a 128-wide tile takes 0.66 of a 256-wide one
+// at the encoder's shapes, not 0.5).  Ties go to the wider tile.  It keeps
+// the widths measured best at M = 1500 (256 for N = 10240 and 6144, 128 for
+// N = 1280) and at M = 100 and 800; 192 wins where it fits in as many rounds
+// as 256 (q|k|v at M = 500 and 800, w1|w3 at M = 500).
+// VOX_CUDA_TC_BN = 64 | 128 | 192 | 256 forces a width.
 int tc_gemm_bn(int M, int N) {
     if (const int f = env_tc_bn()) return f;
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = device_sms(dev);
     const int mt = (M + kBM - 1) / kBM;
-    for (int bn = 256; bn > 64; bn >>= 1)
-        if (2 * mt * ((N + bn - 1) / bn) >= sms) return bn;
-    return 64;
+    int best = 256;
+    long long best_t = -1;
+    for (int bn : {256, 192, 128, 64}) {
+        const long long tiles = (long long)mt * ((N + bn - 1) / bn);
+        const long long t = (tiles + sms - 1) / sms * (120 + bn);
+        if (best_t < 0 || t < best_t) best_t = t, best = bn;
+    }
+    return best;
 }
 
 // Pair tile width (256 x BN per CTA pair), same cost model over SM pairs.
 int tc_gemm2_bn(int M, int N) {
-    if (const int f = env_tc_bn()) return f >= 128 ? f : 128;
+    if (const int f = env_tc_bn()) return f >= 192 ? 256 : 128;
     int dev = 0;
     cudaGetDevice(&dev);
     const int pairs = device_sms(dev) / 2;
@@ -1304,7 +1315,7 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     // split activations: 128-wide tiles (each column tile re-reads the whole
     // 128-row [hi; lo] A tile, so wider tiles halve that traffic; measured
     // 4.97 -> 3.89 ms for three streams' 114-row prefill, equal at 38 rows)
-    if (bn == 0) bn = p.hilo ? (env_tc_bn() ? env_tc_bn() : 128) : tc_gemm_bn(p.M, p.N);
+    if (bn == 0) bn = p.hilo ? (env_tc_bn() == 64 ? 64 : 128) : tc_gemm_bn(p.M, p.N);
     p.ksplit = 1;
     if (p.ws && p.ws_cnt && !pair) {
         // Split-K when the tiles leave most SMs idle (small M): up to
@@ -1319,7 +1330,8 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
         if (2 * mt * ((p.N + bn - 1) / bn) < sms && KB >= kTcSplitMinKB) {
             // the last slice to finish sums the others: few slices and
             // narrow tiles keep that sum short (one 32-column chunk per warp)
-            const int bw = env_tc_bn() ? env_tc_bn() : (p.hilo || p.N >= 4096 ? 128 : 64);
+            const int fe = (p.hilo && env_tc_bn() > 128) ? 128 : env_tc_bn();   // (split activations: <= 128)
+            const int bw = fe ? fe : (p.hilo || p.N >= 4096 ? 128 : 64);
             const int tiles = mt * ((p.N + bw - 1) / bw);
             int ks = std::min(kTcMaxSplit, std::min(sms / tiles, KB / 4));
             // one 128 x bw region set per tile and slice (split_region)
@@ -1358,6 +1370,7 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     }
     VC_TC_CASE(64)
     VC_TC_CASE(128)
+    VC_TC_CASE(192)
     VC_TC_CASE(256)
 #undef VC_TC_CASE
     return cudaErrorInvalidValue;
