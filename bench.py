@@ -37,7 +37,7 @@ D, QD, KVD, HID, VOCAB, LAYERS = 3072, 4096, 1024, 9216, 131072, 26
 
 
 def weight_bytes_per_step(layers=LAYERS, vocab=VOCAB):
-    """bf16 weight bytes one decode step streams (SURVEY: 6,857,687,040 B)."""
+    """bf16 weight bytes one decode step streams (6,857,687,040 B at 4B)."""
     return layers * 2 * (6144 * D + D * QD + 2 * HID * D + D * HID) + vocab * D * 2
 
 # DRAM bytes (read + write) per launch of the dominant kernel, the w1|w3
@@ -441,7 +441,7 @@ def upload_bench(V, torch, layers=4, vocab=VOCAB):
 
 
 def single_stream_and_attention(V, torch, dec, steps):
-    """SURVEY configs[1]-[2] beside the batched step: one stream's decode
+    """The one-stream decode configurations beside the batched step: one stream's decode
     step (M = 1, the reference's own case: per-token latency), and the
     stand-alone decode attention (vox_cuda_attention_decode_dev) over
     L = 512 / 2048 / 8192 keys of a ring (the last in a wrapped 8192 + 1024
