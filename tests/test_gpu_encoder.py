@@ -127,6 +127,31 @@ def test_encoder_split_k_matches_unsplit(monkeypatch):
         assert B.rel_l2(a, b) < 2e-3, (i, B.rel_l2(a, b))
 
 
+def test_encoder_tile_widths_agree(monkeypatch):
+    """The tensor-core GEMM's tile width (64 / 128 / 192 / 256 columns, picked
+    by a rounds x tile-cost model) changes which CTA computes an output
+    element, not how: each element sums its K blocks in the same order.
+    500- and 800-row chunks, where the model picks 192 for q|k|v (and at
+    500 for w1|w3), against forced widths: bit-identical.  Split-K is held
+    off: a forced width can change whether wo / w2 split, which regroups
+    their fp32 sums (equally accurate, not bit-identical)."""
+    ew = B.EncoderWeights(seed=15, n_layers=2, distinct=2, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    sizes = [500, 800]
+    outs = {}
+    monkeypatch.setenv("VOX_CUDA_TC_KSPLIT", "1")
+    for bn in ("", "256", "128"):
+        monkeypatch.setenv("VOX_CUDA_TC_BN", bn)
+        st = e.state(max_chunk=800)
+        outs[bn] = [st.step(B.normal_f32((n, B.ENC_DIM), 1110 + i)) for i, n in enumerate(sizes)]
+        st.free()
+    e.free()
+    for i in range(len(sizes)):
+        assert np.isfinite(outs[""][i]).all()
+        assert np.array_equal(outs[""][i], outs["256"][i]), i
+        assert np.array_equal(outs[""][i], outs["128"][i]), i
+
+
 def test_encoder_async_steps_match_sync_steps():
     """vox_cuda_encoder_step_dev enqueues without waiting: chunks issued back
     to back (positions travel by value) equal the synchronous host-pointer
