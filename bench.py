@@ -40,10 +40,24 @@ def weight_bytes_per_step(layers=LAYERS, vocab=VOCAB):
     """bf16 weight bytes one decode step streams (6,857,687,040 B at 4B)."""
     return layers * 2 * (6144 * D + D * QD + 2 * HID * D + D * HID) + vocab * D * 2
 
-# DRAM bytes (read + write) per launch of the dominant kernel, the w1|w3
-# SwiGLU GEMV, from the ncu capture summarised in
-# profiles/gemv_tma_kernel_w13_swiglu_8streams.md (113.37 MB + 3.46 MB).
-NCU_TRAFFIC_W13 = 116_822_784
+def ncu_traffic(kernel_key):
+    """DRAM bytes (read + write) per launch of a kernel from the committed ncu
+    summaries: the first `traffic_bytes_per_launch <key> <bytes> <date> <commit>`
+    line of any profiles/*.md.  Returns (bytes, provenance) or (None, reason)."""
+    d = os.path.join(ROOT, "profiles")
+    try:
+        names = sorted(os.listdir(d))
+    except OSError:
+        return None, "no profiles directory"
+    for n in names:
+        if not n.endswith(".md"):
+            continue
+        with open(os.path.join(d, n)) as f:
+            for line in f:
+                t = line.strip().strip("`").split()
+                if len(t) >= 5 and t[0] == "traffic_bytes_per_launch" and t[1] == kernel_key:
+                    return int(t[2]), f"ncu capture {t[3]} at commit {t[4]} ({n})"
+    return None, f"no traffic line for {kernel_key}"
 
 
 def peaks():
@@ -151,11 +165,20 @@ def job_throughput(ws, streams, steps, ms):
 # CPU side: the reference's own path (oracle/_ref) or the oracle port
 # ---------------------------------------------------------------------------
 
+def cpu_threads():
+    """Host threads for the CPU legs: every core this process may run on."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return max(1, os.cpu_count() or 1)
+
+
 def cpu_decode_rate(threads, steps, warmup=0):
     """Decode tok/s of `threads` independent streams, one host thread each,
     through the reference's vox_decoder_forward (oracle/_ref/libvoxref.so),
     or the C restatement where the reference was not built.  Distinct
-    random-init weights for all 26 layers (6.9 GB of bf16, as on the GPU)."""
+    random-init weights for all 26 layers (6.9 GB of bf16, as on the GPU);
+    each stream's cache holds 400 positions (room for 1024)."""
     sys.path.insert(0, ORACLE)
     import ctypes as C
 
@@ -169,7 +192,7 @@ def cpu_decode_rate(threads, steps, warmup=0):
         ctxs = [B.RefCtx(dec=w) for _ in range(threads)]
         lib = B.ref_lib()
         for c in ctxs:
-            lib.voxref_decoder_kv_preallocate(c.ctx, 8192 + 1024)
+            lib.voxref_decoder_kv_preallocate(c.ctx, 1024)
             lib.voxref_set_dec_kv_state(c.ctx, 400, 0)  # mid-clip cache length
         arr = (C.c_void_p * threads)(*[c.ctx for c in ctxs])
         if warmup:
@@ -195,11 +218,58 @@ def cpu_decode_rate(threads, steps, warmup=0):
     return threads * steps / secs, kind
 
 
+def cpu_encoder_prefill(rows=(100, 500, 1500), prompt=38):
+    """The reference's own CPU path for the encoder chunk and the prompt
+    prefill, on every host core (OpenBLAS threads = cores, as the reference
+    runs): vox_encoder_forward_incremental over 32 distinct random-init layers
+    for one chunk of each row count after a 750-row cached history
+    (voxtral_encoder.c:452-636), and vox_decoder_prefill of a 38-row prompt
+    over 26 distinct layers (voxtral_decoder.c:233-373).  One timed run each
+    after one untimed warm-up of the smallest case."""
+    sys.path.insert(0, ORACLE)
+    import bind as B
+    if not B.ref_available():
+        return None
+    out = {"kind": "reference", "build": B.REF_MARCH, "cores": cpu_threads(),
+           "blas": "OpenBLAS 0.3.15 (all host threads)"}
+    ew = B.EncoderWeights(seed=1, distinct=ENC_LAYERS)
+    ref = B.RefCtx(enc=ew)
+    lib = B.ref_lib()
+    lib.voxref_encoder_kv_preallocate(ref.ctx, 750 + max(rows))
+    enc = {}
+    for i, m in enumerate((rows[0],) + tuple(rows)):
+        x = B.normal_f32((m, ENC_D), 5000 + m, 1.0)
+        lib.voxref_set_enc_kv_state(ref.ctx, 750, 0)
+        t0 = time.perf_counter()
+        ref.encoder_incremental(x)
+        sec = time.perf_counter() - t0
+        if i > 0:
+            enc[f"M{m}"] = {"ms_per_chunk": 1000.0 * sec, "audio_s_per_s": (m / 50.0) / sec}
+    ref.free()
+    del ew
+    out["encoder"] = enc
+    w = B.DecoderWeights(seed=0, n_layers=LAYERS, distinct=LAYERS)
+    ref = B.RefCtx(dec=w)
+    lib.voxref_decoder_kv_preallocate(ref.ctx, 1024)
+    x = B.normal_f32((prompt, D), 77, 0.5)
+    times = []
+    for _ in range(2):
+        lib.voxref_set_dec_kv_state(ref.ctx, 0, 0)
+        t0 = time.perf_counter()
+        ref.decoder_prefill(x)
+        times.append(time.perf_counter() - t0)
+    ref.free()
+    out["prefill"] = {"rows": prompt, "ms": 1000.0 * times[-1]}
+    out["sample"] = (f"one chunk per row count after a 750-row history, 32 layers; one {prompt}-row "
+                     f"prefill over 26 layers; each after a warm-up")
+    return out
+
+
 def reference_arm(args):
     ws, rank, _ = dist_env()
     if rank != 0:
         return
-    threads = min(8, os.cpu_count() or 1)
+    threads = cpu_threads()
     rate, kind = cpu_decode_rate(threads, args.steps, args.warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus,
@@ -208,11 +278,19 @@ def reference_arm(args):
         "data": "synthetic (seeded random-init bf16 weights)",
         "config": config(threads, [400] * threads, ws),
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": f"{threads} streams x {args.steps} decode steps, one host thread each "
-                                   f"(vox_decoder_forward; its GEMV is single-threaded per stream)"},
+                         "build": ref_march(),
+                         "sample": f"{threads} streams (one per host core) x {args.steps} decode steps, "
+                                   f"one host thread each (vox_decoder_forward; its GEMV is "
+                                   f"single-threaded per stream), KV length 400"},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def ref_march():
+    sys.path.insert(0, ORACLE)
+    import bind as B
+    return B.REF_MARCH if B.ref_available() else "port (vo_oracle.c, -march=x86-64-v3)"
 
 
 def config(streams, pos, ws):
@@ -345,15 +423,26 @@ def encoder_bench(V, torch, steps, only_rows=0):
     prof = st.profile(x.data_ptr(), 1500, iters=3)
     out["phase_ms_M1500"] = prof
     w13_flops = 2 * 1500 * 2 * ENC_H * ENC_D * ENC_LAYERS
-    _, _ = peaks()
     tflops = w13_flops / (prof["w13"] / 1000.0) / 1e12
     gemm_flops = 1500 * ENC_FLOPS_PER_ROW
     gemm_ms = prof["qkv"] + prof["wo"] + prof["w13"] + prof["w2"]
-    bf16_peak, bf16_kind = bf16_peaks()
+    # the phase profile puts events around every launch: each GEMM is timed
+    # alone, so the burst peak is its denominator; the whole chunk (all its
+    # launches back to back, ms_per_chunk) is set against the sustained one
+    burst, burst_kind = bf16_peaks("burst")
+    sust, sust_kind = bf16_peaks("sustained")
+    chunk_ms = out["ms_per_chunk"]["M1500"]
+    attn_flops = 1500 * 32 * 4 * 64 * 750 * ENC_LAYERS   # every row attends a full 750-key window
+    chunk_tflops = (gemm_flops + attn_flops) / (chunk_ms / 1000.0) / 1e12
     out["roofline"] = {"kernel": "tc_gemm_kernel<256, TC_SWIGLU> (w1|w3, M=1500)", "bound": "tensor",
-                       "achieved": tflops, "peak": bf16_peak, "peak_kind": bf16_kind, "unit": "TFLOP/s",
-                       "frac": tflops / bf16_peak,
-                       "all_gemms_tflops": gemm_flops / (gemm_ms / 1000.0) / 1e12}
+                       "achieved": tflops, "peak": burst, "peak_kind": burst_kind, "unit": "TFLOP/s",
+                       "frac": tflops / burst,
+                       "timing": "CUDA events around each of the 32 launches (launches timed alone)",
+                       "all_gemms_tflops": gemm_flops / (gemm_ms / 1000.0) / 1e12,
+                       "all_gemms_frac": gemm_flops / (gemm_ms / 1000.0) / 1e12 / burst,
+                       "whole_chunk_tflops": chunk_tflops,
+                       "whole_chunk_frac_of_sustained": chunk_tflops / sust, "sustained_peak": sust,
+                       "sustained_kind": sust_kind}
     st.free()
     enc.free()
     return out
@@ -582,17 +671,19 @@ def front_bench(V, torch, steps, streams=8):
     return res
 
 
-def bf16_peaks():
-    """(peak TFLOP/s, kind): the measured sustained dense bf16 figure, the one
-    for a kernel timed inside a long loop (the encoder chunk), else the burst
-    figure, else the pool's earlier measurement."""
+def bf16_peaks(kind="burst"):
+    """(peak TFLOP/s, label): the measured dense bf16 figure, burst (for a
+    kernel timed alone) or sustained (for work timed inside a long loop at the
+    power cap), else the pool's earlier measurements."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        if "bf16_tflops_sustained" in d:
+        if kind == "sustained" and "bf16_tflops_sustained" in d:
             return float(d["bf16_tflops_sustained"]), "measured sustained (bf16_tflops_sustained)"
         return float(d["bf16_tflops"]), "measured burst (bf16_tflops)"
+    if kind == "sustained":
+        return 1400.0, "fallback (1.4 PFLOP/s sustained)"
     return 1590.0, "fallback (1.59 PFLOP/s burst)"
 
 
@@ -716,15 +807,22 @@ def our_arm(args):
     up_res = upload_bench(V, torch) if not args.no_encoder else None
     enc_res = None if args.no_encoder else encoder_bench(V, torch, args.steps, args.enc_rows)
 
+    traffic, traffic_src = ncu_traffic("gemv_tma_kernel_w13_swiglu_8streams")
     line = None
     if rank == 0:
         cpu = None
         if ws == 1 and not args.no_cpu_baseline:
-            threads = min(8, os.cpu_count() or 1)
-            rate, kind = cpu_decode_rate(threads, 1)
-            cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": kind,
-                   "sample": f"{threads} streams x 1 decode step (vox_decoder_forward, KV length 400), "
-                             f"one host thread per stream"}
+            threads = cpu_threads()
+            rate, kind = cpu_decode_rate(threads, 3, warmup=1)
+            cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": kind, "build": ref_march(),
+                   "sample": f"{threads} streams (one per host core) x 3 decode steps after 1 warm-up "
+                             f"(vox_decoder_forward, KV length 400), one host thread per stream"}
+            if enc_res is not None and not args.no_cpu_encoder:
+                cpu_ep = cpu_encoder_prefill()
+                if cpu_ep is not None:
+                    enc_res["cpu_baseline"] = {k: v for k, v in cpu_ep.items() if k != "prefill"}
+                    pf_res["cpu_baseline"] = {"kind": cpu_ep["kind"], "build": cpu_ep["build"],
+                                              "cores": cpu_ep["cores"], **cpu_ep["prefill"]}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -739,7 +837,8 @@ def our_arm(args):
             "roofline": {"kernel": "gemv_tma_kernel<8, EPI_SWIGLU> (w1|w3 + SwiGLU)", "bound": "hbm",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "peak_kind": peak_kind,
-                         "traffic": NCU_TRAFFIC_W13, "bytes_per_launch": w13_bytes,
+                         "traffic": traffic, "traffic_source": traffic_src,
+                         "bytes_per_launch": w13_bytes,
                          "launch_ms": w13_ms,
                          "timing": "CUDA events around 5 replays of a graph of the 26 layers' w1|w3 "
                                    "launches back to back (PDL on, as in the step); each layer streams "
@@ -772,6 +871,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder", action="store_true")
+    ap.add_argument("--no-cpu-encoder", action="store_true")
     # encoder-only / single chunk size, for small ncu captures
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--prefill-only", action="store_true")

@@ -206,6 +206,15 @@ int vox_cuda_decoder_prefill_batch(vox_cuda_dec_state *const *states, int n, con
 int vox_cuda_decoder_step_batch(vox_cuda_dec_state *const *states, int n, const float *embeds,
                                 int *tokens);
 
+/* The batched step with the per-stream inputs and outputs of
+ * vox_cuda_decoder_full_step (voxtral_metal.h:219): rope_freqs host
+ * [n][64][2] (each stream's table as vox_compute_rope_freqs produces it for
+ * that stream's position, voxtral_decoder.c:441-443) or NULL to derive them,
+ * and logits host [n][vocab] (voxtral_decoder.c:504-506, the buffer
+ * stream_fill_alts and teacher-forced checks read) or NULL. */
+int vox_cuda_decoder_step_batch_ex(vox_cuda_dec_state *const *states, int n, const float *embeds,
+                                   const float *rope_freqs, int *tokens, float *logits);
+
 /* Device-resident form of the batched step for callers that keep the
  * embeddings on the device: embeds_dev [n, 3072], tokens_dev [n] (int32),
  * enqueued on `stream` (NULL: the library's stream) without waiting for it,

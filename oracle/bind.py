@@ -18,7 +18,27 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
-REF_SO = os.path.join(HERE, "_ref", "libvoxref.so")
+REF_SO_V3 = os.path.join(HERE, "_ref", "libvoxref.so")
+REF_SO_V4 = os.path.join(HERE, "_ref", "libvoxref_v4.so")
+
+
+def _host_has_avx512():
+    """True where /proc/cpuinfo lists the x86-64-v4 extensions."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    fl = set(line.split(":", 1)[1].split())
+                    return {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"} <= fl
+    except OSError:
+        pass
+    return False
+
+
+# The reference's own Makefile builds with -march=native; the build here
+# matching this host's CPU stands in for it (x86-64-v4 with AVX-512, else v3).
+REF_SO = REF_SO_V4 if (_host_has_avx512() and os.path.exists(REF_SO_V4)) else REF_SO_V3
+REF_MARCH = "x86-64-v4" if REF_SO == REF_SO_V4 else "x86-64-v3"
 
 DEC_DIM, DEC_LAYERS, DEC_HEADS, DEC_KV_HEADS, DEC_HEAD_DIM = 3072, 26, 32, 8, 128
 DEC_HIDDEN, DEC_WINDOW, VOCAB = 9216, 8192, 131072

@@ -43,6 +43,24 @@ def pack(prefix, arr, out):
     out[prefix + "_size"] = np.int64(flat.size)
 
 
+def pack_vals(prefix, arr, out, n_sample=SAMPLE):
+    """Like pack, without the indices: the sample positions are
+    sample_idx(size) (or all values when size <= n_sample), recomputed by the
+    reader, which keeps files with many outputs of one size small."""
+    flat = np.asarray(arr, np.float32).reshape(-1)
+    idx = sample_idx(flat.size) if n_sample == SAMPLE else sample_n(flat.size, n_sample)
+    out[prefix + "_val"] = flat[idx]
+    out[prefix + "_norm"] = np.float64(np.linalg.norm(flat.astype(np.float64)))
+    out[prefix + "_size"] = np.int64(flat.size)
+
+
+def sample_n(n, k, seed=4242):
+    if n <= k:
+        return np.arange(n, dtype=np.int64)
+    rng = np.random.default_rng(seed + n + k)
+    return np.sort(rng.choice(n, k, replace=False)).astype(np.int64)
+
+
 def checksum(a):
     return np.array(hashlib.sha1(np.ascontiguousarray(a).tobytes()).hexdigest()[:16])
 
@@ -204,6 +222,84 @@ def gen_decoder(w):
         out[f"compact{s}_state"] = np.array(ref.state(), np.int32)
     ref.free()
     np.savez_compressed(os.path.join(HERE, "decoder.npz"), **out)
+
+
+# The benchmarked batched step: 8 streams sharing one decoder, with cached
+# histories of 39 + 100 i positions (streams 0..6) and one full cache of
+# 8200 rows at logical offset 3000 (stream 7), which the reference compacts
+# before its first step and which wraps the device ring (8192 + 1024 slots).
+# Each stream is its own reference context (vox_decoder_forward,
+# voxtral_decoder.c:401-516); the histories are seeded random K / V rows.
+BATCH_N = 8
+BATCH_STEPS = 3
+BATCH_LOGIT_SAMPLE = 8192
+
+
+def batch_history(i):
+    """(rows, logical offset) of stream i's cached history."""
+    if i < BATCH_N - 1:
+        return 39 + 100 * i, 0
+    return COMPACT_MAX, COMPACT_OFFSET
+
+
+def batch_kv(i):
+    rows, _ = batch_history(i)
+    k = B.normal_f32((B.DEC_LAYERS, rows, B.KV_DIM), 7300 + 2 * i, 1.0)
+    v = B.normal_f32((B.DEC_LAYERS, rows, B.KV_DIM), 7301 + 2 * i, 1.0)
+    return k, v
+
+
+def batch_embeds(step):
+    return B.normal_f32((BATCH_N, B.DEC_DIM), 7400 + step, 1.0)
+
+
+def gen_batch8(w):
+    out = {}
+    rope = np.zeros((BATCH_STEPS, BATCH_N, 128), np.float32)
+    for i in range(BATCH_N):
+        rows, off = batch_history(i)
+        ref = B.RefCtx(dec=w)
+        assert B.ref_lib().voxref_decoder_kv_preallocate(ref.ctx, rows if off else rows + 8) == 0
+        k, v = ref.dec_kv()
+        kf, vf = batch_kv(i)
+        k[:, :rows] = kf
+        v[:, :rows] = vf
+        del kf, vf, k, v
+        B.ref_lib().voxref_set_dec_kv_state(ref.ctx, rows, off)
+        for s_ in range(BATCH_STEPS):
+            rope[s_, i] = B.ref_rope_freqs([off + rows + s_], 128)[0]
+            tok, lg = ref.decoder_forward(batch_embeds(s_)[i])
+            pack_vals(f"s{i}_step{s_}", lg, out, BATCH_LOGIT_SAMPLE)
+            out[f"s{i}_step{s_}_token"] = np.int32(tok)
+            srt = np.sort(lg)
+            out[f"s{i}_step{s_}_margin"] = np.float32(srt[-1] - srt[-2])
+        out[f"s{i}_state"] = np.array(ref.state(), np.int32)
+        ref.free()
+    out["rope"] = rope
+    np.savez_compressed(os.path.join(HERE, "batch8.npz"), **out)
+
+
+# The benchmarked encoder chunk sizes (BASELINE configs[2]): a 750-row
+# history, then 500 and 1500 rows, run on the device with max_chunk = 1500
+# as the bench runs them (vox_encoder_forward_incremental,
+# voxtral_encoder.c:452-636).
+ENC_BIG_CHUNKS = [750, 500, 1500]
+
+
+def enc_big_chunks(seed=8501):
+    return [B.normal_f32((n, B.ENC_DIM), seed + i, 1.0) for i, n in enumerate(ENC_BIG_CHUNKS)]
+
+
+def gen_encoder_big(ew):
+    out = {}
+    ref = B.RefCtx(enc=ew)
+    for i, x in enumerate(enc_big_chunks()):
+        y = ref.encoder_incremental(x)
+        pack_vals(f"chunk{i}", y, out)
+        out[f"chunk{i}_state"] = np.array(ref.state(), np.int32)
+        del y
+    ref.free()
+    np.savez_compressed(os.path.join(HERE, "encoder_big.npz"), **out)
 
 
 ENC_CHUNKS = [100, 37, 700, 100]
@@ -419,6 +515,90 @@ def gen_front(ew):
     np.savez_compressed(os.path.join(HERE, "front.npz"), **out)
 
 
+# configs[3] at full length: 60 s of seeded synthetic 16 kHz audio fed in
+# 2.0 s pieces through the stream path's front end (incremental log-mel with
+# the 32-token left pad, conv stem at 312 then 200 pending mel frames, the
+# encoder per stem chunk, the adapter over whole groups of 4 rows,
+# voxtral.c:668-774), the 39-token prompt prefilled as 38 rows plus one step
+# (voxtral.c:836-891), then greedy steps on the reference's own tokens
+# (voxtral.c:893-921) to 750 generated tokens.  Every step's token and top-1
+# margin is kept; the logits of a fixed set of steps are sampled.
+E2E_SAMPLES = 60 * 16000
+E2E_FEED = 32000
+E2E_TOKENS = 750
+E2E_LOGIT_STEPS = [0, 1, 2, 3, 10, 50, 100, 200, 300, 400, 500, 600, 700, 749]
+E2E_LOGIT_SAMPLE = 8192
+
+
+def e2e_audio(seed=8601):
+    return B.synthetic_audio(E2E_SAMPLES, seed)
+
+
+def e2e_mel_schedule(mel_feed, mel_finish):
+    """Drive a mel context (host or device) the way the stream path does:
+    (per-feed frame counts, tail frame count, list of mel frame arrays)."""
+    x = e2e_audio()
+    rows = [mel_feed(x[o:o + E2E_FEED]) for o in range(0, E2E_SAMPLES, E2E_FEED)]
+    z = front_right_pad(E2E_SAMPLES)
+    tail = []
+    while z > 0:
+        c = min(z, 4096)
+        tail.append(mel_feed(np.zeros(c, np.float32)))
+        z -= c
+    tail.append(mel_finish())
+    return [r.shape[0] for r in rows], sum(t.shape[0] for t in tail), rows + tail
+
+
+def gen_e2e(w, ew):
+    out = {}
+    t0 = time.time()
+    mel = B.RefMel(FRONT_LEFT_PAD)
+    feed_frames, fin, parts = e2e_mel_schedule(mel.feed, lambda: mel.finish(0))
+    mel.free()
+    chunks = front_stem_chunks(feed_frames, fin)
+    out["stem_chunks"] = np.array(chunks, np.int32)
+    all_mel = np.concatenate(parts, axis=0)
+    assert all_mel.shape[0] == sum(chunks)
+    stem = B.RefStem(B.ConvStemWeights(seed=DEC_SEED))
+    ref = B.RefCtx(dec=w, enc=ew)
+    enc, off = [], 0
+    for n in chunks:
+        conv = stem.step(all_mel[off:off + n])
+        off += n
+        if conv.shape[0]:
+            enc.append(ref.encoder_incremental(conv))
+    stem.free()
+    enc = np.concatenate(enc, axis=0)
+    out["encoder_rows"] = np.int32(enc.shape[0])
+    usable = enc.shape[0] // 4 * 4
+    ad = ref.adapter(enc[:usable])
+    del enc
+    pack_vals("adapter", ad, out)
+    print("e2e front end", ad.shape, time.time() - t0, flush=True)
+    assert ad.shape[0] >= CHAIN_PROMPT - 1 + E2E_TOKENS
+    prompt = np.stack([chain_embed(w, ad[i], TOKEN_BOS if i == 0 else TOKEN_PAD)
+                       for i in range(CHAIN_PROMPT)])
+    ref.decoder_prefill(prompt[:CHAIN_PROMPT - 1])
+    toks = np.zeros(E2E_TOKENS, np.int32)
+    margins = np.zeros(E2E_TOKENS, np.float32)
+    tok, lg = ref.decoder_forward(prompt[CHAIN_PROMPT - 1])
+    for g in range(E2E_TOKENS):
+        if g > 0:
+            tok, lg = ref.decoder_forward(chain_embed(w, ad[CHAIN_PROMPT - 1 + g], tok))
+        toks[g] = tok
+        srt = np.partition(lg, -2)[-2:]
+        margins[g] = np.float32(abs(srt[1] - srt[0]))
+        if g in E2E_LOGIT_STEPS:
+            pack_vals(f"step{g}_logits", lg, out, E2E_LOGIT_SAMPLE)
+        if g % 50 == 0:
+            print("e2e step", g, time.time() - t0, flush=True)
+    out["tokens"] = toks
+    out["margins"] = margins
+    out["state_after"] = np.array(ref.state(), np.int32)
+    ref.free()
+    np.savez_compressed(os.path.join(HERE, "e2e60.npz"), **out)
+
+
 ALT_CASES = [(61, 3.0, 4, 0.999), (62, 0.5, 4, 0.5), (63, 8.0, 3, 0.99), (64, 1.0, 2, 0.9),
              (65, 0.01, 4, 0.999)]
 
@@ -449,6 +629,18 @@ def main():
         gen_stem()
         print("stem", time.time() - t)
         return
+    if sys.argv[1:] == ["e2e60"]:   # only configs[3] at full length (~15 min)
+        gen_e2e(B.DecoderWeights(seed=DEC_SEED), B.EncoderWeights(seed=DEC_SEED))
+        print("e2e60", time.time() - t)
+        return
+    if sys.argv[1:] == ["batch8"]:   # only the 8-stream batched step
+        gen_batch8(B.DecoderWeights(seed=DEC_SEED))
+        print("batch8", time.time() - t)
+        return
+    if sys.argv[1:] == ["encoder_big"]:   # only the 500 / 1500-row encoder chunks
+        gen_encoder_big(B.EncoderWeights(seed=DEC_SEED))
+        print("encoder_big", time.time() - t)
+        return
     if sys.argv[1:] == ["chain"]:   # only the end-to-end chain
         gen_chain(B.DecoderWeights(seed=DEC_SEED), B.EncoderWeights(seed=DEC_SEED))
         print("chain", time.time() - t)
@@ -461,11 +653,14 @@ def main():
     gen_mel(); print("mel", time.time() - t)
     w = B.DecoderWeights(seed=DEC_SEED)
     gen_decoder(w); print("decoder", time.time() - t)
+    gen_batch8(w); print("batch8", time.time() - t)
     del w
     ew = B.EncoderWeights(seed=DEC_SEED)
     gen_encoder(ew); print("encoder", time.time() - t)
+    gen_encoder_big(ew); print("encoder_big", time.time() - t)
     gen_chain(B.DecoderWeights(seed=DEC_SEED), ew); print("chain", time.time() - t)
     gen_front(ew); print("front", time.time() - t)
+    gen_e2e(B.DecoderWeights(seed=DEC_SEED), ew); print("e2e60", time.time() - t)
 
 
 if __name__ == "__main__":

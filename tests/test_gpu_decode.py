@@ -169,6 +169,50 @@ def test_decoder_prefill_and_steps_match_reference(gpu_dec):
     st.free()
 
 
+def vals_rel(arr, g, prefix, n_sample):
+    """rel-L2 of arr at the sample positions of a pack_vals golden entry."""
+    flat = np.asarray(arr, np.float32).reshape(-1)
+    assert flat.size == int(g[prefix + "_size"])
+    idx = G.sample_n(flat.size, n_sample)
+    return B.rel_l2(flat[idx], g[prefix + "_val"])
+
+
+def test_batched_step_8_streams_matches_reference(gpu_dec):
+    """The benchmarked configuration: 8 streams in one batched step on the
+    full 26-layer, 131072-vocab decoder (every gemv_tma_kernel<8, EPI_*>
+    instance and the 8-row decode attention), stream histories of 39 + 100 i
+    positions and one full 8200-row cache at logical offset 3000 that wraps
+    the device ring.  Each stream's logits and token against the reference's
+    own vox_decoder_forward on that stream alone (golden batch8.npz), with
+    the reference's RoPE tables passed in as the C host passes them."""
+    g = load_golden("batch8")
+    states = []
+    for i in range(G.BATCH_N):
+        rows, off = G.batch_history(i)
+        st = gpu_dec.state(kv_cap=8192 + 1024)
+        kf, vf = G.batch_kv(i)
+        for layer in range(B.DEC_LAYERS):
+            st.load_kv(layer, off, kf[layer], vf[layer])
+        del kf, vf
+        st.set_position(off + rows)
+        states.append(st)
+    worst = 0.0
+    for s in range(G.BATCH_STEPS):
+        toks, lg = V.step_batch_ex(states, G.batch_embeds(s), rope=g["rope"][s])
+        for i in range(G.BATCH_N):
+            key = f"s{i}_step{s}"
+            rel = vals_rel(lg[i], g, key, G.BATCH_LOGIT_SAMPLE)
+            worst = max(worst, rel)
+            assert rel < LOGIT_TOL * 1e-2, (i, s, rel)   # contract 1e-2; measured ~1e-5
+            if toks[i] != int(g[key + "_token"]):
+                assert float(g[key + "_margin"]) <= MARGIN, (i, s, toks[i], int(g[key + "_token"]))
+    print("8-stream batched step: worst logits rel-L2 vs reference", worst)
+    for i, st in enumerate(states):
+        rows, off = G.batch_history(i)
+        assert st.position == off + rows + G.BATCH_STEPS
+        st.free()
+
+
 def test_decoder_ring_matches_reference_compaction(gpu_dec):
     """A full reference cache (len == max == 8200 at logical offset 3000) is
     compacted by the reference before the step; the ring holds the same rows

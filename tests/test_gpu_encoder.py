@@ -65,6 +65,26 @@ def test_encoder_chunks_match_reference(gpu_enc):
     st.free()
 
 
+def test_encoder_benchmark_chunks_match_reference(gpu_enc):
+    """The benchmarked chunk sizes with the bench's
+    max_chunk of 1500: a 750-row history, then 500 rows and 1500 rows, each
+    attending a full 750-row window (golden encoder_big.npz from the
+    reference's vox_encoder_forward_incremental)."""
+    g = load_golden("encoder_big")
+    st = gpu_enc.state(max_chunk=1500)
+    rels = []
+    for i, x in enumerate(G.enc_big_chunks()):
+        y = st.step(x)
+        assert np.isfinite(y).all()
+        flat = y.reshape(-1)
+        assert flat.size == int(g[f"chunk{i}_size"])
+        rels.append(B.rel_l2(flat[G.sample_idx(flat.size)], g[f"chunk{i}_val"]))
+    print("encoder 750/500/1500-row chunks rel-L2 vs reference:", rels)
+    assert max(rels) < ENC_TOL, rels
+    assert st.position == sum(G.ENC_BIG_CHUNKS)
+    st.free()
+
+
 @pytest.mark.parametrize("pair", ["0", "1"])
 def test_encoder_epilogue_paths_agree(pair, monkeypatch):
     """The TMA-store epilogue (staged tiles, TMA reduce-add for the residual)

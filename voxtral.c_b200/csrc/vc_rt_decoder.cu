@@ -1164,8 +1164,9 @@ static int batch_prepare(vox_cuda_dec_state *const *states, int n, vox_cuda_deco
     return VOX_CUDA_OK;
 }
 
-extern "C" int vox_cuda_decoder_step_batch(vox_cuda_dec_state *const *states, int n,
-                                           const float *embeds, int *tokens) {
+extern "C" int vox_cuda_decoder_step_batch_ex(vox_cuda_dec_state *const *states, int n,
+                                              const float *embeds, const float *rope_freqs,
+                                              int *tokens, float *logits) {
     if (!embeds || !tokens) {
         set_error("decoder_step_batch: bad arguments");
         return VOX_CUDA_ERR_ARG;
@@ -1178,15 +1179,25 @@ extern "C" int vox_cuda_decoder_step_batch(vox_cuda_dec_state *const *states, in
     if (rc) return rc;
     StepWork *w = d->batch_work[n];
     memcpy(h_x(w), embeds, (size_t)n * kDecDim * sizeof(float));
+    if (rope_freqs) memcpy(h_rope(w), rope_freqs, (size_t)n * kHeadDim * sizeof(float));
     rc = run_step(d, c, w, true, c->stream, true);
     w->err_pending = false;   // this step's error check covered the earlier ones
     if (rc) return rc;
+    if (logits) {   // the step has completed: [n][vocab] in one copy
+        VC_TRY(cudaMemcpy(logits, w->logits, (size_t)n * d->vocab * sizeof(float),
+                          cudaMemcpyDeviceToHost));
+    }
     for (int i = 0; i < n; i++) {
         tokens[i] = w->h_tokens[i];
         states[i]->pos += 1;
         states[i]->have_logits = false;
     }
     return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_decoder_step_batch(vox_cuda_dec_state *const *states, int n,
+                                           const float *embeds, int *tokens) {
+    return vox_cuda_decoder_step_batch_ex(states, n, embeds, nullptr, tokens, nullptr);
 }
 
 extern "C" int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states, int n,

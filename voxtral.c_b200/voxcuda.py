@@ -101,6 +101,7 @@ def lib():
         "vox_cuda_decoder_prefill_step": ([C.c_void_p, _fp, C.c_int, _fp], C.c_int),
         "vox_cuda_decoder_prefill_batch": ([C.c_void_p, C.c_int, _fp, _ip, _fp], C.c_int),
         "vox_cuda_decoder_step_batch": ([C.c_void_p, C.c_int, _fp, _ip], C.c_int),
+        "vox_cuda_decoder_step_batch_ex": ([C.c_void_p, C.c_int, _fp, _fp, _ip, _fp], C.c_int),
         "vox_cuda_decoder_step_batch_dev": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                              C.c_void_p], C.c_int),
         "vox_cuda_decoder_profile_batch": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, _fp],
@@ -292,6 +293,19 @@ def step_batch(states, embeds):
     check(lib().vox_cuda_decoder_step_batch(arr, n, _f(embeds), toks.ctypes.data_as(_ip)),
           "step_batch")
     return toks.tolist()
+
+
+def step_batch_ex(states, embeds, rope=None, want_logits=True):
+    """Batched step returning (tokens, logits [n, vocab] or None); rope:
+    [n, 128] tables (cos, sin pairs) or None to derive them."""
+    embeds = np.ascontiguousarray(embeds, np.float32)
+    n = len(states)
+    toks = np.empty(n, np.int32)
+    logits = np.empty((n, states[0].dec.vocab), np.float32) if want_logits else None
+    rope = None if rope is None else np.ascontiguousarray(rope, np.float32).reshape(n, -1)
+    check(lib().vox_cuda_decoder_step_batch_ex(states_array(states), n, _f(embeds), _f(rope),
+                                               toks.ctypes.data_as(_ip), _f(logits)), "step_batch_ex")
+    return toks.tolist(), logits
 
 
 def states_array(states):
