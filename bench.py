@@ -380,11 +380,13 @@ def build_device_encoder(V, torch, seed=1):
     return enc
 
 
-def encoder_bench(V, torch, steps, only_rows=0):
+def encoder_bench(V, torch, steps, only_rows=0, enc=None):
     """Encoder chunk throughput: 32 layers at M = 100,
     500, 1500 rows (2, 10, 30 s of audio at 50 Hz) with a full 750-row window
     of earlier context, plus the per-phase profile at M = 1500."""
-    enc = build_device_encoder(V, torch)
+    own = enc is None
+    if own:
+        enc = build_device_encoder(V, torch)
     st = enc.state(max_chunk=1500)
     # a dedicated stream: step_dev is asynchronous, and the legacy default
     # stream's handle (0) would mean "the library's own stream"
@@ -416,7 +418,8 @@ def encoder_bench(V, torch, steps, only_rows=0):
         out["front_end_2s_chunks"] = front_bench(V, torch, steps)
     if only_rows and only_rows != 1500:
         st.free()
-        enc.free()
+        if own:
+            enc.free()
         return out
     st.set_position(750)
     x = x0[:1500].contiguous()
@@ -444,7 +447,8 @@ def encoder_bench(V, torch, steps, only_rows=0):
                        "whole_chunk_frac_of_sustained": chunk_tflops / sust, "sustained_peak": sust,
                        "sustained_kind": sust_kind}
     st.free()
-    enc.free()
+    if own:
+        enc.free()
     return out
 
 
@@ -671,6 +675,185 @@ def front_bench(V, torch, steps, streams=8):
     return res
 
 
+SR, HOP, TOK_SAMPLES = 16000, 160, 1280
+TOKEN_BOS, TOKEN_PAD = 1, 32
+PROMPT_LEN = 1 + 32 + 6          # [BOS] + 32 left-pad tokens + the default delay of 6
+
+
+def synthetic_clips(torch, streams, n_samples, seed):
+    """Seeded 16 kHz test audio on the device, one clip per stream: white noise
+    low-passed by a 4-tap average (pink-ish) plus 200-3000 Hz tone bursts,
+    scaled to -20 dBFS RMS.  Stands in for real speech; the work per sample
+    does not depend on the content."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    x = torch.randn((streams, n_samples + 3), generator=g, device="cuda")
+    x = (x[:, 3:] + x[:, 2:-1] + x[:, 1:-2] + x[:, :-3]) * 0.5
+    t = torch.arange(n_samples, device="cuda", dtype=torch.float32) / SR
+    f = 200.0 + 2800.0 * torch.rand((streams, 1), generator=g, device="cuda")
+    burst = (torch.sin(2 * np.pi * 0.5 * t)[None, :] > 0.3).float()
+    x = x + 3.0 * torch.sin(2 * np.pi * f * t[None, :]) * burst
+    x = x * (10 ** (-20.0 / 20.0) / x.pow(2).mean(dim=1, keepdim=True).sqrt())
+    return x.clamp_(-1.0, 1.0).contiguous()
+
+
+def serving_bench(V, torch, dec, enc, clip_s=60.0, interval_s=2.0, streams=8, seed=4321,
+                  warm_intervals=3, host_audio=False):
+    """`streams` independent seeded clips of `clip_s`
+    seconds, fed every `interval_s` seconds of audio as the reference's
+    stream API does (vox_stream_feed / stream_run_encoder /
+    stream_run_decoder, voxtral.c:668-774, 836-921, 923-1080): per interval
+    every stream's new samples -> incremental log-mel -> conv stem (first call
+    at 312 pending mel frames, then at 200) -> the encoder chunk of all streams
+    in one batched launch -> the adapter over whole groups of 4 rows (the
+    remainder carried) -> once 39 adapter rows exist, the prompt prefill of all
+    streams in shared launches, then one batched decode step per new adapter
+    row, each step's input adapter[pos] + tok_embed(previous token) built on
+    the device.  The finish feeds the zero right pad and flushes the mel
+    context (voxtral.c:979-1007).  Everything is enqueued on one CUDA stream
+    without host waits, except the prefill (host prompt rows, once per clip).
+
+    host_audio: the clips start in pinned host memory and each interval's
+    samples are copied to the device inside the timed region (the end-to-end
+    form); the tokens are read back at the end."""
+    S = streams
+    n_samples = int(clip_s * SR)
+    feed = int(interval_s * SR)
+    right_pad = (TOK_SAMPLES - n_samples % TOK_SAMPLES) % TOK_SAMPLES + (6 + 1 + 10) * TOK_SAMPLES
+    clips = synthetic_clips(torch, S, n_samples, seed)
+    if host_audio:
+        h_clips = clips.cpu().pin_memory()
+        clips = torch.empty_like(clips)
+    zeros = torch.zeros(feed, device="cuda")
+    rng = np.random.default_rng(seed)
+    cw = [(rng.standard_normal(sh) * 0.02).astype(np.float32)
+          for sh in ((ENC_D, 128, 3), (ENC_D,), (ENC_D, ENC_D, 3), (ENC_D,))]
+    MAX_MEL, MAX_ROWS = 512, 256
+    stems = [V.ConvStem(*cw, max_mel=MAX_MEL) for _ in range(S)]
+    est = [enc.state(max_chunk=MAX_ROWS) for _ in range(S)]
+    dst = [dec.state(kv_cap=8192 + 1024) for _ in range(S)]
+    mel_buf = torch.empty((S, MAX_MEL, 128), device="cuda")
+    enc_buf = torch.empty((S, MAX_ROWS + 4, ENC_D), device="cuda")
+    max_tok = n_samples // TOK_SAMPLES + 64 + right_pad // TOK_SAMPLES
+    ad_ring = torch.empty((S, max_tok, D), device="cuda")
+    prompt = torch.empty((S, PROMPT_LEN, D), device="cuda")
+    prompt_tok = torch.tensor([TOKEN_BOS] + [TOKEN_PAD] * (PROMPT_LEN - 1), dtype=torch.int32, device="cuda")
+    tokens = torch.empty((max_tok + 1, S), dtype=torch.int32, device="cuda")
+    st = torch.cuda.Stream()
+    sp = st.cuda_stream
+    f4 = 4   # bytes per float
+
+    def run(n_intervals):
+        mels = [V.Mel(32 * TOK_SAMPLES, feed) for _ in range(S)]
+        for x in stems:
+            x.reset()
+        for x in est:
+            x.reset()
+        for x in dst:
+            x.reset()
+        pending, first, lo = [0] * S, [True] * S, [0] * S
+        total_ad, gen_pos, steps, started = 0, 0, 0, False
+        iv_events = []
+        feeds = [(o, min(feed, n_samples - o)) for o in range(0, n_samples, feed)][:n_intervals]
+        finish = n_intervals * feed >= n_samples
+        plan = [("audio", o, n) for o, n in feeds] + ([("finish", 0, 0)] if finish else [])
+        with torch.cuda.stream(st):
+            tokens[0].fill_(TOKEN_PAD)
+        for kind, off, n in plan:
+            e_a = torch.cuda.Event(enable_timing=True)
+            e_a.record(st)
+            if kind == "audio":
+                if host_audio:
+                    with torch.cuda.stream(st):
+                        clips[:, off:off + n].copy_(h_clips[:, off:off + n], non_blocking=True)
+                for i in range(S):
+                    got = mels[i].feed_dev(clips[i, off:].data_ptr(), n, mel_buf[i, pending[i]].data_ptr(),
+                                           MAX_MEL - pending[i], sp)
+                    pending[i] += got
+            else:   # the stream finish: the zero right pad, then the mel flush
+                for i in range(S):
+                    z = right_pad
+                    while z > 0:
+                        c = min(z, feed)
+                        pending[i] += mels[i].feed_dev(zeros.data_ptr(), c, mel_buf[i, pending[i]].data_ptr(),
+                                                       MAX_MEL - pending[i], sp)
+                        z -= c
+                    pending[i] += mels[i].finish_dev(0, mel_buf[i, pending[i]].data_ptr(), MAX_MEL - pending[i], sp)
+            rows = [0] * S
+            for i in range(S):
+                if pending[i] >= (312 if first[i] else 200) or (kind == "finish" and pending[i] > 0):
+                    rows[i] = stems[i].step_dev(mel_buf[i].data_ptr(), pending[i], enc_buf[i, lo[i]].data_ptr(), sp)
+                    pending[i], first[i] = 0, False
+            act = [i for i in range(S) if rows[i] > 0]
+            if act:
+                V.encoder_step_batch_dev([est[i] for i in act], [enc_buf[i, lo[i]].data_ptr() for i in act],
+                                         [rows[i] for i in act], sp)
+            new_ad = []
+            for i in range(S):
+                have = lo[i] + rows[i]
+                usable = have // 4 * 4
+                if usable:
+                    est[i].adapter_dev(enc_buf[i].data_ptr(), usable, ad_ring[i, total_ad].data_ptr(), sp)
+                    left = have - usable
+                    if left:
+                        with torch.cuda.stream(st):
+                            enc_buf[i, :left].copy_(enc_buf[i, usable:have])
+                    lo[i] = left
+                new_ad.append(usable // 4)
+            assert len(set(new_ad)) == 1, "streams share one schedule"
+            total_ad += new_ad[0]
+            if not started and total_ad >= PROMPT_LEN:
+                for i in range(S):
+                    V.embed_dev(dec, PROMPT_LEN, ad_ring[i].data_ptr(), prompt_tok.data_ptr(),
+                                prompt[i].data_ptr(), sp)
+                st.synchronize()
+                V.prefill_batch(dst, [prompt[i, :PROMPT_LEN - 1].cpu().numpy() for i in range(S)])
+                gen_pos, started = PROMPT_LEN - 1, True
+            while started and gen_pos < total_ad:
+                V.step_batch_tokens_dev(dst, [ad_ring[i, gen_pos].data_ptr() for i in range(S)],
+                                        tokens[steps].data_ptr(), tokens[steps + 1].data_ptr(), sp)
+                steps += 1
+                gen_pos += 1
+            e_b = torch.cuda.Event(enable_timing=True)
+            e_b.record(st)
+            iv_events.append((e_a, e_b))
+        out = tokens[1:steps + 1].cpu() if host_audio else None
+        for m in mels:
+            m.free()
+        return steps, iv_events, out
+
+    run(warm_intervals)        # captures the graphs of every launch shape but the finish's
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(st)
+    steps, ivs, out = run(10 ** 9)
+    e1.record(st)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    dev_ms = e0.elapsed_time(e1)
+    iv_ms = [a.elapsed_time(b) for a, b in ivs]
+    for x in stems:
+        x.free()
+    for x in est:
+        x.free()
+    for x in dst:
+        x.free()
+    sec = wall if host_audio else dev_ms / 1000.0
+    return {
+        "streams": S, "clip_s": clip_s, "interval_s": interval_s, "intervals": len(ivs),
+        "decode_steps_per_stream": steps, "seconds": sec, "device_ms": dev_ms, "wall_s": wall,
+        "tokens_per_s": S * steps / sec, "audio_s_per_s": S * clip_s / sec,
+        "rtf": sec / clip_s,
+        "interval_ms": {"mean": float(np.mean(iv_ms)), "max": float(np.max(iv_ms)),
+                        "first": iv_ms[0], "last": iv_ms[-1]},
+        "h2d_bytes": S * n_samples * 4 if host_audio else 0,
+        "d2h_bytes": S * steps * 4 if host_audio else 0,
+        "timing": ("wall clock, audio copied from pinned host memory per interval, tokens read back"
+                   if host_audio else "CUDA events on the loop's stream, audio resident on the device"),
+    }
+
+
 def bf16_peaks(kind="burst"):
     """(peak TFLOP/s, label): the measured dense bf16 figure, burst (for a
     kernel timed alone) or sustained (for work timed inside a long loop at the
@@ -803,9 +986,24 @@ def our_arm(args):
     ss_res = single_stream_and_attention(V, torch, dec, args.steps)
     for st in states:
         st.free()
+    enc = None if args.no_encoder else build_device_encoder(V, torch)
+    serving = None
+    if enc is not None and not args.no_serving and (args.layers, args.vocab) == (LAYERS, VOCAB):
+        # configs[4] end to end: every rank serves its own streams, no collectives
+        serving = {}
+        for key, host_audio in (("device", False), ("e2e", True)):
+            barrier()
+            r = serving_bench(V, torch, dec, enc, clip_s=args.clip_s, streams=S, seed=4321 + 97 * rank,
+                              host_audio=host_audio)
+            sec = rank_max(r["seconds"])
+            r.update({"seconds_max_over_ranks": sec, "job_tokens_per_s": ws * S * r["decode_steps_per_stream"] / sec,
+                      "job_audio_s_per_s": ws * S * r["clip_s"] / sec, "rtf_max_over_ranks": sec / r["clip_s"]})
+            serving[key] = r
     dec.free()
     up_res = upload_bench(V, torch) if not args.no_encoder else None
-    enc_res = None if args.no_encoder else encoder_bench(V, torch, args.steps, args.enc_rows)
+    enc_res = None if args.no_encoder else encoder_bench(V, torch, args.steps, args.enc_rows, enc=enc)
+    if enc is not None:
+        enc.free()
 
     traffic, traffic_src = ncu_traffic("gemv_tma_kernel_w13_swiglu_8streams")
     line = None
@@ -847,6 +1045,7 @@ def our_arm(args):
             "step_roofline": {"bytes_per_step": step_bytes,
                               "achieved_gbs": step_bytes / (ms_step / 1000.0) / 1e9,
                               "frac": step_bytes / (ms_step / 1000.0) / 1e9 / hbm},
+            "serving": serving,
             "prefill": pf_res,
             "single_stream_decode_and_attention": ss_res,
             "weight_upload": up_res,
@@ -872,6 +1071,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder", action="store_true")
     ap.add_argument("--no-cpu-encoder", action="store_true")
+    ap.add_argument("--no-serving", action="store_true")
+    ap.add_argument("--clip-s", type=float, default=60.0)   # serving: seconds of audio per stream
     # encoder-only / single chunk size, for small ncu captures
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--prefill-only", action="store_true")

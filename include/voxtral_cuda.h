@@ -133,6 +133,14 @@ typedef struct vox_cuda_dec_state vox_cuda_dec_state; /* one stream: KV ring + s
 vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights *w);
 void vox_cuda_decoder_free(vox_cuda_decoder *d);
 
+/* Replace the per-layer ada scale (host [n_layers][3072], or NULL for none)
+ * after vox_set_delay recomputed it (voxtral.c:1344-1350, 46-79).  The scale
+ * is folded into the FFN norm weights on the device (ffn_norm * (1 + ada),
+ * voxtral_decoder.c:488-492), so only those 26 x 3072 floats are rewritten:
+ * no weight re-upload.  The decoder's states share the new scale from their
+ * next step on; steps already queued finish with the old one. */
+int vox_cuda_decoder_set_ada_scale(vox_cuda_decoder *d, const float *ada_scale);
+
 /* Per-stream state: device KV ring of kv_cap positions per layer (>= 8192 to
  * hold the full sliding window; the reference preallocates 8192+1024,
  * voxtral.c:233).  Replaces kv_cache_init / vox_decoder_kv_cache_preallocate
@@ -225,6 +233,29 @@ int vox_cuda_decoder_step_batch_ex(vox_cuda_dec_state *const *states, int n, con
  * its states is ordered after the pending asynchronous steps. */
 int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states, int n,
                                     const float *embeds_dev, int *tokens_dev, void *stream);
+
+/* The stream loop's decode step on the device (stream_run_decoder,
+ * voxtral.c:893-921: step_embed = adapter[gen_pos] + tok_embed(prev_token)):
+ * stream i's input row is rows_dev[i] (a device pointer to its [3072] adapter
+ * row; rows_dev itself is a host array of n pointers) plus the bf16 token
+ * embedding of prev_tokens_dev[i] (device int32, e.g. the tokens_dev of the
+ * previous call), added on the device.  Tokens land in tokens_dev [n]; no
+ * token or embedding crosses to the host, so a serving loop can enqueue its
+ * steps back to back.  Asynchronous as vox_cuda_decoder_step_batch_dev.  An id
+ * outside [0, vocab) adds no embedding and is reported as an error by a later
+ * call. */
+int vox_cuda_decoder_step_batch_tokens_dev(vox_cuda_dec_state *const *states, int n,
+                                           const float *const *rows_dev,
+                                           const int *prev_tokens_dev, int *tokens_dev,
+                                           void *stream);
+
+/* out_dev[i] = rows_dev[i] + tok_embed(tokens_dev[i]) for i < n ([n][3072]
+ * fp32, device pointers; rows_dev may be NULL for the plain lookup): the
+ * prompt rows of a stream start (voxtral.c:846-851, BOS / STREAMING_PAD
+ * embeddings added to the adapter rows) without the bf16 table on the host.
+ * Enqueued on `stream` (NULL: the library's stream). */
+int vox_cuda_decoder_embed_dev(vox_cuda_decoder *d, int n, const float *rows_dev, const int *tokens_dev,
+                               float *out_dev, void *stream);
 
 /* Per-phase device time of the batched step, for profiling (the CUDA-event
  * phase timers the reference keeps with gettimeofday, voxtral.c:679-680,
@@ -345,6 +376,14 @@ int vox_cuda_encoder_profile(vox_cuda_enc_state *s, const float *x_dev, int new_
  * Linear(3072->3072); host enc [n, 1280] -> out [n/4, 3072]
  * (vox_adapter_forward, voxtral_encoder.c:642-674). */
 int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc, int n, float *out);
+
+/* Device-resident form: enc_dev [n, 1280] -> out_dev [n/4, 3072] (device
+ * pointers), enqueued on `stream` (NULL: the library's stream) without a host
+ * wait, ordered after the state's earlier asynchronous work (it shares the
+ * state's workspace).  A device-side wait that timed out is reported by a later
+ * call on the state. */
+int vox_cuda_adapter_forward_dev(vox_cuda_enc_state *s, const float *enc_dev, int n, float *out_dev,
+                                 void *stream);
 
 /* Conv stem: the encoder's two causal convolutions over the mel stream,
  * conv0 (128 -> 1280, kernel 3, stride 1) and conv1 (1280 -> 1280, kernel 3,

@@ -107,10 +107,40 @@ def ref_available():
     return os.path.exists(REF_SO)
 
 
+HOST_CUDA_SO = os.path.join(HERE, "..", "integration", "_build", "libvoxhost_cuda.so")
+_host_cuda = None
+
+
+def host_cuda_available():
+    return os.path.exists(HOST_CUDA_SO)
+
+
+def host_cuda_lib():
+    """The reference host built as `make cuda` (integration/Makefile): its own
+    sources with the USE_CUDA hooks, linked to libvoxtral_cuda.so, plus the
+    ref_shim.c test entry points.  Same functions as ref_lib(), and
+    vox_cuda_init / vox_cuda_host_attach / vox_cuda_host_detach / vox_set_delay."""
+    global _host_cuda
+    if _host_cuda is None:
+        lib = _setup_ref(C.CDLL(HOST_CUDA_SO))
+        lib.vox_cuda_init.restype = C.c_int
+        lib.vox_cuda_last_error.restype = C.c_char_p
+        lib.vox_cuda_host_attach.argtypes = [C.c_void_p]
+        lib.vox_cuda_host_attach.restype = C.c_int
+        lib.vox_cuda_host_detach.argtypes = [C.c_void_p]
+        _host_cuda = lib
+    return _host_cuda
+
+
 def ref_lib():
     global _ref
     if _ref is None:
-        lib = C.CDLL(REF_SO)
+        _ref = _setup_ref(C.CDLL(REF_SO))
+    return _ref
+
+
+def _setup_ref(lib):
+    if True:
         lib.vox_linear_nobias_bf16.argtypes = [_fp, _fp, _u16p, C.c_int, C.c_int, C.c_int]
         lib.vox_linear_bf16.argtypes = [_fp, _fp, _u16p, _fp, C.c_int, C.c_int, C.c_int]
         lib.vox_matmul_t_bf16.argtypes = [_fp, _fp, _u16p, C.c_int, C.c_int, C.c_int]
@@ -128,6 +158,7 @@ def ref_lib():
         lib.voxref_set_ada_mlp.argtypes = [C.c_void_p, C.c_int, _fp, _fp]
         lib.voxref_time_conditioning.argtypes = [C.c_void_p, C.c_int]
         lib.voxref_time_conditioning.restype = _fp
+        lib.vox_set_delay.argtypes = [C.c_void_p, C.c_int]
         lib.voxref_decoder_forward.argtypes = [C.c_void_p, _fp, _fp]
         lib.voxref_decoder_forward.restype = C.c_int
         lib.voxref_decoder_prefill.argtypes = [C.c_void_p, _fp, C.c_int]
@@ -167,8 +198,7 @@ def ref_lib():
         lib.voxref_stem_step.argtypes = [C.c_void_p, _fp, C.c_int, _fp]
         lib.voxref_stem_step.restype = C.c_int
         lib.voxref_stem_free.argtypes = [C.c_void_p]
-        _ref = lib
-    return _ref
+    return lib
 
 
 # ---------------------------------------------------------------------------
@@ -534,10 +564,10 @@ class OracleEncoder:
 class RefCtx:
     """A reference vox_ctx_t over caller-owned synthetic weights."""
 
-    def __init__(self, dec: DecoderWeights | None = None, enc: EncoderWeights | None = None):
+    def __init__(self, dec: DecoderWeights | None = None, enc: EncoderWeights | None = None, lib=None):
         assert dec is None or (dec.n_layers == DEC_LAYERS and dec.vocab == VOCAB)
         assert enc is None or enc.n_layers == ENC_LAYERS
-        lib = ref_lib()
+        lib = lib or ref_lib()
         self.lib = lib
         self.ctx = lib.voxref_ctx_new()
         self.dec, self.enc = dec, enc

@@ -502,3 +502,109 @@ def test_tc_prefill_across_the_ring_wrap(small_w, monkeypatch):
     sb.free()
     a.free()
     b.free()
+
+
+# ---------------------------------------------------------------------------
+# the stream loop's device-resident step: adapter row + token embedding
+# ---------------------------------------------------------------------------
+
+def test_token_embedding_steps_match_host_embedded_steps(small_w):
+    """vox_cuda_decoder_step_batch_tokens_dev builds each stream's input as
+    adapter_row + tok_embed(prev_token) on the device (voxtral.c:898-906) and
+    feeds its own tokens back: the tokens and ring rows equal those of
+    step_batch with the same rows embedded on the host, and
+    vox_cuda_decoder_embed_dev equals the host lookup."""
+    import torch
+    d = make_gpu_decoder(small_w)
+    n, steps = 4, 5
+    prompts = [B.normal_f32((3 + i, B.DEC_DIM), 1500 + i) for i in range(n)]
+    host_states, dev_states = [], []
+    for i in range(n):
+        for lst in (host_states, dev_states):
+            st = d.state(kv_cap=64)
+            st.prefill(prompts[i])
+            lst.append(st)
+    adapter = B.normal_f32((steps, n, B.DEC_DIM), 1510, 1.0)
+    first = np.array([5, 999, small_w.vocab - 1, 1234], np.int32)
+    # host: embeds = adapter + tok_emb[prev] from the bf16 table
+    want, prev = [], first.copy()
+    for s in range(steps):
+        e = adapter[s] + B.bf16_to_f32(small_w.tok_emb[prev])
+        toks = V.step_batch(host_states, e)
+        want.append(toks)
+        prev = np.array(toks, np.int32)
+    # device: the same, tokens never leave the device
+    dev_adapter = torch.from_numpy(adapter).cuda()
+    toks_dev = [torch.from_numpy(first).cuda()] + [torch.zeros(n, dtype=torch.int32, device="cuda")
+                                                   for _ in range(steps)]
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    for s in range(steps):
+        rows = [dev_adapter[s, i].data_ptr() for i in range(n)]
+        V.step_batch_tokens_dev(dev_states, rows, toks_dev[s].data_ptr(), toks_dev[s + 1].data_ptr(),
+                                stream.cuda_stream)
+    stream.synchronize()
+    for s in range(steps):
+        assert toks_dev[s + 1].cpu().tolist() == want[s], s
+    for i in range(n):
+        last = 3 + i + steps - 1
+        k1, v1 = host_states[i].read_kv(small_w.n_layers - 1, last - steps + 1, steps)
+        k2, v2 = dev_states[i].read_kv(small_w.n_layers - 1, last - steps + 1, steps)
+        assert np.array_equal(k1, k2) and np.array_equal(v1, v2), i
+    # the plain lookup and the lookup added to rows
+    tok = torch.tensor([0, 1, 32, small_w.vocab - 1, 4097], dtype=torch.int32, device="cuda")
+    out = torch.empty((5, B.DEC_DIM), dtype=torch.float32, device="cuda")
+    V.embed_dev(d, 5, None, tok.data_ptr(), out.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), B.bf16_to_f32(small_w.tok_emb[tok.cpu().numpy()]))
+    base = torch.from_numpy(B.normal_f32((5, B.DEC_DIM), 1520, 1.0)).cuda()
+    V.embed_dev(d, 5, base.data_ptr(), tok.data_ptr(), out.data_ptr())
+    torch.cuda.synchronize()
+    want_rows = base.cpu().numpy() + B.bf16_to_f32(small_w.tok_emb[tok.cpu().numpy()])
+    assert np.array_equal(out.cpu().numpy(), want_rows)
+    for st in host_states + dev_states:
+        st.free()
+    d.free()
+
+
+def test_token_embedding_step_rejects_out_of_vocab_ids(small_w):
+    """An id outside [0, vocab) is not read: the step reports an argument
+    error at the next call, and the context keeps working."""
+    import torch
+    d = make_gpu_decoder(small_w)
+    st = d.state(kv_cap=64)
+    st.prefill(B.normal_f32((3, B.DEC_DIM), 1530))
+    row = torch.from_numpy(B.normal_f32(B.DEC_DIM, 1531, 1.0)).cuda()
+    bad = torch.tensor([small_w.vocab + 7], dtype=torch.int32, device="cuda")
+    out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    V.step_batch_tokens_dev([st], [row.data_ptr()], bad.data_ptr(), out.data_ptr())
+    torch.cuda.synchronize()
+    with pytest.raises(V.VoxCudaError):
+        V.step_batch([st], B.normal_f32((1, B.DEC_DIM), 1532))
+    tok = V.step_batch([st], B.normal_f32((1, B.DEC_DIM), 1533))
+    assert 0 <= tok[0] < small_w.vocab
+    st.free()
+    d.free()
+
+
+def test_set_ada_scale_equals_a_decoder_created_with_it(small_w):
+    """vox_cuda_decoder_set_ada_scale rewrites only the folded FFN norm: a
+    decoder created with scale A then switched to B gives the logits of one
+    created with B."""
+    import copy
+    wb = copy.copy(small_w)
+    wb.ada_scale = B.normal_f32((small_w.n_layers, B.DEC_DIM), 1540, 0.1)
+    a = make_gpu_decoder(small_w)
+    b = make_gpu_decoder(wb)
+    a.set_ada_scale(wb.ada_scale)
+    prompt = B.normal_f32((4, B.DEC_DIM), 1541)
+    e = B.normal_f32(B.DEC_DIM, 1542)
+    out = []
+    for dec in (a, b):
+        st = dec.state(kv_cap=64)
+        st.prefill(prompt)
+        out.append(st.step(e))
+        st.free()
+    assert out[0][0] == out[1][0] and np.array_equal(out[0][1], out[1][1])
+    a.free()
+    b.free()

@@ -42,7 +42,8 @@ def gpu_front_end(x_unused=None):
     chunks = G.front_stem_chunks(feed_frames, fin)
     all_mel = np.concatenate(parts, axis=0)
     stem = V.ConvStem(cw.w0, cw.b0, cw.w1, cw.b1, max_mel=max(chunks))
-    st = enc.state(max_chunk=max(chunks) // 2 + 2)
+    st_rows = max(chunks) // 2 + 2
+    st = enc.state(max_chunk=st_rows)
     outs, off = [], 0
     for n in chunks:
         conv = stem.step(all_mel[off:off + n])
@@ -51,7 +52,8 @@ def gpu_front_end(x_unused=None):
             outs.append(st.step(conv))
     enc_out = np.concatenate(outs, axis=0)
     usable = enc_out.shape[0] // 4 * 4
-    ad = st.adapter(enc_out[:usable])
+    piece = st_rows // 4 * 4    # the adapter's rows per call fit the state's workspace
+    ad = np.concatenate([st.adapter(enc_out[r:min(r + piece, usable)]) for r in range(0, usable, piece)], axis=0)
     st.free()
     stem.free()
     enc.free()

@@ -319,3 +319,20 @@ def test_encoder_ring_wraps_match_oracle():
     assert st.position == pos
     st.free()
     e.free()
+
+
+def test_adapter_dev_matches_host_adapter(gpu_enc):
+    """vox_cuda_adapter_forward_dev (device rows in and out, asynchronous)
+    gives the host entry point's rows bit for bit."""
+    import torch
+    st = gpu_enc.state(max_chunk=256)
+    enc = B.normal_f32((200, B.ENC_DIM), 1600, 1.0)
+    want = st.adapter(enc)
+    d_in = torch.from_numpy(enc).cuda()
+    d_out = torch.empty((50, B.DEC_DIM), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    st.adapter_dev(d_in.data_ptr(), 200, d_out.data_ptr(), stream.cuda_stream)
+    stream.synchronize()
+    assert np.array_equal(d_out.cpu().numpy(), want)
+    st.free()

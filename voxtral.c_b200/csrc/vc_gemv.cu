@@ -622,4 +622,45 @@ cudaError_t launch_tile_weights(uint16_t *dst, const uint16_t *src, int N, int K
     return cudaGetLastError();
 }
 
+// One thread per pair of columns (k, k+1) of one row: the pair is one 32-bit
+// word of the tiled layout (the inverse of tile_weights_kernel's mapping).
+__global__ void embed_tokens_kernel(float *x, const float *const *row_ptrs, const float *rows, size_t row_stride,
+                                    const int *tokens, int n, const uint16_t *E, int vocab, int K,
+                                    unsigned *err) {
+    const int m = blockIdx.y;
+    const int k = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (m >= n || k >= K) return;
+    const int tok = tokens[m];
+    const bool valid = tok >= 0 && tok < vocab;
+    float e0 = 0.f, e1 = 0.f;
+    if (valid) {
+        const int KB = (K + 15) >> 4;
+        const int t = (tok >> 4) & 3, rr = tok & 15, g = rr & 7, hi = rr >> 3;
+        const int kb = k >> 4, kk = k & 15, q = (kk & 7) >> 1, khalf = kk >> 3;
+        const size_t word = ((((size_t)(tok >> 6) * KB + kb) * 4 + t) * 32 + g * 4 + q) * 4 + khalf * 2 + hi;
+        const uint32_t v = reinterpret_cast<const uint32_t *>(E)[word];
+        e0 = __uint_as_float(v << 16);
+        e1 = __uint_as_float(v & 0xffff0000u);
+    } else if (k == 0 && err) {
+        atomicOr(err, 2u);
+    }
+    const float *r = row_ptrs ? row_ptrs[m] : (rows ? rows + (size_t)m * row_stride : nullptr);
+    float a0 = 0.f, a1 = 0.f;
+    if (r) {
+        a0 = r[k];
+        if (k + 1 < K) a1 = r[k + 1];
+    }
+    x[(size_t)m * K + k] = a0 + e0;
+    if (k + 1 < K) x[(size_t)m * K + k + 1] = a1 + e1;
+}
+
+cudaError_t launch_embed_tokens(float *x, const float *const *row_ptrs, const float *rows, size_t row_stride,
+                                const int *tokens, int n, const uint16_t *E, int vocab, int K,
+                                unsigned *err, cudaStream_t st) {
+    if (n <= 0 || K <= 0 || (K & 1)) return cudaErrorInvalidValue;
+    dim3 grid((K / 2 + 255) / 256, n);
+    embed_tokens_kernel<<<grid, 256, 0, st>>>(x, row_ptrs, rows, row_stride, tokens, n, E, vocab, K, err);
+    return cudaGetLastError();
+}
+
 }  // namespace vc

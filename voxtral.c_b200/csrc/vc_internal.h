@@ -75,6 +75,14 @@ constexpr int kGemvRowAlign = 64;           // tiled weights are padded to this 
 // (Np = N rounded up to kGemvRowAlign, Kp = K rounded up to 16).
 cudaError_t launch_tile_weights(uint16_t *dst, const uint16_t *src, int N, int K, int Np, int Kp,
                                 cudaStream_t st);
+// x[m][k] = rows_m[k] + E[tokens[m]][k] for m < n, k < K, with E [vocab, K]
+// bf16 in the fragment-tiled layout above.  Row m of the addend is
+// row_ptrs[m] (a device array of n pointers) when row_ptrs is given, else
+// rows + m * row_stride, else nothing (a plain lookup).  A token outside
+// [0, vocab) adds no embedding and sets bit 1 of *err.
+cudaError_t launch_embed_tokens(float *x, const float *const *row_ptrs, const float *rows, size_t row_stride,
+                                const int *tokens, int n, const uint16_t *E, int vocab, int K,
+                                unsigned *err, cudaStream_t st);
 
 struct AttnParams {
     const float *q;           // [M][4096], RoPE applied

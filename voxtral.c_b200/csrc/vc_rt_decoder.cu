@@ -37,6 +37,7 @@ struct StepWork {
     size_t dblock_bytes = 0;
     StreamSlot *slots = nullptr;
     float *rope = nullptr;             // [n][128]
+    const float **rows = nullptr;      // [n] addend rows of the token-embedding steps
     float *x = nullptr;                // [n][3072] residual stream
     float *q = nullptr, *att = nullptr;  // [n][4096]
     float *h = nullptr;                // [n][9216]
@@ -113,6 +114,7 @@ struct vox_cuda_decoder {
     bool tail_set = false;
     bool tc_prefill = false;      // row-major weights kept: prefill on the tensor cores
     PrefillTc *pf = nullptr;
+    std::vector<float> ffn_norm;  // [n_layers][3072] host copy: g_ffn is recomputed when ada changes
 };
 
 struct vox_cuda_dec_state {
@@ -157,6 +159,7 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     };
     const size_t o_slots = take(sizeof(StreamSlot) * n);
     const size_t o_rope = take(sizeof(float) * n * kHeadDim);
+    const size_t o_rows = take(sizeof(float *) * n);
     const size_t o_x = take(sizeof(float) * n * kDecDim);
     w->dblock_bytes = o_x + sizeof(float) * n * kDecDim;   // the uploaded prefix
     const size_t o_q = take(sizeof(float) * n * kQDim);
@@ -188,6 +191,7 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     char *b = w->dblock;
     w->slots = (StreamSlot *)(b + o_slots);
     w->rope = (float *)(b + o_rope);
+    w->rows = (const float **)(b + o_rows);
     w->x = (float *)(b + o_x);
     w->q = (float *)(b + o_q);
     w->att = (float *)(b + o_att);
@@ -226,6 +230,7 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
 StreamSlot *h_slots(StepWork *w) { return (StreamSlot *)w->hblock; }
 float *h_rope(StepWork *w) { return (float *)(w->hblock + ((char *)w->rope - w->dblock)); }
 float *h_x(StepWork *w) { return (float *)(w->hblock + ((char *)w->x - w->dblock)); }
+const float **h_rows(StepWork *w) { return (const float **)(w->hblock + ((char *)w->rows - w->dblock)); }
 
 // Bytes of a decode weight matrix [N, K] in the tiled layout.
 size_t tiled_bytes(int N, int K) { return (size_t)round_up(N, kGemvRowAlign) * round_up(K, 16) * 2; }
@@ -395,9 +400,14 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
 // The error word copied back after the tokens: a device-side bounded wait
 // expired during the step.
 int check_step_error(StepWork *w, cudaStream_t st) {
-    if (w->h_tokens[w->n] == 0) return VOX_CUDA_OK;
+    const unsigned e = (unsigned)w->h_tokens[w->n];
+    if (e == 0) return VOX_CUDA_OK;
     w->h_tokens[w->n] = 0;
     cudaMemsetAsync(w->err, 0, sizeof(unsigned), st);
+    if (e == 2u) {   // launch_embed_tokens: an id outside the vocabulary
+        set_error("decoder step: a previous token id was outside [0, vocab) (its embedding was skipped)");
+        return VOX_CUDA_ERR_ARG;
+    }
     set_error("decoder step: a device-side wait timed out (results discarded)");
     return VOX_CUDA_ERR_CUDA;
 }
@@ -795,6 +805,7 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
         };
         fetch(ha.data(), L.attention_norm);
         fetch(hf.data(), L.ffn_norm);
+        d->ffn_norm.insert(d->ffn_norm.end(), hf.begin(), hf.end());
         if (w->ada_scale) fetch(hada.data(), w->ada_scale + (size_t)l * D);
         for (size_t i = 0; i < D; i++) hf[i] = hf[i] * (1.0f + hada[i]);
         float *g = (float *)alloc(2 * D * 4);
@@ -825,6 +836,31 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
         return nullptr;
     }
     return d;
+}
+
+extern "C" int vox_cuda_decoder_set_ada_scale(vox_cuda_decoder *d, const float *ada_scale) {
+    if (!d || d->ffn_norm.size() != (size_t)d->n_layers * kDecDim) {
+        set_error("decoder_set_ada_scale: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    DevCtx *c = ctx_for(d->device);
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(d->device);
+    // the g_ffn vectors are read by every step and prefill: the update is
+    // ordered after the pending ones on the library stream (which the
+    // asynchronous steps join) and completes before this call returns
+    std::lock_guard<std::mutex> lk(d->mu);
+    std::vector<float> g((size_t)d->n_layers * kDecDim);
+    for (int l = 0; l < d->n_layers; l++)
+        for (int i = 0; i < kDecDim; i++) {
+            const size_t j = (size_t)l * kDecDim + i;
+            g[j] = d->ffn_norm[j] * (1.0f + (ada_scale ? ada_scale[j] : 0.0f));
+        }
+    VC_TRY(cudaStreamSynchronize(c->stream));
+    for (int l = 0; l < d->n_layers; l++)
+        VC_TRY(cudaMemcpy((void *)d->L[l].g_ffn, g.data() + (size_t)l * kDecDim, kDecDim * sizeof(float),
+                          cudaMemcpyHostToDevice));
+    return VOX_CUDA_OK;
 }
 
 extern "C" void vox_cuda_decoder_free(vox_cuda_decoder *d) {
@@ -1200,17 +1236,13 @@ extern "C" int vox_cuda_decoder_step_batch(vox_cuda_dec_state *const *states, in
     return vox_cuda_decoder_step_batch_ex(states, n, embeds, nullptr, tokens, nullptr);
 }
 
-extern "C" int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states, int n,
-                                               const float *embeds_dev, int *tokens_dev,
-                                               void *stream) {
-    if (!embeds_dev || !tokens_dev) {
-        set_error("decoder_step_batch_dev: bad arguments");
-        return VOX_CUDA_ERR_ARG;
-    }
-    if (((uintptr_t)embeds_dev & 3u) || ((uintptr_t)tokens_dev & 3u)) {
-        set_error("decoder_step_batch_dev: misaligned device pointers");
-        return VOX_CUDA_ERR_ARG;
-    }
+// The asynchronous batched step.  The step's input rows x come either from
+// embeds_dev ([n][3072], copied), or - token-embedding steps - from
+// rows[i] + E[prev_tokens_dev[i]] (E the tiled LM head / token table), built
+// on the device by one kernel ahead of the step's graph.
+static int step_batch_async(vox_cuda_dec_state *const *states, int n, const float *embeds_dev,
+                            const float *const *rows, const int *prev_tokens_dev, int *tokens_dev,
+                            void *stream, const char *what) {
     vox_cuda_decoder *d = nullptr;
     DevCtx *c = nullptr;
     if (!states || n <= 0 || n > kMaxBatch || !states[0]) return batch_prepare(states, n, &d, &c);
@@ -1226,17 +1258,24 @@ extern "C" int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states
         if ((rc = check_step_error(w, st))) return rc;
     }
     if (!d->tail && cudaEventCreateWithFlags(&d->tail, cudaEventDisableTiming) != cudaSuccess) {
-        set_error("decoder_step_batch_dev: event creation failed");
+        set_error("%s: event creation failed", what);
         return VOX_CUDA_ERR_CUDA;
     }
     // the previous asynchronous step may have run on another stream
     if (d->tail_set && st != c->stream) VC_TRY(cudaStreamWaitEvent(st, d->tail, 0));
-    // slots + rope tables from the host block; the embeddings from the device
+    // slots, rope tables and row addresses from the host block; the step's
+    // input rows from the device
+    if (rows)
+        for (int i = 0; i < n; i++) h_rows(w)[i] = rows[i];
     const size_t head = (char *)w->x - w->dblock;
     VC_TRY(cudaMemcpyAsync(w->dblock, w->hblock, head, cudaMemcpyHostToDevice, st));
     VC_TRY(cudaEventRecord(w->staged, st));
     w->staged_pending = true;
-    VC_TRY(cudaMemcpyAsync(w->x, embeds_dev, (size_t)n * kDecDim * 4, cudaMemcpyDeviceToDevice, st));
+    if (prev_tokens_dev)
+        VC_TRY(launch_embed_tokens(w->x, w->rows, nullptr, 0, prev_tokens_dev, n, d->tok_emb, d->vocab, kDecDim,
+                                   w->err, st));
+    else
+        VC_TRY(cudaMemcpyAsync(w->x, embeds_dev, (size_t)n * kDecDim * 4, cudaMemcpyDeviceToDevice, st));
     cudaGraphExec_t &g = w->graph[1];
     if (!g) {
         cudaGraph_t graph = nullptr;
@@ -1268,6 +1307,58 @@ extern "C" int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states
         states[i]->pos += 1;
         states[i]->have_logits = false;
     }
+    return VOX_CUDA_OK;
+}
+
+extern "C" int vox_cuda_decoder_step_batch_dev(vox_cuda_dec_state *const *states, int n,
+                                               const float *embeds_dev, int *tokens_dev,
+                                               void *stream) {
+    if (!embeds_dev || !tokens_dev) {
+        set_error("decoder_step_batch_dev: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (((uintptr_t)embeds_dev & 3u) || ((uintptr_t)tokens_dev & 3u)) {
+        set_error("decoder_step_batch_dev: misaligned device pointers");
+        return VOX_CUDA_ERR_ARG;
+    }
+    return step_batch_async(states, n, embeds_dev, nullptr, nullptr, tokens_dev, stream,
+                            "decoder_step_batch_dev");
+}
+
+extern "C" int vox_cuda_decoder_step_batch_tokens_dev(vox_cuda_dec_state *const *states, int n,
+                                                      const float *const *rows_dev,
+                                                      const int *prev_tokens_dev, int *tokens_dev,
+                                                      void *stream) {
+    if (!rows_dev || !prev_tokens_dev || !tokens_dev) {
+        set_error("decoder_step_batch_tokens_dev: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    if (((uintptr_t)prev_tokens_dev & 3u) || ((uintptr_t)tokens_dev & 3u)) {
+        set_error("decoder_step_batch_tokens_dev: misaligned device pointers");
+        return VOX_CUDA_ERR_ARG;
+    }
+    for (int i = 0; i < n && i < kMaxBatch; i++)
+        if (!rows_dev[i] || ((uintptr_t)rows_dev[i] & 7u)) {
+            set_error("decoder_step_batch_tokens_dev: row %d is NULL or misaligned", i);
+            return VOX_CUDA_ERR_ARG;
+        }
+    return step_batch_async(states, n, nullptr, rows_dev, prev_tokens_dev, tokens_dev, stream,
+                            "decoder_step_batch_tokens_dev");
+}
+
+extern "C" int vox_cuda_decoder_embed_dev(vox_cuda_decoder *d, int n, const float *rows_dev,
+                                          const int *tokens_dev, float *out_dev, void *stream) {
+    if (!d || n <= 0 || !tokens_dev || !out_dev || ((uintptr_t)tokens_dev & 3u) ||
+        ((uintptr_t)out_dev & 7u) || ((uintptr_t)rows_dev & 7u)) {
+        set_error("decoder_embed_dev: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    DevCtx *c = ctx_for(d->device);
+    if (!c) return VOX_CUDA_ERR_UNAVAILABLE;
+    cudaSetDevice(d->device);
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    VC_TRY(launch_embed_tokens(out_dev, nullptr, rows_dev, kDecDim, tokens_dev, n, d->tok_emb, d->vocab,
+                               kDecDim, nullptr, st));
     return VOX_CUDA_OK;
 }
 

@@ -813,20 +813,15 @@ extern "C" int vox_cuda_encoder_step_batch_dev(vox_cuda_enc_state *const *states
     return VOX_CUDA_OK;
 }
 
-extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc, int n, float *out) {
-    int rc = enc_check(s, n);
-    if (rc) return rc;
-    if (!enc || !out || n % 4 != 0) {
-        set_error("adapter_forward: n must be a positive multiple of 4");
-        return VOX_CUDA_ERR_ARG;
-    }
-    DevCtx *c = ctx_for(s->enc->device);
-    cudaStream_t st = c->stream;
+namespace {
+
+// Adapter over n encoder rows already on the device (enc_dev [n][1280]) into
+// out_dev [n/4][3072] fp32, on stream st: 4x stacking (4 consecutive [1280]
+// rows are one [5120] row: the same memory), Linear + GELU, Linear.
+int enqueue_adapter(vox_cuda_enc_state *s, const float *enc_dev, int n, float *out_dev, cudaStream_t st) {
     vox_cuda_encoder *e = s->enc;
     const int rows = n / 4, K0 = 4 * kEncDim;
-    // 4 consecutive [1280] rows are one [5120] row: the same memory
-    VC_TRY(cudaMemcpyAsync(s->x, enc, (size_t)n * kEncDim * 4, cudaMemcpyHostToDevice, st));
-    VC_TRY(launch_rows_to_bf16(s->x, rows, K0, K0, nullptr, s->a16, st, false, true));
+    VC_TRY(launch_rows_to_bf16(enc_dev, rows, K0, K0, nullptr, s->a16, st, false, true));
     TcGemmParams p = {};
     p.M = rows;
     p.N = kDecDim;
@@ -844,7 +839,7 @@ extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc,
     p.M = rows;
     p.N = kDecDim;
     p.K = kDecDim;
-    p.out = s->aout;
+    p.out = out_dev;
     p.ldo = kDecDim;
     p.err = s->err;
     p.f16 = 1;
@@ -852,8 +847,50 @@ extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc,
     p.ws_floats = kEncSplitFloats;
     p.ws_cnt = s->split_cnt;
     VC_TRY(launch_tc_gemm(TC_STORE, p, s->mid16, e->adapter1, st, false));
-    VC_TRY(cudaMemcpyAsync(out, s->aout, (size_t)rows * kDecDim * 4, cudaMemcpyDeviceToHost, st));
+    return VOX_CUDA_OK;
+}
+
+int adapter_check(vox_cuda_enc_state *s, const void *enc, int n, const void *out) {
+    int rc = enc_check(s, n);
+    if (rc) return rc;
+    if (!enc || !out || n % 4 != 0) {
+        set_error("adapter_forward: n must be a positive multiple of 4");
+        return VOX_CUDA_ERR_ARG;
+    }
+    return VOX_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc, int n, float *out) {
+    int rc = adapter_check(s, enc, n, out);
+    if (rc) return rc;
+    DevCtx *c = ctx_for(s->enc->device);
+    cudaStream_t st = c->stream;
+    VC_TRY(cudaMemcpyAsync(s->x, enc, (size_t)n * kEncDim * 4, cudaMemcpyHostToDevice, st));
+    if ((rc = enqueue_adapter(s, s->x, n, s->aout, st))) return rc;
+    VC_TRY(cudaMemcpyAsync(out, s->aout, (size_t)(n / 4) * kDecDim * 4, cudaMemcpyDeviceToHost, st));
     return enc_err_check(s, st);
+}
+
+extern "C" int vox_cuda_adapter_forward_dev(vox_cuda_enc_state *s, const float *enc_dev, int n, float *out_dev,
+                                            void *stream) {
+    int rc = adapter_check(s, enc_dev, n, out_dev);
+    if (rc) return rc;
+    DevCtx *c = ctx_for(s->enc->device);
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    // the state's workspace may still be in use by its asynchronous chunk
+    if (s->tail_set && st != c->stream) VC_TRY(cudaStreamWaitEvent(st, s->tail, 0));
+    if ((rc = enqueue_adapter(s, enc_dev, n, out_dev, st))) return rc;
+    if (!s->err_pending) {   // one flag copy in flight at a time
+        VC_TRY(cudaMemcpyAsync(s->h_err, s->err, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+        VC_TRY(cudaEventRecord(s->err_ev, st));
+        s->err_pending = true;
+    }
+    VC_TRY(cudaEventRecord(s->tail, st));
+    if (st != c->stream) VC_TRY(cudaStreamWaitEvent(c->stream, s->tail, 0));
+    s->tail_set = true;
+    return VOX_CUDA_OK;
 }
 
 extern "C" int vox_cuda_enc_state_set_position(vox_cuda_enc_state *s, int logical_pos) {

@@ -102,6 +102,12 @@ def lib():
         "vox_cuda_decoder_prefill_batch": ([C.c_void_p, C.c_int, _fp, _ip, _fp], C.c_int),
         "vox_cuda_decoder_step_batch": ([C.c_void_p, C.c_int, _fp, _ip], C.c_int),
         "vox_cuda_decoder_step_batch_ex": ([C.c_void_p, C.c_int, _fp, _fp, _ip, _fp], C.c_int),
+        "vox_cuda_decoder_set_ada_scale": ([C.c_void_p, _fp], C.c_int),
+        "vox_cuda_decoder_step_batch_tokens_dev": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                    C.c_void_p], C.c_int),
+        "vox_cuda_decoder_embed_dev": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p],
+                                       C.c_int),
+        "vox_cuda_adapter_forward_dev": ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
         "vox_cuda_decoder_step_batch_dev": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                              C.c_void_p], C.c_int),
         "vox_cuda_decoder_profile_batch": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, _fp],
@@ -223,6 +229,10 @@ class Decoder:
     def state(self, kv_cap=8192 + 1024):
         return DecState(self, kv_cap)
 
+    def set_ada_scale(self, ada_scale):
+        ada = None if ada_scale is None else np.ascontiguousarray(ada_scale, np.float32)
+        check(lib().vox_cuda_decoder_set_ada_scale(self.h, _f(ada)), "set_ada_scale")
+
     def free(self):
         if self.h:
             lib().vox_cuda_decoder_free(self.h)
@@ -335,6 +345,20 @@ def step_batch_dev(states, embeds_dev, tokens_dev, stream=None):
           "step_batch_dev")
 
 
+def step_batch_tokens_dev(states, row_ptrs, prev_tokens_dev, tokens_dev, stream=None):
+    """Token-embedding batched step: row_ptrs is a list of n device addresses
+    (each stream's [3072] adapter row); prev_tokens_dev / tokens_dev int32
+    device addresses."""
+    rows = (C.c_void_p * len(states))(*row_ptrs)
+    check(lib().vox_cuda_decoder_step_batch_tokens_dev(states_array(states), len(states), rows,
+                                                       prev_tokens_dev, tokens_dev, stream),
+          "step_batch_tokens_dev")
+
+
+def embed_dev(dec, n, rows_dev, tokens_dev, out_dev, stream=None):
+    check(lib().vox_cuda_decoder_embed_dev(dec.h, n, rows_dev, tokens_dev, out_dev, stream), "embed_dev")
+
+
 def profile_batch(states, embeds_dev, iters=3):
     """Mean ms per step of each phase (PROF_PHASES) of the batched step."""
     ms = np.zeros(len(PROF_PHASES), np.float32)
@@ -424,6 +448,9 @@ class EncState:
 
     def set_position(self, pos):
         check(lib().vox_cuda_enc_state_set_position(self.h, pos), "enc_state_set_position")
+
+    def adapter_dev(self, enc_dev, n, out_dev, stream=None):
+        check(lib().vox_cuda_adapter_forward_dev(self.h, enc_dev, n, out_dev, stream), "adapter_forward_dev")
 
     def step_dev(self, x_dev, n, stream=None):
         check(lib().vox_cuda_encoder_step_dev(self.h, x_dev, n, stream), "encoder_step_dev")
