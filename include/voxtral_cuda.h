@@ -490,8 +490,12 @@ int vox_cuda_attention_decode_dev(const float *q, const float *k_ring, const flo
  * array's device address and should come before any stream capture.  All
  * calls on a device share the array, which keeps the last call's contents:
  * calls that overlap on the GPU (other threads or streams) race, so callers
- * serialise them.  Returns 0 or a VOX_CUDA_ERR_* code; the call returns after
- * the result is in `out`. */
+ * serialise them.  Every call blocks the calling thread until its work on
+ * `stream` has finished (it synchronises `stream`), and returns 0 or a
+ * VOX_CUDA_ERR_* code with the result in `out`.  The array's address is looked
+ * up once per device ordinal, in the device's primary context: a caller that
+ * resets the device (cudaDeviceReset) or runs in another driver context does
+ * not use this entry point afterwards. */
 int vox_cuda_attention_decode_noalloc(const float *q, const float *k_ring, const float *v_ring,
                                       int kv_cap, int pos, float *out, void *stream);
 

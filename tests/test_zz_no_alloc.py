@@ -49,6 +49,30 @@ def test_noalloc_matches_allocating_entry_twice(L, slot, seed):
     assert B.rel_l2(b1, bref) < ATTN_TOL
 
 
+def test_noalloc_on_a_caller_stream_and_each_visible_device():
+    """A stream handle from the caller, and - where more than one GPU is
+    visible - the same call on every device (each looks up its own copy of
+    the array), against the allocating entry point."""
+    import torch
+    lib = V.lib()
+    q, k, v = G.attn_decode_inputs(512, 41)
+    for dev in range(torch.cuda.device_count()):
+        torch.cuda.set_device(dev)
+        dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+        s = torch.cuda.Stream()
+        out = torch.empty(B.Q_DIM, dtype=torch.float32, device="cuda")
+        rc = lib.vox_cuda_attention_decode_noalloc(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), 512, 511,
+                                                   out.data_ptr(), s.cuda_stream)
+        assert rc == 0, V.last_error()
+        got = out.cpu().numpy()
+        V.check(lib.vox_cuda_set_device(dev), "set_device")
+        V.init(dev)
+        ref = _run(lib.vox_cuda_attention_decode_dev, dq, dk, dv, 512, 511, torch)
+        assert B.rel_l2(got, ref) < ATTN_TOL, dev
+    torch.cuda.set_device(0)
+    V.check(lib.vox_cuda_set_device(0), "set_device")
+
+
 def test_noalloc_rejects_a_ring_smaller_than_the_window():
     import torch
     z = torch.zeros(16 * B.KV_DIM, dtype=torch.float32, device="cuda")

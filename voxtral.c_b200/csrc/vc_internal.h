@@ -100,6 +100,42 @@ struct AttnParams {
 };
 constexpr int kAttnSplits = 128;   // >= 8192 / 64 keys per split
 
+// ---- the persistent decode step (vc_step_persist.cu) ----
+struct PersistLayer {             // device array, one entry per decoder layer
+    const uint16_t *qkv, *wo, *w13, *w2;   // fragment-tiled weights
+    const float *g_attn, *g_ffn;           // the folded norm weights
+};
+struct PersistParams {
+    const PersistLayer *layers;   // [n_layers]
+    int n_layers;
+    int M;                        // streams (1..8)
+    int with_head;                // LM head + argmax after the layers
+    int vocab;
+    const uint16_t *lm;           // tiled LM head / token table
+    const float *final_norm;
+    const StreamSlot *slots;      // [M]
+    const float *rope;            // [M][128]
+    float *x;                     // [M][3072] residual stream
+    float *q;                     // [M][4096]
+    uint32_t *xf_attn, *xf_ffn, *xf_att, *xf_h;   // activation fragments
+    float *ss_attn, *ss_ffn;      // [M][48] sums of x^2 per row block
+    float *logits;                // [M][vocab]
+    ArgmaxPartial *amax;          // [vocab / 64][M]
+    int *tokens;                  // [M]
+    float *part_o, *part_ml;      // attention split partials ([M][32][kAttnSplits] x 128 / x 2)
+    float *gpart;                 // split-K partials: [items][64][8]
+    unsigned *sync;               // persist_sync_words() words, zero at launch
+    unsigned *err;
+    int ks[5];                    // K slices of q|k|v, wo, w1|w3, w2, LM head
+    int l2_ahead;                 // weight stages the L2 prefetch runs ahead of the ring
+};
+// Whether this slicing's activation slices fit one CTA's shared area (host check).
+bool persist_slicing_fits(const int *ks, int vocab, int grid);
+size_t persist_sync_words();
+size_t persist_gpart_floats(const PersistParams &p);
+// One cooperative launch of gridDim = the SM count.
+cudaError_t launch_step_persist(const PersistParams &p, cudaStream_t st, int *grid_out);
+
 cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl);
 // *dst = v in stream order (the descriptor travels as a kernel argument)
 cudaError_t launch_set_slot(StreamSlot *dst, const StreamSlot &v, cudaStream_t st);

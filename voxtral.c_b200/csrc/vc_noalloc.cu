@@ -57,6 +57,8 @@ extern "C" int vox_cuda_attention_decode_noalloc(const float *q, const float *k_
         return VOX_CUDA_ERR_ARG;
     }
     const int n_keys = (pos + 1 < kDecWindow) ? pos + 1 : kDecWindow;
+    // With today's constants the window (8192) equals the scratch's capacity,
+    // so this cannot fire; it guards a later change of either constant.
     if (n_keys > VOX_NOALLOC_MAX_KEYS) {
         vc::set_last_error("attention_decode_noalloc: %d keys exceed the static scratch (max %d)", n_keys,
                  VOX_NOALLOC_MAX_KEYS);
@@ -94,7 +96,9 @@ extern "C" int vox_cuda_attention_decode_noalloc(const float *q, const float *k_
     StreamSlot *slot = reinterpret_cast<StreamSlot *>(base);
     unsigned *tickets = reinterpret_cast<unsigned *>(base + kTicketOff);
     // the descriptor and the tickets (which must start at zero) are rewritten
-    // by every call: the array keeps the previous call's contents
+    // by every call: the array keeps the previous call's contents.  A launch
+    // that completes leaves its tickets at zero already; the reset is for a
+    // previous launch that failed or was cut short, so it stays.
     if (cudaMemcpyAsync(slot, &h, sizeof(h), cudaMemcpyHostToDevice, st) != cudaSuccess ||
         cudaMemsetAsync(tickets, 0, kDecKvHeads * sizeof(unsigned), st) != cudaSuccess) {
         vc::set_last_error("attention_decode_noalloc: staging the descriptor failed");

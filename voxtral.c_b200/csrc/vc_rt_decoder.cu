@@ -54,6 +54,9 @@ struct StepWork {
     uint32_t *xf_att = nullptr;        // B fragments of the attention output (wo input)
     uint32_t *xf_h = nullptr;          // B fragments of silu(g) * u (w2 input)
     unsigned *err = nullptr;           // follows tokens: bounded-wait error word
+    float *gpart = nullptr;            // persistent step: split-K partials
+    unsigned *psync = nullptr;         // persistent step: counters, zeroed per step
+    size_t psync_bytes = 0;
     size_t bytes = 0;
     // host (pinned)
     char *hblock = nullptr;
@@ -115,6 +118,7 @@ struct vox_cuda_decoder {
     bool tc_prefill = false;      // row-major weights kept: prefill on the tensor cores
     PrefillTc *pf = nullptr;
     std::vector<float> ffn_norm;  // [n_layers][3072] host copy: g_ffn is recomputed when ada changes
+    PersistLayer *players = nullptr;   // device [n_layers]: the persistent step's weight table
 };
 
 struct vox_cuda_dec_state {
@@ -144,6 +148,38 @@ void free_work(DevCtx *c, StepWork *w) {
         c->bytes -= w->bytes;
     }
     delete w;
+}
+
+// K slices of the persistent step's GEMV phases (q|k|v, wo, w1|w3, w2, LM
+// head): the fewest items that still give most SMs work (96, 48 x 3, 288,
+// 48 x 3, 2048); per-item reduction and epilogue latency made finer slicing
+// slower.  VOX_CUDA_PERSIST_KS="a,b,c,d,e" overrides.
+void persist_ks(int *ks) {
+    static int v[5] = {0, 0, 0, 0, 0};
+    if (v[0] == 0) {
+        int t[5] = {1, 3, 1, 3, 1};
+        const char *e = getenv("VOX_CUDA_PERSIST_KS");
+        if (e && *e) {
+            int r[5];
+            if (sscanf(e, "%d,%d,%d,%d,%d", &r[0], &r[1], &r[2], &r[3], &r[4]) == 5) {
+                bool good = true;
+                for (int i = 0; i < 5; i++) good &= r[i] >= 1 && r[i] <= 16;
+                if (good) memcpy(t, r, sizeof(t));
+            }
+        }
+        memcpy(v, t, sizeof(v));
+    }
+    memcpy(ks, v, sizeof(v));
+}
+
+// The decode steps launch the per-phase kernels (the GEMVs of vc_gemv.cu and
+// the attention of vc_decode.cu) with programmatic dependent launch.
+// VOX_CUDA_PERSIST=1 runs each step with the LM head as one persistent kernel
+// instead (vc_step_persist.cu): correct, but measured slower at 8 streams
+// (3.0 ms against 1.73 ms per step), so it is not the default.
+bool persist_on() {   // read when a step's graph is captured (once per workspace)
+    const char *e = getenv("VOX_CUDA_PERSIST");
+    return e && e[0] == '1';
 }
 
 StepWork *make_work(DevCtx *c, int n, int vocab) {
@@ -182,6 +218,11 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     const size_t o_xft = take(xfrag_bytes(kQDim));
     const size_t o_xfh = take(xfrag_bytes(kDecHidden));
     const size_t frag_bytes = off - o_frag0;
+    PersistParams pk = {};
+    persist_ks(pk.ks);
+    pk.vocab = vocab;
+    const size_t o_gpart = take(sizeof(float) * std::max<size_t>(persist_gpart_floats(pk), 1));
+    const size_t o_psync = take(sizeof(unsigned) * persist_sync_words());
     if (dev_alloc(c, (void **)&w->dblock, off) != cudaSuccess) {
         set_error("decoder workspace: cudaMalloc(%zu) failed", off);
         delete w;
@@ -210,6 +251,9 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     w->xf_att = (uint32_t *)(b + o_xft);
     w->xf_h = (uint32_t *)(b + o_xfh);
     w->err = (unsigned *)(w->tokens + n);
+    w->gpart = (float *)(b + o_gpart);
+    w->psync = (unsigned *)(b + o_psync);
+    w->psync_bytes = sizeof(unsigned) * persist_sync_words();
     // fragments of streams >= n are never written and must read as zeros
     if (cudaMemset(b + o_frag0, 0, frag_bytes) != cudaSuccess ||
         cudaMemset(w->tokens, 0, sizeof(int) * (n + 1)) != cudaSuccess ||
@@ -256,8 +300,47 @@ unsigned long long l2pf_attn_budget() { return env_mb("VOX_CUDA_L2PF_ATTN_MB", 3
 // evs (profiling only): 2 events per launch, recorded around it.
 // only (profiling only): >= 0 enqueues that phase's launches alone
 // (VOX_CUDA_PROF_*), one per layer, back to back.
+int enqueue_persist(vox_cuda_decoder *d, StepWork *w, cudaStream_t st) {
+    PersistParams p = {};
+    p.layers = d->players;
+    p.n_layers = d->n_layers;
+    p.M = w->n;
+    p.with_head = 1;
+    p.vocab = d->vocab;
+    p.lm = d->tok_emb;
+    p.final_norm = d->norm;
+    p.slots = w->slots;
+    p.rope = w->rope;
+    p.x = w->x;
+    p.q = w->q;
+    p.xf_attn = w->xf_attn;
+    p.xf_ffn = w->xf_ffn;
+    p.xf_att = w->xf_att;
+    p.xf_h = w->xf_h;
+    p.ss_attn = w->ss_attn;
+    p.ss_ffn = w->ss_ffn;
+    p.logits = w->logits;
+    p.amax = w->amax;
+    p.tokens = w->tokens;
+    p.part_o = w->part_o;
+    p.part_ml = w->part_ml;
+    p.gpart = w->gpart;
+    p.sync = w->psync;
+    p.err = w->err;
+    persist_ks(p.ks);
+    // weight stages (16 KB) the L2 prefetch runs ahead of the shared ring;
+    // VOX_CUDA_PERSIST_L2 overrides
+    const char *e = getenv("VOX_CUDA_PERSIST_L2");
+    p.l2_ahead = (e && *e) ? std::max(0, atoi(e)) : 16;
+    VC_TRY(cudaMemsetAsync(w->psync, 0, w->psync_bytes, st));
+    VC_TRY(launch_prep_xfrag(w->x, w->n, kDecDim, kDecDim, d->L[0].g_attn, w->xf_attn, w->ss_attn, st, false));
+    VC_TRY(launch_step_persist(p, st, nullptr));
+    return VOX_CUDA_OK;
+}
+
 int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_t st,
                    cudaEvent_t *evs = nullptr, int only = -1) {
+    if (with_head && evs == nullptr && only < 0 && d->players && persist_on()) return enqueue_persist(d, w, st);
     const int n = w->n;
     const bool pdl = d->pdl && evs == nullptr;
     const int ss_parts = gemv_row_blocks(kDecDim);
@@ -830,6 +913,14 @@ extern "C" vox_cuda_decoder *vox_cuda_decoder_create(const vox_cuda_dec_weights 
         }
     }
     cudaFree(stage);
+    if (ok) {   // the persistent step's table of per-layer weights
+        std::vector<PersistLayer> pl(d->n_layers);
+        for (int l = 0; l < d->n_layers; l++)
+            pl[l] = PersistLayer{d->L[l].qkv, d->L[l].wo, d->L[l].w13, d->L[l].w2, d->L[l].g_attn, d->L[l].g_ffn};
+        d->players = (PersistLayer *)alloc(sizeof(PersistLayer) * pl.size());
+        ok = d->players && cudaMemcpy(d->players, pl.data(), sizeof(PersistLayer) * pl.size(),
+                                      cudaMemcpyHostToDevice) == cudaSuccess;
+    }
     if (!ok) {
         if (!reported) set_error("decoder_create: weight upload failed (out of device memory?)");
         vox_cuda_decoder_free(d);
