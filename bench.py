@@ -564,32 +564,42 @@ def single_stream_and_attention(V, torch, dec, steps):
     return out
 
 
-def attention_bench(V, torch):
+def attention_bench(V, torch, iters=20):
     """The stand-alone decode attention (vox_cuda_attention_decode_dev) over
-    L = 512 / 2048 / 8192 keys, the last in a wrapped 8192 + 1024 ring."""
+    L = 512 / 2048 / 8192 keys, the last in a wrapped 8192 + 1024 ring.  Each
+    call is timed alone with CUDA events on its stream, after a 256 MB read
+    that flushes the 126 MB L2 (a read, so no dirty lines are written back
+    during the call), so the keys come from HBM as they do in a decode step
+    (median of `iters`)."""
     stream = torch.cuda.Stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     hbm, _ = peaks()
     cap = 8192 + 1024
     k = torch.randn((cap, KVD), device="cuda", dtype=torch.float32)
     v = torch.randn((cap, KVD), device="cuda", dtype=torch.float32)
     q = torch.randn((QD,), device="cuda", dtype=torch.float32)
     o = torch.empty((QD,), device="cuda", dtype=torch.float32)
+    flush = torch.ones(64 << 20, device="cuda", dtype=torch.float32)    # 256 MB
+    sink = torch.empty(1, device="cuda", dtype=torch.float32)
     att = {}
     for L, pos in ((512, 511), (2048, 2047), (8192, 5000 + 8192 - 1)):
         for _ in range(3):
             V.attention_decode_dev(q.data_ptr(), k.data_ptr(), v.data_ptr(), cap, pos, o.data_ptr(),
                                    stream.cuda_stream)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(20):
+        times = []
+        for _ in range(iters):
+            with torch.cuda.stream(stream):   # read 256 MB: L2 ends up holding other, clean lines
+                torch.sum(flush, dim=0, keepdim=True, out=sink)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
             V.attention_decode_dev(q.data_ptr(), k.data_ptr(), v.data_ptr(), cap, pos, o.data_ptr(),
                                    stream.cuda_stream)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) / 20 * 1000.0
+            e1.record(stream)
+            stream.synchronize()
+            times.append(e0.elapsed_time(e1) * 1000.0)
+        us = statistics.median(times)
         gbs = L * KVD * 4 * 2 / (us / 1e6) / 1e9
-        att[f"L{L}"] = {"us": us, "gbs": gbs, "frac_of_hbm": gbs / hbm}
+        att[f"L{L}"] = {"us": us, "gbs": gbs, "frac_of_hbm": gbs / hbm, "l2": "flushed (256 MB read) before each call"}
+    del flush
     return att
 
 

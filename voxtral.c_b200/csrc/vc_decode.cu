@@ -291,19 +291,22 @@ attn_decode_kernel(const AttnParams p) {
 
 constexpr int kTileKeys = 32;
 
-struct Attn4Shared {
-    float k[2][kTileKeys][kHeadDim];   // 2 x 16 KB, chunk-swizzled
-    float v[2][kTileKeys][kHeadDim];   // 2 x 16 KB
+template <int NS>
+struct Attn4SharedT {
+    float k[NS][kTileKeys][kHeadDim];   // NS x 16 KB, chunk-swizzled
+    float v[NS][kTileKeys][kHeadDim];   // NS x 16 KB
     float q[4][kHeadDim];
     float p[4][kTileKeys];             // this tile's exp(s - m)
     float alpha[4];                    // this tile's rescale of the running sums
     int last;
 };
+using Attn4Shared = Attn4SharedT<2>;
 static_assert(sizeof(float) * 2 * kTileKeys * kHeadDim >= sizeof(float) * 4 * kAttnSplits, "merge weights fit");
 
 // cp.async of keys [j0, j1) of the tile starting at key kb (logical index
 // from `first`) into buffer b: K swizzled, V as is.
-__device__ __forceinline__ void attn4_stage(Attn4Shared &sh, int b, const float *kbase, const float *vbase,
+template <int NS>
+__device__ __forceinline__ void attn4_stage(Attn4SharedT<NS> &sh, int b, const float *kbase, const float *vbase,
                                             int first, int kb, int cap, int j0, int j1, int tid) {
     const int n = (j1 - j0) * (kHeadDim / 4);
     for (int c = tid; c < n; c += 128) {
@@ -314,10 +317,14 @@ __device__ __forceinline__ void attn4_stage(Attn4Shared &sh, int b, const float 
     }
 }
 
+// NS tile buffers: NS - 1 tiles in flight while one is computed.  NS = 2 with
+// three CTAs per SM (v4), or NS = 6 with one CTA per SM (the deep variant
+// for long contexts: 160 KB of keys in flight per SM).
+template <int NS>
 __global__ void __launch_bounds__(128)
 attn_decode_v4_kernel(const AttnParams p) {
     extern __shared__ __align__(16) unsigned char attn_smem[];
-    Attn4Shared &sh = *reinterpret_cast<Attn4Shared *>(attn_smem);
+    Attn4SharedT<NS> &sh = *reinterpret_cast<Attn4SharedT<NS> *>(attn_smem);
     const int kvh = blockIdx.y, m = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) l2_prefetch_share(p.pf, p.pf_bytes);   // the wo GEMV's weights (this kernel leaves HBM idle)
@@ -337,11 +344,11 @@ attn_decode_v4_kernel(const AttnParams p) {
     const int n_old = max(0, min(slt.fresh, slt.pos) - first);   // keys [0, n_old) predate this launch
     auto tile_keys = [&](int t) { return min(kTileKeys, n_keys - t * kTileKeys); };
 
-    // the old keys of the first two tiles, before the wait (they overlap the
-    // producer kernel's tail)
-    for (int t = t0; t < min(t1, t0 + 2); t++) {
+    // the old keys of the first NS - 1 tiles, before the wait (they overlap
+    // the producer kernel's tail): one commit group
+    for (int t = t0; t < min(t1, t0 + NS - 1); t++) {
         const int kb = t * kTileKeys;
-        attn4_stage(sh, t & 1, kbase, vbase, first, kb, cap, 0, max(0, min(tile_keys(t), n_old - kb)), tid);
+        attn4_stage(sh, t % NS, kbase, vbase, first, kb, cap, 0, max(0, min(tile_keys(t), n_old - kb)), tid);
     }
     cp_async_commit();
     grid_dep_wait();
@@ -351,19 +358,25 @@ attn_decode_v4_kernel(const AttnParams p) {
                                                            (kvh * 4 + warp) * kHeadDim + 4 * lane);
         *reinterpret_cast<float4 *>(&sh.q[warp][4 * lane]) = v;
     }
-    for (int t = t0; t < min(t1, t0 + 2); t++) {   // their fresh keys, one group per tile
-        const int kb = t * kTileKeys;
-        attn4_stage(sh, t & 1, kbase, vbase, first, kb, cap, max(0, min(tile_keys(t), n_old - kb)), tile_keys(t),
-                    tid);
+    for (int t = t0; t < t0 + NS - 1; t++) {   // their fresh keys: one group per tile (empty past t1)
+        if (t < t1) {
+            const int kb = t * kTileKeys;
+            attn4_stage(sh, t % NS, kbase, vbase, first, kb, cap, max(0, min(tile_keys(t), n_old - kb)),
+                        tile_keys(t), tid);
+        }
         cp_async_commit();
     }
 
     float m_run = -INFINITY, l_run = 0.f;    // warp h: head h's running max / sum
     float o[4] = {0.f, 0.f, 0.f, 0.f};       // thread = dimension, 4 heads
     for (int t = t0; t < t1; t++) {
-        const int b = t & 1, nk = tile_keys(t);
-        if (t + 1 < t1) cp_async_wait_group<1>();
-        else cp_async_wait_group<0>();
+        const int b = t % NS, nk = tile_keys(t);
+        // tile t + NS - 1 into the buffer freed by tile t - 1; then tile t has landed
+        if (t + NS - 1 < t1)
+            attn4_stage(sh, (t + NS - 1) % NS, kbase, vbase, first, (t + NS - 1) * kTileKeys, cap, 0,
+                        tile_keys(t + NS - 1), tid);
+        cp_async_commit();
+        cp_async_wait_group<NS - 1>();
         __syncthreads();
         {   // scores (warp = head, lane = key): swizzled K chunks, broadcast q
             const int h = warp;
@@ -408,11 +421,8 @@ attn_decode_v4_kernel(const AttnParams p) {
             }
         }
         __syncthreads();   // buffer b consumed
-        if (t + 2 < t1) {
-            attn4_stage(sh, b, kbase, vbase, first, (t + 2) * kTileKeys, cap, 0, tile_keys(t + 2), tid);
-            cp_async_commit();
-        }
     }
+    cp_async_wait_group<0>();   // (only empty groups remain)
     // this CTA's partial: unnormalised o, running (max, sum) per head
     const int s = blockIdx.x;
 #pragma unroll
@@ -506,6 +516,30 @@ int attn4_ctas_per_head(int M) {
     return g < 16 ? 16 : g;
 }
 
+// The deep variant: two CTAs of 3 tile buffers (96 KB) per SM, the SMs
+// shared by the launch's (row, KV head) pairs.
+constexpr int kDeepStages = 3;
+int attn_deep_ctas_per_head(int M) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int g = 2 * sms / (kDecKvHeads * (M > 0 ? M : 1));
+    return g < 1 ? 1 : g;
+}
+
+// Long contexts take the deep variant: 2 tiles in flight per CTA keep
+// ~128 KB of keys moving per SM, where v4's 3 CTAs x 1 tile do ~96 KB.  The
+// caller passes a hint of the keys it expects (0: unknown, v4).
+// VOX_CUDA_ATTN = deep forces it.
+bool attn_use_deep(int M, int keys_hint) {
+    static int forced = -1;
+    if (forced < 0) {
+        const char *e = getenv("VOX_CUDA_ATTN");
+        forced = (e && strcmp(e, "deep") == 0) ? 1 : (e && strcmp(e, "v4") == 0) ? 0 : -2;
+    }
+    if (forced >= 0) return forced == 1;
+    return M <= 2 && keys_hint >= kAttnDeepKeys;
+}
+
 int attn_ctas_per_head(int M) {
     static int fixed = -1;
     if (fixed < 0) {   // tuning knob: VOX_CUDA_ATTN_CTAS fixes the CTAs per (stream, KV head)
@@ -533,7 +567,7 @@ static bool attn_use_v3(int M) {
     static int forced = -1;   // 0 auto, 3, 4
     if (forced < 0) {
         const char *e = getenv("VOX_CUDA_ATTN");
-        forced = (e && strcmp(e, "v3") == 0) ? 3 : (e && strcmp(e, "v4") == 0) ? 4 : 0;
+        forced = (e && strcmp(e, "v3") == 0) ? 3 : (e && (strcmp(e, "v4") == 0 || strcmp(e, "deep") == 0)) ? 4 : 0;
     }
     return forced == 3 || (forced == 0 && M > 2);
 }
@@ -549,25 +583,32 @@ cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool
         e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)sizeof(AttnShared));
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(attn_decode_v4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)sizeof(Attn4Shared));
+            e = cudaFuncSetAttribute(attn_decode_v4_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)sizeof(Attn4SharedT<2>));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attn_decode_v4_kernel<kDeepStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)sizeof(Attn4SharedT<kDeepStages>));
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
     cudaLaunchConfig_t cfg = {};
     // CTAs per (row, KV head): no more than the partials this launch's
     // buffers hold (a prefill of fresh rows attends to few keys: S = 1)
-    const int g = std::min(v3 ? attn_ctas_per_head(M) : attn4_ctas_per_head(M), std::max(1, p.S));
+    const bool deep = !v3 && attn_use_deep(M, p.deep_hint);
+    const int g = std::min(v3 ? attn_ctas_per_head(M) : deep ? attn_deep_ctas_per_head(M) : attn4_ctas_per_head(M),
+                           std::max(1, p.S));
     cfg.gridDim = dim3(g, kDecKvHeads, M);
     cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = v3 ? sizeof(AttnShared) : sizeof(Attn4Shared);
+    cfg.dynamicSmemBytes = v3 ? sizeof(AttnShared) : deep ? sizeof(Attn4SharedT<kDeepStages>) : sizeof(Attn4SharedT<2>);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return v3 ? cudaLaunchKernelEx(&cfg, attn_decode_kernel, p) : cudaLaunchKernelEx(&cfg, attn_decode_v4_kernel, p);
+    if (v3) return cudaLaunchKernelEx(&cfg, attn_decode_kernel, p);
+    return deep ? cudaLaunchKernelEx(&cfg, attn_decode_v4_kernel<kDeepStages>, p)
+                : cudaLaunchKernelEx(&cfg, attn_decode_v4_kernel<2>, p);
 }
 
 // ---------------------------------------------------------------------------

@@ -97,8 +97,10 @@ struct AttnParams {
     int S;                    // key splits per KV head
     const void *pf;           // weights of a later kernel to start pulling into L2 (or NULL)
     unsigned long long pf_bytes;   // a multiple of 16
+    int deep_hint;            // keys the caller expects per row (0: unknown); selects the deep variant
 };
 constexpr int kAttnSplits = 128;   // >= 8192 / 64 keys per split
+constexpr int kAttnDeepKeys = 2048;  // keys from which one or two rows take the deep attention variant
 
 // ---- the persistent decode step (vc_step_persist.cu) ----
 struct PersistLayer {             // device array, one entry per decoder layer

@@ -558,6 +558,7 @@ extern "C" int vox_cuda_attention_decode_dev(const float *q, const float *k_ring
     p.part_ml = c->attn_part_ml;
     p.counters = c->attn_counters;
     p.S = kAttnSplits;
+    p.deep_hint = n_keys;
     VC_TRY(launch_attn_decode(1, p, st, false));
     VC_TRY(cudaEventRecord(c->attn_done, st));
     return VOX_CUDA_OK;
