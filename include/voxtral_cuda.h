@@ -385,6 +385,16 @@ int vox_cuda_adapter_forward(vox_cuda_enc_state *s, const float *enc, int n, flo
 int vox_cuda_adapter_forward_dev(vox_cuda_enc_state *s, const float *enc_dev, int n, float *out_dev,
                                  void *stream);
 
+/* The encoder path keeps its GEMM operands, its K / V ring and its attention
+ * output in fp16 (where the reference keeps fp32, voxtral_encoder.c:452-636).
+ * A value beyond fp16's range (|v| > 65504) is clamped to +-65504 rather than
+ * becoming infinite, and counted, as is a NaN reaching an fp16 store.  This
+ * returns the count on the current device (every encoder, adapter and conv
+ * stem on it) since the library was loaded or the last reset (reset != 0),
+ * after waiting for the device's queued work.  Non-zero means the results may
+ * deviate from the fp32 reference: a caller with such weights checks it. */
+int vox_cuda_fp16_saturations(unsigned long long *count, int reset);
+
 /* Conv stem: the encoder's two causal convolutions over the mel stream,
  * conv0 (128 -> 1280, kernel 3, stride 1) and conv1 (1280 -> 1280, kernel 3,
  * stride 2), each followed by GELU, with the streaming state of

@@ -336,3 +336,59 @@ def test_adapter_dev_matches_host_adapter(gpu_enc):
     stream.synchronize()
     assert np.array_equal(d_out.cpu().numpy(), want)
     st.free()
+
+
+def _to_bf16_bits(a):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def _heavy_tailed(ew, seed, scale=1.0, w13_gain=1.0):
+    """Replace every weight matrix of `ew` in place by Student-t (3 degrees of
+    freedom) values with the same 0.02 scale: heavy tails, as real checkpoints
+    have; w1 / w3 (and the adapter's first matrix) optionally amplified."""
+    rng = np.random.default_rng(seed)
+    for ws, _, _ in ew.sets:
+        for j, w in enumerate(ws):
+            gain = w13_gain if j in (4, 6) else 1.0
+            t = rng.standard_t(3, size=w.shape).astype(np.float32) * (0.02 / np.sqrt(3.0)) * scale * gain
+            w[...] = _to_bf16_bits(t)
+
+
+def test_heavy_tailed_weights_match_oracle_without_saturation():
+    """Heavy-tailed weights (Student-t, df 3) and inputs at scale 1e3: the
+    fp16 operands stay in range (no saturations counted) and the encoder
+    stays within its parity bound against the fp32 oracle."""
+    ew = B.EncoderWeights(seed=11, n_layers=3, distinct=3, norm_noise=0.1)
+    _heavy_tailed(ew, 1800)
+    e = make_gpu_encoder(ew)
+    st = e.state(max_chunk=256)
+    o = B.OracleEncoder(ew, kv_max=1024)
+    V.fp16_saturations(reset=True)
+    for i, n in enumerate((100, 37, 160)):
+        x = B.normal_f32((n, B.ENC_DIM), 1810 + i, 1000.0)
+        y = st.step(x)
+        want = o.step(x)
+        assert np.isfinite(y).all()
+        assert B.rel_l2(y, want) < ENC_TOL, (i, B.rel_l2(y, want))
+    assert V.fp16_saturations() == 0
+    st.free()
+    e.free()
+
+
+def test_fp16_overflow_is_clamped_and_counted():
+    """w1 / w3 amplified so that silu(gate) * up exceeds fp16's range: the
+    values are clamped to +-65504 (no inf or NaN reaches the residual
+    stream) and counted by vox_cuda_fp16_saturations."""
+    ew = B.EncoderWeights(seed=12, n_layers=2, distinct=2)
+    _heavy_tailed(ew, 1900, w13_gain=400.0)
+    e = make_gpu_encoder(ew)
+    st = e.state(max_chunk=128)
+    V.fp16_saturations(reset=True)
+    y = st.step(B.normal_f32((64, B.ENC_DIM), 1901, 1.0))
+    n = V.fp16_saturations(reset=True)
+    assert n > 0
+    assert np.isfinite(y).all()
+    assert V.fp16_saturations() == 0   # the reset took
+    st.free()
+    e.free()

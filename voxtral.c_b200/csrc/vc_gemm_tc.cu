@@ -75,8 +75,22 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
     return bf16_bits_rn(a) | (bf16_bits_rn(b) << 16);
 }
 
+// fp16 operands and rings (the encoder, its adapter, the conv stem's GEMMs):
+// a value outside fp16's finite range is clamped to +-65504 instead of
+// becoming inf, and counted (NaN passes through, counted), so that an
+// overflow on real weights is visible (vox_cuda_fp16_saturations) rather
+// than silent.  The compare is off the common path's critical chain.
+__device__ unsigned long long g_f16_sat_gemm;
+__device__ __forceinline__ float sat_f16(float a) {
+    if (!(fabsf(a) <= 65504.0f)) {
+        atomicAdd(&g_f16_sat_gemm, 1ull);
+        if (a == a) a = copysignf(65504.0f, a);
+    }
+    return a;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
+    const __half2 h = __floats2half2_rn(sat_f16(a), sat_f16(b));
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
@@ -85,7 +99,7 @@ __device__ __forceinline__ uint32_t pack16x2(float a, float b, int f16) {
     return f16 ? pack_half2(a, b) : pack_bf16x2(a, b);
 }
 __device__ __forceinline__ uint16_t bits16(float a, int f16) {
-    return f16 ? __half_as_ushort(__float2half_rn(a)) : (uint16_t)bf16_bits_rn(a);
+    return f16 ? __half_as_ushort(__float2half_rn(sat_f16(a))) : (uint16_t)bf16_bits_rn(a);
 }
 
 // v = hi + lo in bf16: hi = bf16(v), lo = bf16(v - hi) (~2^-17 relative)
@@ -1565,4 +1579,16 @@ cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const floa
     return cudaLaunchKernelEx(&cfg, rows_to_bf16_kernel, x, M, K, ld, w, out, vec, f16 ? 1 : 0);
 }
 
+}  // namespace vc
+
+namespace vc {
+unsigned long long f16_saturations_gemm(bool reset) {
+    unsigned long long v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_f16_sat_gemm, sizeof(v)) != cudaSuccess) return 0;
+    if (reset) {
+        const unsigned long long z = 0;
+        cudaMemcpyToSymbol(g_f16_sat_gemm, &z, sizeof(z));
+    }
+    return v;
+}
 }  // namespace vc

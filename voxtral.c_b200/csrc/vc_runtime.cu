@@ -662,3 +662,15 @@ extern "C" int vox_cuda_gemm_bf16_dev(int M, int N, int K, const uint16_t *A_bf1
     VC_TRY(launch_tc_gemm(TC_STORE, tp, A_bf16, W_bf16, st, false));
     return VOX_CUDA_OK;
 }
+
+extern "C" int vox_cuda_fp16_saturations(unsigned long long *count, int reset) {
+    if (!count) {
+        set_error("fp16_saturations: bad arguments");
+        return VOX_CUDA_ERR_ARG;
+    }
+    // the counters are written by kernels that may still be queued
+    VC_TRY(cudaDeviceSynchronize());
+    *count = f16_saturations_gemm(reset != 0) + f16_saturations_attn(reset != 0) +
+             f16_saturations_stem(reset != 0);
+    return VOX_CUDA_OK;
+}

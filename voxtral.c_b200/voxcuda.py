@@ -108,6 +108,7 @@ def lib():
         "vox_cuda_decoder_embed_dev": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p],
                                        C.c_int),
         "vox_cuda_adapter_forward_dev": ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
+        "vox_cuda_fp16_saturations": ([C.c_void_p, C.c_int], C.c_int),
         "vox_cuda_decoder_step_batch_dev": ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                              C.c_void_p], C.c_int),
         "vox_cuda_decoder_profile_batch": ([C.c_void_p, C.c_int, C.c_void_p, C.c_int, _fp],
@@ -353,6 +354,13 @@ def step_batch_tokens_dev(states, row_ptrs, prev_tokens_dev, tokens_dev, stream=
     check(lib().vox_cuda_decoder_step_batch_tokens_dev(states_array(states), len(states), rows,
                                                        prev_tokens_dev, tokens_dev, stream),
           "step_batch_tokens_dev")
+
+
+def fp16_saturations(reset=False):
+    """fp16 values clamped (or NaN) by the encoder path on this device."""
+    n = C.c_ulonglong(0)
+    check(lib().vox_cuda_fp16_saturations(C.byref(n), 1 if reset else 0), "fp16_saturations")
+    return n.value
 
 
 def embed_dev(dec, n, rows_dev, tokens_dev, out_dev, stream=None):
