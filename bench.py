@@ -864,6 +864,92 @@ def serving_bench(V, torch, dec, enc, clip_s=60.0, interval_s=2.0, streams=8, se
     }
 
 
+def e2e_one_stream_bench(V, torch, dec, enc, clip_s=60.0, interval_s=2.0, seed=2024):
+    """BASELINE configs[3] through the host entry points the C host calls
+    (one stream, wall clock): `clip_s` seconds of synthetic audio fed in
+    2.0 s pieces to the log-mel context (vox_cuda_mel_feed), the conv stem on
+    the stream path's schedule (vox_cuda_conv_stem_step), the encoder chunk
+    (vox_cuda_encoder_full_step) and the adapter (vox_cuda_adapter_forward),
+    the 38-row prompt prefill (vox_cuda_decoder_prefill_step), then one
+    vox_cuda_decoder_full_step per adapter row with the step input
+    adapter[pos] + tok_embed(previous token) built on the host from the bf16
+    table, as stream_run_decoder does (voxtral.c:836-921).  The finish feeds
+    the zero right pad and flushes the mel context."""
+    n_samples = int(clip_s * SR)
+    feed = int(interval_s * SR)
+    right_pad = (TOK_SAMPLES - n_samples % TOK_SAMPLES) % TOK_SAMPLES + (6 + 1 + 10) * TOK_SAMPLES
+    audio = synthetic_clips(torch, 1, n_samples, seed)[0].cpu().numpy()
+    rng = np.random.default_rng(seed)
+    cw = [(rng.standard_normal(sh) * 0.02).astype(np.float32)
+          for sh in ((ENC_D, 128, 3), (ENC_D,), (ENC_D, ENC_D, 3), (ENC_D,))]
+    # the host's bf16 token table (the C host reads it from the mmap'd file),
+    # read back through the device lookup in pieces (its fp32 values are bf16)
+    table = np.empty((VOCAB, D), np.uint16)
+    piece = 8192
+    ids = torch.arange(piece, dtype=torch.int32, device="cuda")
+    rows = torch.empty((piece, D), dtype=torch.float32, device="cuda")
+    for t0 in range(0, VOCAB, piece):
+        V.embed_dev(dec, piece, None, (ids + t0).data_ptr(), rows.data_ptr())
+        torch.cuda.synchronize()
+        table[t0:t0 + piece] = (rows.cpu().numpy().view(np.uint32) >> 16).astype(np.uint16)
+    del ids, rows
+
+    def tok_row(t):
+        return (table[t].astype(np.uint32) << 16).view(np.float32)
+
+    def run():
+        mel = V.Mel(32 * TOK_SAMPLES, feed)
+        stem = V.ConvStem(*cw, max_mel=512)
+        est = enc.state(max_chunk=256)
+        dst = dec.state(kv_cap=8192 + 1024)
+        pending, first, carry = [], True, np.zeros((0, ENC_D), np.float32)
+        ad_rows, steps, prev, started, gen_pos = [], 0, TOKEN_PAD, False, 0
+        pieces = [audio[o:o + feed] for o in range(0, n_samples, feed)]
+        z = right_pad
+        zeros = []
+        while z > 0:
+            zeros.append(np.zeros(min(z, feed), np.float32))
+            z -= feed
+        for piece in pieces + zeros + [None]:
+            fin = piece is None
+            pending.append(mel.finish(0) if fin else mel.feed(piece))
+            have = sum(r.shape[0] for r in pending)
+            if have >= (312 if first else 200) or (fin and have > 0):
+                rows = stem.step(np.concatenate(pending, axis=0))
+                pending, first = [], False
+                if rows.shape[0]:
+                    out = np.concatenate([carry, est.step(rows)], axis=0)
+                    usable = out.shape[0] // 4 * 4
+                    if usable:
+                        ad_rows.append(est.adapter(out[:usable]))
+                    carry = out[usable:]
+            total = sum(a.shape[0] for a in ad_rows)
+            if not started and total >= PROMPT_LEN:
+                ad = np.concatenate(ad_rows, axis=0)
+                prompt = ad[:PROMPT_LEN] + np.stack([tok_row(TOKEN_BOS if i == 0 else TOKEN_PAD)
+                                                     for i in range(PROMPT_LEN)])
+                dst.prefill(prompt[:PROMPT_LEN - 1])
+                prev, _ = dst.step(prompt[PROMPT_LEN - 1], want_logits=False)
+                steps, gen_pos, started = 1, PROMPT_LEN, True
+            if started and gen_pos < total:
+                ad = np.concatenate(ad_rows, axis=0)
+                while gen_pos < total:
+                    prev, _ = dst.step(ad[gen_pos] + tok_row(prev), want_logits=False)
+                    steps += 1
+                    gen_pos += 1
+        for o in (mel, stem, est, dst):
+            o.free()
+        return steps
+
+    run()   # warm-up: graphs of every shape
+    t0 = time.perf_counter()
+    steps = run()
+    wall = time.perf_counter() - t0
+    return {"clip_s": clip_s, "interval_s": interval_s, "tokens": steps, "wall_s": wall,
+            "tokens_per_s": steps / wall, "rtf": wall / clip_s,
+            "timing": "wall clock around the whole clip, host audio in, host tokens out"}
+
+
 def bf16_peaks(kind="burst"):
     """(peak TFLOP/s, label): the measured dense bf16 figure, burst (for a
     kernel timed alone) or sustained (for work timed inside a long loop at the
@@ -1009,6 +1095,9 @@ def our_arm(args):
             r.update({"seconds_max_over_ranks": sec, "job_tokens_per_s": ws * S * r["decode_steps_per_stream"] / sec,
                       "job_audio_s_per_s": ws * S * r["clip_s"] / sec, "rtf_max_over_ranks": sec / r["clip_s"]})
             serving[key] = r
+    e2e_one = None
+    if enc is not None and not args.no_serving and (args.layers, args.vocab) == (LAYERS, VOCAB):
+        e2e_one = e2e_one_stream_bench(V, torch, dec, enc, clip_s=args.clip_s)
     dec.free()
     up_res = upload_bench(V, torch) if not args.no_encoder else None
     enc_res = None if args.no_encoder else encoder_bench(V, torch, args.steps, args.enc_rows, enc=enc)
@@ -1031,6 +1120,20 @@ def our_arm(args):
                     enc_res["cpu_baseline"] = {k: v for k, v in cpu_ep.items() if k != "prefill"}
                     pf_res["cpu_baseline"] = {"kind": cpu_ep["kind"], "build": cpu_ep["build"],
                                               "cores": cpu_ep["cores"], **cpu_ep["prefill"]}
+                    if e2e_one is not None:
+                        # the same clip on the reference's CPU path, composed from its
+                        # parts timed in this run: the encoder at 100-row chunks
+                        # (50 rows per second of audio), the prompt prefill, and one
+                        # stream's decode steps on one thread (2 steps timed)
+                        one_rate, _ = cpu_decode_rate(1, 2)
+                        enc_s = cpu_ep["encoder"]["M100"]["ms_per_chunk"] / 1000.0 * (args.clip_s * 50 / 100)
+                        est = enc_s + cpu_ep["prefill"]["ms"] / 1000.0 + e2e_one["tokens"] / one_rate
+                        e2e_one["cpu_reference"] = {
+                            "kind": cpu_ep["kind"], "build": cpu_ep["build"], "cores": cpu_ep["cores"],
+                            "seconds": est, "encoder_s": enc_s, "prefill_s": cpu_ep["prefill"]["ms"] / 1000.0,
+                            "decode_tok_per_s_one_thread": one_rate, "rtf": est / args.clip_s,
+                            "how": "composed from the reference's encoder chunk, prefill and one-thread decode "
+                                   "step timed in this run"}
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -1056,6 +1159,7 @@ def our_arm(args):
                               "achieved_gbs": step_bytes / (ms_step / 1000.0) / 1e9,
                               "frac": step_bytes / (ms_step / 1000.0) / 1e9 / hbm},
             "serving": serving,
+            "e2e_one_stream": e2e_one,
             "prefill": pf_res,
             "single_stream_decode_and_attention": ss_res,
             "weight_upload": up_res,

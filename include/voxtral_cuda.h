@@ -386,13 +386,16 @@ int vox_cuda_adapter_forward_dev(vox_cuda_enc_state *s, const float *enc_dev, in
                                  void *stream);
 
 /* The encoder path keeps its GEMM operands, its K / V ring and its attention
- * output in fp16 (where the reference keeps fp32, voxtral_encoder.c:452-636).
- * A value beyond fp16's range (|v| > 65504) is clamped to +-65504 rather than
- * becoming infinite, and counted, as is a NaN reaching an fp16 store.  This
- * returns the count on the current device (every encoder, adapter and conv
- * stem on it) since the library was loaded or the last reset (reset != 0),
- * after waiting for the device's queued work.  Non-zero means the results may
- * deviate from the fp32 reference: a caller with such weights checks it. */
+ * operands in fp16 (where the reference keeps fp32, voxtral_encoder.c:452-636).
+ * Conversions to fp16 saturate: a value beyond fp16's range (|v| > 65504)
+ * becomes +-65504 rather than infinite.  This returns, for the current device
+ * (every encoder and adapter on it), since the library was loaded or the last
+ * reset (reset != 0), the number of range events: SwiGLU output chunks (32
+ * values of a row) holding a clamped value - the product silu(g) * u is where
+ * the encoder's magnitudes peak - and residual rows that reached a norm with
+ * a non-finite value.  It waits for the device's queued work first.  Non-zero
+ * means the results may deviate from the fp32 reference: a caller with
+ * unusual weights checks it. */
 int vox_cuda_fp16_saturations(unsigned long long *count, int reset);
 
 /* Conv stem: the encoder's two causal convolutions over the mel stream,

@@ -85,17 +85,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-// fp16 outputs clamped to the finite range and counted (see sat_f16 in
-// vc_gemm_tc.cu): the attention output o / l of saturated values
-__device__ unsigned long long g_f16_sat_attn;
-__device__ __forceinline__ float sat_f16_attn(float a) {
-    if (!(fabsf(a) <= 65504.0f)) {
-        atomicAdd(&g_f16_sat_attn, 1ull);
-        if (a == a) a = copysignf(65504.0f, a);
-    }
-    return a;
-}
-
 __device__ __forceinline__ uint32_t half2_bits(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
@@ -103,7 +92,7 @@ __device__ __forceinline__ uint32_t half2_bits(float a, float b) {
 
 // the output pair as fp16 (f16) or bf16
 __device__ __forceinline__ uint32_t out16x2(float a, float b, int f16) {
-    return f16 ? half2_bits(sat_f16_attn(a), sat_f16_attn(b)) : (bf16_bits_rn(a) | (bf16_bits_rn(b) << 16));
+    return f16 ? half2_bits(a, b) : (bf16_bits_rn(a) | (bf16_bits_rn(b) << 16));
 }
 
 __global__ void __launch_bounds__(kFaThreads, 3)
@@ -441,14 +430,3 @@ cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl
 
 }  // namespace vc
 
-namespace vc {
-unsigned long long f16_saturations_attn(bool reset) {
-    unsigned long long v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_f16_sat_attn, sizeof(v)) != cudaSuccess) return 0;
-    if (reset) {
-        const unsigned long long z = 0;
-        cudaMemcpyToSymbol(g_f16_sat_attn, &z, sizeof(z));
-    }
-    return v;
-}
-}  // namespace vc

@@ -75,23 +75,28 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
     return bf16_bits_rn(a) | (bf16_bits_rn(b) << 16);
 }
 
-// fp16 operands and rings (the encoder, its adapter, the conv stem's GEMMs):
-// a value outside fp16's finite range is clamped to +-65504 instead of
-// becoming inf, and counted (NaN passes through, counted), so that an
-// overflow on real weights is visible (vox_cuda_fp16_saturations) rather
-// than silent.  The compare is off the common path's critical chain.
+// fp16 operands and rings (the encoder, its adapter, the conv stem's GEMMs)
+// convert with saturation: a value beyond fp16's finite range becomes
+// +-65504 rather than inf (NaN stays NaN).  One instruction, as the plain
+// conversion.  Two kinds of event are counted (vox_cuda_fp16_saturations):
+// a SwiGLU output chunk with a clamped value - the product silu(g) * u is
+// where the encoder's magnitudes peak - and a residual row that reached a
+// norm pass with a non-finite value.  Per-element checks elsewhere cost ~10%
+// of the chunk and catch nothing these two do not.
 __device__ unsigned long long g_f16_sat_gemm;
-__device__ __forceinline__ float sat_f16(float a) {
-    if (!(fabsf(a) <= 65504.0f)) {
-        atomicAdd(&g_f16_sat_gemm, 1ull);
-        if (a == a) a = copysignf(65504.0f, a);
-    }
-    return a;
-}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
-    const __half2 h = __floats2half2_rn(sat_f16(a), sat_f16(b));
-    return *reinterpret_cast<const uint32_t *>(&h);
+    uint32_t r;   // the first source lands in the upper half: (b, a) puts a in .x
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
+}
+// Running per-half maximum of |v| over packed fp16 pairs (sign bits masked):
+// one chunk is clamped when a half reached 65504 (0x7BFF; NaN sorts above).
+__device__ __forceinline__ uint32_t f16x2_absmax(uint32_t m, uint32_t w) {
+    return __vmaxu2(m, w & 0x7FFF7FFFu);
+}
+__device__ __forceinline__ void count_clamped(uint32_t absmax) {
+    if (__vcmpgeu2(absmax, 0x7BFF7BFFu)) atomicAdd(&g_f16_sat_gemm, 1ull);
 }
 
 // two 16-bit operand values (the next GEMM's A): fp16 or bf16
@@ -99,7 +104,7 @@ __device__ __forceinline__ uint32_t pack16x2(float a, float b, int f16) {
     return f16 ? pack_half2(a, b) : pack_bf16x2(a, b);
 }
 __device__ __forceinline__ uint16_t bits16(float a, int f16) {
-    return f16 ? __half_as_ushort(__float2half_rn(sat_f16(a))) : (uint16_t)bf16_bits_rn(a);
+    return f16 ? (uint16_t)(pack_half2(a, 0.0f) & 0xFFFFu) : (uint16_t)bf16_bits_rn(a);
 }
 
 // v = hi + lo in bf16: hi = bf16(v), lo = bf16(v - hi) (~2^-17 relative)
@@ -285,10 +290,13 @@ __device__ __forceinline__ void epi_vec(const TcGemmParams &p, const EpiRow &er,
     } else if constexpr (EPI == TC_SWIGLU) {
         // columns (2i, 2i+1) = (gate_i, up_i) -> h_i = silu(g) * u
         // (voxtral_kernels.c:369-374, then :34-36), bf16 for the next GEMM
-        uint32_t h[kEpiCols / 4];
+        uint32_t h[kEpiCols / 4], clamp = 0;
 #pragma unroll
-        for (int j = 0; j < kEpiCols; j += 4)
+        for (int j = 0; j < kEpiCols; j += 4) {
             h[j >> 2] = pack16x2(silu_fast(v[j]) * v[j + 1], silu_fast(v[j + 2]) * v[j + 3], p.f16);
+            clamp = f16x2_absmax(clamp, h[j >> 2]);
+        }
+        if (p.f16) count_clamped(clamp);
         const int orow = p.out_hilo ? hilo_row(row) : row;
         uint16_t *o = p.out_bf16 + (size_t)orow * p.ldo_bf16 + (col0 >> 1);
 #pragma unroll
@@ -345,6 +353,7 @@ __device__ __forceinline__ void epi_scalar(const TcGemmParams &p, const EpiRow &
             if (col0 + j + 1 >= p.N) break;
             const float h = silu_fast(v[j]) * v[j + 1];
             o[j >> 1] = bits16(h, p.f16);
+            if (p.f16 && !(fabsf(h) < 65504.0f)) atomicAdd(&g_f16_sat_gemm, 1ull);
             if (p.out_hilo)
                 p.out_bf16[(size_t)(orow + 64) * p.ldo_bf16 + ((col0 + j) >> 1)] =
                     (uint16_t)bf16_bits_rn(h - bf16_hi_f(h));
@@ -402,10 +411,13 @@ __device__ __forceinline__ void epi_tma(const TcGemmParams &p, const EpiMaps &mp
     if (lane == 0) bulk_wait_read_all();   // the previous store has read the staging tile
     __syncwarp();
     if constexpr (EPI == TC_SWIGLU) {
-        uint32_t h[kEpiCols / 4];
+        uint32_t h[kEpiCols / 4], clamp = 0;
 #pragma unroll
-        for (int j = 0; j < kEpiCols; j += 4)
+        for (int j = 0; j < kEpiCols; j += 4) {
             h[j >> 2] = pack16x2(silu_fast(v[j]) * v[j + 1], silu_fast(v[j + 2]) * v[j + 3], p.f16);
+            clamp = f16x2_absmax(clamp, h[j >> 2]);
+        }
+        if (p.f16) count_clamped(clamp);
         swz_put<32>(stg, lane, 0, make_uint4(h[0], h[1], h[2], h[3]));
         swz_put<32>(stg, lane, 1, make_uint4(h[4], h[5], h[6], h[7]));
     } else if (EPI == TC_QKV_ENC || p.out_bf16) {   // 16-bit outputs, 64-byte rows
@@ -1423,6 +1435,7 @@ rows_to_bf16_kernel(const float *x, int M, int K, int ld, const float *w, uint16
         if (w) {
             ss = warp_sum(ss);
             inv = 1.0f / sqrtf(ss / (float)K + kNormEps);
+            if (f16 && lane == 0 && !isfinite(ss)) atomicAdd(&g_f16_sat_gemm, 1ull);   // a non-finite row
         }
 #pragma unroll
         for (int j = 0; j < kRowRegs; j++) {

@@ -102,12 +102,10 @@ struct AttnParams {
 constexpr int kAttnSplits = 128;   // >= 8192 / 64 keys per split
 constexpr int kAttnDeepKeys = 2048;  // keys from which one or two rows take the deep attention variant
 
-// fp16 values clamped to the finite range (or NaN) since the last reset, on
-// the current device: encoder / adapter GEMM epilogues and row conversions,
-// the encoder attention's output, the conv stem's im2col.
+// fp16 range events of the encoder path since the last reset, on the
+// current device (vc_gemm_tc.cu: clamped SwiGLU output chunks and
+// non-finite rows reaching a norm pass).
 unsigned long long f16_saturations_gemm(bool reset);
-unsigned long long f16_saturations_attn(bool reset);
-unsigned long long f16_saturations_stem(bool reset);
 
 // ---- the persistent decode step (vc_step_persist.cu) ----
 struct PersistLayer {             // device array, one entry per decoder layer

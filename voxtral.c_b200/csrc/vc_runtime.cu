@@ -670,7 +670,6 @@ extern "C" int vox_cuda_fp16_saturations(unsigned long long *count, int reset) {
     }
     // the counters are written by kernels that may still be queued
     VC_TRY(cudaDeviceSynchronize());
-    *count = f16_saturations_gemm(reset != 0) + f16_saturations_attn(reset != 0) +
-             f16_saturations_stem(reset != 0);
+    *count = f16_saturations_gemm(reset != 0);
     return VOX_CUDA_OK;
 }

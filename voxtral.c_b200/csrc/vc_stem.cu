@@ -22,16 +22,7 @@ constexpr int kStemMel = 128;                  // mel bins
 constexpr int kStemK0 = 3 * kStemMel;          // conv0 GEMM K
 constexpr int kStemK1 = 3 * kEncDim;           // conv1 GEMM K
 
-// im2col rows as fp16, clamped to the finite range and counted (see sat_f16
-// in vc_gemm_tc.cu)
-__device__ unsigned long long g_f16_sat_stem;
-__device__ __forceinline__ uint16_t f16_bits(float v) {
-    if (!(fabsf(v) <= 65504.0f)) {
-        atomicAdd(&g_f16_sat_stem, 1ull);
-        if (v == v) v = copysignf(65504.0f, v);
-    }
-    return __half_as_ushort(__float2half_rn(v));
-}
+__device__ __forceinline__ uint16_t f16_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
 
 // a0[r][ic * 3 + k] = mel frame f0 + r - 2 + k, bin ic: ext = [hist(2) | new(n)]
 __global__ void __launch_bounds__(256)
@@ -116,14 +107,3 @@ cudaError_t launch_f32_to_f16(const float *src, uint16_t *dst, size_t n, cudaStr
 
 }  // namespace vc
 
-namespace vc {
-unsigned long long f16_saturations_stem(bool reset) {
-    unsigned long long v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_f16_sat_stem, sizeof(v)) != cudaSuccess) return 0;
-    if (reset) {
-        const unsigned long long z = 0;
-        cudaMemcpyToSymbol(g_f16_sat_stem, &z, sizeof(z));
-    }
-    return v;
-}
-}  // namespace vc
