@@ -587,9 +587,12 @@ def attention_bench(V, torch, iters=20):
                                    stream.cuda_stream)
         times = []
         for _ in range(iters):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             with torch.cuda.stream(stream):   # read 256 MB: L2 ends up holding other, clean lines
                 torch.sum(flush, dim=0, keepdim=True, out=sink)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                # ~50 us of device time before e0, so the host's launch path
+                # is queued behind it and the events time the device alone
+                torch.cuda._sleep(100000)
             e0.record(stream)
             V.attention_decode_dev(q.data_ptr(), k.data_ptr(), v.data_ptr(), cap, pos, o.data_ptr(),
                                    stream.cuda_stream)

@@ -109,7 +109,7 @@ attn_decode_kernel(const AttnParams p) {
 
     // The slots were written before this step's first kernel; ring rows of
     // positions below slt.pos were written by earlier steps.
-    const StreamSlot slt = p.slots[m];
+    const StreamSlot slt = p.slot_inline ? p.slot1 : p.slots[m];
     const int n_keys = slt.n_keys;
     const int S = max(1, min(p.S, (n_keys + kKeysPerSplit - 1) / kKeysPerSplit));
     if ((int)blockIdx.x >= S) return;   // CTA-uniform, before any barrier
@@ -329,7 +329,7 @@ attn_decode_v4_kernel(const AttnParams p) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) l2_prefetch_share(p.pf, p.pf_bytes);   // the wo GEMV's weights (this kernel leaves HBM idle)
 
-    const StreamSlot slt = p.slots[m];
+    const StreamSlot slt = p.slot_inline ? p.slot1 : p.slots[m];
     const int n_keys = slt.n_keys;
     const int tiles = (n_keys + kTileKeys - 1) / kTileKeys;
     const int P = min((int)gridDim.x, tiles);           // CTAs with keys = partials
@@ -501,6 +501,291 @@ attn_decode_v4_kernel(const AttnParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// v5: keys streamed straight into registers, no shared-memory staging.
+//
+// A CTA of NW warps takes a contiguous range of one (row, KV head)'s keys,
+// each warp a contiguous sub-range in steps of 4 keys.  Lane l holds dims
+// [4l, 4l + 4) of each key's K and V row (one coalesced 512-byte load per
+// row); the next step's rows are in flight while a step is computed, and a
+// warp's first two steps of keys older than the launch are loaded before
+// griddepcontrol.wait.  The 16 dot products of a step (4 keys x the KV
+// head's 4 query heads) are summed across the warp by a halving exchange
+// (8 + 4 + 2 + 1 + 1 shuffles), after which lane l holds the score of key
+// l >> 3 for head (l >> 1) & 3.  Online softmax per head over the steps; the
+// step's probabilities reach every lane through shared memory for P.V.  The
+// warps' partials merge in shared memory; a row with several CTAs merges
+// their partials in the last CTA to finish (atomic ticket, no spinning),
+// with eight partials' loads in flight per thread.
+// ---------------------------------------------------------------------------
+constexpr int kV5Step = 4;        // keys per warp step
+constexpr float kV5Lazy = 8.0f;   // log2 of the largest probability before the running max moves
+
+// 2^x by the hardware approximation (relative error ~2^-22)
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <int NW>
+struct Attn5Shared {
+    float4 pk[NW][kV5Step];                   // a step's probabilities: [key] = (4 heads)
+    float4 alpha[NW];                         // a step's rescale of the running sums, per head
+    float4 o[NW][4][kHeadDim / 4];            // warp partials: unnormalised o per head
+    float2 ml[NW][4];                         // warp partials: (max, sum) per head
+    float mw[4][kAttnSplits];                 // merge: CTA partial maxima, then their weights
+    float lw[4][kAttnSplits];                 // merge: CTA partial sums
+    float4 grp[NW / 4][4 * kHeadDim / 4];     // merge: the thread groups' sums
+    float gl[4];                              // merge: per-head total sum
+    int last;
+};
+
+__device__ __forceinline__ float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+__device__ __forceinline__ float comp4(const float4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ void fma4(float4 &acc, float w, const float4 &v) {
+    acc.x = fmaf(w, v.x, acc.x);
+    acc.y = fmaf(w, v.y, acc.y);
+    acc.z = fmaf(w, v.z, acc.z);
+    acc.w = fmaf(w, v.w, acc.w);
+}
+__device__ __forceinline__ float dot4(const float4 &a, const float4 &b) {
+    return fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, a.x * b.x)));
+}
+// halving exchange step: of 2n values, keep the half selected by this lane's
+// bit (upper when set), add the partner's copy of it, send it the other half
+template <int N>
+__device__ __forceinline__ void xhalve(float *a, bool upper, int mask) {
+#pragma unroll
+    for (int j = 0; j < N; j++) {
+        const float send = upper ? a[j] : a[j + N], keep = upper ? a[j + N] : a[j];
+        a[j] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+    }
+}
+
+template <int NW>
+__global__ void __launch_bounds__(NW * 32, NW == 4 ? 4 : 2)
+attn_decode_v5_kernel(const AttnParams p) {
+    __shared__ Attn5Shared<NW> sh;
+    const int kvh = blockIdx.y, m = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) l2_prefetch_share(p.pf, p.pf_bytes);   // the wo GEMV's weights (this kernel leaves HBM idle)
+
+    const StreamSlot slt = p.slot_inline ? p.slot1 : p.slots[m];
+    const int n_keys = slt.n_keys;
+    const int min_keys = p.min_keys > 0 ? p.min_keys : NW * 8;
+    const int P = max(1, min((int)gridDim.x, (n_keys + min_keys - 1) / min_keys));   // CTAs with keys
+    if ((int)blockIdx.x >= P) return;   // CTA-uniform, before any barrier
+    const int c0 = (int)((long long)blockIdx.x * n_keys / P), c1 = (int)((long long)(blockIdx.x + 1) * n_keys / P);
+    const int k0 = c0 + (int)((long long)warp * (c1 - c0) / NW);
+    const int k1 = c0 + (int)((long long)(warp + 1) * (c1 - c0) / NW);
+    const int nsteps = (k1 - k0 + kV5Step - 1) / kV5Step;
+    const int first = slt.pos - n_keys + 1;   // logical position of key 0
+    const int cap = slt.cap;
+    const size_t layer_off = (size_t)p.layer * cap * kKvDim + kvh * kHeadDim + 4 * lane;
+    const float *kbase = slt.k_ring + layer_off;
+    const float *vbase = slt.v_ring + layer_off;
+    const int n_old = max(0, min(slt.fresh, slt.pos) - first);   // keys [0, n_old) predate this launch
+    // key j's ring row: one modulo per warp, then a conditional wrap (the
+    // warp's keys span fewer than cap positions)
+    const int slot0 = (first + k0) % cap;
+    auto row_of = [&](int j) {
+        int sl = slot0 + (j - k0);
+        sl = sl >= cap ? sl - cap : sl;
+        return (size_t)sl * kKvDim;
+    };
+
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 kc[kV5Step], vc[kV5Step], kn[kV5Step], vn[kV5Step];   // step i, step i + 1
+#pragma unroll
+    for (int u = 0; u < kV5Step; u++) kc[u] = vc[u] = kn[u] = vn[u] = z4;
+    // steps 0 and 1: keys older than the launch before the wait (they
+    // overlap the producer kernel's tail), this launch's own after it
+#pragma unroll
+    for (int u = 0; u < kV5Step; u++) {
+        const int j0 = k0 + u, j1 = k0 + kV5Step + u;
+        if (j0 < k1 && j0 < n_old) kc[u] = ldcg4(kbase + row_of(j0)), vc[u] = ldcg4(vbase + row_of(j0));
+        if (j1 < k1 && j1 < n_old) kn[u] = ldcg4(kbase + row_of(j1)), vn[u] = ldcg4(vbase + row_of(j1));
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+#pragma unroll
+    for (int u = 0; u < kV5Step; u++) {
+        const int j0 = k0 + u, j1 = k0 + kV5Step + u;
+        if (j0 < k1 && j0 >= n_old) kc[u] = ldcg4(kbase + row_of(j0)), vc[u] = ldcg4(vbase + row_of(j0));
+        if (j1 < k1 && j1 >= n_old) kn[u] = ldcg4(kbase + row_of(j1)), vn[u] = ldcg4(vbase + row_of(j1));
+    }
+    float4 q[4];   // the KV head's 4 query heads, this lane's 4 dims
+#pragma unroll
+    for (int h = 0; h < 4; h++) q[h] = ldcg4(p.q + (size_t)m * kQDim + (kvh * 4 + h) * kHeadDim + 4 * lane);
+
+    // scores in log2 units: p = 2^(s * scale * log2 e - m)
+    const float scale2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
+    const int kl = lane >> 3, hl = (lane >> 1) & 3;   // the (key, head) whose score this lane ends with
+    float m_run = -INFINITY, l_run = 0.f;              // head hl's running max (log2 units) / sum
+    float4 o[4] = {z4, z4, z4, z4};                    // unnormalised output, 4 heads x this lane's dims
+    float *pkw = reinterpret_cast<float *>(sh.pk[warp]);
+    float *alw = reinterpret_cast<float *>(&sh.alpha[warp]);
+    // step i from (ck, cv); step i + 1 goes out into (nk, nv) first (steps 0
+    // and 1 went out above).  Two calls per loop pass swap the buffers.
+    auto step = [&](int i, float4 *ck, float4 *cv, float4 *nk, float4 *nv) {
+        if (i >= 1 && i + 1 < nsteps) {
+#pragma unroll
+            for (int u = 0; u < kV5Step; u++) {
+                const int j = k0 + (i + 1) * kV5Step + u;
+                nk[u] = j < k1 ? ldcg4(kbase + row_of(j)) : z4;
+                nv[u] = j < k1 ? ldcg4(vbase + row_of(j)) : z4;
+            }
+        }
+        float a[16];   // a[4u + h]: q_h . k_u over this lane's 4 dims
+#pragma unroll
+        for (int u = 0; u < kV5Step; u++)
+#pragma unroll
+            for (int h = 0; h < 4; h++) a[4 * u + h] = dot4(q[h], ck[u]);
+        xhalve<8>(a, lane & 16, 16);
+        xhalve<4>(a, lane & 8, 8);
+        xhalve<2>(a, lane & 4, 4);
+        xhalve<1>(a, lane & 2, 2);
+        a[0] += __shfl_xor_sync(0xffffffffu, a[0], 1);
+        const bool valid = k0 + i * kV5Step + kl < k1;
+        const float sc = valid ? a[0] * scale2 : -INFINITY;
+        float tm = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 8));
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
+        // the running max moves only when a score exceeds it by more than
+        // 2^8 (p stays <= 256): most steps then need no rescale
+        const float nm = (tm > m_run + kV5Lazy) ? tm : m_run;   // finite: the step's first key is valid
+        const float pj = valid ? ex2f(sc - nm) : 0.f;
+        float ps = pj + __shfl_xor_sync(0xffffffffu, pj, 8);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+        const bool moved = __any_sync(0xffffffffu, nm != m_run);   // warp-uniform
+        float alpha = 1.0f;
+        if (moved) alpha = (m_run == -INFINITY) ? 0.f : ex2f(m_run - nm);
+        l_run = l_run * alpha + ps;
+        m_run = nm;
+        if ((lane & 1) == 0) pkw[lane >> 1] = pj;   // = pk[kl][hl]
+        if (moved && (lane & 0x19) == 0) alw[hl] = alpha;   // lanes 0, 2, 4, 6
+        __syncwarp();
+        float4 pk[kV5Step];
+#pragma unroll
+        for (int u = 0; u < kV5Step; u++) pk[u] = sh.pk[warp][u];
+        if (moved) {
+            const float4 al = sh.alpha[warp];
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                const float ah = comp4(al, h);
+                o[h] = make_float4(o[h].x * ah, o[h].y * ah, o[h].z * ah, o[h].w * ah);
+            }
+        }
+        __syncwarp();   // read before the next step's writes
+#pragma unroll
+        for (int h = 0; h < 4; h++)
+#pragma unroll
+            for (int u = 0; u < kV5Step; u++) fma4(o[h], comp4(pk[u], h), cv[u]);
+    };
+    for (int i = 0; i < nsteps; i += 2) {
+        step(i, kc, vc, kn, vn);
+        if (i + 1 < nsteps) step(i + 1, kn, vn, kc, vc);
+    }
+
+    // ---- the warps' partials -> this CTA's (threads 0..127: head, 4 dims) ----
+#pragma unroll
+    for (int h = 0; h < 4; h++) sh.o[warp][h][lane] = o[h];
+    if ((lane & 0x19) == 0) sh.ml[warp][hl] = make_float2(m_run, l_run);
+    __syncthreads();
+    const int hh = (tid >> 5) & 3, c = lane;   // (threads >= 128 only help with the cross-CTA merge)
+    float4 co = z4;
+    float cm = -INFINITY, cl = 0.f;
+    if (tid < 128) {
+#pragma unroll
+        for (int w = 0; w < NW; w++)
+            if (sh.ml[w][hh].y > 0.f) cm = fmaxf(cm, sh.ml[w][hh].x);
+#pragma unroll
+        for (int w = 0; w < NW; w++) {
+            const float2 ml = sh.ml[w][hh];
+            const float cw = ml.y > 0.f ? ex2f(ml.x - cm) : 0.f;
+            cl += ml.y * cw;
+            fma4(co, cw, sh.o[w][hh][c]);
+        }
+    }
+    const int hg = kvh * 4 + hh;   // query head
+    if (P == 1) {   // the row's only CTA: the output itself
+        if (tid < 128) {
+            const float inv = cl > 0.f ? 1.0f / cl : 0.f;
+            attn_store_out(p, m, hg * kHeadDim + 4 * c, co.x * inv, co.y * inv, co.z * inv, co.w * inv);
+        }
+        return;
+    }
+    if (tid < 128) {
+        const size_t pidx = ((size_t)m * kDecHeads + hg) * p.S + blockIdx.x;
+        reinterpret_cast<float4 *>(p.part_o + pidx * kHeadDim)[c] = co;
+        if (c == 0) {
+            p.part_ml[pidx * 2] = cm;
+            p.part_ml[pidx * 2 + 1] = cl;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sh.last = (atomicAdd(&p.counters[m * kDecKvHeads + kvh], 1u) + 1u == (unsigned)P);
+    __syncthreads();
+    if (!sh.last) return;
+    __threadfence();
+
+    // ---- merge the P partials (last CTA of this row / KV head) ----
+    for (int i = tid; i < 4 * P; i += NW * 32) {
+        const int h = i / P, t = i % P;
+        const size_t pidx = ((size_t)m * kDecHeads + kvh * 4 + h) * p.S + t;
+        sh.mw[h][t] = __ldcg(p.part_ml + pidx * 2);
+        sh.lw[h][t] = __ldcg(p.part_ml + pidx * 2 + 1);
+    }
+    __syncthreads();
+    if (warp < 4) {   // warp h: the head's maximum, the partials' weights, the total sum
+        float gm = -INFINITY;
+        for (int t = lane; t < P; t += 32)
+            if (sh.lw[warp][t] > 0.f) gm = fmaxf(gm, sh.mw[warp][t]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, off));
+        float gd = 0.f;
+        for (int t = lane; t < P; t += 32) {
+            const float w = sh.lw[warp][t] > 0.f ? ex2f(sh.mw[warp][t] - gm) : 0.f;
+            gd += sh.lw[warp][t] * w;
+            sh.mw[warp][t] = w;
+        }
+        gd = warp_sum(gd);
+        if (lane == 0) sh.gl[warp] = gd;
+    }
+    __syncthreads();
+    // thread group g (128 threads: head, 4 dims) sums partials g, g + NW/4, ...
+    constexpr int G = NW / 4;
+    const int g = tid >> 7;
+    const float4 *src = reinterpret_cast<const float4 *>(p.part_o) + ((size_t)m * kDecHeads + hg) * p.S * (kHeadDim / 4) + c;
+    float4 acc = z4;
+    int t = g;
+    for (; t + 7 * G < P; t += 8 * G) {   // eight loads in flight
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = __ldcg(src + (size_t)(t + u * G) * (kHeadDim / 4));
+#pragma unroll
+        for (int u = 0; u < 8; u++) fma4(acc, sh.mw[hh][t + u * G], v[u]);
+    }
+    for (; t < P; t += G) fma4(acc, sh.mw[hh][t], __ldcg(src + (size_t)t * (kHeadDim / 4)));
+    if constexpr (G > 1) {
+        sh.grp[g][tid & 127] = acc;
+        __syncthreads();
+        if (g != 0) return;
+        acc = z4;
+#pragma unroll
+        for (int j = 0; j < G; j++) {
+            const float4 v = sh.grp[j][tid];
+            acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+        }
+    }
+    const float inv = sh.gl[hh] > 0.f ? 1.0f / sh.gl[hh] : 0.f;
+    attn_store_out(p, m, hg * kHeadDim + 4 * c, acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    if (tid == 0) p.counters[m * kDecKvHeads + kvh] = 0u;
+}
+
 // CTAs per (stream, KV head): each loops over splits blockIdx.x + G*i.
 // v4: CTAs per (row, KV head).  A long context (8192 keys = 256 tiles) at
 // M = 1 gets 48 CTAs of ~5 pipelined tiles (3 CTAs/SM x 148 SMs over the 8 KV
@@ -526,18 +811,18 @@ int attn_deep_ctas_per_head(int M) {
     return g < 1 ? 1 : g;
 }
 
-// Long contexts take the deep variant: 2 tiles in flight per CTA keep
-// ~128 KB of keys moving per SM, where v4's 3 CTAs x 1 tile do ~96 KB.  The
-// caller passes a hint of the keys it expects (0: unknown, v4).
-// VOX_CUDA_ATTN = deep forces it.
+// The deep v4 variant: 2 tiles in flight per CTA keep ~128 KB of keys
+// moving per SM, where v4's 3 CTAs x 1 tile do ~96 KB.  Only on request
+// (VOX_CUDA_ATTN = deep): long contexts take v5 (attn_use_v5).
 bool attn_use_deep(int M, int keys_hint) {
+    (void)M;
+    (void)keys_hint;
     static int forced = -1;
     if (forced < 0) {
         const char *e = getenv("VOX_CUDA_ATTN");
-        forced = (e && strcmp(e, "deep") == 0) ? 1 : (e && strcmp(e, "v4") == 0) ? 0 : -2;
+        forced = (e && strcmp(e, "deep") == 0) ? 1 : 0;
     }
-    if (forced >= 0) return forced == 1;
-    return M <= 2 && keys_hint >= kAttnDeepKeys;
+    return forced == 1;
 }
 
 int attn_ctas_per_head(int M) {
@@ -551,12 +836,6 @@ int attn_ctas_per_head(int M) {
     return g < 16 ? 16 : g;
 }
 
-__global__ void set_slot_kernel(StreamSlot *dst, StreamSlot v) { *dst = v; }
-
-cudaError_t launch_set_slot(StreamSlot *dst, const StreamSlot &v, cudaStream_t st) {
-    set_slot_kernel<<<1, 1, 0, st>>>(dst, v);
-    return cudaGetLastError();
-}
 
 // Which kernel for a launch of M rows.  Measured on B200: v4's pipelined
 // tiles win for one or two rows (one stream at 740 keys: 1.605 vs 1.641
@@ -572,10 +851,60 @@ static bool attn_use_v3(int M) {
     return forced == 3 || (forced == 0 && M > 2);
 }
 
+// v5 (keys in registers) for one or two rows of long contexts (the caller's
+// hint of the keys per row >= kAttnDeepKeys).  Measured on B200, stand-alone
+// (one row, device time after an L2 flush): 8192 keys 24.6 us against 30.7
+// (v4, 3 tile buffers), 2048 keys 16.4 against 18.5; one stream's decode
+// step at 740 keys ties with v4 (1.582 / 1.585 ms per token); 8 streams'
+// step is slower than v3 (1.82 against 1.72 ms: v3 stages a whole 64-key
+// split per CTA before griddepcontrol.wait, v5 two 4-key steps per warp).
+// VOX_CUDA_ATTN = v5 forces it for every launch; VOX_CUDA_ATTN_V5_CTAS /
+// _MINKEYS set its CTAs per (row, KV head) and the fewest keys per CTA.
+static bool attn_use_v5(int M, int keys_hint) {
+    static int forced = -1;
+    if (forced < 0) {
+        const char *e = getenv("VOX_CUDA_ATTN");
+        forced = (e && strcmp(e, "v5") == 0) ? 1 : (e && *e) ? 0 : 2;
+    }
+    if (forced != 2) return forced == 1;
+    return M <= 2 && keys_hint >= kAttnDeepKeys;
+}
+
+static int env_pos(const char *name) {
+    const char *e = getenv(name);
+    return (e && atoi(e) > 0) ? atoi(e) : 0;
+}
+
+static cudaError_t launch_attn_v5(int M, const AttnParams &p, cudaStream_t st, bool pdl, int dev) {
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // one or two rows (long contexts): 8-warp CTAs, two per SM over the KV
+    // heads; more rows: 4-warp CTAs, 16 per (row, KV head) at most
+    const bool wide = M <= 2;
+    int g = wide ? std::max(1, 2 * sms / (kDecKvHeads * M)) : 16;
+    if (env_pos("VOX_CUDA_ATTN_V5_CTAS")) g = env_pos("VOX_CUDA_ATTN_V5_CTAS");
+    g = std::min(g, std::max(1, std::min(p.S, kAttnSplits)));
+    AttnParams q = p;
+    q.min_keys = env_pos("VOX_CUDA_ATTN_V5_MINKEYS") ? env_pos("VOX_CUDA_ATTN_V5_MINKEYS") : wide ? 64 : 32;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(g, kDecKvHeads, M);
+    cfg.blockDim = dim3(wide ? 256 : 128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return wide ? cudaLaunchKernelEx(&cfg, attn_decode_v5_kernel<8>, q)
+                : cudaLaunchKernelEx(&cfg, attn_decode_v5_kernel<4>, q);
+}
+
 cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (p.variant != 4 && attn_use_v5(M, p.deep_hint)) return launch_attn_v5(M, p, st, pdl, dev);
     const bool v3 = attn_use_v3(M);
     static std::atomic<uint64_t> attr_set{0};   // the shared-memory opt-in is per device
     const uint64_t bit = 1ull << (dev & 63);

@@ -722,21 +722,42 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // A and W are both re-read by other tiles (A by every column tile, W by
+    // every row tile); keep both in L2.
+    uint64_t pol = 0;
+    // The first unit's first S weight stages go out before the dependency
+    // wait: W is never written by the kernel this launch depends on (every
+    // programmatic-dependent launch passes resident weights), so the weight
+    // stream overlaps the previous kernel's tail; A follows the wait.
+    int pre = 0;
+    if (threadIdx.x == 0) {
+        asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+        if ((int)blockIdx.x < units) {
+            const int t = (int)blockIdx.x / KS, ks = (int)blockIdx.x % KS, n0 = (t / MT) * BN;
+            const int kb0 = ks * KB / KS, nkb = (ks + 1) * KB / KS - kb0;
+            pre = nkb < S ? nkb : S;
+            for (int s = 0; s < pre; s++) {
+                mbar_expect_tx(&full[s], Cfg::kABytes + Cfg::kBBytes);
+                tma_load_2d(sB + s * Cfg::kBBytes, &tmB, (kb0 + s) * kBK, n0, &full[s], pol);
+            }
+        }
+    }
+
     grid_dep_wait();
     grid_dep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
-            // A and W are both re-read by other tiles (A by every column tile,
-            // W by every row tile); keep both in L2.
-            uint64_t pol;
-            asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
             uint32_t it = 0;
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
                 const int t = u / KS, ks = u % KS;
                 const int m0 = (t % MT) * kBM, n0 = (t / MT) * BN;
                 for (int kb = ks * KB / KS; kb < (ks + 1) * KB / KS; kb++, it++) {
                     const int s = it % S;
+                    if (it < (uint32_t)pre) {   // its W is in flight already
+                        tma_load_2d(sA + s * Cfg::kABytes, &tmA, kb * kBK, m0, &full[s], pol);
+                        continue;
+                    }
                     if (it >= (uint32_t)S && !mbar_wait(&empty[s], ((it / S) + 1) & 1u, deadline)) {
                         ok = false;
                         break;
@@ -1231,6 +1252,11 @@ int env_tc_pair() {
     return (s && *s) ? atoi(s) : -1;
 }
 
+int env_int(const char *name) {
+    const char *s = getenv(name);
+    return (s && *s) ? atoi(s) : 0;
+}
+
 int env_tc_bn() {
     const char *s = getenv("VOX_CUDA_TC_BN");
     const int n = s ? atoi(s) : 0;
@@ -1353,13 +1379,19 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
         const int mt = p.hilo ? (p.M + 63) / 64 : (p.M + kBM - 1) / kBM, KB = (p.K + kBK - 1) / kBK;
         // measured at M = 100 with the lane-contiguous workspace: a win for
         // K = 5120 (w2) and K = 2048 (wo, 2.45 -> 2.32 ms per 32-layer chunk)
-        if (2 * mt * ((p.N + bn - 1) / bn) < sms && KB >= kTcSplitMinKB) {
+        // VOX_CUDA_TC_SPLIT_MINKB / _BW / _MAX override the gate's k-block
+        // minimum, the split tile width (also used for the gate) and the
+        // slice cap
+        const int e_minkb = env_int("VOX_CUDA_TC_SPLIT_MINKB"), e_bw = env_int("VOX_CUDA_TC_SPLIT_BW"),
+                  e_max = env_int("VOX_CUDA_TC_SPLIT_MAX");
+        const int gate_bn = (e_bw == 64 || e_bw == 128 || e_bw == 256) && !p.hilo ? e_bw : bn;
+        if (2 * mt * ((p.N + gate_bn - 1) / gate_bn) < sms && KB >= (e_minkb > 0 ? e_minkb : kTcSplitMinKB)) {
             // the last slice to finish sums the others: few slices and
             // narrow tiles keep that sum short (one 32-column chunk per warp)
             const int fe = (p.hilo && env_tc_bn() > 128) ? 128 : env_tc_bn();   // (split activations: <= 128)
-            const int bw = fe ? fe : (p.hilo || p.N >= 4096 ? 128 : 64);
+            const int bw = gate_bn != bn ? gate_bn : fe ? fe : (p.hilo || p.N >= 4096 ? 128 : 64);
             const int tiles = mt * ((p.N + bw - 1) / bw);
-            int ks = std::min(kTcMaxSplit, std::min(sms / tiles, KB / 4));
+            int ks = std::min(e_max >= 2 && e_max <= 8 ? e_max : kTcMaxSplit, std::min(sms / tiles, KB / 4));
             // one 128 x bw region set per tile and slice (split_region)
             ks = (int)std::min<size_t>((size_t)ks, p.ws_floats / ((size_t)tiles * kBM * bw));
             const char *ev = getenv("VOX_CUDA_TC_KSPLIT");

@@ -97,10 +97,14 @@ struct AttnParams {
     int S;                    // key splits per KV head
     const void *pf;           // weights of a later kernel to start pulling into L2 (or NULL)
     unsigned long long pf_bytes;   // a multiple of 16
-    int deep_hint;            // keys the caller expects per row (0: unknown); selects the deep variant
+    int deep_hint;            // keys the caller expects per row (0: unknown); selects v5 for long contexts
+    int min_keys;             // v5: fewest keys per CTA (set by launch_attn_decode)
+    StreamSlot slot1;         // with slot_inline (M = 1): the row's slot by value, slots unused
+    int slot_inline;
+    int variant;              // 0: chosen by launch_attn_decode; 4: the v4 kernel
 };
 constexpr int kAttnSplits = 128;   // >= 8192 / 64 keys per split
-constexpr int kAttnDeepKeys = 2048;  // keys from which one or two rows take the deep attention variant
+constexpr int kAttnDeepKeys = 2048;  // keys from which one or two rows take the v5 attention kernel
 
 // fp16 range events of the encoder path since the last reset, on the
 // current device (vc_gemm_tc.cu: clamped SwiGLU output chunks and
@@ -144,8 +148,6 @@ size_t persist_gpart_floats(const PersistParams &p);
 cudaError_t launch_step_persist(const PersistParams &p, cudaStream_t st, int *grid_out);
 
 cudaError_t launch_attn_decode(int M, const AttnParams &p, cudaStream_t st, bool pdl);
-// *dst = v in stream order (the descriptor travels as a kernel argument)
-cudaError_t launch_set_slot(StreamSlot *dst, const StreamSlot &v, cudaStream_t st);
 
 // Alternatives from device logits (stream_fill_alts semantics).
 cudaError_t launch_fill_alts(const float *logits, int vocab, const int *best, int n_alt,
@@ -220,7 +222,9 @@ constexpr int kTcSplitCounters = 4096;   // split-K tickets a caller provides (8
 constexpr size_t kEncSplitFloats = (size_t)4 << 20;   // the encoder state's split-K workspace (16 MB)
 
 // C = A . W^T with bf16 A [M, K] and W [N, K] (row-major, 16-byte aligned,
-// K % 8 == 0).  bn = 0 picks the tile width.
+// K % 8 == 0).  bn = 0 picks the tile width.  With pdl the kernel starts
+// loading W before the preceding kernel has finished: W must not be written
+// by that kernel (resident weights only).
 cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p, const void *A, const void *W, cudaStream_t st,
                            bool pdl, int bn = 0);
 int tc_gemm_bn(int M, int N);

@@ -113,6 +113,7 @@ extern "C" int vox_cuda_attention_decode_noalloc(const float *q, const float *k_
     p.part_o = base + kPartOff + kPartML;
     p.counters = tickets;
     p.S = kAttnSplits;
+    p.variant = 4;   // this entry keeps the v4 kernel its scratch was sized and tested for
     cudaError_t e = launch_attn_decode(1, p, st, false);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);   // h lives on this stack frame
     if (e != cudaSuccess) {

@@ -546,12 +546,13 @@ extern "C" int vox_cuda_attention_decode_dev(const float *q, const float *k_ring
     // the scratch is shared: a call on another stream waits for the last one
     if (!c->attn_done) VC_TRY(cudaEventCreateWithFlags(&c->attn_done, cudaEventDisableTiming));
     else VC_TRY(cudaStreamWaitEvent(st, c->attn_done, 0));
-    // the slot descriptor travels by value into a stream-ordered write, so
+    // the slot descriptor travels by value in the launch's parameters, so
     // back-to-back calls neither race on it nor wait on the host
-    VC_TRY(launch_set_slot(c->attn_slot, h, st));
     AttnParams p = {};
     p.q = q;
     p.slots = c->attn_slot;
+    p.slot1 = h;
+    p.slot_inline = 1;
     p.layer = 0;
     p.out = out;
     p.part_o = c->attn_part_o;
