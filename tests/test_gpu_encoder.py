@@ -147,6 +147,31 @@ def test_encoder_split_k_matches_unsplit(monkeypatch):
         assert B.rel_l2(a, b) < 2e-3, (i, B.rel_l2(a, b))
 
 
+def test_folded_norm_matches_separate_norm_pass_and_oracle(monkeypatch):
+    """The RMSNorms folded into the GEMMs (the residual epilogues write
+    fp16(x * w) and per-chunk sums of squares, the consumers scale their rows
+    by 1 / rms) against the separate normalisation pass
+    (VOX_CUDA_ENC_FOLD_NORM=0) and the oracle: ragged chunks, the single-state
+    path and the batched one."""
+    ew = B.EncoderWeights(seed=16, n_layers=3, distinct=3, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    sizes = [100, 37, 256, 3]
+    xs = [B.normal_f32((n, B.ENC_DIM), 1160 + i) for i, n in enumerate(sizes)]
+    outs = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("VOX_CUDA_ENC_FOLD_NORM", mode)
+        st = e.state(max_chunk=256)
+        outs[mode] = [st.step(x) for x in xs]
+        st.free()
+    o = B.OracleEncoder(ew, kv_max=2400)
+    ref = [o.step(x) for x in xs]
+    for i in range(len(sizes)):
+        assert np.isfinite(outs["1"][i]).all()
+        assert B.rel_l2(outs["1"][i], outs["0"][i]) < 2e-3, (i, B.rel_l2(outs["1"][i], outs["0"][i]))
+        assert B.rel_l2(outs["1"][i], ref[i]) < 5e-3, (i, B.rel_l2(outs["1"][i], ref[i]))
+    e.free()
+
+
 def test_encoder_tile_widths_agree(monkeypatch):
     """The tensor-core GEMM's tile width (64 / 128 / 192 / 256 columns, picked
     by a rounds x tile-cost model) changes which CTA computes an output

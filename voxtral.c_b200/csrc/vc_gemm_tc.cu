@@ -125,7 +125,26 @@ struct EpiRow {
     uint16_t *ek, *ev;   // TC_QKV_ENC: the row's rings (this layer)
     int ecap;            // TC_QKV_ENC: their capacity
     float *kd, *vd; // TC_QKV_DEC: the row's K / V ring rows (this layer)
+    float rs;       // ss_in: the row's 1 / rms (else 1)
 };
+
+// 1 / sqrt(mean square + eps) of a row from its per-32-column-chunk sums of
+// squares (K / 32 chunks, summed in chunk order: the same value whatever
+// the producer's tile width); eight loads in flight
+__device__ __forceinline__ float row_inv_rms(const float *ss, int ld, int row, int K) {
+    const int nch = K / kEpiCols;
+    float acc = 0.f;
+    int c = 0;
+    for (; c + 8 <= nch; c += 8) {
+        float t[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) t[u] = __ldcg(ss + (size_t)(c + u) * ld + row);
+#pragma unroll
+        for (int u = 0; u < 8; u++) acc += t[u];
+    }
+    for (; c < nch; c++) acc += __ldcg(ss + (size_t)c * ld + row);
+    return 1.0f / sqrtf(acc / (float)K + kNormEps);
+}
 
 // The per-row facts of TC_QKV_ENC / TC_QKV_DEC for output row `row`.
 template <int EPI>
@@ -137,6 +156,7 @@ __device__ __forceinline__ EpiRow epi_row(const TcGemmParams &p, int row) {
     er.kd = er.vd = nullptr;
     er.ek = er.ev = nullptr;
     er.ecap = 0;
+    er.rs = 1.0f;   // (ss_in: set by the caller, computed before the accumulator is ready)
     if constexpr (EPI == TC_QKV_ENC) {
         if (p.segs) {   // several streams' rows: the row's segment (row0 ascending)
             int s = 0;
@@ -256,6 +276,41 @@ __device__ __forceinline__ int qkv_apply(const TcGemmParams &p, const EpiRow &er
     return 2;
 }
 
+// ss_in: the accumulator row times the row's 1 / rms (the consumer half of
+// the folded RMSNorm)
+template <int EPI>
+__device__ __forceinline__ void scale_row(const TcGemmParams &p, const EpiRow &er, float (&v)[kEpiCols]) {
+    if constexpr (EPI == TC_QKV_ENC || EPI == TC_SWIGLU) {
+        if (p.ss_in) {
+#pragma unroll
+            for (int j = 0; j < kEpiCols; j++) v[j] *= er.rs;
+        }
+    }
+}
+
+// TC_RESID with xn_out: the updated residual chunk v (32 columns from col0,
+// all inside N) -> its sum of squares and fp16(v * gain) (the producer half
+// of the folded RMSNorm, vox_rms_norm at voxtral_kernels.c:346-363)
+__device__ __forceinline__ void norm_prep_chunk(const TcGemmParams &p, int row, int col0, const float (&v)[kEpiCols]) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kEpiCols; j++) ss = fmaf(v[j], v[j], ss);
+    p.ss_out[(size_t)(col0 / kEpiCols) * p.ss_ld + row] = ss;
+    uint32_t h[kEpiCols / 2], mx = 0;
+#pragma unroll
+    for (int j = 0; j < kEpiCols; j += 4) {
+        const float4 g = __ldg(reinterpret_cast<const float4 *>(p.xn_gain + col0 + j));
+        h[j >> 1] = pack_half2(v[j] * g.x, v[j + 1] * g.y);
+        h[(j >> 1) + 1] = pack_half2(v[j + 2] * g.z, v[j + 3] * g.w);
+        mx = f16x2_absmax(mx, h[j >> 1]);
+        mx = f16x2_absmax(mx, h[(j >> 1) + 1]);
+    }
+    count_clamped(mx);
+    uint16_t *o = p.xn_out + (size_t)row * p.ldo + col0;
+#pragma unroll
+    for (int j = 0; j < kEpiCols; j += 8) st16(o + j, h[j >> 1], h[(j >> 1) + 1], h[(j >> 1) + 2], h[(j >> 1) + 3]);
+}
+
 // Direct stores of one row's chunk [col0, col0 + 32), all inside N, 16-byte
 // aligned destinations (p.vec).  TC_QKV_ENC: bias / RoPE already applied.
 template <int EPI>
@@ -286,6 +341,9 @@ __device__ __forceinline__ void epi_vec(const TcGemmParams &p, const EpiRow &er,
 #pragma unroll
             for (int j = 0; j < kEpiCols; j += 4)
                 *reinterpret_cast<float4 *>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+        if constexpr (EPI == TC_RESID) {
+            if (p.xn_out) norm_prep_chunk(p, row, col0, v);
         }
     } else if constexpr (EPI == TC_SWIGLU) {
         // columns (2i, 2i+1) = (gate_i, up_i) -> h_i = silu(g) * u
@@ -336,6 +394,7 @@ __device__ __forceinline__ void epi_scalar(const TcGemmParams &p, const EpiRow &
     if constexpr (EPI == TC_STORE || EPI == TC_RESID) {
         add_bias(v, p.bias, col0, p.N);
         float *o = p.out + (size_t)row * p.ldo + col0;
+        float ss = 0.f;
 #pragma unroll
         for (int j = 0; j < kEpiCols; j++) {
             if (col0 + j >= p.N) break;
@@ -344,6 +403,17 @@ __device__ __forceinline__ void epi_scalar(const TcGemmParams &p, const EpiRow &
             if (p.act == 1) x = gelu_tanh(x);
             if (p.out_bf16) p.out_bf16[(size_t)row * p.ldo_bf16 + col0 + j] = bits16(x, p.f16);
             else o[j] = x;
+            if constexpr (EPI == TC_RESID) {
+                if (p.xn_out) {
+                    ss = fmaf(x, x, ss);
+                    const float xg = x * __ldg(p.xn_gain + col0 + j);
+                    p.xn_out[(size_t)row * p.ldo + col0 + j] = bits16(xg, 1);
+                    if (!(fabsf(xg) < 65504.0f)) atomicAdd(&g_f16_sat_gemm, 1ull);
+                }
+            }
+        }
+        if constexpr (EPI == TC_RESID) {
+            if (p.xn_out) p.ss_out[(size_t)(col0 / kEpiCols) * p.ss_ld + row] = ss;
         }
     } else if constexpr (EPI == TC_SWIGLU) {
         const int orow = p.out_hilo ? hilo_row(row) : row;
@@ -455,21 +525,68 @@ __device__ __forceinline__ void epi_tma(const TcGemmParams &p, const EpiMaps &mp
     }
 }
 
+// TC_RESID with the folded norm (direct stores): the warp's half of the BN
+// columns of its 32 rows, 32 columns per step.  Every step's residual line
+// (128 bytes of the row) is prefetched into L1 first, and each step issues
+// its residual loads before its accumulator read, so the L2 latency of the
+// read-modify-write overlaps; then x, fp16(x * gain) and the chunk sums.
+template <int BN>
+__device__ __forceinline__ void resid_norm_tile(const TcGemmParams &p, uint32_t tbase, int row, int n0, int half,
+                                                bool rv) {
+    constexpr int kSteps = BN / 2 / kEpiCols;
+    const int c0 = half * (BN / 2);
+    float *xr = p.out + (size_t)row * p.ldo + n0 + c0;
+    if (rv) {
+#pragma unroll
+        for (int i = 0; i < kSteps; i++)
+            if (n0 + c0 + i * kEpiCols < p.N) asm volatile("prefetch.global.L1 [%0];" ::"l"(xr + i * kEpiCols));
+    }
+#pragma unroll 1
+    for (int i = 0; i < kSteps; i++) {
+        const int c = c0 + i * kEpiCols, col0 = n0 + c;
+        const bool in = rv && col0 < p.N;
+        float4 r[kEpiCols / 4];
+#pragma unroll
+        for (int j = 0; j < kEpiCols / 4; j++)
+            r[j] = in ? *reinterpret_cast<const float4 *>(xr + i * kEpiCols + 4 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float v[kEpiCols];
+        tmem_ld32(tbase + (uint32_t)c, v);   // warp-collective: before any branch
+        if (!in) continue;
+        add_bias(v, p.bias, col0, p.N);
+#pragma unroll
+        for (int j = 0; j < kEpiCols / 4; j++)
+            v[4 * j] += r[j].x, v[4 * j + 1] += r[j].y, v[4 * j + 2] += r[j].z, v[4 * j + 3] += r[j].w;
+        float *o = xr + i * kEpiCols;
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 4)
+            *reinterpret_cast<float4 *>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        norm_prep_chunk(p, row, col0, v);
+    }
+}
+
 // The epilogue of one accumulator for one epilogue warp: this thread's row
 // (its TMEM lane) and the warp's half of the BN columns from n0, 32 columns
 // per tcgen05.ld.  row0 = the warp's first row.
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const TcGemmParams &p, const EpiMaps &mp, uint32_t tbase, int row0,
-                                              int n0, int half, int lane, unsigned char *stg) {
+                                              int n0, int half, int lane, unsigned char *stg, float rs = 1.0f) {
     static_assert(BN % (2 * kEpiCols) == 0, "each epilogue warp takes whole 32-column chunks");
-    const EpiRow er = epi_row<EPI>(p, row0 + lane);
+    EpiRow er = epi_row<EPI>(p, row0 + lane);
+    er.rs = rs;
     const bool rv = er.row < p.M;
+    if constexpr (EPI == TC_RESID) {
+        if (p.xn_out && p.vec && !p.tma_out) {
+            resid_norm_tile<BN>(p, tbase, er.row, n0, half, rv);
+            return;
+        }
+    }
 #pragma unroll 1
     for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
         float v[kEpiCols];
         tmem_ld32(tbase + (uint32_t)c, v);   // warp-collective: before any branch
         const int col0 = n0 + c;
         if (col0 >= p.N) continue;           // warp-uniform
+        scale_row<EPI>(p, er, v);
         if (p.tma_out) {
             epi_tma<EPI>(p, mp, er, v, row0, col0, lane, stg);
             continue;
@@ -514,8 +631,10 @@ __device__ __forceinline__ void split_partial(const TcGemmParams &p, uint32_t tb
 // whichever slice finished last) and run the epilogue on it.
 template <int BN, int EPI>
 __device__ __forceinline__ void split_finish(const TcGemmParams &p, const EpiMaps &mp, int row0, int n0, int half,
-                                             int lane, unsigned char *stg, int KS, int q, int t, int tiles) {
-    const EpiRow er = epi_row<EPI>(p, row0 + lane);
+                                             int lane, unsigned char *stg, int KS, int q, int t, int tiles,
+                                             float rs = 1.0f) {
+    EpiRow er = epi_row<EPI>(p, row0 + lane);
+    er.rs = rs;
     const bool rv = er.row < p.M;
     const size_t slice = (size_t)tiles * kEpiWarps * 16 * BN;   // floats between slices
     const float4 *src0 = reinterpret_cast<const float4 *>(p.ws + split_region(0, t, tiles, q, half, BN)) + lane;
@@ -547,6 +666,7 @@ __device__ __forceinline__ void split_finish(const TcGemmParams &p, const EpiMap
                 for (int j = 0; j < kEpiCols / 4; j++) cur[j] = nxt[j];
             }
         }
+        scale_row<EPI>(p, er, v);
         if (p.tma_out) {
             epi_tma<EPI>(p, mp, er, v, row0, col0, lane, stg);
             continue;
@@ -812,6 +932,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int u = blockIdx.x; u < units; u += gridDim.x, lt++) {
             const int t = u / KS, ks = u % KS;
             const uint32_t b = lt & 1u;
+            // ss_in: the row's 1 / rms while the accumulator is still being
+            // summed (with split-K whichever slice finishes last scales)
+            float rs = 1.0f;
+            if constexpr (!HILO && (EPI == TC_QKV_ENC || EPI == TC_SWIGLU)) {
+                const int r = (t % MT) * kBM + 32 * q + lane;
+                if (p.ss_in && r < p.M) rs = row_inv_rms(p.ss_in, p.ss_ld, r, p.K);
+            }
             const bool got = mbar_wait(&tfull[b], (lt >> 1) & 1u, deadline);
             if (!__all_sync(0xffffffffu, got)) {
                 ok = false;
@@ -853,7 +980,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 continue;
             }
             if (KS == 1) {
-                epilogue_tile<BN, EPI>(p, mp, tb, m0 + 32 * q, n0, half, lane, stg);
+                epilogue_tile<BN, EPI>(p, mp, tb, m0 + 32 * q, n0, half, lane, stg, rs);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[b]);
@@ -872,7 +999,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 prev = __shfl_sync(0xffffffffu, prev, 0);
                 if (prev == (unsigned)(KS - 1)) {
                     __threadfence();
-                    split_finish<BN, EPI>(p, mp, m0 + 32 * q, n0, half, lane, stg, KS, q, t, tiles);
+                    split_finish<BN, EPI>(p, mp, m0 + 32 * q, n0, half, lane, stg, KS, q, t, tiles, rs);
                     if (lane == 0) p.ws_cnt[t * kEpiWarps + (warp - 2)] = 0u;
                 }
             }
@@ -1314,12 +1441,19 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.K % 8 != 0 || !p.err || ((uintptr_t)A & 15) || ((uintptr_t)W & 15))
         return cudaErrorInvalidValue;
     if (epi == TC_SWIGLU && (p.N % 32 != 0)) return cudaErrorInvalidValue;
+    // the folded RMSNorm: producer TC_RESID (fp16), consumers TC_QKV_ENC /
+    // TC_SWIGLU; not with split activations
+    if (p.xn_out && (epi != TC_RESID || !p.xn_gain || !p.ss_out || p.ss_ld < p.M || !p.f16 || p.hilo))
+        return cudaErrorInvalidValue;
+    if (p.ss_in && ((epi != TC_QKV_ENC && epi != TC_SWIGLU) || p.ss_ld < p.M || p.K % 32 != 0 || p.hilo))
+        return cudaErrorInvalidValue;
     switch (epi) {
         case TC_STORE:
         case TC_RESID: {
             const bool need_out = epi == TC_RESID || !p.out_bf16;
             p.vec = (!p.bias || al16(p.bias)) && (!need_out || (al16(p.out) && p.ldo % 4 == 0)) &&
-                    (!p.out_bf16 || (al16(p.out_bf16) && p.ldo_bf16 % 8 == 0));
+                    (!p.out_bf16 || (al16(p.out_bf16) && p.ldo_bf16 % 8 == 0)) &&
+                    (!p.xn_out || (al16(p.xn_out) && al16(p.xn_gain) && p.ldo % 8 == 0));
             break;
         }
         case TC_SWIGLU: p.vec = al16(p.out_bf16) && p.ldo_bf16 % 8 == 0; break;
@@ -1341,13 +1475,16 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     memset(&mv, 0, sizeof(mv));
     const char *env_tma = getenv("VOX_CUDA_TC_TMA_OUT");
     // (the split-activation epilogue stores directly)
-    p.tma_out = (p.vec && !(env_tma && atoi(env_tma) == 0) && !p.hilo && make_out_maps(epi, p, &mo, &mk, &mv))
+    // (the folded norm's producer needs the updated residual in registers:
+    // direct stores, not the TMA reduce-add)
+    p.tma_out = (p.vec && !(env_tma && atoi(env_tma) == 0) && !p.hilo && !p.xn_out &&
+                 make_out_maps(epi, p, &mo, &mk, &mv))
                     ? 1
                     : 0;
     if (p.hilo && p.f16) return cudaErrorInvalidValue;   // the split is into bf16 halves
     // CTA pairs only on request: at the encoder shapes they measured no faster
     // than single-CTA tiles (the MMA pipe, not L2 -> SMEM traffic, is the limit)
-    const bool pair = env_tc_pair() == 1 && p.M > kBM && !p.hilo;
+    const bool pair = env_tc_pair() == 1 && p.M > kBM && !p.hilo && !p.ss_in && !p.xn_out;
     if (pair) {
         const int pbn = tc_gemm2_bn(p.M, p.N);
 #define VC_TC2_CASE(BN)                                                            \
@@ -1622,6 +1759,58 @@ cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const floa
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, rows_to_bf16_kernel, x, M, K, ld, w, out, vec, f16 ? 1 : 0);
+}
+
+// The first layer's half of the folded RMSNorm: row x -> fp16(x * w) and
+// the sums of squares of x per 32-column chunk, ss[c][row].  One warp per
+// row, the row in registers; lane l holds float4 i = l + 32 j, so the 8 lanes
+// of group l / 8 hold chunk 4 j + l / 8 (K % 128 == 0, K <= 2048).
+__global__ void __launch_bounds__(256)
+rows_prenorm_kernel(const float *x, int M, int K, const float *w, uint16_t *out, float *ss, int ss_ld) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)warp * K);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    uint2 *o = reinterpret_cast<uint2 *>(out + (size_t)warp * K);
+    const int nj = K / 128;
+    float4 a[kRowRegs];
+#pragma unroll
+    for (int j = 0; j < kRowRegs; j++)
+        if (j < nj) a[j] = x4[lane + 32 * j];
+    uint32_t mx = 0;
+#pragma unroll
+    for (int j = 0; j < kRowRegs; j++) {
+        if (j >= nj) break;
+        const int i = lane + 32 * j;
+        float s2 = fmaf(a[j].w, a[j].w, fmaf(a[j].z, a[j].z, fmaf(a[j].y, a[j].y, a[j].x * a[j].x)));
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
+        if ((lane & 7) == 0) ss[(size_t)(4 * j + (lane >> 3)) * ss_ld + warp] = s2;
+        const float4 g = __ldg(w4 + i);
+        const uint2 h = make_uint2(pack_half2(a[j].x * g.x, a[j].y * g.y), pack_half2(a[j].z * g.z, a[j].w * g.w));
+        mx = f16x2_absmax(f16x2_absmax(mx, h.x), h.y);
+        o[i] = h;
+    }
+    count_clamped(mx);
+}
+
+cudaError_t launch_rows_prenorm(const float *x, int M, int K, const float *w, uint16_t *out, float *ss, int ss_ld,
+                                cudaStream_t st, bool pdl) {
+    if (K % 128 != 0 || K > 32 * 4 * kRowRegs || ss_ld < M || !al16(x) || !al16(w) || ((uintptr_t)out & 7) != 0)
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((M + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, rows_prenorm_kernel, x, M, K, w, out, ss, ss_ld);
 }
 
 }  // namespace vc

@@ -214,6 +214,16 @@ struct TcGemmParams {
     // TC_QKV_ENC over several streams' rows (batched encoder), or NULL
     const EncSeg *segs;      // device [n_segs], row0 ascending
     int n_segs;
+    // RMSNorm folded into the GEMMs around it (encoder): TC_RESID also writes
+    // the next GEMM's operand fp16(x * xn_gain) (x the updated residual, not
+    // yet normalised) and, per row, the sum of squares of x over each
+    // 32-column chunk; TC_QKV_ENC / TC_SWIGLU scale accumulator row r by
+    // 1 / sqrt(sum / K + eps) from those sums (ss_in) before their epilogue
+    uint16_t *xn_out;        // TC_RESID: [M][ldo] fp16, or NULL
+    const float *xn_gain;    // TC_RESID: [N], the next norm's weights
+    float *ss_out;           // TC_RESID: [N / 32][ss_ld]
+    const float *ss_in;      // TC_QKV_ENC / TC_SWIGLU: [K / 32][ss_ld], or NULL
+    int ss_ld;               // rows per chunk plane (>= M)
     int vec;                 // set by launch_tc_gemm: all destinations allow 16-byte stores
     int tma_out;             // set by launch_tc_gemm: the epilogue stores through TMA
 };
@@ -231,6 +241,11 @@ int tc_gemm_bn(int M, int N);
 // fp32 rows -> bf16 (or fp16, f16) rows, optionally RMS-normalised with weights w.
 cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const float *w, uint16_t *out,
                                 cudaStream_t st, bool pdl, bool f16 = false);
+// fp32 rows -> fp16(x * w) rows (not normalised) and, per row, the sum of
+// squares of x over each 32-column chunk, ss[K / 32][ss_ld]: the operand and
+// the row scales of a consumer GEMM with ss_in (K % 128 == 0, K <= 2048)
+cudaError_t launch_rows_prenorm(const float *x, int M, int K, const float *w, uint16_t *out, float *ss, int ss_ld,
+                                cudaStream_t st, bool pdl);
 // In place: bf16 -> fp16 (round to nearest even; the values of bf16 weights
 // are inside fp16's range).
 // fp32 rows -> bf16 hi / lo rows in the hilo_row layout, v = x
