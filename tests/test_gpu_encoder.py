@@ -172,6 +172,30 @@ def test_folded_norm_matches_separate_norm_pass_and_oracle(monkeypatch):
     e.free()
 
 
+def test_encoder_attention_key_split_matches_unsplit(monkeypatch):
+    """Chunks of few row tiles split each tile's key blocks over up to 4 CTAs
+    (unnormalised partials merged by the last CTA): against the unsplit
+    kernel (VOX_CUDA_ENC_ATTN_KSPLIT=1), from position 0 (splits with no key
+    block) through window-crossing and ragged chunks, and against the oracle."""
+    ew = B.EncoderWeights(seed=17, n_layers=2, distinct=2, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    sizes = [100, 37, 256, 3, 100, 64]
+    xs = [B.normal_f32((n, B.ENC_DIM), 1170 + i) for i, n in enumerate(sizes)]
+    outs = {}
+    for mode in ("1", ""):
+        monkeypatch.setenv("VOX_CUDA_ENC_ATTN_KSPLIT", mode)
+        st = e.state(max_chunk=256)
+        outs[mode] = [st.step(x) for x in xs]
+        st.free()
+    o = B.OracleEncoder(ew, kv_max=2400)
+    for i, x in enumerate(xs):
+        ref = o.step(x)
+        assert np.isfinite(outs[""][i]).all()
+        assert B.rel_l2(outs[""][i], outs["1"][i]) < 1e-3, (i, B.rel_l2(outs[""][i], outs["1"][i]))
+        assert B.rel_l2(outs[""][i], ref) < 5e-3, (i, B.rel_l2(outs[""][i], ref))
+    e.free()
+
+
 def test_encoder_tile_widths_agree(monkeypatch):
     """The tensor-core GEMM's tile width (64 / 128 / 192 / 256 columns, picked
     by a rounds x tile-cost model) changes which CTA computes an output

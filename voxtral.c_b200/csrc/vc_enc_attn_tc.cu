@@ -28,6 +28,10 @@
 // positions and the ring capacity is a multiple of 128, so a block never
 // wraps in the ring.  Every mbarrier wait is bounded (2 s of %globaltimer);
 // on expiry the CTA raises the error word and exits after a grace period.
+// Key split (chunks with few row tiles, e.g. 100 rows = 32 tiles): blockIdx.z
+// takes consecutive key blocks of the tile's range; the softmax threads leave
+// their row's unnormalised o, running max and sum in a workspace, and the
+// last of the tile's ksplit CTAs to finish (atomic ticket) merges them.
 #include "vc_common.cuh"
 #include "vc_internal.h"
 #include "vc_tc.cuh"
@@ -51,6 +55,9 @@ constexpr uint64_t kFaWaitNs = 2000000000ull;
 constexpr float kFaRescale = 8.0f;   // log2 of the largest P before the max moves
 constexpr int kFaKStages = 3;        // K ring depth
 constexpr int kFaVStages = 2;        // V ring depth
+constexpr int kFaPartFloats = kEncHeadDim + 4;   // a key split's row partial: o, max, sum (16-byte rows)
+constexpr int kFaMaxSplit = 8;                   // key splits at most
+constexpr size_t kFaSpreadSmem = 120 * 1024;     // > half an SM's shared memory: one CTA per SM
 
 struct FaSmem {
     unsigned char q[kFaRows * 128];                // Q [128 rows][64 dims] fp16, 128-byte swizzle
@@ -61,6 +68,7 @@ struct FaSmem {
     uint64_t k_full[kFaKStages], k_empty[kFaKStages];
     uint64_t v_full[kFaVStages], v_empty[kFaVStages];
     uint32_t tmem;
+    int last;   // key split: this CTA merges
 };
 
 // Instruction descriptor, kind::f16 with fp16 A and B (format 0), fp32 D;
@@ -77,6 +85,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_mn(const void *p) {
     const uint64_t addr = smem_u32(p);
     return ((addr >> 4) & 0x3FFFull) | ((uint64_t)(16384 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
            (1ull << 46) | (2ull << 61);
+}
+
+// barrier `id` over `n` threads (whole warps; id 0 is __syncthreads')
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -140,8 +153,13 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const int pos0 = p.pos0_dev ? *p.pos0_dev : p.pos0;
     const int p_first = pos0 + r0;
     const int p_last = pos0 + min(r0 + kFaRows, M) - 1;
-    const int kstart = max(0, p_first - (kEncWindow - 1)) / kFaKeys * kFaKeys;
-    const int nb = (p_last - kstart) / kFaKeys + 1;
+    const int kall = max(0, p_first - (kEncWindow - 1)) / kFaKeys * kFaKeys;
+    const int nball = (p_last - kall) / kFaKeys + 1;
+    // this CTA's key blocks: all, or split z of KZ (possibly none)
+    const int KZ = p.ksplit > 1 ? p.ksplit : 1, z = blockIdx.z;
+    const int bz0 = z * nball / KZ, bz1 = (z + 1) * nball / KZ;
+    const int kstart = kall + bz0 * kFaKeys;
+    const int nb = bz1 - bz0;
 
     if (!ok) {
         // misaligned shared memory: nothing was issued
@@ -149,8 +167,10 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         if (lane == 0) {
             uint64_t pol;
             asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-            mbar_expect_tx(&sh.q_full, kFaRows * 128);
-            tma_load_2d(sh.q, &tmQ, head * kEncHeadDim, r0, &sh.q_full, pol);
+            if (nb > 0) {
+                mbar_expect_tx(&sh.q_full, kFaRows * 128);
+                tma_load_2d(sh.q, &tmQ, head * kEncHeadDim, r0, &sh.q_full, pol);
+            }
             for (int b = 0; b < nb; b++) {
                 const int kbuf = b % kFaKStages, vbuf = b % kFaVStages;
                 const int slot = (kstart + b * kFaKeys) % p.cap;
@@ -194,7 +214,7 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 tc_commit(&sh.k_empty[kbuf]);
                 return true;
             };
-            ok = mbar_wait(&sh.q_full, 0u, deadline) && issue_s(0);
+            ok = nb == 0 || (mbar_wait(&sh.q_full, 0u, deadline) && issue_s(0));
             for (int b = 0; b < nb && ok; b++) {
                 if (b + 1 < nb) {
                     // S is one TMEM buffer: S_{b+1} after the softmax's read of S_b
@@ -319,13 +339,13 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             if (lane == 0) mbar_arrive(&sh.p_full);
         }
         // the last O MMA, then o / l as bf16 (the wo GEMM's A operand)
-        bool got_o = ok && nb > 0 && mbar_wait(&sh.o_full, (nb - 1) & 1u, deadline);
+        bool got_o = ok && (nb == 0 || mbar_wait(&sh.o_full, (nb - 1) & 1u, deadline));
         if (!__all_sync(0xffffffffu, got_o)) ok = false;
-        if (ok) {
+        uint16_t *dst = p.out + (size_t)(r0 + row) * kEncQkv + head * kEncHeadDim;
+        const bool rv = r0 + row < M;
+        if (ok && KZ == 1) {
             tc_fence_after();
             const float il = (l > 0.f) ? 1.0f / l : 0.f;
-            uint16_t *dst = p.out + (size_t)(r0 + row) * kEncQkv + head * kEncHeadDim;
-            const bool rv = r0 + row < M;
 #pragma unroll
             for (int c = 0; c < kEncHeadDim; c += 32) {
                 float ov[32];
@@ -339,6 +359,88 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                        out16x2(ov[j + 4] * il, ov[j + 5] * il, p.f16),
                                        out16x2(ov[j + 6] * il, ov[j + 7] * il, p.f16));
                 }
+            }
+        } else if (KZ > 1) {
+            // this split's row partial: o (64 fp32), then (max, sum)
+            const size_t pr_idx = ((size_t)z * M + (r0 + row)) * kEncHeads + head;
+            float *po = p.part + pr_idx * kFaPartFloats;
+            if (ok && nb > 0) tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < kEncHeadDim; c += 32) {
+                float ov[32];
+                if (nb > 0) tmem_ld32(tl + kFaKeys + (uint32_t)c, ov);   // (warp-uniform)
+                else {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) ov[j] = 0.f;
+                }
+                if (rv) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        __stcg(reinterpret_cast<float4 *>(po + c + j), make_float4(ov[j], ov[j + 1], ov[j + 2], ov[j + 3]));
+                }
+            }
+            if (rv) __stcg(reinterpret_cast<float2 *>(po + kEncHeadDim), make_float2(m, l));
+            __threadfence();
+            named_bar_sync(1, 128);   // the four softmax warps
+            if (threadIdx.x == 64) {
+                const unsigned t = atomicAdd(&p.cnt[blockIdx.x * kEncHeads + head], 1u);
+                sh.last = (t + 1u == (unsigned)KZ) ? 1 : 0;
+            }
+            named_bar_sync(1, 128);
+            if (sh.last) {
+                __threadfence();
+                if (rv) {
+                    // max over the splits that saw keys, then the weighted sums in split order
+                    float mz[kFaMaxSplit], lz[kFaMaxSplit];
+                    float gm = -INFINITY;
+#pragma unroll
+                    for (int s2 = 0; s2 < kFaMaxSplit; s2++) {
+                        mz[s2] = -INFINITY;
+                        lz[s2] = 0.f;
+                        if (s2 < KZ) {
+                            const float2 v = __ldcg(reinterpret_cast<const float2 *>(
+                                p.part + (((size_t)s2 * M + (r0 + row)) * kEncHeads + head) * kFaPartFloats +
+                                kEncHeadDim));
+                            mz[s2] = v.x;
+                            lz[s2] = v.y;
+                            if (v.y > 0.f) gm = fmaxf(gm, v.x);
+                        }
+                    }
+                    float gl = 0.f, wz[kFaMaxSplit];
+#pragma unroll
+                    for (int s2 = 0; s2 < kFaMaxSplit; s2++) {
+                        wz[s2] = (s2 < KZ && lz[s2] > 0.f) ? fast_exp2(mz[s2] - gm) : 0.f;
+                        gl += lz[s2] * wz[s2];
+                    }
+                    const float il = gl > 0.f ? 1.0f / gl : 0.f;
+#pragma unroll
+                    for (int c = 0; c < kEncHeadDim; c += 16) {
+                        float4 acc[4] = {};
+#pragma unroll
+                        for (int s2 = 0; s2 < kFaMaxSplit; s2++) {
+                            if (s2 >= KZ) break;
+                            const float4 *src = reinterpret_cast<const float4 *>(
+                                p.part + (((size_t)s2 * M + (r0 + row)) * kEncHeads + head) * kFaPartFloats + c);
+                            const float w = wz[s2];
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                const float4 v = __ldcg(src + j);
+                                acc[j].x = fmaf(w, v.x, acc[j].x);
+                                acc[j].y = fmaf(w, v.y, acc[j].y);
+                                acc[j].z = fmaf(w, v.z, acc[j].z);
+                                acc[j].w = fmaf(w, v.w, acc[j].w);
+                            }
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; j += 2)
+                            *reinterpret_cast<uint4 *>(dst + c + 4 * j) =
+                                make_uint4(out16x2(acc[j].x * il, acc[j].y * il, p.f16),
+                                           out16x2(acc[j].z * il, acc[j].w * il, p.f16),
+                                           out16x2(acc[j + 1].x * il, acc[j + 1].y * il, p.f16),
+                                           out16x2(acc[j + 1].z * il, acc[j + 1].w * il, p.f16));
+                    }
+                }
+                if (threadIdx.x == 64) p.cnt[blockIdx.x * kEncHeads + head] = 0u;
             }
         }
     }
@@ -392,6 +494,25 @@ bool fa_map(CUtensorMap *m, const void *ptr, int rows, int box_rows) {
 
 }  // namespace
 
+// Key splits for an M-row chunk, off unless VOX_CUDA_ENC_ATTN_KSPLIT = n
+// (n <= 8) asks for them: a 100-row chunk has 32 tiles (one per head) of ~14
+// key blocks each, and splitting the blocks over up to n CTAs fills more
+// SMs, as long as the partials fit the workspace.  Measured per 32-layer
+// chunk (one CTA per SM): 100 rows 2.15 ms unsplit, 2.18 ms at 2 splits,
+// 2.20 ms at 4; 500 rows 3.22 / 3.59 / 3.81 ms.  The per-tile merge (a
+// fence, a ticket, four dependent L2 round trips) costs more than the
+// shorter key loop saves.
+int enc_attn_ksplit(int M, size_t ws_floats) {
+    const char *e = getenv("VOX_CUDA_ENC_ATTN_KSPLIT");
+    const int cap = (e && atoi(e) >= 1) ? std::min(atoi(e), kFaMaxSplit) : 1;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = (M + kFaRows - 1) / kFaRows * kEncHeads;
+    int ks = std::min(cap, std::max(1, 3 * sms / tiles));
+    while (ks > 1 && (size_t)ks * M * kEncHeads * kFaPartFloats > ws_floats) ks--;
+    return ks;
+}
+
 bool enc_attn_tc_supported(const EncAttnParams &p) {
     return p.cap % kEncRingAlign == 0 && p.cap >= p.M + kEncWindow - 1 && p.err != nullptr &&
            ((uintptr_t)p.q & 15) == 0 && ((uintptr_t)p.k_ring & 15) == 0 && ((uintptr_t)p.v_ring & 15) == 0 &&
@@ -411,14 +532,27 @@ cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_set.load() & bit)) {
         e = cudaFuncSetAttribute(enc_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)sizeof(FaSmem));
+                                 (int)std::max(sizeof(FaSmem), kFaSpreadSmem));
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
+    const int kz = p.ksplit > 1 ? p.ksplit : 1;
+    if (kz > 1 && (kz > kFaMaxSplit || !p.part || !p.cnt ||
+                   (p.M + kFaRows - 1) / kFaRows * kEncHeads > kTcSplitCounters))
+        return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((p.M + kFaRows - 1) / kFaRows, kEncHeads);
+    const int ctas = (p.M + kFaRows - 1) / kFaRows * kEncHeads * kz;
+    cfg.gridDim = dim3((p.M + kFaRows - 1) / kFaRows, kEncHeads, kz);
     cfg.blockDim = dim3(kFaThreads);
-    cfg.dynamicSmemBytes = sizeof(FaSmem);
+    // A launch with no more CTAs than SMs reserves enough shared memory for
+    // one CTA per SM: launched early (programmatic dependent launch) while
+    // the q|k|v GEMM still holds most SMs, its CTAs would otherwise pack
+    // three to an SM on the few free ones and share their issue slots.
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const char *sp = getenv("VOX_CUDA_ENC_ATTN_SPREAD");
+    const bool spread = sp ? atoi(sp) != 0 : ctas <= sms;
+    cfg.dynamicSmemBytes = spread ? std::max(sizeof(FaSmem), kFaSpreadSmem) : sizeof(FaSmem);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

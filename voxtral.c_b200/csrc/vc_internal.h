@@ -266,7 +266,16 @@ struct EncAttnParams {
     uint16_t *out;            // [M][2048], bf16 or (f16) fp16: the wo GEMM's A operand
     int f16;
     unsigned *err;            // raised when a bounded wait expires (tensor-core kernel)
+    // key split (tensor-core kernel, chunks with few row tiles): ksplit CTAs
+    // per (row tile, head) take consecutive key blocks and leave unnormalised
+    // partials; the last to finish merges them (ticket in cnt)
+    int ksplit;               // 1 (or 0): no split
+    float *part;              // [ksplit][M][32 heads] x (64 o + max + sum) floats
+    unsigned *cnt;            // [row tiles][32], zero between launches
 };
+// key splits of the tensor-core encoder attention for an M-row chunk whose
+// partials may take ws_floats floats
+int enc_attn_ksplit(int M, size_t ws_floats);
 // Windowed encoder attention: the tcgen05 kernel when enc_attn_tc_supported
 // (ring capacity a multiple of 128, err set) unless VOX_CUDA_ENC_ATTN=mma,
 // else the mma.sync kernel.

@@ -433,6 +433,11 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         a.out = s->att16;
         a.f16 = 1;
         a.err = s->err;
+        // few row tiles: split the key blocks (partials in the split-K
+        // workspace, which no GEMM uses while the attention runs)
+        a.ksplit = enc_attn_ksplit(M, kEncSplitFloats);
+        a.part = s->split;
+        a.cnt = s->split_cnt;
         VC_EV_BEGIN(VOX_CUDA_EPROF_ATTN);
         VC_TRY(launch_enc_attn(a, st, pdl));
         VC_EV_END();
