@@ -277,16 +277,18 @@ gemv_tma_kernel(const GemvParams p) {
         }
         __syncthreads();
     }
-    if (tid < 8) {
-        float inv = 1.0f;
-        if (p.ss_in != nullptr && tid < M) {
-            // RMSNorm (voxtral_kernels.c:346-363): 1/sqrt(mean(x^2) + eps); the
-            // producer supplied per-row-block sums of x^2
-            float ss = 0.f;
-            for (int j = 0; j < p.ss_parts; j++) ss += p.ss_in[tid * p.ss_parts + j];
-            inv = 1.0f / sqrtf(ss / (float)p.K + kNormEps);
-        }
-        sh.s_inv[tid] = inv;
+    if (warp == 0) {
+        // RMSNorm consumer (voxtral_kernels.c:346-363): each stream's
+        // 1/sqrt(mean(x^2) + eps) from the producer's per-row-block sums of
+        // x^2.  Lane = (stream lane & 7, part group lane >> 3): four loads in
+        // flight per stream; the groups' sums are added in a fixed order.
+        float ss = 0.f;
+        const int sm = lane & 7;
+        if (p.ss_in != nullptr && sm < M)
+            for (int j = lane >> 3; j < p.ss_parts; j += 4) ss += __ldcg(p.ss_in + sm * p.ss_parts + j);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 8);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 16);
+        if (lane < 8) sh.s_inv[lane] = (p.ss_in != nullptr && lane < M) ? 1.0f / sqrtf(ss / (float)p.K + kNormEps) : 1.0f;
     }
     __syncthreads();
 
