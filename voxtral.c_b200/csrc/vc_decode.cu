@@ -42,10 +42,10 @@ __device__ __forceinline__ bool arg_better(float v, int i, float bv, int bi) {
 constexpr int kKeysPerSplit = 64;
 
 struct AttnShared {
-    float k[kKeysPerSplit][kHeadDim];   // 32 KB; the merge reuses it for its weights
+    float k[kKeysPerSplit][kHeadDim];   // 32 KB, chunk-swizzled; the merge reuses it for its weights
     float v[kKeysPerSplit][kHeadDim];   // 32 KB
     float q[4][kHeadDim];
-    float p[4][kKeysPerSplit];          // exp(score - split max)
+    float4 p4[kKeysPerSplit];           // exp(score - split max) of key j for the 4 heads
     float ml[4][2];                     // per head: (split max, sum of exp)
     int last;
 };
@@ -87,14 +87,16 @@ __device__ __forceinline__ void attn_store_out(const AttnParams &p, int m, int i
 }
 
 // cp.async of the K and V rows of keys [j0, j1) of a split (key j of the
-// split at ring slot (first + kb + j) % cap), 16 bytes per copy.
+// split at ring slot (first + kb + j) % cap), 16 bytes per copy.  K's
+// 16-byte chunk c of key j goes to chunk c ^ (j & 31): lane j reading its
+// key's chunk c is conflict-free while the query chunk c is one broadcast.
 __device__ __forceinline__ void attn_stage_keys(AttnShared &sh, const float *kbase, const float *vbase, int first,
                                                 int kb, int cap, int j0, int j1, int tid) {
     const int n = (j1 - j0) * (kHeadDim / 4);   // 16-byte pieces per matrix
     for (int c = tid; c < n; c += 128) {
         const int j = j0 + c / (kHeadDim / 4), piece = c % (kHeadDim / 4);
         const size_t row = (size_t)((first + kb + j) % cap) * kKvDim + 4 * piece;
-        cp_async16(&sh.k[j][4 * piece], kbase + row);
+        cp_async16(&sh.k[j][4 * (piece ^ (j & 31))], kbase + row);
         cp_async16(&sh.v[j][4 * piece], vbase + row);
     }
 }
@@ -156,30 +158,32 @@ attn_decode_kernel(const AttnParams p) {
         {
             const int h = warp;
             const float4 *q4 = reinterpret_cast<const float4 *>(sh.q[h]);
-            float sc[2];
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const int j = lane + 32 * u;
-                const float4 *k4 = reinterpret_cast<const float4 *>(sh.k[j]);
-                float a = 0.f;
+            const float4 *k0 = reinterpret_cast<const float4 *>(sh.k[lane]);
+            const float4 *k1 = reinterpret_cast<const float4 *>(sh.k[lane + 32]);
+            float a0 = 0.f, a1 = 0.f;
 #pragma unroll 8
-                for (int i = 0; i < kHeadDim / 4; i++) {
-                    const int f = (i + lane) & (kHeadDim / 4 - 1);   // rotation: no bank conflicts
-                    const float4 kk = k4[f], qq = q4[f];
-                    a = fmaf(qq.x, kk.x, a);
-                    a = fmaf(qq.y, kk.y, a);
-                    a = fmaf(qq.z, kk.z, a);
-                    a = fmaf(qq.w, kk.w, a);
-                }
-                sc[u] = (j < nk) ? a * scale : -INFINITY;
+            for (int c = 0; c < kHeadDim / 4; c++) {
+                const float4 qq = q4[c];                                   // broadcast
+                const float4 x0 = k0[c ^ lane], x1 = k1[c ^ lane];         // swizzled rows
+                a0 = fmaf(qq.x, x0.x, a0);
+                a0 = fmaf(qq.y, x0.y, a0);
+                a0 = fmaf(qq.z, x0.z, a0);
+                a0 = fmaf(qq.w, x0.w, a0);
+                a1 = fmaf(qq.x, x1.x, a1);
+                a1 = fmaf(qq.y, x1.y, a1);
+                a1 = fmaf(qq.z, x1.z, a1);
+                a1 = fmaf(qq.w, x1.w, a1);
             }
+            float sc[2];
+            sc[0] = (lane < nk) ? a0 * scale : -INFINITY;
+            sc[1] = (lane + 32 < nk) ? a1 * scale : -INFINITY;
             float mx = fmaxf(sc[0], sc[1]);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
             const float pa = (lane < nk) ? expf(sc[0] - mx) : 0.f;
             const float pb = (lane + 32 < nk) ? expf(sc[1] - mx) : 0.f;
-            sh.p[h][lane] = pa;
-            sh.p[h][lane + 32] = pb;
+            reinterpret_cast<float *>(&sh.p4[lane])[h] = pa;
+            reinterpret_cast<float *>(&sh.p4[lane + 32])[h] = pb;
             const float sum = warp_sum(pa + pb);
             if (lane == 0) {
                 sh.ml[h][0] = mx;
@@ -188,13 +192,18 @@ attn_decode_kernel(const AttnParams p) {
         }
         __syncthreads();
 
-        // ---- P.V: thread = dimension, 4 heads ----
+        // ---- P.V: thread = dimension, 4 heads (one broadcast read of the
+        // key's 4 probabilities) ----
         {
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
             for (int j = 0; j < nk; j++) {
                 const float vj = sh.v[j][tid];
-#pragma unroll
-                for (int h = 0; h < 4; h++) acc[h] = fmaf(sh.p[h][j], vj, acc[h]);
+                const float4 pj = sh.p4[j];
+                acc[0] = fmaf(pj.x, vj, acc[0]);
+                acc[1] = fmaf(pj.y, vj, acc[1]);
+                acc[2] = fmaf(pj.z, vj, acc[2]);
+                acc[3] = fmaf(pj.w, vj, acc[3]);
             }
 #pragma unroll
             for (int h = 0; h < 4; h++) {
