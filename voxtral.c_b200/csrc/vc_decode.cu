@@ -232,6 +232,13 @@ attn_decode_kernel(const AttnParams p) {
         const int hh = warp, d4 = 4 * lane;
         const int h = kvh * 4 + hh;
         const size_t pbase = ((size_t)m * kDecHeads + h) * p.S;
+        // the first eight partials' o go out with the (max, sum) loads: one
+        // L2 round trip for the usual S <= 8 instead of three
+        float4 o8[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+            o8[u] = (u < S) ? __ldcg(reinterpret_cast<const float4 *>(p.part_o + (pbase + u) * kHeadDim + d4))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
         float mloc[kAttnSplits / 32], dloc[kAttnSplits / 32];
         float gm = -INFINITY;
 #pragma unroll
@@ -256,7 +263,16 @@ attn_decode_kernel(const AttnParams p) {
         gd = warp_sum(gd);
         __syncwarp();
         float go[4] = {0.f, 0.f, 0.f, 0.f};
-        int t = 0;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {   // (split order, as below)
+            if (u >= S) break;
+            const float c = smw[hh][u];
+            go[0] += o8[u].x * c;
+            go[1] += o8[u].y * c;
+            go[2] += o8[u].z * c;
+            go[3] += o8[u].w * c;
+        }
+        int t = 8;
         for (; t + 4 <= S; t += 4) {   // 4 independent loads in flight
             float4 ov[4];
 #pragma unroll
