@@ -403,7 +403,13 @@ gemv_tma_kernel(const GemvParams p) {
                         const int oi = __shfl_xor_sync(0xffffffffu, ib, o);
                         if (arg_better(ov, oi, b, ib)) { b = ov; ib = oi; }
                     }
-                    if (lane == 0) p.tokens[warp] = ib;
+                    if (lane == 0) {
+                        p.tokens[warp] = ib;
+                        if (p.tokens_to != nullptr) {
+                            int *dst = *p.tokens_to;   // the caller's buffer of this step
+                            if (dst != nullptr) dst[warp] = ib;
+                        }
+                    }
                 }
                 if (tid == 0) *p.counter = 0u;
             }

@@ -56,6 +56,8 @@ struct GemvParams {
     ArgmaxPartial *partials;  // [gridDim.x * M]
     unsigned *counter;        // 1 counter, zero between launches
     int *tokens;              // [M]
+    int *const *tokens_to;    // EPI_LOGITS: a device word holding a second destination of the tokens
+                              //   (read when the argmax finishes; NULL pointer or word: none)
     // weights of a later kernel to start pulling into L2 (or NULL)
     const void *pf;
     unsigned long long pf_bytes;   // a multiple of 16

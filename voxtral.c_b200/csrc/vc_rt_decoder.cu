@@ -38,6 +38,7 @@ struct StepWork {
     StreamSlot *slots = nullptr;
     float *rope = nullptr;             // [n][128]
     const float **rows = nullptr;      // [n] addend rows of the token-embedding steps
+    int **tokens_to = nullptr;         // [1] the caller's token buffer of an asynchronous step (or NULL)
     float *x = nullptr;                // [n][3072] residual stream
     float *q = nullptr, *att = nullptr;  // [n][4096]
     float *h = nullptr;                // [n][9216]
@@ -67,6 +68,8 @@ struct StepWork {
     cudaEvent_t err_ev = nullptr;
     bool staged_pending = false;
     bool err_pending = false;
+    unsigned err_tick = 0;             // asynchronous steps since the last error-word copy
+    bool graph_persist = false;        // graph[1] holds the persistent step (its tokens are copied out)
     // graphs: [0] layers only (prefill), [1] layers + LM head
     cudaGraphExec_t graph[2] = {nullptr, nullptr};
 };
@@ -196,6 +199,7 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     const size_t o_slots = take(sizeof(StreamSlot) * n);
     const size_t o_rope = take(sizeof(float) * n * kHeadDim);
     const size_t o_rows = take(sizeof(float *) * n);
+    const size_t o_tto = take(sizeof(int *));
     const size_t o_x = take(sizeof(float) * n * kDecDim);
     w->dblock_bytes = o_x + sizeof(float) * n * kDecDim;   // the uploaded prefix
     const size_t o_q = take(sizeof(float) * n * kQDim);
@@ -233,6 +237,7 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
     w->slots = (StreamSlot *)(b + o_slots);
     w->rope = (float *)(b + o_rope);
     w->rows = (const float **)(b + o_rows);
+    w->tokens_to = (int **)(b + o_tto);
     w->x = (float *)(b + o_x);
     w->q = (float *)(b + o_q);
     w->att = (float *)(b + o_att);
@@ -265,8 +270,8 @@ StepWork *make_work(DevCtx *c, int n, int vocab) {
         free_work(c, w);
         return nullptr;
     }
+    memset(w->hblock, 0, align_up(w->dblock_bytes, 16) + sizeof(int) * (n + 1));   // (tokens_to: none)
     w->h_tokens = (int *)(w->hblock + align_up(w->dblock_bytes, 16));
-    w->h_tokens[n] = 0;
     return w;
 }
 
@@ -275,6 +280,7 @@ StreamSlot *h_slots(StepWork *w) { return (StreamSlot *)w->hblock; }
 float *h_rope(StepWork *w) { return (float *)(w->hblock + ((char *)w->rope - w->dblock)); }
 float *h_x(StepWork *w) { return (float *)(w->hblock + ((char *)w->x - w->dblock)); }
 const float **h_rows(StepWork *w) { return (const float **)(w->hblock + ((char *)w->rows - w->dblock)); }
+int **h_tokens_to(StepWork *w) { return (int **)(w->hblock + ((char *)w->tokens_to - w->dblock)); }
 
 // Bytes of a decode weight matrix [N, K] in the tiled layout.
 size_t tiled_bytes(int N, int K) { return (size_t)round_up(N, kGemvRowAlign) * round_up(K, 16) * 2; }
@@ -469,6 +475,7 @@ int enqueue_layers(vox_cuda_decoder *d, StepWork *w, bool with_head, cudaStream_
         p.partials = w->amax;
         p.counter = w->counters + n * kDecKvHeads;
         p.tokens = w->tokens;
+        p.tokens_to = w->tokens_to;
         p.err = w->err;
         VC_EV_BEGIN();
         VC_TRY(launch_gemv(n, EPI_LOGITS, p, st, pdl));
@@ -499,10 +506,12 @@ int check_step_error(StepWork *w, cudaStream_t st) {
 // the tokens.
 int run_step(vox_cuda_decoder *d, DevCtx *c, StepWork *w, bool with_head, cudaStream_t st,
              bool sync) {
+    *h_tokens_to(w) = nullptr;   // the tokens come back through h_tokens
     VC_TRY(cudaMemcpyAsync(w->dblock, w->hblock, w->dblock_bytes, cudaMemcpyHostToDevice, st));
     cudaGraphExec_t &g = w->graph[with_head ? 1 : 0];
     if (!g) {
         cudaGraph_t graph = nullptr;
+        if (with_head) w->graph_persist = d->players && persist_on();   // (as enqueue_layers decides)
         VC_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         int rc = enqueue_layers(d, w, with_head, st);
         cudaError_t e = cudaStreamEndCapture(st, &graph);
@@ -1358,6 +1367,10 @@ static int step_batch_async(vox_cuda_dec_state *const *states, int n, const floa
     // input rows from the device
     if (rows)
         for (int i = 0; i < n; i++) h_rows(w)[i] = rows[i];
+    // the LM head's argmax writes the caller's tokens itself (per-phase
+    // kernels; the persistent step writes its own buffer, copied below)
+    const bool persist = w->graph[1] ? w->graph_persist : (d->players && persist_on());
+    *h_tokens_to(w) = persist ? nullptr : tokens_dev;
     const size_t head = (char *)w->x - w->dblock;
     VC_TRY(cudaMemcpyAsync(w->dblock, w->hblock, head, cudaMemcpyHostToDevice, st));
     VC_TRY(cudaEventRecord(w->staged, st));
@@ -1370,6 +1383,7 @@ static int step_batch_async(vox_cuda_dec_state *const *states, int n, const floa
     cudaGraphExec_t &g = w->graph[1];
     if (!g) {
         cudaGraph_t graph = nullptr;
+        w->graph_persist = persist;
         VC_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         rc = enqueue_layers(d, w, true, st);
         cudaError_t e = cudaStreamEndCapture(st, &graph);
@@ -1383,8 +1397,10 @@ static int step_batch_async(vox_cuda_dec_state *const *states, int n, const floa
         VC_TRY(e);
     }
     VC_TRY(cudaGraphLaunch(g, st));
-    VC_TRY(cudaMemcpyAsync(tokens_dev, w->tokens, sizeof(int) * n, cudaMemcpyDeviceToDevice, st));
-    if (!w->err_pending) {   // one error-word copy in flight at a time
+    if (w->graph_persist) VC_TRY(cudaMemcpyAsync(tokens_dev, w->tokens, sizeof(int) * n, cudaMemcpyDeviceToDevice, st));
+    // the sticky error word comes back every 8th asynchronous step (and with
+    // every synchronous one), one copy in flight at a time
+    if (!w->err_pending && (++w->err_tick & 7u) == 0u) {
         VC_TRY(cudaMemcpyAsync(w->h_tokens + n, w->err, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
         VC_TRY(cudaEventRecord(w->err_ev, st));
         w->err_pending = true;
