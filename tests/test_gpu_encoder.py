@@ -196,6 +196,30 @@ def test_encoder_attention_key_split_matches_unsplit(monkeypatch):
     e.free()
 
 
+def test_encoder_attention_softmax_split_matches(monkeypatch):
+    """The attention's softmax as one warp per TMEM lane quarter (all 64 key
+    columns) or two (32 each, block maxima and row sums exchanged through
+    shared memory): chunk sizes that take either launch shape by default, both
+    forced, against each other and the oracle."""
+    ew = B.EncoderWeights(seed=18, n_layers=2, distinct=2, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    sizes = [100, 37, 256, 3, 700]
+    xs = [B.normal_f32((n, B.ENC_DIM), 1180 + i) for i, n in enumerate(sizes)]
+    outs = {}
+    for nh in ("1", "2"):
+        monkeypatch.setenv("VOX_CUDA_ENC_ATTN_NH", nh)
+        st = e.state(max_chunk=700)
+        outs[nh] = [st.step(x) for x in xs]
+        st.free()
+    o = B.OracleEncoder(ew, kv_max=2400)
+    for i, x in enumerate(xs):
+        ref = o.step(x)
+        assert np.isfinite(outs["2"][i]).all()
+        assert B.rel_l2(outs["2"][i], outs["1"][i]) < 1e-4, (i, B.rel_l2(outs["2"][i], outs["1"][i]))
+        assert B.rel_l2(outs["2"][i], ref) < 5e-3, (i, B.rel_l2(outs["2"][i], ref))
+    e.free()
+
+
 def test_encoder_tile_widths_agree(monkeypatch):
     """The tensor-core GEMM's tile width (64 / 128 / 192 / 256 columns, picked
     by a rounds x tile-cost model) changes which CTA computes an output

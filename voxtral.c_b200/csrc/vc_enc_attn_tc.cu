@@ -2,9 +2,9 @@
 // cores (vox_causal_attention for seq_q = new_len, window 750, 32 heads x 64,
 // voxtral_kernels.c:412-482 as called at voxtral_encoder.c:574-576).
 //
-// One CTA = 128 query rows of one head (TMEM lane = query row), 192 threads,
-// three CTAs per SM (72 KB shared memory, 128 TMEM columns, <= 112 registers)
-// so that a 1500-row chunk's 12 x 32 tiles run in one wave:
+// One CTA = 128 query rows of one head (TMEM lane = query row), 192 or 320
+// threads, three CTAs per SM (73 KB shared memory, 128 TMEM columns) so that
+// a 1500-row chunk's 12 x 32 tiles run in one wave:
 //   warp 0 (one thread)  TMA: the Q tile once, then 64-key blocks of K and V
 //                        from the fp16 ring: K into a 3-deep ring (a slot is
 //                        free once its S MMA completes), V into a 2-deep one
@@ -12,11 +12,16 @@
 //   warp 1 (one thread)  MMAs: S_b = Q K_b^T (M 128, N 64, K 64) into TMEM
 //                        columns [0,64); O += P_b V_b (M 128, N 64, K 64, V
 //                        an MN-major operand) accumulating in columns [64,128)
-//   warps 2-5            softmax, thread = row: one tcgen05.ld of S_b, mask
-//                        (the row's own window [pos - 749, pos]), block max,
+//   warps 2-5 (2-9)      softmax, one (two) warp(s) per TMEM lane quarter,
+//                        thread = row, each warp 64 (32) of the block's 64 key
+//                        columns: tcgen05.ld of its columns of S_b, mask (the row's own
+//                        window [pos - 749, pos]), the row's block max over
+//                        both halves (exchanged through shared memory under a
+//                        64-thread named barrier per quarter), its half of
 //                        P_b = 2^(s - m) as fp16 into shared memory (the A
-//                        operand of the O MMA), row sum in fp32; at the end
-//                        O / l as fp16 (or bf16) for the wo GEMM
+//                        operand of the O MMA), its half's row sum in fp32;
+//                        at the end its 32 columns of O / l (l summed over
+//                        both halves) as fp16 (or bf16) for the wo GEMM
 // The running max m of a row moves only when a block's max exceeds it by more
 // than 2^8 (P stays <= 256, exact enough in fp16 and fp32); then the thread
 // rescales its O row in TMEM (tcgen05.ld / st) and its sum after writing
@@ -27,7 +32,9 @@
 // O MMA (whose completion also frees P).  Key blocks start at multiples of 64
 // positions and the ring capacity is a multiple of 128, so a block never
 // wraps in the ring.  Every mbarrier wait is bounded (2 s of %globaltimer);
-// on expiry the CTA raises the error word and exits after a grace period.
+// on expiry the CTA raises the error word and exits after a grace period;
+// the softmax warps then run their remaining blocks with every wait failing
+// at once, so both warps of a pair reach every named barrier.
 // Key split (chunks with few row tiles, e.g. 100 rows = 32 tiles): blockIdx.z
 // takes consecutive key blocks of the tile's range; the softmax threads leave
 // their row's unnormalised o, running max and sum in a workspace, and the
@@ -49,7 +56,8 @@ using namespace tc;
 
 constexpr int kFaRows = 128;      // query rows per CTA = TMEM lanes
 constexpr int kFaKeys = 64;       // keys per block
-constexpr int kFaThreads = 192;
+// softmax warps: NH (1 or 2) per TMEM lane quarter; 64 + 128 NH threads
+constexpr int fa_threads(int nh) { return 64 + 128 * nh; }
 constexpr int kFaTmemCols = 128;  // S [0,64), O [64,128)
 constexpr uint64_t kFaWaitNs = 2000000000ull;
 constexpr float kFaRescale = 8.0f;   // log2 of the largest P before the max moves
@@ -68,6 +76,7 @@ struct FaSmem {
     uint64_t k_full[kFaKStages], k_empty[kFaKStages];
     uint64_t v_full[kFaVStages], v_empty[kFaVStages];
     uint32_t tmem;
+    float mx[2][kFaRows];   // the two halves' row maxima (then row sums)
     int last;   // key split: this CTA merges
 };
 
@@ -108,7 +117,8 @@ __device__ __forceinline__ uint32_t out16x2(float a, float b, int f16) {
     return f16 ? half2_bits(a, b) : (bf16_bits_rn(a) | (bf16_bits_rn(b) << 16));
 }
 
-__global__ void __launch_bounds__(kFaThreads, 3)
+template <int NH>
+__global__ void __launch_bounds__(64 + 128 * NH, 3)
 enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const EncAttnParams p) {
     extern __shared__ __align__(1024) unsigned char fa_smem_raw[];
@@ -121,8 +131,8 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (threadIdx.x == 0) {
         mbar_init(&sh.q_full, 1);
         mbar_init(&sh.s_full, 1);
-        mbar_init(&sh.s_free, 4);   // one arrival per softmax warp
-        mbar_init(&sh.p_full, 4);
+        mbar_init(&sh.s_free, 4 * NH);   // one arrival per softmax warp
+        mbar_init(&sh.p_full, 4 * NH);
         mbar_init(&sh.o_full, 1);
         for (int i = 0; i < kFaKStages; i++) {
             mbar_init(&sh.k_full[i], 1);
@@ -246,47 +256,51 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
         }
     } else {
-        // ---- softmax: thread = query row = TMEM lane ----
-        const int q = warp & 3;
+        // ---- softmax: NH warps per TMEM lane quarter, thread = query row,
+        // each warp CW of the 64 key columns (and of O) ----
+        constexpr int CW = kFaKeys / NH;
+        const int q = warp & 3, half = NH == 2 ? (warp - 2) >> 2 : 0;
         const int row = 32 * q + lane;
         const int pr = pos0 + r0 + row;                     // this row's logical position
         const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
+        const uint32_t ts = tl + (uint32_t)(half * CW);               // this warp's S columns
+        const uint32_t to = tl + (uint32_t)(kFaKeys + half * CW);     // and O columns
         const float sl2 = 0.18033688011112042f;              // (1 / sqrt(64)) * log2(e)
-        float m = -INFINITY, l = 0.f;
+        float m = -INFINITY, l = 0.f;                        // l: this half's columns only
         for (int b = 0; b < nb; b++) {
             const bool got = mbar_wait(&sh.s_full, b & 1u, deadline);
             if (!__all_sync(0xffffffffu, got)) {
                 ok = false;
-                break;
             }
             tc_fence_after();
-            float sa[32], sb[32];   // S_b columns 0-31 and 32-63
-            tmem_ld32(tl, sa);
-            tmem_ld32(tl + 32u, sb);
+            float sv[CW];   // S_b columns half*CW .. half*CW+CW-1
+#pragma unroll
+            for (int c2 = 0; c2 < CW; c2 += 32) tmem_ld32(ts + (uint32_t)c2, *reinterpret_cast<float(*)[32]>(sv + c2));
             // S_b is in registers: the MMA warp may overwrite S with S_{b+1}
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.s_free);
-#define SV(j) ((j) < 32 ? sa[(j) & 31] : sb[(j) & 31])
-            const int kb0 = kstart + b * kFaKeys;
+            const int kb0 = kstart + b * kFaKeys + half * CW;
             // every key of the block inside every valid row's window: no mask;
             // else key offset c is valid for this row iff (unsigned)(c - lo) <= 749
-            const bool full = kb0 >= p_last - (kEncWindow - 1) && kb0 + kFaKeys - 1 <= p_first;
+            const bool full = kstart + b * kFaKeys >= p_last - (kEncWindow - 1) &&
+                              kstart + b * kFaKeys + kFaKeys - 1 <= p_first;
             const int lo = pr - (kEncWindow - 1) - kb0;
             if (!full) {
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    if ((unsigned)(j - lo) > (unsigned)(kEncWindow - 1)) sa[j] = -INFINITY;
-                    if ((unsigned)(j + 32 - lo) > (unsigned)(kEncWindow - 1)) sb[j] = -INFINITY;
-                }
+                for (int j = 0; j < CW; j++)
+                    if ((unsigned)(j - lo) > (unsigned)(kEncWindow - 1)) sv[j] = -INFINITY;
             }
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                mx4[j & 3] = fmaxf(mx4[j & 3], sa[j]);
-                mx4[j & 3] = fmaxf(mx4[j & 3], sb[j]);
+            for (int j = 0; j < CW; j++) mx4[j & 3] = fmaxf(mx4[j & 3], sv[j]);
+            float mb = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            if constexpr (NH == 2) {   // the row's block maximum over both halves (pair barrier q + 1)
+                sh.mx[half][row] = mb;
+                named_bar_sync(1 + q, 64);
+                mb = fmaxf(sh.mx[0][row], sh.mx[1][row]);
             }
-            const float mb = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+            mb *= sl2;
             // move the running max only when this block's max exceeds it by > 2^8
             const bool move = mb > m + kFaRescale;
             float factor = 1.f;
@@ -298,10 +312,7 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             // O += P_{b-1} V_{b-1} complete: P is free and O can be rescaled
             if (b > 0) {
                 const bool got_o = mbar_wait(&sh.o_full, (b - 1) & 1u, deadline);
-                if (!__all_sync(0xffffffffu, got_o)) {
-                    ok = false;
-                    break;
-                }
+                if (!__all_sync(0xffffffffu, got_o)) ok = false;
                 tc_fence_after();
             }
             const float base = (m == -INFINITY) ? 0.f : m;
@@ -309,28 +320,28 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             float rs4[4] = {0.f, 0.f, 0.f, 0.f};
             unsigned char *ph = sh.p + row * 128;
 #pragma unroll
-            for (int c = 0; c < kFaKeys; c += 8) {
+            for (int c = 0; c < CW; c += 8) {
                 uint32_t h[4];
 #pragma unroll
                 for (int j = 0; j < 8; j += 2) {
-                    const float ea = fast_exp2(fmaf(SV(c + j), sl2, -base));
-                    const float eb = fast_exp2(fmaf(SV(c + j + 1), sl2, -base));
+                    const float ea = fast_exp2(fmaf(sv[c + j], sl2, -base));
+                    const float eb = fast_exp2(fmaf(sv[c + j + 1], sl2, -base));
                     rs4[(j >> 1) & 3] += ea + eb;
                     h[j >> 1] = half2_bits(ea, eb);
                 }
-                *reinterpret_cast<uint4 *>(ph + 16 * ((c >> 3) ^ (row & 7))) = make_uint4(h[0], h[1], h[2], h[3]);
+                const int chunk = (half * CW + c) >> 3;
+                *reinterpret_cast<uint4 *>(ph + 16 * (chunk ^ (row & 7))) = make_uint4(h[0], h[1], h[2], h[3]);
             }
-#undef SV
             l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
             // rows whose max moved rescale their O row (after P, so S is dead)
             if (b > 0 && __any_sync(0xffffffffu, move)) {
 #pragma unroll
-                for (int c = 0; c < kEncHeadDim; c += 32) {
+                for (int c2 = 0; c2 < CW; c2 += 32) {
                     float ov[32];
-                    tmem_ld32(tl + kFaKeys + (uint32_t)c, ov);
+                    tmem_ld32(to + (uint32_t)c2, ov);
 #pragma unroll
                     for (int j = 0; j < 32; j++) ov[j] *= factor;
-                    tmem_st32(tl + kFaKeys + (uint32_t)c, ov);
+                    tmem_st32(to + (uint32_t)c2, ov);
                 }
             }
             fence_async_smem();   // P visible to the tensor core
@@ -338,22 +349,28 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.p_full);
         }
-        // the last O MMA, then o / l as bf16 (the wo GEMM's A operand)
+        // the last O MMA, then o / l as fp16 (the wo GEMM's A operand)
         bool got_o = ok && (nb == 0 || mbar_wait(&sh.o_full, (nb - 1) & 1u, deadline));
         if (!__all_sync(0xffffffffu, got_o)) ok = false;
-        uint16_t *dst = p.out + (size_t)(r0 + row) * kEncQkv + head * kEncHeadDim;
+        float lt = l;
+        if constexpr (NH == 2) {   // the row's sum over both halves (pair barrier q + 1)
+            sh.mx[half][row] = l;
+            named_bar_sync(1 + q, 64);
+            lt = sh.mx[0][row] + sh.mx[1][row];
+        }
+        uint16_t *dst = p.out + (size_t)(r0 + row) * kEncQkv + head * kEncHeadDim + half * CW;
         const bool rv = r0 + row < M;
         if (ok && KZ == 1) {
             tc_fence_after();
-            const float il = (l > 0.f) ? 1.0f / l : 0.f;
+            const float il = (lt > 0.f) ? 1.0f / lt : 0.f;
 #pragma unroll
-            for (int c = 0; c < kEncHeadDim; c += 32) {
+            for (int c2 = 0; c2 < CW; c2 += 32) {
                 float ov[32];
-                tmem_ld32(tl + kFaKeys + (uint32_t)c, ov);
+                tmem_ld32(to + (uint32_t)c2, ov);
                 if (rv) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 8)
-                        *reinterpret_cast<uint4 *>(dst + c + j) =
+                        *reinterpret_cast<uint4 *>(dst + c2 + j) =
                             make_uint4(out16x2(ov[j] * il, ov[j + 1] * il, p.f16),
                                        out16x2(ov[j + 2] * il, ov[j + 3] * il, p.f16),
                                        out16x2(ov[j + 4] * il, ov[j + 5] * il, p.f16),
@@ -366,9 +383,9 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             float *po = p.part + pr_idx * kFaPartFloats;
             if (ok && nb > 0) tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < kEncHeadDim; c += 32) {
+            for (int c2 = 0; c2 < CW; c2 += 32) {
                 float ov[32];
-                if (nb > 0) tmem_ld32(tl + kFaKeys + (uint32_t)c, ov);   // (warp-uniform)
+                if (nb > 0) tmem_ld32(to + (uint32_t)c2, ov);   // (warp-uniform)
                 else {
 #pragma unroll
                     for (int j = 0; j < 32; j++) ov[j] = 0.f;
@@ -376,17 +393,18 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 if (rv) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
-                        __stcg(reinterpret_cast<float4 *>(po + c + j), make_float4(ov[j], ov[j + 1], ov[j + 2], ov[j + 3]));
+                        __stcg(reinterpret_cast<float4 *>(po + half * CW + c2 + j),
+                               make_float4(ov[j], ov[j + 1], ov[j + 2], ov[j + 3]));
                 }
             }
-            if (rv) __stcg(reinterpret_cast<float2 *>(po + kEncHeadDim), make_float2(m, l));
+            if (rv && half == 0) __stcg(reinterpret_cast<float2 *>(po + kEncHeadDim), make_float2(m, lt));
             __threadfence();
-            named_bar_sync(1, 128);   // the four softmax warps
+            named_bar_sync(5, 128 * NH);   // every softmax warp
             if (threadIdx.x == 64) {
                 const unsigned t = atomicAdd(&p.cnt[blockIdx.x * kEncHeads + head], 1u);
                 sh.last = (t + 1u == (unsigned)KZ) ? 1 : 0;
             }
-            named_bar_sync(1, 128);
+            named_bar_sync(5, 128 * NH);
             if (sh.last) {
                 __threadfence();
                 if (rv) {
@@ -414,13 +432,14 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     }
                     const float il = gl > 0.f ? 1.0f / gl : 0.f;
 #pragma unroll
-                    for (int c = 0; c < kEncHeadDim; c += 16) {
+                    for (int c = 0; c < CW; c += 16) {   // this warp's columns
                         float4 acc[4] = {};
 #pragma unroll
                         for (int s2 = 0; s2 < kFaMaxSplit; s2++) {
                             if (s2 >= KZ) break;
                             const float4 *src = reinterpret_cast<const float4 *>(
-                                p.part + (((size_t)s2 * M + (r0 + row)) * kEncHeads + head) * kFaPartFloats + c);
+                                p.part + (((size_t)s2 * M + (r0 + row)) * kEncHeads + head) * kFaPartFloats +
+                                half * CW + c);
                             const float w = wz[s2];
 #pragma unroll
                             for (int j = 0; j < 4; j++) {
@@ -531,8 +550,11 @@ cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl
     static std::atomic<uint64_t> attr_set{0};   // the shared-memory opt-in is per device
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_set.load() & bit)) {
-        e = cudaFuncSetAttribute(enc_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(enc_attn_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)std::max(sizeof(FaSmem), kFaSpreadSmem));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(enc_attn_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)std::max(sizeof(FaSmem), kFaSpreadSmem));
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
@@ -543,15 +565,19 @@ cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl
     cudaLaunchConfig_t cfg = {};
     const int ctas = (p.M + kFaRows - 1) / kFaRows * kEncHeads * kz;
     cfg.gridDim = dim3((p.M + kFaRows - 1) / kFaRows, kEncHeads, kz);
-    cfg.blockDim = dim3(kFaThreads);
     // A launch with no more CTAs than SMs reserves enough shared memory for
     // one CTA per SM: launched early (programmatic dependent launch) while
     // the q|k|v GEMM still holds most SMs, its CTAs would otherwise pack
-    // three to an SM on the few free ones and share their issue slots.
+    // three to an SM on the few free ones and share their issue slots.  Such
+    // a CTA alone on its SM splits the softmax over two warps per TMEM lane
+    // quarter (NH = 2; VOX_CUDA_ENC_ATTN_NH = 1 | 2 forces one).
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const char *sp = getenv("VOX_CUDA_ENC_ATTN_SPREAD");
     const bool spread = sp ? atoi(sp) != 0 : ctas <= sms;
+    const char *nh_env = getenv("VOX_CUDA_ENC_ATTN_NH");
+    const int nh = (nh_env && (atoi(nh_env) == 1 || atoi(nh_env) == 2)) ? atoi(nh_env) : spread ? 2 : 1;
+    cfg.blockDim = dim3(fa_threads(nh));
     cfg.dynamicSmemBytes = spread ? std::max(sizeof(FaSmem), kFaSpreadSmem) : sizeof(FaSmem);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -559,7 +585,8 @@ cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel, mq, mk, mv, p);
+    return nh == 2 ? cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel<2>, mq, mk, mv, p)
+                   : cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel<1>, mq, mk, mv, p);
 }
 
 }  // namespace vc
