@@ -427,6 +427,31 @@ def test_tc_prefill_matches_decode_kernel_prefill(small_w, monkeypatch):
     b.free()
 
 
+def test_tc_prefill_folded_norm_matches_separate_pass(small_w, monkeypatch):
+    """The prefill's RMSNorms folded into its GEMMs (the residual epilogues
+    write the next hi / lo operand of x * g and the row sums of squares, the
+    consumers scale their rows; VOX_CUDA_DEC_FOLD_NORM=1) against the separate
+    normalisation pass (the default): the same KV rings and the same next
+    steps."""
+    w = small_w
+    rng = np.random.default_rng(61)
+    rows = (rng.standard_normal((38, B.DEC_DIM)) * 0.5).astype(np.float32)
+    embeds = (rng.standard_normal((3, B.DEC_DIM)) * 0.5).astype(np.float32)
+    out = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("VOX_CUDA_DEC_FOLD_NORM", mode)
+        dec = make_gpu_decoder(w)
+        st = dec.state(kv_cap=1024)
+        st.prefill(rows)
+        lg = [st.step(embeds[i], want_logits=True)[1] for i in range(3)]
+        kv = [np.concatenate([a.reshape(-1) for a in st.read_kv(l, 0, 41)]) for l in range(w.n_layers)]
+        out[mode] = (np.concatenate([x.reshape(-1) for x in lg]), np.concatenate(kv))
+        st.free()
+        dec.free()
+    assert B.rel_l2(out["1"][0], out["0"][0]) < 1e-4, B.rel_l2(out["1"][0], out["0"][0])
+    assert B.rel_l2(out["1"][1], out["0"][1]) < 1e-4, B.rel_l2(out["1"][1], out["0"][1])
+
+
 def test_prefill_batch_matches_one_state_at_a_time(small_w):
     """Several streams' prompts in shared tensor-core launches (one with no
     rows, one continuing from position 7) equal per-state prefills."""

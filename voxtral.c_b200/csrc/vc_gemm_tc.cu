@@ -130,17 +130,17 @@ struct EpiRow {
 
 // 1 / sqrt(mean square + eps) of a row from its per-32-column-chunk sums of
 // squares (K / 32 chunks, summed in chunk order: the same value whatever
-// the producer's tile width); eight loads in flight
+// the producer's tile width); sixteen loads in flight
 __device__ __forceinline__ float row_inv_rms(const float *ss, int ld, int row, int K) {
     const int nch = K / kEpiCols;
     float acc = 0.f;
     int c = 0;
-    for (; c + 8 <= nch; c += 8) {
-        float t[8];
+    for (; c + 16 <= nch; c += 16) {
+        float t[16];
 #pragma unroll
-        for (int u = 0; u < 8; u++) t[u] = __ldcg(ss + (size_t)(c + u) * ld + row);
+        for (int u = 0; u < 16; u++) t[u] = __ldcg(ss + (size_t)(c + u) * ld + row);
 #pragma unroll
-        for (int u = 0; u < 8; u++) acc += t[u];
+        for (int u = 0; u < 16; u++) acc += t[u];
     }
     for (; c < nch; c++) acc += __ldcg(ss + (size_t)c * ld + row);
     return 1.0f / sqrtf(acc / (float)K + kNormEps);
@@ -280,7 +280,7 @@ __device__ __forceinline__ int qkv_apply(const TcGemmParams &p, const EpiRow &er
 // the folded RMSNorm)
 template <int EPI>
 __device__ __forceinline__ void scale_row(const TcGemmParams &p, const EpiRow &er, float (&v)[kEpiCols]) {
-    if constexpr (EPI == TC_QKV_ENC || EPI == TC_SWIGLU) {
+    if constexpr (EPI == TC_QKV_ENC || EPI == TC_SWIGLU || EPI == TC_QKV_DEC) {
         if (p.ss_in) {
 #pragma unroll
             for (int j = 0; j < kEpiCols; j++) v[j] *= er.rs;
@@ -296,6 +296,24 @@ __device__ __forceinline__ void norm_prep_chunk(const TcGemmParams &p, int row, 
 #pragma unroll
     for (int j = 0; j < kEpiCols; j++) ss = fmaf(v[j], v[j], ss);
     p.ss_out[(size_t)(col0 / kEpiCols) * p.ss_ld + row] = ss;
+    if (p.hilo) {   // split activations: bf16 hi / lo rows of x * gain
+        uint32_t hh[kEpiCols / 2], ll[kEpiCols / 2];
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 4) {
+            const float4 g = __ldg(reinterpret_cast<const float4 *>(p.xn_gain + col0 + j));
+            const float a = v[j] * g.x, b = v[j + 1] * g.y, c = v[j + 2] * g.z, d = v[j + 3] * g.w;
+            hh[j >> 1] = pack_bf16x2(a, b), hh[(j >> 1) + 1] = pack_bf16x2(c, d);
+            ll[j >> 1] = pack_bf16_lo2(a, b), ll[(j >> 1) + 1] = pack_bf16_lo2(c, d);
+        }
+        uint16_t *oh = p.xn_out + (size_t)hilo_row(row) * p.ldo + col0;
+        uint16_t *ol = oh + (size_t)64 * p.ldo;
+#pragma unroll
+        for (int j = 0; j < kEpiCols; j += 8) {
+            st16(oh + j, hh[j >> 1], hh[(j >> 1) + 1], hh[(j >> 1) + 2], hh[(j >> 1) + 3]);
+            st16(ol + j, ll[j >> 1], ll[(j >> 1) + 1], ll[(j >> 1) + 2], ll[(j >> 1) + 3]);
+        }
+        return;
+    }
     uint32_t h[kEpiCols / 2], mx = 0;
 #pragma unroll
     for (int j = 0; j < kEpiCols; j += 4) {
@@ -718,9 +736,11 @@ __device__ __forceinline__ void epi_direct(const TcGemmParams &p, const EpiRow &
 // pair.  Returns false when a wait expired.
 template <int BN, int EPI>
 __device__ __forceinline__ bool epilogue_pair(const TcGemmParams &p, uint32_t tbase, int tm, int n0, int q, int half,
-                                              int lane, float *xch, volatile int *flg, int &seq, uint64_t deadline) {
+                                              int lane, float *xch, volatile int *flg, int &seq, uint64_t deadline,
+                                              float rs = 1.0f) {
     const bool hi = q < 2;
-    const EpiRow er = epi_row<EPI>(p, tm * 64 + 32 * (q & 1) + lane);
+    EpiRow er = epi_row<EPI>(p, tm * 64 + 32 * (q & 1) + lane);
+    er.rs = rs;
     const bool rv = er.row < p.M;
 #pragma unroll 1
     for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kEpiCols) {
@@ -750,6 +770,7 @@ __device__ __forceinline__ bool epilogue_pair(const TcGemmParams &p, uint32_t tb
             flg[1] = seq + 1;
         }
         seq++;
+        scale_row<EPI>(p, er, v);
         if (rv) epi_direct<EPI>(p, er, v, col0);
     }
     return true;
@@ -760,8 +781,9 @@ __device__ __forceinline__ bool epilogue_pair(const TcGemmParams &p, uint32_t tb
 // summed in slice order.
 template <int BN, int EPI>
 __device__ __forceinline__ void split_finish_pair(const TcGemmParams &p, int tm, int qq, int n0, int half, int lane,
-                                                  int KS, int t, int tiles) {
-    const EpiRow er = epi_row<EPI>(p, tm * 64 + 32 * qq + lane);
+                                                  int KS, int t, int tiles, float rs = 1.0f) {
+    EpiRow er = epi_row<EPI>(p, tm * 64 + 32 * qq + lane);
+    er.rs = rs;
     if (er.row >= p.M) return;
     const size_t slice = (size_t)tiles * kEpiWarps * 16 * BN / 4;   // float4s between slices
     const float4 *hi0 = reinterpret_cast<const float4 *>(p.ws + split_region(0, t, tiles, qq, half, BN)) + lane;
@@ -785,6 +807,7 @@ __device__ __forceinline__ void split_finish_pair(const TcGemmParams &p, int tm,
                     v[4 * j + 3] += x.w + y.w;
             }
         }
+        scale_row<EPI>(p, er, v);
         epi_direct<EPI>(p, er, v, col0);
     }
 }
@@ -935,8 +958,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // ss_in: the row's 1 / rms while the accumulator is still being
             // summed (with split-K whichever slice finishes last scales)
             float rs = 1.0f;
-            if constexpr (!HILO && (EPI == TC_QKV_ENC || EPI == TC_SWIGLU)) {
-                const int r = (t % MT) * kBM + 32 * q + lane;
+            if constexpr (EPI == TC_QKV_ENC || EPI == TC_SWIGLU || EPI == TC_QKV_DEC) {
+                // (HILO: the pair's output rows; either warp may finish them)
+                const int r = HILO ? (t % MT) * 64 + 32 * (q & 1) + lane : (t % MT) * kBM + 32 * q + lane;
                 if (p.ss_in && r < p.M) rs = row_inv_rms(p.ss_in, p.ss_ld, r, p.K);
             }
             const bool got = mbar_wait(&tfull[b], (lt >> 1) & 1u, deadline);
@@ -952,7 +976,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     // the lo warp of the pair (warp - 2 for a hi warp) stages its chunks
                     float *xch = reinterpret_cast<float *>(sStage + ((q < 2 ? warp - 2 : warp) - 2) * kStageBytes);
                     if (!epilogue_pair<BN, EPI>(p, tb, t % MT, n0, q, half, lane, xch,
-                                                pair_flags + 2 * (half * 2 + (q & 1)), pair_seq, deadline)) {
+                                                pair_flags + 2 * (half * 2 + (q & 1)), pair_seq, deadline, rs)) {
                         ok = false;
                         break;
                     }
@@ -973,7 +997,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     prev = __shfl_sync(0xffffffffu, prev, 0);
                     if (prev == (unsigned)(2 * KS - 1)) {
                         __threadfence();
-                        split_finish_pair<BN, EPI>(p, t % MT, q & 1, n0, half, lane, KS, t, tiles);
+                        split_finish_pair<BN, EPI>(p, t % MT, q & 1, n0, half, lane, KS, t, tiles, rs);
                         if (lane == 0) p.ws_cnt[t * 4 + pair] = 0u;
                     }
                 }
@@ -1443,9 +1467,10 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     if (epi == TC_SWIGLU && (p.N % 32 != 0)) return cudaErrorInvalidValue;
     // the folded RMSNorm: producer TC_RESID (fp16), consumers TC_QKV_ENC /
     // TC_SWIGLU; not with split activations
-    if (p.xn_out && (epi != TC_RESID || !p.xn_gain || !p.ss_out || p.ss_ld < p.M || !p.f16 || p.hilo))
+    // (split activations: bf16 hi / lo operand rows, consumers TC_QKV_DEC / TC_SWIGLU)
+    if (p.xn_out && (epi != TC_RESID || !p.xn_gain || !p.ss_out || p.ss_ld < p.M || (p.hilo ? p.f16 : !p.f16)))
         return cudaErrorInvalidValue;
-    if (p.ss_in && ((epi != TC_QKV_ENC && epi != TC_SWIGLU) || p.ss_ld < p.M || p.K % 32 != 0 || p.hilo))
+    if (p.ss_in && ((epi != TC_QKV_ENC && epi != TC_SWIGLU && epi != TC_QKV_DEC) || p.ss_ld < p.M || p.K % 32 != 0))
         return cudaErrorInvalidValue;
     switch (epi) {
         case TC_STORE:
@@ -1795,6 +1820,56 @@ rows_prenorm_kernel(const float *x, int M, int K, const float *w, uint16_t *out,
         o[i] = h;
     }
     count_clamped(mx);
+}
+
+// The same for split activations (the first layer of the decoder prefill):
+// row x -> bf16 hi / lo rows of x * w at hilo_row(r) and 64 rows below, and
+// the sums of squares of x per 32-column chunk.  One CTA of 256 threads per
+// row (float4 i = tid + 256 j: the 8 threads of a chunk share a warp);
+// K % 128 == 0, K <= 8192.
+__global__ void __launch_bounds__(256)
+rows_prenorm_hilo_kernel(const float *x, int M, int K, const float *w, uint16_t *out, float *ss, int ss_ld) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int row = blockIdx.x, tid = threadIdx.x;
+    if (row >= M) return;   // CTA-uniform
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)row * K);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    uint2 *oh = reinterpret_cast<uint2 *>(out + (size_t)hilo_row(row) * K);
+    uint2 *ol = reinterpret_cast<uint2 *>(out + (size_t)(hilo_row(row) + 64) * K);
+    const int K4 = K >> 2;
+#pragma unroll
+    for (int j = 0; j < kHiloRegs; j++) {
+        const int i = tid + 256 * j;
+        if (i >= K4) break;   // warp-uniform: K4 % 32 == 0
+        const float4 a = x4[i];
+        float s2 = fmaf(a.w, a.w, fmaf(a.z, a.z, fmaf(a.y, a.y, a.x * a.x)));
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
+        if ((tid & 7) == 0) ss[(size_t)(i >> 3) * ss_ld + row] = s2;
+        const float4 g = __ldg(w4 + i);
+        const float v0 = a.x * g.x, v1 = a.y * g.y, v2 = a.z * g.z, v3 = a.w * g.w;
+        oh[i] = make_uint2(pack_bf16x2(v0, v1), pack_bf16x2(v2, v3));
+        ol[i] = make_uint2(pack_bf16_lo2(v0, v1), pack_bf16_lo2(v2, v3));
+    }
+}
+
+cudaError_t launch_rows_prenorm_hilo(const float *x, int M, int K, const float *w, uint16_t *out, float *ss,
+                                     int ss_ld, cudaStream_t st, bool pdl) {
+    if (M <= 0 || K % 128 != 0 || K > 4 * 256 * kHiloRegs || ss_ld < M || !al16(x) || !al16(w) ||
+        ((uintptr_t)out & 7) != 0)
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(M);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, rows_prenorm_hilo_kernel, x, M, K, w, out, ss, ss_ld);
 }
 
 cudaError_t launch_rows_prenorm(const float *x, int M, int K, const float *w, uint16_t *out, float *ss, int ss_ld,

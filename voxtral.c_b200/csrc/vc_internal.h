@@ -248,6 +248,9 @@ cudaError_t launch_rows_to_bf16(const float *x, int M, int K, int ld, const floa
 // the row scales of a consumer GEMM with ss_in (K % 128 == 0, K <= 2048)
 cudaError_t launch_rows_prenorm(const float *x, int M, int K, const float *w, uint16_t *out, float *ss, int ss_ld,
                                 cudaStream_t st, bool pdl);
+// the same as bf16 hi / lo rows in the hilo_row layout (split activations)
+cudaError_t launch_rows_prenorm_hilo(const float *x, int M, int K, const float *w, uint16_t *out, float *ss,
+                                     int ss_ld, cudaStream_t st, bool pdl);
 // In place: bf16 -> fp16 (round to nearest even; the values of bf16 weights
 // are inside fp16's range).
 // fp32 rows -> bf16 hi / lo rows in the hilo_row layout, v = x

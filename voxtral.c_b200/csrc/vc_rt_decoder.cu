@@ -95,6 +95,7 @@ struct PrefillTc {
     uint16_t *att16 = nullptr;   // [2 cap][4096]
     uint16_t *h16 = nullptr;     // [2 cap][9216]
     unsigned *counters = nullptr;  // [cap][8]
+    float *ss = nullptr;         // folded RMSNorm: sums of squares per 32-column chunk [96][cap]
     float *split = nullptr;      // split-K partials [kEncSplitFloats]
     unsigned *split_cnt = nullptr;
     unsigned *err = nullptr;
@@ -591,6 +592,7 @@ PrefillTc *make_prefill(DevCtx *c, int cap) {
     const size_t o_q = take(4 * C * kQDim);
     const size_t o_xn = take(2 * 2 * C * kDecDim), o_att16 = take(2 * 2 * C * kQDim);
     const size_t o_h16 = take(2 * 2 * C * kDecHidden), o_cnt = take(4 * C * kDecKvHeads);
+    const size_t o_ss = take(4 * C * (kDecDim / 32));
     const size_t o_split = take(4 * kEncSplitFloats), o_scnt = take(4 * kTcSplitCounters), o_err = take(4);
     f->bytes = off;
     if (dev_alloc(c, (void **)&f->block, f->bytes) != cudaSuccess ||
@@ -610,6 +612,7 @@ PrefillTc *make_prefill(DevCtx *c, int cap) {
     f->att16 = (uint16_t *)(b + o_att16);
     f->h16 = (uint16_t *)(b + o_h16);
     f->counters = (unsigned *)(b + o_cnt);
+    f->ss = (float *)(b + o_ss);
     f->split = (float *)(b + o_split);
     f->split_cnt = (unsigned *)(b + o_scnt);
     f->err = (unsigned *)(b + o_err);
@@ -658,10 +661,24 @@ int enqueue_prefill(vox_cuda_decoder *d, PrefillTc *f, int M, int S, cudaStream_
         p.ws_cnt = f->split_cnt;
         return p;
     };
+    // VOX_CUDA_DEC_FOLD_NORM = 1 folds the RMSNorms into the GEMMs around
+    // them (the residual epilogues write the next operand's hi / lo rows of
+    // x * g and the row sums of squares, the consumers scale their rows by
+    // 1 / rms), as the encoder does.  Off by default: measured 2.68 -> 2.72 ms
+    // for 38 rows and 3.82 -> 3.80 ms for 114 (the consumers' 96-chunk row
+    // sums and the wider residual epilogue cost what the two norm launches
+    // per layer saved).
+    const char *fe = getenv("VOX_CUDA_DEC_FOLD_NORM");
+    const bool fold = fe && fe[0] == '1';
+    if (fold) VC_TRY(launch_rows_prenorm_hilo(f->x, M, kDecDim, d->L[0].g_attn, f->xn, f->ss, f->cap, st, pdl));
     for (int l = 0; l < d->n_layers; l++) {
         const DecLayer &L = d->L[l];
-        VC_TRY(launch_rows_hilo(f->x, M, kDecDim, kDecDim, L.g_attn, f->xn, st, pdl));
+        if (!fold) VC_TRY(launch_rows_hilo(f->x, M, kDecDim, kDecDim, L.g_attn, f->xn, st, pdl));
         TcGemmParams p = gemm(M, kQkvRows, kDecDim);
+        if (fold) {
+            p.ss_in = f->ss;
+            p.ss_ld = f->cap;
+        }
         p.q32 = f->q;
         p.slots = f->slots;
         p.layer = l;
@@ -680,16 +697,32 @@ int enqueue_prefill(vox_cuda_decoder *d, PrefillTc *f, int M, int S, cudaStream_
         p = gemm(M, kDecDim, kQDim);
         p.out = f->x;
         p.ldo = kDecDim;
+        if (fold) {
+            p.xn_out = f->xn;
+            p.xn_gain = L.g_ffn;
+            p.ss_out = f->ss;
+            p.ss_ld = f->cap;
+        }
         VC_TRY(launch_tc_gemm(TC_RESID, p, f->att16, L.wo_rm, st, pdl));
-        VC_TRY(launch_rows_hilo(f->x, M, kDecDim, kDecDim, L.g_ffn, f->xn, st, pdl));
+        if (!fold) VC_TRY(launch_rows_hilo(f->x, M, kDecDim, kDecDim, L.g_ffn, f->xn, st, pdl));
         p = gemm(M, 2 * kDecHidden, kDecDim);
         p.out_bf16 = f->h16;
         p.ldo_bf16 = kDecHidden;
         p.out_hilo = 1;
+        if (fold) {
+            p.ss_in = f->ss;
+            p.ss_ld = f->cap;
+        }
         VC_TRY(launch_tc_gemm(TC_SWIGLU, p, f->xn, L.w13_rm, st, pdl));
         p = gemm(M, kDecDim, kDecHidden);
         p.out = f->x;
         p.ldo = kDecDim;
+        if (fold && l + 1 < d->n_layers) {   // the next layer's operand and row sums
+            p.xn_out = f->xn;
+            p.xn_gain = d->L[l + 1].g_attn;
+            p.ss_out = f->ss;
+            p.ss_ld = f->cap;
+        }
         VC_TRY(launch_tc_gemm(TC_RESID, p, f->h16, L.w2_rm, st, pdl));
     }
     return VOX_CUDA_OK;
