@@ -1328,6 +1328,9 @@ static int batch_prepare(vox_cuda_dec_state *const *states, int n, vox_cuda_deco
         fill_slot(states[i], states[i]->pos, h_slots(w) + i);
         host_rope_table(states[i]->pos, kHeadDim, h_rope(w) + i * kHeadDim);
     }
+    // no caller token buffer unless the asynchronous step sets one (a
+    // profile or synchronous launch must not write an earlier call's buffer)
+    *h_tokens_to(w) = nullptr;
     *pd = d;
     *pc = c;
     return VOX_CUDA_OK;
