@@ -341,6 +341,14 @@ def test_async_batched_steps_match_sync_batched_steps(small_w):
         assert np.array_equal(dev_tokens[s].cpu().numpy(), want[s]), s
     for i in range(n):
         assert async_states[i].position == sync_states[i].position
+    # the argmax writes an asynchronous step's caller buffer itself; later
+    # synchronous steps and profiles must leave the last such buffer alone
+    dev_tokens[-1].fill_(-7)
+    torch.cuda.synchronize()
+    V.step_batch(async_states, embeds[0])
+    V.profile_batch(async_states, dev_embeds[0].data_ptr(), iters=1)
+    torch.cuda.synchronize()
+    assert (dev_tokens[-1].cpu().numpy() == -7).all()
     for st in sync_states + async_states:
         st.free()
     d.free()
