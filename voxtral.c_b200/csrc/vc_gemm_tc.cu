@@ -56,8 +56,8 @@ struct TcCfg {
     static constexpr int kStages = (196608 / (kABytes + kBBytes)) < 6 ? (196608 / (kABytes + kBBytes)) : 6;
     // two accumulators of BN columns; the allocation is a power of two
     static constexpr int kTmemCols = (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-    static constexpr int kSmem =
-        kStages * (kABytes + kBBytes) + kEpiWarps * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int kSmem = kStages * (kABytes + kBBytes) + kEpiWarps * kStageBytes + 1024 /*align*/ +
+                                 256 /*barriers*/ + 512 /*row scales of a cluster split*/;
 };
 
 __device__ __forceinline__ float gelu_tanh(float v) {
@@ -812,6 +812,54 @@ __device__ __forceinline__ void split_finish_pair(const TcGemmParams &p, int tm,
     }
 }
 
+// ---- cluster split-K (one row tile, p.cluster): the KS K slices of a tile
+// are the KS CTAs of a thread-block cluster.  Each stages its fp32 partial in
+// its drained stage ring, 32 x 32 chunks lane-contiguous ([8 float4][32
+// lanes], the epilogue warp's region); after a cluster barrier the 8 x KS
+// epilogue warps of the cluster split the tile's chunks, each summing one
+// chunk over the KS CTAs (distributed shared memory, rank order: the same
+// sum whichever CTA reads) and running the epilogue on it.
+
+// this warp's chunks (of its column half) of the accumulator -> its region
+template <int BN>
+__device__ __forceinline__ void cl_stage_partial(uint32_t tbase, float4 *part, int ew, int half, int lane) {
+#pragma unroll 1
+    for (int cc = 0; cc < BN / 64; cc++) {
+        float v[kEpiCols];
+        tmem_ld32(tbase + (uint32_t)(half * (BN / 2) + cc * kEpiCols), v);
+        float4 *d = part + (size_t)(ew * (BN / 64) + cc) * 256 + lane;
+#pragma unroll
+        for (int j = 0; j < kEpiCols / 4; j++) d[32 * j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+}
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr_cluster) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr_cluster)
+                 : "memory");
+    return v;
+}
+
+// chunk uu of the tile summed over the KS CTAs, in rank order
+template <int BN>
+__device__ __forceinline__ void cl_sum_chunk(const float4 *part, int uu, int KS, int lane, float (&v)[kEpiCols]) {
+    const uint32_t base = smem_u32(part + (size_t)uu * 256 + lane);
+#pragma unroll
+    for (int j = 0; j < kEpiCols; j++) v[j] = 0.f;
+    for (int r = 0; r < KS; r++) {
+        float4 a[kEpiCols / 4];
+        const uint32_t ra = mapa_shared(base, (uint32_t)r);
+#pragma unroll
+        for (int j = 0; j < kEpiCols / 4; j++) a[j] = ld_dsmem_f4(ra + 512u * j);
+#pragma unroll
+        for (int j = 0; j < kEpiCols / 4; j++) {
+            v[4 * j] += a[j].x, v[4 * j + 1] += a[j].y, v[4 * j + 2] += a[j].z, v[4 * j + 3] += a[j].w;
+        }
+    }
+}
+
 template <int BN, int EPI, bool HILO = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -830,8 +878,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t *tempty = tfull + 2;    // [2] accumulator b was drained by the epilogue
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
     volatile int *pair_flags = reinterpret_cast<volatile int *>(tmem_slot + 1);   // HILO: [4 pairs][2]
+    float *rs_s = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(full) + 256);   // [128]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool CL = !HILO && p.cluster != 0;   // cluster split-K: one unit per CTA
     // row tiles: 128 output rows, or (HILO) 64 output rows = 128 A rows [hi; lo]
     const int MT = HILO ? (p.M + 63) / 64 : (p.M + kBM - 1) / kBM;
     const int tiles = MT * ((p.N + BN - 1) / BN);
@@ -1003,7 +1053,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
                 continue;
             }
-            if (KS == 1) {
+            if (CL) {   // this slice's partial into the drained ring; the epilogue runs after the cluster barrier
+                cl_stage_partial<BN>(tb, reinterpret_cast<float4 *>(smem), warp - 2, half, lane);
+                if (half == 0) rs_s[32 * q + lane] = rs;
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);
+            } else if (KS == 1) {
                 epilogue_tile<BN, EPI>(p, mp, tb, m0 + 32 * q, n0, half, lane, stg, rs);
                 tc_fence_before();
                 __syncwarp();
@@ -1030,6 +1086,40 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     }
 
+    if (CL) {
+        // every slice's partial is in its CTA's shared memory (every thread of
+        // every CTA arrives, whatever failed before: no CTA waits forever)
+        cluster_sync_all();
+        if (warp >= 2 && ok) {
+            const int t = (int)blockIdx.x / KS, rank = (int)blockIdx.x % KS;
+            const int m0 = (t % MT) * kBM, n0 = (t / MT) * BN;
+            const EpiMaps mp = {&tmO, &tmK, &tmV};
+            unsigned char *stg = sStage + (warp - 2) * kStageBytes;
+            constexpr int U = kEpiWarps * (BN / 64);   // 32 x 32 chunks of the tile
+            for (int uu = (warp - 2) * KS + rank; uu < U; uu += kEpiWarps * KS) {
+                const int ew = uu / (BN / 64), cc = uu % (BN / 64);
+                const int q = (ew + 2) & 3, half = ew >> 2;   // the writing warp's lane quarter / half
+                const int row0 = m0 + 32 * q, col0 = n0 + half * (BN / 2) + cc * kEpiCols;
+                float v[kEpiCols];
+                cl_sum_chunk<BN>(reinterpret_cast<const float4 *>(smem), uu, KS, lane, v);
+                if (col0 >= p.N) continue;   // warp-uniform
+                EpiRow er = epi_row<EPI>(p, row0 + lane);
+                er.rs = rs_s[32 * q + lane];
+                scale_row<EPI>(p, er, v);
+                if (p.tma_out) {
+                    epi_tma<EPI>(p, mp, er, v, row0, col0, lane, stg);
+                    continue;
+                }
+                if (er.row >= p.M) continue;
+                int region = 0;
+                if constexpr (EPI == TC_QKV_ENC) region = qkv_apply(p, er, v, col0);
+                if constexpr (EPI == TC_QKV_DEC) region = dec_qkv_apply(p, er, v, col0);
+                if (p.vec && col0 + kEpiCols <= p.N) epi_vec<EPI>(p, er, v, col0, region);
+                else epi_scalar<EPI>(p, er, v, col0, region);
+            }
+        }
+        cluster_sync_all();   // no CTA leaves while a peer still reads its partial
+    }
     if (warp >= 2 && lane == 0 && p.tma_out) bulk_wait_all();   // epilogue stores complete
     if (!__all_sync(0xffffffffu, ok)) ok = false;
     if (!ok) {
@@ -1326,15 +1416,27 @@ cudaError_t launch_bn(const TcGemmParams &p, const void *A, const void *W, cudaS
     const int units = mt * ((p.N + BN - 1) / BN) * (p.ksplit > 1 ? p.ksplit : 1);
     const int sms = device_sms(dev);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(units < sms ? units : sms);
+    // (cluster split-K: exactly one unit per CTA, the slices of a tile one cluster)
+    cfg.gridDim = dim3(p.cluster ? units : (units < sms ? units : sms));
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = TcCfg<BN>::kSmem;
     cfg.stream = st;
-    cudaLaunchAttribute attr1[1];
-    attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr1[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr1[2];
+    int na = 0;
+    if (pdl) {
+        attr1[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr1[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (p.cluster) {
+        attr1[na].id = cudaLaunchAttributeClusterDimension;
+        attr1[na].val.clusterDim.x = p.ksplit;
+        attr1[na].val.clusterDim.y = 1;
+        attr1[na].val.clusterDim.z = 1;
+        na++;
+    }
     cfg.attrs = attr1;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, EPI, HILO>, ma, mb, mo, mk, mv, p);
 }
 
@@ -1424,6 +1526,49 @@ int env_tc_bn() {
 // N = 1280) and at M = 100 and 800; 192 wins where it fits in as many rounds
 // as 256 (q|k|v at M = 500 and 800, w1|w3 at M = 500).
 // VOX_CUDA_TC_BN = 64 | 128 | 192 | 256 forces a width.
+// How many clusters of ks CTAs of the BN-wide kernel the device runs at
+// once (one CTA per SM; clusters sit inside one GPC, so a cluster size that
+// does not divide the GPCs' SM counts leaves SMs idle).  Cached per BN and
+// cluster size; 0 when the query fails.
+template <int BN>
+int tc_max_clusters(int ks) {
+    static std::atomic<int> cache[9];   // 0: not asked yet; -1: failed
+    if (ks < 2 || ks > 8) return 0;
+    int c = cache[ks].load();
+    if (c == 0) {
+        int n = 0;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(ks * 32);
+        cfg.blockDim = dim3(kTcThreads);
+        cfg.dynamicSmemBytes = TcCfg<BN>::kSmem;
+        cudaLaunchAttribute a[1];
+        a[0].id = cudaLaunchAttributeClusterDimension;
+        a[0].val.clusterDim.x = ks;
+        a[0].val.clusterDim.y = 1;
+        a[0].val.clusterDim.z = 1;
+        cfg.attrs = a;
+        cfg.numAttrs = 1;
+        if (cudaFuncSetAttribute(tc_gemm_kernel<BN, TC_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 TcCfg<BN>::kSmem) != cudaSuccess ||
+            cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<BN, TC_STORE>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        c = n > 0 ? n : -1;
+        cache[ks].store(c);
+    }
+    return c > 0 ? c : 0;
+}
+
+int tc_max_clusters_bn(int bn, int ks) {
+    switch (bn) {
+        case 64: return tc_max_clusters<64>(ks);
+        case 128: return tc_max_clusters<128>(ks);
+        case 256: return tc_max_clusters<256>(ks);
+    }
+    return 0;
+}
+
 int tc_gemm_bn(int M, int N) {
     if (const int f = env_tc_bn()) return f;
     int dev = 0;
@@ -1531,13 +1676,41 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     // 4.97 -> 3.89 ms for three streams' 114-row prefill, equal at 38 rows)
     if (bn == 0) bn = p.hilo ? (env_tc_bn() == 64 ? 64 : 128) : tc_gemm_bn(p.M, p.N);
     p.ksplit = 1;
-    if (p.ws && p.ws_cnt && !pair) {
+    p.cluster = 0;
+    const int e_cl = env_int("VOX_CUDA_TC_CLUSTER");   // 0 / unset: automatic; -1: off; n >= 2: at most n slices
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = device_sms(dev);
+    if (!p.hilo && !pair && p.M <= kBM && e_cl >= 0 && 2 * ((p.N + bn - 1) / bn) < sms) {
+        // One row tile (M <= 128) whose column tiles leave most SMs idle: a
+        // k-block costs about the same time whatever the tile width, so
+        // split K over a cluster and reduce in distributed shared memory.
+        // The most CTAs (<= one per SM) with >= 4 k-blocks per slice whose
+        // clusters all run at once (a second wave of clusters costs more
+        // than the split saves); on a tie the fewer slices.
+        const int KB = (p.K + kBK - 1) / kBK;
+        int best_ctas = 0, best_bn = 0, best_ks = 1;
+        for (int w : {64, 128, 256}) {
+            if (env_tc_bn() && w != env_tc_bn()) continue;
+            const int tiles = (p.N + w - 1) / w;
+            for (int ks = 2; ks <= std::min(e_cl >= 2 ? e_cl : 8, KB / 4); ks++) {
+                if (tiles * ks > sms || tiles * ks <= best_ctas) continue;
+                if (tiles > tc_max_clusters_bn(w, ks)) continue;
+                best_ctas = tiles * ks;
+                best_bn = w;
+                best_ks = ks;
+            }
+        }
+        if (best_ks >= 2) {
+            bn = best_bn;
+            p.ksplit = best_ks;
+            p.cluster = 1;
+        }
+    }
+    if (p.ws && p.ws_cnt && !pair && !p.cluster) {
         // Split-K when the tiles leave most SMs idle (small M): up to
         // kTcMaxSplit K slices of >= 4 k-blocks each, at most one unit per SM.
         // VOX_CUDA_TC_KSPLIT = n caps the slices (1: off).
-        int dev = 0;
-        cudaGetDevice(&dev);
-        const int sms = device_sms(dev);
         const int mt = p.hilo ? (p.M + 63) / 64 : (p.M + kBM - 1) / kBM, KB = (p.K + kBK - 1) / kBK;
         // measured at M = 100 with the lane-contiguous workspace: a win for
         // K = 5120 (w2) and K = 2048 (wo, 2.45 -> 2.32 ms per 32-layer chunk)

@@ -228,6 +228,8 @@ struct TcGemmParams {
     int ss_ld;               // rows per chunk plane (>= M)
     int vec;                 // set by launch_tc_gemm: all destinations allow 16-byte stores
     int tma_out;             // set by launch_tc_gemm: the epilogue stores through TMA
+    int cluster;             // set by launch_tc_gemm: the ksplit slices of a tile are one cluster,
+                             //   reduced through distributed shared memory (one row tile)
 };
 
 constexpr int kTcSplitCounters = 4096;   // split-K tickets a caller provides (8 per tile)
