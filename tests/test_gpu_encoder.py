@@ -130,21 +130,29 @@ def test_encoder_attention_kernels_agree(monkeypatch):
 
 
 def test_encoder_split_k_matches_unsplit(monkeypatch):
-    """Small chunks run their GEMMs split along K (fp32 partials summed in a
-    fixed slice order by the last slice to finish); against the same chunks
-    with split-K off only the fp32 summation grouping differs."""
+    """Small chunks run their GEMMs split along K: by default the slices of a
+    tile are one thread-block cluster summed through distributed shared
+    memory in rank order (one or two row tiles here: 100, 3, 256, 64 rows);
+    with VOX_CUDA_TC_CLUSTER=-1 through the global workspace (fp32 partials
+    summed in a fixed slice order by the last slice to finish).  Against the
+    same chunks with split-K off (VOX_CUDA_TC_KSPLIT=1) only the fp32
+    summation grouping differs; a second run of the default is bit-identical."""
     ew = B.EncoderWeights(seed=10, n_layers=3, distinct=3, norm_noise=0.1)
     e = make_gpu_encoder(ew)
     outs = {}
-    for mode in ("", "1"):
-        monkeypatch.setenv("VOX_CUDA_TC_KSPLIT", mode)
+    for mode, ks, cl in (("cluster", "", ""), ("workspace", "", "-1"), ("off", "1", ""), ("again", "", "")):
+        monkeypatch.setenv("VOX_CUDA_TC_KSPLIT", ks)
+        monkeypatch.setenv("VOX_CUDA_TC_CLUSTER", cl)
         st = e.state(max_chunk=256)
         outs[mode] = [st.step(B.normal_f32((n, B.ENC_DIM), 1010 + i)) for i, n in enumerate([100, 3, 256, 64])]
         st.free()
     e.free()
-    for i, (a, b) in enumerate(zip(outs[""], outs["1"])):
+    for i in range(4):
+        a = outs["cluster"][i]
         assert np.isfinite(a).all()
-        assert B.rel_l2(a, b) < 2e-3, (i, B.rel_l2(a, b))
+        assert np.array_equal(a, outs["again"][i]), i
+        for other in ("workspace", "off"):
+            assert B.rel_l2(a, outs[other][i]) < 2e-3, (i, other, B.rel_l2(a, outs[other][i]))
 
 
 def test_folded_norm_matches_separate_norm_pass_and_oracle(monkeypatch):

@@ -87,3 +87,26 @@ def test_sgemm_tensor_core_path_matches_reference(case):
     y = V.sgemm_bf16(x, W, b)
     idx, val, _, _ = unpack(g, name)
     assert B.rel_l2(y.reshape(-1)[idx], val) < TC_GEMM_TOL
+
+
+# (VOX_CUDA_TC_CLUSTER, VOX_CUDA_TC_BN): the cluster split-K for few-tile
+# launches (K slices of a tile = the CTAs of one cluster, partials summed
+# through distributed shared memory), automatic, capped at 2 / 3 / 8 slices,
+# with forced 64- and 128-wide tiles, and off
+CLUSTER_MODES = [("0", ""), ("2", ""), ("3", ""), ("8", ""), ("0", "64"), ("0", "128"), ("-1", "")]
+
+
+@pytest.mark.parametrize("mode", CLUSTER_MODES, ids=[f"cl{c}-bn{b or 'auto'}" for c, b in CLUSTER_MODES])
+@pytest.mark.parametrize("M,N,K", [(100, 1280, 5120), (25, 3072, 5120), (300, 1280, 2048), (129, 200, 1032)],
+                         ids=["w2-100", "25rows", "wo-300", "ragged"])
+def test_tc_gemm_cluster_split(M, N, K, mode, monkeypatch):
+    monkeypatch.setenv("VOX_CUDA_TC_CLUSTER", mode[0])
+    monkeypatch.setenv("VOX_CUDA_TC_BN", mode[1])
+    A = B.normal_bf16((M, K), 1200 + M, std=1.0)
+    W = B.normal_bf16((N, K), 2200 + N + K)
+    bias = B.normal_f32(N, 3200 + N, 0.02)
+    C = run_gemm(A, W, bias)
+    ref = B.bf16_to_f32(A).astype(np.float64) @ B.bf16_to_f32(W).astype(np.float64).T + bias
+    assert np.isfinite(C).all()
+    assert B.rel_l2(C, ref) < 1e-5
+    assert np.array_equal(C, run_gemm(A, W, bias))   # deterministic: the same sum whichever CTA reads

@@ -1677,22 +1677,29 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     if (bn == 0) bn = p.hilo ? (env_tc_bn() == 64 ? 64 : 128) : tc_gemm_bn(p.M, p.N);
     p.ksplit = 1;
     p.cluster = 0;
-    const int e_cl = env_int("VOX_CUDA_TC_CLUSTER");   // 0 / unset: automatic; -1: off; n >= 2: at most n slices
+    // VOX_CUDA_TC_CLUSTER 0 / unset: automatic; -1: off; n >= 2: at most n
+    // slices (VOX_CUDA_TC_KSPLIT = n caps these slices too; 1: no split)
+    int e_cl = env_int("VOX_CUDA_TC_CLUSTER");
+    const int e_ks = env_int("VOX_CUDA_TC_KSPLIT");
+    if (e_ks == 1) e_cl = -1;
+    else if (e_ks >= 2 && e_cl >= 0) e_cl = e_cl >= 2 ? std::min(e_cl, e_ks) : e_ks;
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = device_sms(dev);
-    if (!p.hilo && !pair && p.M <= kBM && e_cl >= 0 && 2 * ((p.N + bn - 1) / bn) < sms) {
-        // One row tile (M <= 128) whose column tiles leave most SMs idle: a
-        // k-block costs about the same time whatever the tile width, so
-        // split K over a cluster and reduce in distributed shared memory.
-        // The most CTAs (<= one per SM) with >= 4 k-blocks per slice whose
-        // clusters all run at once (a second wave of clusters costs more
-        // than the split saves); on a tie the fewer slices.
+    const int mt_cl = (p.M + kBM - 1) / kBM;
+    if (!p.hilo && !pair && e_cl >= 0 && 4 * mt_cl * ((p.N + bn - 1) / bn) < 3 * sms) {
+        // Few tiles (fewer than 3/4 of the SMs): a k-block costs about the
+        // same time whatever the tile width, so split K over a cluster and
+        // reduce in distributed shared memory.  The most CTAs (<= one per
+        // SM) with >= 4 k-blocks per slice whose clusters all run at once (a
+        // second wave of clusters costs more than the split saves); on a tie
+        // the fewer slices; 64- or 128-wide tiles (256-wide split tiles
+        // measured slower); only when that is 1.5x the unsplit CTAs.
         const int KB = (p.K + kBK - 1) / kBK;
         int best_ctas = 0, best_bn = 0, best_ks = 1;
-        for (int w : {64, 128, 256}) {
+        for (int w : {64, 128}) {
             if (env_tc_bn() && w != env_tc_bn()) continue;
-            const int tiles = (p.N + w - 1) / w;
+            const int tiles = mt_cl * ((p.N + w - 1) / w);
             for (int ks = 2; ks <= std::min(e_cl >= 2 ? e_cl : 8, KB / 4); ks++) {
                 if (tiles * ks > sms || tiles * ks <= best_ctas) continue;
                 if (tiles > tc_max_clusters_bn(w, ks)) continue;
@@ -1701,7 +1708,7 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
                 best_ks = ks;
             }
         }
-        if (best_ks >= 2) {
+        if (best_ks >= 2 && 2 * best_ctas >= 3 * mt_cl * ((p.N + bn - 1) / bn)) {
             bn = best_bn;
             p.ksplit = best_ks;
             p.cluster = 1;
