@@ -180,6 +180,39 @@ def test_folded_norm_matches_separate_norm_pass_and_oracle(monkeypatch):
     e.free()
 
 
+def test_folded_norm_tma_residual_path_is_bit_identical(monkeypatch):
+    """Where a residual GEMM's stage ring is free (the CTA's last tile, or the
+    reduction of a cluster split), the folded norm's producer loads its
+    residual tiles and stores the updated rows by TMA: the same arithmetic as
+    the direct loads and stores (VOX_CUDA_TC_FOLD_TMA=0), so bit-identical.
+    The fold is forced up to 1500 rows; chunks of one row tile (cluster
+    split), several row tiles, 1500 rows (one tile per CTA) and 1500 rows
+    with 64-wide tiles (two tiles on some CTAs: the first by direct stores,
+    the last through TMA); the 1500-row chunk also against the oracle."""
+    ew = B.EncoderWeights(seed=18, n_layers=2, distinct=2, norm_noise=0.1)
+    e = make_gpu_encoder(ew)
+    sizes = [100, 37, 700, 1500]
+    xs = [B.normal_f32((n, B.ENC_DIM), 1180 + i) for i, n in enumerate(sizes)]
+    monkeypatch.setenv("VOX_CUDA_ENC_FOLD_MAX_ROWS", "1500")
+    outs = {}
+    for bn in ("", "64"):
+        monkeypatch.setenv("VOX_CUDA_TC_BN", bn)
+        for mode in ("0", ""):
+            monkeypatch.setenv("VOX_CUDA_TC_FOLD_TMA", mode)
+            st = e.state(max_chunk=1500)
+            outs[(bn, mode)] = [st.step(x) for x in xs]
+            st.free()
+    e.free()
+    for bn in ("", "64"):
+        for i in range(len(sizes)):
+            a, b = outs[(bn, "")][i], outs[(bn, "0")][i]
+            assert np.isfinite(a).all()
+            assert np.array_equal(a, b), (bn, sizes[i])
+    o = B.OracleEncoder(ew, kv_max=2400)
+    ref = [o.step(x) for x in xs]
+    assert B.rel_l2(outs[("", "")][3], ref[3]) < 5e-3, B.rel_l2(outs[("", "")][3], ref[3])
+
+
 def test_encoder_attention_key_split_matches_unsplit(monkeypatch):
     """Chunks of few row tiles split each tile's key blocks over up to 4 CTAs
     (unnormalised partials merged by the last CTA): against the unsplit

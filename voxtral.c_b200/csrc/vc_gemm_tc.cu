@@ -582,6 +582,62 @@ __device__ __forceinline__ void resid_norm_tile(const TcGemmParams &p, uint32_t 
     }
 }
 
+// TC_RESID with the folded norm when the stage ring is drained (the CTA's
+// last tile, or a cluster split's reduction): the warp's residual chunks
+// (32 rows x 32 fp32 columns each) arrive by TMA in the 128-byte swizzle
+// into `buf` (already issued on `bar`); the updated rows go back into the
+// same tiles and out by TMA stores (whole lines), while fp16(x * gain) and
+// the chunk sums of squares are stored per row (norm_prep_chunk).  The same
+// arithmetic as resid_norm_tile: x = (acc + bias) + residual.
+__device__ __forceinline__ void resid_fold_chunk_tma(const TcGemmParams &p, const EpiMaps &mp, float (&v)[kEpiCols],
+                                                     int row0, int col0, int lane, unsigned char *t) {
+    add_bias(v, p.bias, col0, p.N);
+#pragma unroll
+    for (int j = 0; j < kEpiCols / 4; j++) {
+        float4 *a = reinterpret_cast<float4 *>(t + lane * 128 + 16 * (j ^ (lane & 7)));
+        const float4 r = *a;
+        v[4 * j] += r.x, v[4 * j + 1] += r.y, v[4 * j + 2] += r.z, v[4 * j + 3] += r.w;
+        *a = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) tma_store_2d(mp.o, t, col0, row0);
+    if (row0 + lane < p.M) norm_prep_chunk(p, row0 + lane, col0, v);
+}
+
+// issue the residual loads of the warp's chunks [col0, col0 + 32 n) of rows
+// row0.. (lane 0); the number of chunks inside N, 0 when none is loaded
+__device__ __forceinline__ int resid_fold_issue(const TcGemmParams &p, const EpiMaps &mp, int row0, int col0,
+                                                int n, int lane, unsigned char *buf, uint64_t *bar) {
+    if (row0 >= p.M) return 0;
+    int nin = 0;
+    while (nin < n && col0 + nin * kEpiCols < p.N) nin++;
+    if (lane == 0 && nin > 0) {
+        mbar_expect_tx(bar, (uint32_t)(nin * kStageBytes));
+        for (int i = 0; i < nin; i++) tma_load_2d_plain(buf + i * kStageBytes, mp.o, col0 + i * kEpiCols, row0, bar);
+    }
+    return nin;
+}
+
+template <int BN>
+__device__ __forceinline__ bool resid_fold_tile_tma(const TcGemmParams &p, const EpiMaps &mp, uint32_t tbase,
+                                                    int row0, int n0, int half, int lane, unsigned char *buf,
+                                                    uint64_t *bar, uint64_t deadline) {
+    constexpr int kSteps = BN / 2 / kEpiCols;
+    const int c0 = half * (BN / 2);
+    const int nin = resid_fold_issue(p, mp, row0, n0 + c0, kSteps, lane, buf, bar);
+    bool got = true;
+    if (nin > 0) got = __all_sync(0xffffffffu, mbar_wait(bar, 0, deadline));
+#pragma unroll 1
+    for (int i = 0; i < kSteps; i++) {
+        float v[kEpiCols];
+        tmem_ld32(tbase + (uint32_t)(c0 + i * kEpiCols), v);   // warp-collective: before any branch
+        if (i < nin && got) resid_fold_chunk_tma(p, mp, v, row0, n0 + c0 + i * kEpiCols, lane, buf + i * kStageBytes);
+    }
+    if (lane == 0 && nin > 0) bulk_commit();
+    return got;
+}
+
 // The epilogue of one accumulator for one epilogue warp: this thread's row
 // (its TMEM lane) and the warp's half of the BN columns from n0, 32 columns
 // per tcgen05.ld.  row0 = the warp's first row.
@@ -879,6 +935,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
     volatile int *pair_flags = reinterpret_cast<volatile int *>(tmem_slot + 1);   // HILO: [4 pairs][2]
     float *rs_s = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(full) + 256);   // [128]
+    // the folded norm's residual loads: one barrier per epilogue warp, used once
+    uint64_t *ebar = reinterpret_cast<uint64_t *>(reinterpret_cast<unsigned char *>(full) + 192);
+    static_assert((2 * S + 4) * 8 + 4 + 32 <= 192, "barrier block overlaps the residual-load barriers");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool CL = !HILO && p.cluster != 0;   // cluster split-K: one unit per CTA
@@ -890,6 +949,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int units = tiles * KS;
     const uint64_t deadline = globaltimer() + kTcWaitNs;
     bool ok = true;
+    int cl_fold = 0;   // cluster split, folded norm: this warp's residual chunk is on its way
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
@@ -901,10 +961,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(&tempty[b], kEpiWarps);    // one arrival per epilogue warp
         }
         for (int i = 0; i < 8; i++) pair_flags[i] = 0;
+        for (int w = 0; w < kEpiWarps; w++) mbar_init(&ebar[w], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
-        if (p.tma_out) prefetch_tensormap(&tmO);
+        if (p.tma_out || p.fold_tma) prefetch_tensormap(&tmO);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -1056,11 +1117,35 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (CL) {   // this slice's partial into the drained ring; the epilogue runs after the cluster barrier
                 cl_stage_partial<BN>(tb, reinterpret_cast<float4 *>(smem), warp - 2, half, lane);
                 if (half == 0) rs_s[32 * q + lane] = rs;
+                if constexpr (EPI == TC_RESID) {
+                    if (p.fold_tma) {   // the residual of this warp's first reduced chunk, behind the partials
+                        const int uu = (warp - 2) * KS + ks;
+                        if (uu < kEpiWarps * (BN / 64)) {
+                            const int ew = uu / (BN / 64), cc = uu % (BN / 64);
+                            cl_fold = resid_fold_issue(p, mp, m0 + 32 * ((ew + 2) & 3),
+                                                       n0 + (ew >> 2) * (BN / 2) + cc * kEpiCols, 1, lane,
+                                                       smem + BN * 512 + (warp - 2) * kStageBytes, &ebar[warp - 2]);
+                        }
+                    }
+                }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[b]);
             } else if (KS == 1) {
-                epilogue_tile<BN, EPI>(p, mp, tb, m0 + 32 * q, n0, half, lane, stg, rs);
+                bool done = false;
+                if constexpr (EPI == TC_RESID) {
+                    if (p.fold_tma && u + (int)gridDim.x >= units) {
+                        // the CTA's last tile: the drained stage ring holds the residual tiles
+                        if (!resid_fold_tile_tma<BN>(p, mp, tb, m0 + 32 * q, n0, half, lane,
+                                                     smem + (warp - 2) * (BN / 64) * kStageBytes, &ebar[warp - 2],
+                                                     deadline)) {
+                            ok = false;
+                            break;
+                        }
+                        done = true;
+                    }
+                }
+                if (!done) epilogue_tile<BN, EPI>(p, mp, tb, m0 + 32 * q, n0, half, lane, stg, rs);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[b]);
@@ -1103,6 +1188,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 float v[kEpiCols];
                 cl_sum_chunk<BN>(reinterpret_cast<const float4 *>(smem), uu, KS, lane, v);
                 if (col0 >= p.N) continue;   // warp-uniform
+                if constexpr (EPI == TC_RESID) {
+                    if (cl_fold && uu == (warp - 2) * KS + rank) {   // the chunk whose residual was loaded
+                        if (!__all_sync(0xffffffffu, mbar_wait(&ebar[warp - 2], 0, deadline))) {
+                            ok = false;
+                            break;
+                        }
+                        resid_fold_chunk_tma(p, mp, v, row0, col0, lane, smem + BN * 512 + (warp - 2) * kStageBytes);
+                        if (lane == 0) bulk_commit();
+                        continue;
+                    }
+                }
                 EpiRow er = epi_row<EPI>(p, row0 + lane);
                 er.rs = rs_s[32 * q + lane];
                 scale_row<EPI>(p, er, v);
@@ -1120,7 +1216,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         cluster_sync_all();   // no CTA leaves while a peer still reads its partial
     }
-    if (warp >= 2 && lane == 0 && p.tma_out) bulk_wait_all();   // epilogue stores complete
+    if (warp >= 2 && lane == 0 && (p.tma_out || p.fold_tma)) bulk_wait_all();   // epilogue stores complete
     if (!__all_sync(0xffffffffu, ok)) ok = false;
     if (!ok) {
         if (lane == 0) atomicExch(p.err, 1u);
@@ -1651,6 +1747,13 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
                  make_out_maps(epi, p, &mo, &mk, &mv))
                     ? 1
                     : 0;
+    // the folded norm's producer: residual tiles in and updated rows out by
+    // TMA where the stage ring is free (VOX_CUDA_TC_FOLD_TMA = 0: direct)
+    const char *env_ft = getenv("VOX_CUDA_TC_FOLD_TMA");
+    p.fold_tma = (epi == TC_RESID && p.xn_out && !p.hilo && p.vec && p.N % kEpiCols == 0 &&
+                  !(env_ft && atoi(env_ft) == 0) && make_out_maps(TC_RESID, p, &mo, &mk, &mv))
+                     ? 1
+                     : 0;
     if (p.hilo && p.f16) return cudaErrorInvalidValue;   // the split is into bf16 halves
     // CTA pairs only on request: at the encoder shapes they measured no faster
     // than single-CTA tiles (the MMA pipe, not L2 -> SMEM traffic, is the limit)

@@ -230,6 +230,8 @@ struct TcGemmParams {
     int tma_out;             // set by launch_tc_gemm: the epilogue stores through TMA
     int cluster;             // set by launch_tc_gemm: the ksplit slices of a tile are one cluster,
                              //   reduced through distributed shared memory (one row tile)
+    int fold_tma;            // set by launch_tc_gemm: the folded norm's producer (TC_RESID with xn_out)
+                             //   moves the residual tiles through TMA (a CTA's last tile)
 };
 
 constexpr int kTcSplitCounters = 4096;   // split-K tickets a caller provides (8 per tile)

@@ -18,18 +18,19 @@ constexpr int kEncSsChunks = kEncDim / 32;   // folded RMSNorm: 32-column chunks
 
 // The RMSNorms fold into the GEMMs around them (the residual epilogues write
 // the next operand and sums of squares, the consumers scale their rows):
-// five launches per layer instead of seven, for chunks of up to
-// VOX_CUDA_ENC_FOLD_MAX_ROWS rows (default 1024).  Measured per 32-layer
-// chunk: 100 rows 2.36 -> 2.12 ms, 500 rows 3.62 -> 3.49 ms; 1500 rows
-// 4.62 -> 4.74 ms, where wo and w2 run one 128-row tile per CTA and the
-// residual epilogue's direct stores (the TMA reduce-add cannot return the
-// updated rows) cost more than the separate pass.  VOX_CUDA_ENC_FOLD_NORM = 0
-// turns folding off (read when a graph is captured).
+// five launches per layer instead of seven, for chunks of any size (or of
+// up to VOX_CUDA_ENC_FOLD_MAX_ROWS rows).  Measured per 32-layer chunk: 100
+// rows 2.36 -> 2.12 ms, 500 rows 3.62 -> 3.49 ms; 1500 rows 4.62 -> 4.74 ms
+// while the residual epilogue read and wrote its rows with per-row direct
+// loads and stores (one tile per CTA leaves that epilogue exposed), and
+// 4.63 -> 4.53 ms since the drained stage ring takes the residual tiles in
+// and out by TMA.  VOX_CUDA_ENC_FOLD_NORM = 0 turns folding off (read when a
+// graph is captured).
 bool enc_fold_norm(int M) {
     const char *e = getenv("VOX_CUDA_ENC_FOLD_NORM");
     if (e && e[0] == '0') return false;
     const char *r = getenv("VOX_CUDA_ENC_FOLD_MAX_ROWS");
-    const int max_rows = (r && atoi(r) > 0) ? atoi(r) : 1024;
+    const int max_rows = (r && atoi(r) > 0) ? atoi(r) : 1 << 30;
     return M <= max_rows;
 }
 
