@@ -585,13 +585,17 @@ __device__ __forceinline__ void resid_norm_tile(const TcGemmParams &p, uint32_t 
 // TC_RESID with the folded norm when the stage ring is drained (the CTA's
 // last tile, or a cluster split's reduction): the warp's residual chunks
 // (32 rows x 32 fp32 columns each) arrive by TMA in the 128-byte swizzle
-// into `buf` (already issued on `bar`); the updated rows go back into the
-// same tiles and out by TMA stores (whole lines), while fp16(x * gain) and
-// the chunk sums of squares are stored per row (norm_prep_chunk).  The same
-// arithmetic as resid_norm_tile: x = (acc + bias) + residual.
+// into `t` (already issued on the warp's barrier); the updated rows go back
+// into the same tile, fp16(x * gain) into `t16` (64-byte swizzle), and both
+// leave by TMA stores (whole lines; rows past M are clipped); the chunk sums
+// of squares are stored per row.  The same arithmetic as resid_norm_tile and
+// norm_prep_chunk: x = (acc + bias) + residual, one fp16 rounding of x * gain.
 __device__ __forceinline__ void resid_fold_chunk_tma(const TcGemmParams &p, const EpiMaps &mp, float (&v)[kEpiCols],
-                                                     int row0, int col0, int lane, unsigned char *t) {
+                                                     int row0, int col0, int lane, unsigned char *t,
+                                                     unsigned char *t16) {
     add_bias(v, p.bias, col0, p.N);
+    const bool rv = row0 + lane < p.M;
+    float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < kEpiCols / 4; j++) {
         float4 *a = reinterpret_cast<float4 *>(t + lane * 128 + 16 * (j ^ (lane & 7)));
@@ -599,10 +603,27 @@ __device__ __forceinline__ void resid_fold_chunk_tma(const TcGemmParams &p, cons
         v[4 * j] += r.x, v[4 * j + 1] += r.y, v[4 * j + 2] += r.z, v[4 * j + 3] += r.w;
         *a = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
+#pragma unroll
+    for (int j = 0; j < kEpiCols; j++) ss = fmaf(v[j], v[j], ss);
+    if (rv) p.ss_out[(size_t)(col0 / kEpiCols) * p.ss_ld + row0 + lane] = ss;
+    uint32_t h[kEpiCols / 2], mx = 0;
+#pragma unroll
+    for (int j = 0; j < kEpiCols; j += 4) {
+        const float4 g = __ldg(reinterpret_cast<const float4 *>(p.xn_gain + col0 + j));
+        h[j >> 1] = pack_half2(v[j] * g.x, v[j + 1] * g.y);
+        h[(j >> 1) + 1] = pack_half2(v[j + 2] * g.z, v[j + 3] * g.w);
+        mx = f16x2_absmax(mx, h[j >> 1]);
+        mx = f16x2_absmax(mx, h[(j >> 1) + 1]);
+    }
+    if (rv) count_clamped(mx);
+#pragma unroll
+    for (int c = 0; c < 4; c++) swz_put<64>(t16, lane, c, make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]));
     fence_async_smem();
     __syncwarp();
-    if (lane == 0) tma_store_2d(mp.o, t, col0, row0);
-    if (row0 + lane < p.M) norm_prep_chunk(p, row0 + lane, col0, v);
+    if (lane == 0) {
+        tma_store_2d(mp.o, t, col0, row0);
+        tma_store_2d(mp.k, t16, col0, row0);
+    }
 }
 
 // issue the residual loads of the warp's chunks [col0, col0 + 32 n) of rows
@@ -622,7 +643,7 @@ __device__ __forceinline__ int resid_fold_issue(const TcGemmParams &p, const Epi
 template <int BN>
 __device__ __forceinline__ bool resid_fold_tile_tma(const TcGemmParams &p, const EpiMaps &mp, uint32_t tbase,
                                                     int row0, int n0, int half, int lane, unsigned char *buf,
-                                                    uint64_t *bar, uint64_t deadline) {
+                                                    unsigned char *buf16, uint64_t *bar, uint64_t deadline) {
     constexpr int kSteps = BN / 2 / kEpiCols;
     const int c0 = half * (BN / 2);
     const int nin = resid_fold_issue(p, mp, row0, n0 + c0, kSteps, lane, buf, bar);
@@ -632,7 +653,9 @@ __device__ __forceinline__ bool resid_fold_tile_tma(const TcGemmParams &p, const
     for (int i = 0; i < kSteps; i++) {
         float v[kEpiCols];
         tmem_ld32(tbase + (uint32_t)(c0 + i * kEpiCols), v);   // warp-collective: before any branch
-        if (i < nin && got) resid_fold_chunk_tma(p, mp, v, row0, n0 + c0 + i * kEpiCols, lane, buf + i * kStageBytes);
+        if (i < nin && got)
+            resid_fold_chunk_tma(p, mp, v, row0, n0 + c0 + i * kEpiCols, lane, buf + i * kStageBytes,
+                                 buf16 + i * (kStageBytes / 2));
     }
     if (lane == 0 && nin > 0) bulk_commit();
     return got;
@@ -938,6 +961,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // the folded norm's residual loads: one barrier per epilogue warp, used once
     uint64_t *ebar = reinterpret_cast<uint64_t *>(reinterpret_cast<unsigned char *>(full) + 192);
     static_assert((2 * S + 4) * 8 + 4 + 32 <= 192, "barrier block overlaps the residual-load barriers");
+    // the folded norm's tiles fit the drained ring: a last tile's fp32 + fp16
+    // chunks, and (cluster splits: 64- or 128-wide) the partials + one chunk per warp
+    static_assert(BN * 768 <= S * (Cfg::kABytes + Cfg::kBBytes), "fold tiles exceed the stage ring");
+    static_assert(BN > 128 || BN * 512 + kEpiWarps * kStageBytes * 3 / 2 <= S * (Cfg::kABytes + Cfg::kBBytes),
+                  "cluster fold tiles exceed the stage ring");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool CL = !HILO && p.cluster != 0;   // cluster split-K: one unit per CTA
@@ -966,6 +994,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
         if (p.tma_out || p.fold_tma) prefetch_tensormap(&tmO);
+        if (p.fold_tma) prefetch_tensormap(&tmK);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -1136,9 +1165,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if constexpr (EPI == TC_RESID) {
                     if (p.fold_tma && u + (int)gridDim.x >= units) {
                         // the CTA's last tile: the drained stage ring holds the residual tiles
+                        // (fp32 tiles [0, BN * 512), fp16 tiles [BN * 512, BN * 768) of the ring)
                         if (!resid_fold_tile_tma<BN>(p, mp, tb, m0 + 32 * q, n0, half, lane,
-                                                     smem + (warp - 2) * (BN / 64) * kStageBytes, &ebar[warp - 2],
-                                                     deadline)) {
+                                                     smem + (warp - 2) * (BN / 64) * kStageBytes,
+                                                     smem + BN * 512 + (warp - 2) * (BN / 64) * (kStageBytes / 2),
+                                                     &ebar[warp - 2], deadline)) {
                             ok = false;
                             break;
                         }
@@ -1194,7 +1225,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                             ok = false;
                             break;
                         }
-                        resid_fold_chunk_tma(p, mp, v, row0, col0, lane, smem + BN * 512 + (warp - 2) * kStageBytes);
+                        resid_fold_chunk_tma(p, mp, v, row0, col0, lane, smem + BN * 512 + (warp - 2) * kStageBytes,
+                                             smem + BN * 512 + kEpiWarps * kStageBytes +
+                                                 (warp - 2) * (kStageBytes / 2));
                         if (lane == 0) bulk_commit();
                         continue;
                     }
@@ -1750,8 +1783,11 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     // the folded norm's producer: residual tiles in and updated rows out by
     // TMA where the stage ring is free (VOX_CUDA_TC_FOLD_TMA = 0: direct)
     const char *env_ft = getenv("VOX_CUDA_TC_FOLD_TMA");
+    // (x as for the TMA reduce-add; the fp16 operand rows through the k map)
     p.fold_tma = (epi == TC_RESID && p.xn_out && !p.hilo && p.vec && p.N % kEpiCols == 0 &&
-                  !(env_ft && atoi(env_ft) == 0) && make_out_maps(TC_RESID, p, &mo, &mk, &mv))
+                  !(env_ft && atoi(env_ft) == 0) && make_out_maps(TC_RESID, p, &mo, &mk, &mv) &&
+                  make_map_2d(&mk, p.xn_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.M, p.N, p.ldo, 32, 32,
+                              CU_TENSOR_MAP_SWIZZLE_64B))
                      ? 1
                      : 0;
     if (p.hilo && p.f16) return cudaErrorInvalidValue;   // the split is into bf16 halves
