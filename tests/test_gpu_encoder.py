@@ -214,26 +214,33 @@ def test_folded_norm_tma_residual_path_is_bit_identical(monkeypatch):
 
 
 def test_encoder_attention_key_split_matches_unsplit(monkeypatch):
-    """Chunks of few row tiles split each tile's key blocks over up to 4 CTAs
-    (unnormalised partials merged by the last CTA): against the unsplit
-    kernel (VOX_CUDA_ENC_ATTN_KSPLIT=1), from position 0 (splits with no key
-    block) through window-crossing and ragged chunks, and against the oracle."""
+    """Chunks of few row tiles split each tile's key blocks over several CTAs:
+    by default the CTAs of one thread-block cluster whose partials are merged
+    through distributed shared memory ("cluster"; at most 2 of them with
+    VOX_CUDA_ENC_ATTN_CLUSTER=2), or (VOX_CUDA_ENC_ATTN_KSPLIT=4) unnormalised
+    partials in a workspace merged by the last CTA ("workspace").  Against
+    the unsplit kernel ("off"), from position 0 (splits with no key block)
+    through window-crossing and ragged chunks, and against the oracle."""
     ew = B.EncoderWeights(seed=17, n_layers=2, distinct=2, norm_noise=0.1)
     e = make_gpu_encoder(ew)
     sizes = [100, 37, 256, 3, 100, 64]
     xs = [B.normal_f32((n, B.ENC_DIM), 1170 + i) for i, n in enumerate(sizes)]
     outs = {}
-    for mode in ("1", ""):
-        monkeypatch.setenv("VOX_CUDA_ENC_ATTN_KSPLIT", mode)
+    modes = {"off": ("1", "-1"), "workspace": ("4", "-1"), "cluster": ("", ""), "cluster2": ("", "2")}
+    for mode, (ks, cl) in modes.items():
+        monkeypatch.setenv("VOX_CUDA_ENC_ATTN_KSPLIT", ks)
+        monkeypatch.setenv("VOX_CUDA_ENC_ATTN_CLUSTER", cl)
         st = e.state(max_chunk=256)
         outs[mode] = [st.step(x) for x in xs]
         st.free()
     o = B.OracleEncoder(ew, kv_max=2400)
     for i, x in enumerate(xs):
         ref = o.step(x)
-        assert np.isfinite(outs[""][i]).all()
-        assert B.rel_l2(outs[""][i], outs["1"][i]) < 1e-3, (i, B.rel_l2(outs[""][i], outs["1"][i]))
-        assert B.rel_l2(outs[""][i], ref) < 5e-3, (i, B.rel_l2(outs[""][i], ref))
+        for mode in ("workspace", "cluster", "cluster2"):
+            a = outs[mode][i]
+            assert np.isfinite(a).all(), (i, mode)
+            assert B.rel_l2(a, outs["off"][i]) < 1e-3, (i, mode, B.rel_l2(a, outs["off"][i]))
+            assert B.rel_l2(a, ref) < 5e-3, (i, mode, B.rel_l2(a, ref))
     e.free()
 
 

@@ -167,6 +167,8 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const int nball = (p_last - kall) / kFaKeys + 1;
     // this CTA's key blocks: all, or split z of KZ (possibly none)
     const int KZ = p.ksplit > 1 ? p.ksplit : 1, z = blockIdx.z;
+    // the KZ splits are one cluster (rank = z); launched with two softmax warps per quarter
+    const bool KCL = NH == 2 && KZ > 1 && p.kcluster > 1;
     const int bz0 = z * nball / KZ, bz1 = (z + 1) * nball / KZ;
     const int kstart = kall + bz0 * kFaKeys;
     const int nb = bz1 - bz0;
@@ -377,6 +379,25 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                        out16x2(ov[j + 6] * il, ov[j + 7] * il, p.f16));
                 }
             }
+        } else if (KCL) {
+            // this split's row partial into its drained Q / K tiles: [128 rows]
+            // x (64 o, max, sum, 2 unused); merged after the cluster barrier
+            float *pt = reinterpret_cast<float *>(fa_smem_raw) + row * kFaPartFloats;
+            if (ok && nb > 0) tc_fence_after();
+#pragma unroll
+            for (int c2 = 0; c2 < CW; c2 += 32) {
+                float ov[32];
+                if (nb > 0) tmem_ld32(to + (uint32_t)c2, ov);   // (warp-uniform)
+                else {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) ov[j] = 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4 *>(pt + half * CW + c2 + j) =
+                        make_float4(ov[j], ov[j + 1], ov[j + 2], ov[j + 3]);
+            }
+            if (half == 0) *reinterpret_cast<float2 *>(pt + kEncHeadDim) = make_float2(m, lt);
         } else if (KZ > 1) {
             // this split's row partial: o (64 fp32), then (max, sum)
             const size_t pr_idx = ((size_t)z * M + (r0 + row)) * kEncHeads + head;
@@ -464,6 +485,69 @@ enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
     }
 
+    if (KCL) {
+        // every split's partial is in its CTA's shared memory (every thread of
+        // every CTA arrives, whatever failed before: no CTA waits forever);
+        // rank z merges the tile rows r with r % KZ == z: the maximum over the
+        // splits that saw keys, then the weighted sums in split order (the
+        // same arithmetic as the workspace merge)
+        cluster_sync_all();
+        if (warp >= 2 && ok) {
+            constexpr int CW = kFaKeys / NH;
+            const int q = warp & 3, half = NH == 2 ? (warp - 2) >> 2 : 0;
+            const int row = 32 * q + lane;
+            if (row % KZ == z && r0 + row < M) {
+                const uint32_t base = smem_u32(reinterpret_cast<float *>(fa_smem_raw) + row * kFaPartFloats);
+                float mz[kFaMaxSplit], lz[kFaMaxSplit];
+                float gm = -INFINITY;
+#pragma unroll
+                for (int s2 = 0; s2 < kFaMaxSplit; s2++) {
+                    mz[s2] = -INFINITY;
+                    lz[s2] = 0.f;
+                    if (s2 < KZ) {
+                        const float2 v = ld_dsmem_f2(mapa_shared(base + 4u * kEncHeadDim, (uint32_t)s2));
+                        mz[s2] = v.x;
+                        lz[s2] = v.y;
+                        if (v.y > 0.f) gm = fmaxf(gm, v.x);
+                    }
+                }
+                float gl = 0.f, wz[kFaMaxSplit];
+#pragma unroll
+                for (int s2 = 0; s2 < kFaMaxSplit; s2++) {
+                    wz[s2] = (s2 < KZ && lz[s2] > 0.f) ? fast_exp2(mz[s2] - gm) : 0.f;
+                    gl += lz[s2] * wz[s2];
+                }
+                const float il = gl > 0.f ? 1.0f / gl : 0.f;
+                uint16_t *dst = p.out + (size_t)(r0 + row) * kEncQkv + head * kEncHeadDim + half * CW;
+#pragma unroll
+                for (int c = 0; c < CW; c += 16) {   // this thread's columns
+                    float4 acc[4] = {};
+#pragma unroll
+                    for (int s2 = 0; s2 < kFaMaxSplit; s2++) {
+                        if (s2 >= KZ) break;
+                        const uint32_t src = mapa_shared(base + 4u * (half * CW + c), (uint32_t)s2);
+                        const float w = wz[s2];
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float4 v = ld_dsmem_f4(src + 16u * j);
+                            acc[j].x = fmaf(w, v.x, acc[j].x);
+                            acc[j].y = fmaf(w, v.y, acc[j].y);
+                            acc[j].z = fmaf(w, v.z, acc[j].z);
+                            acc[j].w = fmaf(w, v.w, acc[j].w);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; j += 2)
+                        *reinterpret_cast<uint4 *>(dst + c + 4 * j) =
+                            make_uint4(out16x2(acc[j].x * il, acc[j].y * il, p.f16),
+                                       out16x2(acc[j].z * il, acc[j].w * il, p.f16),
+                                       out16x2(acc[j + 1].x * il, acc[j + 1].y * il, p.f16),
+                                       out16x2(acc[j + 1].z * il, acc[j + 1].w * il, p.f16));
+                }
+            }
+        }
+        cluster_sync_all();   // no CTA leaves while a peer still reads its partials
+    }
     if (!__all_sync(0xffffffffu, ok)) ok = false;
     if (!ok) {
         if (lane == 0 && p.err) atomicExch(p.err, 1u);
@@ -532,13 +616,67 @@ int enc_attn_ksplit(int M, size_t ws_floats) {
     return ks;
 }
 
+namespace {
+
+// Clusters of kz spread CTAs (one per SM, two softmax warps per lane
+// quarter) the device runs at once; cached per cluster size, 0 if unknown.
+int fa_max_clusters(int kz) {
+    static std::atomic<int> cache[kFaMaxSplit + 1];
+    if (kz < 2 || kz > kFaMaxSplit) return 0;
+    int c = cache[kz].load();
+    if (c == 0) {
+        int n = 0;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1, kEncHeads, kz);
+        cfg.blockDim = dim3(fa_threads(2));
+        cfg.dynamicSmemBytes = std::max(sizeof(FaSmem), kFaSpreadSmem);
+        cudaLaunchAttribute a[1];
+        a[0].id = cudaLaunchAttributeClusterDimension;
+        a[0].val.clusterDim.x = 1;
+        a[0].val.clusterDim.y = 1;
+        a[0].val.clusterDim.z = kz;
+        cfg.attrs = a;
+        cfg.numAttrs = 1;
+        if (cudaFuncSetAttribute(enc_attn_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)cfg.dynamicSmemBytes) != cudaSuccess ||
+            cudaOccupancyMaxActiveClusters(&n, enc_attn_tc_kernel<2>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        c = n > 0 ? n : -1;
+        cache[kz].store(c);
+    }
+    return c > 0 ? c : 0;
+}
+
+// Cluster key split for an M-row chunk (p.kcluster = 1, no workspace split):
+// when the (row tile, head) tiles fill at most half the SMs, each tile's key
+// blocks go to kz CTAs of one cluster (>= 2 blocks each, every cluster
+// resident at once), merged through distributed shared memory.
+// VOX_CUDA_ENC_ATTN_CLUSTER = -1 turns it off, n >= 2 caps kz.
+int fa_cluster_split(int M, int sms) {
+    const char *e = getenv("VOX_CUDA_ENC_ATTN_CLUSTER");
+    const int env = (e && *e) ? atoi(e) : 0;
+    if (env < 0) return 1;
+    const int tiles = (M + kFaRows - 1) / kFaRows * kEncHeads;
+    if (2 * tiles > sms) return 1;
+    const int nball = (M - 1 + kEncWindow - 1 + kFaKeys - 1) / kFaKeys + 1;   // at most
+    int kz = std::min(std::min(kFaMaxSplit, sms / tiles), nball / 2);
+    if (env >= 2) kz = std::min(kz, env);
+    while (kz >= 2 && tiles > fa_max_clusters(kz)) kz--;
+    return kz >= 2 ? kz : 1;
+}
+
+}  // namespace
+
 bool enc_attn_tc_supported(const EncAttnParams &p) {
     return p.cap % kEncRingAlign == 0 && p.cap >= p.M + kEncWindow - 1 && p.err != nullptr &&
            ((uintptr_t)p.q & 15) == 0 && ((uintptr_t)p.k_ring & 15) == 0 && ((uintptr_t)p.v_ring & 15) == 0 &&
            ((uintptr_t)p.out & 15) == 0;
 }
 
-cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl) {
+cudaError_t launch_enc_attn_tc(const EncAttnParams &p_in, cudaStream_t st, bool pdl) {
+    EncAttnParams p = p_in;
     if (p.M <= 0 || !enc_attn_tc_supported(p)) return cudaErrorInvalidValue;
     CUtensorMap mq, mk, mv;
     if (!fa_map(&mq, p.q, p.M, kFaRows) || !fa_map(&mk, p.k_ring, p.cap, kFaKeys) ||
@@ -558,9 +696,17 @@ cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl
         if (e != cudaSuccess) return e;
         attr_set.fetch_or(bit);
     }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (p.ksplit <= 1 && p.kcluster == 1) {
+        p.ksplit = fa_cluster_split(p.M, sms);
+        p.kcluster = p.ksplit > 1 ? p.ksplit : 0;
+    } else {
+        p.kcluster = 0;
+    }
     const int kz = p.ksplit > 1 ? p.ksplit : 1;
-    if (kz > 1 && (kz > kFaMaxSplit || !p.part || !p.cnt ||
-                   (p.M + kFaRows - 1) / kFaRows * kEncHeads > kTcSplitCounters))
+    if (kz > 1 && !p.kcluster &&
+        (kz > kFaMaxSplit || !p.part || !p.cnt || (p.M + kFaRows - 1) / kFaRows * kEncHeads > kTcSplitCounters))
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     const int ctas = (p.M + kFaRows - 1) / kFaRows * kEncHeads * kz;
@@ -571,20 +717,34 @@ cudaError_t launch_enc_attn_tc(const EncAttnParams &p, cudaStream_t st, bool pdl
     // three to an SM on the few free ones and share their issue slots.  Such
     // a CTA alone on its SM splits the softmax over two warps per TMEM lane
     // quarter (NH = 2; VOX_CUDA_ENC_ATTN_NH = 1 | 2 forces one).
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // (a cluster split always spreads, two softmax warps per quarter: the
+    // cluster residency was checked for that shape)
     const char *sp = getenv("VOX_CUDA_ENC_ATTN_SPREAD");
-    const bool spread = sp ? atoi(sp) != 0 : ctas <= sms;
+    const bool spread = p.kcluster ? true : sp ? atoi(sp) != 0 : ctas <= sms;
     const char *nh_env = getenv("VOX_CUDA_ENC_ATTN_NH");
-    const int nh = (nh_env && (atoi(nh_env) == 1 || atoi(nh_env) == 2)) ? atoi(nh_env) : spread ? 2 : 1;
+    const int nh = p.kcluster                                          ? 2
+                   : (nh_env && (atoi(nh_env) == 1 || atoi(nh_env) == 2)) ? atoi(nh_env)
+                   : spread                                            ? 2
+                                                                       : 1;
     cfg.blockDim = dim3(fa_threads(nh));
     cfg.dynamicSmemBytes = spread ? std::max(sizeof(FaSmem), kFaSpreadSmem) : sizeof(FaSmem);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (p.kcluster) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = kz;
+        na++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     return nh == 2 ? cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel<2>, mq, mk, mv, p)
                    : cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel<1>, mq, mk, mv, p);
 }

@@ -912,15 +912,6 @@ __device__ __forceinline__ void cl_stage_partial(uint32_t tbase, float4 *part, i
     }
 }
 
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr_cluster) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr_cluster)
-                 : "memory");
-    return v;
-}
-
 // chunk uu of the tile summed over the KS CTAs, in rank order
 template <int BN>
 __device__ __forceinline__ void cl_sum_chunk(const float4 *part, int uu, int KS, int lane, float (&v)[kEpiCols]) {

@@ -281,6 +281,10 @@ struct EncAttnParams {
     int ksplit;               // 1 (or 0): no split
     float *part;              // [ksplit][M][32 heads] x (64 o + max + sum) floats
     unsigned *cnt;            // [row tiles][32], zero between launches
+    // 1: with ksplit <= 1, the launcher may split the key blocks over a
+    // thread-block cluster instead (partials merged through distributed
+    // shared memory; no workspace); set by the launcher to the cluster size
+    int kcluster;
 };
 // key splits of the tensor-core encoder attention for an M-row chunk whose
 // partials may take ws_floats floats

@@ -439,6 +439,7 @@ int enqueue_encoder(vox_cuda_enc_state *s, int M, bool table, cudaStream_t st, c
         a.ksplit = enc_attn_ksplit(M, kEncSplitFloats);
         a.part = s->split;
         a.cnt = s->split_cnt;
+        a.kcluster = 1;   // (unless split above: the launcher may split over a cluster)
         VC_EV_BEGIN(VOX_CUDA_EPROF_ATTN);
         VC_TRY(launch_enc_attn(a, st, pdl));
         VC_EV_END();

@@ -137,6 +137,20 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
 }
+// loads from distributed shared memory (a shared::cluster address)
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr_cluster) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr_cluster)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ float2 ld_dsmem_f2(uint32_t addr_cluster) {
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr_cluster) : "memory");
+    return v;
+}
 // shared::cluster address of the variable at shared::cta address `addr` in CTA `rank`
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
     uint32_t r;
