@@ -285,6 +285,10 @@ struct EncAttnParams {
     // thread-block cluster instead (partials merged through distributed
     // shared memory; no workspace); set by the launcher to the cluster size
     int kcluster;
+    // 1: launched beside other attention launches (one per stream of a
+    // batched encoder step): three CTAs per SM unless VOX_CUDA_ENC_ATTN_SPREAD
+    // asks otherwise (spreading one CTA per SM would queue the streams)
+    int shared_sms;
 };
 // key splits of the tensor-core encoder attention for an M-row chunk whose
 // partials may take ws_floats floats

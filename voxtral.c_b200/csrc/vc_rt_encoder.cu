@@ -756,6 +756,7 @@ int enqueue_encoder_batch(vox_cuda_encoder *e, EncBatch *b, vox_cuda_enc_state *
             a.out = b->att16 + (size_t)row0[i] * kEncQkv;
             a.f16 = 1;
             a.err = b->err;
+            a.shared_sms = 1;   // the other states' attention runs beside it
             VC_TRY(launch_enc_attn(a, b->side[i], false));
             VC_TRY(cudaEventRecord(b->join[i], b->side[i]));
             VC_TRY(cudaStreamWaitEvent(st, b->join[i], 0));
