@@ -899,6 +899,24 @@ __device__ __forceinline__ void split_finish_pair(const TcGemmParams &p, int tm,
 // chunk over the KS CTAs (distributed shared memory, rank order: the same
 // sum whichever CTA reads) and running the epilogue on it.
 
+// split activations: chunks uh (hi rows) and ul (lo rows) summed over the KS
+// CTAs, hi + lo per slice, in rank order
+template <int BN>
+__device__ __forceinline__ void cl_sum_chunk_pair(const float4 *part, int uh, int ul, int KS, int lane,
+                                                  float (&v)[kEpiCols]) {
+    const uint32_t bh = smem_u32(part + (size_t)uh * 256 + lane), bl = smem_u32(part + (size_t)ul * 256 + lane);
+#pragma unroll
+    for (int j = 0; j < kEpiCols; j++) v[j] = 0.f;
+    for (int r = 0; r < KS; r++) {
+        const uint32_t rh = mapa_shared(bh, (uint32_t)r), rl = mapa_shared(bl, (uint32_t)r);
+#pragma unroll
+        for (int j = 0; j < kEpiCols / 4; j++) {
+            const float4 x = ld_dsmem_f4(rh + 512u * j), y = ld_dsmem_f4(rl + 512u * j);
+            v[4 * j] += x.x + y.x, v[4 * j + 1] += x.y + y.y, v[4 * j + 2] += x.z + y.z, v[4 * j + 3] += x.w + y.w;
+        }
+    }
+}
+
 // this warp's chunks (of its column half) of the accumulator -> its region
 template <int BN>
 __device__ __forceinline__ void cl_stage_partial(uint32_t tbase, float4 *part, int ew, int half, int lane) {
@@ -959,7 +977,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                   "cluster fold tiles exceed the stage ring");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const bool CL = !HILO && p.cluster != 0;   // cluster split-K: one unit per CTA
+    const bool CL = p.cluster != 0;   // cluster split-K: one unit per CTA
     // row tiles: 128 output rows, or (HILO) 64 output rows = 128 A rows [hi; lo]
     const int MT = HILO ? (p.M + 63) / 64 : (p.M + kBM - 1) / kBM;
     const int tiles = MT * ((p.N + BN - 1) / BN);
@@ -1103,7 +1121,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int m0 = (t % MT) * kBM, n0 = (t / MT) * BN;
             const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + b * (Cfg::kTmemCols / 2);
             if constexpr (HILO) {
-                if (KS == 1) {
+                if (CL) {   // this slice's hi / lo partials into the drained ring (summed after the barrier)
+                    cl_stage_partial<BN>(tb, reinterpret_cast<float4 *>(smem), warp - 2, half, lane);
+                    if (half == 0) rs_s[32 * q + lane] = rs;
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[b]);
+                } else if (KS == 1) {
                     // the lo warp of the pair (warp - 2 for a hi warp) stages its chunks
                     float *xch = reinterpret_cast<float *>(sStage + ((q < 2 ? warp - 2 : warp) - 2) * kStageBytes);
                     if (!epilogue_pair<BN, EPI>(p, tb, t % MT, n0, q, half, lane, xch,
@@ -1203,7 +1227,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const EpiMaps mp = {&tmO, &tmK, &tmV};
             unsigned char *stg = sStage + (warp - 2) * kStageBytes;
             constexpr int U = kEpiWarps * (BN / 64);   // 32 x 32 chunks of the tile
-            for (int uu = (warp - 2) * KS + rank; uu < U; uu += kEpiWarps * KS) {
+            if constexpr (HILO) {
+                // output chunks: 2 row quarters (hi rows 32 qq.., lo rows 64 + 32 qq..)
+                // x 2 column halves x BN / 64; each sums its hi and lo partials
+                // over the KS CTAs, hi + lo per slice in slice order (as the
+                // workspace split's split_finish_pair)
+                constexpr int C2 = BN / 64;
+                for (int uu = (warp - 2) * KS + rank; uu < 4 * C2; uu += kEpiWarps * KS) {
+                    const int qq = uu / (2 * C2), hf = (uu / C2) & 1, cc = uu % C2;
+                    const int col0 = n0 + hf * (BN / 2) + cc * kEpiCols;
+                    float v[kEpiCols];
+                    cl_sum_chunk_pair<BN>(reinterpret_cast<const float4 *>(smem), (4 * hf + qq + 2) * C2 + cc,
+                                          (4 * hf + qq) * C2 + cc, KS, lane, v);
+                    if (col0 >= p.N) continue;   // warp-uniform
+                    EpiRow er = epi_row<EPI>(p, (t % MT) * 64 + 32 * qq + lane);
+                    er.rs = rs_s[32 * qq + lane];
+                    if (er.row >= p.M) continue;
+                    scale_row<EPI>(p, er, v);
+                    epi_direct<EPI>(p, er, v, col0);
+                }
+            }
+            for (int uu = (warp - 2) * KS + rank; !HILO && uu < U; uu += kEpiWarps * KS) {
                 const int ew = uu / (BN / 64), cc = uu % (BN / 64);
                 const int q = (ew + 2) & 3, half = ew >> 2;   // the writing warp's lane quarter / half
                 const int row0 = m0 + 32 * q, col0 = n0 + half * (BN / 2) + cc * kEpiCols;
@@ -1816,8 +1860,9 @@ cudaError_t launch_tc_gemm(int epi, const TcGemmParams &p_in, const void *A, con
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = device_sms(dev);
-    const int mt_cl = (p.M + kBM - 1) / kBM;
-    if (!p.hilo && !pair && e_cl >= 0 && 4 * mt_cl * ((p.N + bn - 1) / bn) < 3 * sms) {
+    // (split activations: 64 output rows per tile, [hi; lo] A rows)
+    const int mt_cl = p.hilo ? (p.M + 63) / 64 : (p.M + kBM - 1) / kBM;
+    if (!pair && e_cl >= 0 && 4 * mt_cl * ((p.N + bn - 1) / bn) < 3 * sms) {
         // Few tiles (fewer than 3/4 of the SMs): a k-block costs about the
         // same time whatever the tile width, so split K over a cluster and
         // reduce in distributed shared memory.  The most CTAs (<= one per
