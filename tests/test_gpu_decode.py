@@ -435,6 +435,34 @@ def test_tc_prefill_matches_decode_kernel_prefill(small_w, monkeypatch):
     b.free()
 
 
+def test_tc_prefill_cluster_split_matches_workspace_split(small_w, monkeypatch):
+    """The prefill's split-activation GEMMs split K over a thread-block
+    cluster by default (hi and lo partials summed through distributed shared
+    memory); VOX_CUDA_TC_CLUSTER=-1 takes the global-workspace split instead
+    (read when the prefill's graph is captured, so each mode gets its own
+    decoder).  Both sum the same slices hi + lo in slice order, with slice
+    counts chosen independently: K / V rows of every layer and the next
+    step's logits agree within the prefill tolerance."""
+    outs = {}
+    for mode in ("", "-1"):
+        monkeypatch.setenv("VOX_CUDA_TC_CLUSTER", mode)
+        d = make_gpu_decoder(small_w)
+        st = d.state(kv_cap=256)
+        st.prefill(B.normal_f32((38, B.DEC_DIM), 990))
+        kv = [st.read_kv(layer, 0, 38) for layer in range(small_w.n_layers)]
+        tok, logits = st.step(B.normal_f32(B.DEC_DIM, 991))
+        outs[mode] = (kv, tok, logits)
+        st.free()
+        d.free()
+    (kv_c, t_c, l_c), (kv_w, t_w, l_w) = outs[""], outs["-1"]
+    for layer in range(small_w.n_layers):
+        (kc, vc), (kw, vw) = kv_c[layer], kv_w[layer]
+        assert np.isfinite(kc).all() and np.isfinite(vc).all()
+        assert B.rel_l2(kc, kw) < PREFILL_TOL and B.rel_l2(vc, vw) < PREFILL_TOL, (layer, B.rel_l2(kc, kw))
+    assert B.rel_l2(l_c, l_w) < PREFILL_TOL
+    assert t_c == t_w or np.sort(l_w)[-1] - np.sort(l_w)[-2] <= MARGIN
+
+
 def test_tc_prefill_folded_norm_matches_separate_pass(small_w, monkeypatch):
     """The prefill's RMSNorms folded into its GEMMs (the residual epilogues
     write the next hi / lo operand of x * g and the row sums of squares, the
